@@ -1,0 +1,136 @@
+/*
+ * qlin -- C ABI of the B200 (sm_100a) quantised-linear hot path.
+ *
+ * Every entry point replaces one Python/Triton entry point of the reference
+ * engine's kernel layer (paths relative to the reference project root; the
+ * citation is given per function).  The Python mirror in
+ * qwen_3.5_comfy_prompt_enhancer_b200/kernels/{gemm,w4,norm}.py keeps the
+ * reference's names, argument order and in-place/return conventions and calls
+ * these functions; callers in other languages bind them directly.
+ *
+ * Conventions shared by every entry point
+ *  - All pointers are device pointers on the current CUDA device.  bf16 data is
+ *    passed as `void*` (16-bit IEEE bfloat16, row-major).
+ *  - Shapes follow the reference: activations a_q int8 [M, K] contiguous with
+ *    one fp32 scale per 64 K elements, a_s [M, K/64] contiguous; W8 weights
+ *    int8 [K, N] (N contiguous) with fp32 per-column scales [N]; W4 weights
+ *    packed uint8 [K/2, N] (byte j of a column: K = 2j in the low nibble,
+ *    K = 2j+1 in the high nibble), bf16 group scales [K/WG, N] and optional
+ *    uint8 zeros [K/WG, N] (value = nibble - zero; no zeros means zero = 8).
+ *  - Outputs are preallocated by the caller and written in place; `ldo`/`ldr`
+ *    are row strides in elements.  `residual` may alias `out`.
+ *  - Work is enqueued on `stream` (a cudaStream_t; NULL = legacy default
+ *    stream) and returns immediately.  Kernels are launched with programmatic
+ *    dependent launch: they begin streaming WEIGHTS before the preceding
+ *    kernel on the stream has finished, so weights must not be written by the
+ *    kernel launched immediately before on the same stream (they are read-only
+ *    model parameters in the engine).  Activations, residuals and outputs are
+ *    ordered normally.
+ *  - Return value: QLIN_OK or a qlin_status code; qlin_last_error() gives a
+ *    thread-local message for the most recent failure.
+ *  - Requirements beyond the reference's (checked, reported as
+ *    QLIN_ERR_SHAPE / QLIN_ERR_ALIGNMENT): K % 64 == 0 (the reference
+ *    silently assumes it, kernels/common.py:5-7), N % 16 == 0, 16-byte
+ *    aligned base pointers for a_q and every weight / scale / zero tensor.
+ */
+#ifndef QLIN_H_
+#define QLIN_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  QLIN_OK = 0,
+  QLIN_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative size, bad flag */
+  QLIN_ERR_SHAPE = 2,            /* shape not supported by the reference contract */
+  QLIN_ERR_ALIGNMENT = 3,        /* pointer or stride alignment */
+  QLIN_ERR_UNSUPPORTED = 4,      /* valid request this build cannot run */
+  QLIN_ERR_CUDA = 5,             /* CUDA runtime / launch error */
+  QLIN_ERR_DEVICE_FAULT = 6      /* a bounded device-side wait gave up */
+} qlin_status;
+
+/* Library version (major*10000 + minor*100 + patch). */
+int qlin_version(void);
+
+/* Static string for a status code. */
+const char* qlin_status_string(int status);
+
+/* Thread-local detail message of the last failing call on this thread. */
+const char* qlin_last_error(void);
+
+/* Reads (and if `clear`, resets) the device fault word of the current device:
+ * a bitmask of bounded waits that gave up inside qlin kernels since the last
+ * clear.  Synchronous; for diagnostics and tests.  Returns -1 on CUDA error. */
+int qlin_device_fault(int clear);
+
+/* kernels/gemm.py:60-92 (gemm_i8, W8 branch) and gemm.py:20-57 (kernel):
+ *   out[m,n] = bf16( (sum_kb float(int32 dot of block kb) * a_s[m,kb]) * b_s[n]
+ *                    (+ residual[m,n]) )                                     */
+int qlin_gemm_i8(const int8_t* a_q, const float* a_s, int64_t M, int64_t K,
+                 const int8_t* b, const float* b_s, int64_t N,
+                 void* out, int64_t ldo, const void* residual, int64_t ldr,
+                 void* stream);
+
+/* kernels/w4.py:139-166 (gemm_w4) and w4.py:64-136 (_w4_acc, kernel):
+ *   out[m,n] = bf16( sum_sub float(int32 dot of sub-block) * (a_s * ws)
+ *                    (+ residual[m,n]) ),  SUB = min(WG, 64).
+ * b_z may be NULL (symmetric, zero = 8).  WG = K / rows(b_s) is passed as
+ * `wgrp` and must be 32 or a multiple of 64. */
+int qlin_gemm_w4(const int8_t* a_q, const float* a_s, int64_t M, int64_t K,
+                 const uint8_t* b, const void* b_s, const uint8_t* b_z, int64_t N, int64_t wgrp,
+                 void* out, int64_t ldo, const void* residual, int64_t ldr,
+                 void* stream);
+
+/* kernels/gemm.py:290-312 (proj3) and gemm.py:234-287 (kernel): three W8
+ * projections sharing A, written to out[:, 0:n1], [n1:n1+n2], [n1+n2:...].
+ * A segment with n_i == 0 is skipped (its pointers may be NULL). */
+int qlin_proj3(const int8_t* a_q, const float* a_s, int64_t M, int64_t K,
+               const int8_t* w1, const float* s1, int64_t n1,
+               const int8_t* w2, const float* s2, int64_t n2,
+               const int8_t* w3, const float* s3, int64_t n3,
+               void* out, int64_t ldo, void* stream);
+
+/* kernels/w4.py:220-251 (proj3_w4) and w4.py:169-217 (kernel).  Per-segment
+ * zeros z_i may be NULL (that segment decodes with zero = 8). */
+int qlin_proj3_w4(const int8_t* a_q, const float* a_s, int64_t M, int64_t K,
+                  const uint8_t* w1, const void* s1, const uint8_t* z1, int64_t n1,
+                  const uint8_t* w2, const void* s2, const uint8_t* z2, int64_t n2,
+                  const uint8_t* w3, const void* s3, const uint8_t* z3, int64_t n3,
+                  int64_t wgrp, void* out, int64_t ldo, void* stream);
+
+/* kernels/gemm.py:140-151 (mlp_gate_up) and gemm.py:95-137 (kernel):
+ *   out = bf16( silu(g * sg) * (u * su) ), out row stride ldo. */
+int qlin_mlp_gate_up(const int8_t* a_q, const float* a_s, int64_t M, int64_t K,
+                     const int8_t* wg, const float* sg, const int8_t* wu, const float* su,
+                     int64_t N, void* out, int64_t ldo, void* stream);
+
+/* kernels/gemm.py:214-231 (mlp_gate_up_quant) and gemm.py:154-211 (kernel):
+ *   h = bf16_round( silu(g * sg) * (u * su) );  per (m, 64-column group):
+ *   s = max(amax|h| / 127, 1e-8), q = round_half_away(h / s) clamped to +-127.
+ * out_q int8 [M, N] contiguous, out_s fp32 [M, N/64] contiguous; N % 64 == 0. */
+int qlin_mlp_gate_up_quant(const int8_t* a_q, const float* a_s, int64_t M, int64_t K,
+                           const int8_t* wg, const float* sg, const int8_t* wu, const float* su,
+                           int64_t N, int8_t* out_q, float* out_s, void* stream);
+
+/* kernels/w4.py:300-323 (mlp_gate_up_quant_w4) and w4.py:254-297 (kernel):
+ * as above with W4 weights (scales applied per sub-block inside the K loop). */
+int qlin_mlp_gate_up_quant_w4(const int8_t* a_q, const float* a_s, int64_t M, int64_t K,
+                              const uint8_t* wg, const void* sg, const uint8_t* zg,
+                              const uint8_t* wu, const void* su, const uint8_t* zu,
+                              int64_t N, int64_t wgrp, int8_t* out_q, float* out_s,
+                              void* stream);
+
+/* kernels/norm.py:75-92 (quant_row) and norm.py:15-25 (_quant_groups):
+ * bf16 x [M, K] (row stride ldx) -> int8 q [M, K], fp32 s [M, K/64]:
+ *   s = max(amax / 127, 1e-8) (IEEE division), q = round_half_away(x / s). */
+int qlin_quant_row(const void* x, int64_t ldx, int64_t M, int64_t K,
+                   int8_t* q, float* s, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QLIN_H_ */

@@ -1,0 +1,307 @@
+"""CPU oracle for the quantised-linear hot path -- TEST INFRASTRUCTURE ONLY.
+
+This module is the checker, never the product.  Only ``tests/``,
+``__graft_entry__.smoke()`` and the ``cpu_baseline`` / ``--impl reference`` legs of
+``bench.py`` may import it.  The shipped package calls CUDA through the C-ABI
+library and has no CPU path.
+
+Every function restates, in numpy, the arithmetic of one reference function of
+``kernels/gemm.py``, ``kernels/w4.py``, ``kernels/norm.py`` or
+``kernels/common.py`` (paths relative to the reference project root; line
+numbers cited per function).  The restatement is exact at the level the
+reference defines it:
+
+* integer parts bit-exact: int32 sums per 64-element K block (per ``SUB``
+  sub-block for W4), nibble decode ``nibble - z``, int8 activation codes;
+* fp32 epilogue in the reference's program order, one rounding per numpy
+  float32 operation (no fused multiply-add), K blocks summed in ascending
+  order;
+* bf16 output rounding selectable: ``"rne"`` (round-to-nearest-even, what a
+  GPU build of the reference does) or ``"trunc"`` (what Triton's CPU
+  interpreter does; used only to pin this oracle against fixtures produced by
+  running the reference under ``TRITON_INTERPRET=1``, see
+  ``tests/golden/make_golden.py``).
+
+The oracle is pinned bit-exactly against those fixtures by
+``tests/test_oracle_golden.py``.
+
+``dequant_matmul_*`` are the reference's own pure-PyTorch CPU formulation
+(``.dev/test_kernels.py:40-41``) used as the timed CPU baseline.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+GROUP = 64  # kernels/common.py:7
+
+
+# ----------------------------------------------------------------------------
+# bf16 helpers (bf16 is stored as uint16 bit patterns in numpy)
+# ----------------------------------------------------------------------------
+
+def f32_to_bf16_bits(x: np.ndarray, mode: str = "rne") -> np.ndarray:
+    """fp32 -> bf16 bit pattern (uint16).  ``mode`` is "rne" or "trunc"."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    b = x.view(np.uint32).astype(np.uint64)
+    if mode == "trunc":
+        r = b >> 16
+    elif mode == "rne":
+        r = (b + 0x7FFF + ((b >> 16) & 1)) >> 16
+        nan = np.isnan(x)
+        r = np.where(nan, (b >> 16) | 0x40, r)
+    else:
+        raise ValueError(mode)
+    return r.astype(np.uint16)
+
+
+def bf16_bits_to_f32(h: np.ndarray) -> np.ndarray:
+    h = np.ascontiguousarray(h, dtype=np.uint16)
+    return (h.astype(np.uint32) << 16).view(np.float32)
+
+
+def bf16_round(x: np.ndarray, mode: str = "rne") -> np.ndarray:
+    """x.to(bf16).to(fp32) as the reference writes it (gemm.py:200, w4.py:286)."""
+    return bf16_bits_to_f32(f32_to_bf16_bits(x, mode))
+
+
+# ----------------------------------------------------------------------------
+# common.py helpers
+# ----------------------------------------------------------------------------
+
+def round_i8(v: np.ndarray) -> np.ndarray:
+    """kernels/common.py:24-29: trunc(v + (v >= 0 ? 0.5 : -0.5)) clamped to +-127.
+
+    The +-0.5 add is an fp32 operation (it can itself round), the conversion
+    truncates toward zero.  This is round-half-away-from-zero, not numpy's
+    half-to-even ``np.round``.
+    """
+    v = np.asarray(v, dtype=np.float32)
+    half = np.where(v >= np.float32(0.0), np.float32(0.5), np.float32(-0.5)).astype(np.float32)
+    t = (v + half).astype(np.float32)
+    with np.errstate(invalid="ignore"):
+        r = np.trunc(t)
+    r = np.clip(r, -127, 127)
+    return r.astype(np.int8)
+
+
+def silu(x: np.ndarray) -> np.ndarray:
+    """kernels/common.py:32-34 with Triton's ``sigmoid = 1 / (1 + exp(-x))``."""
+    x = np.asarray(x, dtype=np.float32)
+    with np.errstate(over="ignore"):
+        e = np.exp(-x).astype(np.float32)
+    sig = (np.float32(1.0) / (np.float32(1.0) + e).astype(np.float32)).astype(np.float32)
+    return (x * sig).astype(np.float32)
+
+
+def quant_groups(y: np.ndarray):
+    """kernels/norm.py:15-25 (``_quant_groups``): per row, per 64-group.
+
+    ``s = max(amax / 127, 1e-8)`` (IEEE fp32 division), ``q = round_i8(y / s)``
+    (true division, not multiply by reciprocal).  Returns (int8 [M,K],
+    fp32 [M,K/64]).
+    """
+    y = np.asarray(y, dtype=np.float32)
+    M, K = y.shape
+    assert K % GROUP == 0
+    y3 = y.reshape(M, K // GROUP, GROUP)
+    amax = np.abs(y3).max(axis=2).astype(np.float32)
+    s = np.maximum((amax / np.float32(127.0)).astype(np.float32), np.float32(1e-8)).astype(np.float32)
+    q = round_i8((y3 / s[:, :, None]).astype(np.float32))
+    return q.reshape(M, K), s
+
+
+def quant_row(x_bits: np.ndarray):
+    """kernels/norm.py:75-92: bf16 X [M,K] -> (int8 [M,K], fp32 [M,K/64])."""
+    return quant_groups(bf16_bits_to_f32(x_bits))
+
+
+# ----------------------------------------------------------------------------
+# int8 x int8 -> int32 block sums
+# ----------------------------------------------------------------------------
+
+def _block_sums(a_q: np.ndarray, w: np.ndarray, blk: int) -> np.ndarray:
+    """int32 [K/blk, M, N]: exact sum over each K block of a[m,k] * w[k,n]."""
+    M, K = a_q.shape
+    assert w.shape[0] == K and K % blk == 0
+    a = a_q.astype(np.int64).reshape(M, K // blk, blk).transpose(1, 0, 2)
+    ww = w.astype(np.int64).reshape(K // blk, blk, -1)
+    return np.matmul(a, ww).astype(np.int32)
+
+
+def unpack_w4(b: np.ndarray, b_z, wgrp: int) -> np.ndarray:
+    """kernels/w4.py:3-15, 48-61, 78-88: packed uint8 [K/2, N] -> int8 [K, N].
+
+    Byte j of column n holds k = 2j in the low nibble and k = 2j+1 in the high
+    nibble; the signed value is ``nibble - z`` with ``z`` the per-(group, n)
+    zero (uint8 [K/WG, N]) or 8 when there is none.
+    """
+    b = np.asarray(b, dtype=np.uint8)
+    K2, N = b.shape
+    K = 2 * K2
+    nib = np.empty((K, N), dtype=np.int32)
+    nib[0::2] = b & 0x0F
+    nib[1::2] = (b >> 4) & 0x0F
+    if b_z is None:
+        z = np.full((K, N), 8, dtype=np.int32)
+    else:
+        z = np.repeat(np.asarray(b_z, dtype=np.int32), wgrp, axis=0)
+    return (nib - z).astype(np.int8)
+
+
+# ----------------------------------------------------------------------------
+# a1: gemm_i8  (kernels/gemm.py:20-92)
+# ----------------------------------------------------------------------------
+
+def gemm_i8_f32(a_q, a_s, b, b_s, residual_f32=None) -> np.ndarray:
+    """fp32 result of gemm_i8 before the bf16 store (gemm.py:38-55).
+
+    ``out += float(int32 block dot) * a_s[m, kb]`` for kb ascending, then
+    ``out *= b_s[n]``, then ``out += residual``.
+    """
+    a_s = np.asarray(a_s, dtype=np.float32)
+    b_s = np.asarray(b_s, dtype=np.float32)
+    M, K = a_q.shape
+    N = b.shape[1]
+    sums = _block_sums(a_q, b, GROUP)
+    out = np.zeros((M, N), dtype=np.float32)
+    for kb in range(K // GROUP):
+        prod = (sums[kb].astype(np.float32) * a_s[:, kb:kb + 1]).astype(np.float32)
+        out = (out + prod).astype(np.float32)
+    out = (out * b_s[None, :]).astype(np.float32)
+    if residual_f32 is not None:
+        out = (out + residual_f32).astype(np.float32)
+    return out
+
+
+def gemm_i8(a_q, a_s, b, b_s, residual_bits=None, mode="rne") -> np.ndarray:
+    """kernels/gemm.py:60-92 -> bf16 bits [M,N]."""
+    res = None if residual_bits is None else bf16_bits_to_f32(residual_bits)
+    return f32_to_bf16_bits(gemm_i8_f32(a_q, a_s, b, b_s, res), mode)
+
+
+# ----------------------------------------------------------------------------
+# a5: gemm_w4  (kernels/w4.py:64-166)
+# ----------------------------------------------------------------------------
+
+def w4_sub(wgrp: int) -> int:
+    """w4.py:113: SUB = BLOCK_K if WGRP >= BLOCK_K else WGRP."""
+    return GROUP if wgrp >= GROUP else wgrp
+
+
+def gemm_w4_f32(a_q, a_s, b, b_s_bits, b_z=None, residual_f32=None) -> np.ndarray:
+    """fp32 result of gemm_w4 before the bf16 store (w4.py:124-134).
+
+    Per sub-block of ``SUB = min(WGRP, 64)`` at k0 (ascending):
+    ``out += float(int32 dot) * (a_s[m, k0/64] * float(ws[k0/WGRP, n]))``.
+    """
+    a_s = np.asarray(a_s, dtype=np.float32)
+    M, K = a_q.shape
+    ws = bf16_bits_to_f32(b_s_bits)
+    wgrp = K // ws.shape[0]
+    sub = w4_sub(wgrp)
+    w = unpack_w4(b, b_z, wgrp)
+    sums = _block_sums(a_q, w, sub)
+    N = w.shape[1]
+    out = np.zeros((M, N), dtype=np.float32)
+    for i in range(K // sub):
+        k0 = i * sub
+        sc = (a_s[:, k0 // GROUP][:, None] * ws[k0 // wgrp][None, :]).astype(np.float32)
+        prod = (sums[i].astype(np.float32) * sc).astype(np.float32)
+        out = (out + prod).astype(np.float32)
+    if residual_f32 is not None:
+        out = (out + residual_f32).astype(np.float32)
+    return out
+
+
+def gemm_w4(a_q, a_s, b, b_s_bits, b_z=None, residual_bits=None, mode="rne"):
+    """kernels/w4.py:139-166 -> bf16 bits [M,N]."""
+    res = None if residual_bits is None else bf16_bits_to_f32(residual_bits)
+    return f32_to_bf16_bits(gemm_w4_f32(a_q, a_s, b, b_s_bits, b_z, res), mode)
+
+
+# ----------------------------------------------------------------------------
+# a2 / a6: proj3  (kernels/gemm.py:234-312, kernels/w4.py:169-251)
+# ----------------------------------------------------------------------------
+
+def proj3(a_q, a_s, segs, mode="rne"):
+    """Three projections sharing A, written side by side (gemm.py:252-287).
+
+    ``segs`` is a list of ``(w, s, z)``; ``w`` int8 [K,N_i] (W8, ``s`` fp32
+    [N_i]) or uint8 [K/2,N_i] (W4, ``s`` bf16 bits [K/WG,N_i], ``z`` optional
+    zeros).  ``None`` entries are skipped (N_i = 0).  Returns bf16 bits
+    [M, sum N_i].
+    """
+    parts = []
+    for seg in segs:
+        if seg is None or seg[0] is None:
+            continue
+        w, s, z = seg
+        if w.dtype == np.uint8:
+            parts.append(gemm_w4(a_q, a_s, w, s, z, None, mode))
+        else:
+            parts.append(gemm_i8(a_q, a_s, w, s, None, mode))
+    return np.concatenate(parts, axis=1)
+
+
+# ----------------------------------------------------------------------------
+# a3 / a4 / a7: fused gate/up
+# ----------------------------------------------------------------------------
+
+def _gate_up_w8_h(a_q, a_s, wg, sg, wu, su):
+    """gemm.py:180-197: h = silu(g * sg) * (u * su), fp32."""
+    g = gemm_i8_f32(a_q, a_s, wg, np.ones_like(np.asarray(sg, dtype=np.float32)))
+    u = gemm_i8_f32(a_q, a_s, wu, np.ones_like(np.asarray(su, dtype=np.float32)))
+    # gemm_i8_f32 multiplies by 1.0 (exact); apply the real scales here in the
+    # reference order: silu(g * sg) * (u * su).
+    g = (g * np.asarray(sg, dtype=np.float32)[None, :]).astype(np.float32)
+    u = (u * np.asarray(su, dtype=np.float32)[None, :]).astype(np.float32)
+    return (silu(g) * u).astype(np.float32)
+
+
+def mlp_gate_up(a_q, a_s, wg, sg, wu, su, mode="rne"):
+    """kernels/gemm.py:95-151 -> bf16 bits [M,N]."""
+    return f32_to_bf16_bits(_gate_up_w8_h(a_q, a_s, wg, sg, wu, su), mode)
+
+
+def _quant_h(h, mode):
+    """gemm.py:198-211 / w4.py:285-297: round h through bf16, then per-64 quant."""
+    return quant_groups(bf16_round(h, mode))
+
+
+def mlp_gate_up_quant(a_q, a_s, wg, sg, wu, su, mode="rne"):
+    """kernels/gemm.py:154-231 -> (int8 [M,N], fp32 [M,N/64])."""
+    return _quant_h(_gate_up_w8_h(a_q, a_s, wg, sg, wu, su), mode)
+
+
+def mlp_gate_up_quant_w4(a_q, a_s, wg, sg_bits, wu, su_bits, zg=None, zu=None, mode="rne"):
+    """kernels/w4.py:254-323: g, u with scales inside the K loop, h = silu(g)*u."""
+    g = gemm_w4_f32(a_q, a_s, wg, sg_bits, zg)
+    u = gemm_w4_f32(a_q, a_s, wu, su_bits, zu)
+    h = (silu(g) * u).astype(np.float32)
+    return _quant_h(h, mode)
+
+
+# ----------------------------------------------------------------------------
+# CPU baseline: the reference's own dequant-then-matmul (.dev/test_kernels.py:40-41)
+# ----------------------------------------------------------------------------
+
+def dequant_matmul_w8(a_q, a_s, b, b_s):
+    """``(a_q.float() * a_s.repeat_interleave(64, 1)) @ b.float() * b_s`` (torch, CPU)."""
+    import torch
+    af = a_q.float() * a_s.repeat_interleave(GROUP, dim=1)
+    return (af @ b.float()) * b_s[None, :]
+
+
+def dequant_matmul_w4(a_q, a_s, b, b_s, b_z=None):
+    """The W4 analogue: dequantise ``(nibble - z) * scale`` then one fp32 matmul."""
+    import torch
+    K2, N = b.shape
+    K = 2 * K2
+    wgrp = K // b_s.shape[0]
+    nib = torch.empty((K, N), dtype=torch.int16)
+    nib[0::2] = (b & 0x0F).to(torch.int16)
+    nib[1::2] = (b >> 4).to(torch.int16)
+    z = torch.full((1, 1), 8, dtype=torch.int16) if b_z is None else b_z.to(torch.int16).repeat_interleave(wgrp, 0)
+    w = (nib - z).float() * b_s.float().repeat_interleave(wgrp, 0)
+    af = a_q.float() * a_s.repeat_interleave(GROUP, dim=1)
+    return af @ w

@@ -1,0 +1,73 @@
+"""ctypes binding of the qlin C ABI (``include/qlin.h``).
+
+The shared library ``libqlin.so`` is built in-tree next to this file by
+``build.py``.  There is no fallback: if the library is missing or fails to
+load, every entry point raises.
+"""
+import ctypes
+import os
+import threading
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libqlin.so")
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int64
+
+# name -> argument types (every function returns int status unless listed in _RESTYPES)
+SIGNATURES = {
+    "qlin_version": [],
+    "qlin_status_string": [ctypes.c_int],
+    "qlin_last_error": [],
+    "qlin_device_fault": [ctypes.c_int],
+    "qlin_gemm_i8": [_P, _P, _I, _I, _P, _P, _I, _P, _I, _P, _I, _P],
+    "qlin_gemm_w4": [_P, _P, _I, _I, _P, _P, _P, _I, _I, _P, _I, _P, _I, _P],
+    "qlin_proj3": [_P, _P, _I, _I, _P, _P, _I, _P, _P, _I, _P, _P, _I, _P, _I, _P],
+    "qlin_proj3_w4": [_P, _P, _I, _I, _P, _P, _P, _I, _P, _P, _P, _I, _P, _P, _P, _I, _I, _P, _I, _P],
+    "qlin_mlp_gate_up": [_P, _P, _I, _I, _P, _P, _P, _P, _I, _P, _I, _P],
+    "qlin_mlp_gate_up_quant": [_P, _P, _I, _I, _P, _P, _P, _P, _I, _P, _P, _P],
+    "qlin_mlp_gate_up_quant_w4": [_P, _P, _I, _I, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P],
+    "qlin_quant_row": [_P, _I, _I, _I, _P, _P, _P],
+}
+_RESTYPES = {
+    "qlin_status_string": ctypes.c_char_p,
+    "qlin_last_error": ctypes.c_char_p,
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load():
+    """Load (once) and return the ctypes handle of libqlin.so."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(
+                    f"qlin native library not found at {LIB_PATH}; build it first "
+                    "(python -c 'import __graft_entry__ as g; g.build()')")
+            lib = ctypes.CDLL(LIB_PATH)
+            for name, argtypes in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.argtypes = argtypes
+                fn.restype = _RESTYPES.get(name, ctypes.c_int)
+            _lib = lib
+    return _lib
+
+
+class QlinError(RuntimeError):
+    """A qlin entry point returned a non-zero status."""
+
+    def __init__(self, fn, status):
+        lib = load()
+        self.status = status
+        msg = lib.qlin_last_error().decode(errors="replace")
+        super().__init__(f"{fn}: {lib.qlin_status_string(status).decode()} ({status}): {msg}")
+
+
+def check(fn, status):
+    if status != 0:
+        raise QlinError(fn, status)

@@ -1,0 +1,525 @@
+// C ABI of the qlin library: argument validation, launch planning, TMA
+// descriptor encoding and kernel launch.  Declarations: include/qlin.h.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/qlin.h"
+#include "gemv.cuh"
+#include "quant.cuh"
+
+namespace qlin {
+
+__device__ unsigned int g_qlin_fault;
+
+namespace {
+
+constexpr int kVersion = 100;  // 0.1.0
+constexpr int kMaxDevices = 64;
+
+thread_local char g_err[512];
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(QLIN_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+// ---------------------------------------------------------------- device info
+struct DevInfo {
+  int sms = 0;
+  unsigned* fault = nullptr;
+};
+
+DevInfo g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+int device_info(DevInfo* out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(QLIN_ERR_UNSUPPORTED, "device index %d", dev);
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DevInfo& d = g_dev[dev];
+  if (d.sms == 0) {
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    void* fp = nullptr;
+    e = cudaGetSymbolAddress(&fp, g_qlin_fault);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_qlin_fault)");
+    d.fault = static_cast<unsigned*>(fp);
+    d.sms = sms;
+  }
+  *out = d;
+  return QLIN_OK;
+}
+
+// ---------------------------------------------------------------- TMA descriptors
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+int encode_fn(PFN_cuTensorMapEncodeTiled_v12000* fn) {
+  std::call_once(g_encode_once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  if (!g_encode) return fail(QLIN_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  *fn = g_encode;
+  return QLIN_OK;
+}
+
+// Row-major 2-D tensor [rows, cols] with `row_bytes` between rows, loaded in
+// boxes of [box_rows, box_cols].
+int make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t cols, uint64_t rows,
+             uint64_t row_bytes, uint32_t box_cols, uint32_t box_rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 fn;
+  if (int r = encode_fn(&fn)) return r;
+  const cuuint64_t gdim[2] = {cols, rows};
+  const cuuint64_t gstride[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estride[2] = {1, 1};
+  CUresult r = fn(m, dt, 2, const_cast<void*>(base), gdim, gstride, box, estride,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(QLIN_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) cols=%llu rows=%llu", (int)r,
+                (unsigned long long)cols, (unsigned long long)rows);
+  return QLIN_OK;
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// ---------------------------------------------------------------- GEMV planning / launch
+struct GemvPlan {
+  int split, ring, gmax;
+  size_t smem;
+};
+
+int gemv_mr(int64_t M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8; }
+
+// Choose the K split (cluster size) that spreads tiles x split CTAs most
+// evenly over the SMs, then the deepest ring that fits the per-CTA budget.
+GemvPlan plan_gemv(int wb, int mr, int ns, int K, int wgrp, int tiles, int rowblocks, int sms) {
+  const int G = K / kGroup;
+  GemvPlan best{1, 1, G, 0};
+  double best_cost = 1e30;
+  const int smax = G < 8 ? G : 8;
+  for (int s = 1; s <= smax; ++s) {
+    const int gmax = (G + s - 1) / s;
+    if (static_cast<long long>(gmax) * 64 * mr > 64 * 1024) continue;  // activation slice
+    const long long ctas = static_cast<long long>(tiles) * s * rowblocks;
+    const double waves = static_cast<double>((ctas + sms - 1) / sms);
+    const double cost = waves / s * (1.0 + 0.02 * s);
+    if (cost < best_cost - 1e-12) {
+      best_cost = cost;
+      best.split = s;
+      best.gmax = gmax;
+    }
+  }
+  const long long ctas = static_cast<long long>(tiles) * best.split * rowblocks;
+  const uint32_t budget = ctas <= sms ? 200 * 1024 : 100 * 1024;
+  const GemvLayout l1 = gemv_layout(wb, mr, ns, wgrp, best.gmax, 1);
+  const uint32_t fixed = l1.total - l1.ring_bytes;
+  int ring = static_cast<int>((budget > fixed ? budget - fixed : 0) / l1.stage_bytes);
+  if (ring < 2) ring = 2;
+  if (ring > best.gmax) ring = best.gmax;
+  best.ring = ring;
+  best.smem = gemv_layout(wb, mr, ns, wgrp, best.gmax, ring).total;
+  return best;
+}
+
+template <int WB, int MR, int EPI>
+int launch_gemv_t(const GemvArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
+  auto kern = gemv_kernel<WB, MR, EPI>;
+  static std::atomic<unsigned long long> configured{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(configured.load() & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(smem)");
+    configured.fetch_or(bit);
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kGemvThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = grid.x;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(gemv)");
+  return QLIN_OK;
+}
+
+template <int WB, int EPI>
+int launch_gemv_mr(int mr, const GemvArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
+  switch (mr) {
+    case 1: return launch_gemv_t<WB, 1, EPI>(a, grid, smem, st);
+    case 2: return launch_gemv_t<WB, 2, EPI>(a, grid, smem, st);
+    case 4: return launch_gemv_t<WB, 4, EPI>(a, grid, smem, st);
+    default: return launch_gemv_t<WB, 8, EPI>(a, grid, smem, st);
+  }
+}
+
+// Fills the split / ring fields of `a`, then launches.
+int run_gemv(int wb, int epi, GemvArgs& a, int tiles, cudaStream_t st) {
+  DevInfo di;
+  if (int r = device_info(&di)) return r;
+  const int mr = gemv_mr(a.M);
+  const int rowblocks = (a.M + mr - 1) / mr;
+  if (rowblocks > 65535 || tiles > 65535) return fail(QLIN_ERR_SHAPE, "grid too large (M=%d)", a.M);
+  const int ns = epi == kEpiOut ? 1 : 2;
+  const GemvPlan pl = plan_gemv(wb, mr, ns, a.K, a.wgrp, tiles, rowblocks, di.sms);
+  a.split = pl.split;
+  a.ring = pl.ring;
+  a.gmax = pl.gmax;
+  a.fault = di.fault;
+  const dim3 grid(pl.split, tiles, rowblocks);
+  if (wb == 8) {
+    switch (epi) {
+      case kEpiOut: return launch_gemv_mr<8, kEpiOut>(mr, a, grid, pl.smem, st);
+      case kEpiSiluBf16: return launch_gemv_mr<8, kEpiSiluBf16>(mr, a, grid, pl.smem, st);
+      default: return launch_gemv_mr<8, kEpiSiluQuant>(mr, a, grid, pl.smem, st);
+    }
+  }
+  switch (epi) {
+    case kEpiOut: return launch_gemv_mr<4, kEpiOut>(mr, a, grid, pl.smem, st);
+    default: return launch_gemv_mr<4, kEpiSiluQuant>(mr, a, grid, pl.smem, st);
+  }
+}
+
+// ---------------------------------------------------------------- argument checks
+int check_common(const int8_t* a_q, const float* a_s, int64_t M, int64_t K, int64_t N) {
+  if (M < 0 || K < 0 || N < 0) return fail(QLIN_ERR_INVALID_ARGUMENT, "negative size");
+  if (M > (1ll << 30) || K > (1ll << 30) || N > (1ll << 30)) return fail(QLIN_ERR_SHAPE, "size too large");
+  if (K == 0 || K % kGroup != 0) return fail(QLIN_ERR_SHAPE, "K=%lld must be a positive multiple of 64", (long long)K);
+  if (M > 0 && (!a_q || !a_s)) return fail(QLIN_ERR_INVALID_ARGUMENT, "null activation pointer");
+  if (!aligned(a_q, 16)) return fail(QLIN_ERR_ALIGNMENT, "a_q must be 16-byte aligned");
+  if (!aligned(a_s, 4)) return fail(QLIN_ERR_ALIGNMENT, "a_s must be 4-byte aligned");
+  return QLIN_OK;
+}
+
+int check_n(int64_t N) {
+  if (N % 16 != 0) return fail(QLIN_ERR_ALIGNMENT, "N=%lld must be a multiple of 16", (long long)N);
+  return QLIN_OK;
+}
+
+int check_wgrp(int64_t K, int64_t wgrp) {
+  if (!(wgrp == 32 || (wgrp >= 64 && wgrp % 64 == 0)) || K % wgrp != 0)
+    return fail(QLIN_ERR_SHAPE, "W4 group size %lld unsupported for K=%lld (32 or a multiple of 64)",
+                (long long)wgrp, (long long)K);
+  return QLIN_OK;
+}
+
+int seg_w8(GemvSeg& s, const int8_t* w, const float* bs, int64_t K, int64_t n) {
+  if (!w || !bs) return fail(QLIN_ERR_INVALID_ARGUMENT, "null W8 weight/scale pointer");
+  if (!aligned(w, 16)) return fail(QLIN_ERR_ALIGNMENT, "W8 weight must be 16-byte aligned");
+  if (!aligned(bs, 4)) return fail(QLIN_ERR_ALIGNMENT, "W8 scales must be 4-byte aligned");
+  if (int r = make_map(&s.tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, n, K, n, kTileN, 64)) return r;
+  s.bs = bs;
+  s.n = static_cast<int>(n);
+  s.has_z = 0;
+  return QLIN_OK;
+}
+
+int seg_w4(GemvSeg& s, const uint8_t* w, const void* sc, const uint8_t* z, int64_t K, int64_t n,
+           int64_t wgrp) {
+  if (!w || !sc) return fail(QLIN_ERR_INVALID_ARGUMENT, "null W4 weight/scale pointer");
+  if (!aligned(w, 16) || !aligned(sc, 16) || (z && !aligned(z, 16)))
+    return fail(QLIN_ERR_ALIGNMENT, "W4 weight/scale/zero tensors must be 16-byte aligned");
+  const uint32_t nsr = wgrp == 32 ? 2 : 1;
+  if (int r = make_map(&s.tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, n, K / 2, n, kTileN, 32)) return r;
+  if (int r = make_map(&s.ts, sc, CU_TENSOR_MAP_DATA_TYPE_UINT16, n, K / wgrp, 2 * n, kTileN, nsr)) return r;
+  if (z) {
+    if (int r = make_map(&s.tz, z, CU_TENSOR_MAP_DATA_TYPE_UINT8, n, K / wgrp, n, kTileN, nsr)) return r;
+  }
+  s.bs = nullptr;
+  s.n = static_cast<int>(n);
+  s.has_z = z ? 1 : 0;
+  return QLIN_OK;
+}
+
+int tiles_of(int64_t n) { return static_cast<int>((n + kTileN - 1) / kTileN); }
+
+}  // namespace
+}  // namespace qlin
+
+using namespace qlin;
+
+// =====================================================================================
+extern "C" {
+
+int qlin_version(void) { return kVersion; }
+
+const char* qlin_status_string(int s) {
+  switch (s) {
+    case QLIN_OK: return "ok";
+    case QLIN_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case QLIN_ERR_SHAPE: return "unsupported shape";
+    case QLIN_ERR_ALIGNMENT: return "misaligned pointer or stride";
+    case QLIN_ERR_UNSUPPORTED: return "unsupported";
+    case QLIN_ERR_CUDA: return "CUDA error";
+    case QLIN_ERR_DEVICE_FAULT: return "device-side wait timed out";
+    default: return "unknown status";
+  }
+}
+
+const char* qlin_last_error(void) { return g_err; }
+
+int qlin_device_fault(int clear) {
+  DevInfo di;
+  if (device_info(&di) != QLIN_OK) return -1;
+  unsigned v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_qlin_fault, sizeof(v)) != cudaSuccess) return -1;
+  if (clear) {
+    const unsigned z = 0;
+    if (cudaMemcpyToSymbol(g_qlin_fault, &z, sizeof(z)) != cudaSuccess) return -1;
+  }
+  return static_cast<int>(v);
+}
+
+int qlin_gemm_i8(const int8_t* a_q, const float* a_s, int64_t M, int64_t K, const int8_t* b,
+                 const float* b_s, int64_t N, void* out, int64_t ldo, const void* residual,
+                 int64_t ldr, void* stream) {
+  if (int r = check_common(a_q, a_s, M, K, N)) return r;
+  if (int r = check_n(N)) return r;
+  if (M == 0 || N == 0) return QLIN_OK;
+  if (!out) return fail(QLIN_ERR_INVALID_ARGUMENT, "null out");
+  if (ldo < N || (residual && ldr < N)) return fail(QLIN_ERR_SHAPE, "row stride smaller than N");
+  GemvArgs a;
+  memset(&a, 0, sizeof(a));
+  if (int r = seg_w8(a.seg[0], b, b_s, K, N)) return r;
+  a.nseg = 1;
+  a.a_q = a_q;
+  a.a_s = a_s;
+  a.M = static_cast<int>(M);
+  a.K = static_cast<int>(K);
+  a.wgrp = 64;
+  a.out = out;
+  a.ldo = ldo;
+  a.res = residual;
+  a.ldr = residual ? ldr : 0;
+  return run_gemv(8, kEpiOut, a, tiles_of(N), static_cast<cudaStream_t>(stream));
+}
+
+int qlin_gemm_w4(const int8_t* a_q, const float* a_s, int64_t M, int64_t K, const uint8_t* b,
+                 const void* b_s, const uint8_t* b_z, int64_t N, int64_t wgrp, void* out, int64_t ldo,
+                 const void* residual, int64_t ldr, void* stream) {
+  if (int r = check_common(a_q, a_s, M, K, N)) return r;
+  if (int r = check_n(N)) return r;
+  if (int r = check_wgrp(K, wgrp)) return r;
+  if (M == 0 || N == 0) return QLIN_OK;
+  if (!out) return fail(QLIN_ERR_INVALID_ARGUMENT, "null out");
+  if (ldo < N || (residual && ldr < N)) return fail(QLIN_ERR_SHAPE, "row stride smaller than N");
+  GemvArgs a;
+  memset(&a, 0, sizeof(a));
+  if (int r = seg_w4(a.seg[0], b, b_s, b_z, K, N, wgrp)) return r;
+  a.nseg = 1;
+  a.a_q = a_q;
+  a.a_s = a_s;
+  a.M = static_cast<int>(M);
+  a.K = static_cast<int>(K);
+  a.wgrp = static_cast<int>(wgrp);
+  a.out = out;
+  a.ldo = ldo;
+  a.res = residual;
+  a.ldr = residual ? ldr : 0;
+  return run_gemv(4, kEpiOut, a, tiles_of(N), static_cast<cudaStream_t>(stream));
+}
+
+int qlin_proj3(const int8_t* a_q, const float* a_s, int64_t M, int64_t K, const int8_t* w1,
+               const float* s1, int64_t n1, const int8_t* w2, const float* s2, int64_t n2,
+               const int8_t* w3, const float* s3, int64_t n3, void* out, int64_t ldo, void* stream) {
+  const int64_t ns[3] = {n1, n2, n3};
+  const int8_t* ws[3] = {w1, w2, w3};
+  const float* ss[3] = {s1, s2, s3};
+  const int64_t NT = n1 + n2 + n3;
+  if (int r = check_common(a_q, a_s, M, K, NT)) return r;
+  if (M == 0 || NT == 0) return QLIN_OK;
+  if (!out) return fail(QLIN_ERR_INVALID_ARGUMENT, "null out");
+  if (ldo < NT) return fail(QLIN_ERR_SHAPE, "row stride smaller than n1+n2+n3");
+  GemvArgs a;
+  memset(&a, 0, sizeof(a));
+  int tiles = 0, col = 0, k = 0;
+  for (int i = 0; i < 3; ++i) {
+    if (ns[i] < 0) return fail(QLIN_ERR_INVALID_ARGUMENT, "negative segment width");
+    if (ns[i] == 0) continue;
+    if (int r = check_n(ns[i])) return r;
+    if (int r = seg_w8(a.seg[k], ws[i], ss[i], K, ns[i])) return r;
+    a.seg[k].out_col = col;
+    a.seg[k].tile_begin = tiles;
+    col += static_cast<int>(ns[i]);
+    tiles += tiles_of(ns[i]);
+    ++k;
+  }
+  a.nseg = k;
+  a.a_q = a_q;
+  a.a_s = a_s;
+  a.M = static_cast<int>(M);
+  a.K = static_cast<int>(K);
+  a.wgrp = 64;
+  a.out = out;
+  a.ldo = ldo;
+  return run_gemv(8, kEpiOut, a, tiles, static_cast<cudaStream_t>(stream));
+}
+
+int qlin_proj3_w4(const int8_t* a_q, const float* a_s, int64_t M, int64_t K, const uint8_t* w1,
+                  const void* s1, const uint8_t* z1, int64_t n1, const uint8_t* w2, const void* s2,
+                  const uint8_t* z2, int64_t n2, const uint8_t* w3, const void* s3, const uint8_t* z3,
+                  int64_t n3, int64_t wgrp, void* out, int64_t ldo, void* stream) {
+  const int64_t ns[3] = {n1, n2, n3};
+  const uint8_t* ws[3] = {w1, w2, w3};
+  const void* ss[3] = {s1, s2, s3};
+  const uint8_t* zs[3] = {z1, z2, z3};
+  const int64_t NT = n1 + n2 + n3;
+  if (int r = check_common(a_q, a_s, M, K, NT)) return r;
+  if (int r = check_wgrp(K, wgrp)) return r;
+  if (M == 0 || NT == 0) return QLIN_OK;
+  if (!out) return fail(QLIN_ERR_INVALID_ARGUMENT, "null out");
+  if (ldo < NT) return fail(QLIN_ERR_SHAPE, "row stride smaller than n1+n2+n3");
+  GemvArgs a;
+  memset(&a, 0, sizeof(a));
+  int tiles = 0, col = 0, k = 0;
+  for (int i = 0; i < 3; ++i) {
+    if (ns[i] < 0) return fail(QLIN_ERR_INVALID_ARGUMENT, "negative segment width");
+    if (ns[i] == 0) continue;
+    if (int r = check_n(ns[i])) return r;
+    if (int r = seg_w4(a.seg[k], ws[i], ss[i], zs[i], K, ns[i], wgrp)) return r;
+    a.seg[k].out_col = col;
+    a.seg[k].tile_begin = tiles;
+    col += static_cast<int>(ns[i]);
+    tiles += tiles_of(ns[i]);
+    ++k;
+  }
+  a.nseg = k;
+  a.a_q = a_q;
+  a.a_s = a_s;
+  a.M = static_cast<int>(M);
+  a.K = static_cast<int>(K);
+  a.wgrp = static_cast<int>(wgrp);
+  a.out = out;
+  a.ldo = ldo;
+  return run_gemv(4, kEpiOut, a, tiles, static_cast<cudaStream_t>(stream));
+}
+
+static int gate_up_w8(const int8_t* a_q, const float* a_s, int64_t M, int64_t K, const int8_t* wg,
+                      const float* sg, const int8_t* wu, const float* su, int64_t N, int epi,
+                      void* out, int64_t ldo, int8_t* out_q, float* out_s, cudaStream_t st) {
+  if (int r = check_common(a_q, a_s, M, K, N)) return r;
+  if (int r = check_n(N)) return r;
+  if (M == 0 || N == 0) return QLIN_OK;
+  GemvArgs a;
+  memset(&a, 0, sizeof(a));
+  if (int r = seg_w8(a.seg[0], wg, sg, K, N)) return r;
+  if (int r = seg_w8(a.seg[1], wu, su, K, N)) return r;
+  a.nseg = 2;
+  a.a_q = a_q;
+  a.a_s = a_s;
+  a.M = static_cast<int>(M);
+  a.K = static_cast<int>(K);
+  a.wgrp = 64;
+  a.out = out;
+  a.ldo = ldo;
+  a.out_q = out_q;
+  a.out_s = out_s;
+  a.n_q = static_cast<int>(N);
+  return run_gemv(8, epi, a, tiles_of(N), st);
+}
+
+int qlin_mlp_gate_up(const int8_t* a_q, const float* a_s, int64_t M, int64_t K, const int8_t* wg,
+                     const float* sg, const int8_t* wu, const float* su, int64_t N, void* out,
+                     int64_t ldo, void* stream) {
+  if (M > 0 && N > 0 && !out) return fail(QLIN_ERR_INVALID_ARGUMENT, "null out");
+  if (ldo < N) return fail(QLIN_ERR_SHAPE, "row stride smaller than N");
+  return gate_up_w8(a_q, a_s, M, K, wg, sg, wu, su, N, kEpiSiluBf16, out, ldo, nullptr, nullptr,
+                    static_cast<cudaStream_t>(stream));
+}
+
+int qlin_mlp_gate_up_quant(const int8_t* a_q, const float* a_s, int64_t M, int64_t K,
+                           const int8_t* wg, const float* sg, const int8_t* wu, const float* su,
+                           int64_t N, int8_t* out_q, float* out_s, void* stream) {
+  if (N % 64 != 0) return fail(QLIN_ERR_SHAPE, "N=%lld must be a multiple of 64", (long long)N);
+  if (M > 0 && N > 0 && (!out_q || !out_s)) return fail(QLIN_ERR_INVALID_ARGUMENT, "null output");
+  return gate_up_w8(a_q, a_s, M, K, wg, sg, wu, su, N, kEpiSiluQuant, nullptr, 0, out_q, out_s,
+                    static_cast<cudaStream_t>(stream));
+}
+
+int qlin_mlp_gate_up_quant_w4(const int8_t* a_q, const float* a_s, int64_t M, int64_t K,
+                              const uint8_t* wg, const void* sg, const uint8_t* zg, const uint8_t* wu,
+                              const void* su, const uint8_t* zu, int64_t N, int64_t wgrp,
+                              int8_t* out_q, float* out_s, void* stream) {
+  if (int r = check_common(a_q, a_s, M, K, N)) return r;
+  if (int r = check_n(N)) return r;
+  if (int r = check_wgrp(K, wgrp)) return r;
+  if (N % 64 != 0) return fail(QLIN_ERR_SHAPE, "N=%lld must be a multiple of 64", (long long)N);
+  if (M == 0 || N == 0) return QLIN_OK;
+  if (!out_q || !out_s) return fail(QLIN_ERR_INVALID_ARGUMENT, "null output");
+  GemvArgs a;
+  memset(&a, 0, sizeof(a));
+  if (int r = seg_w4(a.seg[0], wg, sg, zg, K, N, wgrp)) return r;
+  if (int r = seg_w4(a.seg[1], wu, su, zu, K, N, wgrp)) return r;
+  a.nseg = 2;
+  a.a_q = a_q;
+  a.a_s = a_s;
+  a.M = static_cast<int>(M);
+  a.K = static_cast<int>(K);
+  a.wgrp = static_cast<int>(wgrp);
+  a.out_q = out_q;
+  a.out_s = out_s;
+  a.n_q = static_cast<int>(N);
+  return run_gemv(4, kEpiSiluQuant, a, tiles_of(N), static_cast<cudaStream_t>(stream));
+}
+
+int qlin_quant_row(const void* x, int64_t ldx, int64_t M, int64_t K, int8_t* q, float* s,
+                   void* stream) {
+  if (M < 0 || K < 0) return fail(QLIN_ERR_INVALID_ARGUMENT, "negative size");
+  if (K == 0 || K % kGroup != 0) return fail(QLIN_ERR_SHAPE, "K=%lld must be a positive multiple of 64", (long long)K);
+  if (M == 0) return QLIN_OK;
+  if (M > 65535) return fail(QLIN_ERR_SHAPE, "M=%lld too large", (long long)M);
+  if (!x || !q || !s) return fail(QLIN_ERR_INVALID_ARGUMENT, "null pointer");
+  if (ldx < K) return fail(QLIN_ERR_SHAPE, "row stride smaller than K");
+  if (!aligned(x, 4) || (ldx % 2) != 0 || !aligned(q, 2) || !aligned(s, 4))
+    return fail(QLIN_ERR_ALIGNMENT, "x needs 4-byte aligned rows, q 2-byte, s 4-byte alignment");
+  const int G = static_cast<int>(K / kGroup);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((G + kQuantWarps - 1) / kQuantWarps, static_cast<unsigned>(M), 1);
+  cfg.blockDim = dim3(kQuantWarps * 32, 1, 1);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, quant_row_kernel, static_cast<const __nv_bfloat16*>(x),
+                                     static_cast<long long>(ldx), static_cast<int>(M),
+                                     static_cast<int>(K), q, s);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(quant_row)");
+  return QLIN_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,160 @@
+// Shared device helpers for the qlin sm_100a kernels: mbarrier / TMA / PDL
+// wrappers written as inline PTX, integer dot helpers and the reference's
+// rounding rules.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace qlin {
+
+// Activation scale granularity along K (kernels/common.py:7 GROUP = 64).
+constexpr int kGroup = 64;
+
+// Fault bits written to g_qlin_fault by bounded waits that gave up.
+enum : unsigned {
+  kFaultFullWait = 1u,      // consumer waited too long for a TMA stage
+  kFaultEmptyWait = 2u,     // producer waited too long for a free ring slot
+  kFaultTmemAlloc = 4u,     // tensor-memory allocation wait
+  kFaultMmaWait = 8u,       // tcgen05 commit wait
+};
+
+// Bound on mbarrier polls; each failed poll sleeps ~64 ns after a short spin,
+// so a wait gives up after roughly a quarter of a second.
+constexpr uint32_t kWaitLimit = 1u << 22;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------- mbarrier
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase with the given parity to complete.  Returns false
+// (and leaves the barrier alone) if it did not complete within kWaitLimit polls.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (i >= 16) __nanosleep(64);
+  }
+  return false;
+}
+
+// ---------------------------------------------------------------- TMA
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+// 2-D tiled bulk tensor load global -> this CTA's shared memory, completing on
+// `bar` with the copied byte count.  x is the innermost (contiguous) coordinate
+// in elements; callers keep x * element size a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// ---------------------------------------------------------------- PDL
+// Programmatic dependent launch: wait for the preceding grid's results /
+// allow the next grid to start its prologue.  Both are no-ops when the kernel
+// was launched without the programmatic-serialization attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Named barrier over a subset of the CTA's warps (id 0 is __syncthreads).
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ---------------------------------------------------------------- integer dots
+// d = c + sum_i a.u8[i] * b.s8[i]
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+// d = c + sum_i a.s8[i] * b.s8[i]
+__device__ __forceinline__ int dp4a_ss(int a, int b, int c) { return __dp4a(a, b, c); }
+
+// 4x4 byte transpose: rows r0..r3 each hold 4 column bytes; on return c_j
+// holds column j's 4 bytes in row order (byte i = row i).
+__device__ __forceinline__ void transpose4x4(uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3,
+                                             uint32_t& c0, uint32_t& c1, uint32_t& c2,
+                                             uint32_t& c3) {
+  const uint32_t t0 = __byte_perm(r0, r1, 0x5140);  // a0 b0 a1 b1
+  const uint32_t t1 = __byte_perm(r0, r1, 0x7362);  // a2 b2 a3 b3
+  const uint32_t t2 = __byte_perm(r2, r3, 0x5140);  // c0 d0 c1 d1
+  const uint32_t t3 = __byte_perm(r2, r3, 0x7362);  // c2 d2 c3 d3
+  c0 = __byte_perm(t0, t2, 0x5410);
+  c1 = __byte_perm(t0, t2, 0x7632);
+  c2 = __byte_perm(t1, t3, 0x5410);
+  c3 = __byte_perm(t1, t3, 0x7632);
+}
+
+// ---------------------------------------------------------------- reference rounding
+// kernels/common.py:24-29: trunc(v + (v >= 0 ? 0.5 : -0.5)) clamped to [-127, 127].
+__device__ __forceinline__ int8_t round_i8(float v) {
+  const float t = __fadd_rn(v, v >= 0.0f ? 0.5f : -0.5f);
+  int r = __float2int_rz(t);
+  r = r > 127 ? 127 : (r < -127 ? -127 : r);
+  return static_cast<int8_t>(r);
+}
+
+// silu(x) = x * sigmoid(x), sigmoid = 1 / (1 + exp(-x)) (kernels/common.py:32-34,
+// Triton's sigmoid); IEEE division, library expf.
+__device__ __forceinline__ float silu_ref(float x) {
+  const float e = expf(-x);
+  const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
+  return __fmul_rn(x, sig);
+}
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint16_t h) {
+  return __uint_as_float(static_cast<uint32_t>(h) << 16);
+}
+__device__ __forceinline__ float bf16_round_f32(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+}  // namespace qlin

@@ -1,0 +1,38 @@
+// Per-64-group int8 activation quantisation (kernels/norm.py:15-25, 75-92).
+#pragma once
+
+#include "qlin_common.cuh"
+
+namespace qlin {
+
+constexpr int kQuantWarps = 8;
+
+// One warp per (row, 64-element group); lane l owns elements 2l and 2l+1.
+//   s = max(amax / 127, 1e-8)           IEEE division, as the reference's fp32 `/`
+//   q = round_i8(x / s)                 true division, round half away from zero
+__global__ void __launch_bounds__(kQuantWarps * 32) quant_row_kernel(
+    const __nv_bfloat16* __restrict__ x, long long ldx, int M, int K, int8_t* __restrict__ q,
+    float* __restrict__ s) {
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = K / kGroup;
+  const int g = blockIdx.x * kQuantWarps + warp;
+  const int row = blockIdx.y;
+  if (g < G) {
+    const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(
+        x + static_cast<long long>(row) * ldx + g * kGroup + 2 * lane);
+    const float a = __bfloat162float(v.x), b = __bfloat162float(v.y);
+    float amax = fmaxf(fabsf(a), fabsf(b));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float sc = fmaxf(__fdiv_rn(amax, 127.0f), 1e-8f);
+    char2 out;
+    out.x = round_i8(__fdiv_rn(a, sc));
+    out.y = round_i8(__fdiv_rn(b, sc));
+    *reinterpret_cast<char2*>(q + static_cast<long long>(row) * K + g * kGroup + 2 * lane) = out;
+    if (lane == 0) s[static_cast<long long>(row) * G + g] = sc;
+  }
+  pdl_launch_dependents();
+}
+
+}  // namespace qlin

@@ -1,0 +1,219 @@
+"""Generate golden input/output vectors by running the reference kernels on CPU.
+
+The reference's Triton kernels (``kernels/gemm.py``, ``kernels/w4.py``,
+``kernels/norm.py``) run on the CPU under Triton's interpreter
+(``TRITON_INTERPRET=1``).  This script imports them from a read-only checkout of
+the reference project, runs every hot-path entry point on small seeded inputs
+and stores inputs and outputs in ``ref_golden.npz`` next to this file.
+
+The interpreter converts fp32 -> bf16 by truncation (a GPU build rounds to
+nearest-even), so the fixtures pin the oracle in its ``mode="trunc"``; every
+other step of the arithmetic is shared by both modes.
+
+Usage (in a container that has the reference checkout)::
+
+    python tests/golden/make_golden.py [/path/to/reference]
+
+bf16 tensors are stored as uint16 bit patterns.  Nothing at test time reads
+the reference: the tests only load the committed ``.npz``.
+"""
+import os
+import sys
+import types
+
+os.environ["TRITON_INTERPRET"] = "1"
+sys.dont_write_bytecode = True
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+OUT = os.path.join(HERE, "ref_golden.npz")
+
+
+def import_reference(root):
+    """Register the reference checkout as package ``qwen35_prompt_enhancer``
+    without executing its ``__init__`` (which pulls in the ComfyUI node)."""
+    pkg = types.ModuleType("qwen35_prompt_enhancer")
+    pkg.__path__ = [root]
+    sys.modules["qwen35_prompt_enhancer"] = pkg
+    from qwen35_prompt_enhancer.kernels import gemm, norm, w4  # noqa: F401
+    return gemm, w4, norm
+
+
+def bits(t):
+    """bf16 torch tensor -> uint16 numpy bit pattern."""
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def main():
+    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    gemm, w4, norm = import_reference(root)
+    G = 64
+    rec = {}
+
+    def gen(seed):
+        g = torch.Generator().manual_seed(seed)
+        return g
+
+    def act(g, M, K, dist="ref"):
+        if dist == "ref":   # .dev/test_kernels.py:34-36
+            a = torch.randint(-127, 127, (M, K), dtype=torch.int8, generator=g)
+            s = torch.rand(M, K // G, generator=g) * 0.02
+            return a, s
+        x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+        q = torch.empty(M, K, dtype=torch.int8)
+        s = torch.empty(M, K // G, dtype=torch.float32)
+        norm.quant_row(x, q, s)
+        return q, s
+
+    def w8(g, K, N):
+        b = torch.randint(-127, 127, (K, N), dtype=torch.int8, generator=g)
+        bs = torch.rand(N, generator=g) * 0.002
+        return b, bs
+
+    def w4w(g, K, N, wg, zeros):
+        b = torch.randint(0, 256, (K // 2, N), dtype=torch.int32, generator=g).to(torch.uint8)
+        s = torch.exp(torch.randn(K // wg, N, generator=g) * 0.5 - 5.0).to(torch.bfloat16)
+        z = torch.randint(0, 16, (K // wg, N), dtype=torch.int32, generator=g).to(torch.uint8) if zeros else None
+        return b, s, z
+
+    # ---------------- a9: quant_row (norm.py:75-92), incl. outliers and zero groups
+    for i, (M, K) in enumerate([(3, 256), (5, 2048)]):
+        g = gen(100 + i)
+        x = torch.randn(M, K, generator=g)
+        x[torch.rand(M, K, generator=g) < 0.01] *= 20.0
+        x[0, 64:128] = 0.0                       # all-zero group -> scale 1e-8
+        x[-1, :4] = torch.tensor([0.5, -0.5, 1e-30, -3.0])
+        x = x.to(torch.bfloat16)
+        q = torch.empty(M, K, dtype=torch.int8)
+        s = torch.empty(M, K // G, dtype=torch.float32)
+        norm.quant_row(x, q, s)
+        p = f"quant_row_{i}_"
+        rec[p + "x"] = bits(x)
+        rec[p + "q"] = q.numpy()
+        rec[p + "s"] = s.numpy()
+
+    # ---------------- a1: gemm_i8 (gemm.py:60-92)
+    cases = [
+        (1, 192, 256, False, "ref"),
+        (4, 320, 512, True, "ref"),
+        (5, 208, 128, True, "x"),      # ragged N (not a multiple of the tile), quant_row acts
+        (37, 128, 256, False, "ref"),  # M > 16 -> reference's larger tile path
+    ]
+    for i, (M, N, K, res, dist) in enumerate(cases):
+        g = gen(200 + i)
+        a, s = act(g, M, K, dist)
+        b, bs = w8(g, K, N)
+        p = f"gemm_i8_{i}_"
+        if res:
+            # out is a row-slice of a wider buffer and aliases the residual,
+            # exactly as the engine calls it (engine.py:238-240).
+            buf = torch.randn(M, N + 48, generator=g).to(torch.bfloat16)
+            rec[p + "res"] = bits(buf[:, :N])
+            out = buf[:, :N]
+            gemm.gemm_i8(a, s, b, bs, out, residual=out)
+        else:
+            out = torch.empty(M, N, dtype=torch.bfloat16)
+            gemm.gemm_i8(a, s, b, bs, out)
+        rec[p + "a"] = a.numpy(); rec[p + "as"] = s.numpy()
+        rec[p + "b"] = b.numpy(); rec[p + "bs"] = bs.numpy()
+        rec[p + "out"] = bits(out)
+
+    # ---------------- a5: gemm_w4 (w4.py:139-166), groups 32/64/128, zeros on/off
+    cases = [
+        (1, 128, 256, 128, True, False),
+        (4, 192, 256, 64, False, True),
+        (3, 128, 256, 32, True, True),
+        (2, 256, 512, 256, True, False),
+    ]
+    for i, (M, N, K, wg, zeros, res) in enumerate(cases):
+        g = gen(300 + i)
+        a, s = act(g, M, K, "x")
+        b, bsc, bz = w4w(g, K, N, wg, zeros)
+        p = f"gemm_w4_{i}_"
+        out = torch.empty(M, N, dtype=torch.bfloat16)
+        r = None
+        if res:
+            r = torch.randn(M, N, generator=g).to(torch.bfloat16)
+            rec[p + "res"] = bits(r)
+        w4.gemm_w4(a, s, b, bsc, out, residual=r, b_z=bz)
+        rec[p + "a"] = a.numpy(); rec[p + "as"] = s.numpy()
+        rec[p + "b"] = b.numpy(); rec[p + "bs"] = bits(bsc)
+        if bz is not None:
+            rec[p + "bz"] = bz.numpy()
+        rec[p + "out"] = bits(out)
+
+    # ---------------- a2: proj3 W8 (gemm.py:290-312), out wider than N1+N2+N3
+    for i, (M, K, ns) in enumerate([(2, 256, (192, 64, 64)), (3, 128, (128, 64, 0))]):
+        g = gen(400 + i)
+        a, s = act(g, M, K, "ref")
+        ws = [w8(g, K, n) if n else (None, None) for n in ns]
+        out = torch.zeros(M, sum(ns) + 64, dtype=torch.bfloat16)
+        gemm.proj3(a, s, ws[0][0], ws[0][1], ws[1][0], ws[1][1], ws[2][0], ws[2][1], out)
+        p = f"proj3_{i}_"
+        rec[p + "a"] = a.numpy(); rec[p + "as"] = s.numpy()
+        for j, (w, sc) in enumerate(ws):
+            if w is not None:
+                rec[p + f"w{j}"] = w.numpy(); rec[p + f"s{j}"] = sc.numpy()
+        rec[p + "out"] = bits(out)
+
+    # ---------------- a6: proj3_w4 (w4.py:220-251)
+    for i, (M, K, ns, wg, zeros) in enumerate([(1, 256, (128, 64, 64), 128, True),
+                                                (4, 256, (192, 64, 0), 64, False)]):
+        g = gen(500 + i)
+        a, s = act(g, M, K, "x")
+        ws = [w4w(g, K, n, wg, zeros) if n else (None, None, None) for n in ns]
+        out = torch.zeros(M, sum(ns) + 32, dtype=torch.bfloat16)
+        w4.proj3_w4(a, s, ws[0][0], ws[0][1], ws[1][0], ws[1][1], ws[2][0], ws[2][1], out,
+                    z1=ws[0][2], z2=ws[1][2], z3=ws[2][2])
+        p = f"proj3_w4_{i}_"
+        rec[p + "a"] = a.numpy(); rec[p + "as"] = s.numpy()
+        for j, (w, sc, z) in enumerate(ws):
+            if w is not None:
+                rec[p + f"w{j}"] = w.numpy(); rec[p + f"s{j}"] = bits(sc)
+                if z is not None:
+                    rec[p + f"z{j}"] = z.numpy()
+        rec[p + "out"] = bits(out)
+
+    # ---------------- a4 / a3: mlp_gate_up (bf16) and mlp_gate_up_quant (gemm.py:140-231)
+    for i, (M, K, N) in enumerate([(1, 256, 192), (5, 128, 128)]):
+        g = gen(600 + i)
+        a, s = act(g, M, K, "ref")
+        wg_, sg = w8(g, K, N)
+        wu_, su = w8(g, K, N)
+        h = torch.empty(M, N, dtype=torch.bfloat16)
+        gemm.mlp_gate_up(a, s, wg_, sg, wu_, su, h)
+        q = torch.empty(M, N, dtype=torch.int8)
+        qs = torch.empty(M, N // G, dtype=torch.float32)
+        gemm.mlp_gate_up_quant(a, s, wg_, sg, wu_, su, q, qs)
+        p = f"gate_up_{i}_"
+        rec[p + "a"] = a.numpy(); rec[p + "as"] = s.numpy()
+        rec[p + "wg"] = wg_.numpy(); rec[p + "sg"] = sg.numpy()
+        rec[p + "wu"] = wu_.numpy(); rec[p + "su"] = su.numpy()
+        rec[p + "h"] = bits(h); rec[p + "q"] = q.numpy(); rec[p + "qs"] = qs.numpy()
+
+    # ---------------- a7: mlp_gate_up_quant_w4 (w4.py:300-323)
+    for i, (M, K, N, wg, zeros) in enumerate([(1, 256, 128, 128, True), (4, 256, 192, 64, False),
+                                               (2, 128, 128, 32, True)]):
+        g = gen(700 + i)
+        a, s = act(g, M, K, "x")
+        wgt, sg, zg = w4w(g, K, N, wg, zeros)
+        wut, su, zu = w4w(g, K, N, wg, zeros)
+        q = torch.empty(M, N, dtype=torch.int8)
+        qs = torch.empty(M, N // G, dtype=torch.float32)
+        w4.mlp_gate_up_quant_w4(a, s, wgt, sg, wut, su, q, qs, zg=zg, zu=zu)
+        p = f"gate_up_w4_{i}_"
+        rec[p + "a"] = a.numpy(); rec[p + "as"] = s.numpy()
+        rec[p + "wg"] = wgt.numpy(); rec[p + "sg"] = bits(sg)
+        rec[p + "wu"] = wut.numpy(); rec[p + "su"] = bits(su)
+        if zeros:
+            rec[p + "zg"] = zg.numpy(); rec[p + "zu"] = zu.numpy()
+        rec[p + "q"] = q.numpy(); rec[p + "qs"] = qs.numpy()
+
+    np.savez_compressed(OUT, **rec)
+    print(f"wrote {OUT}: {len(rec)} arrays, {os.path.getsize(OUT)} bytes")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,50 @@
+"""Host-side logic of the Python mirror: dispatch and argument validation
+(no kernels are launched: every case fails before reaching the C ABI)."""
+import pytest
+import torch
+
+
+def test_reference_names_exported(pkg):
+    for name in ("gemm_i8", "mlp_gate_up", "mlp_gate_up_quant", "proj3", "gemm_w4", "proj3_w4",
+                 "mlp_gate_up_quant_w4", "quant_row", "GROUP"):
+        assert hasattr(pkg, name)
+    assert pkg.GROUP == 64
+
+
+def test_cpu_tensors_rejected(pkg):
+    a = torch.zeros(1, 64, dtype=torch.int8)
+    s = torch.zeros(1, 1)
+    b = torch.zeros(64, 128, dtype=torch.int8)
+    bs = torch.zeros(128)
+    out = torch.zeros(1, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        pkg.gemm_i8(a, s, b, bs, out)
+
+
+def test_w4_dispatch_on_uint8(pkg, monkeypatch):
+    """uint8 weights route gemm_i8 -> gemm_w4 (kernels/gemm.py:69-72)."""
+    from qwen35_b200.kernels import gemm as G
+    seen = {}
+
+    def fake(*args, **kw):
+        seen["w4"] = True
+        return "w4"
+
+    monkeypatch.setattr(G, "gemm_w4", fake)
+    b = torch.zeros(32, 128, dtype=torch.uint8)
+    assert G.gemm_i8(None, None, b, None, None) == "w4" and seen["w4"]
+
+
+def test_gate_up_and_proj3_dispatch(pkg, monkeypatch):
+    from qwen35_b200.kernels import gemm as G
+    monkeypatch.setattr(G, "mlp_gate_up_quant_w4", lambda *a, **k: "gu4")
+    monkeypatch.setattr(G, "proj3_w4", lambda *a, **k: "p34")
+    w = torch.zeros(32, 128, dtype=torch.uint8)
+    assert G.mlp_gate_up_quant(None, None, w, None, w, None, None, None) == "gu4"
+    assert G.proj3(None, None, w, None, None, None, None, None, None) == "p34"
+
+
+def test_block_k_must_be_group(pkg):
+    a = torch.zeros(1, 64, dtype=torch.int8)
+    with pytest.raises(ValueError, match="block_k"):
+        pkg.gemm_i8(a, None, torch.zeros(64, 16, dtype=torch.int8), None, None, block_k=32)
