@@ -134,7 +134,11 @@ GemvPlan plan_gemv(int wb, int mr, int ns, int K, int wgrp, int tiles, int rowbl
     }
   }
   const long long ctas = static_cast<long long>(tiles) * best.split * rowblocks;
-  const uint32_t budget = ctas <= sms ? 200 * 1024 : 100 * 1024;
+  // ~110 KB per CTA keeps two CTAs resident per SM: one of this grid and
+  // one of the next launch, which then streams its weights under PDL while
+  // this one finishes.
+  (void)ctas;
+  const uint32_t budget = 110 * 1024;
   const GemvLayout l1 = gemv_layout(wb, mr, ns, wgrp, best.gmax, 1);
   const uint32_t fixed = l1.total - l1.ring_bytes;
   int ring = static_cast<int>((budget > fixed ? budget - fixed : 0) / l1.stage_bytes);

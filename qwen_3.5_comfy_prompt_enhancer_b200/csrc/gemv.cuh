@@ -18,8 +18,8 @@
 //
 // Inside a CTA one producer warp streams the tile's weight rows (and W4
 // group scales / zeros) with 2-D TMA loads into a ring of shared-memory
-// stages, one stage per 64-row activation group.  Eight consumer warps take
-// stages round-robin; in a warp each lane owns 4 adjacent columns and runs
+// stages, one stage per 64-row activation group.  Eight consumer warps own
+// the ring slots round-robin; in a warp each lane owns 4 adjacent columns and runs
 // over all 64 K rows of the group, so the int32 sum of every
 // (row, column, group) is formed completely inside one thread -- exactly the
 // reference's per-64-block `tl.dot` (kernels/gemm.py:43, kernels/w4.py:89)
@@ -69,6 +69,7 @@ struct GemvArgs {
   int M, K, wgrp;
   int split;          // K ranges per tile == cluster size
   int ring;           // stages in the shared-memory ring
+  int aring;          // tcgen05 W4 path: stages of the unpacked-weight ring
   int gmax;           // max groups one CTA handles
   void* out;          // bf16, row stride ldo
   long long ldo;
@@ -243,7 +244,7 @@ __device__ __forceinline__ void w4_group(const uint8_t* __restrict__ st, uint32_
 // The kernel.
 // ---------------------------------------------------------------------------
 template <int WB, int MR, int EPI>
-__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_constant__ GemvArgs p) {
+__global__ void __launch_bounds__(kGemvThreads, (MR <= 4 ? 2 : 1)) gemv_kernel(const __grid_constant__ GemvArgs p) {
   namespace cg = cooperative_groups;
   constexpr int NS = (EPI == kEpiOut) ? 1 : 2;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -268,6 +269,22 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
   const int g0 = static_cast<int>(static_cast<long long>(rank) * G / p.split);
   const int g1 = static_cast<int>(static_cast<long long>(rank + 1) * G / p.split);
   const int nst = g1 - g0;
+
+  // Epilogue operands, fetched early by the epilogue threads (rank 0,
+  // threads 0..127) so that no global round trip is left after the K loop:
+  // W8 column scales now (weights never depend on the preceding kernel), the
+  // residual right after the grid-dependency wait.
+  const bool epi_thread = (rank == 0) && (threadIdx.x < kTileN);
+  const int en = n0 + static_cast<int>(threadIdx.x);
+  const bool evalid = epi_thread && en < S0.n;
+  float pre_s0 = 1.0f, pre_s1 = 1.0f;
+  if (WB == 8 && evalid) {
+    pre_s0 = __ldg((NS == 1 ? S0.bs : p.seg[0].bs) + en);
+    if (NS == 2) pre_s1 = __ldg(p.seg[1].bs + en);
+  }
+  float pre_res[MR];
+#pragma unroll
+  for (int m = 0; m < MR; ++m) pre_res[m] = 0.0f;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < p.ring; ++i) {
@@ -317,6 +334,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
     // ------------------------------------------------------------ consumers
     pdl_wait();
     const int tid = threadIdx.x;
+    if (EPI == kEpiOut && evalid && p.res) {
+      const __nv_bfloat16* res = reinterpret_cast<const __nv_bfloat16*>(p.res);
+#pragma unroll
+      for (int m = 0; m < MR; ++m)
+        if (m0 + m < p.M)
+          pre_res[m] = __bfloat162float(res[static_cast<long long>(m0 + m) * p.ldr + S0.out_col + en]);
+    }
     int* actw = reinterpret_cast<int*>(smem + L.act_off);
     int* asum = reinterpret_cast<int*>(smem + L.asum_off);
     float* ass = reinterpret_cast<float*>(smem + L.as_off);
@@ -376,8 +400,12 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[s][m][j] = 0.0f;
 
-    for (int i = warp; i < nst; i += kConsumerWarps) {
+    // Ring slot s is always consumed by warp s % kConsumerWarps, so every slot's
+    // fills are waited for in order by one warp (an mbarrier parity wait is
+    // only unambiguous when the previous phase has been observed).
+    for (int i = 0; i < nst; ++i) {
       const int slot = i % p.ring;
+      if (slot % kConsumerWarps != warp) continue;
       if (!mbar_wait(full + slot, (i / p.ring) & 1)) {
         if (lane == 0) atomicOr(p.fault, kFaultFullWait);
         break;
@@ -435,25 +463,17 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
         for (int m = 0; m < MR; ++m) vs[s][m] = __fadd_rn(vs[s][m], rp[(s * MR + m) * kTileN + c]);
     }
     if (EPI == kEpiOut) {
-      float bsv = 1.0f;
-      if (WB == 8) bsv = valid ? __ldg(S0.bs + n) : 0.0f;
       __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
-      const __nv_bfloat16* res = reinterpret_cast<const __nv_bfloat16*>(p.res);
 #pragma unroll
       for (int m = 0; m < MR; ++m) {
         if (!valid || m0 + m >= p.M) continue;
         float v = vs[0][m];
-        if (WB == 8) v = __fmul_rn(v, bsv);  // out * bs (kernels/gemm.py:51-52)
-        const long long col = S0.out_col + n;
-        if (res) v = __fadd_rn(v, __bfloat162float(res[static_cast<long long>(m0 + m) * p.ldr + col]));
-        out[static_cast<long long>(m0 + m) * p.ldo + col] = __float2bfloat16_rn(v);
+        if (WB == 8) v = __fmul_rn(v, pre_s0);  // out * bs (kernels/gemm.py:51-52)
+        if (p.res) v = __fadd_rn(v, pre_res[m]);
+        out[static_cast<long long>(m0 + m) * p.ldo + S0.out_col + n] = __float2bfloat16_rn(v);
       }
     } else {
-      float sg = 1.0f, su = 1.0f;
-      if (WB == 8 && valid) {
-        sg = __ldg(p.seg[0].bs + n);
-        su = __ldg(p.seg[1].bs + n);
-      }
+      const float sg = pre_s0, su = pre_s1;
       float* xchg = reinterpret_cast<float*>(smem + L.xchg_off);
 #pragma unroll
       for (int m = 0; m < MR; ++m) {
