@@ -8,11 +8,13 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <cstdlib>
 #include <mutex>
 
 #include "../../include/qlin.h"
 #include "gemv.cuh"
 #include "quant.cuh"
+#include "tcgemv.cuh"
 
 namespace qlin {
 
@@ -88,7 +90,7 @@ int encode_fn(PFN_cuTensorMapEncodeTiled_v12000* fn) {
 // Row-major 2-D tensor [rows, cols] with `row_bytes` between rows, loaded in
 // boxes of [box_rows, box_cols].
 int make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t cols, uint64_t rows,
-             uint64_t row_bytes, uint32_t box_cols, uint32_t box_rows) {
+             uint64_t row_bytes, uint32_t box_cols, uint32_t box_rows, bool sw128 = false) {
   PFN_cuTensorMapEncodeTiled_v12000 fn;
   if (int r = encode_fn(&fn)) return r;
   const cuuint64_t gdim[2] = {cols, rows};
@@ -96,7 +98,8 @@ int make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t 
   const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t estride[2] = {1, 1};
   CUresult r = fn(m, dt, 2, const_cast<void*>(base), gdim, gstride, box, estride,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  sw128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(QLIN_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) cols=%llu rows=%llu", (int)r,
@@ -105,6 +108,16 @@ int make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t 
 }
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Kernel family for the small-M path: tcgen05 weight streaming (default) or
+// the CUDA-core dp4a GEMV (QLIN_SMALLM_KERNEL=dp4a, kept for comparison).
+bool use_tc() {
+  static const bool tc = [] {
+    const char* e = getenv("QLIN_SMALLM_KERNEL");
+    return !(e && strcmp(e, "dp4a") == 0);
+  }();
+  return tc;
+}
 
 // ---------------------------------------------------------------- GEMV planning / launch
 struct GemvPlan {
@@ -190,8 +203,133 @@ int launch_gemv_mr(int mr, const GemvArgs& a, dim3 grid, size_t smem, cudaStream
   }
 }
 
+// ---------------------------------------------------------------- tcgen05 path planning / launch
+// Activation rows per row block: 1..16, and 32 for W8 (the W4 drain of 32
+// rows does not fit its register budget).
+int tc_mr(int wb, int64_t M) {
+  const int mr = M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : M <= 8 ? 8 : M <= 16 ? 16 : 32;
+  return (wb == 4 && mr > 16) ? 16 : mr;
+}
+
+struct TcPlan {
+  int split, ring, aring, gmax;
+  size_t smem;
+};
+
+TcPlan plan_tc(int wb, int mr, int ns, int K, int wgrp, int tiles, int rowblocks, int sms) {
+  const int G = K / kGroup;
+  const int nm = mr < 16 ? 16 : mr;
+  TcPlan best{1, 1, wb == 4 ? 4 : 0, G, 0};
+  double best_cost = 1e30;
+  const int smax = G < 8 ? G : 8;
+  for (int s = 1; s <= smax; ++s) {
+    const int gmax = (G + s - 1) / s;
+    if (static_cast<long long>(gmax) * 64 * nm > 48 * 1024) continue;  // activation operand
+    const long long ctas = static_cast<long long>(tiles) * s * rowblocks;
+    const double waves = static_cast<double>((ctas + sms - 1) / sms);
+    const double cost = waves / s * (1.0 + 0.02 * s);
+    if (cost < best_cost - 1e-12) {
+      best_cost = cost;
+      best.split = s;
+      best.gmax = gmax;
+    }
+  }
+  // ~100 KB per CTA: two CTAs per SM (this launch and the next one under PDL).
+  const uint32_t budget = 100 * 1024;
+  const TcLayout l1 = tc_layout(wb, nm, ns, wgrp, best.gmax, 1, best.aring);
+  const uint32_t fixed = l1.total - l1.raw_stage;
+  int ring = static_cast<int>((budget > fixed ? budget - fixed : 0) / l1.raw_stage);
+  if (ring < 2) ring = 2;
+  if (ring > best.gmax) ring = best.gmax;
+  best.ring = ring;
+  const TcLayout L = tc_layout(wb, nm, ns, wgrp, best.gmax, ring, best.aring);
+  // At most 512 / tmem_cols CTAs may share an SM, or a tensor-memory
+  // allocation could wait on a CTA of the next launch: pad shared memory so
+  // that no more CTAs than that fit.
+  const uint32_t max_ctas = 512 / L.tmem_cols;
+  uint32_t smem = L.total;
+  const uint32_t floor_smem = (228 * 1024) / (max_ctas + 1) - 1024 + 16;
+  if (smem < floor_smem) smem = floor_smem;
+  best.smem = smem;
+  return best;
+}
+
+template <int WB, int MR, int EPI>
+int launch_tc_t(const GemvArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
+  auto kern = tc_gemv_kernel<WB, MR, EPI>;
+  static std::atomic<unsigned long long> configured{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(configured.load() & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(smem)");
+    configured.fetch_or(bit);
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(tc_threads(WB), 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = grid.x;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(tc_gemv)");
+  return QLIN_OK;
+}
+
+template <int WB, int EPI>
+int launch_tc_mr(int mr, const GemvArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
+  switch (mr) {
+    case 1: return launch_tc_t<WB, 1, EPI>(a, grid, smem, st);
+    case 2: return launch_tc_t<WB, 2, EPI>(a, grid, smem, st);
+    case 4: return launch_tc_t<WB, 4, EPI>(a, grid, smem, st);
+    case 8: return launch_tc_t<WB, 8, EPI>(a, grid, smem, st);
+    case 16: return launch_tc_t<WB, 16, EPI>(a, grid, smem, st);
+    default:
+      if constexpr (WB == 8) return launch_tc_t<WB, 32, EPI>(a, grid, smem, st);
+      return fail(QLIN_ERR_UNSUPPORTED, "row block %d", mr);
+  }
+}
+
+int run_tc(int wb, int epi, GemvArgs& a, int tiles, cudaStream_t st) {
+  DevInfo di;
+  if (int r = device_info(&di)) return r;
+  const int mr = tc_mr(wb, a.M);
+  const int nm = mr < 16 ? 16 : mr;
+  const int rowblocks = (a.M + nm - 1) / nm;
+  if (rowblocks > 65535 || tiles > 65535) return fail(QLIN_ERR_SHAPE, "grid too large (M=%d)", a.M);
+  const int ns = epi == kEpiOut ? 1 : 2;
+  const TcPlan pl = plan_tc(wb, mr, ns, a.K, a.wgrp, tiles, rowblocks, di.sms);
+  a.split = pl.split;
+  a.ring = pl.ring;
+  a.aring = pl.aring;
+  a.gmax = pl.gmax;
+  a.fault = di.fault;
+  const dim3 grid(pl.split, tiles, rowblocks);
+  if (wb == 8) {
+    switch (epi) {
+      case kEpiOut: return launch_tc_mr<8, kEpiOut>(mr, a, grid, pl.smem, st);
+      case kEpiSiluBf16: return launch_tc_mr<8, kEpiSiluBf16>(mr, a, grid, pl.smem, st);
+      default: return launch_tc_mr<8, kEpiSiluQuant>(mr, a, grid, pl.smem, st);
+    }
+  }
+  switch (epi) {
+    case kEpiOut: return launch_tc_mr<4, kEpiOut>(mr, a, grid, pl.smem, st);
+    default: return launch_tc_mr<4, kEpiSiluQuant>(mr, a, grid, pl.smem, st);
+  }
+}
+
 // Fills the split / ring fields of `a`, then launches.
 int run_gemv(int wb, int epi, GemvArgs& a, int tiles, cudaStream_t st) {
+  if (use_tc()) return run_tc(wb, epi, a, tiles, st);
   DevInfo di;
   if (int r = device_info(&di)) return r;
   const int mr = gemv_mr(a.M);
@@ -244,7 +382,9 @@ int seg_w8(GemvSeg& s, const int8_t* w, const float* bs, int64_t K, int64_t n) {
   if (!w || !bs) return fail(QLIN_ERR_INVALID_ARGUMENT, "null W8 weight/scale pointer");
   if (!aligned(w, 16)) return fail(QLIN_ERR_ALIGNMENT, "W8 weight must be 16-byte aligned");
   if (!aligned(bs, 4)) return fail(QLIN_ERR_ALIGNMENT, "W8 scales must be 4-byte aligned");
-  if (int r = make_map(&s.tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, n, K, n, kTileN, 64)) return r;
+  // 128-byte swizzle: the tile lands in the canonical MN-major layout that
+  // tcgen05.mma reads (the dp4a kernel reads plain rows).
+  if (int r = make_map(&s.tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, n, K, n, kTileN, 64, use_tc())) return r;
   s.bs = bs;
   s.n = static_cast<int>(n);
   s.has_z = 0;

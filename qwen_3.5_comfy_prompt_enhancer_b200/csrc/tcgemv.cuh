@@ -1,0 +1,474 @@
+// Weight-streaming tensor-core kernel (tcgen05, kind::i8) for the quantised
+// hot path at small M (decode and short prefill chunks; up to 32 activation
+// rows per row block).
+//
+// Orientation.  The MMA computes D[n, m] = sum_k W[k, n] * a[m, k] with the
+// weight tile as operand A (M_mma = 128 output columns, MN-major: the
+// engine's [K, N] weight rows are N-contiguous, which tcgen05 reads directly
+// through a 128-byte-swizzled MN-major descriptor -- no transpose anywhere)
+// and the activations as operand B (N_mma = 16 or 32 rows, K-major).  The
+// int32 accumulator of each 64-element activation group lives in tensor
+// memory; drain warps read it back, apply the per-(row, group) activation
+// scale and accumulate fp32 in registers -- the reference's per-64-block
+// `tl.dot` followed by `out += acc * a_s` (kernels/gemm.py:40-49,
+// kernels/w4.py:125-130).  Integer sums are exact; only the fp32 order of
+// the K-split reduction differs from the reference.
+//
+// Warp roles (one CTA = one 128-column tile x one K range):
+//   warp 0      TMA producer: weight rows (+ W4 group scales / zeros) into a
+//               ring of shared-memory stages, one stage per 64-K group.
+//   warp 1      tensor-memory owner and MMA issuer (one thread).
+//   warps 2-5   drain: stage the activation operand, then per group read the
+//               int32 accumulator (thread = output column), rescale, sum;
+//               finally the epilogue.
+//   warps 6-9   (W4 only) unpack: packed nibbles -> uint8 rows of the
+//               swizzled A tile.  Low nibble of packed row j is K = 2j, high
+//               nibble K = 2j+1.  The MMA multiplies unsigned nibbles with
+//               signed activations; the zero point is removed exactly in
+//               integers by the drain: sum(a*(nib - z)) = sum(a*nib) - z*sum(a).
+//
+// Split-K across the CTAs of a thread-block cluster, combined through
+// distributed shared memory in a fixed order (no global scratch), as in
+// gemv.cuh.  PDL: weights stream before griddepcontrol.wait.
+#pragma once
+
+#include <cooperative_groups.h>
+
+#include "gemv.cuh"
+#include "qlin_common.cuh"
+
+namespace qlin {
+
+constexpr int kTcWarpTma = 0;
+constexpr int kTcWarpMma = 1;
+constexpr int kTcWarpDrain = 2;   // 4 warps
+constexpr int kTcWarpUnpack = 6;  // 4 warps (W4)
+constexpr int kDrainThreads = 128;
+
+__host__ __device__ constexpr int tc_threads(int wb) { return (wb == 8 ? 6 : 10) * 32; }
+
+struct TcLayout {
+  uint32_t nsub, raw_stream, raw_stage, raw_off, a_off, b_off, as_off, asum_off, part_off, xchg_off,
+      bar_off, tmem_slot_off, total, tmem_cols;
+};
+
+__host__ __device__ inline uint32_t pow2_at_least(uint32_t x) {
+  uint32_t p = 32;
+  while (p < x) p <<= 1;
+  return p;
+}
+
+// Shared-memory carve-up relative to a 1024-byte aligned base; `total`
+// includes 1 KB of alignment slack.
+__host__ __device__ inline TcLayout tc_layout(int wb, int nm, int ns, int wgrp, int gmax, int ring,
+                                              int aring) {
+  TcLayout L;
+  L.nsub = (wb == 4 && wgrp == 32) ? 2 : 1;
+  L.raw_stream = wb == 8 ? 64 * kTileN : 32 * kTileN + L.nsub * kTileN * 2 + L.nsub * kTileN;
+  L.raw_stage = ns * L.raw_stream;
+  uint32_t off = 0;
+  L.raw_off = off;
+  off = align_up(off + ring * L.raw_stage, 1024);
+  L.a_off = off;
+  if (wb == 4) off = align_up(off + aring * ns * 64 * kTileN, 1024);
+  L.b_off = off;
+  off = align_up(off + gmax * 64 * nm, 128);
+  L.as_off = off;
+  off = align_up(off + gmax * nm * 4, 16);
+  L.asum_off = off;
+  off = align_up(off + (wb == 4 ? gmax * 2 * nm * 4 : 0), 16);
+  L.part_off = off;
+  off = align_up(off + ns * nm * kTileN * 4, 16);
+  L.xchg_off = off;
+  off = align_up(off + 4 * nm * 4, 16);
+  L.bar_off = off;
+  off = align_up(off + 8 * (2 * ring + 2 * aring + 4 + 1), 16);
+  L.tmem_slot_off = off;
+  off += 16;
+  L.total = off + 1024;
+  L.tmem_cols = pow2_at_least(2u * ns * L.nsub * (nm < 16 ? 16 : nm));
+  return L;
+}
+
+template <int WB, int MR, int EPI>
+__global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid_constant__ GemvArgs p) {
+  namespace cg = cooperative_groups;
+  constexpr int NS = (EPI == kEpiOut) ? 1 : 2;
+  constexpr int NM = MR < 16 ? 16 : MR;   // MMA N (activation rows, padded)
+  constexpr int LDN = MR <= 8 ? 8 : MR;   // TMEM columns read per accumulator
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+  const int aring = WB == 4 ? p.aring : 0;
+  const int aring_div = aring > 0 ? aring : 1;  // W8 has no unpacked ring
+  const TcLayout L = tc_layout(WB, NM, NS, p.wgrp, p.gmax, p.ring, aring);
+  const int NSUB = static_cast<int>(L.nsub);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
+  uint64_t* empty = full + p.ring;
+  uint64_t* afull = empty + p.ring;
+  uint64_t* aempty = afull + aring;
+  uint64_t* tfull = aempty + aring;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* bready = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.tmem_slot_off);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int rank = blockIdx.x;
+  const int tile = blockIdx.y;
+  const int m0 = blockIdx.z * NM;
+
+  int si = 0;
+  if (EPI == kEpiOut) {
+    if (p.nseg > 1 && tile >= p.seg[1].tile_begin) si = 1;
+    if (p.nseg > 2 && tile >= p.seg[2].tile_begin) si = 2;
+  }
+  const GemvSeg& S0 = p.seg[si];
+  const int n0 = (tile - S0.tile_begin) * kTileN;
+  const int G = p.K / kGroup;
+  const int g0 = static_cast<int>(static_cast<long long>(rank) * G / p.split);
+  const int g1 = static_cast<int>(static_cast<long long>(rank + 1) * G / p.split);
+  const int nst = g1 - g0;
+
+  // Drain thread -> output column of this tile (TMEM lane 32*(warp%4) + lane).
+  const bool is_drain = warp >= kTcWarpDrain && warp < kTcWarpDrain + 4;
+  const int q = warp & 3;
+  const int c = 32 * q + lane;
+  const bool epi_thread = is_drain && rank == 0;
+  const int en = n0 + c;
+  const bool evalid = epi_thread && en < S0.n;
+  float pre_s0 = 1.0f, pre_s1 = 1.0f;
+  if (WB == 8 && evalid) {
+    pre_s0 = __ldg((NS == 1 ? S0.bs : p.seg[0].bs) + en);
+    if (NS == 2) pre_s1 = __ldg(p.seg[1].bs + en);
+  }
+  float pre_res[MR];
+#pragma unroll
+  for (int m = 0; m < MR; ++m) pre_res[m] = 0.0f;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < p.ring; ++i) {
+      mbar_init(full + i, 1);
+      mbar_init(empty + i, WB == 8 ? 1 : 8);
+    }
+    for (int i = 0; i < aring; ++i) {
+      mbar_init(afull + i, 128);
+      mbar_init(aempty + i, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(tfull + i, 1);
+      mbar_init(tempty + i, kDrainThreads);
+    }
+    mbar_init(bready, kDrainThreads);
+    fence_mbar_init();
+  }
+  if (warp == kTcWarpMma) {
+    tmem_alloc(tmem_slot, L.tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+
+  uint8_t* raw = smem + L.raw_off;
+  uint8_t* abuf = smem + L.a_off;
+  uint8_t* bop = smem + L.b_off;
+  float* ass = reinterpret_cast<float*>(smem + L.as_off);
+  int* asum = reinterpret_cast<int*>(smem + L.asum_off);
+  float* part = reinterpret_cast<float*>(smem + L.part_off);
+  // B operand (K-major, no swizzle): core matrix (k-chunk kc, row group mg) of
+  // group gl at gl*64*NM + (kc*(NM/8) + mg)*128; rows of 16 bytes.
+  constexpr uint32_t kLboB = (NM / 8) * 128;  // K-direction core-matrix stride
+  constexpr uint32_t kSboB = 128;             // row-group stride
+  // TMEM accumulator column of (buffer, stream, sub-block).
+  auto tcol = [&](int tb, int s, int sub) -> uint32_t {
+    return static_cast<uint32_t>(((tb * NS + s) * NSUB + sub) * NM);
+  };
+
+  if (warp == kTcWarpTma) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_first();
+      uint32_t bytes = 0;
+#pragma unroll
+      for (int s = 0; s < NS; ++s) {
+        const GemvSeg& sg = NS == 1 ? S0 : p.seg[s];
+        bytes += WB == 8 ? 64 * kTileN : 32 * kTileN + L.nsub * kTileN * 2 + (sg.has_z ? L.nsub * kTileN : 0);
+      }
+      for (int i = 0; i < nst; ++i) {
+        const int slot = i % p.ring;
+        if (i >= p.ring && !mbar_wait(empty + slot, ((i / p.ring) & 1) ^ 1)) {
+          atomicOr(p.fault, kFaultEmptyWait);
+          break;
+        }
+        mbar_arrive_expect_tx(full + slot, bytes);
+        const int g = g0 + i;
+#pragma unroll
+        for (int s = 0; s < NS; ++s) {
+          const GemvSeg& sg = NS == 1 ? S0 : p.seg[s];
+          uint8_t* dst = raw + slot * L.raw_stage + s * L.raw_stream;
+          if (WB == 8) {
+            tma_load_2d(dst, &sg.tw, n0, g * 64, full + slot, pol);
+          } else {
+            tma_load_2d(dst, &sg.tw, n0, g * 32, full + slot, pol);
+            const int srow = (g * 64) / p.wgrp;
+            tma_load_2d(dst + 32 * kTileN, &sg.ts, n0, srow, full + slot, pol);
+            if (sg.has_z)
+              tma_load_2d(dst + 32 * kTileN + L.nsub * kTileN * 2, &sg.tz, n0, srow, full + slot, pol);
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == kTcWarpMma) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_i8(128, NM, WB == 8, true, true, false);
+      bool ok = mbar_wait(bready, 0);
+      if (!ok) atomicOr(p.fault, kFaultMmaWait);
+      for (int i = 0; ok && i < nst; ++i) {
+        const int tb = i & 1;
+        const int slot = i % p.ring;
+        const int as_ = WB == 4 ? i % aring_div : 0;
+        if (WB == 8) ok = mbar_wait(full + slot, (i / p.ring) & 1);
+        else ok = mbar_wait(afull + as_, (i / aring_div) & 1);
+        ok = ok && mbar_wait(tempty + tb, ((i >> 1) & 1) ^ 1);
+        if (!ok) {
+          atomicOr(p.fault, kFaultMmaWait);
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int s = 0; s < NS; ++s) {
+          const uint8_t* a_tile =
+              WB == 8 ? raw + slot * L.raw_stage + s * L.raw_stream : abuf + (as_ * NS + s) * 64 * kTileN;
+          const uint32_t a_addr = smem_u32(a_tile);
+          const uint32_t b_addr = smem_u32(bop + i * 64 * NM);
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const uint64_t ad = smem_desc(a_addr + 4096 * j, 8192, 1024, kLayoutSw128);
+            const uint64_t bd = smem_desc(b_addr + 2 * j * kLboB, kLboB, kSboB, kLayoutNone);
+            const uint32_t d = tbase + tcol(tb, s, NSUB == 2 ? j : 0);
+            tc_mma_i8(d, ad, bd, idesc, NSUB == 2 ? 0u : static_cast<uint32_t>(j));
+          }
+        }
+        tc_commit(tfull + tb);
+        tc_commit(WB == 8 ? empty + slot : aempty + as_);
+      }
+    }
+    __syncwarp();
+  } else if (is_drain) {
+    // ------------------------------------------------------------------ drain
+    const int td = threadIdx.x - kTcWarpDrain * 32;
+    pdl_wait();
+    if (EPI == kEpiOut && evalid && p.res) {
+      const __nv_bfloat16* res = reinterpret_cast<const __nv_bfloat16*>(p.res);
+#pragma unroll
+      for (int m = 0; m < MR; ++m)
+        if (m0 + m < p.M)
+          pre_res[m] = __bfloat162float(res[static_cast<long long>(m0 + m) * p.ldr + S0.out_col + en]);
+    }
+    // Stage the activation operand (32-byte units: row m, half-group h).
+    const int kbase = g0 * 64;
+    for (int idx = td; idx < NM * nst * 2; idx += kDrainThreads) {
+      const int m = idx % NM;
+      const int gh = idx / NM;  // gl * 2 + h
+      const int gl = gh >> 1, h = gh & 1;
+      int4 v0 = make_int4(0, 0, 0, 0), v1 = make_int4(0, 0, 0, 0);
+      if (m0 + m < p.M) {
+        const int4* src = reinterpret_cast<const int4*>(p.a_q + static_cast<long long>(m0 + m) * p.K + kbase +
+                                                        gl * 64 + h * 32);
+        v0 = __ldg(src);
+        v1 = __ldg(src + 1);
+      }
+      uint8_t* gb = bop + gl * 64 * NM + (m & 7) * 16;
+      *reinterpret_cast<int4*>(gb + ((2 * h) * (NM / 8) + (m >> 3)) * 128) = v0;
+      *reinterpret_cast<int4*>(gb + ((2 * h + 1) * (NM / 8) + (m >> 3)) * 128) = v1;
+      if (WB == 4) {
+        int s = 0;
+        s = dp4a_ss(v0.x, 0x01010101, s); s = dp4a_ss(v0.y, 0x01010101, s);
+        s = dp4a_ss(v0.z, 0x01010101, s); s = dp4a_ss(v0.w, 0x01010101, s);
+        s = dp4a_ss(v1.x, 0x01010101, s); s = dp4a_ss(v1.y, 0x01010101, s);
+        s = dp4a_ss(v1.z, 0x01010101, s); s = dp4a_ss(v1.w, 0x01010101, s);
+        asum[gh * NM + m] = s;
+      }
+    }
+    for (int idx = td; idx < NM * nst; idx += kDrainThreads) {
+      const int m = idx % NM, gl = idx / NM;
+      ass[gl * NM + m] = (m0 + m < p.M) ? __ldg(p.a_s + static_cast<long long>(m0 + m) * G + g0 + gl) : 0.0f;
+    }
+    fence_proxy_async_smem();
+    mbar_arrive(bready);
+    named_bar_sync(1, kDrainThreads);  // ass / asum visible to all drain threads
+    pdl_launch_dependents();
+
+    float acc[NS][MR];
+#pragma unroll
+    for (int s = 0; s < NS; ++s)
+#pragma unroll
+      for (int m = 0; m < MR; ++m) acc[s][m] = 0.0f;
+
+    const uint32_t lane_base = tbase + (static_cast<uint32_t>(32 * q) << 16);
+    for (int i = 0; i < nst; ++i) {
+      const int tb = i & 1;
+      const int slot = i % p.ring;
+      bool ok = true;
+      if (WB == 4) ok = mbar_wait(full + slot, (i / p.ring) & 1);
+      ok = ok && mbar_wait(tfull + tb, (i >> 1) & 1);
+      if (!ok) {
+        if (lane == 0) atomicOr(p.fault, kFaultFullWait);
+        break;
+      }
+      tc_fence_after();
+      uint32_t r[NS][2][LDN];
+#pragma unroll
+      for (int s = 0; s < NS; ++s) {
+        tmem_ld32<LDN>(lane_base + tcol(tb, s, 0), r[s][0]);
+        if (WB == 4 && NSUB == 2) tmem_ld32<LDN>(lane_base + tcol(tb, s, 1), r[s][1]);
+      }
+      tc_wait_ld();
+      tc_fence_before();
+      mbar_arrive(tempty + tb);
+      const float* as_g = ass + i * NM;
+      if (WB == 8) {
+        // out += float(int32 group sum) * a_s[m, kb]   (kernels/gemm.py:43-45)
+#pragma unroll
+        for (int s = 0; s < NS; ++s)
+#pragma unroll
+          for (int m = 0; m < MR; ++m)
+            acc[s][m] = __fadd_rn(acc[s][m], __fmul_rn(__int2float_rn(static_cast<int>(r[s][0][m])), as_g[m]));
+      } else {
+        // out += float(int32 sub-block sum) * (a_s * ws)   (kernels/w4.py:103-104)
+        const int* asum_g = asum + i * 2 * NM;
+#pragma unroll
+        for (int s = 0; s < NS; ++s) {
+          const GemvSeg& sg = NS == 1 ? S0 : p.seg[s];
+          const uint8_t* st = raw + slot * L.raw_stage + s * L.raw_stream;
+          const uint16_t* sc = reinterpret_cast<const uint16_t*>(st + 32 * kTileN);
+          const uint8_t* zz = st + 32 * kTileN + L.nsub * kTileN * 2;
+          for (int sub = 0; sub < NSUB; ++sub) {
+            const float ws = bf16_bits_to_f32(sc[sub * kTileN + c]);
+            const int z = sg.has_z ? static_cast<int>(zz[sub * kTileN + c]) : 8;
+#pragma unroll
+            for (int m = 0; m < MR; ++m) {
+              const int sa = NSUB == 2 ? asum_g[sub * NM + m] : asum_g[m] + asum_g[NM + m];
+              const int v = static_cast<int>(r[s][sub][m]) - z * sa;
+              const float t = __fmul_rn(as_g[m], ws);
+              acc[s][m] = __fadd_rn(acc[s][m], __fmul_rn(__int2float_rn(v), t));
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty + slot);
+      }
+    }
+#pragma unroll
+    for (int s = 0; s < NS; ++s)
+#pragma unroll
+      for (int m = 0; m < MR; ++m) part[(s * NM + m) * kTileN + c] = acc[s][m];
+  } else if constexpr (WB == 4) {
+    // ------------------------------------------------------------------ W4 unpack
+    const int u = threadIdx.x - kTcWarpUnpack * 32;
+    for (int i = 0; i < nst; ++i) {
+      const int slot = i % p.ring;
+      const int as_ = i % aring;
+      if (!mbar_wait(full + slot, (i / p.ring) & 1) || !mbar_wait(aempty + as_, ((i / aring) & 1) ^ 1)) {
+        if (lane == 0) atomicOr(p.fault, kFaultFullWait);
+        break;
+      }
+#pragma unroll
+      for (int s = 0; s < NS; ++s) {
+        const uint8_t* st = raw + slot * L.raw_stage + s * L.raw_stream;
+        uint8_t* at = abuf + (as_ * NS + s) * 64 * kTileN;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int pr = (u >> 3) + 16 * hh;  // packed row: K = 2*pr (low), 2*pr + 1 (high)
+          const int ch = u & 7;               // 16-byte chunk = 16 columns
+          const uint4 v = *reinterpret_cast<const uint4*>(st + pr * kTileN + ch * 16);
+          uint4 lo, hi;
+          lo.x = v.x & 0x0F0F0F0Fu; hi.x = (v.x >> 4) & 0x0F0F0F0Fu;
+          lo.y = v.y & 0x0F0F0F0Fu; hi.y = (v.y >> 4) & 0x0F0F0F0Fu;
+          lo.z = v.z & 0x0F0F0F0Fu; hi.z = (v.z >> 4) & 0x0F0F0F0Fu;
+          lo.w = v.w & 0x0F0F0F0Fu; hi.w = (v.w >> 4) & 0x0F0F0F0Fu;
+          const int r0 = 2 * pr, r1 = 2 * pr + 1;
+          *reinterpret_cast<uint4*>(at + r0 * kTileN + ((ch ^ (r0 & 7)) << 4)) = lo;
+          *reinterpret_cast<uint4*>(at + r1 * kTileN + ((ch ^ (r1 & 7)) << 4)) = hi;
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(afull + as_);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty + slot);
+    }
+  }
+
+  // ------------------------------------------------------------------ cluster combine + epilogue
+  cg::cluster_group cluster = cg::this_cluster();
+  tc_fence_before();
+  cluster.sync();
+  tc_fence_after();
+  if (warp == kTcWarpMma) tmem_dealloc(tbase, L.tmem_cols);
+  if (epi_thread) {
+    const int n = en;
+    const bool valid = n < S0.n;
+    float vs[NS][MR];
+#pragma unroll
+    for (int s = 0; s < NS; ++s)
+#pragma unroll
+      for (int m = 0; m < MR; ++m) vs[s][m] = 0.0f;
+    for (int r = 0; r < p.split; ++r) {
+      const float* rp = cluster.map_shared_rank(part, r);
+#pragma unroll
+      for (int s = 0; s < NS; ++s)
+#pragma unroll
+        for (int m = 0; m < MR; ++m) vs[s][m] = __fadd_rn(vs[s][m], rp[(s * NM + m) * kTileN + c]);
+    }
+    if (EPI == kEpiOut) {
+      __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
+#pragma unroll
+      for (int m = 0; m < MR; ++m) {
+        if (!valid || m0 + m >= p.M) continue;
+        float v = vs[0][m];
+        if (WB == 8) v = __fmul_rn(v, pre_s0);  // out * bs (kernels/gemm.py:51-52)
+        if (p.res) v = __fadd_rn(v, pre_res[m]);
+        out[static_cast<long long>(m0 + m) * p.ldo + S0.out_col + n] = __float2bfloat16_rn(v);
+      }
+    } else {
+      float* xchg = reinterpret_cast<float*>(smem + L.xchg_off);
+#pragma unroll
+      for (int m = 0; m < MR; ++m) {
+        float g = vs[0][m], uu = vs[1][m];
+        if (WB == 8) {
+          g = __fmul_rn(g, pre_s0);
+          uu = __fmul_rn(uu, pre_s1);
+        }
+        const float h = __fmul_rn(silu_ref(g), uu);  // silu(g) * u (kernels/gemm.py:197)
+        const bool store = valid && (m0 + m < p.M);
+        if (EPI == kEpiSiluBf16) {
+          if (store)
+            reinterpret_cast<__nv_bfloat16*>(p.out)[static_cast<long long>(m0 + m) * p.ldo + n] =
+                __float2bfloat16_rn(h);
+        } else {
+          // kernels/gemm.py:198-211: round through bf16, per-64 amax, int8 codes
+          const float hb = bf16_round_f32(h);
+          float amax = fabsf(hb);
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+          if (lane == 0) xchg[q * MR + m] = amax;
+          named_bar_sync(2, kDrainThreads);
+          amax = fmaxf(amax, xchg[(q ^ 1) * MR + m]);  // the other warp of this 64-column group
+          const float sc = fmaxf(__fdiv_rn(amax, 127.0f), 1e-8f);
+          const int8_t qv = round_i8(__fdiv_rn(hb, sc));
+          if (store) {
+            p.out_q[static_cast<long long>(m0 + m) * p.n_q + n] = qv;
+            if ((c & 63) == 0) p.out_s[static_cast<long long>(m0 + m) * (p.n_q / 64) + n / 64] = sc;
+          }
+        }
+      }
+    }
+  }
+  cluster.sync();
+}
+
+}  // namespace qlin
