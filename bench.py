@@ -1,0 +1,442 @@
+"""Benchmark of the quantised-linear hot path (one JSON line on rank 0).
+
+Workload (N=1): every linear of one Qwen3.5-2B-class W4
+layer -- group size 128, bf16 group scales, uint8 zero points, engine layouts
+-- at decode batch M=1 and M=4 (best-of-4):
+  qkv+gate  proj3_w4              2048 -> 4096
+  gate/up   mlp_gate_up_quant_w4  2048 -> 2 x 6144 (+ SiLU*up + int8 requant)
+  down      gemm_w4 + residual    6144 -> 2048
+  o_proj    gemm_w4 + residual    2048 -> 2048
+One step = the four launches at M=1 followed by the four at M=4.  Weights
+rotate over 8 layer copies (about 210 MB, more than the 126 MB L2), so every
+step streams its weights from HBM.  Each step's launches are captured in a CUDA
+graph; the timed region replays exactly K step graphs, bracketed by a barrier
+and device synchronisation, timed with CUDA events (max over ranks).
+
+With --gpus N > 1 every rank runs its own replica of the workload on its own
+layer copies (layers are independent units: weak scaling, no collective on
+the data path); `value` sums the bytes of all ranks over the slowest rank's
+time.
+
+--impl reference times the reference's own CPU formulation of the path
+(dequantise, then one fp32 matmul: .dev/test_kernels.py:40-41 restated in
+oracle/qlin_oracle.py) on the host cores instead.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "W8/W4 GEMV HBM TB/s (M=1..4), W8A8 prefill TFLOPS; %roofline @1/2/4/8 B200"
+H, I, QKV, WG = 2048, 6144, 4096, 128
+MS = (1, 4)
+COPIES = 8
+LAUNCHES_PER_STEP = 4 * len(MS)
+
+
+def linear_bytes(K, N, M, out_bytes_per_col, residual=False):
+    """Algorithmic bytes of one W4 linear: packed weights, bf16 scales, uint8
+    zeros, int8 activations + fp32 per-64 scales, outputs (+ residual read)."""
+    w = K * N // 2 + (K // WG) * N * 2 + (K // WG) * N
+    act = M * K + M * (K // 64) * 4
+    out = M * N * out_bytes_per_col + (M * N * 2 if residual else 0)
+    return w + act + out
+
+
+def step_bytes():
+    total = 0
+    for M in MS:
+        total += linear_bytes(H, QKV, M, 2)
+        total += 2 * (H * I // 2 + (H // WG) * I * 3) + M * H + M * (H // 64) * 4 + M * I + M * (I // 64) * 4
+        total += linear_bytes(I, H, M, 2, residual=True)
+        total += linear_bytes(H, H, M, 2, residual=True)
+    return total
+
+
+def gate_up_bytes(M):
+    return 2 * (H * I // 2 + (H // WG) * I * 3) + M * H + M * (H // 64) * 4 + M * I + M * (I // 64) * 4
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profile_traffic(name):
+    """DRAM bytes per launch of `name` from the committed ncu summary, if any
+    (a line `traffic_bytes_per_launch: <int>` in profiles/<name>.md)."""
+    p = os.path.join(ROOT, "profiles", name + ".md")
+    try:
+        for line in open(p):
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples (SM clock, throttle reasons) during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.reader = threading.Thread(target=self._read, daemon=True)
+            self.reader.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[4:8]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- workload
+def make_layer(pkg, dev, gen):
+    def w4(K, N):
+        b = torch.randint(0, 256, (K // 2, N), dtype=torch.uint8, device=dev, generator=gen)
+        s = torch.exp(torch.randn(K // WG, N, device=dev, generator=gen) * 0.5 - 5.0).to(torch.bfloat16)
+        z = torch.randint(0, 16, (K // WG, N), dtype=torch.uint8, device=dev, generator=gen)
+        return b, s, z
+    return {"qkv": w4(H, QKV), "gate": w4(H, I), "up": w4(H, I), "down": w4(I, H), "o": w4(H, H)}
+
+
+class Workspace:
+    def __init__(self, pkg, dev, M, gen):
+        self.M = M
+        x = torch.randn(M, H, device=dev, generator=gen).to(torch.bfloat16)
+        self.xq = torch.empty(M, H, dtype=torch.int8, device=dev)
+        self.xs = torch.empty(M, H // 64, dtype=torch.float32, device=dev)
+        pkg.quant_row(x, self.xq, self.xs)
+        self.proj = torch.empty(M, QKV, dtype=torch.bfloat16, device=dev)
+        self.hq = torch.empty(M, I, dtype=torch.int8, device=dev)
+        self.hs = torch.empty(M, I // 64, dtype=torch.float32, device=dev)
+        self.hidden = (torch.randn(M, H, device=dev, generator=gen) * 0.1).to(torch.bfloat16)
+
+
+def run_layer(pkg, L, ws):
+    """The four hot-path calls of one layer, exactly as the engine makes them
+    (engine.py:221-279 call pattern, W4 dispatch through the W8 entry points)."""
+    q = L["qkv"]
+    pkg.proj3(ws.xq, ws.xs, q[0], q[1], None, None, None, None, ws.proj, z1=q[2])
+    g, u = L["gate"], L["up"]
+    pkg.mlp_gate_up_quant(ws.xq, ws.xs, g[0], g[1], u[0], u[1], ws.hq, ws.hs, zg=g[2], zu=u[2])
+    d = L["down"]
+    pkg.gemm_i8(ws.hq, ws.hs, d[0], d[1], ws.hidden, residual=ws.hidden, b_z=d[2])
+    o = L["o"]
+    pkg.gemm_i8(ws.xq, ws.xs, o[0], o[1], ws.hidden, residual=ws.hidden, b_z=o[2])
+
+
+def capture(fn, stream):
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        fn()
+    return g
+
+
+def time_graphs(graphs, K, stream):
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for i in range(K):
+            graphs[i % len(graphs)].replay()
+        e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / 1e3  # seconds
+
+
+# ----------------------------------------------------------------------------- CPU reference arm
+def cpu_reference_step(O, layers_cpu, xs_cpu):
+    """One step of the reference's CPU formulation: dequantise each weight and
+    run one fp32 matmul per linear (.dev/test_kernels.py:40-41)."""
+    for M in MS:
+        a_q, a_s = xs_cpu[M]
+        L = layers_cpu
+        O.dequant_matmul_w4(a_q, a_s, *L["qkv"])
+        O.dequant_matmul_w4(a_q, a_s, *L["gate"])
+        O.dequant_matmul_w4(a_q, a_s, *L["up"])
+        hq = torch.randint(-127, 128, (M, I), dtype=torch.int8)
+        hs = torch.rand(M, I // 64) * 0.02
+        O.dequant_matmul_w4(hq, hs, *L["down"])
+        O.dequant_matmul_w4(a_q, a_s, *L["o"])
+
+
+def cpu_setup():
+    from oracle import qlin_oracle as O
+    g = torch.Generator().manual_seed(7)
+
+    def w4(K, N):
+        return (torch.randint(0, 256, (K // 2, N), dtype=torch.int32, generator=g).to(torch.uint8),
+                torch.exp(torch.randn(K // WG, N, generator=g) * 0.5 - 5.0).to(torch.bfloat16),
+                torch.randint(0, 16, (K // WG, N), dtype=torch.int32, generator=g).to(torch.uint8))
+    L = {"qkv": w4(H, QKV), "gate": w4(H, I), "up": w4(H, I), "down": w4(I, H), "o": w4(H, H)}
+    xs = {M: (torch.randint(-127, 128, (M, H), dtype=torch.int8, generator=g),
+              torch.rand(M, H // 64, generator=g) * 0.02) for M in MS}
+    return O, L, xs
+
+
+def cpu_measure(seconds, max_steps=None):
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    O, L, xs = cpu_setup()
+    cpu_reference_step(O, L, xs)  # warm-up
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        cpu_reference_step(O, L, xs)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or (max_steps and n >= max_steps):
+            break
+    return n, el, cores
+
+
+# ----------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", choices=["qlin", "reference"], default="qlin")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    args = ap.parse_args()
+    warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        # Rank 0 alone times the reference's CPU formulation; other ranks exit.
+        if rank != 0:
+            return
+        per_step = step_bytes()
+        w = min(warmup, 1)
+        O, L, xs = cpu_setup()
+        torch.set_num_threads(len(os.sched_getaffinity(0)))
+        for _ in range(w):
+            cpu_reference_step(O, L, xs)
+        n, el, cores = cpu_measure(args.cpu_seconds, max_steps=args.steps)
+        tbs = per_step * n / el / 1e12
+        line = {
+            "impl": "reference", "metric": METRIC, "value": tbs, "unit": "TB/s", "n_gpus": args.gpus,
+            "steps": n, "warmup": w, "ms_per_step": el / n * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+            "config": {"workload": "W4 g128 one 2B-class layer (qkv+gate 2048->4096, gate_up 2048->2x6144, "
+                                   "down 6144->2048, o 2048->2048), M in {1,4}",
+                       "form": "dequantise then fp32 matmul (torch CPU)"},
+            "cpu_baseline": {"value": tbs, "unit": "TB/s", "cores": cores, "kind": "port",
+                             "sample": f"{n} steps in {el:.1f} s"},
+            "e2e": {"value": tbs, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
+        return
+
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        pg = dist
+
+    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+    layers = [make_layer(pkg, dev, gen) for _ in range(COPIES)]
+    wss = {M: Workspace(pkg, dev, M, gen) for M in MS}
+    torch.cuda.synchronize()
+
+    def step(li):
+        for M in MS:
+            run_layer(pkg, layers[li], wss[M])
+
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        for li in range(COPIES):
+            step(li)   # eager warm-up (one-time per-kernel set-up)
+    torch.cuda.synchronize()
+    graphs = [capture(lambda li=li: step(li), stream) for li in range(COPIES)]
+
+    # warm-up replays
+    time_graphs(graphs, warmup, stream)
+    torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        secs = time_graphs(graphs, args.steps, stream)
+        torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    t = torch.tensor([secs], device=dev)
+    if pg:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    secs = float(t.item())
+    per_step = step_bytes()
+    value = per_step * args.steps * world / secs / 1e12
+
+    # ---- dominant kernel: fused W4 gate/up at M=4, alone, rotating copies
+    ws4 = wss[4]
+
+    def gu(li):
+        g, u = layers[li]["gate"], layers[li]["up"]
+        pkg.mlp_gate_up_quant(ws4.xq, ws4.xs, g[0], g[1], u[0], u[1], ws4.hq, ws4.hs, zg=g[2], zu=u[2])
+    ggu = capture(lambda: [gu(li) for li in range(COPIES)], stream)
+    time_graphs([ggu], 5, stream)
+    reps = 200
+    gsecs = time_graphs([ggu], reps, stream)
+    gu_launch_s = gsecs / (reps * COPIES)
+    gu_bytes = gate_up_bytes(4)
+    peak, peak_kind = load_peaks()
+    achieved = gu_bytes / gu_launch_s / 1e9
+
+    # ---- config-1 W8 GEMV (M=1, 2048 -> 6144) alone, rotating copies
+    w8s = [(torch.randint(-127, 128, (H, I), dtype=torch.int8, device=dev, generator=gen),
+            torch.exp(torch.randn(I, device=dev, generator=gen) * 0.5 - 6.0)) for _ in range(16)]
+    o8 = torch.empty(1, I, dtype=torch.bfloat16, device=dev)
+    ws1 = wss[1]
+    g8 = capture(lambda: [pkg.gemm_i8(ws1.xq, ws1.xs, b, s, o8) for b, s in w8s], stream)
+    time_graphs([g8], 5, stream)
+    w8secs = time_graphs([g8], 100, stream) / (100 * len(w8s))
+    w8_bytes = H * I + I * 4 + H + (H // 64) * 4 + I * 2
+
+    # ---- e2e through the public API with host buffers (rank-local)
+    e2e_steps = min(args.steps, 2000)
+    host_x = {M: torch.randn(M, H).to(torch.bfloat16).pin_memory() for M in MS}
+    host_out = {M: torch.empty(M, H, dtype=torch.bfloat16).pin_memory() for M in MS}
+    dev_x = {M: torch.empty(M, H, dtype=torch.bfloat16, device=dev) for M in MS}
+
+    def e2e_step(li):
+        for M in MS:
+            ws = wss[M]
+            dev_x[M].copy_(host_x[M], non_blocking=True)
+            pkg.quant_row(dev_x[M], ws.xq, ws.xs)
+            run_layer(pkg, layers[li], ws)
+            host_out[M].copy_(ws.hidden, non_blocking=True)
+    with torch.cuda.stream(stream):
+        for li in range(3):
+            e2e_step(li)
+        stream.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(e2e_steps):
+            e2e_step(i % COPIES)
+        e1.record(stream)
+    e1.synchronize()
+    e2e_secs = e0.elapsed_time(e1) / 1e3
+    h2d = sum(M * H * 2 for M in MS)
+    d2h = sum(M * H * 2 for M in MS)
+    e2e_value = per_step * e2e_steps / e2e_secs / 1e12
+    et = torch.tensor([e2e_value], device=dev)
+    if pg:
+        pg.all_reduce(et, op=pg.ReduceOp.MIN)
+        e2e_value = float(et.item()) * world
+
+    cpu = None
+    if rank == 0 and world == 1:
+        n, el, cores = cpu_measure(args.cpu_seconds)
+        cpu = {"value": per_step * n / el / 1e12, "unit": "TB/s", "cores": cores, "kind": "port",
+               "sample": f"{n} full steps (the workload above, dequantise-then-fp32-matmul on CPU) in {el:.1f} s"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": warmup, "ms_per_step": secs / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {
+                "workload": "W4 g128 GEMV over every linear of one 2B-class layer (qkv+gate 2048->4096, "
+                            "gate_up 2048->2x6144 fused SiLU+requant, down 6144->2048 +res, o 2048->2048 +res), "
+                            "M=1 and M=4 per step",
+                "bytes_per_step": per_step, "weight_copies": COPIES,
+                "l2": "rotating 8 layer copies (~210 MB > 126 MB L2)",
+                "launches_per_step": LAUNCHES_PER_STEP, "timing": "CUDA graph per step, CUDA events",
+                "parallelism": f"replicas x{world}"},
+            "roofline": {"bound": "hbm", "kernel": "mlp_gate_up_quant_w4 M=4 (tcgen05 weight streaming)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_kind": peak_kind, "bytes_per_launch": gu_bytes,
+                         "launch_us": gu_launch_s * 1e6,
+                         "traffic": profile_traffic("mlp_gate_up_quant_w4_m4")},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "TB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "steps": e2e_steps, "ms_per_step": e2e_secs / e2e_steps * 1e3},
+            "gpu_launches": args.steps * LAUNCHES_PER_STEP,
+            "clocks": clk.summary(),
+            "detail": {
+                "w8_gemv_cfg1_tbs": w8_bytes / w8secs / 1e12, "w8_gemv_cfg1_us": w8secs * 1e6,
+                "gate_up_w4_m4_us": gu_launch_s * 1e6,
+                "fault_word": pkg._lib.load().qlin_device_fault(0),
+            },
+        }
+        print(json.dumps(line), flush=True)
+    for g in graphs:
+        del g
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

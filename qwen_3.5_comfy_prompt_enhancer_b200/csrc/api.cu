@@ -109,6 +109,18 @@ int make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t 
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Tuning overrides (environment, read once): QLIN_TUNE_SPLIT forces the K
+// split / cluster size, QLIN_TUNE_PDL=0 launches without programmatic
+// dependent launch, QLIN_TUNE_BUDGET_KB sets the per-CTA shared-memory
+// budget.  They change scheduling and the fp32 summation order only.
+int env_int(const char* name, int dflt) {
+  const char* e = getenv(name);
+  return (e && *e) ? atoi(e) : dflt;
+}
+int tune_split() { static const int v = env_int("QLIN_TUNE_SPLIT", 0); return v; }
+int tune_pdl() { static const int v = env_int("QLIN_TUNE_PDL", 1); return v; }
+int tune_budget() { static const int v = env_int("QLIN_TUNE_BUDGET_KB", 0); return v; }
+
 // Kernel family for the small-M path: tcgen05 weight streaming (default) or
 // the CUDA-core dp4a GEMV (QLIN_SMALLM_KERNEL=dp4a, kept for comparison).
 bool use_tc() {
@@ -185,7 +197,7 @@ int launch_gemv_t(const GemvArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].val.programmaticStreamSerializationAllowed = tune_pdl() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
@@ -219,12 +231,13 @@ struct TcPlan {
 TcPlan plan_tc(int wb, int mr, int ns, int K, int wgrp, int tiles, int rowblocks, int sms) {
   const int G = K / kGroup;
   const int nm = mr < 16 ? 16 : mr;
-  TcPlan best{1, 1, wb == 4 ? 4 : 0, G, 0};
+  TcPlan best{1, 1, wb == 4 ? 2 : 0, G, 0};  // W4: two unpacked A stages
   double best_cost = 1e30;
   const int smax = G < 8 ? G : 8;
   for (int s = 1; s <= smax; ++s) {
     const int gmax = (G + s - 1) / s;
     if (static_cast<long long>(gmax) * 64 * nm > 48 * 1024) continue;  // activation operand
+    if (tune_split() > 0 && s != tune_split() && tune_split() <= smax) continue;
     const long long ctas = static_cast<long long>(tiles) * s * rowblocks;
     const double waves = static_cast<double>((ctas + sms - 1) / sms);
     const double cost = waves / s * (1.0 + 0.02 * s);
@@ -235,7 +248,7 @@ TcPlan plan_tc(int wb, int mr, int ns, int K, int wgrp, int tiles, int rowblocks
     }
   }
   // ~100 KB per CTA: two CTAs per SM (this launch and the next one under PDL).
-  const uint32_t budget = 100 * 1024;
+  const uint32_t budget = (tune_budget() > 0 ? tune_budget() : 100) * 1024;
   const TcLayout l1 = tc_layout(wb, nm, ns, wgrp, best.gmax, 1, best.aring);
   const uint32_t fixed = l1.total - l1.raw_stage;
   int ring = static_cast<int>((budget > fixed ? budget - fixed : 0) / l1.raw_stage);
@@ -277,7 +290,7 @@ int launch_tc_t(const GemvArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].val.programmaticStreamSerializationAllowed = tune_pdl() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
@@ -307,6 +320,7 @@ int run_tc(int wb, int epi, GemvArgs& a, int tiles, cudaStream_t st) {
   const int rowblocks = (a.M + nm - 1) / nm;
   if (rowblocks > 65535 || tiles > 65535) return fail(QLIN_ERR_SHAPE, "grid too large (M=%d)", a.M);
   const int ns = epi == kEpiOut ? 1 : 2;
+  if (int r = make_map(&a.ta, a.a_q, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.K, a.M, a.K, 128, nm, true)) return r;
   const TcPlan pl = plan_tc(wb, mr, ns, a.K, a.wgrp, tiles, rowblocks, di.sms);
   a.split = pl.split;
   a.ring = pl.ring;

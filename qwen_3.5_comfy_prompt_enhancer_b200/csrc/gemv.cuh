@@ -62,6 +62,7 @@ struct GemvSeg {
 };
 
 struct GemvArgs {
+  CUtensorMap ta;    // tcgen05 path: activations a_q [M, K], 128-byte-swizzled boxes of 128 K x rows
   GemvSeg seg[3];    // kEpiOut: column segments; gate/up epilogues: seg[0]=gate, seg[1]=up
   int nseg;
   const int8_t* a_q;  // [M, K]

@@ -21,9 +21,16 @@ enum : unsigned {
   kFaultMmaWait = 8u,       // tcgen05 commit wait
 };
 
-// Bound on mbarrier polls; each failed poll sleeps ~64 ns after a short spin,
-// so a wait gives up after roughly a quarter of a second.
-constexpr uint32_t kWaitLimit = 1u << 22;
+// Bound on any single mbarrier wait, in nanoseconds of %globaltimer.  A wait
+// that has not completed after this long records a fault bit and returns, so
+// a logic error surfaces as an error status instead of a hung GPU.
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -58,14 +65,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait for the phase with the given parity to complete.  Returns false
-// (and leaves the barrier alone) if it did not complete within kWaitLimit polls.
+// Bounded wait for the phase with the given parity to complete (try_wait
+// already suspends the thread in hardware between polls).  Returns false if
+// the phase did not complete within kWaitLimitNs.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (i >= 16) __nanosleep(64);
+    if ((i & 255u) == 0 && global_ns() - t0 > kWaitLimitNs) return false;
   }
-  return false;
+}
+
+// One elected lane of a fully converged warp.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n .reg .b32 r;\n .reg .pred p;\n elect.sync r|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(pred));
+  return pred != 0;
 }
 
 // ---------------------------------------------------------------- TMA

@@ -6,21 +6,30 @@
 // weight tile as operand A (M_mma = 128 output columns, MN-major: the
 // engine's [K, N] weight rows are N-contiguous, which tcgen05 reads directly
 // through a 128-byte-swizzled MN-major descriptor -- no transpose anywhere)
-// and the activations as operand B (N_mma = 16 or 32 rows, K-major).  The
-// int32 accumulator of each 64-element activation group lives in tensor
-// memory; drain warps read it back, apply the per-(row, group) activation
-// scale and accumulate fp32 in registers -- the reference's per-64-block
-// `tl.dot` followed by `out += acc * a_s` (kernels/gemm.py:40-49,
-// kernels/w4.py:125-130).  Integer sums are exact; only the fp32 order of
-// the K-split reduction differs from the reference.
+// and the activations as operand B (N_mma = 16 or 32 rows, K-major, loaded by
+// one TMA into the 128-byte-swizzled layout).  The int32 accumulator of each
+// 64-element activation group lives in tensor memory; drain warps read it
+// back, apply the per-(row, group) activation scale and accumulate fp32 in
+// registers -- the reference's per-64-block `tl.dot` followed by
+// `out += acc * a_s` (kernels/gemm.py:40-49, kernels/w4.py:125-130).
+// Integer sums are exact; only the fp32 order of the K-split reduction
+// differs from the reference.
 //
-// Warp roles (one CTA = one 128-column tile x one K range):
+// Warp roles (one CTA = one 128-column tile x one K range).  Every role runs
+// as a converged warp; an elected lane issues TMA / MMA / commit (a lone
+// active lane waits on mbarriers about twice as slowly).
 //   warp 0      TMA producer: weight rows (+ W4 group scales / zeros) into a
-//               ring of shared-memory stages, one stage per 64-K group.
-//   warp 1      tensor-memory owner and MMA issuer (one thread).
-//   warps 2-5   drain: stage the activation operand, then per group read the
-//               int32 accumulator (thread = output column), rescale, sum;
-//               finally the epilogue.
+//               ring of shared-memory stages, one stage per 64-K group.  The
+//               first ring-full of stages is requested before the CTA-wide
+//               set-up barrier.
+//   warp 1      tensor-memory owner and MMA issuer.  After the grid
+//               dependency it loads the activation tile by TMA.  Each
+//               in-flight group gets its own accumulator (up to the CTA's
+//               256-column share), so the issuer only waits for the drain
+//               when it wraps around that pool.
+//   warps 2-5   drain: activation scales, then per group read the int32
+//               accumulator (thread = output column), rescale, sum; finally
+//               the epilogue.
 //   warps 6-9   (W4 only) unpack: packed nibbles -> uint8 rows of the
 //               swizzled A tile.  Low nibble of packed row j is K = 2j, high
 //               nibble K = 2j+1.  The MMA multiplies unsigned nibbles with
@@ -45,11 +54,15 @@ constexpr int kTcWarpDrain = 2;   // 4 warps
 constexpr int kTcWarpUnpack = 6;  // 4 warps (W4)
 constexpr int kDrainThreads = 128;
 
+// Tensor-memory columns one CTA may hold: two CTAs share an SM (this launch
+// and the next one, under programmatic dependent launch).
+constexpr uint32_t kTmemBudget = 256;
+
 __host__ __device__ constexpr int tc_threads(int wb) { return (wb == 8 ? 6 : 10) * 32; }
 
 struct TcLayout {
-  uint32_t nsub, raw_stream, raw_stage, raw_off, a_off, b_off, as_off, asum_off, part_off, xchg_off,
-      bar_off, tmem_slot_off, total, tmem_cols;
+  uint32_t nsub, raw_stream, raw_stage, raw_off, a_off, b_off, nbox, as_off, asum_off, part_off, xchg_off,
+      bar_off, tmem_slot_off, total, tmem_cols, nbuf;
 };
 
 __host__ __device__ inline uint32_t pow2_at_least(uint32_t x) {
@@ -71,8 +84,10 @@ __host__ __device__ inline TcLayout tc_layout(int wb, int nm, int ns, int wgrp, 
   off = align_up(off + ring * L.raw_stage, 1024);
   L.a_off = off;
   if (wb == 4) off = align_up(off + aring * ns * 64 * kTileN, 1024);
+  // Activation operand: boxes of 128 K (one swizzle row) x nm rows.
   L.b_off = off;
-  off = align_up(off + gmax * 64 * nm, 128);
+  L.nbox = (gmax + 1) / 2;
+  off = align_up(off + L.nbox * nm * 128, 1024);
   L.as_off = off;
   off = align_up(off + gmax * nm * 4, 16);
   L.asum_off = off;
@@ -81,12 +96,19 @@ __host__ __device__ inline TcLayout tc_layout(int wb, int nm, int ns, int wgrp, 
   off = align_up(off + ns * nm * kTileN * 4, 16);
   L.xchg_off = off;
   off = align_up(off + 4 * nm * 4, 16);
+  // One accumulator (ns x nsub x nm columns) per in-flight group, up to the
+  // CTA's tensor-memory budget.
+  const uint32_t per_buf = ns * L.nsub * nm;
+  uint32_t nbuf = kTmemBudget / per_buf;
+  if (nbuf > static_cast<uint32_t>(gmax)) nbuf = gmax;
+  if (nbuf < 2) nbuf = 2;
+  L.nbuf = nbuf;
   L.bar_off = off;
-  off = align_up(off + 8 * (2 * ring + 2 * aring + 4 + 1), 16);
+  off = align_up(off + 8 * (2 * ring + 2 * aring + 2 * nbuf + 1), 16);
   L.tmem_slot_off = off;
   off += 16;
   L.total = off + 1024;
-  L.tmem_cols = pow2_at_least(2u * ns * L.nsub * (nm < 16 ? 16 : nm));
+  L.tmem_cols = pow2_at_least(nbuf * per_buf);
   return L;
 }
 
@@ -103,13 +125,14 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
   const int aring_div = aring > 0 ? aring : 1;  // W8 has no unpacked ring
   const TcLayout L = tc_layout(WB, NM, NS, p.wgrp, p.gmax, p.ring, aring);
   const int NSUB = static_cast<int>(L.nsub);
+  const int NB = static_cast<int>(L.nbuf);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
   uint64_t* empty = full + p.ring;
   uint64_t* afull = empty + p.ring;
   uint64_t* aempty = afull + aring;
   uint64_t* tfull = aempty + aring;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* bready = tempty + 2;
+  uint64_t* tempty = tfull + NB;
+  uint64_t* bfull = tempty + NB;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.tmem_slot_off);
 
   const int warp = threadIdx.x >> 5;
@@ -130,6 +153,13 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
   const int g1 = static_cast<int>(static_cast<long long>(rank + 1) * G / p.split);
   const int nst = g1 - g0;
 
+  uint8_t* raw = smem + L.raw_off;
+  uint8_t* abuf = smem + L.a_off;
+  uint8_t* bop = smem + L.b_off;
+  float* ass = reinterpret_cast<float*>(smem + L.as_off);
+  int* asum = reinterpret_cast<int*>(smem + L.asum_off);
+  float* part = reinterpret_cast<float*>(smem + L.part_off);
+
   // Drain thread -> output column of this tile (TMEM lane 32*(warp%4) + lane).
   const bool is_drain = warp >= kTcWarpDrain && warp < kTcWarpDrain + 4;
   const int q = warp & 3;
@@ -146,23 +176,59 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
 #pragma unroll
   for (int m = 0; m < MR; ++m) pre_res[m] = 0.0f;
 
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < p.ring; ++i) {
-      mbar_init(full + i, 1);
-      mbar_init(empty + i, WB == 8 ? 1 : 8);
-    }
-    for (int i = 0; i < aring; ++i) {
-      mbar_init(afull + i, 128);
-      mbar_init(aempty + i, 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(tfull + i, 1);
-      mbar_init(tempty + i, kDrainThreads);
-    }
-    mbar_init(bready, kDrainThreads);
-    fence_mbar_init();
+  // ---------------------------------------------------------------- set-up
+  uint32_t stage_bytes = 0;
+#pragma unroll
+  for (int s = 0; s < NS; ++s) {
+    const GemvSeg& sg = NS == 1 ? S0 : p.seg[s];
+    stage_bytes += WB == 8 ? 64 * kTileN : 32 * kTileN + L.nsub * kTileN * 2 + (sg.has_z ? L.nsub * kTileN : 0);
   }
-  if (warp == kTcWarpMma) {
+  auto issue_stage = [&](int i, uint64_t pol) {
+    const int slot = i % p.ring;
+    mbar_arrive_expect_tx(full + slot, stage_bytes);
+    const int g = g0 + i;
+#pragma unroll
+    for (int s = 0; s < NS; ++s) {
+      const GemvSeg& sg = NS == 1 ? S0 : p.seg[s];
+      uint8_t* dst = raw + slot * L.raw_stage + s * L.raw_stream;
+      if (WB == 8) {
+        tma_load_2d(dst, &sg.tw, n0, g * 64, full + slot, pol);
+      } else {
+        tma_load_2d(dst, &sg.tw, n0, g * 32, full + slot, pol);
+        const int srow = (g * 64) / p.wgrp;
+        tma_load_2d(dst + 32 * kTileN, &sg.ts, n0, srow, full + slot, pol);
+        if (sg.has_z) tma_load_2d(dst + 32 * kTileN + L.nsub * kTileN * 2, &sg.tz, n0, srow, full + slot, pol);
+      }
+    }
+  };
+  const int prefill = nst < p.ring ? nst : p.ring;
+
+  if (warp == kTcWarpTma) {
+    if (lane == 0) {
+      for (int i = 0; i < p.ring; ++i) {
+        mbar_init(full + i, 1);
+        mbar_init(empty + i, WB == 8 ? 1 : 8);
+      }
+      for (int i = 0; i < aring; ++i) {
+        mbar_init(afull + i, 128);
+        mbar_init(aempty + i, 1);
+      }
+      for (int i = 0; i < NB; ++i) {
+        mbar_init(tfull + i, 1);
+        mbar_init(tempty + i, kDrainThreads);
+      }
+      mbar_init(bfull, 1);
+      fence_mbar_init();
+    }
+    __syncwarp();
+    // Weights never depend on the preceding kernel: request the first
+    // ring-full of stages right away, before the CTA-wide barrier.
+    if (elect_one()) {
+      const uint64_t pol = l2_policy_evict_first();
+      for (int i = 0; i < prefill; ++i) issue_stage(i, pol);
+    }
+    __syncwarp();
+  } else if (warp == kTcWarpMma) {
     tmem_alloc(tmem_slot, L.tmem_cols);
     tmem_relinquish();
   }
@@ -171,16 +237,6 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
 
-  uint8_t* raw = smem + L.raw_off;
-  uint8_t* abuf = smem + L.a_off;
-  uint8_t* bop = smem + L.b_off;
-  float* ass = reinterpret_cast<float*>(smem + L.as_off);
-  int* asum = reinterpret_cast<int*>(smem + L.asum_off);
-  float* part = reinterpret_cast<float*>(smem + L.part_off);
-  // B operand (K-major, no swizzle): core matrix (k-chunk kc, row group mg) of
-  // group gl at gl*64*NM + (kc*(NM/8) + mg)*128; rows of 16 bytes.
-  constexpr uint32_t kLboB = (NM / 8) * 128;  // K-direction core-matrix stride
-  constexpr uint32_t kSboB = 128;             // row-group stride
   // TMEM accumulator column of (buffer, stream, sub-block).
   auto tcol = [&](int tb, int s, int sub) -> uint32_t {
     return static_cast<uint32_t>(((tb * NS + s) * NSUB + sub) * NM);
@@ -188,67 +244,48 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
 
   if (warp == kTcWarpTma) {
     // ------------------------------------------------------------------ producer
-    if (lane == 0) {
-      const uint64_t pol = l2_policy_evict_first();
-      uint32_t bytes = 0;
-#pragma unroll
-      for (int s = 0; s < NS; ++s) {
-        const GemvSeg& sg = NS == 1 ? S0 : p.seg[s];
-        bytes += WB == 8 ? 64 * kTileN : 32 * kTileN + L.nsub * kTileN * 2 + (sg.has_z ? L.nsub * kTileN : 0);
+    const uint64_t pol = l2_policy_evict_first();
+    for (int i = prefill; i < nst; ++i) {
+      const int slot = i % p.ring;
+      if (!mbar_wait(empty + slot, ((i / p.ring) & 1) ^ 1)) {
+        if (lane == 0) atomicOr(p.fault, kFaultEmptyWait);
+        break;
       }
-      for (int i = 0; i < nst; ++i) {
-        const int slot = i % p.ring;
-        if (i >= p.ring && !mbar_wait(empty + slot, ((i / p.ring) & 1) ^ 1)) {
-          atomicOr(p.fault, kFaultEmptyWait);
-          break;
-        }
-        mbar_arrive_expect_tx(full + slot, bytes);
-        const int g = g0 + i;
-#pragma unroll
-        for (int s = 0; s < NS; ++s) {
-          const GemvSeg& sg = NS == 1 ? S0 : p.seg[s];
-          uint8_t* dst = raw + slot * L.raw_stage + s * L.raw_stream;
-          if (WB == 8) {
-            tma_load_2d(dst, &sg.tw, n0, g * 64, full + slot, pol);
-          } else {
-            tma_load_2d(dst, &sg.tw, n0, g * 32, full + slot, pol);
-            const int srow = (g * 64) / p.wgrp;
-            tma_load_2d(dst + 32 * kTileN, &sg.ts, n0, srow, full + slot, pol);
-            if (sg.has_z)
-              tma_load_2d(dst + 32 * kTileN + L.nsub * kTileN * 2, &sg.tz, n0, srow, full + slot, pol);
-          }
-        }
-      }
+      if (elect_one()) issue_stage(i, pol);
+      __syncwarp();
     }
-    __syncwarp();
   } else if (warp == kTcWarpMma) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_i8(128, NM, WB == 8, true, true, false);
-      bool ok = mbar_wait(bready, 0);
-      if (!ok) atomicOr(p.fault, kFaultMmaWait);
-      for (int i = 0; ok && i < nst; ++i) {
-        const int tb = i & 1;
-        const int slot = i % p.ring;
-        const int as_ = WB == 4 ? i % aring_div : 0;
-        if (WB == 8) ok = mbar_wait(full + slot, (i / p.ring) & 1);
-        else ok = mbar_wait(afull + as_, (i / aring_div) & 1);
-        ok = ok && mbar_wait(tempty + tb, ((i >> 1) & 1) ^ 1);
-        if (!ok) {
-          atomicOr(p.fault, kFaultMmaWait);
-          break;
-        }
-        tc_fence_after();
+    pdl_wait();
+    if (elect_one()) {
+      mbar_arrive_expect_tx(bfull, L.nbox * NM * 128);
+      const uint64_t pol = l2_policy_evict_last();
+      for (uint32_t b = 0; b < L.nbox; ++b)
+        tma_load_2d(bop + b * NM * 128, &p.ta, g0 * 64 + 128 * b, m0, bfull, pol);
+    }
+    __syncwarp();
+    constexpr uint32_t idesc = idesc_i8(128, NM, WB == 8, true, true, false);
+    bool ok = mbar_wait(bfull, 0);
+    for (int i = 0; ok && i < nst; ++i) {
+      const int tb = i % NB;
+      const int slot = i % p.ring;
+      const int as_ = WB == 4 ? i % aring_div : 0;
+      if (WB == 8) ok = mbar_wait(full + slot, (i / p.ring) & 1);
+      else ok = mbar_wait(afull + as_, (i / aring_div) & 1);
+      if (i >= NB) ok = ok && mbar_wait(tempty + tb, ((i / NB) & 1) ^ 1);
+      if (!ok) break;
+      tc_fence_after();
+      if (elect_one()) {
+        const uint32_t b_row = smem_u32(bop + (i >> 1) * NM * 128) + (i & 1) * 64;
 #pragma unroll
         for (int s = 0; s < NS; ++s) {
           const uint8_t* a_tile =
               WB == 8 ? raw + slot * L.raw_stage + s * L.raw_stream : abuf + (as_ * NS + s) * 64 * kTileN;
           const uint32_t a_addr = smem_u32(a_tile);
-          const uint32_t b_addr = smem_u32(bop + i * 64 * NM);
 #pragma unroll
           for (int j = 0; j < 2; ++j) {
             const uint64_t ad = smem_desc(a_addr + 4096 * j, 8192, 1024, kLayoutSw128);
-            const uint64_t bd = smem_desc(b_addr + 2 * j * kLboB, kLboB, kSboB, kLayoutNone);
+            const uint64_t bd = smem_desc(b_row + 32 * j, 16, 1024, kLayoutSw128);
             const uint32_t d = tbase + tcol(tb, s, NSUB == 2 ? j : 0);
             tc_mma_i8(d, ad, bd, idesc, NSUB == 2 ? 0u : static_cast<uint32_t>(j));
           }
@@ -256,8 +293,9 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
         tc_commit(tfull + tb);
         tc_commit(WB == 8 ? empty + slot : aempty + as_);
       }
+      __syncwarp();
     }
-    __syncwarp();
+    if (!ok && lane == 0) atomicOr(p.fault, kFaultMmaWait);
   } else if (is_drain) {
     // ------------------------------------------------------------------ drain
     const int td = threadIdx.x - kTcWarpDrain * 32;
@@ -269,37 +307,30 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
         if (m0 + m < p.M)
           pre_res[m] = __bfloat162float(res[static_cast<long long>(m0 + m) * p.ldr + S0.out_col + en]);
     }
-    // Stage the activation operand (32-byte units: row m, half-group h).
-    const int kbase = g0 * 64;
-    for (int idx = td; idx < NM * nst * 2; idx += kDrainThreads) {
-      const int m = idx % NM;
-      const int gh = idx / NM;  // gl * 2 + h
-      const int gl = gh >> 1, h = gh & 1;
-      int4 v0 = make_int4(0, 0, 0, 0), v1 = make_int4(0, 0, 0, 0);
-      if (m0 + m < p.M) {
-        const int4* src = reinterpret_cast<const int4*>(p.a_q + static_cast<long long>(m0 + m) * p.K + kbase +
-                                                        gl * 64 + h * 32);
-        v0 = __ldg(src);
-        v1 = __ldg(src + 1);
-      }
-      uint8_t* gb = bop + gl * 64 * NM + (m & 7) * 16;
-      *reinterpret_cast<int4*>(gb + ((2 * h) * (NM / 8) + (m >> 3)) * 128) = v0;
-      *reinterpret_cast<int4*>(gb + ((2 * h + 1) * (NM / 8) + (m >> 3)) * 128) = v1;
-      if (WB == 4) {
-        int s = 0;
-        s = dp4a_ss(v0.x, 0x01010101, s); s = dp4a_ss(v0.y, 0x01010101, s);
-        s = dp4a_ss(v0.z, 0x01010101, s); s = dp4a_ss(v0.w, 0x01010101, s);
-        s = dp4a_ss(v1.x, 0x01010101, s); s = dp4a_ss(v1.y, 0x01010101, s);
-        s = dp4a_ss(v1.z, 0x01010101, s); s = dp4a_ss(v1.w, 0x01010101, s);
-        asum[gh * NM + m] = s;
-      }
-    }
     for (int idx = td; idx < NM * nst; idx += kDrainThreads) {
       const int m = idx % NM, gl = idx / NM;
       ass[gl * NM + m] = (m0 + m < p.M) ? __ldg(p.a_s + static_cast<long long>(m0 + m) * G + g0 + gl) : 0.0f;
     }
-    fence_proxy_async_smem();
-    mbar_arrive(bready);
+    bool ok = true;
+    if (WB == 4) {
+      // Sum of the activation over each 32-K half group, read from the
+      // swizzled B tile (rows past M are zero-filled by the TMA).
+      ok = mbar_wait(bfull, 0);
+      for (int idx = td; ok && idx < NM * nst * 2; idx += kDrainThreads) {
+        const int m = idx % NM, gh = idx / NM;
+        const int gl = gh >> 1, h = gh & 1;
+        const int c0 = (gl & 1) * 4 + h * 2;  // logical 16-byte chunk in the 128-byte row
+        const uint8_t* row = bop + (gl >> 1) * NM * 128 + m * 128;
+        const int4 v0 = *reinterpret_cast<const int4*>(row + ((c0 ^ (m & 7)) << 4));
+        const int4 v1 = *reinterpret_cast<const int4*>(row + (((c0 + 1) ^ (m & 7)) << 4));
+        int sa = 0;
+        sa = dp4a_ss(v0.x, 0x01010101, sa); sa = dp4a_ss(v0.y, 0x01010101, sa);
+        sa = dp4a_ss(v0.z, 0x01010101, sa); sa = dp4a_ss(v0.w, 0x01010101, sa);
+        sa = dp4a_ss(v1.x, 0x01010101, sa); sa = dp4a_ss(v1.y, 0x01010101, sa);
+        sa = dp4a_ss(v1.z, 0x01010101, sa); sa = dp4a_ss(v1.w, 0x01010101, sa);
+        asum[gh * NM + m] = sa;
+      }
+    }
     named_bar_sync(1, kDrainThreads);  // ass / asum visible to all drain threads
     pdl_launch_dependents();
 
@@ -310,16 +341,12 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
       for (int m = 0; m < MR; ++m) acc[s][m] = 0.0f;
 
     const uint32_t lane_base = tbase + (static_cast<uint32_t>(32 * q) << 16);
-    for (int i = 0; i < nst; ++i) {
-      const int tb = i & 1;
+    for (int i = 0; ok && i < nst; ++i) {
+      const int tb = i % NB;
       const int slot = i % p.ring;
-      bool ok = true;
       if (WB == 4) ok = mbar_wait(full + slot, (i / p.ring) & 1);
-      ok = ok && mbar_wait(tfull + tb, (i >> 1) & 1);
-      if (!ok) {
-        if (lane == 0) atomicOr(p.fault, kFaultFullWait);
-        break;
-      }
+      ok = ok && mbar_wait(tfull + tb, (i / NB) & 1);
+      if (!ok) break;
       tc_fence_after();
       uint32_t r[NS][2][LDN];
 #pragma unroll
@@ -363,6 +390,7 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
         if (lane == 0) mbar_arrive(empty + slot);
       }
     }
+    if (!ok && lane == 0) atomicOr(p.fault, kFaultFullWait);
 #pragma unroll
     for (int s = 0; s < NS; ++s)
 #pragma unroll
@@ -404,6 +432,7 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
   }
 
   // ------------------------------------------------------------------ cluster combine + epilogue
+  __syncwarp();
   cg::cluster_group cluster = cg::this_cluster();
   tc_fence_before();
   cluster.sync();
