@@ -224,14 +224,14 @@ int tc_mr(int wb, int64_t M) {
 }
 
 struct TcPlan {
-  int split, ring, aring, gmax;
+  int split, gmax, bs, rb, ab, nbb;
   size_t smem;
 };
 
 TcPlan plan_tc(int wb, int mr, int ns, int K, int wgrp, int tiles, int rowblocks, int sms) {
   const int G = K / kGroup;
   const int nm = mr < 16 ? 16 : mr;
-  TcPlan best{1, 1, wb == 4 ? 2 : 0, G, 0};  // W4: two unpacked A stages
+  TcPlan best{1, G, 1, 1, 0, 1, 0};
   double best_cost = 1e30;
   const int smax = G < 8 ? G : 8;
   for (int s = 1; s <= smax; ++s) {
@@ -247,15 +247,32 @@ TcPlan plan_tc(int wb, int mr, int ns, int K, int wgrp, int tiles, int rowblocks
       best.gmax = gmax;
     }
   }
-  // ~100 KB per CTA: two CTAs per SM (this launch and the next one under PDL).
-  const uint32_t budget = (tune_budget() > 0 ? tune_budget() : 100) * 1024;
-  const TcLayout l1 = tc_layout(wb, nm, ns, wgrp, best.gmax, 1, best.aring);
-  const uint32_t fixed = l1.total - l1.raw_stage;
-  int ring = static_cast<int>((budget > fixed ? budget - fixed : 0) / l1.raw_stage);
-  if (ring < 2) ring = 2;
-  if (ring > best.gmax) ring = best.gmax;
-  best.ring = ring;
-  const TcLayout L = tc_layout(wb, nm, ns, wgrp, best.gmax, ring, best.aring);
+  // Batch plan.  ~110 KB per CTA keeps two CTAs resident per SM (this launch
+  // and the next one under PDL); the tensor-memory share is 256 columns.
+  const uint32_t budget = (tune_budget() > 0 ? tune_budget() : 110) * 1024;
+  const TcLayout base = tc_layout(wb, nm, ns, wgrp, best.gmax, 0, 0, 0, 2);
+  const uint32_t fixed = base.total;
+  const uint32_t per_buf = base.per_buf;
+  const int tmem_groups = static_cast<int>(kTmemBudget / per_buf);
+  const uint32_t raw_g = base.raw_stage;               // weight ring bytes per group
+  const uint32_t a_g = wb == 4 ? ns * 64 * kTileN : 0;  // unpacked A bytes per group
+  const uint32_t room = budget > fixed ? budget - fixed : 0;
+  if (best.gmax <= tmem_groups && best.gmax * (raw_g + a_g) <= room) {
+    best.bs = best.gmax;  // whole K range in one batch
+    best.rb = 1;
+    best.ab = wb == 4 ? 1 : 0;
+    best.nbb = 1;
+  } else {
+    const int rb = 2, ab = wb == 4 ? 2 : 0;
+    int bs = static_cast<int>(room / (rb * raw_g + ab * a_g));
+    if (bs > tmem_groups / 2) bs = tmem_groups / 2;
+    if (bs < 1) bs = 1;
+    best.bs = bs;
+    best.rb = rb;
+    best.ab = ab;
+    best.nbb = 2;
+  }
+  const TcLayout L = tc_layout(wb, nm, ns, wgrp, best.gmax, best.bs, best.rb, best.ab, best.nbb);
   // At most 512 / tmem_cols CTAs may share an SM, or a tensor-memory
   // allocation could wait on a CTA of the next launch: pad shared memory so
   // that no more CTAs than that fit.
@@ -323,9 +340,11 @@ int run_tc(int wb, int epi, GemvArgs& a, int tiles, cudaStream_t st) {
   if (int r = make_map(&a.ta, a.a_q, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.K, a.M, a.K, 128, nm, true)) return r;
   const TcPlan pl = plan_tc(wb, mr, ns, a.K, a.wgrp, tiles, rowblocks, di.sms);
   a.split = pl.split;
-  a.ring = pl.ring;
-  a.aring = pl.aring;
   a.gmax = pl.gmax;
+  a.bs = pl.bs;
+  a.rb = pl.rb;
+  a.ab = pl.ab;
+  a.nbb = pl.nbb;
   a.fault = di.fault;
   const dim3 grid(pl.split, tiles, rowblocks);
   if (wb == 8) {

@@ -70,7 +70,11 @@ struct GemvArgs {
   int M, K, wgrp;
   int split;          // K ranges per tile == cluster size
   int ring;           // stages in the shared-memory ring
-  int aring;          // tcgen05 W4 path: stages of the unpacked-weight ring
+  int aring;          // (unused by tc_gemv)
+  int bs;             // tc_gemv: 64-K groups per batch (one barrier / commit per batch)
+  int rb;             // tc_gemv: batch slots in the weight ring
+  int ab;             // tc_gemv W4: batch slots in the unpacked-weight ring
+  int nbb;            // tc_gemv: batch accumulators in tensor memory
   int gmax;           // max groups one CTA handles
   void* out;          // bf16, row stride ldo
   long long ldo;

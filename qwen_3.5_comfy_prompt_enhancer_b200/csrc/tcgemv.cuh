@@ -15,26 +15,30 @@
 // Integer sums are exact; only the fp32 order of the K-split reduction
 // differs from the reference.
 //
-// Warp roles (one CTA = one 128-column tile x one K range).  Every role runs
-// as a converged warp; an elected lane issues TMA / MMA / commit (a lone
-// active lane waits on mbarriers about twice as slowly).
-//   warp 0      TMA producer: weight rows (+ W4 group scales / zeros) into a
-//               ring of shared-memory stages, one stage per 64-K group.  The
-//               first ring-full of stages is requested before the CTA-wide
-//               set-up barrier.
+// Batches.  The CTA's K range (nst groups of 64) is processed in batches of
+// `bs` groups.  Every hand-off between warps -- weights landed, weights
+// unpacked, accumulators ready, slots free -- is one mbarrier phase per
+// batch, not per group: a completed-phase wait costs a converged warp
+// ~150-200 cycles and a tcgen05.commit ~60, against ~60-90 for one
+// 128x16x32 MMA, so per-group hand-offs would dominate the issue loop.  When
+// the whole K range fits (the usual decode case) there is a single batch.
+//
+// Warp roles (one CTA = one 128-column tile x one K range); every role runs
+// as a converged warp and an elected lane issues TMA / MMA / commit:
+//   warp 0      TMA producer: weight rows (+ W4 group scales / zeros) of a
+//               batch into a ring slot.  The first ring-full is requested
+//               before the CTA-wide set-up barrier (weights never depend on
+//               the preceding kernel).
 //   warp 1      tensor-memory owner and MMA issuer.  After the grid
-//               dependency it loads the activation tile by TMA.  Each
-//               in-flight group gets its own accumulator (up to the CTA's
-//               256-column share), so the issuer only waits for the drain
-//               when it wraps around that pool.
-//   warps 2-5   drain: activation scales, then per group read the int32
-//               accumulator (thread = output column), rescale, sum; finally
+//               dependency it loads the activation tile by TMA.
+//   warps 2-5   drain: activation scales, then per batch read the int32
+//               accumulators (thread = output column), rescale, sum; finally
 //               the epilogue.
-//   warps 6-9   (W4 only) unpack: packed nibbles -> uint8 rows of the
-//               swizzled A tile.  Low nibble of packed row j is K = 2j, high
-//               nibble K = 2j+1.  The MMA multiplies unsigned nibbles with
-//               signed activations; the zero point is removed exactly in
-//               integers by the drain: sum(a*(nib - z)) = sum(a*nib) - z*sum(a).
+//   warps 6-9   (W4 only) unpack: packed nibbles -> uint8 rows of swizzled A
+//               tiles.  Low nibble of packed row j is K = 2j, high nibble
+//               K = 2j+1.  The MMA multiplies unsigned nibbles with signed
+//               activations; the zero point is removed exactly in integers
+//               by the drain: sum(a*(nib - z)) = sum(a*nib) - z*sum(a).
 //
 // Split-K across the CTAs of a thread-block cluster, combined through
 // distributed shared memory in a fixed order (no global scratch), as in
@@ -62,7 +66,7 @@ __host__ __device__ constexpr int tc_threads(int wb) { return (wb == 8 ? 6 : 10)
 
 struct TcLayout {
   uint32_t nsub, raw_stream, raw_stage, raw_off, a_off, b_off, nbox, as_off, asum_off, part_off, xchg_off,
-      bar_off, tmem_slot_off, total, tmem_cols, nbuf;
+      bar_off, tmem_slot_off, total, tmem_cols, per_buf;
 };
 
 __host__ __device__ inline uint32_t pow2_at_least(uint32_t x) {
@@ -72,18 +76,19 @@ __host__ __device__ inline uint32_t pow2_at_least(uint32_t x) {
 }
 
 // Shared-memory carve-up relative to a 1024-byte aligned base; `total`
-// includes 1 KB of alignment slack.
-__host__ __device__ inline TcLayout tc_layout(int wb, int nm, int ns, int wgrp, int gmax, int ring,
-                                              int aring) {
+// includes 1 KB of alignment slack.  bs groups per batch, rb weight-ring
+// slots, ab unpacked-ring slots (W4), nbb accumulator batches.
+__host__ __device__ inline TcLayout tc_layout(int wb, int nm, int ns, int wgrp, int gmax, int bs, int rb, int ab,
+                                              int nbb) {
   TcLayout L;
   L.nsub = (wb == 4 && wgrp == 32) ? 2 : 1;
   L.raw_stream = wb == 8 ? 64 * kTileN : 32 * kTileN + L.nsub * kTileN * 2 + L.nsub * kTileN;
   L.raw_stage = ns * L.raw_stream;
   uint32_t off = 0;
   L.raw_off = off;
-  off = align_up(off + ring * L.raw_stage, 1024);
+  off = align_up(off + rb * bs * L.raw_stage, 1024);
   L.a_off = off;
-  if (wb == 4) off = align_up(off + aring * ns * 64 * kTileN, 1024);
+  if (wb == 4) off = align_up(off + ab * bs * ns * 64 * kTileN, 1024);
   // Activation operand: boxes of 128 K (one swizzle row) x nm rows.
   L.b_off = off;
   L.nbox = (gmax + 1) / 2;
@@ -96,19 +101,13 @@ __host__ __device__ inline TcLayout tc_layout(int wb, int nm, int ns, int wgrp, 
   off = align_up(off + ns * nm * kTileN * 4, 16);
   L.xchg_off = off;
   off = align_up(off + 4 * nm * 4, 16);
-  // One accumulator (ns x nsub x nm columns) per in-flight group, up to the
-  // CTA's tensor-memory budget.
-  const uint32_t per_buf = ns * L.nsub * nm;
-  uint32_t nbuf = kTmemBudget / per_buf;
-  if (nbuf > static_cast<uint32_t>(gmax)) nbuf = gmax;
-  if (nbuf < 2) nbuf = 2;
-  L.nbuf = nbuf;
   L.bar_off = off;
-  off = align_up(off + 8 * (2 * ring + 2 * aring + 2 * nbuf + 1), 16);
+  off = align_up(off + 8 * (2 * rb + 2 * ab + 2 * nbb + 1), 16);
   L.tmem_slot_off = off;
   off += 16;
   L.total = off + 1024;
-  L.tmem_cols = pow2_at_least(nbuf * per_buf);
+  L.per_buf = ns * L.nsub * nm;
+  L.tmem_cols = pow2_at_least(nbb * bs * L.per_buf);
   return L;
 }
 
@@ -121,18 +120,18 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
-  const int aring = WB == 4 ? p.aring : 0;
-  const int aring_div = aring > 0 ? aring : 1;  // W8 has no unpacked ring
-  const TcLayout L = tc_layout(WB, NM, NS, p.wgrp, p.gmax, p.ring, aring);
+  const int BS = p.bs, RB = p.rb, NBB = p.nbb;
+  const int AB = WB == 4 ? p.ab : 0;
+  const int ab_div = AB > 0 ? AB : 1;  // W8 has no unpacked ring
+  const TcLayout L = tc_layout(WB, NM, NS, p.wgrp, p.gmax, BS, RB, AB, NBB);
   const int NSUB = static_cast<int>(L.nsub);
-  const int NB = static_cast<int>(L.nbuf);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
-  uint64_t* empty = full + p.ring;
-  uint64_t* afull = empty + p.ring;
-  uint64_t* aempty = afull + aring;
-  uint64_t* tfull = aempty + aring;
-  uint64_t* tempty = tfull + NB;
-  uint64_t* bfull = tempty + NB;
+  uint64_t* empty = full + RB;
+  uint64_t* afull = empty + RB;
+  uint64_t* aempty = afull + AB;
+  uint64_t* tfull = aempty + AB;
+  uint64_t* tempty = tfull + NBB;
+  uint64_t* bfull = tempty + NBB;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.tmem_slot_off);
 
   const int warp = threadIdx.x >> 5;
@@ -152,6 +151,8 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
   const int g0 = static_cast<int>(static_cast<long long>(rank) * G / p.split);
   const int g1 = static_cast<int>(static_cast<long long>(rank + 1) * G / p.split);
   const int nst = g1 - g0;
+  const int nbatch = (nst + BS - 1) / BS;
+  auto batch_len = [&](int b) { return (b + 1) * BS <= nst ? BS : nst - b * BS; };
 
   uint8_t* raw = smem + L.raw_off;
   uint8_t* abuf = smem + L.a_off;
@@ -159,6 +160,9 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
   float* ass = reinterpret_cast<float*>(smem + L.as_off);
   int* asum = reinterpret_cast<int*>(smem + L.asum_off);
   float* part = reinterpret_cast<float*>(smem + L.part_off);
+  // Raw stage of (ring slot, group-in-batch, stream); A tile of (slot, j, stream).
+  auto raw_stage = [&](int rs, int j, int s) { return raw + (rs * BS + j) * L.raw_stage + s * L.raw_stream; };
+  auto a_tile = [&](int as, int j, int s) { return abuf + ((as * BS + j) * NS + s) * 64 * kTileN; };
 
   // Drain thread -> output column of this tile (TMEM lane 32*(warp%4) + lane).
   const bool is_drain = warp >= kTcWarpDrain && warp < kTcWarpDrain + 4;
@@ -177,43 +181,46 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
   for (int m = 0; m < MR; ++m) pre_res[m] = 0.0f;
 
   // ---------------------------------------------------------------- set-up
-  uint32_t stage_bytes = 0;
+  uint32_t group_bytes = 0;
 #pragma unroll
   for (int s = 0; s < NS; ++s) {
     const GemvSeg& sg = NS == 1 ? S0 : p.seg[s];
-    stage_bytes += WB == 8 ? 64 * kTileN : 32 * kTileN + L.nsub * kTileN * 2 + (sg.has_z ? L.nsub * kTileN : 0);
+    group_bytes += WB == 8 ? 64 * kTileN : 32 * kTileN + L.nsub * kTileN * 2 + (sg.has_z ? L.nsub * kTileN : 0);
   }
-  auto issue_stage = [&](int i, uint64_t pol) {
-    const int slot = i % p.ring;
-    mbar_arrive_expect_tx(full + slot, stage_bytes);
-    const int g = g0 + i;
+  auto issue_batch = [&](int b, uint64_t pol) {
+    const int rs = b % RB;
+    const int nb = batch_len(b);
+    mbar_arrive_expect_tx(full + rs, group_bytes * nb);
+    for (int j = 0; j < nb; ++j) {
+      const int g = g0 + b * BS + j;
 #pragma unroll
-    for (int s = 0; s < NS; ++s) {
-      const GemvSeg& sg = NS == 1 ? S0 : p.seg[s];
-      uint8_t* dst = raw + slot * L.raw_stage + s * L.raw_stream;
-      if (WB == 8) {
-        tma_load_2d(dst, &sg.tw, n0, g * 64, full + slot, pol);
-      } else {
-        tma_load_2d(dst, &sg.tw, n0, g * 32, full + slot, pol);
-        const int srow = (g * 64) / p.wgrp;
-        tma_load_2d(dst + 32 * kTileN, &sg.ts, n0, srow, full + slot, pol);
-        if (sg.has_z) tma_load_2d(dst + 32 * kTileN + L.nsub * kTileN * 2, &sg.tz, n0, srow, full + slot, pol);
+      for (int s = 0; s < NS; ++s) {
+        const GemvSeg& sg = NS == 1 ? S0 : p.seg[s];
+        uint8_t* dst = raw_stage(rs, j, s);
+        if (WB == 8) {
+          tma_load_2d(dst, &sg.tw, n0, g * 64, full + rs, pol);
+        } else {
+          tma_load_2d(dst, &sg.tw, n0, g * 32, full + rs, pol);
+          const int srow = (g * 64) / p.wgrp;
+          tma_load_2d(dst + 32 * kTileN, &sg.ts, n0, srow, full + rs, pol);
+          if (sg.has_z) tma_load_2d(dst + 32 * kTileN + L.nsub * kTileN * 2, &sg.tz, n0, srow, full + rs, pol);
+        }
       }
     }
   };
-  const int prefill = nst < p.ring ? nst : p.ring;
+  const int prefill = nbatch < RB ? nbatch : RB;
 
   if (warp == kTcWarpTma) {
     if (lane == 0) {
-      for (int i = 0; i < p.ring; ++i) {
+      for (int i = 0; i < RB; ++i) {
         mbar_init(full + i, 1);
         mbar_init(empty + i, WB == 8 ? 1 : 8);
       }
-      for (int i = 0; i < aring; ++i) {
+      for (int i = 0; i < AB; ++i) {
         mbar_init(afull + i, 128);
         mbar_init(aempty + i, 1);
       }
-      for (int i = 0; i < NB; ++i) {
+      for (int i = 0; i < NBB; ++i) {
         mbar_init(tfull + i, 1);
         mbar_init(tempty + i, kDrainThreads);
       }
@@ -221,11 +228,9 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
       fence_mbar_init();
     }
     __syncwarp();
-    // Weights never depend on the preceding kernel: request the first
-    // ring-full of stages right away, before the CTA-wide barrier.
     if (elect_one()) {
       const uint64_t pol = l2_policy_evict_first();
-      for (int i = 0; i < prefill; ++i) issue_stage(i, pol);
+      for (int b = 0; b < prefill; ++b) issue_batch(b, pol);
     }
     __syncwarp();
   } else if (warp == kTcWarpMma) {
@@ -237,21 +242,21 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
 
-  // TMEM accumulator column of (buffer, stream, sub-block).
-  auto tcol = [&](int tb, int s, int sub) -> uint32_t {
-    return static_cast<uint32_t>(((tb * NS + s) * NSUB + sub) * NM);
+  // TMEM accumulator column of (batch buffer, group-in-batch, stream, sub-block).
+  auto tcol = [&](int tb, int j, int s, int sub) -> uint32_t {
+    return static_cast<uint32_t>((((tb * BS + j) * NS + s) * NSUB + sub) * NM);
   };
 
   if (warp == kTcWarpTma) {
     // ------------------------------------------------------------------ producer
     const uint64_t pol = l2_policy_evict_first();
-    for (int i = prefill; i < nst; ++i) {
-      const int slot = i % p.ring;
-      if (!mbar_wait(empty + slot, ((i / p.ring) & 1) ^ 1)) {
+    for (int b = prefill; b < nbatch; ++b) {
+      const int rs = b % RB;
+      if (!mbar_wait(empty + rs, ((b / RB) & 1) ^ 1)) {
         if (lane == 0) atomicOr(p.fault, kFaultEmptyWait);
         break;
       }
-      if (elect_one()) issue_stage(i, pol);
+      if (elect_one()) issue_batch(b, pol);
       __syncwarp();
     }
   } else if (warp == kTcWarpMma) {
@@ -260,38 +265,40 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
     if (elect_one()) {
       mbar_arrive_expect_tx(bfull, L.nbox * NM * 128);
       const uint64_t pol = l2_policy_evict_last();
-      for (uint32_t b = 0; b < L.nbox; ++b)
-        tma_load_2d(bop + b * NM * 128, &p.ta, g0 * 64 + 128 * b, m0, bfull, pol);
+      for (uint32_t bx = 0; bx < L.nbox; ++bx)
+        tma_load_2d(bop + bx * NM * 128, &p.ta, g0 * 64 + 128 * bx, m0, bfull, pol);
     }
     __syncwarp();
     constexpr uint32_t idesc = idesc_i8(128, NM, WB == 8, true, true, false);
     bool ok = mbar_wait(bfull, 0);
-    for (int i = 0; ok && i < nst; ++i) {
-      const int tb = i % NB;
-      const int slot = i % p.ring;
-      const int as_ = WB == 4 ? i % aring_div : 0;
-      if (WB == 8) ok = mbar_wait(full + slot, (i / p.ring) & 1);
-      else ok = mbar_wait(afull + as_, (i / aring_div) & 1);
-      if (i >= NB) ok = ok && mbar_wait(tempty + tb, ((i / NB) & 1) ^ 1);
+    for (int b = 0; ok && b < nbatch; ++b) {
+      const int rs = b % RB;
+      const int as = WB == 4 ? b % ab_div : 0;
+      const int tb = b % NBB;
+      if (WB == 8) ok = mbar_wait(full + rs, (b / RB) & 1);
+      else ok = mbar_wait(afull + as, (b / ab_div) & 1);
+      if (b >= NBB) ok = ok && mbar_wait(tempty + tb, ((b / NBB) & 1) ^ 1);
       if (!ok) break;
       tc_fence_after();
       if (elect_one()) {
-        const uint32_t b_row = smem_u32(bop + (i >> 1) * NM * 128) + (i & 1) * 64;
+        const int nb = batch_len(b);
+        for (int j = 0; j < nb; ++j) {
+          const int i = b * BS + j;  // group within the CTA's K range
+          const uint32_t b_row = smem_u32(bop + (i >> 1) * NM * 128) + (i & 1) * 64;
 #pragma unroll
-        for (int s = 0; s < NS; ++s) {
-          const uint8_t* a_tile =
-              WB == 8 ? raw + slot * L.raw_stage + s * L.raw_stream : abuf + (as_ * NS + s) * 64 * kTileN;
-          const uint32_t a_addr = smem_u32(a_tile);
+          for (int s = 0; s < NS; ++s) {
+            const uint32_t a_addr = smem_u32(WB == 8 ? raw_stage(rs, j, s) : a_tile(as, j, s));
 #pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const uint64_t ad = smem_desc(a_addr + 4096 * j, 8192, 1024, kLayoutSw128);
-            const uint64_t bd = smem_desc(b_row + 32 * j, 16, 1024, kLayoutSw128);
-            const uint32_t d = tbase + tcol(tb, s, NSUB == 2 ? j : 0);
-            tc_mma_i8(d, ad, bd, idesc, NSUB == 2 ? 0u : static_cast<uint32_t>(j));
+            for (int kk = 0; kk < 2; ++kk) {
+              const uint64_t ad = smem_desc(a_addr + 4096 * kk, 8192, 1024, kLayoutSw128);
+              const uint64_t bd = smem_desc(b_row + 32 * kk, 16, 1024, kLayoutSw128);
+              const uint32_t d = tbase + tcol(tb, j, s, NSUB == 2 ? kk : 0);
+              tc_mma_i8(d, ad, bd, idesc, NSUB == 2 ? 0u : static_cast<uint32_t>(kk));
+            }
           }
         }
         tc_commit(tfull + tb);
-        tc_commit(WB == 8 ? empty + slot : aempty + as_);
+        tc_commit(WB == 8 ? empty + rs : aempty + as);
       }
       __syncwarp();
     }
@@ -341,53 +348,59 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
       for (int m = 0; m < MR; ++m) acc[s][m] = 0.0f;
 
     const uint32_t lane_base = tbase + (static_cast<uint32_t>(32 * q) << 16);
-    for (int i = 0; ok && i < nst; ++i) {
-      const int tb = i % NB;
-      const int slot = i % p.ring;
-      if (WB == 4) ok = mbar_wait(full + slot, (i / p.ring) & 1);
-      ok = ok && mbar_wait(tfull + tb, (i / NB) & 1);
+    for (int b = 0; ok && b < nbatch; ++b) {
+      const int rs = b % RB;
+      const int tb = b % NBB;
+      if (WB == 4) ok = mbar_wait(full + rs, (b / RB) & 1);
+      ok = ok && mbar_wait(tfull + tb, (b / NBB) & 1);
       if (!ok) break;
       tc_fence_after();
-      uint32_t r[NS][2][LDN];
-#pragma unroll
-      for (int s = 0; s < NS; ++s) {
-        tmem_ld32<LDN>(lane_base + tcol(tb, s, 0), r[s][0]);
-        if (WB == 4 && NSUB == 2) tmem_ld32<LDN>(lane_base + tcol(tb, s, 1), r[s][1]);
-      }
-      tc_wait_ld();
-      tc_fence_before();
-      mbar_arrive(tempty + tb);
-      const float* as_g = ass + i * NM;
-      if (WB == 8) {
-        // out += float(int32 group sum) * a_s[m, kb]   (kernels/gemm.py:43-45)
-#pragma unroll
-        for (int s = 0; s < NS; ++s)
-#pragma unroll
-          for (int m = 0; m < MR; ++m)
-            acc[s][m] = __fadd_rn(acc[s][m], __fmul_rn(__int2float_rn(static_cast<int>(r[s][0][m])), as_g[m]));
-      } else {
-        // out += float(int32 sub-block sum) * (a_s * ws)   (kernels/w4.py:103-104)
-        const int* asum_g = asum + i * 2 * NM;
+      const int nb = batch_len(b);
+      for (int j = 0; j < nb; ++j) {
+        const int i = b * BS + j;
+        uint32_t r[NS][2][LDN];
 #pragma unroll
         for (int s = 0; s < NS; ++s) {
-          const GemvSeg& sg = NS == 1 ? S0 : p.seg[s];
-          const uint8_t* st = raw + slot * L.raw_stage + s * L.raw_stream;
-          const uint16_t* sc = reinterpret_cast<const uint16_t*>(st + 32 * kTileN);
-          const uint8_t* zz = st + 32 * kTileN + L.nsub * kTileN * 2;
-          for (int sub = 0; sub < NSUB; ++sub) {
-            const float ws = bf16_bits_to_f32(sc[sub * kTileN + c]);
-            const int z = sg.has_z ? static_cast<int>(zz[sub * kTileN + c]) : 8;
+          tmem_ld32<LDN>(lane_base + tcol(tb, j, s, 0), r[s][0]);
+          if (WB == 4 && NSUB == 2) tmem_ld32<LDN>(lane_base + tcol(tb, j, s, 1), r[s][1]);
+        }
+        tc_wait_ld();
+        const float* as_g = ass + i * NM;
+        if (WB == 8) {
+          // out += float(int32 group sum) * a_s[m, kb]   (kernels/gemm.py:43-45)
 #pragma unroll
-            for (int m = 0; m < MR; ++m) {
-              const int sa = NSUB == 2 ? asum_g[sub * NM + m] : asum_g[m] + asum_g[NM + m];
-              const int v = static_cast<int>(r[s][sub][m]) - z * sa;
-              const float t = __fmul_rn(as_g[m], ws);
-              acc[s][m] = __fadd_rn(acc[s][m], __fmul_rn(__int2float_rn(v), t));
+          for (int s = 0; s < NS; ++s)
+#pragma unroll
+            for (int m = 0; m < MR; ++m)
+              acc[s][m] = __fadd_rn(acc[s][m], __fmul_rn(__int2float_rn(static_cast<int>(r[s][0][m])), as_g[m]));
+        } else {
+          // out += float(int32 sub-block sum) * (a_s * ws)   (kernels/w4.py:103-104)
+          const int* asum_g = asum + i * 2 * NM;
+#pragma unroll
+          for (int s = 0; s < NS; ++s) {
+            const GemvSeg& sg = NS == 1 ? S0 : p.seg[s];
+            const uint8_t* st = raw_stage(rs, j, s);
+            const uint16_t* sc = reinterpret_cast<const uint16_t*>(st + 32 * kTileN);
+            const uint8_t* zz = st + 32 * kTileN + L.nsub * kTileN * 2;
+            for (int sub = 0; sub < NSUB; ++sub) {
+              const float ws = bf16_bits_to_f32(sc[sub * kTileN + c]);
+              const int z = sg.has_z ? static_cast<int>(zz[sub * kTileN + c]) : 8;
+#pragma unroll
+              for (int m = 0; m < MR; ++m) {
+                const int sa = NSUB == 2 ? asum_g[sub * NM + m] : asum_g[m] + asum_g[NM + m];
+                const int v = static_cast<int>(r[s][sub][m]) - z * sa;
+                const float t = __fmul_rn(as_g[m], ws);
+                acc[s][m] = __fadd_rn(acc[s][m], __fmul_rn(__int2float_rn(v), t));
+              }
             }
           }
         }
+      }
+      tc_fence_before();
+      mbar_arrive(tempty + tb);
+      if (WB == 4) {
         __syncwarp();
-        if (lane == 0) mbar_arrive(empty + slot);
+        if (lane == 0) mbar_arrive(empty + rs);
       }
     }
     if (!ok && lane == 0) atomicOr(p.fault, kFaultFullWait);
@@ -398,36 +411,39 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
   } else if constexpr (WB == 4) {
     // ------------------------------------------------------------------ W4 unpack
     const int u = threadIdx.x - kTcWarpUnpack * 32;
-    for (int i = 0; i < nst; ++i) {
-      const int slot = i % p.ring;
-      const int as_ = i % aring;
-      if (!mbar_wait(full + slot, (i / p.ring) & 1) || !mbar_wait(aempty + as_, ((i / aring) & 1) ^ 1)) {
+    for (int b = 0; b < nbatch; ++b) {
+      const int rs = b % RB;
+      const int as = b % AB;
+      if (!mbar_wait(full + rs, (b / RB) & 1) || !mbar_wait(aempty + as, ((b / AB) & 1) ^ 1)) {
         if (lane == 0) atomicOr(p.fault, kFaultFullWait);
         break;
       }
+      const int nb = batch_len(b);
+      for (int j = 0; j < nb; ++j) {
 #pragma unroll
-      for (int s = 0; s < NS; ++s) {
-        const uint8_t* st = raw + slot * L.raw_stage + s * L.raw_stream;
-        uint8_t* at = abuf + (as_ * NS + s) * 64 * kTileN;
+        for (int s = 0; s < NS; ++s) {
+          const uint8_t* st = raw_stage(rs, j, s);
+          uint8_t* at = a_tile(as, j, s);
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const int pr = (u >> 3) + 16 * hh;  // packed row: K = 2*pr (low), 2*pr + 1 (high)
-          const int ch = u & 7;               // 16-byte chunk = 16 columns
-          const uint4 v = *reinterpret_cast<const uint4*>(st + pr * kTileN + ch * 16);
-          uint4 lo, hi;
-          lo.x = v.x & 0x0F0F0F0Fu; hi.x = (v.x >> 4) & 0x0F0F0F0Fu;
-          lo.y = v.y & 0x0F0F0F0Fu; hi.y = (v.y >> 4) & 0x0F0F0F0Fu;
-          lo.z = v.z & 0x0F0F0F0Fu; hi.z = (v.z >> 4) & 0x0F0F0F0Fu;
-          lo.w = v.w & 0x0F0F0F0Fu; hi.w = (v.w >> 4) & 0x0F0F0F0Fu;
-          const int r0 = 2 * pr, r1 = 2 * pr + 1;
-          *reinterpret_cast<uint4*>(at + r0 * kTileN + ((ch ^ (r0 & 7)) << 4)) = lo;
-          *reinterpret_cast<uint4*>(at + r1 * kTileN + ((ch ^ (r1 & 7)) << 4)) = hi;
+          for (int hh = 0; hh < 2; ++hh) {
+            const int pr = (u >> 3) + 16 * hh;  // packed row: K = 2*pr (low), 2*pr + 1 (high)
+            const int ch = u & 7;               // 16-byte chunk = 16 columns
+            const uint4 v = *reinterpret_cast<const uint4*>(st + pr * kTileN + ch * 16);
+            uint4 lo, hi;
+            lo.x = v.x & 0x0F0F0F0Fu; hi.x = (v.x >> 4) & 0x0F0F0F0Fu;
+            lo.y = v.y & 0x0F0F0F0Fu; hi.y = (v.y >> 4) & 0x0F0F0F0Fu;
+            lo.z = v.z & 0x0F0F0F0Fu; hi.z = (v.z >> 4) & 0x0F0F0F0Fu;
+            lo.w = v.w & 0x0F0F0F0Fu; hi.w = (v.w >> 4) & 0x0F0F0F0Fu;
+            const int r0 = 2 * pr, r1 = 2 * pr + 1;
+            *reinterpret_cast<uint4*>(at + r0 * kTileN + ((ch ^ (r0 & 7)) << 4)) = lo;
+            *reinterpret_cast<uint4*>(at + r1 * kTileN + ((ch ^ (r1 & 7)) << 4)) = hi;
+          }
         }
       }
       fence_proxy_async_smem();
-      mbar_arrive(afull + as_);
+      mbar_arrive(afull + as);
       __syncwarp();
-      if (lane == 0) mbar_arrive(empty + slot);
+      if (lane == 0) mbar_arrive(empty + rs);
     }
   }
 
