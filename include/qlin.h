@@ -129,6 +129,16 @@ int qlin_mlp_gate_up_quant_w4(const int8_t* a_q, const float* a_s, int64_t M, in
 int qlin_quant_row(const void* x, int64_t ldx, int64_t M, int64_t K,
                    int8_t* q, float* s, void* stream);
 
+/* Diagnostic (no GPU needed, nothing launched): the launch plan of the
+ * small-M weight-streaming kernel for wbits 8 or 4, `gate_up` 0 (one output
+ * stream: gemm / proj3) or 1 (fused gate/up), M rows, K, `tiles` 128-column
+ * output tiles (sum over proj3 segments), W4 group size and `sms` SMs.
+ * out[0..7] = K split (cluster size), 64-K groups per CTA, groups per batch,
+ * weight-ring slots, unpacked-ring slots, accumulator buffers, dynamic
+ * shared memory bytes, activation rows per row block. */
+int qlin_plan_small_m(int wbits, int gate_up, int64_t M, int64_t K, int64_t tiles, int64_t wgrp,
+                      int sms, int64_t* out);
+
 #ifdef __cplusplus
 }
 #endif

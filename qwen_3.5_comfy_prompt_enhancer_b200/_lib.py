@@ -28,6 +28,7 @@ SIGNATURES = {
     "qlin_mlp_gate_up_quant": [_P, _P, _I, _I, _P, _P, _P, _P, _I, _P, _P, _P],
     "qlin_mlp_gate_up_quant_w4": [_P, _P, _I, _I, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P],
     "qlin_quant_row": [_P, _I, _I, _I, _P, _P, _P],
+    "qlin_plan_small_m": [ctypes.c_int, ctypes.c_int, _I, _I, _I, _I, ctypes.c_int, _P],
 }
 _RESTYPES = {
     "qlin_status_string": ctypes.c_char_p,
@@ -71,3 +72,13 @@ class QlinError(RuntimeError):
 def check(fn, status):
     if status != 0:
         raise QlinError(fn, status)
+
+
+PLAN_FIELDS = ("split", "gmax", "bs", "rb", "ab", "nbb", "smem", "mr")
+
+
+def plan_small_m(wbits, gate_up, M, K, tiles, wgrp=64, sms=148):
+    """Launch plan of the small-M kernel (``qlin_plan_small_m``) as a dict."""
+    out = (ctypes.c_int64 * 8)()
+    check("qlin_plan_small_m", load().qlin_plan_small_m(wbits, int(bool(gate_up)), M, K, tiles, wgrp, sms, out))
+    return dict(zip(PLAN_FIELDS, list(out)))

@@ -120,6 +120,7 @@ int env_int(const char* name, int dflt) {
 int tune_split() { static const int v = env_int("QLIN_TUNE_SPLIT", 0); return v; }
 int tune_pdl() { static const int v = env_int("QLIN_TUNE_PDL", 1); return v; }
 int tune_budget() { static const int v = env_int("QLIN_TUNE_BUDGET_KB", 0); return v; }
+int tune_ctas_per_sm() { static const int v = env_int("QLIN_TUNE_CTAS_PER_SM", 0); return v; }
 
 // Kernel family for the small-M path: tcgen05 weight streaming (default) or
 // the CUDA-core dp4a GEMV (QLIN_SMALLM_KERNEL=dp4a, kept for comparison).
@@ -223,64 +224,79 @@ int tc_mr(int wb, int64_t M) {
   return (wb == 4 && mr > 16) ? 16 : mr;
 }
 
+// Largest K split (thread-block cluster size; 8 is the portable maximum).
+constexpr int kMaxCluster = 8;
+// Dynamic shared memory one CTA may use (B200: 227 KB).
+constexpr size_t kTcMaxSmem = 227 * 1024;
+
 struct TcPlan {
   int split, gmax, bs, rb, ab, nbb;
   size_t smem;
 };
 
-TcPlan plan_tc(int wb, int mr, int ns, int K, int wgrp, int tiles, int rowblocks, int sms) {
-  const int G = K / kGroup;
-  const int nm = mr < 16 ? 16 : mr;
-  TcPlan best{1, G, 1, 1, 0, 1, 0};
-  double best_cost = 1e30;
-  const int smax = G < 8 ? G : 8;
-  for (int s = 1; s <= smax; ++s) {
-    const int gmax = (G + s - 1) / s;
-    if (static_cast<long long>(gmax) * 64 * nm > 48 * 1024) continue;  // activation operand
-    if (tune_split() > 0 && s != tune_split() && tune_split() <= smax) continue;
-    const long long ctas = static_cast<long long>(tiles) * s * rowblocks;
-    const double waves = static_cast<double>((ctas + sms - 1) / sms);
-    const double cost = waves / s * (1.0 + 0.02 * s);
-    if (cost < best_cost - 1e-12) {
-      best_cost = cost;
-      best.split = s;
-      best.gmax = gmax;
-    }
-  }
-  // Batch plan.  ~110 KB per CTA keeps two CTAs resident per SM (this launch
-  // and the next one under PDL); the tensor-memory share is 256 columns.
-  const uint32_t budget = (tune_budget() > 0 ? tune_budget() : 110) * 1024;
-  const TcLayout base = tc_layout(wb, nm, ns, wgrp, best.gmax, 0, 0, 0, 2);
+// Batch plan for one K split: whole K range in one batch when the weight
+// ring (and, for W4, the unpacked tiles) fits the per-CTA budget and the
+// tensor-memory share, otherwise double-buffered batches.
+void plan_batches(int wb, int mr, int ns, int wgrp, TcPlan& pl) {
+  // ~110 KB per CTA keeps two CTAs resident per SM (this launch and the next
+  // one under PDL); the tensor-memory share is 256 columns.
+  const uint32_t budget = (tune_budget() > 0 ? tune_budget() : 112) * 1024;
+  const TcLayout base = tc_layout(wb, mr, ns, wgrp, pl.gmax, 0, 0, 0, 2, pl.split);
   const uint32_t fixed = base.total;
-  const uint32_t per_buf = base.per_buf;
-  const int tmem_groups = static_cast<int>(kTmemBudget / per_buf);
+  const int tmem_groups = static_cast<int>(kTmemBudget / base.per_buf);
   const uint32_t raw_g = base.raw_stage;               // weight ring bytes per group
   const uint32_t a_g = wb == 4 ? ns * 64 * kTileN : 0;  // unpacked A bytes per group
   const uint32_t room = budget > fixed ? budget - fixed : 0;
-  if (best.gmax <= tmem_groups && best.gmax * (raw_g + a_g) <= room) {
-    best.bs = best.gmax;  // whole K range in one batch
-    best.rb = 1;
-    best.ab = wb == 4 ? 1 : 0;
-    best.nbb = 1;
+  if (pl.gmax <= tmem_groups && pl.gmax * (raw_g + a_g) <= room) {
+    pl.bs = pl.gmax;
+    pl.rb = 1;
+    pl.ab = wb == 4 ? 1 : 0;
+    pl.nbb = 1;
   } else {
     const int rb = 2, ab = wb == 4 ? 2 : 0;
     int bs = static_cast<int>(room / (rb * raw_g + ab * a_g));
     if (bs > tmem_groups / 2) bs = tmem_groups / 2;
     if (bs < 1) bs = 1;
-    best.bs = bs;
-    best.rb = rb;
-    best.ab = ab;
-    best.nbb = 2;
+    pl.bs = bs;
+    pl.rb = rb;
+    pl.ab = ab;
+    pl.nbb = 2;
   }
-  const TcLayout L = tc_layout(wb, nm, ns, wgrp, best.gmax, best.bs, best.rb, best.ab, best.nbb);
+  const TcLayout L = tc_layout(wb, mr, ns, wgrp, pl.gmax, pl.bs, pl.rb, pl.ab, pl.nbb, pl.split);
   // At most 512 / tmem_cols CTAs may share an SM, or a tensor-memory
   // allocation could wait on a CTA of the next launch: pad shared memory so
   // that no more CTAs than that fit.
-  const uint32_t max_ctas = 512 / L.tmem_cols;
+  uint32_t max_ctas = 512 / L.tmem_cols;
+  if (tune_ctas_per_sm() > 0 && static_cast<uint32_t>(tune_ctas_per_sm()) < max_ctas) max_ctas = tune_ctas_per_sm();
   uint32_t smem = L.total;
   const uint32_t floor_smem = (228 * 1024) / (max_ctas + 1) - 1024 + 16;
   if (smem < floor_smem) smem = floor_smem;
-  best.smem = smem;
+  pl.smem = smem;
+}
+
+// Choose the K split (cluster size).  Per launch the critical path after
+// the grid dependency is activation load -> MMA -> drain -> cluster combine,
+// and the combine grows with the split; the weight stream itself overlaps the
+// preceding kernel.  Measured on B200 (config-2 layer shapes, K = 2048..6144)
+// the best split is the largest one (up to 8) that keeps the launch at about
+// 1.3 CTAs per SM: more CTAs leave clusters waiting for the previous
+// launch's CTAs to retire, fewer leave HBM under-subscribed.
+TcPlan plan_tc(int wb, int mr, int ns, int K, int wgrp, int tiles, int rowblocks, int sms) {
+  const int G = K / kGroup;
+  const long long target = (static_cast<long long>(sms) * 4 + 2) / 3;  // ~1.33 CTAs per SM
+  TcPlan best{0, 0, 0, 0, 0, 0, 0};  // split 0: no plan fits
+  const int smax = G < kMaxCluster ? G : kMaxCluster;
+  for (int s = 1; s <= smax; ++s) {
+    TcPlan pl{s, (G + s - 1) / s, 1, 1, 0, 1, 0};
+    if (tune_split() > 0 && s != tune_split() && tune_split() <= smax) continue;
+    plan_batches(wb, mr, ns, wgrp, pl);
+    if (pl.smem > kTcMaxSmem) continue;
+    const long long ctas = static_cast<long long>(tiles) * s * rowblocks;
+    // The smallest feasible split always qualifies; larger ones while the
+    // launch stays within the CTA target.
+    if (best.split == 0 || ctas <= target || tune_split() == s) best = pl;
+    if (ctas > target && tune_split() <= 0) break;
+  }
   return best;
 }
 
@@ -329,16 +345,38 @@ int launch_tc_mr(int mr, const GemvArgs& a, dim3 grid, size_t smem, cudaStream_t
   }
 }
 
+// Row block and K split for the tcgen05 path.  Row blocks of 32 rows hold
+// the largest activation and partial-sum buffers; when no split of K fits
+// shared memory, 16-row blocks are used.  Returns QLIN_OK or an error.
+int choose_tc(int wb, int ns, int64_t M, int K, int wgrp, int tiles, int sms, int* mr_out, int* rowblocks_out,
+              TcPlan* pl_out) {
+  int mr = tc_mr(wb, M);
+  for (;;) {
+    const int nm = mr < 16 ? 16 : mr;
+    const int64_t rowblocks = (M + nm - 1) / nm;
+    if (rowblocks > 65535 || tiles > 65535) return fail(QLIN_ERR_SHAPE, "grid too large (M=%lld)", (long long)M);
+    const TcPlan pl = plan_tc(wb, mr, ns, K, wgrp, tiles, static_cast<int>(rowblocks), sms);
+    if (pl.split > 0) {
+      *mr_out = mr;
+      *rowblocks_out = static_cast<int>(rowblocks);
+      *pl_out = pl;
+      return QLIN_OK;
+    }
+    if (mr <= 16) break;
+    mr = 16;
+  }
+  return fail(QLIN_ERR_SHAPE, "K=%d exceeds the shared-memory capacity of the small-M kernel", K);
+}
+
 int run_tc(int wb, int epi, GemvArgs& a, int tiles, cudaStream_t st) {
   DevInfo di;
   if (int r = device_info(&di)) return r;
-  const int mr = tc_mr(wb, a.M);
-  const int nm = mr < 16 ? 16 : mr;
-  const int rowblocks = (a.M + nm - 1) / nm;
-  if (rowblocks > 65535 || tiles > 65535) return fail(QLIN_ERR_SHAPE, "grid too large (M=%d)", a.M);
   const int ns = epi == kEpiOut ? 1 : 2;
+  int mr = 0, rowblocks = 0;
+  TcPlan pl{};
+  if (int r = choose_tc(wb, ns, a.M, a.K, a.wgrp, tiles, di.sms, &mr, &rowblocks, &pl)) return r;
+  const int nm = mr < 16 ? 16 : mr;
   if (int r = make_map(&a.ta, a.a_q, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.K, a.M, a.K, 128, nm, true)) return r;
-  const TcPlan pl = plan_tc(wb, mr, ns, a.K, a.wgrp, tiles, rowblocks, di.sms);
   a.split = pl.split;
   a.gmax = pl.gmax;
   a.bs = pl.bs;
@@ -467,6 +505,23 @@ const char* qlin_status_string(int s) {
 }
 
 const char* qlin_last_error(void) { return g_err; }
+
+int qlin_plan_small_m(int wbits, int gate_up, int64_t M, int64_t K, int64_t tiles, int64_t wgrp, int sms,
+                      int64_t* out) {
+  if ((wbits != 8 && wbits != 4) || !out || M <= 0 || tiles <= 0 || sms <= 0)
+    return fail(QLIN_ERR_INVALID_ARGUMENT, "bad plan query");
+  if (K <= 0 || K % kGroup != 0 || K > (1ll << 30)) return fail(QLIN_ERR_SHAPE, "K=%lld", (long long)K);
+  if (wbits == 4)
+    if (int r = check_wgrp(K, wgrp)) return r;
+  int mr = 0, rowblocks = 0;
+  TcPlan pl{};
+  if (int r = choose_tc(wbits, gate_up ? 2 : 1, M, static_cast<int>(K), wbits == 4 ? static_cast<int>(wgrp) : 64,
+                        static_cast<int>(tiles > 65536 ? 65536 : tiles), sms, &mr, &rowblocks, &pl))
+    return r;
+  const int64_t v[8] = {pl.split, pl.gmax, pl.bs, pl.rb, pl.ab, pl.nbb, static_cast<int64_t>(pl.smem), mr};
+  for (int i = 0; i < 8; ++i) out[i] = v[i];
+  return QLIN_OK;
+}
 
 int qlin_device_fault(int clear) {
   DevInfo di;

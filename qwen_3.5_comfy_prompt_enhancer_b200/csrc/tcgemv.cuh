@@ -40,9 +40,10 @@
 //               activations; the zero point is removed exactly in integers
 //               by the drain: sum(a*(nib - z)) = sum(a*nib) - z*sum(a).
 //
-// Split-K across the CTAs of a thread-block cluster, combined through
-// distributed shared memory in a fixed order (no global scratch), as in
-// gemv.cuh.  PDL: weights stream before griddepcontrol.wait.
+// Split-K across the CTAs of a thread-block cluster: ranks 1..split-1 push
+// their fp32 partial sums into rank 0's shared memory (distributed shared
+// memory, no global scratch) and exit; rank 0 adds them in rank order and
+// runs the epilogue.  PDL: weights stream before griddepcontrol.wait.
 #pragma once
 
 #include <cooperative_groups.h>
@@ -78,8 +79,9 @@ __host__ __device__ inline uint32_t pow2_at_least(uint32_t x) {
 // Shared-memory carve-up relative to a 1024-byte aligned base; `total`
 // includes 1 KB of alignment slack.  bs groups per batch, rb weight-ring
 // slots, ab unpacked-ring slots (W4), nbb accumulator batches.
-__host__ __device__ inline TcLayout tc_layout(int wb, int nm, int ns, int wgrp, int gmax, int bs, int rb, int ab,
-                                              int nbb) {
+__host__ __device__ inline TcLayout tc_layout(int wb, int mr, int ns, int wgrp, int gmax, int bs, int rb, int ab,
+                                              int nbb, int split) {
+  const int nm = mr < 16 ? 16 : mr;
   TcLayout L;
   L.nsub = (wb == 4 && wgrp == 32) ? 2 : 1;
   L.raw_stream = wb == 8 ? 64 * kTileN : 32 * kTileN + L.nsub * kTileN * 2 + L.nsub * kTileN;
@@ -97,12 +99,13 @@ __host__ __device__ inline TcLayout tc_layout(int wb, int nm, int ns, int wgrp, 
   off = align_up(off + gmax * nm * 4, 16);
   L.asum_off = off;
   off = align_up(off + (wb == 4 ? gmax * 2 * nm * 4 : 0), 16);
+  // Partial sums pushed by the cluster's ranks 1..split-1 into rank 0.
   L.part_off = off;
-  off = align_up(off + ns * nm * kTileN * 4, 16);
+  off = align_up(off + (split > 1 ? split - 1 : 0) * ns * mr * kTileN * 4, 16);
   L.xchg_off = off;
-  off = align_up(off + 4 * nm * 4, 16);
+  off = align_up(off + 4 * mr * 4, 16);
   L.bar_off = off;
-  off = align_up(off + 8 * (2 * rb + 2 * ab + 2 * nbb + 1), 16);
+  off = align_up(off + 8 * (2 * rb + 2 * ab + 2 * nbb + 2), 16);
   L.tmem_slot_off = off;
   off += 16;
   L.total = off + 1024;
@@ -123,7 +126,7 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
   const int BS = p.bs, RB = p.rb, NBB = p.nbb;
   const int AB = WB == 4 ? p.ab : 0;
   const int ab_div = AB > 0 ? AB : 1;  // W8 has no unpacked ring
-  const TcLayout L = tc_layout(WB, NM, NS, p.wgrp, p.gmax, BS, RB, AB, NBB);
+  const TcLayout L = tc_layout(WB, MR, NS, p.wgrp, p.gmax, BS, RB, AB, NBB, p.split);
   const int NSUB = static_cast<int>(L.nsub);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
   uint64_t* empty = full + RB;
@@ -132,6 +135,7 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
   uint64_t* tfull = aempty + AB;
   uint64_t* tempty = tfull + NBB;
   uint64_t* bfull = tempty + NBB;
+  uint64_t* recv = bfull + 1;  // rank 0: partial sums of the other ranks landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.tmem_slot_off);
 
   const int warp = threadIdx.x >> 5;
@@ -225,6 +229,7 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
         mbar_init(tempty + i, kDrainThreads);
       }
       mbar_init(bfull, 1);
+      mbar_init(recv, kDrainThreads * (p.split > 1 ? p.split - 1 : 1));
       fence_mbar_init();
     }
     __syncwarp();
@@ -240,7 +245,16 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // Pairs with the cluster wait before the partial sums are pushed: rank 0's
+  // receive barrier is initialised before any other rank arrives on it.
+  if (p.split > 1) cluster_arrive_relaxed();
   const uint32_t tbase = *tmem_slot;
+
+  float acc[NS][MR];  // drain threads: this CTA's partial sums for output column c
+#pragma unroll
+  for (int s = 0; s < NS; ++s)
+#pragma unroll
+    for (int m = 0; m < MR; ++m) acc[s][m] = 0.0f;
 
   // TMEM accumulator column of (batch buffer, group-in-batch, stream, sub-block).
   auto tcol = [&](int tb, int j, int s, int sub) -> uint32_t {
@@ -341,12 +355,6 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
     named_bar_sync(1, kDrainThreads);  // ass / asum visible to all drain threads
     pdl_launch_dependents();
 
-    float acc[NS][MR];
-#pragma unroll
-    for (int s = 0; s < NS; ++s)
-#pragma unroll
-      for (int m = 0; m < MR; ++m) acc[s][m] = 0.0f;
-
     const uint32_t lane_base = tbase + (static_cast<uint32_t>(32 * q) << 16);
     for (int b = 0; ok && b < nbatch; ++b) {
       const int rs = b % RB;
@@ -404,10 +412,6 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
       }
     }
     if (!ok && lane == 0) atomicOr(p.fault, kFaultFullWait);
-#pragma unroll
-    for (int s = 0; s < NS; ++s)
-#pragma unroll
-      for (int m = 0; m < MR; ++m) part[(s * NM + m) * kTileN + c] = acc[s][m];
   } else if constexpr (WB == 4) {
     // ------------------------------------------------------------------ W4 unpack
     const int u = threadIdx.x - kTcWarpUnpack * 32;
@@ -449,25 +453,42 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
 
   // ------------------------------------------------------------------ cluster combine + epilogue
   __syncwarp();
-  cg::cluster_group cluster = cg::this_cluster();
   tc_fence_before();
-  cluster.sync();
+  __syncthreads();  // every tensor-memory read has completed
   tc_fence_after();
   if (warp == kTcWarpMma) tmem_dealloc(tbase, L.tmem_cols);
+  if (p.split > 1) cluster_wait();
+  // Ranks 1..split-1 push their partial sums into rank 0's shared memory and
+  // arrive on its receive barrier (release at cluster scope), then exit:
+  // nothing reads their shared memory, so no closing cluster barrier.
+  if (is_drain && rank > 0) {
+    const uint32_t slot0 = smem_u32(part + static_cast<size_t>(rank - 1) * NS * MR * kTileN);
+    const uint32_t dst = map_to_rank(slot0, 0);
+#pragma unroll
+    for (int s = 0; s < NS; ++s)
+#pragma unroll
+      for (int m = 0; m < MR; ++m) st_cluster_f32(dst + ((s * MR + m) * kTileN + c) * 4, acc[s][m]);
+    mbar_arrive_remote(map_to_rank(smem_u32(recv), 0));
+  }
   if (epi_thread) {
     const int n = en;
     const bool valid = n < S0.n;
+    // Fixed summation order: rank 0, then ranks 1, 2, ...
     float vs[NS][MR];
 #pragma unroll
     for (int s = 0; s < NS; ++s)
 #pragma unroll
-      for (int m = 0; m < MR; ++m) vs[s][m] = 0.0f;
-    for (int r = 0; r < p.split; ++r) {
-      const float* rp = cluster.map_shared_rank(part, r);
+      for (int m = 0; m < MR; ++m) vs[s][m] = acc[s][m];
+    if (p.split > 1 && !mbar_wait_cluster(recv, 0)) {
+      if (lane == 0) atomicOr(p.fault, kFaultFullWait);
+    } else {
+      for (int r = 1; r < p.split; ++r) {
+        const float* rp = part + static_cast<size_t>(r - 1) * NS * MR * kTileN;
 #pragma unroll
-      for (int s = 0; s < NS; ++s)
+        for (int s = 0; s < NS; ++s)
 #pragma unroll
-        for (int m = 0; m < MR; ++m) vs[s][m] = __fadd_rn(vs[s][m], rp[(s * NM + m) * kTileN + c]);
+          for (int m = 0; m < MR; ++m) vs[s][m] = __fadd_rn(vs[s][m], rp[(s * MR + m) * kTileN + c]);
+      }
     }
     if (EPI == kEpiOut) {
       __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
@@ -513,7 +534,6 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
       }
     }
   }
-  cluster.sync();
 }
 
 }  // namespace qlin
