@@ -133,9 +133,11 @@ int qlin_quant_row(const void* x, int64_t ldx, int64_t M, int64_t K,
  * small-M weight-streaming kernel for wbits 8 or 4, `gate_up` 0 (one output
  * stream: gemm / proj3) or 1 (fused gate/up), M rows, K, `tiles` 128-column
  * output tiles (sum over proj3 segments), W4 group size and `sms` SMs.
- * out[0..7] = K split (cluster size), 64-K groups per CTA, groups per batch,
+ * out[0..9] = K split (cluster size), 64-K groups per CTA, groups per batch,
  * weight-ring slots, unpacked-ring slots, accumulator buffers, dynamic
- * shared memory bytes, activation rows per row block. */
+ * shared memory bytes, activation rows per row block, 1 if the split-K
+ * partial sums reuse rank 0's operand region, plan level (2: one batch,
+ * 1: W4 packed weights resident with an unpacked ring, 0: streamed). */
 int qlin_plan_small_m(int wbits, int gate_up, int64_t M, int64_t K, int64_t tiles, int64_t wgrp,
                       int sms, int64_t* out);
 

@@ -74,11 +74,11 @@ def check(fn, status):
         raise QlinError(fn, status)
 
 
-PLAN_FIELDS = ("split", "gmax", "bs", "rb", "ab", "nbb", "smem", "mr")
+PLAN_FIELDS = ("split", "gmax", "bs", "rb", "ab", "nbb", "smem", "mr", "alias", "level")
 
 
 def plan_small_m(wbits, gate_up, M, K, tiles, wgrp=64, sms=148):
     """Launch plan of the small-M kernel (``qlin_plan_small_m``) as a dict."""
-    out = (ctypes.c_int64 * 8)()
+    out = (ctypes.c_int64 * len(PLAN_FIELDS))()
     check("qlin_plan_small_m", load().qlin_plan_small_m(wbits, int(bool(gate_up)), M, K, tiles, wgrp, sms, out))
     return dict(zip(PLAN_FIELDS, list(out)))

@@ -121,6 +121,8 @@ int tune_split() { static const int v = env_int("QLIN_TUNE_SPLIT", 0); return v;
 int tune_pdl() { static const int v = env_int("QLIN_TUNE_PDL", 1); return v; }
 int tune_budget() { static const int v = env_int("QLIN_TUNE_BUDGET_KB", 0); return v; }
 int tune_ctas_per_sm() { static const int v = env_int("QLIN_TUNE_CTAS_PER_SM", 0); return v; }
+int tune_max_level() { static const int v = env_int("QLIN_TUNE_MAX_LEVEL", 2); return v; }
+int tune_max_cluster() { static const int v = env_int("QLIN_TUNE_MAX_CLUSTER", 8); return v; }
 
 // Kernel family for the small-M path: tcgen05 weight streaming (default) or
 // the CUDA-core dp4a GEMV (QLIN_SMALLM_KERNEL=dp4a, kept for comparison).
@@ -224,45 +226,72 @@ int tc_mr(int wb, int64_t M) {
   return (wb == 4 && mr > 16) ? 16 : mr;
 }
 
-// Largest K split (thread-block cluster size; 8 is the portable maximum).
+// Largest K split (thread-block cluster size, the portable maximum).
 constexpr int kMaxCluster = 8;
 // Dynamic shared memory one CTA may use (B200: 227 KB).
 constexpr size_t kTcMaxSmem = 227 * 1024;
 
 struct TcPlan {
-  int split, gmax, bs, rb, ab, nbb;
+  int split, gmax, bs, rb, ab, nbb, alias;
+  // 2: one batch (weights in flight and operands complete before the grid
+  // dependency); 1: W4 packed weights all resident, unpacked in a ring;
+  // 0: weights stream through double-buffered batches.
+  int level;
   size_t smem;
 };
 
-// Batch plan for one K split: whole K range in one batch when the weight
-// ring (and, for W4, the unpacked tiles) fits the per-CTA budget and the
-// tensor-memory share, otherwise double-buffered batches.
+// Batch plan for one K split, first that fits the per-CTA budget of
+// ~112 KB (two CTAs per SM) and the 256-column tensor-memory share:
+//  1. one batch: the whole K range in flight, one hand-off per role;
+//  2. fused W4 gate/up only: every packed weight group resident (all
+//     requested up front), a ring of unpacked tiles and per-group
+//     hand-offs;
+//  3. double-buffered batches (the weights stream behind the MMAs).
+// Plans 1 and 2 are tried without, then with, the partial-sum buffer
+// aliased onto rank 0's finished operand region.  Measured on B200 (config-2
+// shapes): plan 2 beats plan 3 for the two-stream gate/up (11.9 vs 13.7 us)
+// but not for single-stream W4 (11.4 vs 8.4 us for the K = 6144 down
+// projection), whose per-group hand-offs after the grid dependency cost more
+// than the streamed batches.
 void plan_batches(int wb, int mr, int ns, int wgrp, TcPlan& pl) {
-  // ~110 KB per CTA keeps two CTAs resident per SM (this launch and the next
-  // one under PDL); the tensor-memory share is 256 columns.
   const uint32_t budget = (tune_budget() > 0 ? tune_budget() : 112) * 1024;
-  const TcLayout base = tc_layout(wb, mr, ns, wgrp, pl.gmax, 0, 0, 0, 2, pl.split);
-  const uint32_t fixed = base.total;
+  const int s = pl.split, gmax = pl.gmax;
+  const TcLayout base = tc_layout(wb, mr, ns, wgrp, gmax, 1, 1, 1, 1, s, 0);
   const int tmem_groups = static_cast<int>(kTmemBudget / base.per_buf);
-  const uint32_t raw_g = base.raw_stage;               // weight ring bytes per group
-  const uint32_t a_g = wb == 4 ? ns * 64 * kTileN : 0;  // unpacked A bytes per group
-  const uint32_t room = budget > fixed ? budget - fixed : 0;
-  if (pl.gmax <= tmem_groups && pl.gmax * (raw_g + a_g) <= room) {
-    pl.bs = pl.gmax;
-    pl.rb = 1;
-    pl.ab = wb == 4 ? 1 : 0;
-    pl.nbb = 1;
-  } else {
+  auto fits = [&](int bs, int rb, int ab, int nbb, int alias) {
+    const TcLayout L = tc_layout(wb, mr, ns, wgrp, gmax, bs, rb, ab, nbb, s, alias);
+    if (alias && (s < 2 || L.part_bytes > L.op_bytes)) return false;
+    if (L.total > budget) return false;
+    pl.bs = bs;
+    pl.rb = rb;
+    pl.ab = ab;
+    pl.nbb = nbb;
+    pl.alias = alias;
+    return true;
+  };
+  bool ok = false;
+  pl.level = 0;
+  for (int alias = 0; alias < 2 && !ok && tune_max_level() >= 2; ++alias)
+    if (gmax <= tmem_groups && fits(gmax, 1, wb == 4 ? 1 : 0, 1, alias)) ok = true, pl.level = 2;
+  for (int alias = 0; alias < 2 && !ok && wb == 4 && ns == 2 && tune_max_level() >= 1; ++alias)
+    // deepest unpacked ring (up to 4 groups) that fits
+    for (int ab = (gmax < 4 ? gmax : 4); !ok && ab >= 2; --ab)
+      if (fits(1, gmax, ab, gmax < tmem_groups ? gmax : tmem_groups, alias)) ok = true, pl.level = 1;
+  if (!ok) {
     const int rb = 2, ab = wb == 4 ? 2 : 0;
-    int bs = static_cast<int>(room / (rb * raw_g + ab * a_g));
+    const TcLayout one = tc_layout(wb, mr, ns, wgrp, gmax, 1, rb, ab, 2, s, 0);
+    const uint32_t per_group = rb * base.raw_stage + (wb == 4 ? ab * ns * 64 * kTileN : 0);
+    const uint32_t room = budget > one.total - per_group ? budget - (one.total - per_group) : 0;
+    int bs = static_cast<int>(room / per_group);
     if (bs > tmem_groups / 2) bs = tmem_groups / 2;
     if (bs < 1) bs = 1;
     pl.bs = bs;
     pl.rb = rb;
     pl.ab = ab;
     pl.nbb = 2;
+    pl.alias = 0;
   }
-  const TcLayout L = tc_layout(wb, mr, ns, wgrp, pl.gmax, pl.bs, pl.rb, pl.ab, pl.nbb, pl.split);
+  const TcLayout L = tc_layout(wb, mr, ns, wgrp, gmax, pl.bs, pl.rb, pl.ab, pl.nbb, s, pl.alias);
   // At most 512 / tmem_cols CTAs may share an SM, or a tensor-memory
   // allocation could wait on a CTA of the next launch: pad shared memory so
   // that no more CTAs than that fit.
@@ -284,20 +313,31 @@ void plan_batches(int wb, int mr, int ns, int wgrp, TcPlan& pl) {
 TcPlan plan_tc(int wb, int mr, int ns, int K, int wgrp, int tiles, int rowblocks, int sms) {
   const int G = K / kGroup;
   const long long target = (static_cast<long long>(sms) * 4 + 2) / 3;  // ~1.33 CTAs per SM
-  TcPlan best{0, 0, 0, 0, 0, 0, 0};  // split 0: no plan fits
-  const int smax = G < kMaxCluster ? G : kMaxCluster;
+  const long long two_per_sm = 2ll * sms;
+  // Per plan level: the largest split within the CTA target, and the
+  // smallest split beyond it (within two CTAs per SM).
+  TcPlan in[3] = {}, up[3] = {}, any{};
+  const int cmax = tune_max_cluster() < kMaxCluster ? tune_max_cluster() : kMaxCluster;
+  const int smax = G < cmax ? G : cmax;
   for (int s = 1; s <= smax; ++s) {
-    TcPlan pl{s, (G + s - 1) / s, 1, 1, 0, 1, 0};
+    TcPlan pl{s, (G + s - 1) / s, 1, 1, 0, 1, 0, 0, 0};
     if (tune_split() > 0 && s != tune_split() && tune_split() <= smax) continue;
     plan_batches(wb, mr, ns, wgrp, pl);
     if (pl.smem > kTcMaxSmem) continue;
+    if (tune_split() == s) return pl;
     const long long ctas = static_cast<long long>(tiles) * s * rowblocks;
-    // The smallest feasible split always qualifies; larger ones while the
-    // launch stays within the CTA target.
-    if (best.split == 0 || ctas <= target || tune_split() == s) best = pl;
-    if (ctas > target && tune_split() <= 0) break;
+    if (any.split == 0) any = pl;  // smallest feasible split, whatever its size
+    const bool within = ctas <= target;
+    if (within || (s == 1 && in[pl.level].split == 0)) in[pl.level] = pl;
+    else if (ctas <= two_per_sm && up[pl.level].split == 0) up[pl.level] = pl;
   }
-  return best;
+  // Highest level first (more of the work ahead of the grid dependency);
+  // extra splits add combine work, so beyond the target the smallest one.
+  for (int lv = 2; lv >= 0; --lv) {
+    if (in[lv].split) return in[lv];
+    if (up[lv].split) return up[lv];
+  }
+  return any;
 }
 
 template <int WB, int MR, int EPI>
@@ -383,6 +423,7 @@ int run_tc(int wb, int epi, GemvArgs& a, int tiles, cudaStream_t st) {
   a.rb = pl.rb;
   a.ab = pl.ab;
   a.nbb = pl.nbb;
+  a.part_alias = pl.alias;
   a.fault = di.fault;
   const dim3 grid(pl.split, tiles, rowblocks);
   if (wb == 8) {
@@ -518,8 +559,9 @@ int qlin_plan_small_m(int wbits, int gate_up, int64_t M, int64_t K, int64_t tile
   if (int r = choose_tc(wbits, gate_up ? 2 : 1, M, static_cast<int>(K), wbits == 4 ? static_cast<int>(wgrp) : 64,
                         static_cast<int>(tiles > 65536 ? 65536 : tiles), sms, &mr, &rowblocks, &pl))
     return r;
-  const int64_t v[8] = {pl.split, pl.gmax, pl.bs, pl.rb, pl.ab, pl.nbb, static_cast<int64_t>(pl.smem), mr};
-  for (int i = 0; i < 8; ++i) out[i] = v[i];
+  const int64_t v[10] = {pl.split, pl.gmax, pl.bs, pl.rb, pl.ab, pl.nbb, static_cast<int64_t>(pl.smem), mr,
+                         pl.alias, pl.level};
+  for (int i = 0; i < 10; ++i) out[i] = v[i];
   return QLIN_OK;
 }
 

@@ -76,6 +76,7 @@ struct GemvArgs {
   int ab;             // tc_gemv W4: batch slots in the unpacked-weight ring
   int nbb;            // tc_gemv: batch accumulators in tensor memory
   int gmax;           // max groups one CTA handles
+  int part_alias;     // tc_gemv: partial sums land in rank 0's (finished) MMA operand region
   void* out;          // bf16, row stride ldo
   long long ldo;
   const void* res;    // bf16 residual or null, row stride ldr

@@ -66,8 +66,8 @@ constexpr uint32_t kTmemBudget = 256;
 __host__ __device__ constexpr int tc_threads(int wb) { return (wb == 8 ? 6 : 10) * 32; }
 
 struct TcLayout {
-  uint32_t nsub, raw_stream, raw_stage, raw_off, a_off, b_off, nbox, as_off, asum_off, part_off, xchg_off,
-      bar_off, tmem_slot_off, total, tmem_cols, per_buf;
+  uint32_t nsub, raw_stream, raw_stage, raw_off, a_off, b_off, nbox, as_off, asum_off, part_off, part_bytes,
+      op_bytes, xchg_off, bar_off, tmem_slot_off, total, tmem_cols, per_buf;
 };
 
 __host__ __device__ inline uint32_t pow2_at_least(uint32_t x) {
@@ -78,9 +78,12 @@ __host__ __device__ inline uint32_t pow2_at_least(uint32_t x) {
 
 // Shared-memory carve-up relative to a 1024-byte aligned base; `total`
 // includes 1 KB of alignment slack.  bs groups per batch, rb weight-ring
-// slots, ab unpacked-ring slots (W4), nbb accumulator batches.
+// slots, ab unpacked-ring slots (W4), nbb accumulator batches.  With
+// `alias`, the partial sums of ranks 1..split-1 are received in rank 0's MMA
+// operand region (unpacked ring for W4, weight ring for W8) once rank 0's
+// MMAs have completed, instead of a region of their own.
 __host__ __device__ inline TcLayout tc_layout(int wb, int mr, int ns, int wgrp, int gmax, int bs, int rb, int ab,
-                                              int nbb, int split) {
+                                              int nbb, int split, int alias) {
   const int nm = mr < 16 ? 16 : mr;
   TcLayout L;
   L.nsub = (wb == 4 && wgrp == 32) ? 2 : 1;
@@ -100,12 +103,18 @@ __host__ __device__ inline TcLayout tc_layout(int wb, int mr, int ns, int wgrp, 
   L.asum_off = off;
   off = align_up(off + (wb == 4 ? gmax * 2 * nm * 4 : 0), 16);
   // Partial sums pushed by the cluster's ranks 1..split-1 into rank 0.
-  L.part_off = off;
-  off = align_up(off + (split > 1 ? split - 1 : 0) * ns * mr * kTileN * 4, 16);
+  L.part_bytes = (split > 1 ? split - 1 : 0) * ns * mr * kTileN * 4;
+  L.op_bytes = wb == 4 ? ab * bs * ns * 64 * kTileN : rb * bs * L.raw_stage;
+  if (alias) {
+    L.part_off = wb == 4 ? L.a_off : L.raw_off;
+  } else {
+    L.part_off = off;
+    off = align_up(off + L.part_bytes, 16);
+  }
   L.xchg_off = off;
   off = align_up(off + 4 * mr * 4, 16);
   L.bar_off = off;
-  off = align_up(off + 8 * (2 * rb + 2 * ab + 2 * nbb + 2), 16);
+  off = align_up(off + 8 * (2 * rb + 2 * ab + 2 * nbb + 3), 16);
   L.tmem_slot_off = off;
   off += 16;
   L.total = off + 1024;
@@ -126,7 +135,7 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
   const int BS = p.bs, RB = p.rb, NBB = p.nbb;
   const int AB = WB == 4 ? p.ab : 0;
   const int ab_div = AB > 0 ? AB : 1;  // W8 has no unpacked ring
-  const TcLayout L = tc_layout(WB, MR, NS, p.wgrp, p.gmax, BS, RB, AB, NBB, p.split);
+  const TcLayout L = tc_layout(WB, MR, NS, p.wgrp, p.gmax, BS, RB, AB, NBB, p.split, p.part_alias);
   const int NSUB = static_cast<int>(L.nsub);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
   uint64_t* empty = full + RB;
@@ -135,7 +144,8 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
   uint64_t* tfull = aempty + AB;
   uint64_t* tempty = tfull + NBB;
   uint64_t* bfull = tempty + NBB;
-  uint64_t* recv = bfull + 1;  // rank 0: partial sums of the other ranks landed
+  uint64_t* recv = bfull + 1;   // rank 0: partial sums of the other ranks landed
+  uint64_t* ready = recv + 1;   // ranks > 0: rank 0's operand region is free (part_alias)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.tmem_slot_off);
 
   const int warp = threadIdx.x >> 5;
@@ -230,6 +240,7 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
       }
       mbar_init(bfull, 1);
       mbar_init(recv, kDrainThreads * (p.split > 1 ? p.split - 1 : 1));
+      mbar_init(ready, 1);
       fence_mbar_init();
     }
     __syncwarp();
@@ -412,6 +423,15 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
       }
     }
     if (!ok && lane == 0) atomicOr(p.fault, kFaultFullWait);
+    if (p.part_alias && rank == 0) {
+      // The last accumulator batch was observed: every MMA of this CTA has
+      // completed, so its operand region is free to receive the other
+      // ranks' partial sums.  The cluster wait orders this after their
+      // barrier initialisation.
+      cluster_wait();
+      if (ok && td == 0)
+        for (int r = 1; r < p.split; ++r) mbar_arrive_remote(map_to_rank(smem_u32(ready), r));
+    }
   } else if constexpr (WB == 4) {
     // ------------------------------------------------------------------ W4 unpack
     const int u = threadIdx.x - kTcWarpUnpack * 32;
@@ -457,18 +477,26 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
   __syncthreads();  // every tensor-memory read has completed
   tc_fence_after();
   if (warp == kTcWarpMma) tmem_dealloc(tbase, L.tmem_cols);
-  if (p.split > 1) cluster_wait();
+  // (rank 0's drain warps already passed the cluster wait when part_alias)
+  if (p.split > 1 && !(p.part_alias && rank == 0 && is_drain)) cluster_wait();
   // Ranks 1..split-1 push their partial sums into rank 0's shared memory and
   // arrive on its receive barrier (release at cluster scope), then exit:
   // nothing reads their shared memory, so no closing cluster barrier.
   if (is_drain && rank > 0) {
-    const uint32_t slot0 = smem_u32(part + static_cast<size_t>(rank - 1) * NS * MR * kTileN);
-    const uint32_t dst = map_to_rank(slot0, 0);
+    bool go = true;
+    if (p.part_alias && !mbar_wait_cluster(ready, 0)) {
+      go = false;
+      if (lane == 0) atomicOr(p.fault, kFaultFullWait);
+    }
+    if (go) {
+      const uint32_t slot0 = smem_u32(part + static_cast<size_t>(rank - 1) * NS * MR * kTileN);
+      const uint32_t dst = map_to_rank(slot0, 0);
 #pragma unroll
-    for (int s = 0; s < NS; ++s)
+      for (int s = 0; s < NS; ++s)
 #pragma unroll
-      for (int m = 0; m < MR; ++m) st_cluster_f32(dst + ((s * MR + m) * kTileN + c) * 4, acc[s][m]);
-    mbar_arrive_remote(map_to_rank(smem_u32(recv), 0));
+        for (int m = 0; m < MR; ++m) st_cluster_f32(dst + ((s * MR + m) * kTileN + c) * 4, acc[s][m]);
+      mbar_arrive_remote(map_to_rank(smem_u32(recv), 0));
+    }
   }
   if (epi_thread) {
     const int n = en;

@@ -30,27 +30,40 @@ def check_plan(pl, wbits, gate_up, M, K, wgrp):
     nm = max(pl["mr"], 16)
     ns = 2 if gate_up else 1
     nsub = 2 if (wbits == 4 and wgrp == 32) else 1
-    assert pl["nbb"] * pl["bs"] * ns * nsub * nm <= TMEM_SHARE
-    single = pl["bs"] == pl["gmax"]
+    per_buf = ns * nsub * nm
+    assert pl["nbb"] * pl["bs"] * per_buf <= TMEM_SHARE
+    single = pl["bs"] == pl["gmax"] and pl["rb"] == 1
+    resident = wbits == 4 and gate_up and pl["bs"] == 1 and pl["rb"] == pl["gmax"] > 1
     if single:
-        assert (pl["rb"], pl["nbb"]) == (1, 1)
+        assert pl["nbb"] == 1 and pl["ab"] == (1 if wbits == 4 else 0)
+    elif resident:
+        assert 2 <= pl["ab"] <= min(pl["gmax"], 4) or pl["ab"] == pl["gmax"] == 1
+        assert pl["nbb"] == min(pl["gmax"], TMEM_SHARE // per_buf)
     else:
-        assert pl["rb"] == 2 and pl["nbb"] == 2
-    assert pl["ab"] == (0 if wbits == 8 else pl["rb"])
+        assert pl["rb"] == 2 and pl["nbb"] == 2 and pl["ab"] == (2 if wbits == 4 else 0)
+    assert pl["level"] == (2 if single else 1 if resident else 0)
+    if pl["alias"]:
+        # the partial sums of ranks 1..split-1 fit rank 0's operand region
+        assert pl["split"] >= 2 and pl["level"] >= 1
+        part = (pl["split"] - 1) * ns * pl["mr"] * 128 * 4
+        op = (pl["ab"] * pl["bs"] * ns * 64 * 128 if wbits == 4
+              else pl["rb"] * pl["bs"] * ns * 64 * 128)
+        assert part <= op
 
 
-@pytest.mark.parametrize("wbits,gate_up,M,K,N,wgrp,split", [
-    (8, 0, 1, 2048, 6144, 64, 4),      # config 1: W8 projection at decode
-    (4, 1, 4, 2048, 6144, 128, 4),     # config 2: fused gate/up, 4 rows
-    (4, 0, 4, 6144, 2048, 128, 8),     # config 2: down projection (K = 6144)
-    (4, 0, 1, 2048, 2048, 128, 8),     # config 2: o projection
-    (4, 0, 4, 2048, 4096, 128, 6),     # config 2: qkv + gate projection
+@pytest.mark.parametrize("wbits,gate_up,M,K,N,wgrp,split,level", [
+    (8, 0, 1, 2048, 6144, 64, 4, 2),      # config 1: W8 projection at decode, one batch
+    (4, 1, 4, 2048, 6144, 128, 5, 1),     # config 2: fused gate/up, packed weights resident
+    (4, 1, 1, 2048, 6144, 128, 5, 1),
+    (4, 0, 4, 6144, 2048, 128, 8, 0),     # config 2: down projection (K = 6144), streamed
+    (4, 0, 1, 2048, 2048, 128, 8, 2),     # config 2: o projection
+    (4, 0, 4, 2048, 4096, 128, 6, 2),     # config 2: qkv + gate projection
 ])
-def test_config_plans(pkg, wbits, gate_up, M, K, N, wgrp, split):
+def test_config_plans(pkg, wbits, gate_up, M, K, N, wgrp, split, level):
     pl = pkg._lib.plan_small_m(wbits, gate_up, M, K, tiles_of(N), wgrp, SMS)
     check_plan(pl, wbits, gate_up, M, K, wgrp)
-    assert pl["split"] == split
-    assert tiles_of(N) * pl["split"] <= (SMS * 4 + 2) // 3 or pl["split"] == 1
+    assert (pl["split"], pl["level"]) == (split, level)
+    assert tiles_of(N) * pl["split"] <= 2 * SMS
 
 
 @pytest.mark.parametrize("wbits,gate_up", [(8, 0), (8, 1), (4, 0), (4, 1)])
