@@ -119,13 +119,21 @@ def quant_row(x_bits: np.ndarray):
 # int8 x int8 -> int32 block sums
 # ----------------------------------------------------------------------------
 
+def _block_sum(a_q: np.ndarray, w: np.ndarray, k0: int, blk: int) -> np.ndarray:
+    """int32 [M, N]: exact sum over K block [k0, k0+blk) of a[m,k] * w[k,n].
+
+    Computed in float64 (BLAS): every partial sum of int8 x int8 products over
+    a block of <= 64 is an integer below 2^21, exactly representable."""
+    a = a_q[:, k0:k0 + blk].astype(np.float64)
+    ww = w[k0:k0 + blk].astype(np.float64)
+    return (a @ ww).astype(np.int32)
+
+
 def _block_sums(a_q: np.ndarray, w: np.ndarray, blk: int) -> np.ndarray:
     """int32 [K/blk, M, N]: exact sum over each K block of a[m,k] * w[k,n]."""
     M, K = a_q.shape
     assert w.shape[0] == K and K % blk == 0
-    a = a_q.astype(np.int64).reshape(M, K // blk, blk).transpose(1, 0, 2)
-    ww = w.astype(np.int64).reshape(K // blk, blk, -1)
-    return np.matmul(a, ww).astype(np.int32)
+    return np.stack([_block_sum(a_q, w, k0, blk) for k0 in range(0, K, blk)])
 
 
 def unpack_w4(b: np.ndarray, b_z, wgrp: int) -> np.ndarray:
@@ -162,10 +170,10 @@ def gemm_i8_f32(a_q, a_s, b, b_s, residual_f32=None) -> np.ndarray:
     b_s = np.asarray(b_s, dtype=np.float32)
     M, K = a_q.shape
     N = b.shape[1]
-    sums = _block_sums(a_q, b, GROUP)
     out = np.zeros((M, N), dtype=np.float32)
     for kb in range(K // GROUP):
-        prod = (sums[kb].astype(np.float32) * a_s[:, kb:kb + 1]).astype(np.float32)
+        blk = _block_sum(a_q, b, kb * GROUP, GROUP)
+        prod = (blk.astype(np.float32) * a_s[:, kb:kb + 1]).astype(np.float32)
         out = (out + prod).astype(np.float32)
     out = (out * b_s[None, :]).astype(np.float32)
     if residual_f32 is not None:

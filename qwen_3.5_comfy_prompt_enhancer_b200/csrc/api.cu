@@ -14,6 +14,7 @@
 #include "../../include/qlin.h"
 #include "gemv.cuh"
 #include "quant.cuh"
+#include "tcgemm.cuh"
 #include "tcgemv.cuh"
 
 namespace qlin {
@@ -123,6 +124,8 @@ int tune_budget() { static const int v = env_int("QLIN_TUNE_BUDGET_KB", 0); retu
 int tune_ctas_per_sm() { static const int v = env_int("QLIN_TUNE_CTAS_PER_SM", 0); return v; }
 int tune_max_level() { static const int v = env_int("QLIN_TUNE_MAX_LEVEL", 2); return v; }
 int tune_max_cluster() { static const int v = env_int("QLIN_TUNE_MAX_CLUSTER", 8); return v; }
+// Rows from which W8 projections take the tensor-core GEMM (prefill) path.
+int prefill_min_m() { static const int v = env_int("QLIN_PREFILL_MIN_M", 128); return v; }
 
 // Kernel family for the small-M path: tcgen05 weight streaming (default) or
 // the CUDA-core dp4a GEMV (QLIN_SMALLM_KERNEL=dp4a, kept for comparison).
@@ -439,8 +442,61 @@ int run_tc(int wb, int epi, GemvArgs& a, int tiles, cudaStream_t st) {
   }
 }
 
+// ---------------------------------------------------------------- tensor-core GEMM (large M)
+int run_prefill_w8(const GemvArgs& a, int half_tiles, cudaStream_t st) {
+  DevInfo di;
+  if (int r = device_info(&di)) return r;
+  GemmArgs g;
+  memset(&g, 0, sizeof(g));
+  if (int r = make_map(&g.ta, a.a_q, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.K, a.M, a.K, 128, kGmRows, true)) return r;
+  bool vec = aligned(a.out, 16) && a.ldo % 8 == 0 && (!a.res || (aligned(a.res, 16) && a.ldr % 8 == 0));
+  for (int i = 0; i < a.nseg; ++i) {
+    g.seg[i] = a.seg[i];
+    if (int r = make_map(&g.seg[i].tw, a.seg[i].w, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.seg[i].n, a.K, a.seg[i].n,
+                         kTileN, 128, true))
+      return r;
+    vec = vec && a.seg[i].out_col % 8 == 0;
+  }
+  g.nseg = a.nseg;
+  g.half_tiles = half_tiles;
+  g.a_s = a.a_s;
+  g.M = a.M;
+  g.K = a.K;
+  g.out = a.out;
+  g.ldo = a.ldo;
+  g.res = a.res;
+  g.ldr = a.ldr;
+  g.vec_out = vec ? 1 : 0;
+  g.fault = di.fault;
+  const long long tiles = static_cast<long long>((a.M + kGmRows - 1) / kGmRows) * ((half_tiles + 1) / 2);
+  const int grid = static_cast<int>(tiles < di.sms ? tiles : di.sms);
+  static std::atomic<unsigned long long> configured{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(configured.load() & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGmSmem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc_gemm smem)");
+    configured.fetch_or(bit);
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(kGmThreads, 1, 1);
+  cfg.dynamicSmemBytes = kGmSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = tune_pdl() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel, g);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(tc_gemm)");
+  return QLIN_OK;
+}
+
 // Fills the split / ring fields of `a`, then launches.
 int run_gemv(int wb, int epi, GemvArgs& a, int tiles, cudaStream_t st) {
+  if (wb == 8 && epi == kEpiOut && use_tc() && a.M >= prefill_min_m()) return run_prefill_w8(a, tiles, st);
   if (use_tc()) return run_tc(wb, epi, a, tiles, st);
   DevInfo di;
   if (int r = device_info(&di)) return r;
@@ -497,6 +553,7 @@ int seg_w8(GemvSeg& s, const int8_t* w, const float* bs, int64_t K, int64_t n) {
   // 128-byte swizzle: the tile lands in the canonical MN-major layout that
   // tcgen05.mma reads (the dp4a kernel reads plain rows).
   if (int r = make_map(&s.tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, n, K, n, kTileN, 64, use_tc())) return r;
+  s.w = w;
   s.bs = bs;
   s.n = static_cast<int>(n);
   s.has_z = 0;

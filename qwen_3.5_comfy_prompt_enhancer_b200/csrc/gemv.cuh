@@ -59,6 +59,7 @@ struct GemvSeg {
   int out_col;       // first output column of this segment
   int tile_begin;    // first tile index of this segment
   int has_z;         // W4: zeros present
+  const void* w;     // weight base (host side: the prefill path builds its own tensor maps)
 };
 
 struct GemvArgs {

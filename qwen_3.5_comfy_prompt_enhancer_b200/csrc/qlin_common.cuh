@@ -290,6 +290,34 @@ __device__ __forceinline__ void tmem_ld32<32>(uint32_t taddr, uint32_t (&r)[32])
       : "r"(taddr));
 }
 
+// Each thread writes `v` into 32 consecutive 32-bit columns of its own TMEM lane.
+__device__ __forceinline__ void tmem_fill32(uint32_t taddr, uint32_t v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
+      "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
+      "r"(v)
+      : "memory");
+}
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Two fp32 lanes per instruction (sm_100): d = a + b, d = a * b + c.
+__device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
+  float2 d;
+  asm("{\n .reg .b64 x, y, z;\n mov.b64 x, {%2, %3};\n mov.b64 y, {%4, %5};\n add.rn.f32x2 z, x, y;\n"
+      " mov.b64 {%0, %1}, z;\n}\n"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 f2_fma(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n .reg .b64 x, y, z, w;\n mov.b64 x, {%2, %3};\n mov.b64 y, {%4, %5};\n mov.b64 z, {%6, %7};\n"
+      " fma.rn.f32x2 w, x, y, z;\n mov.b64 {%0, %1}, w;\n}\n"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
 // Shared-memory matrix descriptor for tcgen05.mma operands.
 //   bits  0-13  start address >> 4
 //   bits 16-29  leading-dimension byte offset >> 4
