@@ -251,6 +251,101 @@ def cpu_measure(seconds, max_steps=None):
 
 
 # ----------------------------------------------------------------------------- main
+# ----------------------------------------------------------------------------- config 5 / config 3 details
+TP_K, TP_I, TP_H, TP_WG = 5120, 17408, 5120, 128
+
+
+def tp_layer_bytes():
+    """Weights + scales + zeros of the config-5 gate/up + down layer (whole layer, all ranks)."""
+    def w(k, n):
+        return k * n // 2 + (k // TP_WG) * n * 3
+    return 2 * w(TP_K, TP_I) + w(TP_I, TP_H)
+
+
+def tp_detail(pkg, dev, world, pg, reps=20):
+    """Config 5: the column-split W4 MLP at M in {1, 4, 64, 256} on `world` GPUs
+    (strong scaling: the whole layer's work is fixed).  Device time per forward,
+    CUDA events on the current stream, max over ranks."""
+    g = torch.Generator(device=dev).manual_seed(5000)
+
+    def w(k, n):
+        return (torch.randint(0, 256, (k // 2, n), dtype=torch.uint8, device=dev, generator=g),
+                torch.exp(torch.randn(k // TP_WG, n, device=dev, generator=g) * 0.5 - 5.0).to(torch.bfloat16),
+                torch.randint(0, 16, (k // TP_WG, n), dtype=torch.uint8, device=dev, generator=g))
+    gate, up, down = w(TP_K, TP_I), w(TP_K, TP_I), w(TP_I, TP_H)
+    layer = pkg.tp.ColumnParallelW4MLP(gate, up, down, dev)
+    del gate, up, down
+    res = {}
+    for M in (1, 4, 64, 256):
+        a_q = torch.randint(-127, 128, (M, TP_K), dtype=torch.int8, device=dev, generator=g)
+        a_s = torch.rand(M, TP_K // 64, device=dev, generator=g) * 0.02
+        out = torch.empty(M, TP_H, dtype=torch.bfloat16, device=dev)
+        for _ in range(3):
+            layer(a_q, a_s, out)
+        torch.cuda.synchronize()
+        if pg:
+            pg.barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            layer(a_q, a_s, out)
+        e1.record()
+        e1.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / reps * 1e3], device=dev)
+        if pg:
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        us = float(t.item())
+        res[f"M{M}"] = {"us": us, "weight_tbs": tp_layer_bytes() / us / 1e6}
+    return {"workload": "config 5: W4 g128 gate_up 5120->2x17408 (fused SiLU+requant) + down 17408->5120, "
+                        "columns split over ranks, NCCL all-gather of h and of the output",
+            "n_gpus": world, "scaling": "strong", "layer_weight_bytes": tp_layer_bytes(), "per_M": res}
+
+
+def prefill_detail(pkg, dev, gen, reps=20):
+    """Config 3: W8A8 prefill GEMM (tcgen05) M in {512, 2048}, K = 2048, N = 12288; TOPS
+    against the dense int8 tensor peak taken as 2x the measured bf16 GEMM peak."""
+    K, N = 2048, 12288
+    W = [(torch.randint(-127, 128, (K, N), dtype=torch.int8, device=dev, generator=gen),
+          torch.exp(torch.randn(N, device=dev, generator=gen) * 0.5 - 6.0)) for _ in range(4)]
+    out = {}
+    for M in (512, 2048):
+        x = torch.randn(M, K, device=dev, generator=gen).to(torch.bfloat16)
+        q = torch.empty(M, K, dtype=torch.int8, device=dev)
+        s = torch.empty(M, K // 64, dtype=torch.float32, device=dev)
+        o = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+        for i in range(3):
+            pkg.quant_row(x, q, s)
+            pkg.gemm_i8(q, s, W[i % 4][0], W[i % 4][1], o)
+        torch.cuda.synchronize()
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        e[0].record()
+        for i in range(reps):
+            pkg.gemm_i8(q, s, W[i % 4][0], W[i % 4][1], o)
+        e[1].record()
+        for i in range(reps):
+            pkg.quant_row(x, q, s)
+            pkg.gemm_i8(q, s, W[i % 4][0], W[i % 4][1], o)
+        e[2].record()
+        e[2].synchronize()
+        g_us = e[0].elapsed_time(e[1]) / reps * 1e3
+        qg_us = e[1].elapsed_time(e[2]) / reps * 1e3
+        ops = 2.0 * M * N * K
+        out[f"M{M}"] = {"gemm_us": g_us, "gemm_tops": ops / g_us / 1e6, "quant_plus_gemm_us": qg_us}
+    peak_bf16 = None
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak_bf16 = float(json.load(f)["bf16_tflops"])
+    except Exception:
+        peak_bf16 = 1590.0
+    int8_peak = 2 * peak_bf16
+    for v in out.values():
+        v["frac_of_int8_peak"] = v["gemm_tops"] / int8_peak
+    return {"workload": "config 3: W8A8 prefill, X bf16 -> quant_row -> gemm_i8, K=2048, N=12288",
+            "int8_peak_tops": int8_peak, "int8_peak_kind": "2 x measured bf16 GEMM peak", "per_M": out}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -395,6 +490,10 @@ def main():
         pg.all_reduce(et, op=pg.ReduceOp.MIN)
         e2e_value = float(et.item()) * world
 
+    # ---- config 5 (all ranks, collectives) and config 3 (rank-local)
+    tp = tp_detail(pkg, dev, world, pg)
+    prefill = prefill_detail(pkg, dev, gen)
+
     cpu = None
     if rank == 0 and world == 1:
         n, el, cores = cpu_measure(args.cpu_seconds)
@@ -427,6 +526,8 @@ def main():
             "detail": {
                 "w8_gemv_cfg1_tbs": w8_bytes / w8secs / 1e12, "w8_gemv_cfg1_us": w8secs * 1e6,
                 "gate_up_w4_m4_us": gu_launch_s * 1e6,
+                "tp_layer": tp,
+                "prefill": prefill,
                 "fault_word": pkg._lib.load().qlin_device_fault(0),
             },
         }

@@ -8,7 +8,7 @@ The directory name contains a dot, so import it through
 ``__graft_entry__.load_package()`` (registers it as ``qwen35_b200``) or any
 other importlib alias; all imports inside the package are relative.
 """
-from . import _lib  # noqa: F401
+from . import _lib, tp  # noqa: F401
 from .kernels.common import GROUP  # noqa: F401
 from .kernels.gemm import gemm_i8, mlp_gate_up, mlp_gate_up_quant, proj3  # noqa: F401
 from .kernels.norm import quant_row  # noqa: F401

@@ -1,0 +1,109 @@
+"""Column-split W4 MLP (config 5 shapes) on the CUDA path.
+
+One GPU: the layer with world size 1 against the CPU oracle.  Two or more
+GPUs: one NCCL process per GPU; every rank's output must equal the one-GPU
+output bit for bit (a column split changes no per-column arithmetic).
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from oracle import qlin_oracle as O
+from qlin_testutil import bits, gen
+
+pytestmark = pytest.mark.gpu
+
+K, I, H, WG = 5120, 17408, 5120, 128
+
+
+def layer_weights(seed, device):
+    """Config-5 distributions: codes 0..15, lognormal(-5, 0.5) bf16 scales, zeros 0..15."""
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def w(k, n):
+        b = torch.randint(0, 256, (k // 2, n), dtype=torch.uint8, device=device, generator=g)
+        s = torch.exp(torch.randn(k // WG, n, device=device, generator=g) * 0.5 - 5.0).to(torch.bfloat16)
+        z = torch.randint(0, 16, (k // WG, n), dtype=torch.uint8, device=device, generator=g)
+        return b, s, z
+    return w(K, I), w(K, I), w(I, H)
+
+
+def acts(M, seed):
+    g = gen(seed)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    q, s = O.quant_row(bits(x))
+    return torch.from_numpy(q), torch.from_numpy(s)
+
+
+@pytest.mark.parametrize("M", [1, 4])
+def test_tp_layer_world1_matches_oracle(pkg, dev, M):
+    gate, up, down = layer_weights(8000, dev)
+    layer = pkg.tp.ColumnParallelW4MLP(gate, up, down, dev)
+    a_q, a_s = acts(M, 8100 + M)
+    out = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
+    layer(a_q.to(dev), a_s.to(dev), out)
+    cpu = [tuple(t.cpu() for t in w) for w in (gate, up, down)]
+    hq, hs = O.mlp_gate_up_quant_w4(a_q.numpy(), a_s.numpy(), cpu[0][0].numpy(), bits(cpu[0][1]),
+                                    cpu[1][0].numpy(), bits(cpu[1][1]), cpu[0][2].numpy(), cpu[1][2].numpy())
+    # h from the GPU is compared by the fused-quant rule; the down projection is then
+    # checked on the GPU's own h so that one +-1 code does not leak into the bf16 check
+    ghq, ghs = layer._ws[M]["hq"].cpu().numpy(), layer._ws[M]["hs"].cpu().numpy()
+    d = ghq.astype(np.int32) - hq.astype(np.int32)
+    assert np.abs(d).max() <= 1 and (d == 0).mean() >= 0.999
+    ref = O.gemm_w4(ghq, ghs, cpu[2][0].numpy(), bits(cpu[2][1]), cpu[2][2].numpy())
+    from qlin_testutil import assert_bf16_close
+    assert_bf16_close(bits(out), ref, f"tp world1 M={M}")
+
+
+def _rank(rank, world, port, M, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import datetime
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        import __graft_entry__
+        pkg = __graft_entry__.load_package()
+        gate, up, down = layer_weights(8000, dev)
+        layer = pkg.tp.ColumnParallelW4MLP(gate, up, down, dev)
+        a_q, a_s = acts(M, 8100 + M)
+        out = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
+        layer(a_q.to(dev), a_s.to(dev), out)
+        torch.cuda.synchronize()
+        q.put((rank, bits(out)))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("M", [1, 4])
+def test_tp_layer_nccl_ranks_equal_one_gpu(pkg, dev, M):
+    world = min(torch.cuda.device_count(), 8)
+    world = 8 if world >= 8 else (4 if world >= 4 else 2)
+    gate, up, down = layer_weights(8000, dev)
+    one = pkg.tp.ColumnParallelW4MLP(gate, up, down, dev)
+    a_q, a_s = acts(M, 8100 + M)
+    ref = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
+    one(a_q.to(dev), a_s.to(dev), ref)
+    torch.cuda.synchronize()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank, args=(r, world, port, M, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, b in got:
+        np.testing.assert_array_equal(b, bits(ref), err_msg=f"rank {rank} of {world}")
