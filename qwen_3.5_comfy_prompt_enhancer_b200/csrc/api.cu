@@ -90,8 +90,58 @@ int encode_fn(PFN_cuTensorMapEncodeTiled_v12000* fn) {
 
 // Row-major 2-D tensor [rows, cols] with `row_bytes` between rows, loaded in
 // boxes of [box_rows, box_cols].
+// Encoded tensor maps are cached by every encode parameter (a map describes
+// an address range and a layout, never the contents), so the weights and the
+// engine's reused workspace buffers are encoded once.
+struct MapKey {
+  const void* base;
+  uint64_t cols, rows, row_bytes;
+  uint32_t box_cols, box_rows, dt, sw;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && cols == o.cols && rows == o.rows && row_bytes == o.row_bytes &&
+           box_cols == o.box_cols && box_rows == o.box_rows && dt == o.dt && sw == o.sw;
+  }
+};
+constexpr int kMapCache = 256;
+struct MapCache {
+  std::mutex mu;
+  MapKey key[kMapCache];
+  CUtensorMap map[kMapCache];
+  bool used[kMapCache] = {};
+  int next = 0;
+};
+MapCache& map_cache() {
+  static MapCache c;
+  return c;
+}
+
+int encode_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t cols, uint64_t rows,
+               uint64_t row_bytes, uint32_t box_cols, uint32_t box_rows, bool sw128);
+
 int make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t cols, uint64_t rows,
              uint64_t row_bytes, uint32_t box_cols, uint32_t box_rows, bool sw128 = false) {
+  const MapKey k{base, cols, rows, row_bytes, box_cols, box_rows, static_cast<uint32_t>(dt), sw128 ? 1u : 0u};
+  MapCache& c = map_cache();
+  {
+    std::lock_guard<std::mutex> g(c.mu);
+    for (int i = 0; i < kMapCache; ++i)
+      if (c.used[i] && c.key[i] == k) {
+        *m = c.map[i];
+        return QLIN_OK;
+      }
+  }
+  if (int r = encode_map(m, base, dt, cols, rows, row_bytes, box_cols, box_rows, sw128)) return r;
+  std::lock_guard<std::mutex> g(c.mu);
+  const int i = c.next;
+  c.next = (c.next + 1) % kMapCache;
+  c.key[i] = k;
+  c.map[i] = *m;
+  c.used[i] = true;
+  return QLIN_OK;
+}
+
+int encode_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t cols, uint64_t rows,
+               uint64_t row_bytes, uint32_t box_cols, uint32_t box_rows, bool sw128) {
   PFN_cuTensorMapEncodeTiled_v12000 fn;
   if (int r = encode_fn(&fn)) return r;
   const cuuint64_t gdim[2] = {cols, rows};

@@ -14,8 +14,16 @@ def ptr(t):
     return None if t is None else t.data_ptr()
 
 
+try:
+    _raw_stream = torch._C._cuda_getCurrentRawStream
+except AttributeError:  # pragma: no cover - older torch
+    _raw_stream = None
+
+
 def stream_of(t):
     """Raw handle of torch's current CUDA stream on ``t``'s device."""
+    if _raw_stream is not None:
+        return _raw_stream(t.device.index if t.device.index is not None else torch.cuda.current_device())
     return torch.cuda.current_stream(t.device).cuda_stream
 
 

@@ -2,8 +2,9 @@
 
 The gate/up projection and the down projection are split by OUTPUT columns:
 rank r of g owns gate and up columns [r*I/g, (r+1)*I/g) and down columns
-[r*H/g, (r+1)*H/g).  Per-column arithmetic does not change with a column
-split, so every output element is computed exactly as on one GPU:
+[r*H/g, (r+1)*H/g).  Every output element is computed by the same formula as
+on one GPU (only the fp32 order of the kernels' K split, which they choose per
+launch shape, can differ):
 
   1. fused gate/up + SiLU + per-64 requantisation on the local columns
      (``mlp_gate_up_quant_w4``; the 64-column quantisation groups stay on one
@@ -14,8 +15,8 @@ split, so every output element is computed exactly as on one GPU:
      (``gemm_w4``);
   4. all-gather of the bf16 outputs -> [M, H] on every rank.
 
-A K (row) split would need an all-reduce that reorders the fp32 sums, so it is
-not used.  Weights are given in the engine layouts (packed uint8 [K/2, N],
+A K (row) split would add an all-reduce of fp32 partial sums across ranks, so
+it is not used.  Weights are given in the engine layouts (packed uint8 [K/2, N],
 bf16 scales [K/WG, N], optional uint8 zeros [K/WG, N]); each rank keeps a
 contiguous copy of its columns only.
 

@@ -1,8 +1,11 @@
 """Column-split W4 MLP (config 5 shapes) on the CUDA path.
 
 One GPU: the layer with world size 1 against the CPU oracle.  Two or more
-GPUs: one NCCL process per GPU; every rank's output must equal the one-GPU
-output bit for bit (a column split changes no per-column arithmetic).
+GPUs: one NCCL process per GPU.  All ranks must hold the same output bit for
+bit; the gathered h must match the one-GPU h by the fused-quantisation rule
+(the kernels pick their K split per launch shape, so a narrower shard can
+sum in another fp32 order), and each output must be within the bf16
+tolerance of the oracle's down projection of that h.
 """
 import os
 import socket
@@ -76,7 +79,7 @@ def _rank(rank, world, port, M, q):
         out = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
         layer(a_q.to(dev), a_s.to(dev), out)
         torch.cuda.synchronize()
-        q.put((rank, bits(out)))
+        q.put((rank, bits(out), layer._ws[M]["hq"].cpu().numpy(), layer._ws[M]["hs"].cpu().numpy()))
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -105,5 +108,12 @@ def test_tp_layer_nccl_ranks_equal_one_gpu(pkg, dev, M):
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    for rank, b in got:
-        np.testing.assert_array_equal(b, bits(ref), err_msg=f"rank {rank} of {world}")
+    from qlin_testutil import assert_bf16_close, assert_quant_close
+    hq1 = one._ws[M]["hq"].cpu().numpy()
+    hs1 = one._ws[M]["hs"].cpu().numpy()
+    down_cpu = [t.cpu() for t in down]
+    for rank, b, hq, hs in got:
+        np.testing.assert_array_equal(b, got[0][1], err_msg=f"rank {rank} differs from rank {got[0][0]}")
+        assert_quant_close(hq, hs, hq1, hs1, f"gathered h, rank {rank} of {world}")
+        ref_r = O.gemm_w4(hq, hs, down_cpu[0].numpy(), bits(down_cpu[1]), down_cpu[2].numpy())
+        assert_bf16_close(b, ref_r, f"tp rank {rank} of {world} M={M}")
