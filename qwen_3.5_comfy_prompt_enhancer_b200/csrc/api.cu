@@ -173,6 +173,7 @@ int tune_pdl() { static const int v = env_int("QLIN_TUNE_PDL", 1); return v; }
 int tune_budget() { static const int v = env_int("QLIN_TUNE_BUDGET_KB", 0); return v; }
 int tune_ctas_per_sm() { static const int v = env_int("QLIN_TUNE_CTAS_PER_SM", 0); return v; }
 int tune_max_level() { static const int v = env_int("QLIN_TUNE_MAX_LEVEL", 2); return v; }
+int tune_stream_budget() { static const int v = env_int("QLIN_TUNE_STREAM_BUDGET_KB", 0); return v; }
 int tune_max_cluster() { static const int v = env_int("QLIN_TUNE_MAX_CLUSTER", 8); return v; }
 // Rows from which W8 projections take the tensor-core GEMM (prefill) path.
 int prefill_min_m() { static const int v = env_int("QLIN_PREFILL_MIN_M", 128); return v; }
@@ -306,8 +307,13 @@ struct TcPlan {
 // but not for single-stream W4 (11.4 vs 8.4 us for the K = 6144 down
 // projection), whose per-group hand-offs after the grid dependency cost more
 // than the streamed batches.
-void plan_batches(int wb, int mr, int ns, int wgrp, TcPlan& pl) {
+void plan_batches(int wb, int mr, int ns, int wgrp, long long ctas, int sms, bool long_stream, TcPlan& pl) {
   const uint32_t budget = (tune_budget() > 0 ? tune_budget() : 112) * 1024;
+  // A long streamed launch (tens of MB of weights) that fits one CTA per SM
+  // may use most of shared memory for a deeper weight ring; its weight
+  // stream, not the next launch's prologue, is what bounds it.
+  const uint32_t stream_budget =
+      tune_stream_budget() > 0 ? tune_stream_budget() * 1024u : (long_stream && ctas <= sms ? 200u * 1024 : budget);
   const int s = pl.split, gmax = pl.gmax;
   const TcLayout base = tc_layout(wb, mr, ns, wgrp, gmax, 1, 1, 1, 1, s, 0);
   const int tmem_groups = static_cast<int>(kTmemBudget / base.per_buf);
@@ -331,15 +337,27 @@ void plan_batches(int wb, int mr, int ns, int wgrp, TcPlan& pl) {
     for (int ab = (gmax < 4 ? gmax : 4); !ok && ab >= 2; --ab)
       if (fits(1, gmax, ab, gmax < tmem_groups ? gmax : tmem_groups, alias)) ok = true, pl.level = 1;
   if (!ok) {
-    const int rb = 2, ab = wb == 4 ? 2 : 0;
-    const TcLayout one = tc_layout(wb, mr, ns, wgrp, gmax, 1, rb, ab, 2, s, 0);
-    const uint32_t per_group = rb * base.raw_stage + (wb == 4 ? ab * ns * 64 * kTileN : 0);
-    const uint32_t room = budget > one.total - per_group ? budget - (one.total - per_group) : 0;
-    int bs = static_cast<int>(room / per_group);
-    if (bs > tmem_groups / 2) bs = tmem_groups / 2;
-    if (bs < 1) bs = 1;
-    pl.bs = bs;
-    pl.rb = rb;
+    // Streamed: the most groups in flight (weight-ring slots x groups per
+    // batch) that fit, preferring larger batches (fewer hand-offs).
+    const int ab = wb == 4 ? 2 : 0;
+    int best_bs = 1, best_rb = 2;
+    // (short launches keep two slots: measured best for the config-2 shapes)
+    for (int rb = 2; rb <= (long_stream ? 4 : 2); ++rb) {
+      const TcLayout one = tc_layout(wb, mr, ns, wgrp, gmax, 1, rb, ab, 2, s, 0);
+      const uint32_t per_group = rb * base.raw_stage + (wb == 4 ? ab * ns * 64 * kTileN : 0);
+      const uint32_t fixed = one.total - per_group;
+      const uint32_t room = stream_budget > fixed ? stream_budget - fixed : 0;
+      int bs = static_cast<int>(room / per_group);
+      if (bs > tmem_groups / 2) bs = tmem_groups / 2;
+      if (bs > (gmax + rb - 1) / rb) bs = (gmax + rb - 1) / rb;
+      if (bs < 1) continue;
+      if (rb * bs > best_rb * best_bs || (rb * bs == best_rb * best_bs && bs > best_bs)) {
+        best_bs = bs;
+        best_rb = rb;
+      }
+    }
+    pl.bs = best_bs;
+    pl.rb = best_rb;
     pl.ab = ab;
     pl.nbb = 2;
     pl.alias = 0;
@@ -369,21 +387,43 @@ TcPlan plan_tc(int wb, int mr, int ns, int K, int wgrp, int tiles, int rowblocks
   const long long two_per_sm = 2ll * sms;
   // Per plan level: the largest split within the CTA target, and the
   // smallest split beyond it (within two CTAs per SM).
-  TcPlan in[3] = {}, up[3] = {}, any{};
+  TcPlan in[3] = {}, up[3] = {}, any{}, stream{};
+  long long stream_inflight = -1;
+  // Weight bytes of the launch: past a few tens of MB the launch is a long
+  // HBM stream rather than a short step between two dependencies.
+  const long long wbytes = static_cast<long long>(tiles) * ns * kTileN * K / (wb == 8 ? 1 : 2);
+  const bool long_stream = wbytes >= (32ll << 20);
   const int cmax = tune_max_cluster() < kMaxCluster ? tune_max_cluster() : kMaxCluster;
   const int smax = G < cmax ? G : cmax;
   for (int s = 1; s <= smax; ++s) {
     TcPlan pl{s, (G + s - 1) / s, 1, 1, 0, 1, 0, 0, 0};
     if (tune_split() > 0 && s != tune_split() && tune_split() <= smax) continue;
-    plan_batches(wb, mr, ns, wgrp, pl);
+    const long long ctas = static_cast<long long>(tiles) * s * rowblocks;
+    plan_batches(wb, mr, ns, wgrp, ctas, sms, long_stream, pl);
     if (pl.smem > kTcMaxSmem) continue;
     if (tune_split() == s) return pl;
-    const long long ctas = static_cast<long long>(tiles) * s * rowblocks;
     if (any.split == 0) any = pl;  // smallest feasible split, whatever its size
+    if (pl.level == 0 && long_stream) {
+      // Long streamed launches are bound by the weight bytes in flight over
+      // the whole GPU: resident CTAs x ring slots x groups per batch, divided
+      // by the waves the launch needs (measured on the config-5 shapes).
+      const TcLayout L = tc_layout(wb, mr, ns, wgrp, pl.gmax, pl.bs, pl.rb, pl.ab, pl.nbb, s, pl.alias);
+      const long long per_sm = (228 * 1024) / (static_cast<long long>(pl.smem) + 1024);
+      const long long slots = sms * (per_sm < 1 ? 1 : per_sm);
+      const long long resident = ctas < slots ? ctas : slots;
+      const long long waves = (ctas + slots - 1) / slots;  // a second wave serialises behind the first
+      const long long inflight = resident * pl.rb * pl.bs * L.raw_stage / waves;
+      if (inflight > stream_inflight) {
+        stream_inflight = inflight;
+        stream = pl;
+      }
+      continue;
+    }
     const bool within = ctas <= target;
     if (within || (s == 1 && in[pl.level].split == 0)) in[pl.level] = pl;
     else if (ctas <= two_per_sm && up[pl.level].split == 0) up[pl.level] = pl;
   }
+  if (long_stream) in[0] = stream, up[0] = TcPlan{};
   // Highest level first (more of the work ahead of the grid dependency);
   // extra splits add combine work, so beyond the target the smallest one.
   for (int lv = 2; lv >= 0; --lv) {

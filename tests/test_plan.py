@@ -40,7 +40,7 @@ def check_plan(pl, wbits, gate_up, M, K, wgrp):
         assert 2 <= pl["ab"] <= min(pl["gmax"], 4) or pl["ab"] == pl["gmax"] == 1
         assert pl["nbb"] == min(pl["gmax"], TMEM_SHARE // per_buf)
     else:
-        assert pl["rb"] == 2 and pl["nbb"] == 2 and pl["ab"] == (2 if wbits == 4 else 0)
+        assert pl["rb"] in (2, 3, 4) and pl["nbb"] == 2 and pl["ab"] == (2 if wbits == 4 else 0)
     assert pl["level"] == (2 if single else 1 if resident else 0)
     if pl["alias"]:
         # the partial sums of ranks 1..split-1 fit rank 0's operand region
