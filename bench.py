@@ -264,8 +264,9 @@ def tp_layer_bytes():
 
 def tp_detail(pkg, dev, world, pg, reps=20):
     """Config 5: the column-split W4 MLP at M in {1, 4, 64, 256} on `world` GPUs
-    (strong scaling: the whole layer's work is fixed).  Device time per forward,
-    CUDA events on the current stream, max over ranks."""
+    (strong scaling: the whole layer's work is fixed).  Device time per forward
+    (`us`: CUDA-graph replay of kernels + NCCL collectives; `eager_us`: one
+    Python call per forward), CUDA events on the current stream, max over ranks."""
     g = torch.Generator(device=dev).manual_seed(5000)
 
     def w(k, n):
@@ -283,21 +284,30 @@ def tp_detail(pkg, dev, world, pg, reps=20):
         for _ in range(3):
             layer(a_q, a_s, out)
         torch.cuda.synchronize()
-        if pg:
-            pg.barrier()
-        torch.cuda.synchronize()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(reps):
-            layer(a_q, a_s, out)
-        e1.record()
-        e1.synchronize()
-        t = torch.tensor([e0.elapsed_time(e1) / reps * 1e3], device=dev)
-        if pg:
-            pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        us = float(t.item())
-        res[f"M{M}"] = {"us": us, "weight_tbs": tp_layer_bytes() / us / 1e6}
+        graph = layer.capture(a_q, a_s, out)
+        times = []
+        for mode in ("eager", "graph"):
+            torch.cuda.synchronize()
+            if pg:
+                pg.barrier()
+            torch.cuda.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                if mode == "eager":
+                    layer(a_q, a_s, out)
+                else:
+                    graph.replay()
+            e1.record()
+            e1.synchronize()
+            t = torch.tensor([e0.elapsed_time(e1) / reps * 1e3], device=dev)
+            if pg:
+                pg.all_reduce(t, op=pg.ReduceOp.MAX)
+            times.append(float(t.item()))
+        del graph
+        us = times[1]
+        res[f"M{M}"] = {"us": us, "eager_us": times[0], "weight_tbs": tp_layer_bytes() / us / 1e6}
     return {"workload": "config 5: W4 g128 gate_up 5120->2x17408 (fused SiLU+requant) + down 17408->5120, "
                         "columns split over ranks, NCCL all-gather of h and of the output",
             "n_gpus": world, "scaling": "strong", "layer_weight_bytes": tp_layer_bytes(), "per_M": res}

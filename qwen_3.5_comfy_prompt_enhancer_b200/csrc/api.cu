@@ -389,10 +389,11 @@ TcPlan plan_tc(int wb, int mr, int ns, int K, int wgrp, int tiles, int rowblocks
   // smallest split beyond it (within two CTAs per SM).
   TcPlan in[3] = {}, up[3] = {}, any{}, stream{};
   long long stream_inflight = -1;
-  // Weight bytes of the launch: past a few tens of MB the launch is a long
-  // HBM stream rather than a short step between two dependencies.
+  // Weight bytes of the launch: past ~16 MB (the config-2 launches are at
+  // most 13 MB) the launch is a long HBM stream rather than a short step
+  // between two dependencies.
   const long long wbytes = static_cast<long long>(tiles) * ns * kTileN * K / (wb == 8 ? 1 : 2);
-  const bool long_stream = wbytes >= (32ll << 20);
+  const bool long_stream = wbytes >= (16ll << 20);
   const int cmax = tune_max_cluster() < kMaxCluster ? tune_max_cluster() : kMaxCluster;
   const int smax = G < cmax ? G : cmax;
   for (int s = 1; s <= smax; ++s) {

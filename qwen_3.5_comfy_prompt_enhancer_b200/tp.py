@@ -9,8 +9,8 @@ launch shape, can differ):
   1. fused gate/up + SiLU + per-64 requantisation on the local columns
      (``mlp_gate_up_quant_w4``; the 64-column quantisation groups stay on one
      rank because I/g is a multiple of 64);
-  2. all-gather of the int8 codes and their scales -> the full h [M, I] on
-     every rank (NCCL over NVLink);
+  2. one all-gather of the int8 codes and their scales (packed in one byte
+     buffer per rank) -> the full h [M, I] on every rank (NCCL over NVLink);
   3. down projection of the full h against the local down columns
      (``gemm_w4``);
   4. all-gather of the bf16 outputs -> [M, H] on every rank.
@@ -84,11 +84,15 @@ class ColumnParallelW4MLP:
         ws = self._ws.get(M)
         if ws is None:
             d, g = self.device, self.world
+            nq, ns = M * self.i_loc, M * (self.i_loc // GROUP) * 4
+            # The local int8 codes and their fp32 scales share one byte buffer,
+            # so a single all-gather moves both.
+            pack = torch.empty(nq + ns, dtype=torch.uint8, device=d)
             ws = {
-                "hq_loc": torch.empty(M, self.i_loc, dtype=torch.int8, device=d),
-                "hs_loc": torch.empty(M, self.i_loc // GROUP, dtype=torch.float32, device=d),
-                "hq_all": torch.empty(g * M, self.i_loc, dtype=torch.int8, device=d),
-                "hs_all": torch.empty(g * M, self.i_loc // GROUP, dtype=torch.float32, device=d),
+                "pack": pack,
+                "hq_loc": pack[:nq].view(torch.int8).view(M, self.i_loc),
+                "hs_loc": pack[nq:].view(torch.float32).view(M, self.i_loc // GROUP),
+                "pack_all": torch.empty(g * (nq + ns), dtype=torch.uint8, device=d),
                 "hq": torch.empty(M, self.inter, dtype=torch.int8, device=d),
                 "hs": torch.empty(M, self.inter // GROUP, dtype=torch.float32, device=d),
                 "o_loc": torch.empty(M, self.h_loc, dtype=torch.bfloat16, device=d),
@@ -96,6 +100,22 @@ class ColumnParallelW4MLP:
             }
             self._ws[M] = ws
         return ws
+
+    def _gather_h(self, ws, M):
+        """All-gather the packed (codes, scales) shards; reassemble h [M, I] and its scales."""
+        if self.world == 1:
+            ws["hq"].copy_(ws["hq_loc"])
+            ws["hs"].copy_(ws["hs_loc"])
+            return ws["hq"], ws["hs"]
+        dist.all_gather_into_tensor(ws["pack_all"], ws["pack"], group=self.group)
+        g, n, ng = self.world, self.i_loc, self.i_loc // GROUP
+        nq = M * n
+        allp = ws["pack_all"].view(g, -1)
+        codes = allp[:, :nq].view(torch.int8).view(g, M, n)
+        scales = allp[:, nq:].contiguous().view(torch.float32).view(g, M, ng)
+        ws["hq"].view(M, g, n).copy_(codes.permute(1, 0, 2))
+        ws["hs"].view(M, g, ng).copy_(scales.permute(1, 0, 2))
+        return ws["hq"], ws["hs"]
 
     def _gather_cols(self, loc, allbuf, full):
         """all-gather [M, n] shards into [M, world * n] (rank r at columns r*n)."""
@@ -115,9 +135,23 @@ class ColumnParallelW4MLP:
         ws = self._workspace(M)
         g, u, d = self.gate, self.up, self.down
         self.ops.gate_up_quant_w4(a_q, a_s, g[0], g[1], u[0], u[1], ws["hq_loc"], ws["hs_loc"], zg=g[2], zu=u[2])
-        hq = self._gather_cols(ws["hq_loc"], ws["hq_all"], ws["hq"])
-        hs = self._gather_cols(ws["hs_loc"], ws["hs_all"], ws["hs"])
+        hq, hs = self._gather_h(ws, M)
         self.ops.gemm_w4(hq, hs, d[0], d[1], ws["o_loc"], b_z=d[2])
         return self._gather_cols(ws["o_loc"], ws["o_all"], out)
 
     __call__ = forward
+
+    def capture(self, a_q, a_s, out, warmup=2):
+        """CUDA graph of ``forward`` on these buffers (kernels and NCCL
+        collectives).  Replay it after refilling ``a_q``/``a_s`` in place;
+        release the graph before the process group is destroyed."""
+        side = torch.cuda.Stream(device=self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self.forward(a_q, a_s, out)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            self.forward(a_q, a_s, out)
+        return graph
