@@ -15,6 +15,7 @@
 #include "gemv.cuh"
 #include "quant.cuh"
 #include "tcgemm.cuh"
+#include "tcgemm_w4.cuh"
 #include "tcgemv.cuh"
 
 namespace qlin {
@@ -585,9 +586,70 @@ int run_prefill_w8(const GemvArgs& a, int half_tiles, cudaStream_t st) {
   return QLIN_OK;
 }
 
+int run_prefill_w4(const GemvArgs& a, int half_tiles, cudaStream_t st) {
+  DevInfo di;
+  if (int r = device_info(&di)) return r;
+  GemmW4Args g;
+  memset(&g, 0, sizeof(g));
+  if (int r = make_map(&g.ta, a.a_q, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.K, a.M, a.K, 128, kGmRows, true)) return r;
+  const uint32_t nsr = g4_scale_rows(a.wgrp);
+  bool vec = aligned(a.out, 16) && a.ldo % 8 == 0 && (!a.res || (aligned(a.res, 16) && a.ldr % 8 == 0));
+  for (int i = 0; i < a.nseg; ++i) {
+    const GemvSeg& s0 = a.seg[i];
+    GemvSeg& s1 = g.seg[i];
+    s1 = s0;
+    if (int r = make_map(&s1.tw, s0.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, s0.n, a.K / 2, s0.n, kTileN, 64)) return r;
+    if (int r = make_map(&s1.ts, s0.sp, CU_TENSOR_MAP_DATA_TYPE_UINT16, s0.n, a.K / a.wgrp, 2ull * s0.n, kTileN, nsr))
+      return r;
+    if (s0.zp) {
+      if (int r = make_map(&s1.tz, s0.zp, CU_TENSOR_MAP_DATA_TYPE_UINT8, s0.n, a.K / a.wgrp, s0.n, kTileN, nsr))
+        return r;
+    }
+    vec = vec && s0.out_col % 8 == 0;
+  }
+  g.nseg = a.nseg;
+  g.half_tiles = half_tiles;
+  g.a_s = a.a_s;
+  g.M = a.M;
+  g.K = a.K;
+  g.wgrp = a.wgrp;
+  g.out = a.out;
+  g.ldo = a.ldo;
+  g.res = a.res;
+  g.ldr = a.ldr;
+  g.vec_out = vec ? 1 : 0;
+  g.fault = di.fault;
+  const long long tiles = static_cast<long long>((a.M + kGmRows - 1) / kGmRows) * ((half_tiles + 1) / 2);
+  const int grid = static_cast<int>(tiles < di.sms ? tiles : di.sms);
+  static std::atomic<unsigned long long> configured{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(configured.load() & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(tc_gemm_w4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kG4Smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc_gemm_w4 smem)");
+    configured.fetch_or(bit);
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(kG4Threads, 1, 1);
+  cfg.dynamicSmemBytes = kG4Smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = tune_pdl() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_w4_kernel, g);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(tc_gemm_w4)");
+  return QLIN_OK;
+}
+
 // Fills the split / ring fields of `a`, then launches.
 int run_gemv(int wb, int epi, GemvArgs& a, int tiles, cudaStream_t st) {
   if (wb == 8 && epi == kEpiOut && use_tc() && a.M >= prefill_min_m()) return run_prefill_w8(a, tiles, st);
+  if (wb == 4 && epi == kEpiOut && use_tc() && a.M >= prefill_min_m() && a.wgrp % 64 == 0)
+    return run_prefill_w4(a, tiles, st);
   if (use_tc()) return run_tc(wb, epi, a, tiles, st);
   DevInfo di;
   if (int r = device_info(&di)) return r;
@@ -665,6 +727,9 @@ int seg_w4(GemvSeg& s, const uint8_t* w, const void* sc, const uint8_t* z, int64
   s.bs = nullptr;
   s.n = static_cast<int>(n);
   s.has_z = z ? 1 : 0;
+  s.w = w;
+  s.sp = sc;
+  s.zp = z;
   return QLIN_OK;
 }
 

@@ -59,7 +59,9 @@ struct GemvSeg {
   int out_col;       // first output column of this segment
   int tile_begin;    // first tile index of this segment
   int has_z;         // W4: zeros present
-  const void* w;     // weight base (host side: the prefill path builds its own tensor maps)
+  const void* w;     // weight base (host side: the prefill paths build their own tensor maps)
+  const void* sp;    // W4 scale base (host side)
+  const void* zp;    // W4 zero base or null (host side)
 };
 
 struct GemvArgs {

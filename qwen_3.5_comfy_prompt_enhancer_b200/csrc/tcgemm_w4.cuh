@@ -1,0 +1,379 @@
+// Tensor-core GEMM for large M (prefill) with W4 weights: int8 activations x
+// group-quantised 4-bit weights, per-(64-K sub-block) int32 on tcgen05,
+// promoted exactly as the reference's K loop (kernels/w4.py:64-136):
+//   w[k, n]    = nibble(k, n) - z[k / WG, n]          (z = 8 without zeros)
+//   acc[m, n] += float(sum_{k in sub-block} a_q[m, k] * w[k, n]) * (a_s[m, k/64] * ws[k / WG, n])
+//   out[m, n]  = bf16(acc[m, n] (+ residual[m, n]))
+// for weight groups WG that are multiples of 64 (one activation scale and one
+// weight scale per 64-K sub-block).  WG = 32 stays on the small-M kernel.
+//
+// Same tiling, pipeline and promotion as the W8 GEMM (tcgemm.cuh): 128 rows x
+// 256 columns per tile (two 128-column halves of the column segments),
+// persistent CTAs, int32 group sums in two tensor-memory buffers armed with
+// the bits of 2^23 + 2^22.  Differences:
+//   * a stage carries the packed nibbles (64 packed rows = 128 K per half),
+//     the bf16 scale rows and the zero rows of its groups;
+//   * two unpack warps turn each stage into signed int8 tiles (nibble - z,
+//     one SIMD byte subtraction per 4 weights) in a 2-slot ring of
+//     MN-major 128-byte-swizzled operand tiles, and copy the group scales,
+//     converted to fp32, into an 8-slot ring that outlives the raw stage;
+//   * the epilogue multiplies the row's activation scale by each column's
+//     weight scale before the multiply-add, in the reference's order.
+#pragma once
+
+#include "tcgemm.cuh"
+
+namespace qlin {
+
+constexpr int kG4Stages = 4;
+constexpr int kG4Threads = 384;                 // 12 warps
+constexpr int kG4WarpUnpack = 10;               // warps 10, 11
+constexpr int kG4UnpackThreads = 64;
+constexpr int kG4UBufs = 2;                     // unpacked operand ring (stages)
+constexpr int kG4ScaleSlots = 8;                // per-group fp32 scale ring
+constexpr uint32_t kG4A = 128 * 128;            // activation box: 128 K x 128 rows
+constexpr uint32_t kG4Packed = 64 * 128;        // per half: 64 packed rows x 128 columns
+constexpr uint32_t kG4Scale = 2 * 128 * 2;      // per half: up to 2 bf16 scale rows
+constexpr uint32_t kG4Zero = 2 * 128;           // per half: up to 2 zero rows
+constexpr uint32_t kG4Half = kG4Packed + kG4Scale + kG4Zero;   // 8960, multiple of 128
+constexpr uint32_t kG4Stage = kG4A + 2 * kG4Half;                // 34304
+constexpr uint32_t kG4StageAligned = (kG4Stage + 1023) / 1024 * 1024;
+constexpr uint32_t kG4UTile = 128 * 128;        // unpacked: 128 K rows x 128 columns
+constexpr uint32_t kG4UStage = 2 * kG4UTile;
+constexpr uint32_t kG4ScaleRing = kG4ScaleSlots * 2 * 128 * 4;   // [slot][half][128] fp32
+constexpr uint32_t kG4RawOff = 0;
+constexpr uint32_t kG4UOff = kG4Stages * kG4StageAligned;
+constexpr uint32_t kG4ScaleOff = kG4UOff + kG4UBufs * kG4UStage;
+constexpr uint32_t kG4BarOff = kG4ScaleOff + kG4ScaleRing;
+constexpr uint32_t kG4Smem = kG4BarOff + 256 + 1024;
+static_assert(kG4Smem <= 227 * 1024, "W4 prefill ring exceeds shared memory");
+
+struct GemmW4Args {
+  CUtensorMap ta;     // a_q [M, K] int8, box 128 K x 128 rows, 128-byte swizzle
+  GemvSeg seg[3];     // tw: packed [K/2, n] box 128 x 64; ts: bf16 [K/WG, n] box 128 x nsr; tz: zeros, same
+  int nseg;
+  int half_tiles;
+  const float* a_s;   // [M, K/64]
+  int M, K, wgrp;
+  void* out;
+  long long ldo;
+  const void* res;
+  long long ldr;
+  int vec_out;
+  unsigned* fault;
+};
+
+// Scale rows a 128-K stage needs: K/WG rows of the group scale table cover
+// [k0, k0 + 128); with WG >= 128 that is one row, with WG = 64 two.
+__host__ __device__ constexpr int g4_scale_rows(int wgrp) { return wgrp % 128 == 0 ? 1 : 2; }
+
+__device__ __forceinline__ float2 f2_mul(float2 a, float2 b) {
+  float2 d;
+  asm("{\n .reg .b64 x, y, z;\n mov.b64 x, {%2, %3};\n mov.b64 y, {%4, %5};\n mul.rn.f32x2 z, x, y;\n"
+      " mov.b64 {%0, %1}, z;\n}\n"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+__device__ __forceinline__ int g4_seg_of(const GemmW4Args& p, int ht) {
+  int si = 0;
+  if (p.nseg > 1 && ht >= p.seg[1].tile_begin) si = 1;
+  if (p.nseg > 2 && ht >= p.seg[2].tile_begin) si = 2;
+  return si;
+}
+
+__global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_constant__ GemmW4Args p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kG4BarOff);
+  uint64_t* empty = full + kG4Stages;
+  uint64_t* ufull = empty + kG4Stages;
+  uint64_t* uempty = ufull + kG4UBufs;
+  uint64_t* tfull = uempty + kG4UBufs;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  float* sring = reinterpret_cast<float*>(smem + kG4ScaleOff);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.K / kGroup;
+  const int nstage = (G + 1) / 2;
+  const int mtiles = (p.M + kGmRows - 1) / kGmRows;
+  const int ptiles = (p.half_tiles + 1) / 2;
+  const int tiles = mtiles * ptiles;
+  const int nsr = g4_scale_rows(p.wgrp);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int i = 0; i < kG4Stages; ++i) {
+        mbar_init(full + i, 1);
+        mbar_init(empty + i, 1);
+      }
+      for (int i = 0; i < kG4UBufs; ++i) {
+        mbar_init(ufull + i, kG4UnpackThreads);
+        mbar_init(uempty + i, 1);
+      }
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(tfull + i, 1);
+        mbar_init(tempty + i, 256);
+      }
+      fence_mbar_init();
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  pdl_wait();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    uint32_t sc = 0;
+    bool ok = true;
+    const uint64_t pol = l2_policy_evict_last();
+    for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
+      const int m0 = (t % mtiles) * kGmRows;
+      const int pt = t / mtiles;
+      for (int st = 0; st < nstage; ++st, ++sc) {
+        const int slot = sc % kG4Stages;
+        if (!mbar_wait(empty + slot, ((sc / kG4Stages) & 1) ^ 1)) {
+          ok = false;
+          break;
+        }
+        if (elect_one()) {
+          uint8_t* sa = smem + kG4RawOff + slot * kG4StageAligned;
+          uint32_t bytes = kG4A;
+          for (int h = 0; h < 2; ++h) {
+            const int ht = 2 * pt + h;
+            if (ht >= p.half_tiles) continue;
+            bytes += kG4Packed + nsr * 128 * 2 + (p.seg[g4_seg_of(p, ht)].has_z ? nsr * 128 : 0);
+          }
+          mbar_arrive_expect_tx(full + slot, bytes);
+          tma_load_2d(sa, &p.ta, st * 128, m0, full + slot, pol);
+          const int srow = (st * 128) / p.wgrp;
+          for (int h = 0; h < 2; ++h) {
+            const int ht = 2 * pt + h;
+            if (ht >= p.half_tiles) continue;
+            const GemvSeg& sg = p.seg[g4_seg_of(p, ht)];
+            const int n0 = (ht - sg.tile_begin) * kTileN;
+            uint8_t* raw = sa + kG4A + h * kG4Half;
+            tma_load_2d(raw, &sg.tw, n0, st * 64, full + slot, pol);
+            tma_load_2d(raw + kG4Packed, &sg.ts, n0, srow, full + slot, pol);
+            if (sg.has_z) tma_load_2d(raw + kG4Packed + kG4Scale, &sg.tz, n0, srow, full + slot, pol);
+          }
+        }
+        __syncwarp();
+      }
+    }
+    if (!ok && lane == 0) atomicOr(p.fault, kFaultEmptyWait);
+    const uint32_t issued = sc;
+    for (uint32_t i = issued > kG4Stages ? issued - kG4Stages : 0; i < issued; ++i)
+      mbar_wait(full + i % kG4Stages, (i / kG4Stages) & 1);
+  } else if (warp >= kG4WarpUnpack) {
+    // ------------------------------------------------------------------ unpack
+    const int u = threadIdx.x - kG4WarpUnpack * 32;
+    uint32_t sc = 0, gbase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
+      const int pt = t / mtiles;
+      for (int st = 0; st < nstage; ++st, ++sc) {
+        const int slot = sc % kG4Stages;
+        const int ub = sc % kG4UBufs;
+        if (!mbar_wait(full + slot, (sc / kG4Stages) & 1) ||
+            !mbar_wait(uempty + ub, ((sc / kG4UBufs) & 1) ^ 1)) {
+          ok = false;
+          break;
+        }
+        const int ng = (2 * st + 1 < G) ? 2 : 1;
+        const int k0 = st * 128;
+        const int srow = k0 / p.wgrp;
+        for (int h = 0; h < 2; ++h) {
+          const int ht = 2 * pt + h;
+          const uint8_t* raw = smem + kG4RawOff + slot * kG4StageAligned + kG4A + h * kG4Half;
+          uint8_t* ut = smem + kG4UOff + ub * kG4UStage + h * kG4UTile;
+          const bool has_z = ht < p.half_tiles && p.seg[g4_seg_of(p, ht)].has_z;
+          // 64 packed rows x 8 chunks of 16 columns; packed row j holds K = 2j
+          // (low nibble) and 2j + 1 (high nibble) of 16 columns.
+#pragma unroll 2
+          for (int i = 0; i < 8; ++i) {
+            const int idx = u + kG4UnpackThreads * i;
+            const int pr = idx >> 3, ch = idx & 7;
+            const uint4 v = *reinterpret_cast<const uint4*>(raw + pr * 128 + ch * 16);
+            const int zr = (k0 + 2 * pr) / p.wgrp - srow;   // both K of the row share a group
+            const uint4 z = has_z ? *reinterpret_cast<const uint4*>(raw + kG4Packed + kG4Scale + zr * 128 + ch * 16)
+                                  : make_uint4(0x08080808u, 0x08080808u, 0x08080808u, 0x08080808u);
+            uint4 lo, hi;
+            lo.x = __vsub4(v.x & 0x0F0F0F0Fu, z.x); hi.x = __vsub4((v.x >> 4) & 0x0F0F0F0Fu, z.x);
+            lo.y = __vsub4(v.y & 0x0F0F0F0Fu, z.y); hi.y = __vsub4((v.y >> 4) & 0x0F0F0F0Fu, z.y);
+            lo.z = __vsub4(v.z & 0x0F0F0F0Fu, z.z); hi.z = __vsub4((v.z >> 4) & 0x0F0F0F0Fu, z.z);
+            lo.w = __vsub4(v.w & 0x0F0F0F0Fu, z.w); hi.w = __vsub4((v.w >> 4) & 0x0F0F0F0Fu, z.w);
+            const int r0 = 2 * pr, r1 = 2 * pr + 1;
+            *reinterpret_cast<uint4*>(ut + r0 * 128 + ((ch ^ (r0 & 7)) << 4)) = lo;
+            *reinterpret_cast<uint4*>(ut + r1 * 128 + ((ch ^ (r1 & 7)) << 4)) = hi;
+          }
+          // fp32 weight scales of the stage's groups into the ring (two columns per thread)
+          const uint16_t* sc16 = reinterpret_cast<const uint16_t*>(raw + kG4Packed);
+          for (int gi = 0; gi < ng; ++gi) {
+            const int row = (k0 + gi * 64) / p.wgrp - srow;
+            float* dst = sring + (((gbase + gi) % kG4ScaleSlots) * 2 + h) * 128;
+            dst[2 * u] = bf16_bits_to_f32(sc16[row * 128 + 2 * u]);
+            dst[2 * u + 1] = bf16_bits_to_f32(sc16[row * 128 + 2 * u + 1]);
+          }
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(ufull + ub);
+        gbase += ng;
+      }
+    }
+    if (!ok && lane == 0) atomicOr(p.fault, kFaultFullWait);
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = idesc_i8(128, 128, true, true, false, true);
+    uint32_t sc = 0, gc = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
+      const int pt = t / mtiles;
+      const int nh = 2 * pt + 1 < p.half_tiles ? 2 : 1;
+      for (int st = 0; ok && st < nstage; ++st, ++sc) {
+        const int slot = sc % kG4Stages;
+        const int ub = sc % kG4UBufs;
+        ok = mbar_wait(full + slot, (sc / kG4Stages) & 1) && mbar_wait(ufull + ub, (sc / kG4UBufs) & 1);
+        const int ng = (2 * st + 1 < G) ? 2 : 1;
+        for (int gi = 0; ok && gi < ng; ++gi, ++gc) {
+          const int b = gc & 1;
+          ok = mbar_wait(tempty + b, (gc >> 1) & 1);
+          if (!ok) break;
+          tc_fence_after();
+          if (elect_one()) {
+            const uint32_t sa = smem_u32(smem + kG4RawOff + slot * kG4StageAligned);
+            const uint32_t su = smem_u32(smem + kG4UOff + ub * kG4UStage);
+#pragma unroll
+            for (int kk = 0; kk < 2; ++kk) {
+              const uint64_t ad = smem_desc(sa + gi * 64 + kk * 32, 16, 1024, kLayoutSw128);
+              for (int h = 0; h < nh; ++h) {
+                const uint64_t bd = smem_desc(su + h * kG4UTile + (gi * 64 + kk * 32) * 128, 8192, 1024, kLayoutSw128);
+                tc_mma_i8(tbase + b * 256 + h * 128, ad, bd, idesc, 1u);
+              }
+            }
+            tc_commit(tfull + b);
+            if (gi == ng - 1) {
+              tc_commit(empty + slot);
+              tc_commit(uempty + ub);
+            }
+          }
+          __syncwarp();
+        }
+      }
+    }
+    if (!ok && lane == 0) atomicOr(p.fault, kFaultMmaWait);
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2-9)
+    const int q = warp & 3;         // TMEM lane quarter = rows 32q .. 32q+31
+    const int h = (warp - 2) >> 2;  // column half
+    const uint32_t lane_base = tbase + (static_cast<uint32_t>(32 * q) << 16) + h * 128;
+#pragma unroll
+    for (int b = 0; b < 2; ++b)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_fill32(lane_base + b * 256 + 32 * c, kGmMagic);
+    tc_wait_st();
+    tc_fence_before();
+    mbar_arrive(tempty + 0);
+    mbar_arrive(tempty + 1);
+
+    uint32_t gc = 0;
+    bool ok = true;
+    const float2 neg_magic = make_float2(-12582912.0f, -12582912.0f);
+    for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
+      const int m0 = (t % mtiles) * kGmRows;
+      const int ht = 2 * (t / mtiles) + h;
+      const int m = m0 + 32 * q + lane;
+      const bool mvalid = m < p.M;
+      const float* asrow = p.a_s + static_cast<long long>(mvalid ? m : 0) * G;
+      float2 acc[64];
+#pragma unroll
+      for (int j = 0; j < 64; ++j) acc[j] = make_float2(0.0f, 0.0f);
+      float s_next = mvalid ? __ldg(asrow) : 0.0f;
+      for (int g = 0; g < G; ++g, ++gc) {
+        const int b = gc & 1;
+        const float as = s_next;
+        if (g + 1 < G) s_next = mvalid ? __ldg(asrow + g + 1) : 0.0f;
+        ok = mbar_wait(tfull + b, (gc >> 1) & 1);
+        if (!ok) break;
+        tc_fence_after();
+        const float2 as2 = make_float2(as, as);
+        const float* wsg = sring + ((gc % kG4ScaleSlots) * 2 + h) * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint32_t r[16];
+          tmem_ld32<16>(lane_base + b * 256 + 16 * c, r);
+          tc_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            // (a_s * ws) first, then the int32 sum times that (kernels/w4.py:103-104)
+            const float2 ws = *reinterpret_cast<const float2*>(wsg + 16 * c + 2 * j);
+            const float2 t2 = f2_mul(as2, ws);
+            const float2 v = f2_add(make_float2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])), neg_magic);
+            acc[8 * c + j] = f2_fma(v, t2, acc[8 * c + j]);
+          }
+          if (c & 1) tmem_fill32(lane_base + b * 256 + 16 * (c - 1), kGmMagic);
+        }
+        tc_wait_st();
+        tc_fence_before();
+        mbar_arrive(tempty + b);
+      }
+      if (!ok) break;
+      // ---------------------------------------------------------------- tile epilogue
+      if (ht >= p.half_tiles || !mvalid) continue;
+      const GemvSeg& sg = p.seg[g4_seg_of(p, ht)];
+      const int n0 = (ht - sg.tile_begin) * kTileN;
+      __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<long long>(m) * p.ldo + sg.out_col;
+      const __nv_bfloat16* rrow =
+          p.res ? reinterpret_cast<const __nv_bfloat16*>(p.res) + static_cast<long long>(m) * p.ldr + sg.out_col
+                : nullptr;
+#pragma unroll
+      for (int c8 = 0; c8 < 16; ++c8) {
+        const int n = n0 + 8 * c8;
+        if (n >= sg.n) continue;  // N % 16 == 0: a chunk of 8 is all in or all out
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          v[2 * e] = acc[4 * c8 + e].x;
+          v[2 * e + 1] = acc[4 * c8 + e].y;
+        }
+        if (rrow) {
+          if (p.vec_out) {
+            const uint4 rv = *reinterpret_cast<const uint4*>(rrow + n);
+            const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rv);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(v[e], __bfloat162float(rb[e]));
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(v[e], __bfloat162float(rrow[n + e]));
+          }
+        }
+        if (p.vec_out) {
+          uint4 ov;
+          __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&ov);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) ob[e] = __float2bfloat16_rn(v[e]);
+          *reinterpret_cast<uint4*>(orow + n) = ov;
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) orow[n + e] = __float2bfloat16_rn(v[e]);
+        }
+      }
+    }
+    if (!ok && lane == 0) atomicOr(p.fault, kFaultFullWait);
+  }
+  pdl_launch_dependents();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tbase, 512);
+}
+
+}  // namespace qlin

@@ -1,7 +1,8 @@
-"""GPU parity of the large-M (prefill) tensor-core GEMM path against the CPU oracle.
+"""GPU parity of the large-M (prefill) tensor-core GEMM paths against the CPU oracle.
 
-W8 projections with M >= 128 rows take the tcgen05 GEMM (128-row x 256-column
-tiles, per-64-K-group int32 promoted with the activation row scale).  Same
+W8 projections and W4 projections (weight groups of 64 * k) with M >= 128
+rows take the tcgen05 GEMMs (128-row x 256-column tiles, per-64-K-group int32
+promoted with the activation row scale, times the group weight scale for W4).  Same
 bars as the small-M tests: bf16 within 1e-3 + 1e-2|ref|, integer work bit
 exact (unit scales), untouched columns outside the output stay untouched.
 Config 3 (M = 2048, K = 2048, N = 12288) is checked on the full output for
@@ -119,3 +120,68 @@ def test_prefill_matches_small_m_path_at_threshold(pkg, dev):
         out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
         pkg.gemm_i8(cu(a[:M]), cu(s[:M]), cu(b), cu(bs), out)
         assert_bf16_close(bits(out), ref[:M], f"threshold M={M}")
+
+
+# ----------------------------------------------------------------------------- W4 (groups of 64 * k)
+from qlin_testutil import w4  # noqa: E402
+
+
+@pytest.mark.parametrize("M", [128, 200, 300])
+@pytest.mark.parametrize("wg,zeros", [(64, True), (128, True), (128, False), (256, True), (192, True)])
+def test_prefill_gemm_w4(pkg, dev, M, wg, zeros):
+    K = 768 if wg == 192 else 1024
+    N = 400
+    g = gen(6600 + M + wg + zeros)
+    a, s = acts_x(g, M, K)
+    b, sc, z = w4(g, K, N, wg, zeros)
+    res = torch.randn(M, N, generator=g).to(torch.bfloat16)
+    out = res.clone().to(dev)
+    pkg.gemm_w4(cu(a), cu(s), cu(b), cu(sc), out, residual=out, b_z=cu(z))
+    ref = O.gemm_w4(a.numpy(), s.numpy(), b.numpy(), bits(sc), None if z is None else z.numpy(), bits(res))
+    assert_bf16_close(bits(out), ref, f"prefill gemm_w4 M={M} wg={wg} zeros={zeros}")
+
+
+@pytest.mark.parametrize("M,K,wg", [(128, 192, 64), (256, 2048, 128)])
+def test_prefill_w4_integer_exact(pkg, dev, M, K, wg):
+    """Unit scales: the output is the exact integer sum of a * (nibble - z)."""
+    N = 272
+    g = gen(6700 + M)
+    a = torch.randint(-127, 128, (M, K), dtype=torch.int8, generator=g)
+    b, _, z = w4(g, K, N, wg, True)
+    sc = torch.ones(K // wg, N, dtype=torch.bfloat16)
+    out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    pkg.gemm_w4(cu(a), cu(torch.ones(M, K // 64)), cu(b), cu(sc), out, b_z=cu(z))
+    w = O.unpack_w4(b.numpy(), z.numpy(), wg).astype(np.float64)
+    exact = a.numpy().astype(np.float64) @ w
+    np.testing.assert_array_equal(bits(out), O.f32_to_bf16_bits(exact.astype(np.float32)))
+
+
+def test_prefill_proj3_w4(pkg, dev):
+    M, K, wg = 160, 2048, 128
+    g = gen(6800)
+    a, s = acts_x(g, M, K)
+    s1 = w4(g, K, 2048, wg, True)
+    s2 = w4(g, K, 528, wg, True)
+    out = torch.zeros(M, 2576 + 128, dtype=torch.bfloat16, device=dev)
+    pkg.proj3_w4(cu(a), cu(s), cu(s1[0]), cu(s1[1]), cu(s2[0]), cu(s2[1]), None, None, out,
+                 z1=cu(s1[2]), z2=cu(s2[2]))
+    ref = O.proj3(a.numpy(), s.numpy(), [(s1[0].numpy(), bits(s1[1]), s1[2].numpy()),
+                                         (s2[0].numpy(), bits(s2[1]), s2[2].numpy())])
+    assert_bf16_close(bits(out)[:, :2576], ref, "prefill proj3_w4")
+    assert (bits(out)[:, 2576:] == 0).all()
+
+
+def test_config3_prefill_w4_variant(pkg, dev):
+    """Config 3's W4 variant: M = 2048, K = 2048, N = 12288, group 128 with zeros;
+    64 sampled rows against the oracle, every output finite."""
+    M, K, N, wg = 2048, 2048, 12288, 128
+    g = gen(6900)
+    a, s = acts_x(g, M, K, outliers=True)
+    b, sc, z = w4(g, K, N, wg, True)
+    out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    pkg.gemm_w4(cu(a), cu(s), cu(b), cu(sc), out, b_z=cu(z))
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+    rows = np.sort(np.random.default_rng(7).choice(M, 64, replace=False))
+    ref = O.gemm_w4(a.numpy()[rows], s.numpy()[rows], b.numpy(), bits(sc), z.numpy())
+    assert_bf16_close(bits(out)[rows], ref, "config 3 W4")
