@@ -343,6 +343,25 @@ def prefill_detail(pkg, dev, gen, reps=20):
         qg_us = e[1].elapsed_time(e[2]) / reps * 1e3
         ops = 2.0 * M * N * K
         out[f"M{M}"] = {"gemm_us": g_us, "gemm_tops": ops / g_us / 1e6, "quant_plus_gemm_us": qg_us}
+    # the W4 variant at the same shape (g128 with zeros, config-2 distributions)
+    b4 = torch.randint(0, 256, (K // 2, N), dtype=torch.uint8, device=dev, generator=gen)
+    s4 = torch.exp(torch.randn(K // 128, N, device=dev, generator=gen) * 0.5 - 5.0).to(torch.bfloat16)
+    z4 = torch.randint(0, 16, (K // 128, N), dtype=torch.uint8, device=dev, generator=gen)
+    for M in (512, 2048):
+        q = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev, generator=gen)
+        s = torch.rand(M, K // 64, device=dev, generator=gen) * 0.02
+        o = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+        for _ in range(3):
+            pkg.gemm_w4(q, s, b4, s4, o, b_z=z4)
+        torch.cuda.synchronize()
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        e[0].record()
+        for _ in range(reps):
+            pkg.gemm_w4(q, s, b4, s4, o, b_z=z4)
+        e[1].record()
+        e[1].synchronize()
+        us = e[0].elapsed_time(e[1]) / reps * 1e3
+        out[f"W4_M{M}"] = {"gemm_us": us, "gemm_tops": 2.0 * M * N * K / us / 1e6}
     peak_bf16 = None
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -352,7 +371,8 @@ def prefill_detail(pkg, dev, gen, reps=20):
     int8_peak = 2 * peak_bf16
     for v in out.values():
         v["frac_of_int8_peak"] = v["gemm_tops"] / int8_peak
-    return {"workload": "config 3: W8A8 prefill, X bf16 -> quant_row -> gemm_i8, K=2048, N=12288",
+    return {"workload": "config 3: W8A8 prefill, X bf16 -> quant_row -> gemm_i8, K=2048, N=12288; "
+                        "W4 g128 variant (gemm_w4) at the same shape",
             "int8_peak_tops": int8_peak, "int8_peak_kind": "2 x measured bf16 GEMM peak", "per_M": out}
 
 
