@@ -535,7 +535,36 @@ int run_tc(int wb, int epi, GemvArgs& a, int tiles, cudaStream_t st) {
 }
 
 // ---------------------------------------------------------------- tensor-core GEMM (large M)
-int run_prefill_w8(const GemvArgs& a, int half_tiles, cudaStream_t st) {
+template <int EPI>
+int launch_prefill_w8(const GemmArgs& g, int grid, cudaStream_t st) {
+  auto kern = tc_gemm_kernel<EPI>;
+  static std::atomic<unsigned long long> configured{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(configured.load() & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kGmSmem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc_gemm smem)");
+    configured.fetch_or(bit);
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(kGmThreads, 1, 1);
+  cfg.dynamicSmemBytes = kGmSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = tune_pdl() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, g);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(tc_gemm)");
+  return QLIN_OK;
+}
+
+// epi: kEpiOut (gemm / proj3 segments) or the fused gate/up epilogues, whose
+// two segments are gate and up with the same N.
+int run_prefill_w8(int epi, const GemvArgs& a, int half_tiles, cudaStream_t st) {
   DevInfo di;
   if (int r = device_info(&di)) return r;
   GemmArgs g;
@@ -559,34 +588,48 @@ int run_prefill_w8(const GemvArgs& a, int half_tiles, cudaStream_t st) {
   g.res = a.res;
   g.ldr = a.ldr;
   g.vec_out = vec ? 1 : 0;
+  g.out_q = a.out_q;
+  g.out_s = a.out_s;
+  g.n_q = a.n_q;
   g.fault = di.fault;
-  const long long tiles = static_cast<long long>((a.M + kGmRows - 1) / kGmRows) * ((half_tiles + 1) / 2);
+  if (epi != kEpiOut) g.half_tiles = 2 * half_tiles;  // (gate tile, up tile) pairs
+  const long long tiles = static_cast<long long>((a.M + kGmRows - 1) / kGmRows) * ((g.half_tiles + 1) / 2);
   const int grid = static_cast<int>(tiles < di.sms ? tiles : di.sms);
+  switch (epi) {
+    case kEpiOut: return launch_prefill_w8<kEpiOut>(g, grid, st);
+    case kEpiSiluBf16: return launch_prefill_w8<kEpiSiluBf16>(g, grid, st);
+    default: return launch_prefill_w8<kEpiSiluQuant>(g, grid, st);
+  }
+}
+
+template <int EPI>
+int launch_prefill_w4(const GemmW4Args& g, int grid, cudaStream_t st) {
+  auto kern = tc_gemm_w4_kernel<EPI>;
   static std::atomic<unsigned long long> configured{0};
   int dev = 0;
   cudaGetDevice(&dev);
   const unsigned long long bit = 1ull << (dev & 63);
   if (!(configured.load() & bit)) {
-    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGmSmem);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc_gemm smem)");
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kG4Smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc_gemm_w4 smem)");
     configured.fetch_or(bit);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
-  cfg.blockDim = dim3(kGmThreads, 1, 1);
-  cfg.dynamicSmemBytes = kGmSmem;
+  cfg.blockDim = dim3(kG4Threads, 1, 1);
+  cfg.dynamicSmemBytes = kG4Smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = tune_pdl() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel, g);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(tc_gemm)");
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, g);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(tc_gemm_w4)");
   return QLIN_OK;
 }
 
-int run_prefill_w4(const GemvArgs& a, int half_tiles, cudaStream_t st) {
+int run_prefill_w4(int epi, const GemvArgs& a, int half_tiles, cudaStream_t st) {
   DevInfo di;
   if (int r = device_info(&di)) return r;
   GemmW4Args g;
@@ -618,38 +661,20 @@ int run_prefill_w4(const GemvArgs& a, int half_tiles, cudaStream_t st) {
   g.res = a.res;
   g.ldr = a.ldr;
   g.vec_out = vec ? 1 : 0;
+  g.out_q = a.out_q;
+  g.out_s = a.out_s;
+  g.n_q = a.n_q;
   g.fault = di.fault;
-  const long long tiles = static_cast<long long>((a.M + kGmRows - 1) / kGmRows) * ((half_tiles + 1) / 2);
+  if (epi != kEpiOut) g.half_tiles = 2 * half_tiles;  // (gate tile, up tile) pairs
+  const long long tiles = static_cast<long long>((a.M + kGmRows - 1) / kGmRows) * ((g.half_tiles + 1) / 2);
   const int grid = static_cast<int>(tiles < di.sms ? tiles : di.sms);
-  static std::atomic<unsigned long long> configured{0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const unsigned long long bit = 1ull << (dev & 63);
-  if (!(configured.load() & bit)) {
-    cudaError_t e = cudaFuncSetAttribute(tc_gemm_w4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kG4Smem);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc_gemm_w4 smem)");
-    configured.fetch_or(bit);
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid, 1, 1);
-  cfg.blockDim = dim3(kG4Threads, 1, 1);
-  cfg.dynamicSmemBytes = kG4Smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = tune_pdl() ? 1 : 0;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_w4_kernel, g);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(tc_gemm_w4)");
-  return QLIN_OK;
+  return epi == kEpiOut ? launch_prefill_w4<kEpiOut>(g, grid, st) : launch_prefill_w4<kEpiSiluQuant>(g, grid, st);
 }
 
 // Fills the split / ring fields of `a`, then launches.
 int run_gemv(int wb, int epi, GemvArgs& a, int tiles, cudaStream_t st) {
-  if (wb == 8 && epi == kEpiOut && use_tc() && a.M >= prefill_min_m()) return run_prefill_w8(a, tiles, st);
-  if (wb == 4 && epi == kEpiOut && use_tc() && a.M >= prefill_min_m() && a.wgrp % 64 == 0)
-    return run_prefill_w4(a, tiles, st);
+  if (wb == 8 && use_tc() && a.M >= prefill_min_m()) return run_prefill_w8(epi, a, tiles, st);
+  if (wb == 4 && use_tc() && a.M >= prefill_min_m() && a.wgrp % 64 == 0) return run_prefill_w4(epi, a, tiles, st);
   if (use_tc()) return run_tc(wb, epi, a, tiles, st);
   DevInfo di;
   if (int r = device_info(&di)) return r;

@@ -7,7 +7,9 @@
 // Tile: 128 activation rows (MMA M = tensor-memory lanes, one row per
 // epilogue thread) x 256 output columns, issued as two 128-column halves
 // (N = 128 each).  Each half is one 128-column tile of a column segment, so
-// proj3's segments (kernels/gemm.py:234-287) need no special case.  A stage
+// proj3's segments (kernels/gemm.py:234-287) need no special case; the fused
+// gate/up (kernels/gemm.py:95-231) pairs the gate and up tiles of the same
+// columns, and each epilogue thread holds 64 columns of both halves.  A stage
 // holds 128 K (two groups): the activation box (K-major, 128-byte swizzle)
 // and one weight box per half (the engine's [K, N] rows are MN-major for
 // the MMA, 128-byte swizzle).
@@ -56,6 +58,9 @@ struct GemmArgs {
   const void* res;    // bf16 residual or null, row stride ldr
   long long ldr;
   int vec_out;        // 16-byte vector stores / residual loads are aligned
+  int8_t* out_q;      // kEpiSiluQuant: int8 [M, n_q]
+  float* out_s;       // kEpiSiluQuant: fp32 [M, n_q / 64]
+  int n_q;
   unsigned* fault;
 };
 
@@ -66,6 +71,87 @@ __device__ __forceinline__ int gm_seg_of(const GemmArgs& p, int ht) {
   return si;
 }
 
+// Half h of column pair pt: plain projections walk the 128-column tiles of
+// their segments two at a time; the fused gate/up pairs gate tile pt (seg 0)
+// with up tile pt (seg 1), so one thread can hold both for the same columns.
+template <int EPI, class Args>
+__device__ __forceinline__ bool gm_half(const Args& p, int pt, int h, int& si, int& n0) {
+  if (EPI == kEpiOut) {
+    const int ht = 2 * pt + h;
+    if (ht >= p.half_tiles) return false;
+    int s = 0;
+    if (p.nseg > 1 && ht >= p.seg[1].tile_begin) s = 1;
+    if (p.nseg > 2 && ht >= p.seg[2].tile_begin) s = 2;
+    si = s;
+    n0 = (ht - p.seg[s].tile_begin) * kTileN;
+    return true;
+  }
+  si = h;
+  n0 = pt * kTileN;
+  return true;
+}
+
+// Fused gate/up epilogue of one row m and the 64 columns [nb, nb + 64): acc
+// entries 0..31 hold the gate sums, 32..63 the up sums (two columns each).
+// W8 passes its per-column scales (g = acc * sg, u = acc * su,
+// kernels/gemm.py:180-197); W4 applied its scales inside the K loop.
+//   kEpiSiluBf16:  out[m, n] = bf16(silu(g) * u)
+//   kEpiSiluQuant: h = bf16(silu(g) * u); s = max(amax|h| / 127, 1e-8);
+//                  q = round_half_away(h / s)   (kernels/gemm.py:198-211)
+// The 64 columns are one quantisation group, so the amax stays in-thread.
+template <int EPI, class Args>
+__device__ __forceinline__ void gm_gate_up_epilogue(const Args& p, int m, int nb, const float2 (&acc)[64],
+                                                    const float* sg, const float* su) {
+  const int N = p.seg[0].n;
+  if (nb >= N) return;
+  float hv[64];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int n = nb + 2 * j + e;
+      float g = e ? acc[j].y : acc[j].x;
+      float u = e ? acc[32 + j].y : acc[32 + j].x;
+      if (sg != nullptr && n < N) {
+        g = __fmul_rn(g, __ldg(sg + n));
+        u = __fmul_rn(u, __ldg(su + n));
+      }
+      hv[2 * j + e] = __fmul_rn(silu_ref(g), u);
+    }
+  }
+  if constexpr (EPI == kEpiSiluBf16) {
+    __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<long long>(m) * p.ldo;
+#pragma unroll
+    for (int c8 = 0; c8 < 8; ++c8) {
+      const int n = nb + 8 * c8;
+      if (n >= N) continue;  // N % 16 == 0
+      if (p.vec_out) {
+        uint4 ov;
+        __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&ov);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ob[e] = __float2bfloat16_rn(hv[8 * c8 + e]);
+        *reinterpret_cast<uint4*>(orow + n) = ov;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) orow[n + e] = __float2bfloat16_rn(hv[8 * c8 + e]);
+      }
+    }
+  } else {
+    float amax = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 64; ++e) {
+      hv[e] = bf16_round_f32(hv[e]);
+      amax = fmaxf(amax, fabsf(hv[e]));
+    }
+    const float sc = fmaxf(__fdiv_rn(amax, 127.0f), 1e-8f);
+    int8_t* qrow = p.out_q + static_cast<long long>(m) * p.n_q + nb;
+#pragma unroll
+    for (int e = 0; e < 64; ++e) qrow[e] = round_i8(__fdiv_rn(hv[e], sc));
+    p.out_s[static_cast<long long>(m) * (p.n_q / 64) + nb / 64] = sc;
+  }
+}
+
+template <int EPI>
 __global__ void __launch_bounds__(kGmThreads, 1) tc_gemm_kernel(const __grid_constant__ GemmArgs p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -127,11 +213,9 @@ __global__ void __launch_bounds__(kGmThreads, 1) tc_gemm_kernel(const __grid_con
           mbar_arrive_expect_tx(full + slot, bytes);
           tma_load_2d(sa, &p.ta, st * 128, m0, full + slot, pol_a);
           for (int h = 0; h < 2; ++h) {
-            const int ht = 2 * pt + h;
-            if (ht >= p.half_tiles) continue;
-            const GemvSeg& sg = p.seg[gm_seg_of(p, ht)];
-            tma_load_2d(sa + kGmStageA + h * kGmStageB, &sg.tw, (ht - sg.tile_begin) * kTileN, st * 128,
-                        full + slot, pol_b);
+            int si, n0;
+            if (!gm_half<EPI>(p, pt, h, si, n0)) continue;
+            tma_load_2d(sa + kGmStageA + h * kGmStageB, &p.seg[si].tw, n0, st * 128, full + slot, pol_b);
           }
         }
         __syncwarp();
@@ -180,14 +264,20 @@ __global__ void __launch_bounds__(kGmThreads, 1) tc_gemm_kernel(const __grid_con
     if (!ok && lane == 0) atomicOr(p.fault, kFaultMmaWait);
   } else {
     // ------------------------------------------------------------------ epilogue
-    const int q = warp & 3;         // TMEM lane quarter = rows 32q .. 32q+31
-    const int h = (warp - 2) >> 2;  // column half
-    const uint32_t lane_base = tbase + (static_cast<uint32_t>(32 * q) << 16) + h * 128;
+    // Thread = one row (TMEM lane) x the 64 columns [64c2, 64c2 + 64) of BOTH
+    // halves: for the fused gate/up that is the gate and the up value of the
+    // same 64 output columns -- one quantisation group, reduced in-thread.
+    const int q = warp & 3;          // TMEM lane quarter = rows 32q .. 32q+31
+    const int c2 = (warp - 2) >> 2;  // which 64 columns of each half
+    const uint32_t lane_base = tbase + (static_cast<uint32_t>(32 * q) << 16) + c2 * 64;
     // Arm both buffers with the magic bits.
 #pragma unroll
     for (int b = 0; b < 2; ++b)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_fill32(lane_base + b * 256 + 32 * c, kGmMagic);
+      for (int hh = 0; hh < 2; ++hh) {
+        tmem_fill32(lane_base + b * 256 + hh * 128, kGmMagic);
+        tmem_fill32(lane_base + b * 256 + hh * 128 + 32, kGmMagic);
+      }
     tc_wait_st();
     tc_fence_before();
     mbar_arrive(tempty + 0);
@@ -198,11 +288,11 @@ __global__ void __launch_bounds__(kGmThreads, 1) tc_gemm_kernel(const __grid_con
     const float2 neg_magic = make_float2(-12582912.0f, -12582912.0f);
     for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
       const int m0 = (t % mtiles) * kGmRows;
-      const int ht = 2 * (t / mtiles) + h;
+      const int pt = t / mtiles;
       const int m = m0 + 32 * q + lane;
       const bool mvalid = m < p.M;
       const float* asrow = p.a_s + static_cast<long long>(mvalid ? m : 0) * G;
-      float2 acc[64];
+      float2 acc[64];  // [0, 32): half 0 columns, [32, 64): half 1 columns, two per entry
 #pragma unroll
       for (int j = 0; j < 64; ++j) acc[j] = make_float2(0.0f, 0.0f);
       float s_next = mvalid ? __ldg(asrow) : 0.0f;
@@ -216,61 +306,71 @@ __global__ void __launch_bounds__(kGmThreads, 1) tc_gemm_kernel(const __grid_con
         const float2 s2 = make_float2(s, s);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
+          const uint32_t col = b * 256 + (c >> 2) * 128 + 16 * (c & 3);
           uint32_t r[16];
-          tmem_ld32<16>(lane_base + b * 256 + 16 * c, r);
+          tmem_ld32<16>(lane_base + col, r);
           tc_wait_ld();
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const float2 v = f2_add(make_float2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])), neg_magic);
             acc[8 * c + j] = f2_fma(v, s2, acc[8 * c + j]);
           }
-          if (c & 1) tmem_fill32(lane_base + b * 256 + 16 * (c - 1), kGmMagic);  // re-arm the 32 columns just read
+          if (c & 1) tmem_fill32(lane_base + col - 16, kGmMagic);  // re-arm the 32 columns just read
         }
         tc_wait_st();
         tc_fence_before();
         mbar_arrive(tempty + b);
       }
       if (!ok) break;
+      if (!mvalid) continue;
       // ---------------------------------------------------------------- tile epilogue
-      if (ht >= p.half_tiles || !mvalid) continue;
-      const GemvSeg& sg = p.seg[gm_seg_of(p, ht)];
-      const int n0 = (ht - sg.tile_begin) * kTileN;
-      __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<long long>(m) * p.ldo + sg.out_col;
-      const __nv_bfloat16* rrow =
-          p.res ? reinterpret_cast<const __nv_bfloat16*>(p.res) + static_cast<long long>(m) * p.ldr + sg.out_col
-                : nullptr;
+      if constexpr (EPI == kEpiOut) {
 #pragma unroll
-      for (int c8 = 0; c8 < 16; ++c8) {
-        const int n = n0 + 8 * c8;
-        if (n >= sg.n) continue;  // N % 16 == 0: a chunk of 8 is all in or all out
-        float v[8];
-        // out * b_s (kernels/gemm.py:51-52); every lane of the warp reads the same scales
+        for (int hh = 0; hh < 2; ++hh) {
+          int si, n0;
+          if (!gm_half<EPI>(p, pt, hh, si, n0)) continue;
+          const GemvSeg& sg = p.seg[si];
+          __nv_bfloat16* orow =
+              reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<long long>(m) * p.ldo + sg.out_col;
+          const __nv_bfloat16* rrow =
+              p.res ? reinterpret_cast<const __nv_bfloat16*>(p.res) + static_cast<long long>(m) * p.ldr + sg.out_col
+                    : nullptr;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          v[2 * e] = __fmul_rn(acc[4 * c8 + e].x, __ldg(sg.bs + n + 2 * e));
-          v[2 * e + 1] = __fmul_rn(acc[4 * c8 + e].y, __ldg(sg.bs + n + 2 * e + 1));
-        }
-        if (rrow) {
-          if (p.vec_out) {
-            const uint4 rv = *reinterpret_cast<const uint4*>(rrow + n);
-            const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rv);
+          for (int c8 = 0; c8 < 8; ++c8) {
+            const int n = n0 + c2 * 64 + 8 * c8;
+            if (n >= sg.n) continue;  // N % 16 == 0: a chunk of 8 is all in or all out
+            float v[8];
+            // out * b_s (kernels/gemm.py:51-52); every lane of the warp reads the same scales
 #pragma unroll
-            for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(v[e], __bfloat162float(rb[e]));
-          } else {
+            for (int e = 0; e < 4; ++e) {
+              v[2 * e] = __fmul_rn(acc[32 * hh + 4 * c8 + e].x, __ldg(sg.bs + n + 2 * e));
+              v[2 * e + 1] = __fmul_rn(acc[32 * hh + 4 * c8 + e].y, __ldg(sg.bs + n + 2 * e + 1));
+            }
+            if (rrow) {
+              if (p.vec_out) {
+                const uint4 rv = *reinterpret_cast<const uint4*>(rrow + n);
+                const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rv);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(v[e], __bfloat162float(rrow[n + e]));
+                for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(v[e], __bfloat162float(rb[e]));
+              } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(v[e], __bfloat162float(rrow[n + e]));
+              }
+            }
+            if (p.vec_out) {
+              uint4 ov;
+              __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&ov);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) ob[e] = __float2bfloat16_rn(v[e]);
+              *reinterpret_cast<uint4*>(orow + n) = ov;
+            } else {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) orow[n + e] = __float2bfloat16_rn(v[e]);
+            }
           }
         }
-        if (p.vec_out) {
-          uint4 ov;
-          __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&ov);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) ob[e] = __float2bfloat16_rn(v[e]);
-          *reinterpret_cast<uint4*>(orow + n) = ov;
-        } else {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) orow[n + e] = __float2bfloat16_rn(v[e]);
-        }
+      } else {
+        gm_gate_up_epilogue<EPI>(p, m, pt * kTileN + c2 * 64, acc, p.seg[0].bs, p.seg[1].bs);
       }
     }
     if (!ok && lane == 0) atomicOr(p.fault, kFaultFullWait);

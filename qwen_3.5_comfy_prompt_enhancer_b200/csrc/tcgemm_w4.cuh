@@ -60,6 +60,9 @@ struct GemmW4Args {
   const void* res;
   long long ldr;
   int vec_out;
+  int8_t* out_q;      // kEpiSiluQuant: int8 [M, n_q]
+  float* out_s;       // kEpiSiluQuant: fp32 [M, n_q / 64]
+  int n_q;
   unsigned* fault;
 };
 
@@ -76,13 +79,7 @@ __device__ __forceinline__ float2 f2_mul(float2 a, float2 b) {
   return d;
 }
 
-__device__ __forceinline__ int g4_seg_of(const GemmW4Args& p, int ht) {
-  int si = 0;
-  if (p.nseg > 1 && ht >= p.seg[1].tile_begin) si = 1;
-  if (p.nseg > 2 && ht >= p.seg[2].tile_begin) si = 2;
-  return si;
-}
-
+template <int EPI>
 __global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_constant__ GemmW4Args p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -148,18 +145,17 @@ __global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_
           uint8_t* sa = smem + kG4RawOff + slot * kG4StageAligned;
           uint32_t bytes = kG4A;
           for (int h = 0; h < 2; ++h) {
-            const int ht = 2 * pt + h;
-            if (ht >= p.half_tiles) continue;
-            bytes += kG4Packed + nsr * 128 * 2 + (p.seg[g4_seg_of(p, ht)].has_z ? nsr * 128 : 0);
+            int si, n0;
+            if (!gm_half<EPI>(p, pt, h, si, n0)) continue;
+            bytes += kG4Packed + nsr * 128 * 2 + (p.seg[si].has_z ? nsr * 128 : 0);
           }
           mbar_arrive_expect_tx(full + slot, bytes);
           tma_load_2d(sa, &p.ta, st * 128, m0, full + slot, pol);
           const int srow = (st * 128) / p.wgrp;
           for (int h = 0; h < 2; ++h) {
-            const int ht = 2 * pt + h;
-            if (ht >= p.half_tiles) continue;
-            const GemvSeg& sg = p.seg[g4_seg_of(p, ht)];
-            const int n0 = (ht - sg.tile_begin) * kTileN;
+            int si, n0;
+            if (!gm_half<EPI>(p, pt, h, si, n0)) continue;
+            const GemvSeg& sg = p.seg[si];
             uint8_t* raw = sa + kG4A + h * kG4Half;
             tma_load_2d(raw, &sg.tw, n0, st * 64, full + slot, pol);
             tma_load_2d(raw + kG4Packed, &sg.ts, n0, srow, full + slot, pol);
@@ -192,10 +188,11 @@ __global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_
         const int k0 = st * 128;
         const int srow = k0 / p.wgrp;
         for (int h = 0; h < 2; ++h) {
-          const int ht = 2 * pt + h;
+          int si = 0, n0 = 0;
+          const bool valid = gm_half<EPI>(p, pt, h, si, n0);
           const uint8_t* raw = smem + kG4RawOff + slot * kG4StageAligned + kG4A + h * kG4Half;
           uint8_t* ut = smem + kG4UOff + ub * kG4UStage + h * kG4UTile;
-          const bool has_z = ht < p.half_tiles && p.seg[g4_seg_of(p, ht)].has_z;
+          const bool has_z = valid && p.seg[si].has_z;
           // 64 packed rows x 8 chunks of 16 columns; packed row j holds K = 2j
           // (low nibble) and 2j + 1 (high nibble) of 16 columns.
 #pragma unroll 2
@@ -272,13 +269,18 @@ __global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_
     if (!ok && lane == 0) atomicOr(p.fault, kFaultMmaWait);
   } else {
     // ------------------------------------------------------------------ epilogue (warps 2-9)
-    const int q = warp & 3;         // TMEM lane quarter = rows 32q .. 32q+31
-    const int h = (warp - 2) >> 2;  // column half
-    const uint32_t lane_base = tbase + (static_cast<uint32_t>(32 * q) << 16) + h * 128;
+    // Thread = one row (TMEM lane) x the 64 columns [64c2, 64c2 + 64) of both
+    // halves (gate and up of the same columns for the fused epilogue).
+    const int q = warp & 3;          // TMEM lane quarter = rows 32q .. 32q+31
+    const int c2 = (warp - 2) >> 2;  // which 64 columns of each half
+    const uint32_t lane_base = tbase + (static_cast<uint32_t>(32 * q) << 16) + c2 * 64;
 #pragma unroll
     for (int b = 0; b < 2; ++b)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_fill32(lane_base + b * 256 + 32 * c, kGmMagic);
+      for (int hh = 0; hh < 2; ++hh) {
+        tmem_fill32(lane_base + b * 256 + hh * 128, kGmMagic);
+        tmem_fill32(lane_base + b * 256 + hh * 128 + 32, kGmMagic);
+      }
     tc_wait_st();
     tc_fence_before();
     mbar_arrive(tempty + 0);
@@ -289,11 +291,11 @@ __global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_
     const float2 neg_magic = make_float2(-12582912.0f, -12582912.0f);
     for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
       const int m0 = (t % mtiles) * kGmRows;
-      const int ht = 2 * (t / mtiles) + h;
+      const int pt = t / mtiles;
       const int m = m0 + 32 * q + lane;
       const bool mvalid = m < p.M;
       const float* asrow = p.a_s + static_cast<long long>(mvalid ? m : 0) * G;
-      float2 acc[64];
+      float2 acc[64];  // [0, 32): half 0 columns, [32, 64): half 1 columns, two per entry
 #pragma unroll
       for (int j = 0; j < 64; ++j) acc[j] = make_float2(0.0f, 0.0f);
       float s_next = mvalid ? __ldg(asrow) : 0.0f;
@@ -305,66 +307,77 @@ __global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_
         if (!ok) break;
         tc_fence_after();
         const float2 as2 = make_float2(as, as);
-        const float* wsg = sring + ((gc % kG4ScaleSlots) * 2 + h) * 128;
+        const float* wsg = sring + (gc % kG4ScaleSlots) * 2 * 128 + c2 * 64;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
+          const int hh = c >> 2;
+          const uint32_t col = b * 256 + hh * 128 + 16 * (c & 3);
           uint32_t r[16];
-          tmem_ld32<16>(lane_base + b * 256 + 16 * c, r);
+          tmem_ld32<16>(lane_base + col, r);
           tc_wait_ld();
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             // (a_s * ws) first, then the int32 sum times that (kernels/w4.py:103-104)
-            const float2 ws = *reinterpret_cast<const float2*>(wsg + 16 * c + 2 * j);
+            const float2 ws = *reinterpret_cast<const float2*>(wsg + hh * 128 + 16 * (c & 3) + 2 * j);
             const float2 t2 = f2_mul(as2, ws);
             const float2 v = f2_add(make_float2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])), neg_magic);
             acc[8 * c + j] = f2_fma(v, t2, acc[8 * c + j]);
           }
-          if (c & 1) tmem_fill32(lane_base + b * 256 + 16 * (c - 1), kGmMagic);
+          if (c & 1) tmem_fill32(lane_base + col - 16, kGmMagic);
         }
         tc_wait_st();
         tc_fence_before();
         mbar_arrive(tempty + b);
       }
       if (!ok) break;
+      if (!mvalid) continue;
       // ---------------------------------------------------------------- tile epilogue
-      if (ht >= p.half_tiles || !mvalid) continue;
-      const GemvSeg& sg = p.seg[g4_seg_of(p, ht)];
-      const int n0 = (ht - sg.tile_begin) * kTileN;
-      __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<long long>(m) * p.ldo + sg.out_col;
-      const __nv_bfloat16* rrow =
-          p.res ? reinterpret_cast<const __nv_bfloat16*>(p.res) + static_cast<long long>(m) * p.ldr + sg.out_col
-                : nullptr;
+      if constexpr (EPI == kEpiOut) {
 #pragma unroll
-      for (int c8 = 0; c8 < 16; ++c8) {
-        const int n = n0 + 8 * c8;
-        if (n >= sg.n) continue;  // N % 16 == 0: a chunk of 8 is all in or all out
-        float v[8];
+        for (int hh = 0; hh < 2; ++hh) {
+          int si, n0;
+          if (!gm_half<EPI>(p, pt, hh, si, n0)) continue;
+          const GemvSeg& sg = p.seg[si];
+          __nv_bfloat16* orow =
+              reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<long long>(m) * p.ldo + sg.out_col;
+          const __nv_bfloat16* rrow =
+              p.res ? reinterpret_cast<const __nv_bfloat16*>(p.res) + static_cast<long long>(m) * p.ldr + sg.out_col
+                    : nullptr;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          v[2 * e] = acc[4 * c8 + e].x;
-          v[2 * e + 1] = acc[4 * c8 + e].y;
-        }
-        if (rrow) {
-          if (p.vec_out) {
-            const uint4 rv = *reinterpret_cast<const uint4*>(rrow + n);
-            const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rv);
+          for (int c8 = 0; c8 < 8; ++c8) {
+            const int n = n0 + c2 * 64 + 8 * c8;
+            if (n >= sg.n) continue;  // N % 16 == 0: a chunk of 8 is all in or all out
+            float v[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(v[e], __bfloat162float(rb[e]));
-          } else {
+            for (int e = 0; e < 4; ++e) {
+              v[2 * e] = acc[32 * hh + 4 * c8 + e].x;
+              v[2 * e + 1] = acc[32 * hh + 4 * c8 + e].y;
+            }
+            if (rrow) {
+              if (p.vec_out) {
+                const uint4 rv = *reinterpret_cast<const uint4*>(rrow + n);
+                const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rv);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(v[e], __bfloat162float(rrow[n + e]));
+                for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(v[e], __bfloat162float(rb[e]));
+              } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(v[e], __bfloat162float(rrow[n + e]));
+              }
+            }
+            if (p.vec_out) {
+              uint4 ov;
+              __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&ov);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) ob[e] = __float2bfloat16_rn(v[e]);
+              *reinterpret_cast<uint4*>(orow + n) = ov;
+            } else {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) orow[n + e] = __float2bfloat16_rn(v[e]);
+            }
           }
         }
-        if (p.vec_out) {
-          uint4 ov;
-          __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&ov);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) ob[e] = __float2bfloat16_rn(v[e]);
-          *reinterpret_cast<uint4*>(orow + n) = ov;
-        } else {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) orow[n + e] = __float2bfloat16_rn(v[e]);
-        }
+      } else {
+        gm_gate_up_epilogue<EPI>(p, m, pt * kTileN + c2 * 64, acc, nullptr, nullptr);
       }
     }
     if (!ok && lane == 0) atomicOr(p.fault, kFaultFullWait);

@@ -185,3 +185,48 @@ def test_config3_prefill_w4_variant(pkg, dev):
     rows = np.sort(np.random.default_rng(7).choice(M, 64, replace=False))
     ref = O.gemm_w4(a.numpy()[rows], s.numpy()[rows], b.numpy(), bits(sc), z.numpy())
     assert_bf16_close(bits(out)[rows], ref, "config 3 W4")
+
+
+# ----------------------------------------------------------------------------- fused gate/up at M >= 128
+from qlin_testutil import assert_quant_close  # noqa: E402
+
+
+@pytest.mark.parametrize("M,K,N", [(128, 1024, 384), (300, 2048, 1024)])
+def test_prefill_gate_up_quant_w8(pkg, dev, M, K, N):
+    g = gen(7100 + M)
+    a, s = acts_x(g, M, K)
+    wg, sg = w8(g, K, N, "lognormal")
+    wu, su = w8(g, K, N, "lognormal")
+    q = torch.empty(M, N, dtype=torch.int8, device=dev)
+    qs = torch.empty(M, N // 64, dtype=torch.float32, device=dev)
+    pkg.mlp_gate_up_quant(cu(a), cu(s), cu(wg), cu(sg), cu(wu), cu(su), q, qs)
+    rq, rs = O.mlp_gate_up_quant(a.numpy(), s.numpy(), wg.numpy(), sg.numpy(), wu.numpy(), su.numpy())
+    assert_quant_close(q.cpu().numpy(), qs.cpu().numpy(), rq, rs, f"prefill gate_up_quant W8 M={M}")
+
+
+@pytest.mark.parametrize("M,N", [(128, 400), (257, 512)])
+def test_prefill_gate_up_bf16_w8(pkg, dev, M, N):
+    K = 1024
+    g = gen(7200 + M)
+    a, s = acts_x(g, M, K)
+    wg, sg = w8(g, K, N, "lognormal")
+    wu, su = w8(g, K, N, "lognormal")
+    out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    pkg.mlp_gate_up(cu(a), cu(s), cu(wg), cu(sg), cu(wu), cu(su), out)
+    ref = O.mlp_gate_up(a.numpy(), s.numpy(), wg.numpy(), sg.numpy(), wu.numpy(), su.numpy())
+    assert_bf16_close(bits(out), ref, f"prefill gate_up bf16 M={M} N={N}")
+
+
+@pytest.mark.parametrize("M,wg,zeros", [(128, 128, True), (300, 64, False), (200, 256, True)])
+def test_prefill_gate_up_quant_w4(pkg, dev, M, wg, zeros):
+    K, N = 1024, 512
+    g = gen(7300 + M + wg)
+    a, s = acts_x(g, M, K)
+    gw, gs, gz = w4(g, K, N, wg, zeros)
+    uw, us, uz = w4(g, K, N, wg, zeros)
+    q = torch.empty(M, N, dtype=torch.int8, device=dev)
+    qs = torch.empty(M, N // 64, dtype=torch.float32, device=dev)
+    pkg.mlp_gate_up_quant_w4(cu(a), cu(s), cu(gw), cu(gs), cu(uw), cu(us), q, qs, zg=cu(gz), zu=cu(uz))
+    rq, rs = O.mlp_gate_up_quant_w4(a.numpy(), s.numpy(), gw.numpy(), bits(gs), uw.numpy(), bits(us),
+                                    None if gz is None else gz.numpy(), None if uz is None else uz.numpy())
+    assert_quant_close(q.cpu().numpy(), qs.cpu().numpy(), rq, rs, f"prefill gate_up_quant W4 M={M} wg={wg}")
