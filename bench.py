@@ -308,8 +308,13 @@ def tp_detail(pkg, dev, world, pg, reps=20):
         del graph
         us = times[1]
         res[f"M{M}"] = {"us": us, "eager_us": times[0], "weight_tbs": tp_layer_bytes() / us / 1e6}
+    gather = layer.gather
+    if pg:
+        pg.barrier()
+    layer.close()
     return {"workload": "config 5: W4 g128 gate_up 5120->2x17408 (fused SiLU+requant) + down 17408->5120, "
-                        "columns split over ranks, NCCL all-gather of h and of the output",
+                        "columns split over ranks, all-gather of h and of the output",
+            "gather": "NVLink peer-memory stores (own kernel)" if gather == "peer" else "torch.distributed",
             "n_gpus": world, "scaling": "strong", "layer_weight_bytes": tp_layer_bytes(), "per_M": res}
 
 

@@ -129,6 +129,37 @@ int qlin_mlp_gate_up_quant_w4(const int8_t* a_q, const float* a_s, int64_t M, in
 int qlin_quant_row(const void* x, int64_t ldx, int64_t M, int64_t K,
                    int8_t* q, float* s, void* stream);
 
+/* ---- Multi-GPU (column-split layer): NVLink peer memory through CUDA IPC ----
+ * Not part of the reference's interface (it has no multi-GPU path); used by
+ * the package's tp.py for its all-gathers. */
+#define QLIN_IPC_HANDLE_BYTES 64
+
+/* IPC handle (QLIN_IPC_HANDLE_BYTES bytes) of the allocation holding device
+ * pointer `ptr`, and the byte offset of `ptr` inside it. */
+int qlin_ipc_get_handle(const void* ptr, void* handle, int64_t* offset);
+
+/* Opens a peer's handle in this process; *ptr = mapped base + offset. */
+int qlin_ipc_open(const void* handle, int64_t offset, void** ptr);
+
+/* Closes a mapping opened by qlin_ipc_open (same ptr and offset). */
+int qlin_ipc_close(void* ptr, int64_t offset);
+
+/* Zero-filled device allocation of its own (one IPC handle per buffer). */
+int qlin_dev_alloc(int64_t bytes, void** ptr);
+int qlin_dev_free(void* ptr);
+
+/* All-gather of `shard_bytes` (multiple of 16) from `src` into slot `rank` of
+ * every rank's buffer bufs[q] (world x shard_bytes bytes each), then waits
+ * until every rank's shard has landed in bufs[rank]; if `dst` is not null the
+ * gathered world x shard_bytes bytes are then copied there on the same
+ * stream.  arrive[q] is rank q's array of `world` uint32 arrival counters
+ * (zero-initialised once, never reset); `expected` is this rank's device
+ * array of `world` uint32 (zero once).  Every rank must call it with the same
+ * shard_bytes.  A wait that does not finish within 2 s sets the device fault
+ * word. */
+int qlin_peer_allgather(void* const* bufs, void* const* arrive, void* expected, const void* src,
+                        int64_t shard_bytes, int world, int rank, void* dst, void* stream);
+
 /* Diagnostic (no GPU needed, nothing launched): the launch plan of the
  * small-M weight-streaming kernel for wbits 8 or 4, `gate_up` 0 (one output
  * stream: gemm / proj3) or 1 (fused gate/up), M rows, K, `tiles` 128-column

@@ -14,6 +14,7 @@
 #include "../../include/qlin.h"
 #include "gemv.cuh"
 #include "quant.cuh"
+#include "peer.cuh"
 #include "tcgemm.cuh"
 #include "tcgemm_w4.cuh"
 #include "tcgemv.cuh"
@@ -86,6 +87,26 @@ int encode_fn(PFN_cuTensorMapEncodeTiled_v12000* fn) {
   });
   if (!g_encode) return fail(QLIN_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
   *fn = g_encode;
+  return QLIN_OK;
+}
+
+// cuMemGetAddressRange through the runtime's driver entry point (the base of
+// the allocation that holds a pointer, for CUDA IPC offsets).
+typedef CUresult (*PfnAddressRange)(CUdeviceptr*, size_t*, CUdeviceptr);
+std::once_flag g_range_once;
+PfnAddressRange g_range = nullptr;
+int address_range(const void* p, CUdeviceptr* base) {
+  std::call_once(g_range_once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_range = reinterpret_cast<PfnAddressRange>(f);
+  });
+  if (!g_range) return fail(QLIN_ERR_CUDA, "cuMemGetAddressRange entry point unavailable");
+  size_t size = 0;
+  if (g_range(base, &size, reinterpret_cast<CUdeviceptr>(p)) != CUDA_SUCCESS)
+    return fail(QLIN_ERR_INVALID_ARGUMENT, "pointer is not a device allocation");
   return QLIN_OK;
 }
 
@@ -784,6 +805,93 @@ const char* qlin_status_string(int s) {
 }
 
 const char* qlin_last_error(void) { return g_err; }
+
+int qlin_ipc_get_handle(const void* ptr, void* handle, int64_t* offset) {
+  if (!ptr || !handle || !offset) return fail(QLIN_ERR_INVALID_ARGUMENT, "null argument");
+  CUdeviceptr base = 0;
+  if (int r = address_range(ptr, &base)) return r;
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  static_assert(sizeof(h) == QLIN_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle, &h, sizeof(h));
+  *offset = static_cast<int64_t>(reinterpret_cast<uintptr_t>(ptr) - static_cast<uintptr_t>(base));
+  return QLIN_OK;
+}
+
+int qlin_ipc_open(const void* handle, int64_t offset, void** ptr) {
+  if (!handle || !ptr || offset < 0) return fail(QLIN_ERR_INVALID_ARGUMENT, "bad IPC open arguments");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  *ptr = static_cast<uint8_t*>(base) + offset;
+  return QLIN_OK;
+}
+
+int qlin_ipc_close(void* ptr, int64_t offset) {
+  if (!ptr) return QLIN_OK;
+  cudaError_t e = cudaIpcCloseMemHandle(static_cast<uint8_t*>(ptr) - offset);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcCloseMemHandle");
+  return QLIN_OK;
+}
+
+int qlin_dev_alloc(int64_t bytes, void** ptr) {
+  if (bytes <= 0 || !ptr) return fail(QLIN_ERR_INVALID_ARGUMENT, "bad allocation request");
+  cudaError_t e = cudaMalloc(ptr, static_cast<size_t>(bytes));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc");
+  e = cudaMemset(*ptr, 0, static_cast<size_t>(bytes));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemset");
+  return QLIN_OK;
+}
+
+int qlin_dev_free(void* ptr) {
+  if (!ptr) return QLIN_OK;
+  cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFree");
+  return QLIN_OK;
+}
+
+int qlin_peer_allgather(void* const* bufs, void* const* arrive, void* expected, const void* src,
+                        int64_t shard_bytes, int world, int rank, void* dst, void* stream) {
+  if (world < 1 || world > kPeerMax || rank < 0 || rank >= world)
+    return fail(QLIN_ERR_INVALID_ARGUMENT, "world %d / rank %d", world, rank);
+  if (!bufs || !arrive || !expected || !src) return fail(QLIN_ERR_INVALID_ARGUMENT, "null argument");
+  if (shard_bytes <= 0 || shard_bytes % 16 != 0)
+    return fail(QLIN_ERR_SHAPE, "shard of %lld bytes is not a positive multiple of 16", (long long)shard_bytes);
+  if (!aligned(src, 16)) return fail(QLIN_ERR_ALIGNMENT, "source must be 16-byte aligned");
+  DevInfo di;
+  if (int r = device_info(&di)) return r;
+  PeerGatherArgs a;
+  memset(&a, 0, sizeof(a));
+  for (int q = 0; q < world; ++q) {
+    if (!bufs[q] || !arrive[q] || !aligned(bufs[q], 16) || !aligned(arrive[q], 4))
+      return fail(QLIN_ERR_ALIGNMENT, "peer buffer %d is null or misaligned", q);
+    a.bufs[q] = static_cast<uint8_t*>(bufs[q]);
+    a.arrive[q] = static_cast<unsigned*>(arrive[q]);
+  }
+  a.expected = static_cast<unsigned*>(expected);
+  a.src = static_cast<const uint8_t*>(src);
+  a.shard_bytes = shard_bytes;
+  a.world = world;
+  a.rank = rank;
+  a.fault = di.fault;
+  // The grid depends on the shard size only, so every rank launches the same
+  // number of CTAs (each CTA adds one arrival on every rank).
+  long long ctas = (shard_bytes / 16 + kPeerThreads * 4 - 1) / (kPeerThreads * 4);
+  if (ctas < 1) ctas = 1;
+  if (ctas > 64) ctas = 64;
+  peer_allgather_kernel<<<static_cast<int>(ctas), kPeerThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "peer_allgather_kernel launch");
+  if (dst) {
+    e = cudaMemcpyAsync(dst, bufs[rank], static_cast<size_t>(shard_bytes) * world, cudaMemcpyDeviceToDevice,
+                        static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(gathered)");
+  }
+  return QLIN_OK;
+}
 
 int qlin_plan_small_m(int wbits, int gate_up, int64_t M, int64_t K, int64_t tiles, int64_t wgrp, int sms,
                       int64_t* out) {

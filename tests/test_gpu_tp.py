@@ -79,8 +79,10 @@ def _rank(rank, world, port, M, q):
         out = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
         layer(a_q.to(dev), a_s.to(dev), out)
         torch.cuda.synchronize()
+        assert layer.gather == "peer"
         q.put((rank, bits(out), layer._ws[M]["hq"].cpu().numpy(), layer._ws[M]["hs"].cpu().numpy()))
         dist.barrier()
+        layer.close()
     finally:
         dist.destroy_process_group()
 
@@ -117,3 +119,71 @@ def test_tp_layer_nccl_ranks_equal_one_gpu(pkg, dev, M):
         assert_quant_close(hq, hs, hq1, hs1, f"gathered h, rank {rank} of {world}")
         ref_r = O.gemm_w4(hq, hs, down_cpu[0].numpy(), bits(down_cpu[1]), down_cpu[2].numpy())
         assert_bf16_close(b, ref_r, f"tp rank {rank} of {world} M={M}")
+
+
+def _peer_rank(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import datetime
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        import __graft_entry__
+        pkg = __graft_entry__.load_package()
+        ok = True
+        for nbytes in (16, 1040, 1 << 20):
+            pg = pkg.tp.PeerGather(nbytes, dev)
+            src = torch.empty(pg.shard, dtype=torch.uint8, device=dev)
+            # eager calls: the counters advance across calls
+            for it in range(3):
+                src.copy_((torch.arange(pg.shard, device=dev) * (rank + 1) + it) % 251)
+                got = pg(src).view(world, pg.shard).cpu()
+                for r in range(world):
+                    want = (torch.arange(pg.shard) * (r + 1) + it) % 251
+                    ok = ok and torch.equal(got[r], want.to(torch.uint8))
+            # replays of a captured gather
+            s = torch.cuda.Stream(device=dev)
+            with torch.cuda.stream(s):
+                pg(src)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=s):
+                pg(src)
+            for it in range(3, 6):
+                src.copy_((torch.arange(pg.shard, device=dev) * (rank + 1) + it) % 251)
+                graph.replay()
+                got = pg.buf.view(world, pg.shard).cpu()
+                for r in range(world):
+                    want = (torch.arange(pg.shard) * (r + 1) + it) % 251
+                    ok = ok and torch.equal(got[r], want.to(torch.uint8))
+            torch.cuda.synchronize()
+            del graph
+            dist.barrier()
+            pg.close()
+        q.put((rank, bool(ok), pkg._lib.load().qlin_device_fault(1)))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_peer_allgather_eager_and_graph(pkg, dev):
+    world = min(torch.cuda.device_count(), 8)
+    world = 8 if world >= 8 else (4 if world >= 4 else 2)
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_peer_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, ok, fault in got:
+        assert ok, f"rank {rank}: gathered bytes differ"
+        assert fault == 0, f"rank {rank}: device fault word {fault}"
