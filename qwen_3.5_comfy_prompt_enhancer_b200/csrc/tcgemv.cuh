@@ -41,7 +41,8 @@
 //               by the drain: sum(a*(nib - z)) = sum(a*nib) - z*sum(a).
 //
 // Split-K across the CTAs of a thread-block cluster: ranks 1..split-1 push
-// their fp32 partial sums into rank 0's shared memory (distributed shared
+// their fp32 partial sums into rank 0's shared memory with asynchronous
+// remote stores that complete rank 0's receive barrier (distributed shared
 // memory, no global scratch) and exit; rank 0 adds them in rank order and
 // runs the epilogue.  PDL: weights stream before griddepcontrol.wait.
 #pragma once
@@ -239,9 +240,13 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
         mbar_init(tempty + i, kDrainThreads);
       }
       mbar_init(bfull, 1);
-      mbar_init(recv, kDrainThreads * (p.split > 1 ? p.split - 1 : 1));
+      mbar_init(recv, 1);
       mbar_init(ready, 1);
       fence_mbar_init();
+      // Rank 0 expects every other rank's partial sums as asynchronous
+      // remote stores that complete the receive barrier's byte count.
+      if (p.split > 1 && rank == 0)
+        mbar_arrive_expect_tx(recv, static_cast<uint32_t>((p.split - 1) * kDrainThreads * NS * MR * 4));
     }
     __syncwarp();
     if (elect_one()) {
@@ -479,9 +484,10 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
   if (warp == kTcWarpMma) tmem_dealloc(tbase, L.tmem_cols);
   // (rank 0's drain warps already passed the cluster wait when part_alias)
   if (p.split > 1 && !(p.part_alias && rank == 0 && is_drain)) cluster_wait();
-  // Ranks 1..split-1 push their partial sums into rank 0's shared memory and
-  // arrive on its receive barrier (release at cluster scope), then exit:
-  // nothing reads their shared memory, so no closing cluster barrier.
+  // Ranks 1..split-1 push their partial sums into rank 0's shared memory with
+  // asynchronous stores, each completing 4 bytes of rank 0's receive barrier
+  // (armed at set-up with the total), then exit: nothing reads their shared
+  // memory, so no closing cluster barrier.
   if (is_drain && rank > 0) {
     bool go = true;
     if (p.part_alias && !mbar_wait_cluster(ready, 0)) {
@@ -491,11 +497,11 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
     if (go) {
       const uint32_t slot0 = smem_u32(part + static_cast<size_t>(rank - 1) * NS * MR * kTileN);
       const uint32_t dst = map_to_rank(slot0, 0);
+      const uint32_t rbar = map_to_rank(smem_u32(recv), 0);
 #pragma unroll
       for (int s = 0; s < NS; ++s)
 #pragma unroll
-        for (int m = 0; m < MR; ++m) st_cluster_f32(dst + ((s * MR + m) * kTileN + c) * 4, acc[s][m]);
-      mbar_arrive_remote(map_to_rank(smem_u32(recv), 0));
+        for (int m = 0; m < MR; ++m) st_async_f32(dst + ((s * MR + m) * kTileN + c) * 4, acc[s][m], rbar);
     }
   }
   if (epi_thread) {
