@@ -261,9 +261,13 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  // Pairs with the cluster wait before the partial sums are pushed: rank 0's
-  // receive barrier is initialised before any other rank arrives on it.
-  if (p.split > 1) cluster_arrive_relaxed();
+  // Every rank's barriers are initialised (and rank 0's receive barrier armed)
+  // before any rank signals another.  Waiting here, with the weights already
+  // in flight, keeps the cluster barrier off the tail of the launch.
+  if (p.split > 1) {
+    cluster_arrive_relaxed();
+    cluster_wait();
+  }
   const uint32_t tbase = *tmem_slot;
 
   float acc[NS][MR];  // drain threads: this CTA's partial sums for output column c
@@ -431,9 +435,7 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
     if (p.part_alias && rank == 0) {
       // The last accumulator batch was observed: every MMA of this CTA has
       // completed, so its operand region is free to receive the other
-      // ranks' partial sums.  The cluster wait orders this after their
-      // barrier initialisation.
-      cluster_wait();
+      // ranks' partial sums.
       if (ok && td == 0)
         for (int r = 1; r < p.split; ++r) mbar_arrive_remote(map_to_rank(smem_u32(ready), r));
     }
@@ -482,8 +484,6 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
   __syncthreads();  // every tensor-memory read has completed
   tc_fence_after();
   if (warp == kTcWarpMma) tmem_dealloc(tbase, L.tmem_cols);
-  // (rank 0's drain warps already passed the cluster wait when part_alias)
-  if (p.split > 1 && !(p.part_alias && rank == 0 && is_drain)) cluster_wait();
   // Ranks 1..split-1 push their partial sums into rank 0's shared memory with
   // asynchronous stores, each completing 4 bytes of rank 0's receive barrier
   // (armed at set-up with the total), then exit: nothing reads their shared
