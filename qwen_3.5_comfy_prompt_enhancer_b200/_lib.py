@@ -1,10 +1,13 @@
-"""ctypes binding of the qlin C ABI (``include/qlin.h``).
+"""Bindings of the qlin C ABI (``include/qlin.h``).
 
-The shared library ``libqlin.so`` is built in-tree next to this file by
-``build.py``.  There is no fallback: if the library is missing or fails to
-load, every entry point raises.
+``load()`` returns the ctypes handle of ``libqlin.so`` (diagnostics, the plan
+query and the multi-GPU helpers); ``ext()`` returns the compiled torch-tensor
+binding ``_qlin_ext`` that the Python entry points call.  Both are built
+in-tree next to this file by ``build.py``.  There is no fallback: if either is
+missing or fails to load, every entry point raises.
 """
 import ctypes
+import importlib
 import os
 import threading
 
@@ -63,6 +66,26 @@ def load():
                 fn.restype = _RESTYPES.get(name, ctypes.c_int)
             _lib = lib
     return _lib
+
+
+_ext = None
+
+
+def ext():
+    """Import (once) and return the ``_qlin_ext`` binding module."""
+    global _ext
+    if _ext is not None:
+        return _ext
+    load()  # same library, and the clearer error when it is missing
+    with _lock:
+        if _ext is None:
+            try:
+                _ext = importlib.import_module("._qlin_ext", __package__)
+            except ImportError as e:
+                raise RuntimeError(
+                    f"qlin Python binding _qlin_ext not importable from {HERE} ({e}); build it first "
+                    "(python -c 'import __graft_entry__ as g; g.build()')") from e
+    return _ext
 
 
 class QlinError(RuntimeError):

@@ -10,6 +10,7 @@
 #include <cstring>
 #include <cstdlib>
 #include <mutex>
+#include <unordered_map>
 
 #include "../../include/qlin.h"
 #include "gemv.cuh"
@@ -114,7 +115,9 @@ int address_range(const void* p, CUdeviceptr* base) {
 // boxes of [box_rows, box_cols].
 // Encoded tensor maps are cached by every encode parameter (a map describes
 // an address range and a layout, never the contents), so the weights and the
-// engine's reused workspace buffers are encoded once.
+// engine's reused workspace buffers are encoded once.  The cache is a hash
+// table (a layer's launches look up several maps each, among hundreds of
+// weights); when it reaches kMapCache entries it starts over.
 struct MapKey {
   const void* base;
   uint64_t cols, rows, row_bytes;
@@ -124,13 +127,25 @@ struct MapKey {
            box_cols == o.box_cols && box_rows == o.box_rows && dt == o.dt && sw == o.sw;
   }
 };
-constexpr int kMapCache = 256;
+inline uint64_t mix64(uint64_t h, uint64_t v) {
+  h ^= v + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
+  return h;
+}
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    uint64_t h = reinterpret_cast<uintptr_t>(k.base);
+    h = mix64(h, k.cols);
+    h = mix64(h, k.rows);
+    h = mix64(h, k.row_bytes);
+    h = mix64(h, (static_cast<uint64_t>(k.box_cols) << 32) | k.box_rows);
+    h = mix64(h, (static_cast<uint64_t>(k.dt) << 32) | k.sw);
+    return static_cast<size_t>(h);
+  }
+};
+constexpr size_t kMapCache = 8192;
 struct MapCache {
   std::mutex mu;
-  MapKey key[kMapCache];
-  CUtensorMap map[kMapCache];
-  bool used[kMapCache] = {};
-  int next = 0;
+  std::unordered_map<MapKey, CUtensorMap, MapKeyHash> maps;
 };
 MapCache& map_cache() {
   static MapCache c;
@@ -146,19 +161,16 @@ int make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t 
   MapCache& c = map_cache();
   {
     std::lock_guard<std::mutex> g(c.mu);
-    for (int i = 0; i < kMapCache; ++i)
-      if (c.used[i] && c.key[i] == k) {
-        *m = c.map[i];
-        return QLIN_OK;
-      }
+    auto it = c.maps.find(k);
+    if (it != c.maps.end()) {
+      *m = it->second;
+      return QLIN_OK;
+    }
   }
   if (int r = encode_map(m, base, dt, cols, rows, row_bytes, box_cols, box_rows, sw128)) return r;
   std::lock_guard<std::mutex> g(c.mu);
-  const int i = c.next;
-  c.next = (c.next + 1) % kMapCache;
-  c.key[i] = k;
-  c.map[i] = *m;
-  c.used[i] = true;
+  if (c.maps.size() >= kMapCache) c.maps.clear();
+  c.maps.emplace(k, *m);
   return QLIN_OK;
 }
 
@@ -504,8 +516,8 @@ int launch_tc_mr(int mr, const GemvArgs& a, dim3 grid, size_t smem, cudaStream_t
 // Row block and K split for the tcgen05 path.  Row blocks of 32 rows hold
 // the largest activation and partial-sum buffers; when no split of K fits
 // shared memory, 16-row blocks are used.  Returns QLIN_OK or an error.
-int choose_tc(int wb, int ns, int64_t M, int K, int wgrp, int tiles, int sms, int* mr_out, int* rowblocks_out,
-              TcPlan* pl_out) {
+int choose_tc_uncached(int wb, int ns, int64_t M, int K, int wgrp, int tiles, int sms, int* mr_out,
+                       int* rowblocks_out, TcPlan* pl_out) {
   int mr = tc_mr(wb, M);
   for (;;) {
     const int nm = mr < 16 ? 16 : mr;
@@ -522,6 +534,64 @@ int choose_tc(int wb, int ns, int64_t M, int K, int wgrp, int tiles, int sms, in
     mr = 16;
   }
   return fail(QLIN_ERR_SHAPE, "K=%d exceeds the shared-memory capacity of the small-M kernel", K);
+}
+
+// The plan depends only on these inputs (the tuning overrides are read once
+// per process), so it is computed once per shape and looked up afterwards.
+struct TcKey {
+  int wb, ns, K, wgrp, tiles, sms;
+  int64_t M;
+  bool operator==(const TcKey& o) const {
+    return wb == o.wb && ns == o.ns && K == o.K && wgrp == o.wgrp && tiles == o.tiles && sms == o.sms && M == o.M;
+  }
+};
+struct TcKeyHash {
+  size_t operator()(const TcKey& k) const {
+    uint64_t h = static_cast<uint64_t>(k.M);
+    h = mix64(h, (static_cast<uint64_t>(k.wb) << 40) ^ (static_cast<uint64_t>(k.ns) << 32) ^ static_cast<uint32_t>(k.K));
+    h = mix64(h, (static_cast<uint64_t>(static_cast<uint32_t>(k.wgrp)) << 32) ^ static_cast<uint32_t>(k.tiles));
+    return static_cast<size_t>(mix64(h, static_cast<uint64_t>(k.sms)));
+  }
+};
+struct TcChoice {
+  int mr, rowblocks;
+  TcPlan pl;
+};
+constexpr size_t kPlanCache = 4096;
+struct PlanCache {
+  std::mutex mu;
+  std::unordered_map<TcKey, TcChoice, TcKeyHash> plans;
+};
+PlanCache& plan_cache() {
+  static PlanCache c;
+  return c;
+}
+
+int choose_tc(int wb, int ns, int64_t M, int K, int wgrp, int tiles, int sms, int* mr_out, int* rowblocks_out,
+              TcPlan* pl_out) {
+  const TcKey k{wb, ns, K, wgrp, tiles, sms, M};
+  PlanCache& c = plan_cache();
+  {
+    std::lock_guard<std::mutex> g(c.mu);
+    auto it = c.plans.find(k);
+    if (it != c.plans.end()) {
+      *mr_out = it->second.mr;
+      *rowblocks_out = it->second.rowblocks;
+      *pl_out = it->second.pl;
+      return QLIN_OK;
+    }
+  }
+  TcChoice ch{};
+  if (int r = choose_tc_uncached(wb, ns, M, K, wgrp, tiles, sms, &ch.mr, &ch.rowblocks, &ch.pl)) return r;
+  {
+    std::lock_guard<std::mutex> g(c.mu);
+    if (c.plans.size() >= kPlanCache) c.plans.clear();
+    c.plans.emplace(k, ch);
+  }
+  *mr_out = ch.mr;
+  *rowblocks_out = ch.rowblocks;
+  *pl_out = ch.pl;
+  return QLIN_OK;
 }
 
 int run_tc(int wb, int epi, GemvArgs& a, int tiles, cudaStream_t st) {

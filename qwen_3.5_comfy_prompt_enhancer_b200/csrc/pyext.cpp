@@ -1,0 +1,314 @@
+// Python binding of the qlin C ABI for torch tensors (module `_qlin_ext`).
+//
+// The Python entry points (kernels/gemm.py, kernels/w4.py, kernels/norm.py)
+// hand their tensors to these functions, which make the checks the
+// reference's call sites rely on (dtype, rank, contiguity, shapes, one CUDA
+// device for every tensor) and call the extern "C" functions of libqlin.so
+// on torch's current stream of that device.  Doing this in C++ instead of
+// Python + ctypes keeps the host cost of one call to a few microseconds.
+//
+// Checks raise ValueError / TypeError (pybind11 translates
+// py::value_error / py::type_error); a failing C-ABI call returns its
+// qlin_status, which the Python caller turns into QlinError.
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <torch/csrc/utils/pybind.h>
+
+#include <optional>
+#include <string>
+
+#include "qlin.h"
+
+namespace py = pybind11;
+using at::Tensor;
+using OptT = std::optional<Tensor>;
+
+namespace {
+
+constexpr int64_t kGroup = 64;
+
+const char* dtype_name(c10::ScalarType t) {
+  switch (t) {
+    case c10::ScalarType::Char: return "torch.int8";
+    case c10::ScalarType::Byte: return "torch.uint8";
+    case c10::ScalarType::Float: return "torch.float32";
+    case c10::ScalarType::BFloat16: return "torch.bfloat16";
+    default: return c10::toString(t);
+  }
+}
+
+// Python's repr of a shape tuple: (4, 2048) or (128,).
+std::string shape(const Tensor& t) {
+  std::string s = "(";
+  for (int64_t i = 0; i < t.dim(); ++i) {
+    if (i) s += ", ";
+    s += std::to_string(t.size(i));
+  }
+  if (t.dim() == 1) s += ",";
+  return s + ")";
+}
+
+std::string dims(int64_t a, int64_t b) { return "[" + std::to_string(a) + ", " + std::to_string(b) + "]"; }
+
+// Every tensor of one call lives on the device of its first operand.
+struct Call {
+  c10::DeviceIndex dev = -1;
+
+  void need(const Tensor& t, const char* name, c10::ScalarType dt, int64_t rank, bool contiguous = true) {
+    if (!t.is_cuda())
+      throw py::value_error(std::string(name) + " must be a CUDA tensor (no CPU path), got " + t.device().str());
+    if (dev < 0) dev = t.get_device();
+    else if (t.get_device() != dev)
+      throw py::value_error(std::string(name) + " is on cuda:" + std::to_string(t.get_device()) +
+                            ", the other operands on cuda:" + std::to_string(dev));
+    if (t.scalar_type() != dt)
+      throw py::type_error(std::string(name) + " must be " + dtype_name(dt) + ", got " + dtype_name(t.scalar_type()));
+    if (t.dim() != rank)
+      throw py::value_error(std::string(name) + " must be " + std::to_string(rank) + "-D, got shape " + shape(t));
+    if (contiguous && !t.is_contiguous()) throw py::value_error(std::string(name) + " must be contiguous");
+  }
+
+  // 2-D tensor whose rows may be strided but whose elements are contiguous.
+  void need_rows(const Tensor& t, const char* name, c10::ScalarType dt) {
+    need(t, name, dt, 2, false);
+    if (t.size(1) > 1 && t.stride(1) != 1)
+      throw py::value_error(std::string(name) + " must have unit stride along its last dimension");
+  }
+
+  // int8 activations + per-64 fp32 scales; returns (M, K).
+  std::pair<int64_t, int64_t> acts(const Tensor& a_q, const Tensor& a_s) {
+    need(a_q, "a_q", at::kChar, 2);
+    need(a_s, "a_s", at::kFloat, 2);
+    const int64_t M = a_q.size(0), K = a_q.size(1);
+    if (a_s.size(0) != M || a_s.size(1) * kGroup != K)
+      throw py::value_error("a_s must be [M, K/64] = " + dims(M, K / kGroup) + ", got " + shape(a_s));
+    return {M, K};
+  }
+
+  // W8 weight [K, N] int8 + [N] fp32 column scales; returns N.
+  int64_t w8(const Tensor& b, const Tensor& b_s, int64_t K, const std::string& name) {
+    need(b, name.c_str(), at::kChar, 2);
+    need(b_s, (name + "_s").c_str(), at::kFloat, 1);
+    if (b.size(0) != K)
+      throw py::value_error(name + " must be [K=" + std::to_string(K) + ", N], got " + shape(b));
+    if (b_s.size(0) != b.size(1))
+      throw py::value_error(name + " scales must have N=" + std::to_string(b.size(1)) + " entries, got " +
+                            std::to_string(b_s.size(0)));
+    return b.size(1);
+  }
+
+  // W4 weight [K/2, N] uint8 + [K/WGRP, N] bf16 scales (+ uint8 zeros);
+  // returns (N, WGRP).
+  std::pair<int64_t, int64_t> w4(const Tensor& b, const Tensor& b_s, const OptT& b_z, int64_t K,
+                                 const std::string& name) {
+    need(b, name.c_str(), at::kByte, 2);
+    need(b_s, (name + "_s").c_str(), at::kBFloat16, 2);
+    if (b.size(0) * 2 != K)
+      throw py::value_error(name + " must be [K//2=" + std::to_string(K / 2) + ", N], got " + shape(b));
+    const int64_t N = b.size(1);
+    if (b_s.size(1) != N || b_s.size(0) == 0 || K % b_s.size(0) != 0)
+      throw py::value_error(name + " scales must be [K//WGRP, " + std::to_string(N) + "], got " + shape(b_s));
+    if (b_z) {
+      need(*b_z, (name + "_z").c_str(), at::kByte, 2);
+      if (b_z->sizes() != b_s.sizes())
+        throw py::value_error(name + " zeros must match scales " + shape(b_s) + ", got " + shape(*b_z));
+    }
+    return {N, K / b_s.size(0)};
+  }
+
+  void out_mn(const Tensor& t, const char* name, int64_t M, int64_t N) {
+    if (t.size(0) != M || t.size(1) != N)
+      throw py::value_error(std::string(name) + " must be " + dims(M, N) + ", got " + shape(t));
+  }
+
+  void quant_out(const Tensor& out_q, const Tensor& out_s, int64_t M, int64_t N) {
+    need(out_q, "out_q", at::kChar, 2);
+    need(out_s, "out_s", at::kFloat, 2);
+    if (out_q.size(0) != M || out_q.size(1) != N || out_s.size(0) != M || out_s.size(1) != N / kGroup)
+      throw py::value_error("out_q/out_s must be " + dims(M, N) + " / " + dims(M, N / kGroup));
+  }
+
+  // Runs `f(stream)` with the call's device current.
+  template <class F>
+  int launch(F&& f) {
+    c10::cuda::CUDAGuard guard(dev);
+    return f(static_cast<void*>(c10::cuda::getCurrentCUDAStream(dev).stream()));
+  }
+};
+
+template <class T>
+const T* cptr(const Tensor& t) {
+  return static_cast<const T*>(t.data_ptr());
+}
+template <class T>
+const T* cptr(const OptT& t) {
+  return t ? static_cast<const T*>(t->data_ptr()) : nullptr;
+}
+
+// ---------------------------------------------------------------- kernels/gemm.py
+int gemm_i8(const Tensor& a_q, const Tensor& a_s, const Tensor& b, const Tensor& b_s, const Tensor& out,
+            const OptT& residual) {
+  Call c;
+  const auto [M, K] = c.acts(a_q, a_s);
+  const int64_t N = c.w8(b, b_s, K, "b");
+  c.need_rows(out, "out", at::kBFloat16);
+  c.out_mn(out, "out", M, N);
+  if (residual) {
+    c.need_rows(*residual, "residual", at::kBFloat16);
+    c.out_mn(*residual, "residual", M, N);
+  }
+  return c.launch([&](void* st) {
+    return qlin_gemm_i8(cptr<int8_t>(a_q), cptr<float>(a_s), M, K, cptr<int8_t>(b), cptr<float>(b_s), N,
+                        out.data_ptr(), out.stride(0), cptr<void>(residual), residual ? residual->stride(0) : 0, st);
+  });
+}
+
+int mlp_gate_up(const Tensor& a_q, const Tensor& a_s, const Tensor& wg, const Tensor& sg, const Tensor& wu,
+                const Tensor& su, const Tensor& out) {
+  Call c;
+  const auto [M, K] = c.acts(a_q, a_s);
+  const int64_t N = c.w8(wg, sg, K, "wg");
+  if (c.w8(wu, su, K, "wu") != N) throw py::value_error("gate and up weights must have the same N");
+  c.need(out, "out", at::kBFloat16, 2);
+  c.out_mn(out, "out", M, N);
+  return c.launch([&](void* st) {
+    return qlin_mlp_gate_up(cptr<int8_t>(a_q), cptr<float>(a_s), M, K, cptr<int8_t>(wg), cptr<float>(sg),
+                            cptr<int8_t>(wu), cptr<float>(su), N, out.data_ptr(), out.stride(0), st);
+  });
+}
+
+int mlp_gate_up_quant(const Tensor& a_q, const Tensor& a_s, const Tensor& wg, const Tensor& sg, const Tensor& wu,
+                      const Tensor& su, const Tensor& out_q, const Tensor& out_s) {
+  Call c;
+  const auto [M, K] = c.acts(a_q, a_s);
+  const int64_t N = c.w8(wg, sg, K, "wg");
+  if (c.w8(wu, su, K, "wu") != N) throw py::value_error("gate and up weights must have the same N");
+  c.quant_out(out_q, out_s, M, N);
+  return c.launch([&](void* st) {
+    return qlin_mlp_gate_up_quant(cptr<int8_t>(a_q), cptr<float>(a_s), M, K, cptr<int8_t>(wg), cptr<float>(sg),
+                                  cptr<int8_t>(wu), cptr<float>(su), N, static_cast<int8_t*>(out_q.data_ptr()),
+                                  static_cast<float*>(out_s.data_ptr()), st);
+  });
+}
+
+int proj3(const Tensor& a_q, const Tensor& a_s, const OptT& w1, const OptT& s1, const OptT& w2, const OptT& s2,
+          const OptT& w3, const OptT& s3, const Tensor& out) {
+  Call c;
+  const auto [M, K] = c.acts(a_q, a_s);
+  const OptT* w[3] = {&w1, &w2, &w3};
+  const OptT* s[3] = {&s1, &s2, &s3};
+  int64_t n[3] = {0, 0, 0};
+  for (int i = 0; i < 3; ++i) {
+    if (!*w[i]) continue;
+    const std::string name = "w" + std::to_string(i + 1);
+    if (!*s[i]) throw py::value_error(name + " has no scales");
+    n[i] = c.w8(**w[i], **s[i], K, name);
+  }
+  const int64_t NT = n[0] + n[1] + n[2];
+  c.need_rows(out, "out", at::kBFloat16);
+  if (out.size(0) != M || out.size(1) < NT)
+    throw py::value_error("out must be [" + std::to_string(M) + ", >=" + std::to_string(NT) + "], got " + shape(out));
+  return c.launch([&](void* st) {
+    return qlin_proj3(cptr<int8_t>(a_q), cptr<float>(a_s), M, K, cptr<int8_t>(w1), cptr<float>(s1), n[0],
+                      cptr<int8_t>(w2), cptr<float>(s2), n[1], cptr<int8_t>(w3), cptr<float>(s3), n[2],
+                      out.data_ptr(), out.stride(0), st);
+  });
+}
+
+// ---------------------------------------------------------------- kernels/w4.py
+int gemm_w4(const Tensor& a_q, const Tensor& a_s, const Tensor& b, const Tensor& b_s, const Tensor& out,
+            const OptT& residual, const OptT& b_z) {
+  Call c;
+  const auto [M, K] = c.acts(a_q, a_s);
+  const auto [N, wgrp] = c.w4(b, b_s, b_z, K, "b");
+  c.need_rows(out, "out", at::kBFloat16);
+  c.out_mn(out, "out", M, N);
+  if (residual) {
+    c.need_rows(*residual, "residual", at::kBFloat16);
+    c.out_mn(*residual, "residual", M, N);
+  }
+  return c.launch([&](void* st) {
+    return qlin_gemm_w4(cptr<int8_t>(a_q), cptr<float>(a_s), M, K, cptr<uint8_t>(b), cptr<void>(b_s),
+                        cptr<uint8_t>(b_z), N, wgrp, out.data_ptr(), out.stride(0), cptr<void>(residual),
+                        residual ? residual->stride(0) : 0, st);
+  });
+}
+
+int proj3_w4(const Tensor& a_q, const Tensor& a_s, const OptT& w1, const OptT& s1, const OptT& w2, const OptT& s2,
+             const OptT& w3, const OptT& s3, const Tensor& out, const OptT& z1, const OptT& z2, const OptT& z3) {
+  Call c;
+  const auto [M, K] = c.acts(a_q, a_s);
+  const OptT* w[3] = {&w1, &w2, &w3};
+  const OptT* s[3] = {&s1, &s2, &s3};
+  const OptT* z[3] = {&z1, &z2, &z3};
+  int64_t n[3] = {0, 0, 0};
+  int64_t wgrp = 0;
+  for (int i = 0; i < 3; ++i) {
+    if (!*w[i]) continue;
+    const std::string name = "w" + std::to_string(i + 1);
+    if (!*s[i]) throw py::value_error(name + " has no scales");
+    const auto [ni, wg] = c.w4(**w[i], **s[i], *z[i], K, name);
+    if (wgrp == 0) wgrp = wg;
+    else if (wg != wgrp) throw py::value_error("all proj3_w4 segments must share one weight group size");
+    n[i] = ni;
+  }
+  const int64_t NT = n[0] + n[1] + n[2];
+  c.need_rows(out, "out", at::kBFloat16);
+  if (out.size(0) != M || out.size(1) < NT)
+    throw py::value_error("out must be [" + std::to_string(M) + ", >=" + std::to_string(NT) + "], got " + shape(out));
+  // a missing segment contributes no columns: its pointers stay null
+  auto wp = [&](int i) { return *w[i] ? cptr<uint8_t>(*w[i]) : nullptr; };
+  auto sp = [&](int i) { return *w[i] ? cptr<void>(*s[i]) : nullptr; };
+  auto zp = [&](int i) { return *w[i] ? cptr<uint8_t>(*z[i]) : nullptr; };
+  return c.launch([&](void* st) {
+    return qlin_proj3_w4(cptr<int8_t>(a_q), cptr<float>(a_s), M, K, wp(0), sp(0), zp(0), n[0], wp(1), sp(1), zp(1),
+                         n[1], wp(2), sp(2), zp(2), n[2], wgrp ? wgrp : 64, out.data_ptr(), out.stride(0), st);
+  });
+}
+
+int mlp_gate_up_quant_w4(const Tensor& a_q, const Tensor& a_s, const Tensor& wg, const Tensor& sg, const Tensor& wu,
+                         const Tensor& su, const Tensor& out_q, const Tensor& out_s, const OptT& zg,
+                         const OptT& zu) {
+  Call c;
+  const auto [M, K] = c.acts(a_q, a_s);
+  const auto [N, wgrp] = c.w4(wg, sg, zg, K, "wg");
+  const auto [Nu, wgrp_u] = c.w4(wu, su, zu, K, "wu");
+  if (Nu != N || wgrp_u != wgrp) throw py::value_error("gate and up weights must have the same N and group size");
+  c.quant_out(out_q, out_s, M, N);
+  return c.launch([&](void* st) {
+    return qlin_mlp_gate_up_quant_w4(cptr<int8_t>(a_q), cptr<float>(a_s), M, K, cptr<uint8_t>(wg), cptr<void>(sg),
+                                     cptr<uint8_t>(zg), cptr<uint8_t>(wu), cptr<void>(su), cptr<uint8_t>(zu), N,
+                                     wgrp, static_cast<int8_t*>(out_q.data_ptr()),
+                                     static_cast<float*>(out_s.data_ptr()), st);
+  });
+}
+
+// ---------------------------------------------------------------- kernels/norm.py
+int quant_row(const Tensor& x, const Tensor& q, const Tensor& s) {
+  Call c;
+  c.need_rows(x, "x", at::kBFloat16);
+  c.need(q, "q", at::kChar, 2);
+  c.need(s, "s", at::kFloat, 2);
+  const int64_t M = q.size(0), K = q.size(1);
+  if (x.size(0) != M || x.size(1) != K || s.size(0) != M || s.size(1) != K / kGroup)
+    throw py::value_error("shapes must be x [M,K], q [M,K], s [M,K/64]; got " + shape(x) + ", " + shape(q) + ", " +
+                          shape(s));
+  return c.launch([&](void* st) {
+    return qlin_quant_row(x.data_ptr(), x.stride(0), M, K, static_cast<int8_t*>(q.data_ptr()),
+                          static_cast<float*>(s.data_ptr()), st);
+  });
+}
+
+}  // namespace
+
+PYBIND11_MODULE(_qlin_ext, m) {
+  m.doc() = "torch-tensor binding of the qlin C ABI (checks + launch on the current stream)";
+  m.def("gemm_i8", &gemm_i8);
+  m.def("mlp_gate_up", &mlp_gate_up);
+  m.def("mlp_gate_up_quant", &mlp_gate_up_quant);
+  m.def("proj3", &proj3);
+  m.def("gemm_w4", &gemm_w4);
+  m.def("proj3_w4", &proj3_w4);
+  m.def("mlp_gate_up_quant_w4", &mlp_gate_up_quant_w4);
+  m.def("quant_row", &quant_row);
+}
