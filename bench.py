@@ -7,9 +7,10 @@ layer -- group size 128, bf16 group scales, uint8 zero points, engine layouts
   gate/up   mlp_gate_up_quant_w4  2048 -> 2 x 6144 (+ SiLU*up + int8 requant)
   down      gemm_w4 + residual    6144 -> 2048
   o_proj    gemm_w4 + residual    2048 -> 2048
-One step = the four launches at M=1 followed by the four at M=4.  Weights
-rotate over 8 layer copies (about 210 MB, more than the 126 MB L2), so every
-step streams its weights from HBM.  Each step's launches are captured in a CUDA
+One step = the four launches at M=1 followed by the four at M=4, the two Ms on
+different layer copies.  Weights rotate over 8 layer copies (about 210 MB, more
+than the 126 MB L2): no weight is read twice within a step and a copy comes
+back only after four steps, so every step streams its weights from HBM.  Each step's launches are captured in a CUDA
 graph; the timed region replays exactly K step graphs, bracketed by a barrier
 and device synchronisation, timed with CUDA events (max over ranks).
 
@@ -437,9 +438,15 @@ def main():
     wss = {M: Workspace(pkg, dev, M, gen) for M in MS}
     torch.cuda.synchronize()
 
+    def copy_for(li, j):
+        """Layer copy that the j-th M of step li reads: the Ms of one step read
+        different copies, so no weight is read twice within a step, and a copy
+        comes back only after COPIES // len(MS) steps (> L2 of weights)."""
+        return layers[(li + j * (COPIES // len(MS))) % COPIES]
+
     def step(li):
-        for M in MS:
-            run_layer(pkg, layers[li], wss[M])
+        for j, M in enumerate(MS):
+            run_layer(pkg, copy_for(li, j), wss[M])
 
     stream = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(stream):
@@ -503,7 +510,7 @@ def main():
             ws = wss[M]
             dev_x[M].copy_(host_x[M], non_blocking=True)
             pkg.quant_row(dev_x[M], ws.xq, ws.xs)
-            run_layer(pkg, layers[li], ws)
+            run_layer(pkg, copy_for(li, MS.index(M)), ws)
             host_out[M].copy_(ws.hidden, non_blocking=True)
     with torch.cuda.stream(stream):
         for li in range(3):
@@ -545,7 +552,7 @@ def main():
                             "gate_up 2048->2x6144 fused SiLU+requant, down 6144->2048 +res, o 2048->2048 +res), "
                             "M=1 and M=4 per step",
                 "bytes_per_step": per_step, "weight_copies": COPIES,
-                "l2": "rotating 8 layer copies (~210 MB > 126 MB L2)",
+                "l2": "rotating 8 layer copies (~210 MB > 126 MB L2); M=1 and M=4 of a step read different copies",
                 "launches_per_step": LAUNCHES_PER_STEP, "timing": "CUDA graph per step, CUDA events",
                 "parallelism": f"replicas x{world}"},
             "roofline": {"bound": "hbm", "kernel": "mlp_gate_up_quant_w4 M=4 (tcgen05 weight streaming)",

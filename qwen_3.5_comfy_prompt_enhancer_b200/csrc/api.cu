@@ -322,25 +322,20 @@ constexpr size_t kTcMaxSmem = 227 * 1024;
 struct TcPlan {
   int split, gmax, bs, rb, ab, nbb, alias;
   // 2: one batch (weights in flight and operands complete before the grid
-  // dependency); 1: W4 packed weights all resident, unpacked in a ring;
-  // 0: weights stream through double-buffered batches.
+  // dependency); 0: weights stream through double-buffered batches.
   int level;
   size_t smem;
 };
 
 // Batch plan for one K split, first that fits the per-CTA budget of
 // ~112 KB (two CTAs per SM) and the 256-column tensor-memory share:
-//  1. one batch: the whole K range in flight, one hand-off per role;
-//  2. fused W4 gate/up only: every packed weight group resident (all
-//     requested up front), a ring of unpacked tiles and per-group
-//     hand-offs;
-//  3. double-buffered batches (the weights stream behind the MMAs).
-// Plans 1 and 2 are tried without, then with, the partial-sum buffer
-// aliased onto rank 0's finished operand region.  Measured on B200 (config-2
-// shapes): plan 2 beats plan 3 for the two-stream gate/up (11.9 vs 13.7 us)
-// but not for single-stream W4 (11.4 vs 8.4 us for the K = 6144 down
-// projection), whose per-group hand-offs after the grid dependency cost more
-// than the streamed batches.
+//  1. one batch: the whole K range in flight, one hand-off per role (tried
+//     without, then with, the partial-sum buffer aliased onto rank 0's
+//     finished operand region);
+//  2. double-buffered batches (the weights stream behind the MMAs).
+// (A plan with every packed W4 group resident and a ring of unpacked tiles
+// was measured slower than streaming once the W4 operands became the masked
+// nibble tiles: 12.3 vs 10.8 us for the config-2 gate/up at split 4.)
 void plan_batches(int wb, int mr, int ns, int wgrp, long long ctas, int sms, bool long_stream, TcPlan& pl) {
   const uint32_t budget = (tune_budget() > 0 ? tune_budget() : 112) * 1024;
   // A long streamed launch (tens of MB of weights) that fits one CTA per SM
@@ -366,10 +361,6 @@ void plan_batches(int wb, int mr, int ns, int wgrp, long long ctas, int sms, boo
   pl.level = 0;
   for (int alias = 0; alias < 2 && !ok && tune_max_level() >= 2; ++alias)
     if (gmax <= tmem_groups && fits(gmax, 1, wb == 4 ? 1 : 0, 1, alias)) ok = true, pl.level = 2;
-  for (int alias = 0; alias < 2 && !ok && wb == 4 && ns == 2 && tune_max_level() >= 1; ++alias)
-    // deepest unpacked ring (up to 4 groups) that fits
-    for (int ab = (gmax < 4 ? gmax : 4); !ok && ab >= 2; --ab)
-      if (fits(1, gmax, ab, gmax < tmem_groups ? gmax : tmem_groups, alias)) ok = true, pl.level = 1;
   if (!ok) {
     // Streamed: the most groups in flight (weight-ring slots x groups per
     // batch) that fit, preferring larger batches (fewer hand-offs).
@@ -378,7 +369,7 @@ void plan_batches(int wb, int mr, int ns, int wgrp, long long ctas, int sms, boo
     // (short launches keep two slots: measured best for the config-2 shapes)
     for (int rb = 2; rb <= (long_stream ? 4 : 2); ++rb) {
       const TcLayout one = tc_layout(wb, mr, ns, wgrp, gmax, 1, rb, ab, 2, s, 0);
-      const uint32_t per_group = rb * base.raw_stage + (wb == 4 ? ab * ns * 64 * kTileN : 0);
+      const uint32_t per_group = rb * base.raw_stage + (wb == 4 ? ab * ns * base.atile : 0);
       const uint32_t fixed = one.total - per_group;
       const uint32_t room = stream_budget > fixed ? stream_budget - fixed : 0;
       int bs = static_cast<int>(room / per_group);
@@ -459,12 +450,16 @@ TcPlan plan_tc(int wb, int mr, int ns, int K, int wgrp, int tiles, int rowblocks
     else if (ctas <= two_per_sm && up[pl.level].split == 0) up[pl.level] = pl;
   }
   if (long_stream) in[0] = stream, up[0] = TcPlan{};
-  // Highest level first (more of the work ahead of the grid dependency);
-  // extra splits add combine work, so beyond the target the smallest one.
-  for (int lv = 2; lv >= 0; --lv) {
+  // Within the CTA target, the highest level first (more of the work ahead
+  // of the grid dependency); only then beyond the target, where extra splits
+  // add combine work, the smallest one.  Measured on B200 with the W4
+  // nibble-split operands: the one-batch plan of the fused gate/up needs
+  // split 6 (288 CTAs) to fit and takes 15.5 us, the streamed plan at split 4
+  // (192 CTAs) 10.8 us.
+  for (int lv = 2; lv >= 0; --lv)
     if (in[lv].split) return in[lv];
+  for (int lv = 2; lv >= 0; --lv)
     if (up[lv].split) return up[lv];
-  }
   return any;
 }
 
@@ -835,7 +830,10 @@ int seg_w4(GemvSeg& s, const uint8_t* w, const void* sc, const uint8_t* z, int64
   if (!aligned(w, 16) || !aligned(sc, 16) || (z && !aligned(z, 16)))
     return fail(QLIN_ERR_ALIGNMENT, "W4 weight/scale/zero tensors must be 16-byte aligned");
   const uint32_t nsr = wgrp == 32 ? 2 : 1;
-  if (int r = make_map(&s.tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, n, K / 2, n, kTileN, 32)) return r;
+  // 128-byte swizzle for the tcgen05 kernel, which unpacks half of each
+  // group in place into the MMA operand layout; the dp4a kernel reads plain
+  // rows.
+  if (int r = make_map(&s.tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, n, K / 2, n, kTileN, 32, use_tc())) return r;
   if (int r = make_map(&s.ts, sc, CU_TENSOR_MAP_DATA_TYPE_UINT16, n, K / wgrp, 2 * n, kTileN, nsr)) return r;
   if (z) {
     if (int r = make_map(&s.tz, z, CU_TENSOR_MAP_DATA_TYPE_UINT8, n, K / wgrp, n, kTileN, nsr)) return r;

@@ -171,6 +171,16 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
+// Named barrier that also ANDs a predicate over the participating threads.
+__device__ __forceinline__ bool named_bar_and(int id, int nthreads, bool pred) {
+  int r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.s32 p, %1, 0;\n bar.red.and.pred q, %2, %3, p;\n selp.s32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"(static_cast<int>(pred)), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
 
 // ---------------------------------------------------------------- integer dots
 // d = c + sum_i a.u8[i] * b.s8[i]

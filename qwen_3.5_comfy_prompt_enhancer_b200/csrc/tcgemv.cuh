@@ -67,8 +67,8 @@ constexpr uint32_t kTmemBudget = 256;
 __host__ __device__ constexpr int tc_threads(int wb) { return (wb == 8 ? 6 : 10) * 32; }
 
 struct TcLayout {
-  uint32_t nsub, raw_stream, raw_stage, raw_off, a_off, b_off, nbox, as_off, asum_off, part_off, part_bytes,
-      op_bytes, xchg_off, bar_off, tmem_slot_off, total, tmem_cols, per_buf;
+  uint32_t nsub, wtile, sztile, atile, raw_stream, raw_stage, raw_off, sz_off, a_off, b_off, nbox, as_off, asum_off,
+      part_off, part_bytes, op_bytes, xchg_off, bar_off, tmem_slot_off, total, tmem_cols, per_buf;
 };
 
 __host__ __device__ inline uint32_t pow2_at_least(uint32_t x) {
@@ -88,13 +88,23 @@ __host__ __device__ inline TcLayout tc_layout(int wb, int mr, int ns, int wgrp, 
   const int nm = mr < 16 ? 16 : mr;
   TcLayout L;
   L.nsub = (wb == 4 && wgrp == 32) ? 2 : 1;
-  L.raw_stream = wb == 8 ? 64 * kTileN : 32 * kTileN + L.nsub * kTileN * 2 + L.nsub * kTileN;
+  // Per (group, stream): the weight tile as loaded (W8: 64 K rows; W4: 32
+  // packed rows; each a 1024-byte aligned 128-byte-swizzled tile), the W4
+  // group scales (bf16) + zeros (uint8), and the W4 operand-ring tile (the
+  // unpacked K rows 0-31 of the group; rows 32-63 are unpacked in place over
+  // the packed tile).
+  L.wtile = wb == 8 ? 64 * kTileN : 32 * kTileN;
+  L.sztile = wb == 8 ? 0 : L.nsub * kTileN * 3;
+  L.atile = wb == 8 ? 0 : 32 * kTileN;
+  L.raw_stream = L.wtile + L.sztile;
   L.raw_stage = ns * L.raw_stream;
   uint32_t off = 0;
   L.raw_off = off;
-  off = align_up(off + rb * bs * L.raw_stage, 1024);
+  off = align_up(off + rb * bs * ns * L.wtile, 1024);
+  L.sz_off = off;
+  off = align_up(off + rb * bs * ns * L.sztile, 1024);
   L.a_off = off;
-  if (wb == 4) off = align_up(off + ab * bs * ns * 64 * kTileN, 1024);
+  if (wb == 4) off = align_up(off + ab * bs * ns * L.atile, 1024);
   // Activation operand: boxes of 128 K (one swizzle row) x nm rows.
   L.b_off = off;
   L.nbox = (gmax + 1) / 2;
@@ -105,7 +115,7 @@ __host__ __device__ inline TcLayout tc_layout(int wb, int mr, int ns, int wgrp, 
   off = align_up(off + (wb == 4 ? gmax * 2 * nm * 4 : 0), 16);
   // Partial sums pushed by the cluster's ranks 1..split-1 into rank 0.
   L.part_bytes = (split > 1 ? split - 1 : 0) * ns * mr * kTileN * 4;
-  L.op_bytes = wb == 4 ? ab * bs * ns * 64 * kTileN : rb * bs * L.raw_stage;
+  L.op_bytes = wb == 4 ? ab * bs * ns * L.atile : rb * bs * ns * L.wtile;
   if (alias) {
     L.part_off = wb == 4 ? L.a_off : L.raw_off;
   } else {
@@ -170,14 +180,17 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
   auto batch_len = [&](int b) { return (b + 1) * BS <= nst ? BS : nst - b * BS; };
 
   uint8_t* raw = smem + L.raw_off;
+  uint8_t* szr = smem + L.sz_off;
   uint8_t* abuf = smem + L.a_off;
   uint8_t* bop = smem + L.b_off;
   float* ass = reinterpret_cast<float*>(smem + L.as_off);
   int* asum = reinterpret_cast<int*>(smem + L.asum_off);
   float* part = reinterpret_cast<float*>(smem + L.part_off);
-  // Raw stage of (ring slot, group-in-batch, stream); A tile of (slot, j, stream).
-  auto raw_stage = [&](int rs, int j, int s) { return raw + (rs * BS + j) * L.raw_stage + s * L.raw_stream; };
-  auto a_tile = [&](int as, int j, int s) { return abuf + ((as * BS + j) * NS + s) * 64 * kTileN; };
+  // Weight tile, W4 scales + zeros, and W4 operand-ring tile of (ring slot,
+  // group-in-batch, stream).
+  auto raw_w = [&](int rs, int j, int s) { return raw + ((rs * BS + j) * NS + s) * L.wtile; };
+  auto raw_sz = [&](int rs, int j, int s) { return szr + ((rs * BS + j) * NS + s) * L.sztile; };
+  auto a_tile = [&](int as, int j, int s) { return abuf + ((as * BS + j) * NS + s) * L.atile; };
 
   // Drain thread -> output column of this tile (TMEM lane 32*(warp%4) + lane).
   const bool is_drain = warp >= kTcWarpDrain && warp < kTcWarpDrain + 4;
@@ -211,14 +224,15 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
 #pragma unroll
       for (int s = 0; s < NS; ++s) {
         const GemvSeg& sg = NS == 1 ? S0 : p.seg[s];
-        uint8_t* dst = raw_stage(rs, j, s);
+        uint8_t* dst = raw_w(rs, j, s);
         if (WB == 8) {
           tma_load_2d(dst, &sg.tw, n0, g * 64, full + rs, pol);
         } else {
           tma_load_2d(dst, &sg.tw, n0, g * 32, full + rs, pol);
           const int srow = (g * 64) / p.wgrp;
-          tma_load_2d(dst + 32 * kTileN, &sg.ts, n0, srow, full + rs, pol);
-          if (sg.has_z) tma_load_2d(dst + 32 * kTileN + L.nsub * kTileN * 2, &sg.tz, n0, srow, full + rs, pol);
+          uint8_t* sz = raw_sz(rs, j, s);
+          tma_load_2d(sz, &sg.ts, n0, srow, full + rs, pol);
+          if (sg.has_z) tma_load_2d(sz + L.nsub * kTileN * 2, &sg.tz, n0, srow, full + rs, pol);
         }
       }
     }
@@ -321,10 +335,13 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
           const uint32_t b_row = smem_u32(bop + (i >> 1) * NM * 128) + (i & 1) * 64;
 #pragma unroll
           for (int s = 0; s < NS; ++s) {
-            const uint32_t a_addr = smem_u32(WB == 8 ? raw_stage(rs, j, s) : a_tile(as, j, s));
+            // kk = 0 / 1: K rows 0-31 / 32-63 of the group: W8 rows of the
+            // weight tile; W4 the ring tile, then the tile unpacked in place.
+            const uint32_t w_addr = smem_u32(raw_w(rs, j, s));
 #pragma unroll
             for (int kk = 0; kk < 2; ++kk) {
-              const uint64_t ad = smem_desc(a_addr + 4096 * kk, 8192, 1024, kLayoutSw128);
+              const uint32_t src = WB == 8 ? w_addr + 4096 * kk : (kk == 0 ? smem_u32(a_tile(as, j, s)) : w_addr);
+              const uint64_t ad = smem_desc(src, 8192, 1024, kLayoutSw128);
               const uint64_t bd = smem_desc(b_row + 32 * kk, 16, 1024, kLayoutSw128);
               const uint32_t d = tbase + tcol(tb, j, s, NSUB == 2 ? kk : 0);
               tc_mma_i8(d, ad, bd, idesc, NSUB == 2 ? 0u : static_cast<uint32_t>(kk));
@@ -407,9 +424,9 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
 #pragma unroll
           for (int s = 0; s < NS; ++s) {
             const GemvSeg& sg = NS == 1 ? S0 : p.seg[s];
-            const uint8_t* st = raw_stage(rs, j, s);
-            const uint16_t* sc = reinterpret_cast<const uint16_t*>(st + 32 * kTileN);
-            const uint8_t* zz = st + 32 * kTileN + L.nsub * kTileN * 2;
+            const uint8_t* st = raw_sz(rs, j, s);
+            const uint16_t* sc = reinterpret_cast<const uint16_t*>(st);
+            const uint8_t* zz = st + L.nsub * kTileN * 2;
             for (int sub = 0; sub < NSUB; ++sub) {
               const float ws = bf16_bits_to_f32(sc[sub * kTileN + c]);
               const int z = sg.has_z ? static_cast<int>(zz[sub * kTileN + c]) : 8;
@@ -441,35 +458,59 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
     }
   } else if constexpr (WB == 4) {
     // ------------------------------------------------------------------ W4 unpack
+    // Packed row r of a group's tile holds k = 2r (low nibbles) and 2r + 1
+    // (high nibbles) for 128 columns.  K rows 0-31 (packed rows 0-15) go to
+    // the ring tile and K rows 32-63 (packed rows 16-31) are written in place
+    // over the packed tile, both in the 128-byte-swizzled MN-major operand
+    // layout the tensor-map load produced.  Thread u owns packed rows u/8 and
+    // u/8 + 16 in 16-column chunk u%8; the in-place writes wait on a barrier
+    // of the 128 unpack threads until every packed row has been read.
     const int u = threadIdx.x - kTcWarpUnpack * 32;
+    const int pr = u >> 3, ch = u & 7;
+    auto chunk = [&](int r) { return r * kTileN + ((ch ^ (r & 7)) << 4); };
+    auto lo4 = [](const uint4& v) {
+      return make_uint4(v.x & 0x0F0F0F0Fu, v.y & 0x0F0F0F0Fu, v.z & 0x0F0F0F0Fu, v.w & 0x0F0F0F0Fu);
+    };
+    auto hi4 = [](const uint4& v) {
+      return make_uint4((v.x >> 4) & 0x0F0F0F0Fu, (v.y >> 4) & 0x0F0F0F0Fu, (v.z >> 4) & 0x0F0F0F0Fu,
+                        (v.w >> 4) & 0x0F0F0F0Fu);
+    };
+    constexpr int kChunkTiles = 4;  // tiles read per barrier
     for (int b = 0; b < nbatch; ++b) {
       const int rs = b % RB;
       const int as = b % AB;
-      if (!mbar_wait(full + rs, (b / RB) & 1) || !mbar_wait(aempty + as, ((b / AB) & 1) ^ 1)) {
+      const bool waited = mbar_wait(full + rs, (b / RB) & 1) && mbar_wait(aempty + as, ((b / AB) & 1) ^ 1);
+      const int nt = batch_len(b) * NS;
+      bool ok = true;
+      for (int t0 = 0; t0 < nt; t0 += kChunkTiles) {
+        uint4 v0[kChunkTiles], v1[kChunkTiles];
+#pragma unroll
+        for (int q = 0; q < kChunkTiles; ++q) {
+          if (t0 + q >= nt) break;
+          const uint8_t* wt = raw_w(rs, (t0 + q) / NS, (t0 + q) % NS);
+          v0[q] = *reinterpret_cast<const uint4*>(wt + chunk(pr));
+          v1[q] = *reinterpret_cast<const uint4*>(wt + chunk(pr + 16));
+        }
+        // (the first barrier of a batch also agrees on the waits' outcome, so
+        // that all 128 threads leave together after a timed-out wait)
+        if (t0 == 0) ok = named_bar_and(3, 128, waited);
+        else named_bar_sync(3, 128);
+        if (!ok) break;
+#pragma unroll
+        for (int q = 0; q < kChunkTiles; ++q) {
+          if (t0 + q >= nt) break;
+          const int j = (t0 + q) / NS, s = (t0 + q) % NS;
+          uint8_t* wt = raw_w(rs, j, s);
+          uint8_t* at = a_tile(as, j, s);
+          *reinterpret_cast<uint4*>(at + chunk(2 * pr)) = lo4(v0[q]);
+          *reinterpret_cast<uint4*>(at + chunk(2 * pr + 1)) = hi4(v0[q]);
+          *reinterpret_cast<uint4*>(wt + chunk(2 * pr)) = lo4(v1[q]);
+          *reinterpret_cast<uint4*>(wt + chunk(2 * pr + 1)) = hi4(v1[q]);
+        }
+      }
+      if (!ok) {
         if (lane == 0) atomicOr(p.fault, kFaultFullWait);
         break;
-      }
-      const int nb = batch_len(b);
-      for (int j = 0; j < nb; ++j) {
-#pragma unroll
-        for (int s = 0; s < NS; ++s) {
-          const uint8_t* st = raw_stage(rs, j, s);
-          uint8_t* at = a_tile(as, j, s);
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            const int pr = (u >> 3) + 16 * hh;  // packed row: K = 2*pr (low), 2*pr + 1 (high)
-            const int ch = u & 7;               // 16-byte chunk = 16 columns
-            const uint4 v = *reinterpret_cast<const uint4*>(st + pr * kTileN + ch * 16);
-            uint4 lo, hi;
-            lo.x = v.x & 0x0F0F0F0Fu; hi.x = (v.x >> 4) & 0x0F0F0F0Fu;
-            lo.y = v.y & 0x0F0F0F0Fu; hi.y = (v.y >> 4) & 0x0F0F0F0Fu;
-            lo.z = v.z & 0x0F0F0F0Fu; hi.z = (v.z >> 4) & 0x0F0F0F0Fu;
-            lo.w = v.w & 0x0F0F0F0Fu; hi.w = (v.w >> 4) & 0x0F0F0F0Fu;
-            const int r0 = 2 * pr, r1 = 2 * pr + 1;
-            *reinterpret_cast<uint4*>(at + r0 * kTileN + ((ch ^ (r0 & 7)) << 4)) = lo;
-            *reinterpret_cast<uint4*>(at + r1 * kTileN + ((ch ^ (r1 & 7)) << 4)) = hi;
-          }
-        }
       }
       fence_proxy_async_smem();
       mbar_arrive(afull + as);

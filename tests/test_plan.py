@@ -33,28 +33,26 @@ def check_plan(pl, wbits, gate_up, M, K, wgrp):
     per_buf = ns * nsub * nm
     assert pl["nbb"] * pl["bs"] * per_buf <= TMEM_SHARE
     single = pl["bs"] == pl["gmax"] and pl["rb"] == 1
-    resident = wbits == 4 and gate_up and pl["bs"] == 1 and pl["rb"] == pl["gmax"] > 1
     if single:
         assert pl["nbb"] == 1 and pl["ab"] == (1 if wbits == 4 else 0)
-    elif resident:
-        assert 2 <= pl["ab"] <= min(pl["gmax"], 4) or pl["ab"] == pl["gmax"] == 1
-        assert pl["nbb"] == min(pl["gmax"], TMEM_SHARE // per_buf)
     else:
         assert pl["rb"] in (2, 3, 4) and pl["nbb"] == 2 and pl["ab"] == (2 if wbits == 4 else 0)
-    assert pl["level"] == (2 if single else 1 if resident else 0)
+    assert pl["level"] == (2 if single else 0)
     if pl["alias"]:
-        # the partial sums of ranks 1..split-1 fit rank 0's operand region
-        assert pl["split"] >= 2 and pl["level"] >= 1
+        # the partial sums of ranks 1..split-1 fit rank 0's operand region:
+        # W4 ring tiles of 32 rows (high nibbles, groups of 64 k) or 64 rows
+        # (both nibbles, groups of 32); W8 weight tiles of 64 rows
+        assert pl["split"] >= 2 and pl["level"] == 2
         part = (pl["split"] - 1) * ns * pl["mr"] * 128 * 4
-        op = (pl["ab"] * pl["bs"] * ns * 64 * 128 if wbits == 4
-              else pl["rb"] * pl["bs"] * ns * 64 * 128)
+        rows = (64 if wgrp == 32 else 32) if wbits == 4 else 64
+        op = (pl["ab"] if wbits == 4 else pl["rb"]) * pl["bs"] * ns * rows * 128
         assert part <= op
 
 
 @pytest.mark.parametrize("wbits,gate_up,M,K,N,wgrp,split,level", [
     (8, 0, 1, 2048, 6144, 64, 4, 2),      # config 1: W8 projection at decode, one batch
-    (4, 1, 4, 2048, 6144, 128, 5, 1),     # config 2: fused gate/up, packed weights resident
-    (4, 1, 1, 2048, 6144, 128, 5, 1),
+    (4, 1, 4, 2048, 6144, 128, 4, 0),     # config 2: fused gate/up, streamed within the CTA target
+    (4, 1, 1, 2048, 6144, 128, 4, 0),
     (4, 0, 4, 6144, 2048, 128, 8, 0),     # config 2: down projection (K = 6144), streamed
     (4, 0, 1, 2048, 2048, 128, 8, 2),     # config 2: o projection
     (4, 0, 4, 2048, 4096, 128, 6, 2),     # config 2: qkv + gate projection
