@@ -209,6 +209,8 @@ int tune_ctas_per_sm() { static const int v = env_int("QLIN_TUNE_CTAS_PER_SM", 0
 int tune_max_level() { static const int v = env_int("QLIN_TUNE_MAX_LEVEL", 2); return v; }
 int tune_stream_budget() { static const int v = env_int("QLIN_TUNE_STREAM_BUDGET_KB", 0); return v; }
 int tune_max_cluster() { static const int v = env_int("QLIN_TUNE_MAX_CLUSTER", 8); return v; }
+// Weight-ring slots of a streamed plan (0: 3 for short launches, 4 for long ones).
+int tune_rb_max() { static const int v = env_int("QLIN_TUNE_RB_MAX", 0); return v; }
 // Rows from which W8 projections take the tensor-core GEMM (prefill) path.
 int prefill_min_m() { static const int v = env_int("QLIN_PREFILL_MIN_M", 128); return v; }
 
@@ -366,8 +368,10 @@ void plan_batches(int wb, int mr, int ns, int wgrp, long long ctas, int sms, boo
     // batch) that fit, preferring larger batches (fewer hand-offs).
     const int ab = wb == 4 ? 2 : 0;
     int best_bs = 1, best_rb = 2;
-    // (short launches keep two slots: measured best for the config-2 shapes)
-    for (int rb = 2; rb <= (long_stream ? 4 : 2); ++rb) {
+    // (three slots for short launches: measured on the config-2 shapes, the
+    // fused gate/up takes 9.9 us with three, 10.6 us with two)
+    const int rb_max = tune_rb_max() > 0 ? tune_rb_max() : long_stream ? 4 : 3;
+    for (int rb = 2; rb <= rb_max; ++rb) {
       const TcLayout one = tc_layout(wb, mr, ns, wgrp, gmax, 1, rb, ab, 2, s, 0);
       const uint32_t per_group = rb * base.raw_stage + (wb == 4 ? ab * ns * base.atile : 0);
       const uint32_t fixed = one.total - per_group;
@@ -412,7 +416,7 @@ TcPlan plan_tc(int wb, int mr, int ns, int K, int wgrp, int tiles, int rowblocks
   const long long two_per_sm = 2ll * sms;
   // Per plan level: the largest split within the CTA target, and the
   // smallest split beyond it (within two CTAs per SM).
-  TcPlan in[3] = {}, up[3] = {}, any{}, stream{};
+  TcPlan in[3] = {}, up[3] = {}, any{}, stream{}, compact{};
   long long stream_inflight = -1;
   // Weight bytes of the launch: past ~16 MB (the config-2 launches are at
   // most 13 MB) the launch is a long HBM stream rather than a short step
@@ -445,11 +449,21 @@ TcPlan plan_tc(int wb, int mr, int ns, int K, int wgrp, int tiles, int rowblocks
       }
       continue;
     }
+    // One-batch plans with at most one CTA per SM, at most 8 groups per CTA
+    // and clusters of at most 6 (the largest such split).
+    if (pl.level == 2 && ctas <= sms && pl.gmax <= 8 && s <= 6) compact = pl;
     const bool within = ctas <= target;
     if (within || (s == 1 && in[pl.level].split == 0)) in[pl.level] = pl;
     else if (ctas <= two_per_sm && up[pl.level].split == 0) up[pl.level] = pl;
   }
   if (long_stream) in[0] = stream, up[0] = TcPlan{};
+  // A compact one-batch plan first.  Measured on B200 (config-2 shapes): the
+  // o projection (16 tiles, K = 2048) takes 4.1 us at split 6 (96 CTAs) and
+  // 4.6 us at split 8; the qkv projection (32 tiles) 5.1 us at split 4 (128
+  // CTAs) and 5.6 us at split 6 (192 CTAs).  Where none exists (the W8
+  // config-1 GEMV needs 11 groups per CTA at split 3, and is fastest at split
+  // 4 with 192 CTAs), the CTA-target rule below applies.
+  if (compact.split) return compact;
   // Within the CTA target, the highest level first (more of the work ahead
   // of the grid dependency); only then beyond the target, where extra splits
   // add combine work, the smallest one.  Measured on B200 with the W4

@@ -54,8 +54,8 @@ def check_plan(pl, wbits, gate_up, M, K, wgrp):
     (4, 1, 4, 2048, 6144, 128, 4, 0),     # config 2: fused gate/up, streamed within the CTA target
     (4, 1, 1, 2048, 6144, 128, 4, 0),
     (4, 0, 4, 6144, 2048, 128, 8, 0),     # config 2: down projection (K = 6144), streamed
-    (4, 0, 1, 2048, 2048, 128, 8, 2),     # config 2: o projection
-    (4, 0, 4, 2048, 4096, 128, 6, 2),     # config 2: qkv + gate projection
+    (4, 0, 1, 2048, 2048, 128, 6, 2),     # config 2: o projection, compact one-batch plan
+    (4, 0, 4, 2048, 4096, 128, 4, 2),     # config 2: qkv + gate projection, compact one-batch plan
 ])
 def test_config_plans(pkg, wbits, gate_up, M, K, N, wgrp, split, level):
     pl = pkg._lib.plan_small_m(wbits, gate_up, M, K, tiles_of(N), wgrp, SMS)
