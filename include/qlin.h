@@ -168,9 +168,17 @@ int qlin_peer_allgather(void* const* bufs, void* const* arrive, void* expected, 
  * weight-ring slots, unpacked-ring slots, accumulator buffers, dynamic
  * shared memory bytes, activation rows per row block, 1 if the split-K
  * partial sums reuse rank 0's operand region, plan level (2: one batch,
- * 1: W4 packed weights resident with an unpacked ring, 0: streamed). */
+ * 0: streamed).  Needs no GPU: clusters are counted by shared-memory slots,
+ * whereas a launch also checks the device's resident-cluster capacity
+ * (qlin_max_active_clusters) and may then choose another split. */
 int qlin_plan_small_m(int wbits, int gate_up, int64_t M, int64_t K, int64_t tiles, int64_t wgrp,
                       int sms, int64_t* out);
+
+/* Diagnostic: clusters of `split` CTAs with `smem` bytes of dynamic shared
+ * memory that the current device keeps resident at once, for the small-M
+ * kernel instance serving (wbits, gate_up, M)
+ * (cudaOccupancyMaxActiveClusters).  Needs a CUDA device. */
+int qlin_max_active_clusters(int wbits, int gate_up, int64_t M, int split, int64_t smem, int64_t* out);
 
 #ifdef __cplusplus
 }

@@ -32,6 +32,7 @@ SIGNATURES = {
     "qlin_mlp_gate_up_quant_w4": [_P, _P, _I, _I, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P],
     "qlin_quant_row": [_P, _I, _I, _I, _P, _P, _P],
     "qlin_plan_small_m": [ctypes.c_int, ctypes.c_int, _I, _I, _I, _I, ctypes.c_int, _P],
+    "qlin_max_active_clusters": [ctypes.c_int, ctypes.c_int, _I, ctypes.c_int, _I, ctypes.POINTER(ctypes.c_int64)],
     "qlin_ipc_get_handle": [_P, _P, ctypes.POINTER(ctypes.c_int64)],
     "qlin_ipc_open": [_P, _I, ctypes.POINTER(ctypes.c_void_p)],
     "qlin_ipc_close": [_P, _I],

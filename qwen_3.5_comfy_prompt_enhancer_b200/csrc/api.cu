@@ -410,7 +410,32 @@ void plan_batches(int wb, int mr, int ns, int wgrp, long long ctas, int sms, boo
 // the best split is the largest one (up to 8) that keeps the launch at about
 // 1.3 CTAs per SM: more CTAs leave clusters waiting for the previous
 // launch's CTAs to retire, fewer leave HBM under-subscribed.
-TcPlan plan_tc(int wb, int mr, int ns, int K, int wgrp, int tiles, int rowblocks, int sms) {
+int active_clusters(int wb, int mr, int ns, int split, size_t smem);
+
+// Clusters of `s` CTAs that stay resident at once for a plan with `smem`
+// bytes and `tmem_cols` tensor-memory columns per CTA, or -1 without a
+// device.  A cluster must fit one GPC, so the count depends on the GPCs'
+// sizes, not only on the SM count: on B200, clusters of 7 CTAs at one CTA
+// per SM place only 15 at once (105 CTAs), clusters of 6 place 22.
+// cudaOccupancyMaxActiveClusters counts one CTA per SM; with two per SM a
+// GPC of g SMs offers 2g slots, so a cluster of s places like one of s/2
+// (the mean of the two neighbours for odd s).
+long long cluster_capacity(int wb, int mr, int ns, int s, size_t smem, uint32_t tmem_cols) {
+  long long per_sm = (228 * 1024) / (static_cast<long long>(smem) + 1024);
+  const long long by_tmem = tmem_cols ? 512 / tmem_cols : 1;
+  if (by_tmem < per_sm) per_sm = by_tmem;
+  auto c1 = [&](int x) { return static_cast<long long>(active_clusters(wb, mr, ns, x, smem)); };
+  if (per_sm <= 1) return c1(s);
+  if (s == 1) {
+    const long long a = c1(1);
+    return a < 0 ? -1 : 2 * a;
+  }
+  if (s % 2 == 0) return c1(s / 2);
+  const long long a = c1((s - 1) / 2), b = c1((s + 1) / 2);
+  return (a < 0 || b < 0) ? -1 : (a + b) / 2;
+}
+
+TcPlan plan_tc(int wb, int mr, int ns, int K, int wgrp, int tiles, int rowblocks, int sms, bool query) {
   const int G = K / kGroup;
   const long long target = (static_cast<long long>(sms) * 4 + 2) / 3;  // ~1.33 CTAs per SM
   const long long two_per_sm = 2ll * sms;
@@ -433,13 +458,18 @@ TcPlan plan_tc(int wb, int mr, int ns, int K, int wgrp, int tiles, int rowblocks
     if (pl.smem > kTcMaxSmem) continue;
     if (tune_split() == s) return pl;
     if (any.split == 0) any = pl;  // smallest feasible split, whatever its size
+    const TcLayout L = tc_layout(wb, mr, ns, wgrp, pl.gmax, pl.bs, pl.rb, pl.ab, pl.nbb, s, pl.alias);
+    // Resident clusters (from the device's GPC layout when it is queried)
+    // and whether the launch's clusters fit in one wave.
+    const long long clusters = static_cast<long long>(tiles) * rowblocks;
+    const long long cap = query ? cluster_capacity(wb, mr, ns, s, pl.smem, L.tmem_cols) : -1;
+    const bool one_wave = cap < 0 || clusters <= cap;
     if (pl.level == 0 && long_stream) {
       // Long streamed launches are bound by the weight bytes in flight over
       // the whole GPU: resident CTAs x ring slots x groups per batch, divided
       // by the waves the launch needs (measured on the config-5 shapes).
-      const TcLayout L = tc_layout(wb, mr, ns, wgrp, pl.gmax, pl.bs, pl.rb, pl.ab, pl.nbb, s, pl.alias);
       const long long per_sm = (228 * 1024) / (static_cast<long long>(pl.smem) + 1024);
-      const long long slots = sms * (per_sm < 1 ? 1 : per_sm);
+      const long long slots = cap > 0 ? cap * s : sms * (per_sm < 1 ? 1 : per_sm);
       const long long resident = ctas < slots ? ctas : slots;
       const long long waves = (ctas + slots - 1) / slots;  // a second wave serialises behind the first
       const long long inflight = resident * pl.rb * pl.bs * L.raw_stage / waves;
@@ -451,10 +481,10 @@ TcPlan plan_tc(int wb, int mr, int ns, int K, int wgrp, int tiles, int rowblocks
     }
     // One-batch plans with at most one CTA per SM, at most 8 groups per CTA
     // and clusters of at most 6 (the largest such split).
-    if (pl.level == 2 && ctas <= sms && pl.gmax <= 8 && s <= 6) compact = pl;
-    const bool within = ctas <= target;
+    if (pl.level == 2 && ctas <= sms && pl.gmax <= 8 && s <= 6 && one_wave) compact = pl;
+    const bool within = ctas <= target && one_wave;
     if (within || (s == 1 && in[pl.level].split == 0)) in[pl.level] = pl;
-    else if (ctas <= two_per_sm && up[pl.level].split == 0) up[pl.level] = pl;
+    else if (ctas <= two_per_sm && one_wave && up[pl.level].split == 0) up[pl.level] = pl;
   }
   if (long_stream) in[0] = stream, up[0] = TcPlan{};
   // A compact one-batch plan first.  Measured on B200 (config-2 shapes): the
@@ -477,8 +507,9 @@ TcPlan plan_tc(int wb, int mr, int ns, int K, int wgrp, int tiles, int rowblocks
   return any;
 }
 
+// Opt the kernel instance in to the full dynamic shared memory (once per device).
 template <int WB, int MR, int EPI>
-int launch_tc_t(const GemvArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
+int configure_tc() {
   auto kern = tc_gemv_kernel<WB, MR, EPI>;
   static std::atomic<unsigned long long> configured{0};
   int dev = 0;
@@ -489,6 +520,90 @@ int launch_tc_t(const GemvArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(smem)");
     configured.fetch_or(bit);
   }
+  return QLIN_OK;
+}
+
+// Clusters of `split` CTAs with `smem` bytes each that the device keeps
+// resident at once (cudaOccupancyMaxActiveClusters: it accounts for the
+// GPC a cluster must fit in, registers and shared memory), or -1.
+template <int WB, int MR, int EPI>
+int active_clusters_t(int split, size_t smem) {
+  if (configure_tc<WB, MR, EPI>() != QLIN_OK) return -1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(split, 1, 1);
+  cfg.blockDim = dim3(tc_threads(WB), 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = split;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, tc_gemv_kernel<WB, MR, EPI>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  return n;
+}
+
+template <int WB, int EPI>
+int active_clusters_mr(int mr, int split, size_t smem) {
+  switch (mr) {
+    case 1: return active_clusters_t<WB, 1, EPI>(split, smem);
+    case 2: return active_clusters_t<WB, 2, EPI>(split, smem);
+    case 4: return active_clusters_t<WB, 4, EPI>(split, smem);
+    case 8: return active_clusters_t<WB, 8, EPI>(split, smem);
+    case 16: return active_clusters_t<WB, 16, EPI>(split, smem);
+    default:
+      if constexpr (WB == 8) return active_clusters_t<WB, 32, EPI>(split, smem);
+      return -1;
+  }
+}
+
+struct ClusterKey {
+  int dev, wb, mr, ns, split;
+  size_t smem;
+  bool operator==(const ClusterKey& o) const {
+    return dev == o.dev && wb == o.wb && mr == o.mr && ns == o.ns && split == o.split && smem == o.smem;
+  }
+};
+struct ClusterKeyHash {
+  size_t operator()(const ClusterKey& k) const {
+    uint64_t h = mix64(static_cast<uint64_t>(k.smem), (static_cast<uint64_t>(k.dev) << 32) | k.split);
+    return static_cast<size_t>(mix64(h, (static_cast<uint64_t>(k.wb) << 16) | (k.mr << 4) | k.ns));
+  }
+};
+
+// Resident-cluster capacity of the small-M kernel for a plan (cached), or -1
+// when no device answers (the planner then counts shared-memory slots).
+int active_clusters(int wb, int mr, int ns, int split, size_t smem) {
+  static std::mutex mu;
+  static std::unordered_map<ClusterKey, int, ClusterKeyHash> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  const ClusterKey k{dev, wb, mr, ns, split, smem};
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto it = cache.find(k);
+    if (it != cache.end()) return it->second;
+  }
+  int n;
+  if (wb == 8) n = ns == 1 ? active_clusters_mr<8, kEpiOut>(mr, split, smem) : active_clusters_mr<8, kEpiSiluQuant>(mr, split, smem);
+  else n = ns == 1 ? active_clusters_mr<4, kEpiOut>(mr, split, smem) : active_clusters_mr<4, kEpiSiluQuant>(mr, split, smem);
+  std::lock_guard<std::mutex> g(mu);
+  cache.emplace(k, n);
+  return n;
+}
+
+template <int WB, int MR, int EPI>
+int launch_tc_t(const GemvArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
+  auto kern = tc_gemv_kernel<WB, MR, EPI>;
+  if (int r = configure_tc<WB, MR, EPI>()) return r;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(tc_threads(WB), 1, 1);
@@ -525,14 +640,14 @@ int launch_tc_mr(int mr, const GemvArgs& a, dim3 grid, size_t smem, cudaStream_t
 // Row block and K split for the tcgen05 path.  Row blocks of 32 rows hold
 // the largest activation and partial-sum buffers; when no split of K fits
 // shared memory, 16-row blocks are used.  Returns QLIN_OK or an error.
-int choose_tc_uncached(int wb, int ns, int64_t M, int K, int wgrp, int tiles, int sms, int* mr_out,
+int choose_tc_uncached(int wb, int ns, int64_t M, int K, int wgrp, int tiles, int sms, bool query, int* mr_out,
                        int* rowblocks_out, TcPlan* pl_out) {
   int mr = tc_mr(wb, M);
   for (;;) {
     const int nm = mr < 16 ? 16 : mr;
     const int64_t rowblocks = (M + nm - 1) / nm;
     if (rowblocks > 65535 || tiles > 65535) return fail(QLIN_ERR_SHAPE, "grid too large (M=%lld)", (long long)M);
-    const TcPlan pl = plan_tc(wb, mr, ns, K, wgrp, tiles, static_cast<int>(rowblocks), sms);
+    const TcPlan pl = plan_tc(wb, mr, ns, K, wgrp, tiles, static_cast<int>(rowblocks), sms, query);
     if (pl.split > 0) {
       *mr_out = mr;
       *rowblocks_out = static_cast<int>(rowblocks);
@@ -548,10 +663,11 @@ int choose_tc_uncached(int wb, int ns, int64_t M, int K, int wgrp, int tiles, in
 // The plan depends only on these inputs (the tuning overrides are read once
 // per process), so it is computed once per shape and looked up afterwards.
 struct TcKey {
-  int wb, ns, K, wgrp, tiles, sms;
+  int wb, ns, K, wgrp, tiles, sms, dev;  // dev = -1: planned without querying a device
   int64_t M;
   bool operator==(const TcKey& o) const {
-    return wb == o.wb && ns == o.ns && K == o.K && wgrp == o.wgrp && tiles == o.tiles && sms == o.sms && M == o.M;
+    return wb == o.wb && ns == o.ns && K == o.K && wgrp == o.wgrp && tiles == o.tiles && sms == o.sms &&
+           dev == o.dev && M == o.M;
   }
 };
 struct TcKeyHash {
@@ -559,6 +675,7 @@ struct TcKeyHash {
     uint64_t h = static_cast<uint64_t>(k.M);
     h = mix64(h, (static_cast<uint64_t>(k.wb) << 40) ^ (static_cast<uint64_t>(k.ns) << 32) ^ static_cast<uint32_t>(k.K));
     h = mix64(h, (static_cast<uint64_t>(static_cast<uint32_t>(k.wgrp)) << 32) ^ static_cast<uint32_t>(k.tiles));
+    h = mix64(h, static_cast<uint64_t>(static_cast<uint32_t>(k.dev)));
     return static_cast<size_t>(mix64(h, static_cast<uint64_t>(k.sms)));
   }
 };
@@ -576,9 +693,17 @@ PlanCache& plan_cache() {
   return c;
 }
 
-int choose_tc(int wb, int ns, int64_t M, int K, int wgrp, int tiles, int sms, int* mr_out, int* rowblocks_out,
-              TcPlan* pl_out) {
-  const TcKey k{wb, ns, K, wgrp, tiles, sms, M};
+// `query`: plan with the current device's cluster capacity (launch path);
+// without it (the CPU plan query) clusters are counted by shared-memory slots.
+int choose_tc(int wb, int ns, int64_t M, int K, int wgrp, int tiles, int sms, bool query, int* mr_out,
+              int* rowblocks_out, TcPlan* pl_out) {
+  int dev = -1;
+  if (query && cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    dev = -1;
+    query = false;
+  }
+  const TcKey k{wb, ns, K, wgrp, tiles, sms, dev, M};
   PlanCache& c = plan_cache();
   {
     std::lock_guard<std::mutex> g(c.mu);
@@ -591,7 +716,7 @@ int choose_tc(int wb, int ns, int64_t M, int K, int wgrp, int tiles, int sms, in
     }
   }
   TcChoice ch{};
-  if (int r = choose_tc_uncached(wb, ns, M, K, wgrp, tiles, sms, &ch.mr, &ch.rowblocks, &ch.pl)) return r;
+  if (int r = choose_tc_uncached(wb, ns, M, K, wgrp, tiles, sms, query, &ch.mr, &ch.rowblocks, &ch.pl)) return r;
   {
     std::lock_guard<std::mutex> g(c.mu);
     if (c.plans.size() >= kPlanCache) c.plans.clear();
@@ -609,7 +734,7 @@ int run_tc(int wb, int epi, GemvArgs& a, int tiles, cudaStream_t st) {
   const int ns = epi == kEpiOut ? 1 : 2;
   int mr = 0, rowblocks = 0;
   TcPlan pl{};
-  if (int r = choose_tc(wb, ns, a.M, a.K, a.wgrp, tiles, di.sms, &mr, &rowblocks, &pl)) return r;
+  if (int r = choose_tc(wb, ns, a.M, a.K, a.wgrp, tiles, di.sms, true, &mr, &rowblocks, &pl)) return r;
   const int nm = mr < 16 ? 16 : mr;
   if (int r = make_map(&a.ta, a.a_q, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.K, a.M, a.K, 128, nm, true)) return r;
   a.split = pl.split;
@@ -985,11 +1110,21 @@ int qlin_plan_small_m(int wbits, int gate_up, int64_t M, int64_t K, int64_t tile
   int mr = 0, rowblocks = 0;
   TcPlan pl{};
   if (int r = choose_tc(wbits, gate_up ? 2 : 1, M, static_cast<int>(K), wbits == 4 ? static_cast<int>(wgrp) : 64,
-                        static_cast<int>(tiles > 65536 ? 65536 : tiles), sms, &mr, &rowblocks, &pl))
+                        static_cast<int>(tiles > 65536 ? 65536 : tiles), sms, false, &mr, &rowblocks, &pl))
     return r;
   const int64_t v[10] = {pl.split, pl.gmax, pl.bs, pl.rb, pl.ab, pl.nbb, static_cast<int64_t>(pl.smem), mr,
                          pl.alias, pl.level};
   for (int i = 0; i < 10; ++i) out[i] = v[i];
+  return QLIN_OK;
+}
+
+int qlin_max_active_clusters(int wbits, int gate_up, int64_t M, int split, int64_t smem, int64_t* out) {
+  if ((wbits != 8 && wbits != 4) || !out || M <= 0 || split < 1 || split > kMaxCluster || smem < 0 ||
+      smem > static_cast<int64_t>(kTcMaxSmem))
+    return fail(QLIN_ERR_INVALID_ARGUMENT, "bad cluster query");
+  const int n = active_clusters(wbits, tc_mr(wbits, M), gate_up ? 2 : 1, split, static_cast<size_t>(smem));
+  if (n < 0) return fail(QLIN_ERR_CUDA, "cudaOccupancyMaxActiveClusters unavailable");
+  *out = n;
   return QLIN_OK;
 }
 
