@@ -168,9 +168,11 @@ int qlin_peer_allgather(void* const* bufs, void* const* arrive, void* expected, 
  * weight-ring slots, unpacked-ring slots, accumulator buffers, dynamic
  * shared memory bytes, activation rows per row block, 1 if the split-K
  * partial sums reuse rank 0's operand region, plan level (2: one batch,
- * 0: streamed).  Needs no GPU: clusters are counted by shared-memory slots,
- * whereas a launch also checks the device's resident-cluster capacity
- * (qlin_max_active_clusters) and may then choose another split. */
+ * 0: streamed).  With sms > 0 it needs no GPU: clusters are counted by
+ * shared-memory slots, whereas a launch also checks the device's
+ * resident-cluster capacity (qlin_max_active_clusters) and may then choose
+ * another split.  sms = 0 gives exactly the plan a launch on the current
+ * device gets. */
 int qlin_plan_small_m(int wbits, int gate_up, int64_t M, int64_t K, int64_t tiles, int64_t wgrp,
                       int sms, int64_t* out);
 

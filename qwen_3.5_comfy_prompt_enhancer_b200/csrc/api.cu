@@ -1102,15 +1102,23 @@ int qlin_peer_allgather(void* const* bufs, void* const* arrive, void* expected, 
 
 int qlin_plan_small_m(int wbits, int gate_up, int64_t M, int64_t K, int64_t tiles, int64_t wgrp, int sms,
                       int64_t* out) {
-  if ((wbits != 8 && wbits != 4) || !out || M <= 0 || tiles <= 0 || sms <= 0)
+  if ((wbits != 8 && wbits != 4) || !out || M <= 0 || tiles <= 0 || sms < 0)
     return fail(QLIN_ERR_INVALID_ARGUMENT, "bad plan query");
+  // sms = 0: the plan a launch on the current device gets (its SM count and
+  // resident-cluster capacity).
+  const bool on_device = sms == 0;
+  if (on_device) {
+    DevInfo di;
+    if (int r = device_info(&di)) return r;
+    sms = di.sms;
+  }
   if (K <= 0 || K % kGroup != 0 || K > (1ll << 30)) return fail(QLIN_ERR_SHAPE, "K=%lld", (long long)K);
   if (wbits == 4)
     if (int r = check_wgrp(K, wgrp)) return r;
   int mr = 0, rowblocks = 0;
   TcPlan pl{};
   if (int r = choose_tc(wbits, gate_up ? 2 : 1, M, static_cast<int>(K), wbits == 4 ? static_cast<int>(wgrp) : 64,
-                        static_cast<int>(tiles > 65536 ? 65536 : tiles), sms, false, &mr, &rowblocks, &pl))
+                        static_cast<int>(tiles > 65536 ? 65536 : tiles), sms, on_device, &mr, &rowblocks, &pl))
     return r;
   const int64_t v[10] = {pl.split, pl.gmax, pl.bs, pl.rb, pl.ab, pl.nbb, static_cast<int64_t>(pl.smem), mr,
                          pl.alias, pl.level};

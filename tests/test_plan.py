@@ -92,3 +92,48 @@ def test_plan_rejects_bad_query(pkg):
         pkg._lib.plan_small_m(8, 0, 1, 100, 16, 64, SMS)
     with pytest.raises(pkg._lib.QlinError):
         pkg._lib.plan_small_m(4, 0, 1, 2048, 16, 48, SMS)
+
+
+@pytest.mark.gpu
+def test_cluster_capacity_query(pkg):
+    """qlin_max_active_clusters answers on a GPU, never grows with the cluster
+    size, and never exceeds the SM count divided by the cluster size."""
+    import ctypes
+    import torch
+    torch.zeros(1, device="cuda:0")
+    lib = pkg._lib.load()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    out = ctypes.c_int64()
+    prev = None
+    for split in range(1, 9):
+        assert lib.qlin_max_active_clusters(4, 1, 4, split, 100 * 1024, ctypes.byref(out)) == 0
+        assert 1 <= out.value <= sms // split
+        if prev is not None:
+            assert out.value <= prev
+        prev = out.value
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("gate_up,M,K,N", [
+    (1, 1, 5120, 17408), (1, 4, 5120, 17408),       # config 5 gate/up on 1 GPU
+    (0, 1, 17408, 5120), (0, 4, 17408, 5120),       # config 5 down on 1 GPU
+    (0, 1, 17408, 2560), (1, 1, 5120, 4352),        # per-rank shapes of the 2- and 4-way splits
+])
+def test_launch_plans_fit_one_wave_of_clusters(pkg, gate_up, M, K, N):
+    """On the device, the chosen plan's clusters are resident at once when any
+    split allows that (the planner ranks second-wave plans last)."""
+    import ctypes
+    import torch
+    torch.zeros(1, device="cuda:0")
+    lib = pkg._lib.load()
+    pl = pkg._lib.plan_small_m(4, gate_up, M, K, tiles_of(N), 128, 0)
+    check_plan(pl, 4, gate_up, M, K, 128)
+    out = ctypes.c_int64()
+    assert lib.qlin_max_active_clusters(4, gate_up, M, pl["split"], pl["smem"], ctypes.byref(out)) == 0
+    per_sm = min(2, (228 * 1024) // (pl["smem"] + 1024))
+    cap = out.value
+    if per_sm >= 2:  # the query counts one CTA per SM; the planner's estimate for two per SM
+        s = pl["split"]
+        c = lambda x: (lib.qlin_max_active_clusters(4, gate_up, M, x, pl["smem"], ctypes.byref(out)), out.value)[1]
+        cap = 2 * c(1) if s == 1 else c(s // 2) if s % 2 == 0 else (c((s - 1) // 2) + c((s + 1) // 2)) // 2
+    assert tiles_of(N) <= cap, (pl, cap)
