@@ -907,9 +907,25 @@ int run_prefill_w4(int epi, const GemvArgs& a, int half_tiles, cudaStream_t st) 
 }
 
 // Fills the split / ring fields of `a`, then launches.
+// Between 33 and prefill_min_m() rows the small-M kernel streams every weight
+// once per row block (16 rows for W4, 32 for W8), while the tensor-core GEMM
+// streams it once -- but it has no K split, so it needs many output tiles to
+// fill the GPU.  Measured on B200 (one call, M = 64): config-5 fused W4 gate/up
+// (K = 5120, 136 GEMM tiles) 418 us small-M vs 219 us GEMM; W8 K = 5120, N =
+// 17408 (68 tiles) 82 vs 67 us; with 48 or fewer tiles the small-M kernel
+// wins (config-2 gate/up 67 vs 102 us, config-5 down 420 vs 671 us).
+constexpr int kMidGemmMinM = 33;
+constexpr long long kMidGemmMinTiles = 64;
+bool mid_m_takes_gemm(int epi, int64_t M, int tiles) {
+  if (M < kMidGemmMinM) return false;
+  const long long gemm_tiles = ((M + kGmRows - 1) / kGmRows) * (epi == kEpiOut ? (tiles + 1) / 2 : tiles);
+  return gemm_tiles >= kMidGemmMinTiles;
+}
+
 int run_gemv(int wb, int epi, GemvArgs& a, int tiles, cudaStream_t st) {
-  if (wb == 8 && use_tc() && a.M >= prefill_min_m()) return run_prefill_w8(epi, a, tiles, st);
-  if (wb == 4 && use_tc() && a.M >= prefill_min_m() && a.wgrp % 64 == 0) return run_prefill_w4(epi, a, tiles, st);
+  const bool gemm = use_tc() && (a.M >= prefill_min_m() || mid_m_takes_gemm(epi, a.M, tiles));
+  if (wb == 8 && gemm) return run_prefill_w8(epi, a, tiles, st);
+  if (wb == 4 && gemm && a.wgrp % 64 == 0) return run_prefill_w4(epi, a, tiles, st);
   if (use_tc()) return run_tc(wb, epi, a, tiles, st);
   DevInfo di;
   if (int r = device_info(&di)) return r;

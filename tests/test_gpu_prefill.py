@@ -230,3 +230,45 @@ def test_prefill_gate_up_quant_w4(pkg, dev, M, wg, zeros):
     rq, rs = O.mlp_gate_up_quant_w4(a.numpy(), s.numpy(), gw.numpy(), bits(gs), uw.numpy(), bits(us),
                                     None if gz is None else gz.numpy(), None if uz is None else uz.numpy())
     assert_quant_close(q.cpu().numpy(), qs.cpu().numpy(), rq, rs, f"prefill gate_up_quant W4 M={M} wg={wg}")
+
+
+# ----------------------------------------------------------------------------- mid M (33..127), many tiles
+# Below 128 rows, shapes with at least 64 GEMM tiles take the tensor-core GEMM
+# (one pass over the weights) instead of small-M row blocks.
+@pytest.mark.parametrize("M,N,K", [(33, 16384, 256), (64, 16384, 512), (100, 16512, 256)])
+def test_mid_m_gemm_i8_many_tiles(pkg, dev, M, N, K):
+    g = gen(8100 + M)
+    a, s = acts_ref(g, M, K)
+    b, bs = w8(g, K, N)
+    res = torch.randn(M, N, generator=g).to(torch.bfloat16)
+    out = res.clone().to(dev)
+    pkg.gemm_i8(cu(a), cu(s), cu(b), cu(bs), out, residual=out)
+    ref = O.gemm_i8(a.numpy(), s.numpy(), b.numpy(), bs.numpy(), bits(res))
+    assert_bf16_close(bits(out), ref, f"mid-M gemm_i8 M={M} N={N}")
+
+
+@pytest.mark.parametrize("M,wg,zeros", [(40, 128, True), (64, 64, False), (127, 128, True)])
+def test_mid_m_gemm_w4_many_tiles(pkg, dev, M, wg, zeros):
+    K, N = 512, 16384
+    g = gen(8200 + M + wg)
+    a, s = acts_x(g, M, K)
+    b, sc, z = w4(g, K, N, wg, zeros)
+    out = torch.zeros(M, N, dtype=torch.bfloat16, device=dev)
+    pkg.gemm_w4(cu(a), cu(s), cu(b), cu(sc), out, b_z=cu(z))
+    ref = O.gemm_w4(a.numpy(), s.numpy(), b.numpy(), bits(sc), None if z is None else z.numpy())
+    assert_bf16_close(bits(out), ref, f"mid-M gemm_w4 M={M} wg={wg}")
+
+
+@pytest.mark.parametrize("M", [48, 100])
+def test_mid_m_gate_up_quant_w4_many_tiles(pkg, dev, M):
+    K, N, wg = 256, 8192, 128
+    g = gen(8300 + M)
+    a, s = acts_x(g, M, K)
+    gw, gs, gz = w4(g, K, N, wg, True)
+    uw, us, uz = w4(g, K, N, wg, True)
+    q = torch.empty(M, N, dtype=torch.int8, device=dev)
+    qs = torch.empty(M, N // 64, dtype=torch.float32, device=dev)
+    pkg.mlp_gate_up_quant_w4(cu(a), cu(s), cu(gw), cu(gs), cu(uw), cu(us), q, qs, zg=cu(gz), zu=cu(uz))
+    rq, rs = O.mlp_gate_up_quant_w4(a.numpy(), s.numpy(), gw.numpy(), bits(gs), uw.numpy(), bits(us),
+                                    gz.numpy(), uz.numpy())
+    assert_quant_close(q.cpu().numpy(), qs.cpu().numpy(), rq, rs, f"mid-M gate_up_quant W4 M={M}")
