@@ -348,13 +348,19 @@ struct TcPlan {
 // (A plan with every packed W4 group resident and a ring of unpacked tiles
 // was measured slower than streaming once the W4 operands became the masked
 // nibble tiles: 12.3 vs 10.8 us for the config-2 gate/up at split 4.)
-void plan_batches(int wb, int mr, int ns, int wgrp, long long ctas, int sms, bool long_stream, TcPlan& pl) {
-  const uint32_t budget = (tune_budget() > 0 ? tune_budget() : 112) * 1024;
+void plan_batches(int wb, int mr, int ns, int wgrp, long long ctas, int sms, bool long_stream, bool one_per_sm,
+                  TcPlan& pl) {
+  // A kernel instance whose registers fit only one CTA per SM (the 8- to
+  // 32-row blocks) shares no SM with the next launch anyway: it may use most
+  // of shared memory.  Measured on B200, config-2 shapes at M = 16: fused
+  // gate/up 29.4 -> 20.0 us, down 22.4 -> 11.0 us.
+  const uint32_t budget = (tune_budget() > 0 ? tune_budget() : one_per_sm ? 200 : 112) * 1024;
   // A long streamed launch (tens of MB of weights) that fits one CTA per SM
   // may use most of shared memory for a deeper weight ring; its weight
   // stream, not the next launch's prologue, is what bounds it.
   const uint32_t stream_budget =
-      tune_stream_budget() > 0 ? tune_stream_budget() * 1024u : (long_stream && ctas <= sms ? 200u * 1024 : budget);
+      tune_stream_budget() > 0 ? tune_stream_budget() * 1024u
+                               : ((long_stream && ctas <= sms) || one_per_sm ? 200u * 1024 : budget);
   const int s = pl.split, gmax = pl.gmax;
   const TcLayout base = tc_layout(wb, mr, ns, wgrp, gmax, 1, 1, 1, 1, s, 0);
   const int tmem_groups = static_cast<int>(kTmemBudget / base.per_buf);
@@ -421,6 +427,7 @@ void plan_batches(int wb, int mr, int ns, int wgrp, long long ctas, int sms, boo
 // 1.3 CTAs per SM: more CTAs leave clusters waiting for the previous
 // launch's CTAs to retire, fewer leave HBM under-subscribed.
 int active_clusters(int wb, int mr, int ns, int split, size_t smem);
+int blocks_by_regs(int wb, int mr, int ns);
 
 // Clusters of `s` CTAs that stay resident at once for a plan with `smem`
 // bytes and `tmem_cols` tensor-memory columns per CTA, or -1 without a
@@ -434,6 +441,8 @@ long long cluster_capacity(int wb, int mr, int ns, int s, size_t smem, uint32_t 
   long long per_sm = (228 * 1024) / (static_cast<long long>(smem) + 1024);
   const long long by_tmem = tmem_cols ? 512 / tmem_cols : 1;
   if (by_tmem < per_sm) per_sm = by_tmem;
+  const long long by_regs = blocks_by_regs(wb, mr, ns);
+  if (by_regs > 0 && by_regs < per_sm) per_sm = by_regs;
   auto c1 = [&](int x) { return static_cast<long long>(active_clusters(wb, mr, ns, x, smem)); };
   if (per_sm <= 1) return c1(s);
   if (s == 1) {
@@ -447,8 +456,12 @@ long long cluster_capacity(int wb, int mr, int ns, int s, size_t smem, uint32_t 
 
 TcPlan plan_tc(int wb, int mr, int ns, int K, int wgrp, int tiles, int rowblocks, int sms, bool query) {
   const int G = K / kGroup;
-  const long long target = (static_cast<long long>(sms) * 4 + 2) / 3;  // ~1.33 CTAs per SM
-  const long long two_per_sm = 2ll * sms;
+  // CTAs per SM that the instance's registers allow (from the device when it
+  // is queried): with one, the targets below count one CTA per SM.
+  const int reg_blocks = query ? blocks_by_regs(wb, mr, ns) : -1;
+  const bool one_per_sm = reg_blocks == 1;
+  const long long target = one_per_sm ? sms : (static_cast<long long>(sms) * 4 + 2) / 3;  // ~1.33 CTAs per SM
+  const long long two_per_sm = one_per_sm ? sms : 2ll * sms;
   // Per plan level: the largest split within the CTA target, and the
   // smallest split beyond it (within two CTAs per SM).
   TcPlan in[3] = {}, up[3] = {}, any{}, stream{}, compact{};
@@ -464,7 +477,7 @@ TcPlan plan_tc(int wb, int mr, int ns, int K, int wgrp, int tiles, int rowblocks
     TcPlan pl{s, (G + s - 1) / s, 1, 1, 0, 1, 0, 0, 0};
     if (tune_split() > 0 && s != tune_split() && tune_split() <= smax) continue;
     const long long ctas = static_cast<long long>(tiles) * s * rowblocks;
-    plan_batches(wb, mr, ns, wgrp, ctas, sms, long_stream, pl);
+    plan_batches(wb, mr, ns, wgrp, ctas, sms, long_stream, one_per_sm, pl);
     if (pl.smem > kTcMaxSmem) continue;
     if (tune_split() == s) return pl;
     if (any.split == 0) any = pl;  // smallest feasible split, whatever its size
@@ -478,7 +491,8 @@ TcPlan plan_tc(int wb, int mr, int ns, int K, int wgrp, int tiles, int rowblocks
       // Long streamed launches are bound by the weight bytes in flight over
       // the whole GPU: resident CTAs x ring slots x groups per batch, divided
       // by the waves the launch needs (measured on the config-5 shapes).
-      const long long per_sm = (228 * 1024) / (static_cast<long long>(pl.smem) + 1024);
+      long long per_sm = (228 * 1024) / (static_cast<long long>(pl.smem) + 1024);
+      if (one_per_sm) per_sm = 1;
       const long long slots = cap > 0 ? cap * s : sms * (per_sm < 1 ? 1 : per_sm);
       const long long resident = ctas < slots ? ctas : slots;
       const long long waves = (ctas + slots - 1) / slots;  // a second wave serialises behind the first
@@ -605,6 +619,68 @@ int active_clusters(int wb, int mr, int ns, int split, size_t smem) {
   int n;
   if (wb == 8) n = ns == 1 ? active_clusters_mr<8, kEpiOut>(mr, split, smem) : active_clusters_mr<8, kEpiSiluQuant>(mr, split, smem);
   else n = ns == 1 ? active_clusters_mr<4, kEpiOut>(mr, split, smem) : active_clusters_mr<4, kEpiSiluQuant>(mr, split, smem);
+  std::lock_guard<std::mutex> g(mu);
+  cache.emplace(k, n);
+  return n;
+}
+
+// CTAs of a kernel instance that share one SM by registers: two when the
+// instance's registers x threads fit half of the 64K-register file, else
+// one, or -1.  (This matches what runs: per-CTA timelines show two CTAs per
+// SM for the 1- to 4-row instances, 78-98 registers; the 8- to 32-row
+// instances use 112-200.  cudaOccupancyMaxActiveBlocksPerMultiprocessor
+// answers one for all of them, so it is not used.)
+template <int WB, int MR, int EPI>
+int blocks_by_regs_t() {
+  cudaFuncAttributes fa;
+  if (cudaFuncGetAttributes(&fa, tc_gemv_kernel<WB, MR, EPI>) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  return static_cast<long long>(fa.numRegs) * tc_threads(WB) * 2 <= 65536 ? 2 : 1;
+}
+
+template <int WB, int EPI>
+int blocks_by_regs_mr(int mr) {
+  switch (mr) {
+    case 1: return blocks_by_regs_t<WB, 1, EPI>();
+    case 2: return blocks_by_regs_t<WB, 2, EPI>();
+    case 4: return blocks_by_regs_t<WB, 4, EPI>();
+    case 8: return blocks_by_regs_t<WB, 8, EPI>();
+    case 16: return blocks_by_regs_t<WB, 16, EPI>();
+    default:
+      if constexpr (WB == 8) return blocks_by_regs_t<WB, 32, EPI>();
+      return -1;
+  }
+}
+
+// Per device, kernel family and row block (cached).  W8 gate/up has two
+// epilogues; the smaller count of the two is used.
+int blocks_by_regs(int wb, int mr, int ns) {
+  static std::mutex mu;
+  static std::unordered_map<uint64_t, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  const uint64_t k = (static_cast<uint64_t>(dev) << 32) | (static_cast<uint64_t>(wb) << 16) | (mr << 4) | ns;
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto it = cache.find(k);
+    if (it != cache.end()) return it->second;
+  }
+  int n;
+  if (wb == 8) {
+    if (ns == 1) {
+      n = blocks_by_regs_mr<8, kEpiOut>(mr);
+    } else {
+      const int a = blocks_by_regs_mr<8, kEpiSiluBf16>(mr), b = blocks_by_regs_mr<8, kEpiSiluQuant>(mr);
+      n = (a < 0 || b < 0) ? -1 : (a < b ? a : b);
+    }
+  } else {
+    n = ns == 1 ? blocks_by_regs_mr<4, kEpiOut>(mr) : blocks_by_regs_mr<4, kEpiSiluQuant>(mr);
+  }
   std::lock_guard<std::mutex> g(mu);
   cache.emplace(k, n);
   return n;
