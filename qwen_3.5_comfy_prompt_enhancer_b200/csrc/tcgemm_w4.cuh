@@ -14,7 +14,7 @@
 //   * a stage carries the packed nibbles (64 packed rows = 128 K per half),
 //     the bf16 scale rows and the zero rows of its groups;
 //   * two unpack warps turn each stage into signed int8 tiles (nibble - z,
-//     one SIMD byte subtraction per 4 weights) in a 2-slot ring of
+//     one carry-free byte subtraction per 4 weights) in a 2-slot ring of
 //     MN-major 128-byte-swizzled operand tiles, and copy the group scales,
 //     converted to fp32, into an 8-slot ring that outlives the raw stage;
 //   * the epilogue multiplies the row's activation scale by each column's
@@ -195,19 +195,31 @@ __global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_
           const bool has_z = valid && p.seg[si].has_z;
           // 64 packed rows x 8 chunks of 16 columns; packed row j holds K = 2j
           // (low nibble) and 2j + 1 (high nibble) of 16 columns.
-#pragma unroll 2
+          // All eight chunks are loaded before any is converted and stored, so
+          // their shared-memory latencies overlap.
+          uint4 vv[8], zz[8];
+#pragma unroll
           for (int i = 0; i < 8; ++i) {
             const int idx = u + kG4UnpackThreads * i;
             const int pr = idx >> 3, ch = idx & 7;
-            const uint4 v = *reinterpret_cast<const uint4*>(raw + pr * 128 + ch * 16);
-            const int zr = (k0 + 2 * pr) / p.wgrp - srow;   // both K of the row share a group
-            const uint4 z = has_z ? *reinterpret_cast<const uint4*>(raw + kG4Packed + kG4Scale + zr * 128 + ch * 16)
-                                  : make_uint4(0x08080808u, 0x08080808u, 0x08080808u, 0x08080808u);
+            vv[i] = *reinterpret_cast<const uint4*>(raw + pr * 128 + ch * 16);
+            const int zr = (k0 + 2 * pr) / p.wgrp - srow;
+            zz[i] = has_z ? *reinterpret_cast<const uint4*>(raw + kG4Packed + kG4Scale + zr * 128 + ch * 16)
+                          : make_uint4(0x08080808u, 0x08080808u, 0x08080808u, 0x08080808u);
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int idx = u + kG4UnpackThreads * i;
+            const int pr = idx >> 3, ch = idx & 7;
+            const uint4 v = vv[i], z = zz[i];
             uint4 lo, hi;
-            lo.x = __vsub4(v.x & 0x0F0F0F0Fu, z.x); hi.x = __vsub4((v.x >> 4) & 0x0F0F0F0Fu, z.x);
-            lo.y = __vsub4(v.y & 0x0F0F0F0Fu, z.y); hi.y = __vsub4((v.y >> 4) & 0x0F0F0F0Fu, z.y);
-            lo.z = __vsub4(v.z & 0x0F0F0F0Fu, z.z); hi.z = __vsub4((v.z >> 4) & 0x0F0F0F0Fu, z.z);
-            lo.w = __vsub4(v.w & 0x0F0F0F0Fu, z.w); hi.w = __vsub4((v.w >> 4) & 0x0F0F0F0Fu, z.w);
+            // nibble - z per byte as (nibble + (0x80 - z)) ^ 0x80: no carry
+            // or borrow crosses a byte (nibble, z <= 15), same bytes as __vsub4
+            const uint4 zc = make_uint4(0x80808080u - z.x, 0x80808080u - z.y, 0x80808080u - z.z, 0x80808080u - z.w);
+            lo.x = ((v.x & 0x0F0F0F0Fu) + zc.x) ^ 0x80808080u; hi.x = (((v.x >> 4) & 0x0F0F0F0Fu) + zc.x) ^ 0x80808080u;
+            lo.y = ((v.y & 0x0F0F0F0Fu) + zc.y) ^ 0x80808080u; hi.y = (((v.y >> 4) & 0x0F0F0F0Fu) + zc.y) ^ 0x80808080u;
+            lo.z = ((v.z & 0x0F0F0F0Fu) + zc.z) ^ 0x80808080u; hi.z = (((v.z >> 4) & 0x0F0F0F0Fu) + zc.z) ^ 0x80808080u;
+            lo.w = ((v.w & 0x0F0F0F0Fu) + zc.w) ^ 0x80808080u; hi.w = (((v.w >> 4) & 0x0F0F0F0Fu) + zc.w) ^ 0x80808080u;
             const int r0 = 2 * pr, r1 = 2 * pr + 1;
             *reinterpret_cast<uint4*>(ut + r0 * 128 + ((ch ^ (r0 & 7)) << 4)) = lo;
             *reinterpret_cast<uint4*>(ut + r1 * 128 + ((ch ^ (r1 & 7)) << 4)) = hi;
