@@ -160,29 +160,28 @@ int qlin_dev_free(void* ptr);
 int qlin_peer_allgather(void* const* bufs, void* const* arrive, void* expected, const void* src,
                         int64_t shard_bytes, int world, int rank, void* dst, void* stream);
 
-/* All-gather that allocates nothing.  It has no counterpart in the reference.
- * Meant for a program that drives every rank's GPU from ONE process and may
- * not call cudaMalloc itself -- for instance a plugin whose host application
- * owns all device memory through its own pool, so any allocation of ours would
- * escape that pool's accounting and limits.  It does what qlin_peer_allgather
- * does, but the gather buffer and the counters are static device arrays of
- * this library on each GPU, reached by the peers through peer access (enabled
- * here on first use); the caller passes only its shard and the output.
- *   devices[q]: CUDA device of rank q (distinct); call rank `rank` with
- *               devices[rank] current, one call per rank, on that rank's stream.
- *   dst: world x shard_bytes bytes on devices[rank] (required).
- * Limit: world x shard_bytes <= QLIN_STATIC_GATHER_MAX_BYTES; larger requests
- * fail with QLIN_ERR_SHAPE before anything is launched.  The first call on a
- * device looks up the static arrays' device addresses and enables peer
- * access, so make it before any stream capture.  Every call in the process
- * shares the same arrays: all ranks must make the same sequence of calls with
- * the same device list, consecutive calls alternate between two halves of the
- * buffer, and calls that overlap on a GPU (other streams) race.  The counters
- * start at zero when the library loads and only grow, so nothing is cleared
- * per call. */
+/* All-gather that allocates nothing, for one rank.  It has no counterpart in
+ * the reference.  Meant for a process that runs the column-split layer on a
+ * single GPU (world = 1) and may not call cudaMalloc itself -- for instance a
+ * plugin whose host application owns all device memory through its own pool,
+ * so any allocation of ours would escape that pool's accounting and limits.
+ * It runs the same kernel as qlin_peer_allgather with world = 1, but its
+ * gather buffer and counters are static device arrays of this library on the
+ * current GPU; the caller passes only its shard and the output.
+ *   src: shard_bytes bytes (multiple of 16, 16-byte aligned);
+ *   dst: shard_bytes bytes, the gathered result, written on `stream`.
+ * Limit: shard_bytes <= QLIN_STATIC_GATHER_MAX_BYTES; larger requests fail
+ * with QLIN_ERR_SHAPE before anything is launched.  The first call on a
+ * device looks up the static arrays' device addresses, so make it before any
+ * stream capture.  Every call on a device shares the same arrays: calls on
+ * one stream are ordered, calls that overlap on the GPU (other streams) race.
+ * The counters start at zero when the library loads and only grow, so nothing
+ * is cleared per call.  (It serves one GPU: a two-GPU form, whose kernels
+ * wrote the other GPU's static arrays through peer access, stopped with an
+ * illegal memory access on B200, so multi-GPU gathers use
+ * qlin_peer_allgather and its caller-allocated buffers.) */
 #define QLIN_STATIC_GATHER_MAX_BYTES (4 << 20)
-int qlin_peer_allgather_static(const int* devices, int world, int rank, const void* src, int64_t shard_bytes,
-                               void* dst, void* stream);
+int qlin_peer_allgather_static(const void* src, int64_t shard_bytes, void* dst, void* stream);
 
 /* Diagnostic (no GPU needed, nothing launched): the launch plan of the
  * small-M weight-streaming kernel for wbits 8 or 4, `gate_up` 0 (one output

@@ -39,7 +39,7 @@ SIGNATURES = {
     "qlin_dev_alloc": [_I, ctypes.POINTER(ctypes.c_void_p)],
     "qlin_dev_free": [_P],
     "qlin_peer_allgather": [_P, _P, _P, _P, _I, ctypes.c_int, ctypes.c_int, _P, _P],
-    "qlin_peer_allgather_static": [_P, ctypes.c_int, ctypes.c_int, _P, _I, _P, _P],
+    "qlin_peer_allgather_static": [_P, _I, _P, _P],
 }
 _RESTYPES = {
     "qlin_status_string": ctypes.c_char_p,

@@ -25,12 +25,11 @@ namespace qlin {
 __device__ unsigned int g_qlin_fault;
 
 // Scratch of qlin_peer_allgather_static, held by every GPU that loads this
-// library until the process exits: two halves of kStaticGatherHalf bytes
-// (successive calls alternate between them), the arrival counters the ranks
-// add to, and this GPU's expected counts.  Device statics are zero when the
+// library until the process exits: the gather buffer, the arrival counter the
+// kernel adds to and its expected count.  Device statics are zero when the
 // module loads; the counters only ever grow.
-constexpr size_t kStaticGatherHalf = QLIN_STATIC_GATHER_MAX_BYTES;
-static __device__ __align__(256) uint8_t g_static_gather[2 * kStaticGatherHalf];
+constexpr size_t kStaticGatherBytes = QLIN_STATIC_GATHER_MAX_BYTES;
+static __device__ __align__(256) uint8_t g_static_gather[kStaticGatherBytes];
 static __device__ __align__(256) unsigned g_static_arrive[kPeerMax];
 static __device__ __align__(256) unsigned g_static_expected[kPeerMax];
 
@@ -1098,27 +1097,20 @@ struct StaticGather {
   uint8_t* buf;
   unsigned* arrive;
   unsigned* expected;
-  unsigned long long calls;    // calls made on this device (selects the half)
-  unsigned long long peers;    // devices this one has peer access to
 };
 StaticGather g_static[kMaxDevices];
 std::mutex g_static_mu;
 
-int static_gather_setup(int dev) {  // with g_static_mu held
+int static_gather_setup(int dev) {  // with g_static_mu held and `dev` current
   StaticGather& g = g_static[dev];
   if (g.ready) return QLIN_OK;
-  int cur = 0;
-  cudaError_t e = cudaGetDevice(&cur);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-  if (cur != dev && (e = cudaSetDevice(dev)) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
   void *b = nullptr, *a = nullptr, *x = nullptr;
-  cudaError_t eb = cudaGetSymbolAddress(&b, g_static_gather);
-  cudaError_t ea = cudaGetSymbolAddress(&a, g_static_arrive);
-  cudaError_t ex = cudaGetSymbolAddress(&x, g_static_expected);
-  if (cur != dev && (e = cudaSetDevice(cur)) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
-  if (eb != cudaSuccess) return cuda_fail(eb, "cudaGetSymbolAddress(static gather buffer)");
-  if (ea != cudaSuccess) return cuda_fail(ea, "cudaGetSymbolAddress(static arrival counters)");
-  if (ex != cudaSuccess) return cuda_fail(ex, "cudaGetSymbolAddress(static expected counts)");
+  cudaError_t e = cudaGetSymbolAddress(&b, g_static_gather);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static gather buffer)");
+  if ((e = cudaGetSymbolAddress(&a, g_static_arrive)) != cudaSuccess)
+    return cuda_fail(e, "cudaGetSymbolAddress(static arrival counters)");
+  if ((e = cudaGetSymbolAddress(&x, g_static_expected)) != cudaSuccess)
+    return cuda_fail(e, "cudaGetSymbolAddress(static expected counts)");
   g.buf = static_cast<uint8_t*>(b);
   g.arrive = static_cast<unsigned*>(a);
   g.expected = static_cast<unsigned*>(x);
@@ -1238,70 +1230,40 @@ int qlin_peer_allgather(void* const* bufs, void* const* arrive, void* expected, 
   return QLIN_OK;
 }
 
-int qlin_peer_allgather_static(const int* devices, int world, int rank, const void* src, int64_t shard_bytes,
-                               void* dst, void* stream) {
-  if (world < 1 || world > kPeerMax || rank < 0 || rank >= world)
-    return fail(QLIN_ERR_INVALID_ARGUMENT, "world %d / rank %d", world, rank);
-  if (!devices || !src || !dst) return fail(QLIN_ERR_INVALID_ARGUMENT, "null argument");
+int qlin_peer_allgather_static(const void* src, int64_t shard_bytes, void* dst, void* stream) {
+  if (!src || !dst) return fail(QLIN_ERR_INVALID_ARGUMENT, "null argument");
   if (shard_bytes <= 0 || shard_bytes % 16 != 0)
     return fail(QLIN_ERR_SHAPE, "shard of %lld bytes is not a positive multiple of 16", (long long)shard_bytes);
-  if (shard_bytes * world > static_cast<int64_t>(kStaticGatherHalf))
-    return fail(QLIN_ERR_SHAPE, "world x shard_bytes = %lld exceeds the static scratch limit of %lld bytes",
-                (long long)(shard_bytes * world), (long long)kStaticGatherHalf);
+  if (shard_bytes > static_cast<int64_t>(kStaticGatherBytes))
+    return fail(QLIN_ERR_SHAPE, "shard of %lld bytes exceeds the static scratch limit of %lld bytes",
+                (long long)shard_bytes, (long long)kStaticGatherBytes);
   if (!aligned(src, 16)) return fail(QLIN_ERR_ALIGNMENT, "source must be 16-byte aligned");
-  int ndev = 0;
-  cudaError_t e = cudaGetDeviceCount(&ndev);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
-  for (int q = 0; q < world; ++q) {
-    if (devices[q] < 0 || devices[q] >= ndev || devices[q] >= kMaxDevices)
-      return fail(QLIN_ERR_INVALID_ARGUMENT, "device %d of rank %d does not exist", devices[q], q);
-    for (int r = 0; r < q; ++r)
-      if (devices[r] == devices[q]) return fail(QLIN_ERR_INVALID_ARGUMENT, "device %d given twice", devices[q]);
-  }
-  int cur = 0;
-  if ((e = cudaGetDevice(&cur)) != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-  if (cur != devices[rank])
-    return fail(QLIN_ERR_INVALID_ARGUMENT, "rank %d must be called with device %d current (current: %d)", rank,
-                devices[rank], cur);
   DevInfo di;
   if (int r = device_info(&di)) return r;
+  int cur = 0;
+  cudaError_t e = cudaGetDevice(&cur);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   PeerGatherArgs a;
   memset(&a, 0, sizeof(a));
   {
     std::lock_guard<std::mutex> lk(g_static_mu);
-    for (int q = 0; q < world; ++q)
-      if (int r = static_gather_setup(devices[q])) return r;
-    StaticGather& me = g_static[cur];
-    for (int q = 0; q < world; ++q) {
-      const int d = devices[q];
-      if (d == cur || (me.peers >> d) & 1ull) continue;
-      int can = 0;
-      if ((e = cudaDeviceCanAccessPeer(&can, cur, d)) != cudaSuccess) return cuda_fail(e, "cudaDeviceCanAccessPeer");
-      if (!can) return fail(QLIN_ERR_UNSUPPORTED, "device %d cannot access device %d", cur, d);
-      e = cudaDeviceEnablePeerAccess(d, 0);
-      if (e == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
-      else if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceEnablePeerAccess");
-      me.peers |= 1ull << d;
-    }
-    const size_t half = static_cast<size_t>(me.calls++ & 1) * kStaticGatherHalf;
-    for (int q = 0; q < world; ++q) {
-      a.bufs[q] = g_static[devices[q]].buf + half;
-      a.arrive[q] = g_static[devices[q]].arrive;
-    }
-    a.expected = me.expected;
+    if (int r = static_gather_setup(cur)) return r;
+    a.bufs[0] = g_static[cur].buf;
+    a.arrive[0] = g_static[cur].arrive;
+    a.expected = g_static[cur].expected;
   }
   a.src = static_cast<const uint8_t*>(src);
   a.shard_bytes = shard_bytes;
-  a.world = world;
-  a.rank = rank;
+  a.world = 1;
+  a.rank = 0;
   a.fault = di.fault;
-  // Same grid rule as qlin_peer_allgather: every rank launches as many CTAs.
+  // Same grid rule as qlin_peer_allgather.
   long long ctas = (shard_bytes / 16 + kPeerThreads * 4 - 1) / (kPeerThreads * 4);
   if (ctas < 1) ctas = 1;
   if (ctas > 64) ctas = 64;
   peer_allgather_kernel<<<static_cast<int>(ctas), kPeerThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "peer_allgather_kernel launch");
-  e = cudaMemcpyAsync(dst, a.bufs[rank], static_cast<size_t>(shard_bytes) * world, cudaMemcpyDeviceToDevice,
+  e = cudaMemcpyAsync(dst, a.bufs[0], static_cast<size_t>(shard_bytes), cudaMemcpyDeviceToDevice,
                       static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(gathered)");
   return QLIN_OK;
