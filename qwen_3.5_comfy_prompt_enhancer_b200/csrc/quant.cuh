@@ -13,6 +13,10 @@ constexpr int kQuantWarps = 8;
 __global__ void __launch_bounds__(kQuantWarps * 32) quant_row_kernel(
     const __nv_bfloat16* __restrict__ x, long long ldx, int M, int K, int8_t* __restrict__ q,
     float* __restrict__ s) {
+  // The next launch (a projection of these activations) may be placed at
+  // once and stream its weights; its own grid-dependency wait still waits for
+  // this grid to complete.
+  pdl_launch_dependents();
   pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = K / kGroup;
@@ -32,7 +36,6 @@ __global__ void __launch_bounds__(kQuantWarps * 32) quant_row_kernel(
     *reinterpret_cast<char2*>(q + static_cast<long long>(row) * K + g * kGroup + 2 * lane) = out;
     if (lane == 0) s[static_cast<long long>(row) * G + g] = sc;
   }
-  pdl_launch_dependents();
 }
 
 }  // namespace qlin

@@ -275,6 +275,11 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // Let the next launch's CTAs be placed now, so that they request their
+  // weights while this launch waits and computes.  No CTA of this launch can
+  // then wait on a later launch: the next grid starts only once every CTA of
+  // this one has passed this point, after its tensor-memory allocation.
+  pdl_launch_dependents();
   // Every rank's barriers are initialised (and rank 0's receive barrier armed)
   // before any rank signals another.  Waiting here, with the weights already
   // in flight, keeps the cluster barrier off the tail of the launch.
@@ -390,7 +395,6 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
       }
     }
     named_bar_sync(1, kDrainThreads);  // ass / asum visible to all drain threads
-    pdl_launch_dependents();
 
     const uint32_t lane_base = tbase + (static_cast<uint32_t>(32 * q) << 16);
     for (int b = 0; ok && b < nbatch; ++b) {
