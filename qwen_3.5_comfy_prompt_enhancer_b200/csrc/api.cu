@@ -845,9 +845,9 @@ int run_tc(int wb, int epi, GemvArgs& a, int tiles, cudaStream_t st) {
 }
 
 // ---------------------------------------------------------------- tensor-core GEMM (large M)
-template <int EPI>
+template <int EPI, int HS = 2>
 int launch_prefill_w8(const GemmArgs& g, int grid, cudaStream_t st) {
-  auto kern = tc_gemm_kernel<EPI>;
+  auto kern = tc_gemm_kernel<EPI, HS>;
   static std::atomic<unsigned long long> configured{0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -903,18 +903,25 @@ int run_prefill_w8(int epi, const GemvArgs& a, int half_tiles, cudaStream_t st) 
   g.n_q = a.n_q;
   g.fault = di.fault;
   if (epi != kEpiOut) g.half_tiles = 2 * half_tiles;  // (gate tile, up tile) pairs
-  const long long tiles = static_cast<long long>((a.M + kGmRows - 1) / kGmRows) * ((g.half_tiles + 1) / 2);
+  const long long mtiles = (a.M + kGmRows - 1) / kGmRows;
+  // Plain outputs whose 256-column tiles would leave SMs idle take one
+  // 128-column half per tile (twice the tiles; a separate kernel instance, so
+  // the two-half tiles compile unchanged).  Measured on B200: W8 K = 5120,
+  // N = 17408 at M = 64 (68 -> 136 tiles) 69 -> 45 us; config-5 down
+  // projection (K = 17408, N = 5120) at M = 256, 40 -> 80 tiles.
+  const int hs = (epi == kEpiOut && mtiles * ((g.half_tiles + 1) / 2) < di.sms) ? 1 : 2;
+  const long long tiles = mtiles * ((g.half_tiles + hs - 1) / hs);
   const int grid = static_cast<int>(tiles < di.sms ? tiles : di.sms);
   switch (epi) {
-    case kEpiOut: return launch_prefill_w8<kEpiOut>(g, grid, st);
+    case kEpiOut: return hs == 1 ? launch_prefill_w8<kEpiOut, 1>(g, grid, st) : launch_prefill_w8<kEpiOut>(g, grid, st);
     case kEpiSiluBf16: return launch_prefill_w8<kEpiSiluBf16>(g, grid, st);
     default: return launch_prefill_w8<kEpiSiluQuant>(g, grid, st);
   }
 }
 
-template <int EPI>
+template <int EPI, int HS = 2>
 int launch_prefill_w4(const GemmW4Args& g, int grid, cudaStream_t st) {
-  auto kern = tc_gemm_w4_kernel<EPI>;
+  auto kern = tc_gemm_w4_kernel<EPI, HS>;
   static std::atomic<unsigned long long> configured{0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -976,9 +983,12 @@ int run_prefill_w4(int epi, const GemvArgs& a, int half_tiles, cudaStream_t st) 
   g.n_q = a.n_q;
   g.fault = di.fault;
   if (epi != kEpiOut) g.half_tiles = 2 * half_tiles;  // (gate tile, up tile) pairs
-  const long long tiles = static_cast<long long>((a.M + kGmRows - 1) / kGmRows) * ((g.half_tiles + 1) / 2);
+  const long long mtiles = (a.M + kGmRows - 1) / kGmRows;
+  const int hs = (epi == kEpiOut && mtiles * ((g.half_tiles + 1) / 2) < di.sms) ? 1 : 2;  // as for W8
+  const long long tiles = mtiles * ((g.half_tiles + hs - 1) / hs);
   const int grid = static_cast<int>(tiles < di.sms ? tiles : di.sms);
-  return epi == kEpiOut ? launch_prefill_w4<kEpiOut>(g, grid, st) : launch_prefill_w4<kEpiSiluQuant>(g, grid, st);
+  if (epi != kEpiOut) return launch_prefill_w4<kEpiSiluQuant>(g, grid, st);
+  return hs == 1 ? launch_prefill_w4<kEpiOut, 1>(g, grid, st) : launch_prefill_w4<kEpiOut>(g, grid, st);
 }
 
 // Fills the split / ring fields of `a`, then launches.

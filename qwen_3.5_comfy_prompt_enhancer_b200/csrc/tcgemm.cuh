@@ -74,11 +74,13 @@ __device__ __forceinline__ int gm_seg_of(const GemmArgs& p, int ht) {
 // Half h of column pair pt: plain projections walk the 128-column tiles of
 // their segments two at a time; the fused gate/up pairs gate tile pt (seg 0)
 // with up tile pt (seg 1), so one thread can hold both for the same columns.
-template <int EPI, class Args>
+// HS: 128-column halves per tile -- 2, or 1 for plain outputs whose 256-column
+// tiles would leave SMs idle (twice the tiles, each draining one half).
+template <int EPI, int HS = 2, class Args>
 __device__ __forceinline__ bool gm_half(const Args& p, int pt, int h, int& si, int& n0) {
   if (EPI == kEpiOut) {
-    const int ht = 2 * pt + h;
-    if (ht >= p.half_tiles) return false;
+    const int ht = HS * pt + h;
+    if (h >= HS || ht >= p.half_tiles) return false;
     int s = 0;
     if (p.nseg > 1 && ht >= p.seg[1].tile_begin) s = 1;
     if (p.nseg > 2 && ht >= p.seg[2].tile_begin) s = 2;
@@ -151,7 +153,7 @@ __device__ __forceinline__ void gm_gate_up_epilogue(const Args& p, int m, int nb
   }
 }
 
-template <int EPI>
+template <int EPI, int HS>
 __global__ void __launch_bounds__(kGmThreads, 1) tc_gemm_kernel(const __grid_constant__ GemmArgs p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -165,7 +167,7 @@ __global__ void __launch_bounds__(kGmThreads, 1) tc_gemm_kernel(const __grid_con
   const int G = p.K / kGroup;
   const int nstage = (G + 1) / 2;
   const int mtiles = (p.M + kGmRows - 1) / kGmRows;
-  const int ptiles = (p.half_tiles + 1) / 2;
+  const int ptiles = (p.half_tiles + HS - 1) / HS;
   const int tiles = mtiles * ptiles;
 
   if (warp == 0) {
@@ -208,13 +210,13 @@ __global__ void __launch_bounds__(kGmThreads, 1) tc_gemm_kernel(const __grid_con
         if (elect_one()) {
           uint8_t* sa = smem + slot * kGmStageBytes;
           uint32_t bytes = kGmStageA;
-          for (int h = 0; h < 2; ++h)
-            if (2 * pt + h < p.half_tiles) bytes += kGmStageB;
+          for (int h = 0; h < HS; ++h)
+            if (HS * pt + h < p.half_tiles) bytes += kGmStageB;
           mbar_arrive_expect_tx(full + slot, bytes);
           tma_load_2d(sa, &p.ta, st * 128, m0, full + slot, pol_a);
           for (int h = 0; h < 2; ++h) {
             int si, n0;
-            if (!gm_half<EPI>(p, pt, h, si, n0)) continue;
+            if (!gm_half<EPI, HS>(p, pt, h, si, n0)) continue;
             tma_load_2d(sa + kGmStageA + h * kGmStageB, &p.seg[si].tw, n0, st * 128, full + slot, pol_b);
           }
         }
@@ -233,7 +235,7 @@ __global__ void __launch_bounds__(kGmThreads, 1) tc_gemm_kernel(const __grid_con
     bool ok = true;
     for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
       const int pt = t / mtiles;
-      const int nh = 2 * pt + 1 < p.half_tiles ? 2 : 1;
+      const int nh = HS == 2 && 2 * pt + 1 < p.half_tiles ? 2 : 1;
       for (int st = 0; ok && st < nstage; ++st, ++sc) {
         const int slot = sc % kGmStages;
         ok = mbar_wait(full + slot, (sc / kGmStages) & 1);
@@ -305,7 +307,7 @@ __global__ void __launch_bounds__(kGmThreads, 1) tc_gemm_kernel(const __grid_con
         tc_fence_after();
         const float2 s2 = make_float2(s, s);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
+        for (int c = 0; c < 4 * HS; ++c) {
           const uint32_t col = b * 256 + (c >> 2) * 128 + 16 * (c & 3);
           uint32_t r[16];
           tmem_ld32<16>(lane_base + col, r);
@@ -328,7 +330,7 @@ __global__ void __launch_bounds__(kGmThreads, 1) tc_gemm_kernel(const __grid_con
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           int si, n0;
-          if (!gm_half<EPI>(p, pt, hh, si, n0)) continue;
+          if (!gm_half<EPI, HS>(p, pt, hh, si, n0)) continue;
           const GemvSeg& sg = p.seg[si];
           __nv_bfloat16* orow =
               reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<long long>(m) * p.ldo + sg.out_col;

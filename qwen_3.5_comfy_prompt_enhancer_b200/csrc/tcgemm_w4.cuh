@@ -79,7 +79,7 @@ __device__ __forceinline__ float2 f2_mul(float2 a, float2 b) {
   return d;
 }
 
-template <int EPI>
+template <int EPI, int HS>
 __global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_constant__ GemmW4Args p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -96,7 +96,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_
   const int G = p.K / kGroup;
   const int nstage = (G + 1) / 2;
   const int mtiles = (p.M + kGmRows - 1) / kGmRows;
-  const int ptiles = (p.half_tiles + 1) / 2;
+  const int ptiles = (p.half_tiles + HS - 1) / HS;
   const int tiles = mtiles * ptiles;
   const int nsr = g4_scale_rows(p.wgrp);
 
@@ -144,17 +144,17 @@ __global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_
         if (elect_one()) {
           uint8_t* sa = smem + kG4RawOff + slot * kG4StageAligned;
           uint32_t bytes = kG4A;
-          for (int h = 0; h < 2; ++h) {
+          for (int h = 0; h < HS; ++h) {
             int si, n0;
-            if (!gm_half<EPI>(p, pt, h, si, n0)) continue;
+            if (!gm_half<EPI, HS>(p, pt, h, si, n0)) continue;
             bytes += kG4Packed + nsr * 128 * 2 + (p.seg[si].has_z ? nsr * 128 : 0);
           }
           mbar_arrive_expect_tx(full + slot, bytes);
           tma_load_2d(sa, &p.ta, st * 128, m0, full + slot, pol);
           const int srow = (st * 128) / p.wgrp;
-          for (int h = 0; h < 2; ++h) {
+          for (int h = 0; h < HS; ++h) {
             int si, n0;
-            if (!gm_half<EPI>(p, pt, h, si, n0)) continue;
+            if (!gm_half<EPI, HS>(p, pt, h, si, n0)) continue;
             const GemvSeg& sg = p.seg[si];
             uint8_t* raw = sa + kG4A + h * kG4Half;
             tma_load_2d(raw, &sg.tw, n0, st * 64, full + slot, pol);
@@ -187,9 +187,9 @@ __global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_
         const int ng = (2 * st + 1 < G) ? 2 : 1;
         const int k0 = st * 128;
         const int srow = k0 / p.wgrp;
-        for (int h = 0; h < 2; ++h) {
+        for (int h = 0; h < HS; ++h) {
           int si = 0, n0 = 0;
-          const bool valid = gm_half<EPI>(p, pt, h, si, n0);
+          const bool valid = gm_half<EPI, HS>(p, pt, h, si, n0);
           const uint8_t* raw = smem + kG4RawOff + slot * kG4StageAligned + kG4A + h * kG4Half;
           uint8_t* ut = smem + kG4UOff + ub * kG4UStage + h * kG4UTile;
           const bool has_z = valid && p.seg[si].has_z;
@@ -246,7 +246,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_
     bool ok = true;
     for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
       const int pt = t / mtiles;
-      const int nh = 2 * pt + 1 < p.half_tiles ? 2 : 1;
+      const int nh = HS == 2 && 2 * pt + 1 < p.half_tiles ? 2 : 1;
       for (int st = 0; ok && st < nstage; ++st, ++sc) {
         const int slot = sc % kG4Stages;
         const int ub = sc % kG4UBufs;
@@ -321,7 +321,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_
         const float2 as2 = make_float2(as, as);
         const float* wsg = sring + (gc % kG4ScaleSlots) * 2 * 128 + c2 * 64;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
+        for (int c = 0; c < 4 * HS; ++c) {
           const int hh = c >> 2;
           const uint32_t col = b * 256 + hh * 128 + 16 * (c & 3);
           uint32_t r[16];
@@ -348,7 +348,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           int si, n0;
-          if (!gm_half<EPI>(p, pt, hh, si, n0)) continue;
+          if (!gm_half<EPI, HS>(p, pt, hh, si, n0)) continue;
           const GemvSeg& sg = p.seg[si];
           __nv_bfloat16* orow =
               reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<long long>(m) * p.ldo + sg.out_col;
