@@ -276,13 +276,14 @@ def test_gate_up_quant_w4_sweep(pkg, dev, M, wg, zeros):
 
 
 @pytest.mark.parametrize("M,K", [(1, 2048), (4, 6144), (37, 1024), (300, 2048)])
-def test_quant_row_bit_exact(pkg, dev, M, K):
+@pytest.mark.parametrize("pad", [64, 4])   # row stride K + 64: 8 elements per lane; K + 4: 2 per lane
+def test_quant_row_bit_exact(pkg, dev, M, K, pad):
     g = gen(6000 + M + K)
     x = torch.randn(M, K, generator=g)
     x[torch.rand(M, K, generator=g) < 0.001] *= 20.0
     x[0, :64] = 0.0
     xb = x.to(torch.bfloat16)
-    buf = torch.zeros(M, K + 64, dtype=torch.bfloat16, device=dev)
+    buf = torch.zeros(M, K + pad, dtype=torch.bfloat16, device=dev)
     buf[:, :K] = xb.to(dev)
     q = torch.empty(M, K, dtype=torch.int8, device=dev)
     s = torch.empty(M, K // 64, dtype=torch.float32, device=dev)
