@@ -220,6 +220,8 @@ int tune_stream_budget() { static const int v = env_int("QLIN_TUNE_STREAM_BUDGET
 int tune_max_cluster() { static const int v = env_int("QLIN_TUNE_MAX_CLUSTER", 8); return v; }
 // Weight-ring slots of a streamed plan (0: 3 for short launches, 4 for long ones).
 int tune_rb_max() { static const int v = env_int("QLIN_TUNE_RB_MAX", 0); return v; }
+// 128-column halves per GEMM tile for plain outputs (1 or 2; 0: the default, 1).
+int tune_half() { static const int v = env_int("QLIN_TUNE_HALF", 0); return v; }
 // Rows from which W8 projections take the tensor-core GEMM (prefill) path.
 int prefill_min_m() { static const int v = env_int("QLIN_PREFILL_MIN_M", 128); return v; }
 
@@ -904,12 +906,13 @@ int run_prefill_w8(int epi, const GemvArgs& a, int half_tiles, cudaStream_t st) 
   g.fault = di.fault;
   if (epi != kEpiOut) g.half_tiles = 2 * half_tiles;  // (gate tile, up tile) pairs
   const long long mtiles = (a.M + kGmRows - 1) / kGmRows;
-  // Plain outputs whose 256-column tiles would leave SMs idle take one
-  // 128-column half per tile (twice the tiles; a separate kernel instance, so
-  // the two-half tiles compile unchanged).  Measured on B200: W8 K = 5120,
-  // N = 17408 at M = 64 (68 -> 136 tiles) 69 -> 45 us; config-5 down
-  // projection (K = 17408, N = 5120) at M = 256, 40 -> 80 tiles.
-  const int hs = (epi == kEpiOut && mtiles * ((g.half_tiles + 1) / 2) < di.sms) ? 1 : 2;
+  // Plain outputs take one 128-column half per tile (twice the tiles; a
+  // separate kernel instance that drains half the columns per group and
+  // spills nothing).  The fused gate/up keeps its (gate, up) tile pairs.
+  // Measured on B200, config 3 (K = 2048, N = 12288): M = 2048 188 -> 157 us,
+  // M = 512 67 -> 47 us; W8 K = 5120, N = 17408 at M = 64 67 -> 34 us.
+  int hs = epi == kEpiOut ? 1 : 2;
+  if (epi == kEpiOut && (tune_half() == 1 || tune_half() == 2)) hs = tune_half();
   const long long tiles = mtiles * ((g.half_tiles + hs - 1) / hs);
   const int grid = static_cast<int>(tiles < di.sms ? tiles : di.sms);
   switch (epi) {
@@ -984,7 +987,8 @@ int run_prefill_w4(int epi, const GemvArgs& a, int half_tiles, cudaStream_t st) 
   g.fault = di.fault;
   if (epi != kEpiOut) g.half_tiles = 2 * half_tiles;  // (gate tile, up tile) pairs
   const long long mtiles = (a.M + kGmRows - 1) / kGmRows;
-  const int hs = (epi == kEpiOut && mtiles * ((g.half_tiles + 1) / 2) < di.sms) ? 1 : 2;  // as for W8
+  int hs = epi == kEpiOut ? 1 : 2;  // as for W8 (config-3 W4: M = 2048 450 -> 378 us, M = 512 156 -> 107 us)
+  if (epi == kEpiOut && (tune_half() == 1 || tune_half() == 2)) hs = tune_half();
   const long long tiles = mtiles * ((g.half_tiles + hs - 1) / hs);
   const int grid = static_cast<int>(tiles < di.sms ? tiles : di.sms);
   if (epi != kEpiOut) return launch_prefill_w4<kEpiSiluQuant>(g, grid, st);
