@@ -235,11 +235,12 @@ def cpu_setup():
     return O, L, xs
 
 
-def cpu_measure(seconds, max_steps=None):
+def cpu_measure(seconds, max_steps=None, warmup=1):
     cores = len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
     O, L, xs = cpu_setup()
-    cpu_reference_step(O, L, xs)  # warm-up
+    for _ in range(warmup):
+        cpu_reference_step(O, L, xs)
     t0 = time.perf_counter()
     n = 0
     while True:
@@ -263,60 +264,181 @@ def tp_layer_bytes():
     return 2 * w(TP_K, TP_I) + w(TP_I, TP_H)
 
 
-def tp_detail(pkg, dev, world, pg, reps=20):
+def _median_max(pg, dev, values):
+    """Median of this rank's samples, then the max over ranks."""
+    t = torch.tensor([statistics.median(values)], device=dev)
+    if pg:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _graph_us(graph, reps, repeats, pg, dev):
+    """Device time per replay (us): `repeats` samples of `reps` back-to-back
+    replays, each bracketed by CUDA events; median per rank, max over ranks."""
+    samples = []
+    for _ in range(repeats):
+        torch.cuda.synchronize()
+        if pg:
+            pg.barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            graph.replay()
+        e1.record()
+        e1.synchronize()
+        samples.append(e0.elapsed_time(e1) / reps * 1e3)
+    return _median_max(pg, dev, samples)
+
+
+def _tp_parity(pkg, M, world, rank, pg, dev, layer, out, full):
+    """Checks of one column-split forward against the unsplit one-GPU layer
+    (outside any timed region).  Every rank's output must equal rank 0's bit
+    for bit; on rank 0 the gathered h must match the unsplit h by the fused
+    quantisation rule (>= 99.9 % codes equal, all within +-1, scales within 1 %)
+    and the output must be within |d| <= 1e-3 + 1e-2 |ref| of the unsplit down
+    projection of that same h (only the kernels' fp32 K-split order differs).
+    Returns "ok" or the first mismatch (same string on every rank)."""
+    ws = layer._ws[M]
+    hq, hs = ws["hq"], ws["hs"]
+    outs = [torch.empty_like(out) for _ in range(world)] if world > 1 else [out]
+    hqs = [torch.empty_like(hq) for _ in range(world)] if world > 1 else [hq]
+    if world > 1:
+        pg.all_gather(outs, out)
+        pg.all_gather(hqs, hq)
+    msg = "ok"
+    if rank == 0:
+        (gw, gs, gz), (uw, us, uz), (dw, ds, dz) = full
+        hq1 = torch.empty(M, TP_I, dtype=torch.int8, device=dev)
+        hs1 = torch.empty(M, TP_I // 64, dtype=torch.float32, device=dev)
+        pkg.mlp_gate_up_quant_w4(layer._aq, layer._as, gw, gs, uw, us, hq1, hs1, zg=gz, zu=uz)
+        ref = torch.empty(M, TP_H, dtype=torch.bfloat16, device=dev)
+        pkg.gemm_w4(hq, hs, dw, ds, ref, b_z=dz)
+        torch.cuda.synchronize()
+        for r in range(1, world):
+            if not torch.equal(outs[r], outs[0]):
+                msg = f"M={M}: rank {r} output differs from rank 0"
+                break
+            if not torch.equal(hqs[r], hqs[0]):
+                msg = f"M={M}: rank {r} gathered h differs from rank 0"
+                break
+        if msg == "ok":
+            d = (hq.int() - hq1.int()).abs()
+            if int(d.max()) > 1 or float((d == 0).float().mean()) < 0.999:
+                msg = f"M={M}: gathered h vs unsplit h: max code diff {int(d.max())}, " \
+                      f"{float((d == 0).float().mean()) * 100:.3f}% equal"
+            elif not torch.allclose(hs, hs1, rtol=1e-2, atol=0):
+                msg = f"M={M}: gathered h scales differ from the unsplit ones by more than 1%"
+        if msg == "ok":
+            o, r_ = out.float(), ref.float()
+            bad = (o - r_).abs() > 1e-3 + 1e-2 * r_.abs()
+            if bool(bad.any()):
+                i = int(bad.flatten().nonzero()[0])
+                msg = f"M={M}: output vs unsplit down projection: {int(bad.sum())} outside the bar, " \
+                      f"first at {i}: {float(o.flatten()[i])} vs {float(r_.flatten()[i])}"
+    if world > 1:
+        box = [msg]
+        pg.broadcast_object_list(box, src=0)
+        msg = box[0]
+    return msg
+
+
+def tp_detail(pkg, dev, world, rank, pg, reps=20, repeats=5):
     """Config 5: the column-split W4 MLP at M in {1, 4, 64, 256} on `world` GPUs
-    (strong scaling: the whole layer's work is fixed).  Device time per forward
-    (`us`: CUDA-graph replay of kernels + NCCL collectives; `eager_us`: one
-    Python call per forward), CUDA events on the current stream, max over ranks."""
+    (strong scaling: the whole layer's work is fixed).
+
+    Per M: device time per forward (`us`: CUDA-graph replay of the whole
+    forward; `eager_us`: one Python call per forward), the same-run time of
+    the unsplit layer on rank 0's GPU (`one_gpu_us`: the fused gate/up and the
+    down projection of the full weights, graph replay) and their ratio
+    `speedup_vs_1gpu`, the per-stage times of an eager forward (`stages_us`),
+    and a parity check of the split result against the unsplit layer
+    (`_tp_parity`).  CUDA events on the current stream; medians of `repeats`
+    samples per rank, max over ranks."""
     g = torch.Generator(device=dev).manual_seed(5000)
 
     def w(k, n):
         return (torch.randint(0, 256, (k // 2, n), dtype=torch.uint8, device=dev, generator=g),
                 torch.exp(torch.randn(k // TP_WG, n, device=dev, generator=g) * 0.5 - 5.0).to(torch.bfloat16),
                 torch.randint(0, 16, (k // TP_WG, n), dtype=torch.uint8, device=dev, generator=g))
-    gate, up, down = w(TP_K, TP_I), w(TP_K, TP_I), w(TP_I, TP_H)
-    layer = pkg.tp.ColumnParallelW4MLP(gate, up, down, dev)
-    del gate, up, down
+    full = (w(TP_K, TP_I), w(TP_K, TP_I), w(TP_I, TP_H))
+    layer = pkg.tp.ColumnParallelW4MLP(*full, dev)
+    if rank != 0:
+        full = None
     res = {}
+    parity = []
     for M in (1, 4, 64, 256):
         a_q = torch.randint(-127, 128, (M, TP_K), dtype=torch.int8, device=dev, generator=g)
         a_s = torch.rand(M, TP_K // 64, device=dev, generator=g) * 0.02
+        layer._aq, layer._as = a_q, a_s
         out = torch.empty(M, TP_H, dtype=torch.bfloat16, device=dev)
         for _ in range(3):
             layer(a_q, a_s, out)
         torch.cuda.synchronize()
         graph = layer.capture(a_q, a_s, out)
-        times = []
-        for mode in ("eager", "graph"):
+        us = _graph_us(graph, reps, repeats, pg, dev)
+        # eager forwards, with per-stage events on the last of each sample
+        eager, stages = [], []
+        for _ in range(repeats):
             torch.cuda.synchronize()
             if pg:
                 pg.barrier()
             torch.cuda.synchronize()
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
             e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
             e0.record()
-            for _ in range(reps):
-                if mode == "eager":
-                    layer(a_q, a_s, out)
-                else:
-                    graph.replay()
-            e1.record()
-            e1.synchronize()
-            t = torch.tensor([e0.elapsed_time(e1) / reps * 1e3], device=dev)
-            if pg:
-                pg.all_reduce(t, op=pg.ReduceOp.MAX)
-            times.append(float(t.item()))
+            for i in range(reps):
+                layer(a_q, a_s, out, events=ev if i == reps - 1 else None)
+            ev[4].synchronize()
+            eager.append(e0.elapsed_time(ev[4]) / reps * 1e3)
+            stages.append([ev[i].elapsed_time(ev[i + 1]) * 1e3 for i in range(4)])
+        eager_us = _median_max(pg, dev, eager)
+        stage_us = {name: _median_max(pg, dev, [s[i] for s in stages])
+                    for i, name in enumerate(("gate_up", "gather_h", "down", "gather_out"))}
+        torch.cuda.synchronize()
+        # the unsplit layer on rank 0's GPU, same run
+        one_us = torch.zeros(1, device=dev)
+        if rank == 0:
+            (gw, gs, gz), (uw, us_, uz), (dw, ds, dz) = full
+            hq1 = torch.empty(M, TP_I, dtype=torch.int8, device=dev)
+            hs1 = torch.empty(M, TP_I // 64, dtype=torch.float32, device=dev)
+            o1 = torch.empty(M, TP_H, dtype=torch.bfloat16, device=dev)
+
+            def unsplit():
+                pkg.mlp_gate_up_quant_w4(a_q, a_s, gw, gs, uw, us_, hq1, hs1, zg=gz, zu=uz)
+                pkg.gemm_w4(hq1, hs1, dw, ds, o1, b_z=dz)
+            s1 = torch.cuda.Stream(device=dev)
+            s1.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(s1):
+                for _ in range(3):
+                    unsplit()
+            torch.cuda.current_stream(dev).wait_stream(s1)
+            g1 = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g1, stream=s1):
+                unsplit()
+            one_us[0] = _graph_us(g1, reps, repeats, None, dev)
+            del g1
+        if pg:
+            pg.broadcast(one_us, src=0)
+        one = float(one_us.item())
+        parity.append(_tp_parity(pkg, M, world, rank, pg, dev, layer, out, full))
         del graph
-        us = times[1]
-        res[f"M{M}"] = {"us": us, "eager_us": times[0], "weight_tbs": tp_layer_bytes() / us / 1e6}
+        res[f"M{M}"] = {"us": us, "eager_us": eager_us, "one_gpu_us": one, "speedup_vs_1gpu": one / us,
+                        "stages_us": stage_us, "weight_tbs": tp_layer_bytes() / us / 1e6}
     gather = layer.gather
-    if pg:
-        pg.barrier()
     layer.close()
+    bad = [p for p in parity if p != "ok"]
     return {"workload": "config 5: W4 g128 gate_up 5120->2x17408 (fused SiLU+requant) + down 17408->5120, "
                         "columns split over ranks, all-gather of h and of the output",
-            "gather": "NVLink peer-memory stores (own kernel)" if gather == "peer" else "torch.distributed",
-            "n_gpus": world, "scaling": "strong", "layer_weight_bytes": tp_layer_bytes(), "per_M": res}
+            "gather": ("NVLink peer-memory stores into the column slots (own kernel)" if gather == "peer"
+                       else "none (one rank)" if world == 1 else "torch.distributed"),
+            "n_gpus": world, "scaling": "strong", "layer_weight_bytes": tp_layer_bytes(),
+            "parity": bad[0] if bad else "ok",
+            "parity_rule": "ranks bit-equal; gathered h vs unsplit h: >=99.9% codes equal, all within +-1; "
+                           "output vs unsplit down projection of that h: |d| <= 1e-3 + 1e-2|ref|",
+            "timing": f"median of {repeats} samples of {reps} forwards per rank, max over ranks",
+            "per_M": res}
 
 
 def prefill_detail(pkg, dev, gen, reps=20):
@@ -401,12 +523,8 @@ def main():
         if rank != 0:
             return
         per_step = step_bytes()
-        w = min(warmup, 1)
-        O, L, xs = cpu_setup()
-        torch.set_num_threads(len(os.sched_getaffinity(0)))
-        for _ in range(w):
-            cpu_reference_step(O, L, xs)
-        n, el, cores = cpu_measure(args.cpu_seconds, max_steps=args.steps)
+        w = warmup   # the same warm-up as the GPU arm
+        n, el, cores = cpu_measure(args.cpu_seconds, max_steps=args.steps, warmup=w)
         tbs = per_step * n / el / 1e12
         line = {
             "impl": "reference", "metric": METRIC, "value": tbs, "unit": "TB/s", "n_gpus": args.gpus,
@@ -461,16 +579,22 @@ def main():
     if pg:
         pg.barrier()
     torch.cuda.synchronize()
+    # The region of exactly K step replays is timed REPEATS times (at least 10
+    # and at least ~0.5 s in all, so that the clock sampler sees it); the
+    # value is the median region, the max over ranks of each rank's median.
+    samples = []
+    t_start = time.perf_counter()
     with ClockSampler(local) as clk:
-        secs = time_graphs(graphs, args.steps, stream)
+        while len(samples) < 10 or (time.perf_counter() - t_start < 0.5 and len(samples) < 200):
+            samples.append(time_graphs(graphs, args.steps, stream))
         torch.cuda.synchronize()
     if pg:
         pg.barrier()
     torch.cuda.synchronize()
-    t = torch.tensor([secs], device=dev)
+    t = torch.tensor([statistics.median(samples), min(samples), max(samples)], device=dev)
     if pg:
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
-    secs = float(t.item())
+    secs, secs_min, secs_max = (float(v) for v in t.tolist())
     per_step = step_bytes()
     value = per_step * args.steps * world / secs / 1e12
 
@@ -533,7 +657,7 @@ def main():
         e2e_value = float(et.item()) * world
 
     # ---- config 5 (all ranks, collectives) and config 3 (rank-local)
-    tp = tp_detail(pkg, dev, world, pg)
+    tp = tp_detail(pkg, dev, world, rank, pg)
     prefill = prefill_detail(pkg, dev, gen)
 
     cpu = None
@@ -552,14 +676,20 @@ def main():
                             "gate_up 2048->2x6144 fused SiLU+requant, down 6144->2048 +res, o 2048->2048 +res), "
                             "M=1 and M=4 per step",
                 "bytes_per_step": per_step, "weight_copies": COPIES,
-                "l2": "rotating 8 layer copies (~210 MB > 126 MB L2); M=1 and M=4 of a step read different copies",
-                "launches_per_step": LAUNCHES_PER_STEP, "timing": "CUDA graph per step, CUDA events",
+                "l2": "inputs larger than L2: rotating 8 layer copies (~210 MB > 126 MB L2); M=1 and M=4 of a step "
+                      "read different copies",
+                "launches_per_step": LAUNCHES_PER_STEP,
+                "timing": "CUDA graph per step, CUDA events; the K-step region timed repeatedly, median reported",
+                "repeats": len(samples),
+                "ms_per_step_spread": [secs_min / args.steps * 1e3, secs_max / args.steps * 1e3],
                 "parallelism": f"replicas x{world}"},
             "roofline": {"bound": "hbm", "kernel": "mlp_gate_up_quant_w4 M=4 (tcgen05 weight streaming)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": peak_kind, "bytes_per_launch": gu_bytes,
                          "launch_us": gu_launch_s * 1e6,
-                         "traffic": profile_traffic("mlp_gate_up_quant_w4_m4")},
+                         "traffic": profile_traffic("mlp_gate_up_quant_w4_m4"),
+                         "traffic_source": "profiles/mlp_gate_up_quant_w4_m4.md: dram__bytes_read.sum + "
+                                           "dram__bytes_write.sum of one ncu capture of this kernel and shape"},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "TB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "steps": e2e_steps, "ms_per_step": e2e_secs / e2e_steps * 1e3},

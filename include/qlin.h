@@ -28,6 +28,15 @@
  *    ordered normally.
  *  - Return value: QLIN_OK or a qlin_status code; qlin_last_error() gives a
  *    thread-local message for the most recent failure.
+ *  - Device faults.  Every device-side wait (TMA stages, tensor-core commits,
+ *    split-K partial sums, peer arrivals) is bounded in time (2 s, see
+ *    qlin_set_wait_limit_ns).  A wait that gives up records a bit in the
+ *    device fault word and the kernel returns instead of hanging; its outputs
+ *    are then invalid.  Launches are asynchronous, so the launching call has
+ *    already returned QLIN_OK: the fault is reported like CUDA's sticky
+ *    errors instead, by QLIN_ERR_DEVICE_FAULT from every later entry point on
+ *    that device (checked on the host through a mapped pinned word, without
+ *    synchronising), until qlin_device_fault(1) clears it.
  *  - Requirements beyond the reference's (checked, reported as
  *    QLIN_ERR_SHAPE / QLIN_ERR_ALIGNMENT): K % 64 == 0 (the reference
  *    silently assumes it, kernels/common.py:5-7), N % 16 == 0, 16-byte
@@ -65,6 +74,12 @@ const char* qlin_last_error(void);
  * a bitmask of bounded waits that gave up inside qlin kernels since the last
  * clear.  Synchronous; for diagnostics and tests.  Returns -1 on CUDA error. */
 int qlin_device_fault(int clear);
+
+/* Sets the bound of every device-side wait of later launches on the current
+ * device, in nanoseconds (default 2e9).  For tests of the fault path: with a
+ * short bound, a wait that nothing will complete ends quickly.  Not part of
+ * the reference's interface. */
+int qlin_set_wait_limit_ns(int64_t ns);
 
 /* kernels/gemm.py:60-92 (gemm_i8, W8 branch) and gemm.py:20-57 (kernel):
  *   out[m,n] = bf16( (sum_kb float(int32 dot of block kb) * a_s[m,kb]) * b_s[n]
@@ -160,6 +175,41 @@ int qlin_dev_free(void* ptr);
 int qlin_peer_allgather(void* const* bufs, void* const* arrive, void* expected, const void* src,
                         int64_t shard_bytes, int world, int rank, void* dst, void* stream);
 
+/* One 2-D block of this rank's data for qlin_peer_allgather_parts: `rows`
+ * rows of `row_bytes` bytes, `src_ld` bytes apart.  Rank q's block lands in
+ * every rank's gather buffer at byte dst_off + q * row_bytes, rows dst_ld
+ * bytes apart -- so a shard of output COLUMNS goes straight into its column
+ * range of a row-major [rows, world * row_bytes / element size] matrix.
+ * Sizes, strides, offsets and the source address must be multiples of 4
+ * (16 for the fast path). */
+typedef struct {
+  const void* src;
+  int64_t src_ld;
+  int64_t rows;
+  int64_t row_bytes;
+  int64_t dst_off;
+  int64_t dst_ld;
+} qlin_gather_part;
+
+/* Words of the per-rank state array of qlin_peer_allgather_parts. */
+#define QLIN_PEER_STATE_WORDS 16
+
+/* All-gather of one or two 2-D parts (qlin_gather_part) into every rank's
+ * buffer bufs[q] (each must hold dst_off + (rows - 1) * dst_ld +
+ * world * row_bytes bytes for every part), then a wait until every rank's
+ * parts have landed in bufs[rank].  If `dst` is not null, every CTA then
+ * copies the first dst_bytes (multiple of 16) of bufs[rank] to dst within
+ * the same launch.  arrive[q] is rank q's array of `world` uint32 arrival
+ * counters (zero once, never reset); `state` is this rank's device array of
+ * QLIN_PEER_STATE_WORDS uint32 (zero once) holding the expected counts.
+ * Every rank must call it with the same sizes.  A wait that does not finish
+ * within the wait limit records a device fault.  Not part of the
+ * reference's interface (it has no multi-GPU path); the column-split layer
+ * (tp.py) gathers its h codes + scales and its output with it. */
+int qlin_peer_allgather_parts(void* const* bufs, void* const* arrive, void* state,
+                              const qlin_gather_part* parts, int nparts, int world, int rank,
+                              void* dst, int64_t dst_bytes, void* stream);
+
 /* All-gather that allocates nothing, for one rank.  It has no counterpart in
  * the reference.  Meant for a process that runs the column-split layer on a
  * single GPU (world = 1) and may not call cudaMalloc itself -- for instance a
@@ -176,7 +226,11 @@ int qlin_peer_allgather(void* const* bufs, void* const* arrive, void* expected, 
  * stream capture.  Every call on a device shares the same arrays: calls on
  * one stream are ordered, calls that overlap on the GPU (other streams) race.
  * The counters start at zero when the library loads and only grow, so nothing
- * is cleared per call.  (It serves one GPU: a two-GPU form, whose kernels
+ * is cleared per call.  Its wait is bounded like every other: if it gives up,
+ * the call has still returned QLIN_OK and dst holds stale bytes; the fault
+ * word says so (qlin_device_fault, and QLIN_ERR_DEVICE_FAULT from later entry
+ * points once any other entry point has run on the device and set up the
+ * host-visible mirror -- this one allocates nothing, not even that).  (It serves one GPU: a two-GPU form, whose kernels
  * wrote the other GPU's static arrays through peer access, stopped with an
  * illegal memory access on B200, so multi-GPU gathers use
  * qlin_peer_allgather and its caller-allocated buffers.) */

@@ -23,6 +23,7 @@ SIGNATURES = {
     "qlin_status_string": [ctypes.c_int],
     "qlin_last_error": [],
     "qlin_device_fault": [ctypes.c_int],
+    "qlin_set_wait_limit_ns": [_I],
     "qlin_gemm_i8": [_P, _P, _I, _I, _P, _P, _I, _P, _I, _P, _I, _P],
     "qlin_gemm_w4": [_P, _P, _I, _I, _P, _P, _P, _I, _I, _P, _I, _P, _I, _P],
     "qlin_proj3": [_P, _P, _I, _I, _P, _P, _I, _P, _P, _I, _P, _P, _I, _P, _I, _P],
@@ -39,12 +40,22 @@ SIGNATURES = {
     "qlin_dev_alloc": [_I, ctypes.POINTER(ctypes.c_void_p)],
     "qlin_dev_free": [_P],
     "qlin_peer_allgather": [_P, _P, _P, _P, _I, ctypes.c_int, ctypes.c_int, _P, _P],
+    "qlin_peer_allgather_parts": [_P, _P, _P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _I, _P],
     "qlin_peer_allgather_static": [_P, _I, _P, _P],
 }
 _RESTYPES = {
     "qlin_status_string": ctypes.c_char_p,
     "qlin_last_error": ctypes.c_char_p,
 }
+
+
+class GatherPart(ctypes.Structure):
+    """``qlin_gather_part`` of include/qlin.h."""
+    _fields_ = [("src", ctypes.c_void_p), ("src_ld", ctypes.c_int64), ("rows", ctypes.c_int64),
+                ("row_bytes", ctypes.c_int64), ("dst_off", ctypes.c_int64), ("dst_ld", ctypes.c_int64)]
+
+
+PEER_STATE_WORDS = 16  # QLIN_PEER_STATE_WORDS
 
 _lib = None
 _lock = threading.Lock()

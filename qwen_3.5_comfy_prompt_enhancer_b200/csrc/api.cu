@@ -13,7 +13,7 @@
 #include <unordered_map>
 
 #include "../../include/qlin.h"
-#include "gemv.cuh"
+#include "args.cuh"
 #include "quant.cuh"
 #include "peer.cuh"
 #include "tcgemm.cuh"
@@ -54,20 +54,23 @@ int cuda_fail(cudaError_t e, const char* what) {
 
 // ---------------------------------------------------------------- device info
 struct DevInfo {
+  int dev = -1;
   int sms = 0;
-  unsigned* fault = nullptr;
+  unsigned* fault = nullptr;                // device fault word of this GPU
+  volatile unsigned* fault_host = nullptr;  // its host-visible mirror, or null
 };
 
 DevInfo g_dev[kMaxDevices];
 std::mutex g_dev_mu;
 
-int device_info(DevInfo* out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-  if (dev < 0 || dev >= kMaxDevices) return fail(QLIN_ERR_UNSUPPORTED, "device index %d", dev);
+// One mapped pinned host word per device: the kernels' record_fault stores to
+// it, so every later entry point sees a fault without synchronising.
+unsigned* g_fault_host = nullptr;
+
+int device_info_setup(int dev, bool mirror, DevInfo* out) {
   std::lock_guard<std::mutex> lk(g_dev_mu);
   DevInfo& d = g_dev[dev];
+  cudaError_t e;
   if (d.sms == 0) {
     int sms = 0;
     e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -76,10 +79,76 @@ int device_info(DevInfo* out) {
     e = cudaGetSymbolAddress(&fp, g_qlin_fault);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_qlin_fault)");
     d.fault = static_cast<unsigned*>(fp);
+    d.dev = dev;
     d.sms = sms;
+  }
+  if (mirror && !d.fault_host) {
+    if (!g_fault_host) {
+      void* h = nullptr;
+      e = cudaHostAlloc(&h, kMaxDevices * sizeof(unsigned), cudaHostAllocMapped | cudaHostAllocPortable);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaHostAlloc(fault mirror)");
+      memset(h, 0, kMaxDevices * sizeof(unsigned));
+      g_fault_host = static_cast<unsigned*>(h);
+    }
+    void* dp = nullptr;
+    e = cudaHostGetDevicePointer(&dp, g_fault_host + dev, 0);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaHostGetDevicePointer(fault mirror)");
+    e = cudaMemcpyToSymbol(g_qlin_fault_host, &dp, sizeof(dp));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyToSymbol(fault mirror)");
+    d.fault_host = g_fault_host + dev;
   }
   *out = d;
   return QLIN_OK;
+}
+
+int current_device(int* dev) {
+  cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (*dev < 0 || *dev >= kMaxDevices) return fail(QLIN_ERR_UNSUPPORTED, "device index %d", *dev);
+  return QLIN_OK;
+}
+
+// Device attributes, fault word and fault mirror of the current device.  The
+// first call on a device sets them up (and allocates the pinned mirror once
+// per process).
+int device_info(DevInfo* out) {
+  int dev = 0;
+  if (int r = current_device(&dev)) return r;
+  const DevInfo& d = g_dev[dev];
+  if (d.sms != 0 && d.fault_host) {
+    *out = d;
+    return QLIN_OK;
+  }
+  return device_info_setup(dev, true, out);
+}
+
+// As device_info, without the host mirror: allocates nothing.
+int device_info_noalloc(DevInfo* out) {
+  int dev = 0;
+  if (int r = current_device(&dev)) return r;
+  const DevInfo& d = g_dev[dev];
+  if (d.sms != 0) {
+    *out = d;
+    return QLIN_OK;
+  }
+  return device_info_setup(dev, false, out);
+}
+
+// Entry points report a fault recorded by an earlier launch on this device
+// (a bounded device wait that gave up) until qlin_device_fault(1) clears it.
+int sticky_fault(const DevInfo& d) {
+  if (d.fault_host && *d.fault_host)
+    return fail(QLIN_ERR_DEVICE_FAULT,
+                "a bounded device-side wait of an earlier launch on device %d gave up; its results are "
+                "invalid (read and clear with qlin_device_fault(1))",
+                d.dev);
+  return QLIN_OK;
+}
+
+// device_info + sticky_fault: what every launching entry point calls first.
+int launch_info(DevInfo* out) {
+  if (int r = device_info(out)) return r;
+  return sticky_fault(*out);
 }
 
 // ---------------------------------------------------------------- TMA descriptors
@@ -203,121 +272,45 @@ int encode_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
-// Tuning overrides (environment, read once): QLIN_TUNE_SPLIT forces the K
-// split / cluster size, QLIN_TUNE_PDL=0 launches without programmatic
-// dependent launch, QLIN_TUNE_BUDGET_KB sets the per-CTA shared-memory
-// budget.  They change scheduling and the fp32 summation order only.
+// Planner constants.  A build with -DQLIN_TUNING reads overrides of them
+// from the environment once (for on-box sweeps); the shipped library has no
+// run-time switches.  They change scheduling and the fp32 summation order of
+// the K split only, never the integer results.
+//   split          K split / cluster size (0: planner's choice)
+//   budget_kb      per-CTA shared-memory budget (0: 112 KB, 200 KB at one CTA per SM)
+//   ctas_per_sm    cap on co-resident CTAs per SM (0: from tensor memory)
+//   max_level      highest batch-plan level tried (2: one batch)
+//   stream_kb      shared-memory budget of long streamed launches (0: planner's)
+//   max_cluster    largest K split considered
+//   rb_max         weight-ring slots of a streamed plan (0: 3 short, 4 long launches)
+//   half           128-column halves per prefill tile for plain outputs (0/1: 1; 2: two)
+//   prefill_min_m  rows from which projections take the tensor-core GEMM
+//   pdl            programmatic dependent launch (1: on)
+#ifdef QLIN_TUNING
 int env_int(const char* name, int dflt) {
   const char* e = getenv(name);
   return (e && *e) ? atoi(e) : dflt;
 }
-int tune_split() { static const int v = env_int("QLIN_TUNE_SPLIT", 0); return v; }
-int tune_pdl() { static const int v = env_int("QLIN_TUNE_PDL", 1); return v; }
-int tune_budget() { static const int v = env_int("QLIN_TUNE_BUDGET_KB", 0); return v; }
-int tune_ctas_per_sm() { static const int v = env_int("QLIN_TUNE_CTAS_PER_SM", 0); return v; }
-int tune_max_level() { static const int v = env_int("QLIN_TUNE_MAX_LEVEL", 2); return v; }
-int tune_stream_budget() { static const int v = env_int("QLIN_TUNE_STREAM_BUDGET_KB", 0); return v; }
-int tune_max_cluster() { static const int v = env_int("QLIN_TUNE_MAX_CLUSTER", 8); return v; }
-// Weight-ring slots of a streamed plan (0: 3 for short launches, 4 for long ones).
-int tune_rb_max() { static const int v = env_int("QLIN_TUNE_RB_MAX", 0); return v; }
-// 128-column halves per GEMM tile for plain outputs (1 or 2; 0: the default, 1).
-int tune_half() { static const int v = env_int("QLIN_TUNE_HALF", 0); return v; }
-// Rows from which W8 projections take the tensor-core GEMM (prefill) path.
-int prefill_min_m() { static const int v = env_int("QLIN_PREFILL_MIN_M", 128); return v; }
-
-// Kernel family for the small-M path: tcgen05 weight streaming (default) or
-// the CUDA-core dp4a GEMV (QLIN_SMALLM_KERNEL=dp4a, kept for comparison).
-bool use_tc() {
-  static const bool tc = [] {
-    const char* e = getenv("QLIN_SMALLM_KERNEL");
-    return !(e && strcmp(e, "dp4a") == 0);
-  }();
-  return tc;
-}
-
-// ---------------------------------------------------------------- GEMV planning / launch
-struct GemvPlan {
-  int split, ring, gmax;
-  size_t smem;
-};
-
-int gemv_mr(int64_t M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8; }
-
-// Choose the K split (cluster size) that spreads tiles x split CTAs most
-// evenly over the SMs, then the deepest ring that fits the per-CTA budget.
-GemvPlan plan_gemv(int wb, int mr, int ns, int K, int wgrp, int tiles, int rowblocks, int sms) {
-  const int G = K / kGroup;
-  GemvPlan best{1, 1, G, 0};
-  double best_cost = 1e30;
-  const int smax = G < 8 ? G : 8;
-  for (int s = 1; s <= smax; ++s) {
-    const int gmax = (G + s - 1) / s;
-    if (static_cast<long long>(gmax) * 64 * mr > 64 * 1024) continue;  // activation slice
-    const long long ctas = static_cast<long long>(tiles) * s * rowblocks;
-    const double waves = static_cast<double>((ctas + sms - 1) / sms);
-    const double cost = waves / s * (1.0 + 0.02 * s);
-    if (cost < best_cost - 1e-12) {
-      best_cost = cost;
-      best.split = s;
-      best.gmax = gmax;
-    }
+#define QLIN_KNOB(fn, env, dflt) \
+  int fn() {                     \
+    static const int v = env_int(env, dflt); \
+    return v;                    \
   }
-  const long long ctas = static_cast<long long>(tiles) * best.split * rowblocks;
-  // ~110 KB per CTA keeps two CTAs resident per SM: one of this grid and
-  // one of the next launch, which then streams its weights under PDL while
-  // this one finishes.
-  (void)ctas;
-  const uint32_t budget = 110 * 1024;
-  const GemvLayout l1 = gemv_layout(wb, mr, ns, wgrp, best.gmax, 1);
-  const uint32_t fixed = l1.total - l1.ring_bytes;
-  int ring = static_cast<int>((budget > fixed ? budget - fixed : 0) / l1.stage_bytes);
-  if (ring < 2) ring = 2;
-  if (ring > best.gmax) ring = best.gmax;
-  best.ring = ring;
-  best.smem = gemv_layout(wb, mr, ns, wgrp, best.gmax, ring).total;
-  return best;
-}
-
-template <int WB, int MR, int EPI>
-int launch_gemv_t(const GemvArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
-  auto kern = gemv_kernel<WB, MR, EPI>;
-  static std::atomic<unsigned long long> configured{0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const unsigned long long bit = 1ull << (dev & 63);
-  if (!(configured.load() & bit)) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(smem)");
-    configured.fetch_or(bit);
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(kGemvThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = grid.x;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = tune_pdl() ? 1 : 0;
-  cfg.attrs = attr;
-  cfg.numAttrs = 2;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(gemv)");
-  return QLIN_OK;
-}
-
-template <int WB, int EPI>
-int launch_gemv_mr(int mr, const GemvArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
-  switch (mr) {
-    case 1: return launch_gemv_t<WB, 1, EPI>(a, grid, smem, st);
-    case 2: return launch_gemv_t<WB, 2, EPI>(a, grid, smem, st);
-    case 4: return launch_gemv_t<WB, 4, EPI>(a, grid, smem, st);
-    default: return launch_gemv_t<WB, 8, EPI>(a, grid, smem, st);
-  }
-}
+#else
+#define QLIN_KNOB(fn, env, dflt) \
+  constexpr int fn() { return dflt; }
+#endif
+QLIN_KNOB(tune_split, "QLIN_TUNE_SPLIT", 0)
+QLIN_KNOB(tune_pdl, "QLIN_TUNE_PDL", 1)
+QLIN_KNOB(tune_budget, "QLIN_TUNE_BUDGET_KB", 0)
+QLIN_KNOB(tune_ctas_per_sm, "QLIN_TUNE_CTAS_PER_SM", 0)
+QLIN_KNOB(tune_max_level, "QLIN_TUNE_MAX_LEVEL", 2)
+QLIN_KNOB(tune_stream_budget, "QLIN_TUNE_STREAM_BUDGET_KB", 0)
+QLIN_KNOB(tune_max_cluster, "QLIN_TUNE_MAX_CLUSTER", 8)
+QLIN_KNOB(tune_rb_max, "QLIN_TUNE_RB_MAX", 0)
+QLIN_KNOB(tune_half, "QLIN_TUNE_HALF", 0)
+QLIN_KNOB(prefill_min_m, "QLIN_PREFILL_MIN_M", 128)
+#undef QLIN_KNOB
 
 // ---------------------------------------------------------------- tcgen05 path planning / launch
 // Activation rows per row block: 1..16, and 32 for W8 (the W4 drain of 32
@@ -476,7 +469,7 @@ TcPlan plan_tc(int wb, int mr, int ns, int K, int wgrp, int tiles, int rowblocks
   const int smax = G < cmax ? G : cmax;
   for (int s = 1; s <= smax; ++s) {
     TcPlan pl{s, (G + s - 1) / s, 1, 1, 0, 1, 0, 0, 0};
-    if (tune_split() > 0 && s != tune_split() && tune_split() <= smax) continue;
+    if (tune_split() > 0 && s != tune_split() && tune_split() <= smax) continue;  // (tuning builds only)
     const long long ctas = static_cast<long long>(tiles) * s * rowblocks;
     plan_batches(wb, mr, ns, wgrp, ctas, sms, long_stream, one_per_sm, pl);
     if (pl.smem > kTcMaxSmem) continue;
@@ -817,7 +810,7 @@ int choose_tc(int wb, int ns, int64_t M, int K, int wgrp, int tiles, int sms, bo
 
 int run_tc(int wb, int epi, GemvArgs& a, int tiles, cudaStream_t st) {
   DevInfo di;
-  if (int r = device_info(&di)) return r;
+  if (int r = launch_info(&di)) return r;
   const int ns = epi == kEpiOut ? 1 : 2;
   int mr = 0, rowblocks = 0;
   TcPlan pl{};
@@ -878,7 +871,7 @@ int launch_prefill_w8(const GemmArgs& g, int grid, cudaStream_t st) {
 // two segments are gate and up with the same N.
 int run_prefill_w8(int epi, const GemvArgs& a, int half_tiles, cudaStream_t st) {
   DevInfo di;
-  if (int r = device_info(&di)) return r;
+  if (int r = launch_info(&di)) return r;
   GemmArgs g;
   memset(&g, 0, sizeof(g));
   if (int r = make_map(&g.ta, a.a_q, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.K, a.M, a.K, 128, kGmRows, true)) return r;
@@ -912,11 +905,17 @@ int run_prefill_w8(int epi, const GemvArgs& a, int half_tiles, cudaStream_t st) 
   // Measured on B200, config 3 (K = 2048, N = 12288): M = 2048 188 -> 157 us,
   // M = 512 67 -> 47 us; W8 K = 5120, N = 17408 at M = 64 67 -> 34 us.
   int hs = epi == kEpiOut ? 1 : 2;
-  if (epi == kEpiOut && (tune_half() == 1 || tune_half() == 2)) hs = tune_half();
+#ifdef QLIN_TUNING
+  if (epi == kEpiOut && tune_half() == 2) hs = 2;
+#endif
   const long long tiles = mtiles * ((g.half_tiles + hs - 1) / hs);
   const int grid = static_cast<int>(tiles < di.sms ? tiles : di.sms);
   switch (epi) {
-    case kEpiOut: return hs == 1 ? launch_prefill_w8<kEpiOut, 1>(g, grid, st) : launch_prefill_w8<kEpiOut>(g, grid, st);
+    case kEpiOut:
+#ifdef QLIN_TUNING
+      if (hs == 2) return launch_prefill_w8<kEpiOut>(g, grid, st);
+#endif
+      return launch_prefill_w8<kEpiOut, 1>(g, grid, st);
     case kEpiSiluBf16: return launch_prefill_w8<kEpiSiluBf16>(g, grid, st);
     default: return launch_prefill_w8<kEpiSiluQuant>(g, grid, st);
   }
@@ -951,7 +950,7 @@ int launch_prefill_w4(const GemmW4Args& g, int grid, cudaStream_t st) {
 
 int run_prefill_w4(int epi, const GemvArgs& a, int half_tiles, cudaStream_t st) {
   DevInfo di;
-  if (int r = device_info(&di)) return r;
+  if (int r = launch_info(&di)) return r;
   GemmW4Args g;
   memset(&g, 0, sizeof(g));
   if (int r = make_map(&g.ta, a.a_q, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.K, a.M, a.K, 128, kGmRows, true)) return r;
@@ -988,11 +987,16 @@ int run_prefill_w4(int epi, const GemvArgs& a, int half_tiles, cudaStream_t st) 
   if (epi != kEpiOut) g.half_tiles = 2 * half_tiles;  // (gate tile, up tile) pairs
   const long long mtiles = (a.M + kGmRows - 1) / kGmRows;
   int hs = epi == kEpiOut ? 1 : 2;  // as for W8 (config-3 W4: M = 2048 450 -> 378 us, M = 512 156 -> 107 us)
-  if (epi == kEpiOut && (tune_half() == 1 || tune_half() == 2)) hs = tune_half();
+#ifdef QLIN_TUNING
+  if (epi == kEpiOut && tune_half() == 2) hs = 2;
+#endif
   const long long tiles = mtiles * ((g.half_tiles + hs - 1) / hs);
   const int grid = static_cast<int>(tiles < di.sms ? tiles : di.sms);
   if (epi != kEpiOut) return launch_prefill_w4<kEpiSiluQuant>(g, grid, st);
-  return hs == 1 ? launch_prefill_w4<kEpiOut, 1>(g, grid, st) : launch_prefill_w4<kEpiOut>(g, grid, st);
+#ifdef QLIN_TUNING
+  if (hs == 2) return launch_prefill_w4<kEpiOut>(g, grid, st);
+#endif
+  return launch_prefill_w4<kEpiOut, 1>(g, grid, st);
 }
 
 // Fills the split / ring fields of `a`, then launches.
@@ -1012,33 +1016,10 @@ bool mid_m_takes_gemm(int epi, int64_t M, int tiles) {
 }
 
 int run_gemv(int wb, int epi, GemvArgs& a, int tiles, cudaStream_t st) {
-  const bool gemm = use_tc() && (a.M >= prefill_min_m() || mid_m_takes_gemm(epi, a.M, tiles));
+  const bool gemm = a.M >= prefill_min_m() || mid_m_takes_gemm(epi, a.M, tiles);
   if (wb == 8 && gemm) return run_prefill_w8(epi, a, tiles, st);
   if (wb == 4 && gemm && a.wgrp % 64 == 0) return run_prefill_w4(epi, a, tiles, st);
-  if (use_tc()) return run_tc(wb, epi, a, tiles, st);
-  DevInfo di;
-  if (int r = device_info(&di)) return r;
-  const int mr = gemv_mr(a.M);
-  const int rowblocks = (a.M + mr - 1) / mr;
-  if (rowblocks > 65535 || tiles > 65535) return fail(QLIN_ERR_SHAPE, "grid too large (M=%d)", a.M);
-  const int ns = epi == kEpiOut ? 1 : 2;
-  const GemvPlan pl = plan_gemv(wb, mr, ns, a.K, a.wgrp, tiles, rowblocks, di.sms);
-  a.split = pl.split;
-  a.ring = pl.ring;
-  a.gmax = pl.gmax;
-  a.fault = di.fault;
-  const dim3 grid(pl.split, tiles, rowblocks);
-  if (wb == 8) {
-    switch (epi) {
-      case kEpiOut: return launch_gemv_mr<8, kEpiOut>(mr, a, grid, pl.smem, st);
-      case kEpiSiluBf16: return launch_gemv_mr<8, kEpiSiluBf16>(mr, a, grid, pl.smem, st);
-      default: return launch_gemv_mr<8, kEpiSiluQuant>(mr, a, grid, pl.smem, st);
-    }
-  }
-  switch (epi) {
-    case kEpiOut: return launch_gemv_mr<4, kEpiOut>(mr, a, grid, pl.smem, st);
-    default: return launch_gemv_mr<4, kEpiSiluQuant>(mr, a, grid, pl.smem, st);
-  }
+  return run_tc(wb, epi, a, tiles, st);
 }
 
 // ---------------------------------------------------------------- argument checks
@@ -1069,8 +1050,8 @@ int seg_w8(GemvSeg& s, const int8_t* w, const float* bs, int64_t K, int64_t n) {
   if (!aligned(w, 16)) return fail(QLIN_ERR_ALIGNMENT, "W8 weight must be 16-byte aligned");
   if (!aligned(bs, 4)) return fail(QLIN_ERR_ALIGNMENT, "W8 scales must be 4-byte aligned");
   // 128-byte swizzle: the tile lands in the canonical MN-major layout that
-  // tcgen05.mma reads (the dp4a kernel reads plain rows).
-  if (int r = make_map(&s.tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, n, K, n, kTileN, 64, use_tc())) return r;
+  // tcgen05.mma reads.
+  if (int r = make_map(&s.tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, n, K, n, kTileN, 64, true)) return r;
   s.w = w;
   s.bs = bs;
   s.n = static_cast<int>(n);
@@ -1085,9 +1066,8 @@ int seg_w4(GemvSeg& s, const uint8_t* w, const void* sc, const uint8_t* z, int64
     return fail(QLIN_ERR_ALIGNMENT, "W4 weight/scale/zero tensors must be 16-byte aligned");
   const uint32_t nsr = wgrp == 32 ? 2 : 1;
   // 128-byte swizzle for the tcgen05 kernel, which unpacks half of each
-  // group in place into the MMA operand layout; the dp4a kernel reads plain
-  // rows.
-  if (int r = make_map(&s.tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, n, K / 2, n, kTileN, 32, use_tc())) return r;
+  // group in place into the MMA operand layout.
+  if (int r = make_map(&s.tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, n, K / 2, n, kTileN, 32, true)) return r;
   if (int r = make_map(&s.ts, sc, CU_TENSOR_MAP_DATA_TYPE_UINT16, n, K / wgrp, 2 * n, kTileN, nsr)) return r;
   if (z) {
     if (int r = make_map(&s.tz, z, CU_TENSOR_MAP_DATA_TYPE_UINT8, n, K / wgrp, n, kTileN, nsr)) return r;
@@ -1132,6 +1112,32 @@ int static_gather_setup(int dev) {  // with g_static_mu held and `dev` current
   return QLIN_OK;
 }
 
+// Grid of the gather kernel: depends on the sizes only, so every rank (which
+// passes the same sizes) launches the same number of CTAs -- each CTA adds
+// one arrival on every rank.
+int peer_ctas(long long units16) {
+  long long ctas = (units16 + kPeerThreads * 4 - 1) / (kPeerThreads * 4);
+  if (ctas < 1) ctas = 1;
+  if (ctas > kPeerMaxCtas) ctas = kPeerMaxCtas;
+  return static_cast<int>(ctas);
+}
+
+int peer_buffers(PeerGatherArgs& a, void* const* bufs, void* const* arrive, int world) {
+  for (int q = 0; q < world; ++q) {
+    if (!bufs[q] || !arrive[q] || !aligned(bufs[q], 16) || !aligned(arrive[q], 4))
+      return fail(QLIN_ERR_ALIGNMENT, "peer buffer %d is null or misaligned", q);
+    a.bufs[q] = static_cast<uint8_t*>(bufs[q]);
+    a.arrive[q] = static_cast<unsigned*>(arrive[q]);
+  }
+  return QLIN_OK;
+}
+
+int peer_launch(const PeerGatherArgs& a, int ctas, cudaStream_t st) {
+  peer_allgather_kernel<<<ctas, kPeerThreads, 0, st>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "peer_allgather_kernel launch");
+  return QLIN_OK;
+}
 }  // namespace
 }  // namespace qlin
 
@@ -1213,35 +1219,69 @@ int qlin_peer_allgather(void* const* bufs, void* const* arrive, void* expected, 
     return fail(QLIN_ERR_SHAPE, "shard of %lld bytes is not a positive multiple of 16", (long long)shard_bytes);
   if (!aligned(src, 16)) return fail(QLIN_ERR_ALIGNMENT, "source must be 16-byte aligned");
   DevInfo di;
-  if (int r = device_info(&di)) return r;
+  if (int r = launch_info(&di)) return r;
   PeerGatherArgs a;
   memset(&a, 0, sizeof(a));
-  for (int q = 0; q < world; ++q) {
-    if (!bufs[q] || !arrive[q] || !aligned(bufs[q], 16) || !aligned(arrive[q], 4))
-      return fail(QLIN_ERR_ALIGNMENT, "peer buffer %d is null or misaligned", q);
-    a.bufs[q] = static_cast<uint8_t*>(bufs[q]);
-    a.arrive[q] = static_cast<unsigned*>(arrive[q]);
-  }
+  if (int r = peer_buffers(a, bufs, arrive, world)) return r;
   a.expected = static_cast<unsigned*>(expected);
-  a.src = static_cast<const uint8_t*>(src);
-  a.shard_bytes = shard_bytes;
+  // one row of shard_bytes: rank q's shard at byte q * shard_bytes
+  a.part[0] = PeerPart{static_cast<const uint8_t*>(src), 0, 1, shard_bytes, 0, 0, 16};
+  a.nparts = 1;
   a.world = world;
   a.rank = rank;
   a.fault = di.fault;
-  // The grid depends on the shard size only, so every rank launches the same
-  // number of CTAs (each CTA adds one arrival on every rank).
-  long long ctas = (shard_bytes / 16 + kPeerThreads * 4 - 1) / (kPeerThreads * 4);
-  if (ctas < 1) ctas = 1;
-  if (ctas > 64) ctas = 64;
-  peer_allgather_kernel<<<static_cast<int>(ctas), kPeerThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "peer_allgather_kernel launch");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (int r = peer_launch(a, peer_ctas(shard_bytes / 16), st)) return r;
   if (dst) {
-    e = cudaMemcpyAsync(dst, bufs[rank], static_cast<size_t>(shard_bytes) * world, cudaMemcpyDeviceToDevice,
-                        static_cast<cudaStream_t>(stream));
+    cudaError_t e = cudaMemcpyAsync(dst, bufs[rank], static_cast<size_t>(shard_bytes) * world,
+                                    cudaMemcpyDeviceToDevice, st);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(gathered)");
   }
   return QLIN_OK;
+}
+
+int qlin_peer_allgather_parts(void* const* bufs, void* const* arrive, void* state, const qlin_gather_part* parts,
+                              int nparts, int world, int rank, void* dst, int64_t dst_bytes, void* stream) {
+  if (world < 1 || world > kPeerMax || rank < 0 || rank >= world)
+    return fail(QLIN_ERR_INVALID_ARGUMENT, "world %d / rank %d", world, rank);
+  if (!bufs || !arrive || !state || !parts) return fail(QLIN_ERR_INVALID_ARGUMENT, "null argument");
+  if (nparts < 1 || nparts > kPeerMaxParts)
+    return fail(QLIN_ERR_INVALID_ARGUMENT, "%d parts (1 to %d)", nparts, kPeerMaxParts);
+  if (!aligned(state, 4)) return fail(QLIN_ERR_ALIGNMENT, "state must be 4-byte aligned");
+  if (dst && (dst_bytes <= 0 || dst_bytes % 16 != 0 || !aligned(dst, 16)))
+    return fail(QLIN_ERR_ALIGNMENT, "dst must be 16-byte aligned with a positive multiple of 16 bytes");
+  DevInfo di;
+  if (int r = launch_info(&di)) return r;
+  PeerGatherArgs a;
+  memset(&a, 0, sizeof(a));
+  if (int r = peer_buffers(a, bufs, arrive, world)) return r;
+  long long units16 = 0;
+  for (int i = 0; i < nparts; ++i) {
+    const qlin_gather_part& q = parts[i];
+    if (!q.src || q.rows < 1 || q.row_bytes < 4 || q.src_ld < 0 || q.dst_off < 0 || q.dst_ld < 0)
+      return fail(QLIN_ERR_INVALID_ARGUMENT, "part %d: null source or bad size", i);
+    if (q.rows > 1 && (q.src_ld < q.row_bytes || q.dst_ld < static_cast<int64_t>(world) * q.row_bytes))
+      return fail(QLIN_ERR_SHAPE, "part %d: row strides overlap the rows / the ranks' slots", i);
+    auto all_mult = [&](int u) {
+      return q.row_bytes % u == 0 && q.src_ld % u == 0 && q.dst_off % u == 0 && q.dst_ld % u == 0 &&
+             aligned(q.src, u);
+    };
+    const int unit = all_mult(16) ? 16 : all_mult(4) ? 4 : 0;
+    if (!unit) return fail(QLIN_ERR_ALIGNMENT, "part %d: sizes, strides and addresses must be multiples of 4", i);
+    a.part[i] = PeerPart{static_cast<const uint8_t*>(q.src), q.src_ld, q.rows, q.row_bytes, q.dst_off, q.dst_ld,
+                         unit};
+    units16 += (q.rows * q.row_bytes + 15) / 16;
+  }
+  a.nparts = nparts;
+  a.expected = static_cast<unsigned*>(state);
+  a.dst = static_cast<uint8_t*>(dst);
+  a.dst_bytes = dst ? dst_bytes : 0;
+  a.all_wait = dst ? 1 : 0;
+  a.world = world;
+  a.rank = rank;
+  a.fault = di.fault;
+  if (dst && dst_bytes / 16 > units16) units16 = dst_bytes / 16;
+  return peer_launch(a, peer_ctas(units16), static_cast<cudaStream_t>(stream));
 }
 
 int qlin_peer_allgather_static(const void* src, int64_t shard_bytes, void* dst, void* stream) {
@@ -1253,7 +1293,8 @@ int qlin_peer_allgather_static(const void* src, int64_t shard_bytes, void* dst, 
                 (long long)shard_bytes, (long long)kStaticGatherBytes);
   if (!aligned(src, 16)) return fail(QLIN_ERR_ALIGNMENT, "source must be 16-byte aligned");
   DevInfo di;
-  if (int r = device_info(&di)) return r;
+  if (int r = device_info_noalloc(&di)) return r;
+  if (int r = sticky_fault(di)) return r;
   int cur = 0;
   cudaError_t e = cudaGetDevice(&cur);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
@@ -1266,19 +1307,14 @@ int qlin_peer_allgather_static(const void* src, int64_t shard_bytes, void* dst, 
     a.arrive[0] = g_static[cur].arrive;
     a.expected = g_static[cur].expected;
   }
-  a.src = static_cast<const uint8_t*>(src);
-  a.shard_bytes = shard_bytes;
+  a.part[0] = PeerPart{static_cast<const uint8_t*>(src), 0, 1, shard_bytes, 0, 0, 16};
+  a.nparts = 1;
   a.world = 1;
   a.rank = 0;
   a.fault = di.fault;
-  // Same grid rule as qlin_peer_allgather.
-  long long ctas = (shard_bytes / 16 + kPeerThreads * 4 - 1) / (kPeerThreads * 4);
-  if (ctas < 1) ctas = 1;
-  if (ctas > 64) ctas = 64;
-  peer_allgather_kernel<<<static_cast<int>(ctas), kPeerThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
-  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "peer_allgather_kernel launch");
-  e = cudaMemcpyAsync(dst, a.bufs[0], static_cast<size_t>(shard_bytes), cudaMemcpyDeviceToDevice,
-                      static_cast<cudaStream_t>(stream));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (int r = peer_launch(a, peer_ctas(shard_bytes / 16), st)) return r;
+  e = cudaMemcpyAsync(dst, a.bufs[0], static_cast<size_t>(shard_bytes), cudaMemcpyDeviceToDevice, st);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(gathered)");
   return QLIN_OK;
 }
@@ -1321,14 +1357,25 @@ int qlin_max_active_clusters(int wbits, int gate_up, int64_t M, int split, int64
 
 int qlin_device_fault(int clear) {
   DevInfo di;
-  if (device_info(&di) != QLIN_OK) return -1;
+  if (device_info_noalloc(&di) != QLIN_OK) return -1;
   unsigned v = 0;
   if (cudaMemcpyFromSymbol(&v, g_qlin_fault, sizeof(v)) != cudaSuccess) return -1;
   if (clear) {
     const unsigned z = 0;
     if (cudaMemcpyToSymbol(g_qlin_fault, &z, sizeof(z)) != cudaSuccess) return -1;
+    if (di.fault_host) *di.fault_host = 0;
   }
   return static_cast<int>(v);
+}
+
+int qlin_set_wait_limit_ns(int64_t ns) {
+  if (ns <= 0) return fail(QLIN_ERR_INVALID_ARGUMENT, "wait limit must be positive");
+  DevInfo di;
+  if (int r = device_info_noalloc(&di)) return r;
+  const unsigned long long v = static_cast<unsigned long long>(ns);
+  cudaError_t e = cudaMemcpyToSymbol(g_qlin_wait_ns, &v, sizeof(v));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyToSymbol(wait limit)");
+  return QLIN_OK;
 }
 
 int qlin_gemm_i8(const int8_t* a_q, const float* a_s, int64_t M, int64_t K, const int8_t* b,
@@ -1533,6 +1580,8 @@ int qlin_quant_row(const void* x, int64_t ldx, int64_t M, int64_t K, int8_t* q, 
   if (ldx < K) return fail(QLIN_ERR_SHAPE, "row stride smaller than K");
   if (!aligned(x, 4) || (ldx % 2) != 0 || !aligned(q, 2) || !aligned(s, 4))
     return fail(QLIN_ERR_ALIGNMENT, "x needs 4-byte aligned rows, q 2-byte, s 4-byte alignment");
+  DevInfo di;
+  if (int r = launch_info(&di)) return r;
   const int G = static_cast<int>(K / kGroup);
   // 16-byte rows: 8 elements per lane (measured on B200 at M = K = 2048: ~10 us
   // with 2 elements per lane); otherwise the 2-element kernel.

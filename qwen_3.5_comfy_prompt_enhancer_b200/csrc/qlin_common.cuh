@@ -21,10 +21,29 @@ enum : unsigned {
   kFaultMmaWait = 8u,       // tcgen05 commit wait
 };
 
-// Bound on any single mbarrier wait, in nanoseconds of %globaltimer.  A wait
-// that has not completed after this long records a fault bit and returns, so
-// a logic error surfaces as an error status instead of a hung GPU.
+// Bound on any single device-side wait, in nanoseconds of %globaltimer
+// (2 s unless qlin_set_wait_limit_ns changed it on this device).  A wait that
+// has not completed after this long records a fault bit and returns, so a
+// logic error surfaces as an error status instead of a hung GPU.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+__device__ unsigned long long g_qlin_wait_ns = kWaitLimitNs;
+
+// Host-visible mirror of the fault word (mapped pinned host memory, or null
+// until the library has set it up on this device).  record_fault writes it
+// with a plain store, so the host learns of a fault without synchronising.
+__device__ unsigned* g_qlin_fault_host = nullptr;
+
+__device__ __forceinline__ unsigned long long wait_limit_ns() {
+  return *reinterpret_cast<volatile unsigned long long*>(&g_qlin_wait_ns);
+}
+
+// Records that a bounded wait gave up: `bit` into the device fault word and
+// a non-zero value into the host-visible mirror.
+__device__ __forceinline__ void record_fault(unsigned* fault, unsigned bit) {
+  atomicOr(fault, bit);
+  unsigned* h = *reinterpret_cast<unsigned* volatile*>(&g_qlin_fault_host);
+  if (h) *reinterpret_cast<volatile unsigned*>(h) = 1u;
+}
 
 __device__ __forceinline__ unsigned long long global_ns() {
   unsigned long long t;
@@ -67,13 +86,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 // Bounded wait for the phase with the given parity to complete (try_wait
 // already suspends the thread in hardware between polls).  Returns false if
-// the phase did not complete within kWaitLimitNs.
+// the phase did not complete within the wait limit.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0 && global_ns() - t0 > kWaitLimitNs) return false;
+    if ((i & 255u) == 0 && global_ns() - t0 > wait_limit_ns()) return false;
   }
 }
 
@@ -93,7 +112,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
   const unsigned long long t0 = global_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
-    if ((i & 255u) == 0 && global_ns() - t0 > kWaitLimitNs) return false;
+    if ((i & 255u) == 0 && global_ns() - t0 > wait_limit_ns()) return false;
   }
 }
 
@@ -183,29 +202,8 @@ __device__ __forceinline__ bool named_bar_and(int id, int nthreads, bool pred) {
 }
 
 // ---------------------------------------------------------------- integer dots
-// d = c + sum_i a.u8[i] * b.s8[i]
-__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
-  int d;
-  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
-}
 // d = c + sum_i a.s8[i] * b.s8[i]
 __device__ __forceinline__ int dp4a_ss(int a, int b, int c) { return __dp4a(a, b, c); }
-
-// 4x4 byte transpose: rows r0..r3 each hold 4 column bytes; on return c_j
-// holds column j's 4 bytes in row order (byte i = row i).
-__device__ __forceinline__ void transpose4x4(uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3,
-                                             uint32_t& c0, uint32_t& c1, uint32_t& c2,
-                                             uint32_t& c3) {
-  const uint32_t t0 = __byte_perm(r0, r1, 0x5140);  // a0 b0 a1 b1
-  const uint32_t t1 = __byte_perm(r0, r1, 0x7362);  // a2 b2 a3 b3
-  const uint32_t t2 = __byte_perm(r2, r3, 0x5140);  // c0 d0 c1 d1
-  const uint32_t t3 = __byte_perm(r2, r3, 0x7362);  // c2 d2 c3 d3
-  c0 = __byte_perm(t0, t2, 0x5410);
-  c1 = __byte_perm(t0, t2, 0x7632);
-  c2 = __byte_perm(t1, t3, 0x5410);
-  c3 = __byte_perm(t1, t3, 0x7632);
-}
 
 // ---------------------------------------------------------------- reference rounding
 // kernels/common.py:24-29: trunc(v + (v >= 0 ? 0.5 : -0.5)) clamped to [-127, 127].

@@ -32,7 +32,7 @@
 //               residual) and stores bf16.
 #pragma once
 
-#include "gemv.cuh"
+#include "args.cuh"
 #include "qlin_common.cuh"
 
 namespace qlin {
@@ -223,7 +223,7 @@ __global__ void __launch_bounds__(kGmThreads, 1) tc_gemm_kernel(const __grid_con
         __syncwarp();
       }
     }
-    if (!ok && lane == 0) atomicOr(p.fault, kFaultEmptyWait);
+    if (!ok && lane == 0) record_fault(p.fault, kFaultEmptyWait);
     // Copies still in flight land before the CTA may exit.
     const uint32_t issued = sc;
     for (uint32_t i = issued > kGmStages ? issued - kGmStages : 0; i < issued; ++i)
@@ -263,7 +263,7 @@ __global__ void __launch_bounds__(kGmThreads, 1) tc_gemm_kernel(const __grid_con
         }
       }
     }
-    if (!ok && lane == 0) atomicOr(p.fault, kFaultMmaWait);
+    if (!ok && lane == 0) record_fault(p.fault, kFaultMmaWait);
   } else {
     // ------------------------------------------------------------------ epilogue
     // Thread = one row (TMEM lane) x the 64 columns [64c2, 64c2 + 64) of BOTH
@@ -375,7 +375,7 @@ __global__ void __launch_bounds__(kGmThreads, 1) tc_gemm_kernel(const __grid_con
         gm_gate_up_epilogue<EPI>(p, m, pt * kTileN + c2 * 64, acc, p.seg[0].bs, p.seg[1].bs);
       }
     }
-    if (!ok && lane == 0) atomicOr(p.fault, kFaultFullWait);
+    if (!ok && lane == 0) record_fault(p.fault, kFaultFullWait);
   }
   pdl_launch_dependents();
   tc_fence_before();

@@ -165,7 +165,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_
         __syncwarp();
       }
     }
-    if (!ok && lane == 0) atomicOr(p.fault, kFaultEmptyWait);
+    if (!ok && lane == 0) record_fault(p.fault, kFaultEmptyWait);
     const uint32_t issued = sc;
     for (uint32_t i = issued > kG4Stages ? issued - kG4Stages : 0; i < issued; ++i)
       mbar_wait(full + i % kG4Stages, (i / kG4Stages) & 1);
@@ -238,7 +238,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_
         gbase += ng;
       }
     }
-    if (!ok && lane == 0) atomicOr(p.fault, kFaultFullWait);
+    if (!ok && lane == 0) record_fault(p.fault, kFaultFullWait);
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     constexpr uint32_t idesc = idesc_i8(128, 128, true, true, false, true);
@@ -278,7 +278,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_
         }
       }
     }
-    if (!ok && lane == 0) atomicOr(p.fault, kFaultMmaWait);
+    if (!ok && lane == 0) record_fault(p.fault, kFaultMmaWait);
   } else {
     // ------------------------------------------------------------------ epilogue (warps 2-9)
     // Thread = one row (TMEM lane) x the 64 columns [64c2, 64c2 + 64) of both
@@ -392,7 +392,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_
         gm_gate_up_epilogue<EPI>(p, m, pt * kTileN + c2 * 64, acc, nullptr, nullptr);
       }
     }
-    if (!ok && lane == 0) atomicOr(p.fault, kFaultFullWait);
+    if (!ok && lane == 0) record_fault(p.fault, kFaultFullWait);
   }
   pdl_launch_dependents();
   tc_fence_before();

@@ -49,7 +49,7 @@
 
 #include <cooperative_groups.h>
 
-#include "gemv.cuh"
+#include "args.cuh"
 #include "qlin_common.cuh"
 
 namespace qlin {
@@ -306,7 +306,7 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
     for (int b = prefill; b < nbatch; ++b) {
       const int rs = b % RB;
       if (!mbar_wait(empty + rs, ((b / RB) & 1) ^ 1)) {
-        if (lane == 0) atomicOr(p.fault, kFaultEmptyWait);
+        if (lane == 0) record_fault(p.fault, kFaultEmptyWait);
         break;
       }
       if (elect_one()) issue_batch(b, pol);
@@ -358,7 +358,7 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
       }
       __syncwarp();
     }
-    if (!ok && lane == 0) atomicOr(p.fault, kFaultMmaWait);
+    if (!ok && lane == 0) record_fault(p.fault, kFaultMmaWait);
   } else if (is_drain) {
     // ------------------------------------------------------------------ drain
     const int td = threadIdx.x - kTcWarpDrain * 32;
@@ -452,7 +452,7 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
         if (lane == 0) mbar_arrive(empty + rs);
       }
     }
-    if (!ok && lane == 0) atomicOr(p.fault, kFaultFullWait);
+    if (!ok && lane == 0) record_fault(p.fault, kFaultFullWait);
     if (p.part_alias && rank == 0) {
       // The last accumulator batch was observed: every MMA of this CTA has
       // completed, so its operand region is free to receive the other
@@ -513,7 +513,7 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
         }
       }
       if (!ok) {
-        if (lane == 0) atomicOr(p.fault, kFaultFullWait);
+        if (lane == 0) record_fault(p.fault, kFaultFullWait);
         break;
       }
       fence_proxy_async_smem();
@@ -532,12 +532,14 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
   // Ranks 1..split-1 push their partial sums into rank 0's shared memory with
   // asynchronous stores, each completing 4 bytes of rank 0's receive barrier
   // (armed at set-up with the total), then exit: nothing reads their shared
-  // memory, so no closing cluster barrier.
+  // memory, so no closing cluster barrier.  This relies on rank 0 outliving
+  // every remote store: it exits only after its receive barrier completed (or
+  // after two bounded waits for it, on the fault path).
   if (is_drain && rank > 0) {
     bool go = true;
     if (p.part_alias && !mbar_wait_cluster(ready, 0)) {
       go = false;
-      if (lane == 0) atomicOr(p.fault, kFaultFullWait);
+      if (lane == 0) record_fault(p.fault, kFaultFullWait);
     }
     if (go) {
       const uint32_t slot0 = smem_u32(part + static_cast<size_t>(rank - 1) * NS * MR * kTileN);
@@ -559,7 +561,13 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
 #pragma unroll
       for (int m = 0; m < MR; ++m) vs[s][m] = acc[s][m];
     if (p.split > 1 && !mbar_wait_cluster(recv, 0)) {
-      if (lane == 0) atomicOr(p.fault, kFaultFullWait);
+      if (lane == 0) record_fault(p.fault, kFaultFullWait);
+      // The other ranks exit without a closing cluster barrier, so this CTA
+      // must outlive their remote stores into its shared memory.  After a
+      // timed-out receive it waits once more (bounded) for late partial sums
+      // before it exits; the launch's result is wrong either way and the
+      // fault word says so.
+      mbar_wait_cluster(recv, 0);
     } else {
       for (int r = 1; r < p.split; ++r) {
         const float* rp = part + static_cast<size_t>(r - 1) * NS * MR * kTileN;

@@ -9,22 +9,28 @@ launch shape, can differ):
   1. fused gate/up + SiLU + per-64 requantisation on the local columns
      (``mlp_gate_up_quant_w4``; the 64-column quantisation groups stay on one
      rank because I/g is a multiple of 64);
-  2. one all-gather of the int8 codes and their scales (packed in one byte
-     buffer per rank) -> the full h [M, I] on every rank: by default this
-     package's kernel storing straight into the peers' memory over NVLink
-     (``PeerGather``), or torch.distributed's all-gather (NCCL / gloo);
+  2. all-gather of the int8 codes and their scales -> the full h [M, I] and
+     its scales [M, I/64] on every rank;
   3. down projection of the full h against the local down columns
      (``gemm_w4``);
   4. all-gather of the bf16 outputs -> [M, H] on every rank.
+
+With CUDA and world > 1 the gathers are this package's own kernel
+(``qlin_peer_allgather_parts``): each rank stores its column shard straight
+into its column range of every rank's h / output matrix over NVLink (CUDA IPC
+buffers, no NCCL on the data path), so the down projection reads h where it
+landed and the output gather also copies the result into ``out`` in the same
+launch -- four launches per forward.  ``gather="dist"`` uses
+``torch.distributed.all_gather_into_tensor`` (NCCL or gloo) and a column
+reassembly instead; that is the path the CPU tests take.
 
 A K (row) split would add an all-reduce of fp32 partial sums across ranks, so
 it is not used.  Weights are given in the engine layouts (packed uint8 [K/2, N],
 bf16 scales [K/WG, N], optional uint8 zeros [K/WG, N]); each rank keeps a
 contiguous copy of its columns only.
-
-The compute calls go through ``ops`` (default: this package's CUDA kernels);
-collectives use ``torch.distributed`` on the given process group.
 """
+import ctypes
+
 import torch
 import torch.distributed as dist
 
@@ -43,41 +49,56 @@ def _cols(t, lo, hi):
     return None if t is None else t[:, lo:hi].contiguous()
 
 
-class PeerGather:
-    """All-gather of equal byte shards over NVLink peer memory with this
-    package's own kernel (``qlin_peer_allgather``): each rank stores its shard
-    straight into every rank's gather buffer and bumps arrival counters held
-    in the peers' memory; no NCCL call on the data path.
+def _pad16(n):
+    return -(-n // 16) * 16
 
-    One cudaMalloc'd allocation per rank and gather holds the gather buffer
-    (world x shard bytes) and the arrival counters; its CUDA IPC handle is
-    exchanged once through the process group (``group`` must reach every
-    rank).  Each call copies the gathered bytes, rank-major like
-    ``all_gather_into_tensor``, into the torch tensor ``buf``."""
 
-    def __init__(self, shard_bytes, device, group=None):
-        import ctypes
+class _DeviceBytes:
+    """``__cuda_array_interface__`` over raw device memory, so that torch can
+    view a buffer this package allocated (``torch.as_tensor``, no copy)."""
+
+    def __init__(self, ptr, nbytes):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                         "strides": None, "version": 3}
+
+
+class PeerBuffer:
+    """A gather buffer of ``nbytes`` on every rank of ``group``, written by
+    every rank over NVLink peer memory (``qlin_peer_allgather_parts``).
+
+    Each rank allocates its own buffer (one cudaMalloc of its own, shared
+    through one CUDA IPC handle exchanged once over the process group) with
+    its arrival counters behind it, plus a small state array.  ``local`` is a
+    torch uint8 view of this rank's buffer."""
+
+    def __init__(self, nbytes, device, group=None):
         from . import _lib
         self._lib = _lib.load()
-        self.world = dist.get_world_size(group)
-        self.rank = dist.get_rank(group)
-        self.shard = -(-shard_bytes // 16) * 16
+        self._check = _lib.check
+        init = dist.is_initialized()
+        self.world = dist.get_world_size(group) if init else 1
+        self.rank = dist.get_rank(group) if init else 0
+        self.nbytes = _pad16(nbytes)
         self.device = torch.device(device)
-        gbytes = self.world * self.shard
+        total = self.nbytes + 256
         with torch.cuda.device(self.device):
             own = ctypes.c_void_p()
-            _lib.check("qlin_dev_alloc", self._lib.qlin_dev_alloc(gbytes + 256, ctypes.byref(own)))
+            _lib.check("qlin_dev_alloc", self._lib.qlin_dev_alloc(total, ctypes.byref(own)))
             self._own = own.value
             handle = (ctypes.c_ubyte * 64)()
             off = ctypes.c_int64()
             _lib.check("qlin_ipc_get_handle", self._lib.qlin_ipc_get_handle(self._own, handle, ctypes.byref(off)))
-        self.buf = torch.empty(gbytes, dtype=torch.uint8, device=self.device)
-        self.expected = torch.zeros(self.world, dtype=torch.int32, device=self.device)
-        mine = torch.tensor(list(bytes(handle)) + list(off.value.to_bytes(8, "little")), dtype=torch.uint8,
-                            device=self.device)
-        allh = torch.empty(self.world * 72, dtype=torch.uint8, device=self.device)
-        dist.all_gather_into_tensor(allh, mine, group=group)
-        allh = allh.view(self.world, 72).cpu()
+        self.local = torch.as_tensor(_DeviceBytes(self._own, self.nbytes), device=self.device)
+        self.state = torch.zeros(_lib.PEER_STATE_WORDS, dtype=torch.int32, device=self.device)
+        mine = torch.tensor(list(bytes(handle)) + list(off.value.to_bytes(8, "little")), dtype=torch.uint8)
+        if self.world > 1:
+            # the handles travel as device tensors over NCCL, as CPU tensors otherwise
+            where = self.device if dist.get_backend(group) == "nccl" else torch.device("cpu")
+            allh = torch.empty(self.world * 72, dtype=torch.uint8, device=where)
+            dist.all_gather_into_tensor(allh, mine.to(where), group=group)
+            allh = allh.view(self.world, 72).cpu()
+        else:
+            allh = mine.view(1, 72)
         self._opened = []
         bufs, arrive = [], []
         with torch.cuda.device(self.device):
@@ -92,31 +113,41 @@ class PeerGather:
                     base = ptr.value
                     self._opened.append((base, qoff))
                 bufs.append(base)
-                arrive.append(base + gbytes)
+                arrive.append(base + self.nbytes)
         self._bufs = (ctypes.c_void_p * self.world)(*bufs)
         self._arrive = (ctypes.c_void_p * self.world)(*arrive)
         torch.cuda.synchronize(self.device)
-        dist.barrier(group=group)   # every rank's counters are zero before anyone writes
+        if self.world > 1:
+            dist.barrier(group=group)   # every rank's counters are zero before anyone writes
 
-    def __call__(self, src):
-        """Gather ``src`` (``shard`` bytes, contiguous) from every rank; returns ``buf``,
-        the rank-major bytes [world * shard]."""
+    def gather(self, parts, out=None, out_bytes=0):
+        """All-gather ``parts`` (a list of ``_lib.GatherPart``) into every rank's
+        buffer; with ``out``, this rank's gathered first ``out_bytes`` are then
+        copied to the tensor ``out`` in the same launch."""
         from .kernels._host import stream_of
-        from . import _lib
-        rc = self._lib.qlin_peer_allgather(self._bufs, self._arrive, self.expected.data_ptr(), src.data_ptr(),
-                                           self.shard, self.world, self.rank, self.buf.data_ptr(), stream_of(src))
-        _lib.check("qlin_peer_allgather", rc)
-        return self.buf
+        arr = (type(parts[0]) * len(parts))(*parts)
+        rc = self._lib.qlin_peer_allgather_parts(
+            self._bufs, self._arrive, self.state.data_ptr(), arr, len(parts), self.world, self.rank,
+            None if out is None else out.data_ptr(), out_bytes, stream_of(self.local))
+        self._check("qlin_peer_allgather_parts", rc)
 
     def close(self):
-        """Unmap the peers' buffers and free this rank's (after every rank stopped using them)."""
+        """Unmap the peers' buffers and free this rank's.  The caller must
+        make sure every rank has stopped using them first (GPU work
+        synchronised, then a barrier), as ColumnParallelW4MLP.close does."""
         with torch.cuda.device(self.device):
             for base, off in self._opened:
                 self._lib.qlin_ipc_close(base, off)
             self._opened = []
+            self.local = None
             if self._own:
                 self._lib.qlin_dev_free(self._own)
                 self._own = None
+
+
+def _part(src, rows, row_bytes, src_ld, dst_off, dst_ld):
+    from ._lib import GatherPart
+    return GatherPart(src.data_ptr(), src_ld, rows, row_bytes, dst_off, dst_ld)
 
 
 class _KernelOps:
@@ -167,87 +198,127 @@ class ColumnParallelW4MLP:
 
     def _workspace(self, M):
         ws = self._ws.get(M)
-        if ws is None:
-            d, g = self.device, self.world
-            nq, ns = M * self.i_loc, M * (self.i_loc // GROUP) * 4
-            # The local int8 codes and their fp32 scales share one byte buffer
-            # (padded to 16 bytes), so a single all-gather moves both.
-            pack = torch.zeros(-(-(nq + ns) // 16) * 16, dtype=torch.uint8, device=d)
-            ws = {
-                "pack": pack,
-                "hq_loc": pack[:nq].view(torch.int8).view(M, self.i_loc),
-                "hs_loc": pack[nq:nq + ns].view(torch.float32).view(M, self.i_loc // GROUP),
-                "pack_all": torch.empty(g * pack.numel(), dtype=torch.uint8, device=d),
-                "hq": torch.empty(M, self.inter, dtype=torch.int8, device=d),
-                "hs": torch.empty(M, self.inter // GROUP, dtype=torch.float32, device=d),
-                "o_loc": torch.empty(M, self.h_loc, dtype=torch.bfloat16, device=d),
-                "o_all": torch.empty(g * M, self.h_loc, dtype=torch.bfloat16, device=d),
-            }
-            if self.gather == "peer":
-                ws["peer_h"] = PeerGather(pack.numel(), d, self.group)
-                ws["peer_o"] = PeerGather(M * self.h_loc * 2, d, self.group)
-            self._ws[M] = ws
+        if ws is not None:
+            return ws
+        d, g, r = self.device, self.world, self.rank
+        ng_loc, ng = self.i_loc // GROUP, self.inter // GROUP
+        ws = {
+            "hq_loc": torch.empty(M, self.i_loc, dtype=torch.int8, device=d),
+            "hs_loc": torch.empty(M, ng_loc, dtype=torch.float32, device=d),
+        }
+        if g == 1:
+            # nothing to gather: h is the local h, the output is written in place
+            ws["hq"], ws["hs"] = ws["hq_loc"], ws["hs_loc"]
+        elif self.gather == "peer":
+            # h codes at byte 0 and h scales at hs_off of one gather buffer;
+            # the output matrix in a second one.  Rank r's shards land in their
+            # column ranges, so hq / hs / out_full are ordinary row-major views.
+            hs_off = _pad16(M * self.inter)
+            hbuf = PeerBuffer(hs_off + M * ng * 4, d, self.group)
+            obuf = PeerBuffer(M * self.hidden * 2, d, self.group)
+            out_full = obuf.local[:M * self.hidden * 2].view(torch.bfloat16).view(M, self.hidden)
+            ws.update(
+                hbuf=hbuf, obuf=obuf,
+                hq=hbuf.local[:M * self.inter].view(torch.int8).view(M, self.inter),
+                hs=hbuf.local[hs_off:hs_off + M * ng * 4].view(torch.float32).view(M, ng),
+                out_full=out_full,
+                o_slot=out_full[:, r * self.h_loc:(r + 1) * self.h_loc],
+                h_parts=[_part(ws["hq_loc"], M, self.i_loc, self.i_loc, 0, self.inter),
+                         _part(ws["hs_loc"], M, ng_loc * 4, ng_loc * 4, hs_off, ng * 4)])
+            ws["o_parts"] = [_part(ws["o_slot"], M, self.h_loc * 2, self.hidden * 2, 0, self.hidden * 2)]
+        else:
+            nq, ns = M * self.i_loc, M * ng_loc * 4
+            # the local codes and scales share one byte buffer, so a single
+            # all-gather moves both
+            pack = torch.zeros(_pad16(nq + ns), dtype=torch.uint8, device=d)
+            ws.update(
+                pack=pack,
+                hq_loc=pack[:nq].view(torch.int8).view(M, self.i_loc),
+                hs_loc=pack[nq:nq + ns].view(torch.float32).view(M, ng_loc),
+                pack_all=torch.empty(g * pack.numel(), dtype=torch.uint8, device=d),
+                hq=torch.empty(M, self.inter, dtype=torch.int8, device=d),
+                hs=torch.empty(M, ng, dtype=torch.float32, device=d),
+                o_loc=torch.empty(M, self.h_loc, dtype=torch.bfloat16, device=d),
+                o_all=torch.empty(g * M, self.h_loc, dtype=torch.bfloat16, device=d))
+        self._ws[M] = ws
         return ws
 
-    def _gather_h(self, ws, M):
-        """All-gather the packed (codes, scales) shards; reassemble h [M, I] and its scales."""
-        if self.world == 1:
-            ws["hq"].copy_(ws["hq_loc"])
-            ws["hs"].copy_(ws["hs_loc"])
-            return ws["hq"], ws["hs"]
-        if self.gather == "peer":
-            allp = ws["peer_h"](ws["pack"]).view(self.world, -1)
-        else:
-            dist.all_gather_into_tensor(ws["pack_all"], ws["pack"], group=self.group)
-            allp = ws["pack_all"].view(self.world, -1)
+    def _gather_h_dist(self, ws, M):
+        """torch.distributed all-gather of the packed (codes, scales) shards,
+        then the column reassembly of h [M, I] and its scales."""
+        dist.all_gather_into_tensor(ws["pack_all"], ws["pack"], group=self.group)
+        allp = ws["pack_all"].view(self.world, -1)
         g, n, ng = self.world, self.i_loc, self.i_loc // GROUP
         nq = M * n
         codes = allp[:, :nq].view(torch.int8).view(g, M, n)
         scales = allp[:, nq:nq + M * ng * 4].contiguous().view(torch.float32).view(g, M, ng)
         ws["hq"].view(M, g, n).copy_(codes.permute(1, 0, 2))
         ws["hs"].view(M, g, ng).copy_(scales.permute(1, 0, 2))
-        return ws["hq"], ws["hs"]
 
-    def _gather_cols(self, loc, allbuf, full):
-        """all-gather [M, n] shards into [M, world * n] (rank r at columns r*n)."""
-        if self.world == 1:
-            full.copy_(loc)
-            return full
-        dist.all_gather_into_tensor(allbuf, loc, group=self.group)   # [world * M, n], rank-major
-        M, n = loc.shape
-        full.view(M, self.world, n).copy_(allbuf.view(self.world, M, n).permute(1, 0, 2))
-        return full
+    def forward(self, a_q, a_s, out, events=None):
+        """a_q int8 [M, K], a_s fp32 [M, K/64] -> out bf16 [M, H] (every rank).
 
-    def forward(self, a_q, a_s, out):
-        """a_q int8 [M, K], a_s fp32 [M, K/64] -> out bf16 [M, H] (every rank)."""
+        ``events``: optional list of five CUDA events, recorded before the
+        gate/up projection and after it, the h gather, the down projection
+        and the output gather (per-stage timing)."""
         M = a_q.shape[0]
         if a_q.shape[1] != self.k or out.shape != (M, self.hidden):
             raise ValueError("activation / output shape does not match the layer")
         ws = self._workspace(M)
         g, u, d = self.gate, self.up, self.down
+        rec = (lambda i: events[i].record()) if events else (lambda i: None)
+        rec(0)
         self.ops.gate_up_quant_w4(a_q, a_s, g[0], g[1], u[0], u[1], ws["hq_loc"], ws["hs_loc"], zg=g[2], zu=u[2])
-        hq, hs = self._gather_h(ws, M)
-        self.ops.gemm_w4(hq, hs, d[0], d[1], ws["o_loc"], b_z=d[2])
-        if self.gather == "peer" and self.world > 1:
-            allo = ws["peer_o"](ws["o_loc"]).view(torch.bfloat16).view(self.world, M, self.h_loc)
-            out.view(M, self.world, self.h_loc).copy_(allo.permute(1, 0, 2))
+        rec(1)
+        if self.world == 1:
+            rec(2)
+            self.ops.gemm_w4(ws["hq"], ws["hs"], d[0], d[1], out, b_z=d[2])
+            rec(3)
+            rec(4)
             return out
-        return self._gather_cols(ws["o_loc"], ws["o_all"], out)
-
-    def close(self):
-        """Release the peer mappings (before the process group is destroyed)."""
-        for ws in self._ws.values():
-            for k in ("peer_h", "peer_o"):
-                if k in ws:
-                    ws[k].close()
-        self._ws = {}
+        if self.gather == "peer":
+            ws["hbuf"].gather(ws["h_parts"])
+            rec(2)
+            self.ops.gemm_w4(ws["hq"], ws["hs"], d[0], d[1], ws["o_slot"], b_z=d[2])
+            rec(3)
+            direct = out.is_contiguous() and out.data_ptr() % 16 == 0
+            ws["obuf"].gather(ws["o_parts"], out if direct else None, M * self.hidden * 2 if direct else 0)
+            if not direct:
+                out.copy_(ws["out_full"])
+            rec(4)
+            return out
+        self._gather_h_dist(ws, M)
+        rec(2)
+        self.ops.gemm_w4(ws["hq"], ws["hs"], d[0], d[1], ws["o_loc"], b_z=d[2])
+        rec(3)
+        # [world * M, h_loc] rank-major -> columns of out
+        dist.all_gather_into_tensor(ws["o_all"], ws["o_loc"], group=self.group)
+        out.view(M, self.world, self.h_loc).copy_(ws["o_all"].view(self.world, M, self.h_loc).permute(1, 0, 2))
+        rec(4)
+        return out
 
     __call__ = forward
 
+    def close(self):
+        """Release the peer mappings (before the process group is destroyed).
+
+        Peers write into this rank's gather buffers directly, so every rank
+        must have finished using them first: this waits for this rank's GPU
+        work, then for every rank (a barrier on the layer's group), and only
+        then unmaps and frees.  Every rank of the group must call it."""
+        peers = [ws[k] for ws in self._ws.values() for k in ("hbuf", "obuf") if k in ws]
+        if peers:
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
+        for p in peers:
+            p.close()
+        self._ws = {}
+
     def capture(self, a_q, a_s, out, warmup=2):
-        """CUDA graph of ``forward`` on these buffers (kernels and NCCL
-        collectives).  Replay it after refilling ``a_q``/``a_s`` in place;
-        release the graph before the process group is destroyed."""
+        """CUDA graph of ``forward`` on these buffers (kernels and, with the
+        dist gather, NCCL collectives).  Replay it after refilling
+        ``a_q``/``a_s`` in place; release the graph before the process group
+        is destroyed."""
         side = torch.cuda.Stream(device=self.device)
         side.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(side):

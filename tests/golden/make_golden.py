@@ -12,7 +12,7 @@ other step of the arithmetic is shared by both modes.
 
 Usage (in a container that has the reference checkout)::
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py /path/to/reference
 
 bf16 tensors are stored as uint16 bit patterns.  Nothing at test time reads
 the reference: the tests only load the committed ``.npz``.
@@ -47,7 +47,9 @@ def bits(t):
 
 
 def main():
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py /path/to/reference-checkout")
+    root = sys.argv[1]
     gemm, w4, norm = import_reference(root)
     G = 64
     rec = {}

@@ -1,0 +1,93 @@
+"""Fault path of the bounded device-side waits, exercised without faulting the
+GPU.
+
+A peer all-gather is launched as rank 0 of a world of two whose gather
+buffers and arrival counters are all local allocations of this process; the
+second "rank" never calls, so the arrival that rank 0 waits for never comes.
+With the wait bound lowered to 50 ms the kernel gives up, records the fault
+and returns; every access stays inside the buffers.  The test then checks that
+the fault is reported: by the fault word, by QLIN_ERR_DEVICE_FAULT from the
+next entry point (C ABI) and by QlinError (Python), and that clearing it
+restores normal service.
+"""
+import ctypes
+import time
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import qlin_oracle as O
+from qlin_testutil import bits
+
+pytestmark = pytest.mark.gpu
+
+QLIN_ERR_DEVICE_FAULT = 6
+
+
+def _ptrs(*tensors):
+    return (ctypes.c_void_p * len(tensors))(*[t.data_ptr() for t in tensors])
+
+
+@pytest.fixture
+def lib(pkg, dev):
+    """The C ABI; the fault word is cleared again afterwards whatever happens,
+    so that no later test sees this test's fault."""
+    torch.cuda.set_device(dev)
+    lib = pkg._lib.load()
+    yield lib
+    torch.cuda.synchronize()
+    lib.qlin_set_wait_limit_ns(2_000_000_000)
+    lib.qlin_device_fault(1)
+
+
+def test_timed_out_wait_is_reported_and_cleared(pkg, dev, lib):
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    g = torch.Generator(device=dev).manual_seed(11)
+    x = torch.randn(4, 256, device=dev, generator=g).to(torch.bfloat16)
+    q = torch.empty(4, 256, dtype=torch.int8, device=dev)
+    s = torch.empty(4, 4, dtype=torch.float32, device=dev)
+    pkg.quant_row(x, q, s)            # sets up the host-visible fault mirror
+    torch.cuda.synchronize()
+    assert lib.qlin_device_fault(1) == 0
+
+    n = 4096
+    bufs = [torch.zeros(2 * n, dtype=torch.uint8, device=dev) for _ in range(2)]
+    arrive = [torch.zeros(2, dtype=torch.int32, device=dev) for _ in range(2)]
+    expected = torch.zeros(2, dtype=torch.int32, device=dev)
+    src = torch.randint(0, 256, (n,), dtype=torch.uint8, device=dev, generator=g)
+    assert lib.qlin_set_wait_limit_ns(50_000_000) == 0
+    try:
+        t0 = time.perf_counter()
+        rc = lib.qlin_peer_allgather(_ptrs(*bufs), _ptrs(*arrive), expected.data_ptr(), src.data_ptr(), n, 2, 0,
+                                     None, stream)
+        assert rc == 0, lib.qlin_last_error()
+        torch.cuda.synchronize()
+        elapsed = time.perf_counter() - t0
+    finally:
+        assert lib.qlin_set_wait_limit_ns(2_000_000_000) == 0
+    assert elapsed < 1.5, f"kernel returned after {elapsed:.2f} s, not after the 50 ms bound"
+    # rank 0's shard reached slot 0 of both buffers and its arrival was counted;
+    # rank 1's never came
+    assert torch.equal(bufs[0][:n], src) and torch.equal(bufs[1][:n], src)
+    assert arrive[0][0].item() == 1 and arrive[0][1].item() == 0
+    fw = lib.qlin_device_fault(0)
+    assert fw & 1, f"fault word {fw:#x}"
+
+    # the next launch through the C ABI reports the earlier fault ...
+    rc = lib.qlin_quant_row(x.data_ptr(), 256, 4, 256, q.data_ptr(), s.data_ptr(), stream)
+    assert rc == QLIN_ERR_DEVICE_FAULT
+    assert b"earlier launch" in lib.qlin_last_error()
+    # ... and so does the Python layer
+    with pytest.raises(pkg._lib.QlinError) as ei:
+        pkg.quant_row(x, q, s)
+    assert ei.value.status == QLIN_ERR_DEVICE_FAULT
+
+    # clearing restores normal service
+    assert lib.qlin_device_fault(1) & 1
+    assert lib.qlin_device_fault(0) == 0
+    pkg.quant_row(x, q, s)
+    torch.cuda.synchronize()
+    rq, rs = O.quant_row(bits(x))
+    np.testing.assert_array_equal(q.cpu().numpy(), rq)
+    np.testing.assert_array_equal(s.cpu().numpy().view(np.uint32), rs.view(np.uint32))

@@ -121,6 +121,63 @@ def test_tp_layer_nccl_ranks_equal_one_gpu(pkg, dev, M):
         assert_bf16_close(b, ref_r, f"tp rank {rank} of {world} M={M}")
 
 
+# (rows, row_bytes, source row stride, destination gap after the world's slots):
+# 16-byte parts, a 4-byte part (the h scales of config 5 at 8 ranks are 136
+# bytes per row) and one long row
+PART_SHAPES = [(3, 1280, 1296, 32), (5, 136, 136, 8), (1, 1 << 20, 1 << 20, 0)]
+
+
+def _pattern(rank, rows, row_bytes, it):
+    r = torch.arange(rows).view(-1, 1) * 7 + torch.arange(row_bytes).view(1, -1) * (rank + 3) + it * 11
+    return (r % 251).to(torch.uint8)
+
+
+def _check_gather(pkg, rank, world, dev):
+    """Every part shape: eager calls (the counters advance across calls), then
+    replays of a captured gather; each checks every rank's slot of the local
+    buffer and the copy into ``out`` made by the same launch."""
+    ok = True
+    for rows, rb, ld, gap in PART_SHAPES:
+        dst_ld = world * rb + gap
+        nbytes = rows * dst_ld
+        pb = pkg.tp.PeerBuffer(nbytes, dev)
+        src = torch.zeros(rows, ld, dtype=torch.uint8, device=dev)
+        out = torch.zeros(pb.nbytes, dtype=torch.uint8, device=dev)
+        part = pkg.tp._part(src, rows, rb, ld, 0, dst_ld)
+
+        def check(it):
+            got = pb.local[:nbytes].view(rows, dst_ld).cpu()
+            cp = out[:nbytes].view(rows, dst_ld).cpu()
+            good = torch.equal(got, cp)
+            for r in range(world):
+                good = good and torch.equal(got[:, r * rb:(r + 1) * rb], _pattern(r, rows, rb, it))
+            return good
+
+        for it in range(3):
+            src[:, :rb].copy_(_pattern(rank, rows, rb, it))
+            pb.gather([part], out, pb.nbytes)
+            ok = ok and check(it)
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            pb.gather([part], out, pb.nbytes)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            pb.gather([part], out, pb.nbytes)
+        for it in range(3, 6):
+            src[:, :rb].copy_(_pattern(rank, rows, rb, it))
+            graph.replay()
+            ok = ok and check(it)
+        torch.cuda.synchronize()
+        del graph
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        pb.close()
+    return ok
+
+
 def _peer_rank(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     import datetime
@@ -132,40 +189,18 @@ def _peer_rank(rank, world, port, q):
     try:
         import __graft_entry__
         pkg = __graft_entry__.load_package()
-        ok = True
-        for nbytes in (16, 1040, 1 << 20):
-            pg = pkg.tp.PeerGather(nbytes, dev)
-            src = torch.empty(pg.shard, dtype=torch.uint8, device=dev)
-            # eager calls: the counters advance across calls
-            for it in range(3):
-                src.copy_((torch.arange(pg.shard, device=dev) * (rank + 1) + it) % 251)
-                got = pg(src).view(world, pg.shard).cpu()
-                for r in range(world):
-                    want = (torch.arange(pg.shard) * (r + 1) + it) % 251
-                    ok = ok and torch.equal(got[r], want.to(torch.uint8))
-            # replays of a captured gather
-            s = torch.cuda.Stream(device=dev)
-            with torch.cuda.stream(s):
-                pg(src)
-            torch.cuda.synchronize()
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=s):
-                pg(src)
-            for it in range(3, 6):
-                src.copy_((torch.arange(pg.shard, device=dev) * (rank + 1) + it) % 251)
-                graph.replay()
-                got = pg.buf.view(world, pg.shard).cpu()
-                for r in range(world):
-                    want = (torch.arange(pg.shard) * (r + 1) + it) % 251
-                    ok = ok and torch.equal(got[r], want.to(torch.uint8))
-            torch.cuda.synchronize()
-            del graph
-            dist.barrier()
-            pg.close()
+        ok = _check_gather(pkg, rank, world, dev)
         q.put((rank, bool(ok), pkg._lib.load().qlin_device_fault(1)))
         dist.barrier()
     finally:
         dist.destroy_process_group()
+
+
+def test_peer_allgather_parts_world1(pkg, dev):
+    """The parts gather at world 1 on one GPU (its own slot, the fused copy,
+    strided and 4-byte parts, eager and graph replays)."""
+    assert _check_gather(pkg, 0, 1, dev)
+    assert pkg._lib.load().qlin_device_fault(1) == 0
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")

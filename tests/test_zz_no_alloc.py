@@ -1,5 +1,6 @@
 """The all-gather that allocates nothing (``qlin_peer_allgather_static``),
-called through the C ABI and checked byte for byte against the allocating
+called through the C ABI and checked byte for byte against its input (at
+world = 1 the gathered bytes are the shard itself) and against the allocating
 ``qlin_peer_allgather`` (world = 1) on the same shards.
 
 It is for a process that runs the column-split layer on one GPU and may not
@@ -50,7 +51,8 @@ def test_static_gather_matches_allocating_gather_in_a_row(pkg):
         assert rc == 0, lib.qlin_last_error()
     refs = [_existing_gather(lib, s, dev) for s in shards]
     torch.cuda.synchronize()
-    for o, r in zip(outs, refs):
+    for s, o, r in zip(shards, outs, refs):
+        assert torch.equal(o, s)   # world 1: the gathered bytes are the shard itself
         assert torch.equal(o, r)
     assert lib.qlin_device_fault(1) == 0
 
