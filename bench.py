@@ -504,6 +504,71 @@ def prefill_detail(pkg, dev, gen, reps=20):
             "int8_peak_tops": int8_peak, "int8_peak_kind": "2 x measured bf16 GEMM peak", "per_M": out}
 
 
+# ----------------------------------------------------------------------------- single-kernel runs (profiling)
+def _w4(dev, g, K, N):
+    return (torch.randint(0, 256, (K // 2, N), dtype=torch.uint8, device=dev, generator=g),
+            torch.exp(torch.randn(K // WG, N, device=dev, generator=g) * 0.5 - 5.0).to(torch.bfloat16),
+            torch.randint(0, 16, (K // WG, N), dtype=torch.uint8, device=dev, generator=g))
+
+
+def _acts(dev, g, M, K):
+    return (torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev, generator=g),
+            torch.rand(M, K // 64, device=dev, generator=g) * 0.02)
+
+
+def kernel_case(pkg, dev, name):
+    """One named launch of the path (for ncu captures and quick timings):
+    returns (fn, algorithmic bytes or ops per launch, unit)."""
+    g = torch.Generator(device=dev).manual_seed(77)
+    if name.startswith("gate_up_w4_"):
+        K, N, M = {"cfg2_m1": (H, I, 1), "cfg2_m4": (H, I, 4), "cfg5_m1": (TP_K, TP_I, 1),
+                   "cfg5_m4": (TP_K, TP_I, 4)}[name[len("gate_up_w4_"):]]
+        (gw, gs, gz), (uw, us, uz) = _w4(dev, g, K, N), _w4(dev, g, K, N)
+        a_q, a_s = _acts(dev, g, M, K)
+        q = torch.empty(M, N, dtype=torch.int8, device=dev)
+        qs = torch.empty(M, N // 64, dtype=torch.float32, device=dev)
+        nbytes = 2 * (K * N // 2 + (K // WG) * N * 3) + M * K * (1 + 4 / 64) + M * N * (1 + 4 / 64)
+        return (lambda: pkg.mlp_gate_up_quant_w4(a_q, a_s, gw, gs, uw, us, q, qs, zg=gz, zu=uz)), nbytes, "B"
+    if name.startswith("gemm_w4_"):
+        K, N, M = {"cfg2_down_m1": (I, H, 1), "cfg2_down_m4": (I, H, 4), "cfg5_down_m1": (TP_I, TP_H, 1),
+                   "cfg5_down_m4": (TP_I, TP_H, 4), "cfg3_m2048": (2048, 12288, 2048)}[name[len("gemm_w4_"):]]
+        b, bs, bz = _w4(dev, g, K, N)
+        a_q, a_s = _acts(dev, g, M, K)
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+        if M >= 128:
+            return (lambda: pkg.gemm_w4(a_q, a_s, b, bs, out, b_z=bz)), 2.0 * M * N * K, "op"
+        nbytes = K * N // 2 + (K // WG) * N * 3 + M * K * (1 + 4 / 64) + M * N * 2
+        return (lambda: pkg.gemm_w4(a_q, a_s, b, bs, out, b_z=bz)), nbytes, "B"
+    if name in ("gemm_i8_cfg1", "gemm_i8_cfg3_m2048", "gemm_i8_cfg3_m512"):
+        K, N, M = {"gemm_i8_cfg1": (H, I, 1), "gemm_i8_cfg3_m2048": (2048, 12288, 2048),
+                   "gemm_i8_cfg3_m512": (2048, 12288, 512)}[name]
+        b = torch.randint(-127, 128, (K, N), dtype=torch.int8, device=dev, generator=g)
+        bs = torch.exp(torch.randn(N, device=dev, generator=g) * 0.5 - 6.0)
+        a_q, a_s = _acts(dev, g, M, K)
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+        work = (2.0 * M * N * K, "op") if M >= 128 else (K * N + N * 4 + M * K * (1 + 4 / 64) + M * N * 2, "B")
+        return (lambda: pkg.gemm_i8(a_q, a_s, b, bs, out)), work[0], work[1]
+    raise SystemExit(f"unknown --kernel {name}")
+
+
+def run_kernel(pkg, dev, name, launches):
+    fn, work, unit = kernel_case(pkg, dev, name)
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(launches):
+        fn()
+    e1.record()
+    e1.synchronize()
+    us = e0.elapsed_time(e1) / launches * 1e3
+    rate = work / us / 1e6  # TB/s or TOPS
+    print(json.dumps({"kernel": name, "launches": launches, "us_per_launch": us,
+                      ("tb_per_s" if unit == "B" else "tops"): rate, "work_per_launch": work, "unit": unit,
+                      "fault_word": pkg._lib.load().qlin_device_fault(0)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -511,7 +576,18 @@ def main():
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["qlin", "reference"], default="qlin")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--kernel", default=None,
+                    help="run one named launch --launches times (eager, same weights) and print its time; "
+                         "for profiler captures, not a bench line")
+    ap.add_argument("--launches", type=int, default=5)
     args = ap.parse_args()
+    if args.kernel:
+        import __graft_entry__
+        pkg = __graft_entry__.load_package()
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        run_kernel(pkg, dev, args.kernel, args.launches)
+        return
     warmup = max(args.warmup, 3)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -144,6 +144,52 @@ int qlin_mlp_gate_up_quant_w4(const int8_t* a_q, const float* a_s, int64_t M, in
 int qlin_quant_row(const void* x, int64_t ldx, int64_t M, int64_t K,
                    int8_t* q, float* s, void* stream);
 
+/* ---- Activation producers (kernels/norm.py): they write the (a_q, a_s) that
+ * the GEMMs above consume.  Integer codes and scales follow norm.py:15-25
+ * exactly given the fp32 value being quantised; that value comes from fp32
+ * sums whose order is the kernel's own (the reference's is its compiler's).
+ * Inputs need 16-byte aligned rows unless stated otherwise. ---- */
+
+/* kernels/norm.py:28-57 (rmsnorm_quant): per row of bf16 x [M, K] (row
+ * stride ldx), var = sum(x^2)/K, y = x * rsqrt(var + eps) * (w + 1 if
+ * one_plus else w) with w bf16 [K], then per-64 quantisation into int8 q
+ * [M, K] and fp32 s [M, K/64] (both contiguous).  K % 64 == 0, K <= 16384. */
+int qlin_rmsnorm_quant(const void* x, int64_t ldx, const void* w, int64_t M, int64_t K, float eps,
+                       int one_plus, int8_t* q, float* s, void* stream);
+
+/* kernels/norm.py:95-137 (norm_gated_quant): per (token t, head h) of bf16
+ * v [T, N] (contiguous, N = heads * HD), gate z [T, >= N] (row stride ldz)
+ * and bf16 w [HD]: y = x * rsqrt(mean(x^2) + eps) * w * silu(z), rounded
+ * through bf16, then per-64 quantisation within the head into q [T, N],
+ * s [T, N/64].  HD in {64, 128, 256}; 4-byte alignment suffices. */
+int qlin_norm_gated_quant(const void* v, const void* z, int64_t ldz, const void* w, int64_t T, int64_t N,
+                          int64_t HD, float eps, int8_t* q, float* s, void* stream);
+
+/* kernels/norm.py:141-165 (norm_gated): the same y stored as bf16 out [T, N]. */
+int qlin_norm_gated(const void* v, const void* z, int64_t ldz, const void* w, int64_t T, int64_t N,
+                    int64_t HD, float eps, void* out, void* stream);
+
+/* kernels/norm.py:168-188 (gate_mul_quant): y = a * sigmoid(g_gate) for bf16
+ * a [M, N] (contiguous), where the gate of column n is column
+ * (n / hd) * 2 hd + hd + n % hd of the bf16 row g (row stride ldg, the q
+ * projection with its per-head gate halves), then per-64 quantisation into
+ * q [M, N], s [M, N/64]. */
+int qlin_gate_mul_quant(const void* a, const void* g, int64_t ldg, int64_t M, int64_t N, int64_t hd,
+                        int8_t* q, float* s, void* stream);
+
+/* kernels/norm.py:191-208 (silu_mul_quant): y = silu(g) * u for bf16 g, u
+ * [M, N] (contiguous), then per-64 quantisation into q [M, N], s [M, N/64]. */
+int qlin_silu_mul_quant(const void* g, const void* u, int64_t M, int64_t N, int8_t* q, float* s,
+                        void* stream);
+
+/* kernels/norm.py:211-240 (gate_proj): from int8 activations a_q [M, K] with
+ * per-64 scales a_s [M, K/64], x = a_q * a_s; b = wb @ x, av = wa @ x for
+ * bf16 wb, wa [NB, K] (NB <= 32); beta = sigmoid(b),
+ * gate = -exp(a_log) * softplus(av + dt_bias) with bf16 dt_bias, a_log [NB];
+ * beta, gate fp32 [M, NB].  a_q needs 8-byte alignment, wb / wa 16-byte. */
+int qlin_gate_proj(const int8_t* a_q, const float* a_s, int64_t M, int64_t K, const void* wb, const void* wa,
+                   int64_t NB, const void* dt_bias, const void* a_log, float* beta, float* gate, void* stream);
+
 /* ---- Multi-GPU (column-split layer): NVLink peer memory through CUDA IPC ----
  * Not part of the reference's interface (it has no multi-GPU path); used by
  * the package's tp.py for its all-gathers. */

@@ -6,8 +6,8 @@ This module is the checker, never the product.  Only ``tests/``,
 library and has no CPU path.
 
 Every function restates, in numpy, the arithmetic of one reference function of
-``kernels/gemm.py``, ``kernels/w4.py``, ``kernels/norm.py`` or
-``kernels/common.py`` (paths relative to the reference project root; line
+``kernels/gemm.py``, ``kernels/w4.py``, ``kernels/norm.py`` (the activation
+producers included) or ``kernels/common.py`` (paths relative to the reference project root; line
 numbers cited per function).  The restatement is exact at the level the
 reference defines it:
 
@@ -287,6 +287,158 @@ def mlp_gate_up_quant_w4(a_q, a_s, wg, sg_bits, wu, su_bits, zg=None, zu=None, m
     u = gemm_w4_f32(a_q, a_s, wu, su_bits, zu)
     h = (silu(g) * u).astype(np.float32)
     return _quant_h(h, mode)
+
+
+# ----------------------------------------------------------------------------
+# f1: activation producers  (kernels/norm.py)
+# ----------------------------------------------------------------------------
+# The reference reduces with ``tl.sum`` over a row padded with zeros to a
+# power-of-two block; the restatement sums the same padded float32 array with
+# numpy (the CPU interpreter's own reduction), so the golden fixtures pin it
+# bit for bit.  A GPU build sums in another order: its results agree to a
+# few fp32 ulps, and the tests say how that reaches the int8 codes.
+
+def _next_pow2(n: int) -> int:
+    return 1 << max(0, n - 1).bit_length()
+
+
+def _pad(x: np.ndarray, n: int) -> np.ndarray:
+    out = np.zeros(x.shape[:-1] + (n,), dtype=np.float32)
+    out[..., :x.shape[-1]] = x
+    return out
+
+
+def _rsqrt(v):
+    """tl.rsqrt: 1 / sqrt(v) in float32 (correctly rounded sqrt, then division)."""
+    v = np.asarray(v, dtype=np.float32)
+    return (np.float32(1.0) / np.sqrt(v)).astype(np.float32)
+
+
+def sigmoid(x: np.ndarray) -> np.ndarray:
+    """triton.language.standard.sigmoid: 1 / (1 + exp(-x)) in float32."""
+    x = np.asarray(x, dtype=np.float32)
+    with np.errstate(over="ignore"):
+        e = np.exp(-x).astype(np.float32)
+    return (np.float32(1.0) / (np.float32(1.0) + e).astype(np.float32)).astype(np.float32)
+
+
+def softplus(x: np.ndarray) -> np.ndarray:
+    """kernels/common.py:37-39: x > 20 ? x : log(1 + exp(min(x, 20)))."""
+    x = np.asarray(x, dtype=np.float32)
+    e = np.exp(np.minimum(x, np.float32(20.0))).astype(np.float32)
+    lg = np.log((np.float32(1.0) + e).astype(np.float32)).astype(np.float32)
+    return np.where(x > np.float32(20.0), x, lg).astype(np.float32)
+
+
+def rmsnorm_y(x_bits, w_bits, eps=1e-6, one_plus=True) -> np.ndarray:
+    """kernels/norm.py:31-41: the fp32 rows ``x * rsqrt(var + eps) * w`` that
+    rmsnorm_quant quantises; var = sum(x*x) / K over the row padded to
+    BLOCK_K = max(256, next_pow2(K))."""
+    x = bf16_bits_to_f32(x_bits)
+    M, K = x.shape
+    blk = max(256, _next_pow2(K))
+    xp = _pad(x, blk)
+    w = _pad(bf16_bits_to_f32(w_bits)[None, :], blk)[0]
+    if one_plus:
+        w = (w + np.float32(1.0)).astype(np.float32)
+    out = np.empty((M, K), dtype=np.float32)
+    for m in range(M):
+        ss = np.sum((xp[m] * xp[m]).astype(np.float32), dtype=np.float32)
+        var = (np.float32(ss) / np.float32(K)).astype(np.float32)
+        r = _rsqrt((var + np.float32(eps)).astype(np.float32))
+        out[m] = ((xp[m] * r).astype(np.float32) * w).astype(np.float32)[:K]
+    return out
+
+
+def rmsnorm_quant(x_bits, w_bits, eps=1e-6, one_plus=True):
+    """kernels/norm.py:28-57 -> (int8 [M,K], fp32 [M,K/64])."""
+    return quant_groups(rmsnorm_y(x_bits, w_bits, eps, one_plus))
+
+
+def norm_gated_y(v_bits, z_bits, w_bits, eps=1e-6) -> np.ndarray:
+    """kernels/norm.py:111-123 / 150-164: per (token, head) of HD dims,
+    ``x * rsqrt(sum(x*x)/HD + eps) * w * silu(z)`` in fp32 (before any bf16
+    rounding); the head is padded to BLOCK = max(128, next_pow2(HD))."""
+    v = bf16_bits_to_f32(v_bits)
+    T, N = v.shape
+    z = bf16_bits_to_f32(z_bits)[:, :N]
+    w = bf16_bits_to_f32(w_bits)
+    HD = w.shape[0]
+    NV = N // HD
+    blk = max(128, _next_pow2(HD))
+    out = np.empty((T, N), dtype=np.float32)
+    for t in range(T):
+        for h in range(NV):
+            x = _pad(v[t, h * HD:(h + 1) * HD][None, :], blk)[0]
+            ss = np.sum((x * x).astype(np.float32), dtype=np.float32)
+            var = (np.float32(ss) / np.float32(HD)).astype(np.float32)
+            r = _rsqrt((var + np.float32(eps)).astype(np.float32))
+            xx = x[:HD]
+            y = ((xx * r).astype(np.float32) * w).astype(np.float32)
+            out[t, h * HD:(h + 1) * HD] = (y * silu(z[t, h * HD:(h + 1) * HD])).astype(np.float32)
+    return out
+
+
+def norm_gated_quant(v_bits, z_bits, w_bits, eps=1e-6, mode="rne"):
+    """kernels/norm.py:95-137: y rounded through bf16, then per-64 quantisation
+    (groups never straddle heads: HD is a multiple of 64)."""
+    return quant_groups(bf16_round(norm_gated_y(v_bits, z_bits, w_bits, eps), mode))
+
+
+def norm_gated(v_bits, z_bits, w_bits, eps=1e-6, mode="rne"):
+    """kernels/norm.py:141-165 -> bf16 bits [T, N]."""
+    return f32_to_bf16_bits(norm_gated_y(v_bits, z_bits, w_bits, eps), mode)
+
+
+def gate_mul_y(a_bits, g_bits, hd=256) -> np.ndarray:
+    """kernels/norm.py:175-181: a * sigmoid(gate), gate of column n at column
+    (n // hd) * 2 hd + hd + n % hd of the g row."""
+    a = bf16_bits_to_f32(a_bits)
+    M, N = a.shape
+    g = bf16_bits_to_f32(g_bits)
+    n = np.arange(N)
+    gcol = (n // hd) * (2 * hd) + hd + (n % hd)
+    return (a * sigmoid(g[:, gcol])).astype(np.float32)
+
+
+def gate_mul_quant(a_bits, g_bits, hd=256):
+    """kernels/norm.py:168-188 -> (int8 [M,N], fp32 [M,N/64])."""
+    return quant_groups(gate_mul_y(a_bits, g_bits, hd))
+
+
+def silu_mul_quant(g_bits, u_bits):
+    """kernels/norm.py:191-208: silu(g) * u quantised per 64."""
+    g = bf16_bits_to_f32(g_bits)
+    u = bf16_bits_to_f32(u_bits)
+    return quant_groups((silu(g) * u).astype(np.float32))
+
+
+def gate_proj(a_q, a_s, wb_bits, wa_bits, dt_bits, alog_bits):
+    """kernels/norm.py:211-240 -> (beta fp32 [M,NB], gate fp32 [M,NB]).
+
+    x = a_q * a_s[k // 64]; b = sum_k wb[n,k] * x[k], av likewise (row padded
+    to BLOCK_K = max(256, next_pow2(K))); beta = sigmoid(b);
+    gate = -exp(A_log) * softplus(av + dt_bias)."""
+    a_q = np.asarray(a_q, dtype=np.int8)
+    a_s = np.asarray(a_s, dtype=np.float32)
+    M, K = a_q.shape
+    blk = max(256, _next_pow2(K))
+    wb = _pad(bf16_bits_to_f32(wb_bits), blk)
+    wa = _pad(bf16_bits_to_f32(wa_bits), blk)
+    dtb = bf16_bits_to_f32(dt_bits)
+    alog = bf16_bits_to_f32(alog_bits)
+    NB = wb.shape[0]
+    beta = np.empty((M, NB), dtype=np.float32)
+    gate = np.empty((M, NB), dtype=np.float32)
+    for m in range(M):
+        x = (a_q[m].astype(np.float32) * np.repeat(a_s[m], GROUP)).astype(np.float32)
+        x = _pad(x[None, :], blk)[0]
+        b = np.sum((wb * x[None, :]).astype(np.float32), axis=1, dtype=np.float32)
+        av = np.sum((wa * x[None, :]).astype(np.float32), axis=1, dtype=np.float32)
+        beta[m] = sigmoid(b)
+        ea = np.exp(alog).astype(np.float32)
+        gate[m] = ((-ea).astype(np.float32) * softplus((av + dtb).astype(np.float32))).astype(np.float32)
+    return beta, gate
 
 
 # ----------------------------------------------------------------------------

@@ -32,6 +32,12 @@ SIGNATURES = {
     "qlin_mlp_gate_up_quant": [_P, _P, _I, _I, _P, _P, _P, _P, _I, _P, _P, _P],
     "qlin_mlp_gate_up_quant_w4": [_P, _P, _I, _I, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P],
     "qlin_quant_row": [_P, _I, _I, _I, _P, _P, _P],
+    "qlin_rmsnorm_quant": [_P, _I, _P, _I, _I, ctypes.c_float, ctypes.c_int, _P, _P, _P],
+    "qlin_norm_gated_quant": [_P, _P, _I, _P, _I, _I, _I, ctypes.c_float, _P, _P, _P],
+    "qlin_norm_gated": [_P, _P, _I, _P, _I, _I, _I, ctypes.c_float, _P, _P],
+    "qlin_gate_mul_quant": [_P, _P, _I, _I, _I, _I, _P, _P, _P],
+    "qlin_silu_mul_quant": [_P, _P, _I, _I, _P, _P, _P],
+    "qlin_gate_proj": [_P, _P, _I, _I, _P, _P, _I, _P, _P, _P, _P, _P],
     "qlin_plan_small_m": [ctypes.c_int, ctypes.c_int, _I, _I, _I, _I, ctypes.c_int, _P],
     "qlin_max_active_clusters": [ctypes.c_int, ctypes.c_int, _I, ctypes.c_int, _I, ctypes.POINTER(ctypes.c_int64)],
     "qlin_ipc_get_handle": [_P, _P, ctypes.POINTER(ctypes.c_int64)],

@@ -16,6 +16,7 @@
 #include "args.cuh"
 #include "quant.cuh"
 #include "peer.cuh"
+#include "producers.cuh"
 #include "tcgemm.cuh"
 #include "tcgemm_w4.cuh"
 #include "tcgemv.cuh"
@@ -1602,6 +1603,162 @@ int qlin_quant_row(const void* x, int64_t ldx, int64_t M, int64_t K, int8_t* q, 
                                      static_cast<int>(K), q, s);
   if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(quant_row)");
   return QLIN_OK;
+}
+
+
+// ---------------------------------------------------------------- activation producers (kernels/norm.py)
+namespace {
+int prod_launch(const void* kern, dim3 grid, void** args, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kProdThreads, 1, 1);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelExC(&cfg, kern, args);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(producer)");
+  return QLIN_OK;
+}
+
+int check_rows(int64_t M, int64_t K, const char* what) {
+  if (M < 0 || K < 0) return fail(QLIN_ERR_INVALID_ARGUMENT, "%s: negative size", what);
+  if (M > 65535 * 64) return fail(QLIN_ERR_SHAPE, "%s: M=%lld too large", what, (long long)M);
+  return QLIN_OK;
+}
+}  // namespace
+
+int qlin_rmsnorm_quant(const void* x, int64_t ldx, const void* w, int64_t M, int64_t K, float eps, int one_plus,
+                       int8_t* q, float* s, void* stream) {
+  if (int r = check_rows(M, K, "rmsnorm_quant")) return r;
+  if (K == 0 || K % kGroup != 0 || K > 16384)
+    return fail(QLIN_ERR_SHAPE, "rmsnorm_quant: K=%lld must be a positive multiple of 64, at most 16384", (long long)K);
+  if (M == 0) return QLIN_OK;
+  if (M > 2147483647) return fail(QLIN_ERR_SHAPE, "rmsnorm_quant: M too large");
+  if (!x || !w || !q || !s) return fail(QLIN_ERR_INVALID_ARGUMENT, "rmsnorm_quant: null pointer");
+  if (ldx < K) return fail(QLIN_ERR_SHAPE, "rmsnorm_quant: row stride smaller than K");
+  if (!aligned(x, 16) || ldx % 8 != 0 || !aligned(w, 16) || !aligned(q, 8) || !aligned(s, 4))
+    return fail(QLIN_ERR_ALIGNMENT, "rmsnorm_quant: x and w need 16-byte aligned rows, q 8-byte, s 4-byte alignment");
+  DevInfo di;
+  if (int r = launch_info(&di)) return r;
+  const int nch = static_cast<int>(K / 8);
+  const int nv = (nch + kProdThreads - 1) / kProdThreads;
+  long long ldx_ = ldx;
+  int K_ = static_cast<int>(K), one_plus_ = one_plus ? 1 : 0;
+  float eps_ = eps;
+  void* args[] = {const_cast<void**>(&x), &ldx_, const_cast<void**>(&w), &K_, &eps_, &one_plus_, &q, &s};
+  const void* kern = nv <= 1   ? reinterpret_cast<const void*>(rmsnorm_quant_kernel<1>)
+                     : nv <= 2 ? reinterpret_cast<const void*>(rmsnorm_quant_kernel<2>)
+                     : nv <= 4 ? reinterpret_cast<const void*>(rmsnorm_quant_kernel<4>)
+                               : reinterpret_cast<const void*>(rmsnorm_quant_kernel<8>);
+  return prod_launch(kern, dim3(static_cast<unsigned>(M)), args, static_cast<cudaStream_t>(stream));
+}
+
+static int norm_gated_common(const void* v, const void* z, int64_t ldz, const void* w, int64_t T, int64_t N,
+                             int64_t HD, float eps, int8_t* q, float* s, void* out, void* stream) {
+  const bool quant = out == nullptr;
+  if (int r = check_rows(T, N, "norm_gated")) return r;
+  if (!(HD == 64 || HD == 128 || HD == 256) || N % HD != 0)
+    return fail(QLIN_ERR_SHAPE, "norm_gated: head dim %lld must be 64, 128 or 256 and divide N=%lld", (long long)HD,
+                (long long)N);
+  if (T == 0 || N == 0) return QLIN_OK;
+  if (!v || !z || !w || (quant && (!q || !s))) return fail(QLIN_ERR_INVALID_ARGUMENT, "norm_gated: null pointer");
+  if (ldz < N) return fail(QLIN_ERR_SHAPE, "norm_gated: z row stride smaller than N");
+  if (!aligned(v, 4) || !aligned(z, 4) || ldz % 2 != 0 || !aligned(w, 4) || (quant && !aligned(s, 4)))
+    return fail(QLIN_ERR_ALIGNMENT, "norm_gated: v, z rows and w need 4-byte alignment");
+  const long long items = T * (N / HD);
+  if (items > 65535ll * 65535 * 8) return fail(QLIN_ERR_SHAPE, "norm_gated: too many heads");
+  DevInfo di;
+  if (int r = launch_info(&di)) return r;
+  long long ldz_ = ldz;
+  int T_ = static_cast<int>(T), NV = static_cast<int>(N / HD);
+  float eps_ = eps;
+  void* args[] = {const_cast<void**>(&v), const_cast<void**>(&z), &ldz_, const_cast<void**>(&w), &T_, &NV, &eps_,
+                  &q, &s, &out};
+  const void* kern;
+  if (quant) {
+    kern = HD == 64    ? reinterpret_cast<const void*>(norm_gated_kernel<64, true>)
+           : HD == 128 ? reinterpret_cast<const void*>(norm_gated_kernel<128, true>)
+                       : reinterpret_cast<const void*>(norm_gated_kernel<256, true>);
+  } else {
+    kern = HD == 64    ? reinterpret_cast<const void*>(norm_gated_kernel<64, false>)
+           : HD == 128 ? reinterpret_cast<const void*>(norm_gated_kernel<128, false>)
+                       : reinterpret_cast<const void*>(norm_gated_kernel<256, false>);
+  }
+  const unsigned blocks = static_cast<unsigned>((items + kProdThreads / 32 - 1) / (kProdThreads / 32));
+  return prod_launch(kern, dim3(blocks), args, static_cast<cudaStream_t>(stream));
+}
+
+int qlin_norm_gated_quant(const void* v, const void* z, int64_t ldz, const void* w, int64_t T, int64_t N, int64_t HD,
+                          float eps, int8_t* q, float* s, void* stream) {
+  if (!q || !s) return fail(QLIN_ERR_INVALID_ARGUMENT, "norm_gated_quant: null output");
+  return norm_gated_common(v, z, ldz, w, T, N, HD, eps, q, s, nullptr, stream);
+}
+
+int qlin_norm_gated(const void* v, const void* z, int64_t ldz, const void* w, int64_t T, int64_t N, int64_t HD,
+                    float eps, void* out, void* stream) {
+  if (!out) return fail(QLIN_ERR_INVALID_ARGUMENT, "norm_gated: null output");
+  return norm_gated_common(v, z, ldz, w, T, N, HD, eps, nullptr, nullptr, out, stream);
+}
+
+static int mul_quant_common(bool gate_mul, const void* a, int64_t lda, const void* g, int64_t ldg, int64_t M,
+                            int64_t N, int64_t HD, int8_t* q, float* s, void* stream) {
+  const char* what = gate_mul ? "gate_mul_quant" : "silu_mul_quant";
+  if (int r = check_rows(M, N, what)) return r;
+  if (N % kGroup != 0) return fail(QLIN_ERR_SHAPE, "%s: N=%lld must be a multiple of 64", what, (long long)N);
+  if (gate_mul && (HD <= 0 || HD % 8 != 0 || N % HD != 0))
+    return fail(QLIN_ERR_SHAPE, "%s: head dim %lld must be a multiple of 8 dividing N", what, (long long)HD);
+  if (M == 0 || N == 0) return QLIN_OK;
+  if (M > 65535) return fail(QLIN_ERR_SHAPE, "%s: M=%lld too large", what, (long long)M);
+  if (!a || !g || !q || !s) return fail(QLIN_ERR_INVALID_ARGUMENT, "%s: null pointer", what);
+  const int64_t gcols = gate_mul ? 2 * N : N;
+  if (lda < N || ldg < gcols) return fail(QLIN_ERR_SHAPE, "%s: row stride too small", what);
+  if (!aligned(a, 16) || !aligned(g, 16) || lda % 8 != 0 || ldg % 8 != 0 || !aligned(q, 8) || !aligned(s, 4))
+    return fail(QLIN_ERR_ALIGNMENT, "%s: inputs need 16-byte aligned rows, q 8-byte, s 4-byte alignment", what);
+  DevInfo di;
+  if (int r = launch_info(&di)) return r;
+  long long lda_ = lda, ldg_ = ldg;
+  int N_ = static_cast<int>(N), HD_ = static_cast<int>(gate_mul ? HD : 8);
+  void* args[] = {const_cast<void**>(&a), &lda_, const_cast<void**>(&g), &ldg_, &N_, &HD_, &q, &s};
+  const void* kern = gate_mul ? reinterpret_cast<const void*>(mul_quant_kernel<true>)
+                              : reinterpret_cast<const void*>(mul_quant_kernel<false>);
+  const unsigned cblocks = static_cast<unsigned>((N / 8 + kProdThreads - 1) / kProdThreads);
+  return prod_launch(kern, dim3(cblocks, static_cast<unsigned>(M)), args, static_cast<cudaStream_t>(stream));
+}
+
+int qlin_gate_mul_quant(const void* a, const void* g, int64_t ldg, int64_t M, int64_t N, int64_t hd, int8_t* q,
+                        float* s, void* stream) {
+  return mul_quant_common(true, a, N, g, ldg, M, N, hd, q, s, stream);
+}
+
+int qlin_silu_mul_quant(const void* g, const void* u, int64_t M, int64_t N, int8_t* q, float* s, void* stream) {
+  // y = silu(g) * u: the kernel's first operand is the multiplier (u), the second the activation input (g)
+  return mul_quant_common(false, u, N, g, N, M, N, 0, q, s, stream);
+}
+
+int qlin_gate_proj(const int8_t* a_q, const float* a_s, int64_t M, int64_t K, const void* wb, const void* wa,
+                   int64_t NB, const void* dt_bias, const void* a_log, float* beta, float* gate, void* stream) {
+  if (int r = check_rows(M, K, "gate_proj")) return r;
+  if (K == 0 || K % kGroup != 0) return fail(QLIN_ERR_SHAPE, "gate_proj: K=%lld must be a positive multiple of 64", (long long)K);
+  if (NB < 1 || NB > 32) return fail(QLIN_ERR_SHAPE, "gate_proj: NB=%lld must be 1..32", (long long)NB);
+  if (M == 0) return QLIN_OK;
+  if (M > 2147483647) return fail(QLIN_ERR_SHAPE, "gate_proj: M too large");
+  if (!a_q || !a_s || !wb || !wa || !dt_bias || !a_log || !beta || !gate)
+    return fail(QLIN_ERR_INVALID_ARGUMENT, "gate_proj: null pointer");
+  if (!aligned(a_q, 8) || !aligned(wb, 16) || !aligned(wa, 16) || !aligned(a_s, 4) || !aligned(beta, 4) ||
+      !aligned(gate, 4) || !aligned(dt_bias, 2) || !aligned(a_log, 2))
+    return fail(QLIN_ERR_ALIGNMENT, "gate_proj: a_q 8-byte, wb/wa 16-byte aligned");
+  DevInfo di;
+  if (int r = launch_info(&di)) return r;
+  int K_ = static_cast<int>(K), NB_ = static_cast<int>(NB);
+  void* args[] = {const_cast<int8_t**>(&a_q), const_cast<float**>(&a_s), &K_, const_cast<void**>(&wb),
+                  const_cast<void**>(&wa), &NB_, const_cast<void**>(&dt_bias), const_cast<void**>(&a_log), &beta,
+                  &gate};
+  const void* kern = NB <= 16 ? reinterpret_cast<const void*>(gate_proj_kernel<16>)
+                              : reinterpret_cast<const void*>(gate_proj_kernel<32>);
+  return prod_launch(kern, dim3(static_cast<unsigned>(M)), args, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

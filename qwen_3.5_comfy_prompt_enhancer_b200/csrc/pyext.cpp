@@ -299,6 +299,109 @@ int quant_row(const Tensor& x, const Tensor& q, const Tensor& s) {
   });
 }
 
+int rmsnorm_quant(const Tensor& x, const Tensor& w, const Tensor& q, const Tensor& s, double eps, bool one_plus) {
+  Call c;
+  c.need_rows(x, "x", at::kBFloat16);
+  c.need(q, "q", at::kChar, 2);
+  c.need(s, "s", at::kFloat, 2);
+  c.need(w, "w", at::kBFloat16, 1);
+  const int64_t M = q.size(0), K = q.size(1);
+  if (x.size(0) != M || x.size(1) != K || s.size(0) != M || s.size(1) != K / kGroup || w.size(0) != K)
+    throw py::value_error("shapes must be x [M,K], w [K], q [M,K], s [M,K/64]; got " + shape(x) + ", " + shape(w) +
+                          ", " + shape(q) + ", " + shape(s));
+  return c.launch([&](void* st) {
+    return qlin_rmsnorm_quant(x.data_ptr(), x.stride(0), w.data_ptr(), M, K, static_cast<float>(eps),
+                              one_plus ? 1 : 0, static_cast<int8_t*>(q.data_ptr()),
+                              static_cast<float*>(s.data_ptr()), st);
+  });
+}
+
+// v [T, N] contiguous, z [T, >= N] (rows strided), w [HD]; q/s or out.
+int norm_gated(const Tensor& v, const Tensor& z, const Tensor& w, const OptT& q, const OptT& s, const OptT& out,
+               double eps) {
+  Call c;
+  c.need(v, "v", at::kBFloat16, 2);
+  c.need_rows(z, "z", at::kBFloat16);
+  c.need(w, "w", at::kBFloat16, 1);
+  const int64_t T = v.size(0), N = v.size(1), HD = w.size(0);
+  if (z.size(0) != T || z.size(1) < N)
+    throw py::value_error("z must be [" + std::to_string(T) + ", >=" + std::to_string(N) + "], got " + shape(z));
+  if (HD == 0 || N % HD != 0) throw py::value_error("w must have head_dim entries dividing N, got " + shape(w));
+  if (out) {
+    c.need(*out, "out", at::kBFloat16, 2);
+    c.out_mn(*out, "out", T, N);
+    return c.launch([&](void* st) {
+      return qlin_norm_gated(v.data_ptr(), z.data_ptr(), z.stride(0), w.data_ptr(), T, N, HD, static_cast<float>(eps),
+                             out->data_ptr(), st);
+    });
+  }
+  c.need(*q, "q", at::kChar, 2);
+  c.need(*s, "s", at::kFloat, 2);
+  if (q->size(0) != T || q->size(1) != N || s->size(0) != T || s->size(1) != N / kGroup)
+    throw py::value_error("q/s must be " + dims(T, N) + " / " + dims(T, N / kGroup));
+  return c.launch([&](void* st) {
+    return qlin_norm_gated_quant(v.data_ptr(), z.data_ptr(), z.stride(0), w.data_ptr(), T, N, HD,
+                                 static_cast<float>(eps), static_cast<int8_t*>(q->data_ptr()),
+                                 static_cast<float*>(s->data_ptr()), st);
+  });
+}
+
+int gate_mul_quant(const Tensor& a, const Tensor& g, const Tensor& q, const Tensor& s, int64_t hd) {
+  Call c;
+  c.need(a, "a", at::kBFloat16, 2);
+  c.need_rows(g, "g", at::kBFloat16);
+  c.need(q, "q", at::kChar, 2);
+  c.need(s, "s", at::kFloat, 2);
+  const int64_t M = a.size(0), N = a.size(1);
+  if (g.size(0) != M || g.size(1) < 2 * N)
+    throw py::value_error("g must be [" + std::to_string(M) + ", >=" + std::to_string(2 * N) + "], got " + shape(g));
+  if (q.size(0) != M || q.size(1) != N || s.size(0) != M || s.size(1) != N / kGroup)
+    throw py::value_error("q/s must be " + dims(M, N) + " / " + dims(M, N / kGroup));
+  return c.launch([&](void* st) {
+    return qlin_gate_mul_quant(a.data_ptr(), g.data_ptr(), g.stride(0), M, N, hd, static_cast<int8_t*>(q.data_ptr()),
+                               static_cast<float*>(s.data_ptr()), st);
+  });
+}
+
+int silu_mul_quant(const Tensor& g, const Tensor& u, const Tensor& q, const Tensor& s) {
+  Call c;
+  c.need(q, "q", at::kChar, 2);
+  c.need(s, "s", at::kFloat, 2);
+  c.need(g, "g", at::kBFloat16, 2);
+  c.need(u, "u", at::kBFloat16, 2);
+  const int64_t M = q.size(0), N = q.size(1);
+  c.out_mn(g, "g", M, N);
+  c.out_mn(u, "u", M, N);
+  if (s.size(0) != M || s.size(1) != N / kGroup) throw py::value_error("s must be " + dims(M, N / kGroup));
+  return c.launch([&](void* st) {
+    return qlin_silu_mul_quant(g.data_ptr(), u.data_ptr(), M, N, static_cast<int8_t*>(q.data_ptr()),
+                               static_cast<float*>(s.data_ptr()), st);
+  });
+}
+
+int gate_proj(const Tensor& a_q, const Tensor& a_s, const Tensor& wb, const Tensor& wa, const Tensor& beta,
+              const Tensor& gate, const Tensor& dt_bias, const Tensor& a_log) {
+  Call c;
+  const auto [M, K] = c.acts(a_q, a_s);
+  c.need(wb, "wb", at::kBFloat16, 2);
+  c.need(wa, "wa", at::kBFloat16, 2);
+  c.need(beta, "beta", at::kFloat, 2);
+  c.need(gate, "gate", at::kFloat, 2);
+  c.need(dt_bias, "dt_bias", at::kBFloat16, 1);
+  c.need(a_log, "a_log", at::kBFloat16, 1);
+  const int64_t NB = wb.size(0);
+  if (wb.size(1) != K || wa.size(0) != NB || wa.size(1) != K)
+    throw py::value_error("wb/wa must be [NB, K=" + std::to_string(K) + "], got " + shape(wb) + ", " + shape(wa));
+  c.out_mn(beta, "beta", M, NB);
+  c.out_mn(gate, "gate", M, NB);
+  if (dt_bias.size(0) != NB || a_log.size(0) != NB) throw py::value_error("dt_bias / a_log must have NB entries");
+  return c.launch([&](void* st) {
+    return qlin_gate_proj(cptr<int8_t>(a_q), cptr<float>(a_s), M, K, wb.data_ptr(), wa.data_ptr(), NB,
+                          dt_bias.data_ptr(), a_log.data_ptr(), static_cast<float*>(beta.data_ptr()),
+                          static_cast<float*>(gate.data_ptr()), st);
+  });
+}
+
 }  // namespace
 
 PYBIND11_MODULE(_qlin_ext, m) {
@@ -311,4 +414,9 @@ PYBIND11_MODULE(_qlin_ext, m) {
   m.def("proj3_w4", &proj3_w4);
   m.def("mlp_gate_up_quant_w4", &mlp_gate_up_quant_w4);
   m.def("quant_row", &quant_row);
+  m.def("rmsnorm_quant", &rmsnorm_quant);
+  m.def("norm_gated", &norm_gated);
+  m.def("gate_mul_quant", &gate_mul_quant);
+  m.def("silu_mul_quant", &silu_mul_quant);
+  m.def("gate_proj", &gate_proj);
 }

@@ -4,7 +4,8 @@ The reference's Triton kernels (``kernels/gemm.py``, ``kernels/w4.py``,
 ``kernels/norm.py``) run on the CPU under Triton's interpreter
 (``TRITON_INTERPRET=1``).  This script imports them from a read-only checkout of
 the reference project, runs every hot-path entry point on small seeded inputs
-and stores inputs and outputs in ``ref_golden.npz`` next to this file.
+and stores inputs and outputs in ``ref_golden.npz`` (GEMMs, quant_row) and
+``ref_golden_norm.npz`` (the other activation producers) next to this file.
 
 The interpreter converts fp32 -> bf16 by truncation (a GPU build rounds to
 nearest-even), so the fixtures pin the oracle in its ``mode="trunc"``; every
@@ -12,7 +13,7 @@ other step of the arithmetic is shared by both modes.
 
 Usage (in a container that has the reference checkout)::
 
-    python tests/golden/make_golden.py /path/to/reference
+    python tests/golden/make_golden.py /path/to/reference [gemm|norm|all]
 
 bf16 tensors are stored as uint16 bit patterns.  Nothing at test time reads
 the reference: the tests only load the committed ``.npz``.
@@ -46,11 +47,108 @@ def bits(t):
     return t.contiguous().view(torch.int16).numpy().view(np.uint16)
 
 
+def producers(norm):
+    """Activation producers of kernels/norm.py -> ref_golden_norm.npz."""
+    G = 64
+    rec = {}
+
+    def bf(t):
+        return t.to(torch.bfloat16)
+
+    # rmsnorm_quant (norm.py:28-57): K a power of two, K padded inside the
+    # reference's block (1088 -> 2048), a strided x, one_plus on/off,
+    # outliers and an all-zero row
+    for i, (M, K, one_plus, strided) in enumerate([(3, 256, True, False), (4, 2048, True, True),
+                                                    (2, 1088, False, False)]):
+        g = torch.Generator().manual_seed(900 + i)
+        xw = torch.randn(M, K + (64 if strided else 0), generator=g)
+        xw[torch.rand(xw.shape, generator=g) < 0.002] *= 20.0
+        xw[-1] = 0.0 if M > 2 else xw[-1]
+        xb = bf(xw)
+        x = xb[:, :K]
+        w = bf(torch.randn(K, generator=g) * 0.2)
+        q = torch.empty(M, K, dtype=torch.int8)
+        s = torch.empty(M, K // G, dtype=torch.float32)
+        norm.rmsnorm_quant(x, w, q, s, 1e-6, one_plus)
+        p = f"rmsnorm_quant_{i}_"
+        rec[p + "x"] = bits(x.contiguous()); rec[p + "w"] = bits(w)
+        rec[p + "one_plus"] = np.array(int(one_plus)); rec[p + "q"] = q.numpy(); rec[p + "s"] = s.numpy()
+
+    # norm_gated_quant / norm_gated (norm.py:95-165): HD = 128 and 64, z a
+    # column slice of a wider projection row (engine.py:230-231)
+    for i, (T, NV, HD) in enumerate([(3, 16, 128), (2, 2, 256)]):
+        g = torch.Generator().manual_seed(950 + i)
+        N = NV * HD
+        v = bf(torch.randn(T, N, generator=g) * 0.7)
+        proj = bf(torch.randn(T, N + 96, generator=g))
+        z = proj[:, 96:]
+        w = bf(torch.randn(HD, generator=g) * 0.3 + 1.0)
+        q = torch.empty(T, N, dtype=torch.int8)
+        s = torch.empty(T, N // G, dtype=torch.float32)
+        norm.norm_gated_quant(v, z, w, q, s, 1e-6)
+        o = torch.empty(T, N, dtype=torch.bfloat16)
+        norm.norm_gated(v, z, w, o, 1e-6)
+        p = f"norm_gated_{i}_"
+        rec[p + "v"] = bits(v); rec[p + "z"] = bits(z.contiguous()); rec[p + "w"] = bits(w)
+        rec[p + "q"] = q.numpy(); rec[p + "s"] = s.numpy(); rec[p + "out"] = bits(o)
+
+    # gate_mul_quant (norm.py:168-188): the q projection row holds (q, gate)
+    # halves per head and is wider than 2N (engine.py:262)
+    for i, (M, NQ, HD) in enumerate([(3, 8, 256), (2, 2, 128)]):
+        g = torch.Generator().manual_seed(970 + i)
+        N = NQ * HD
+        a = bf(torch.randn(M, N, generator=g))
+        proj = bf(torch.randn(M, 2 * N + 128, generator=g) * 2.0)
+        q = torch.empty(M, N, dtype=torch.int8)
+        s = torch.empty(M, N // G, dtype=torch.float32)
+        norm.gate_mul_quant(a, proj, q, s, hd=HD)
+        p = f"gate_mul_quant_{i}_"
+        rec[p + "a"] = bits(a); rec[p + "g"] = bits(proj); rec[p + "hd"] = np.array(HD)
+        rec[p + "q"] = q.numpy(); rec[p + "s"] = s.numpy()
+
+    # silu_mul_quant (norm.py:191-208)
+    g = torch.Generator().manual_seed(980)
+    gg = bf(torch.randn(2, 512, generator=g) * 2.0)
+    uu = bf(torch.randn(2, 512, generator=g))
+    q = torch.empty(2, 512, dtype=torch.int8)
+    s = torch.empty(2, 512 // G, dtype=torch.float32)
+    norm.silu_mul_quant(gg, uu, q, s)
+    rec["silu_mul_quant_0_g"] = bits(gg); rec["silu_mul_quant_0_u"] = bits(uu)
+    rec["silu_mul_quant_0_q"] = q.numpy(); rec["silu_mul_quant_0_s"] = s.numpy()
+
+    # gate_proj (norm.py:211-240), .dev/test_kernels.py:83-99 distributions,
+    # K a power of two and a padded K
+    for i, (M, K, NB) in enumerate([(5, 2048, 16), (2, 320, 16)]):
+        g = torch.Generator().manual_seed(990 + i)
+        a = torch.randint(-127, 127, (M, K), dtype=torch.int8, generator=g)
+        a_s = torch.rand(M, K // G, generator=g) * 0.02
+        wb = bf(torch.randn(NB, K, generator=g) * 0.05)
+        wa = bf(torch.randn(NB, K, generator=g) * 0.05)
+        dt = bf(torch.randn(NB, generator=g))
+        al = bf(torch.randn(NB, generator=g))
+        beta = torch.empty(M, NB)
+        gate = torch.empty(M, NB)
+        norm.gate_proj(a, a_s, wb, wa, beta, gate, dt, al)
+        p = f"gate_proj_{i}_"
+        rec[p + "a"] = a.numpy(); rec[p + "as"] = a_s.numpy(); rec[p + "wb"] = bits(wb); rec[p + "wa"] = bits(wa)
+        rec[p + "dt"] = bits(dt); rec[p + "alog"] = bits(al)
+        rec[p + "beta"] = beta.numpy(); rec[p + "gate"] = gate.numpy()
+
+    out = os.path.join(HERE, "ref_golden_norm.npz")
+    np.savez_compressed(out, **rec)
+    print(f"wrote {out}: {len(rec)} arrays, {os.path.getsize(out)} bytes")
+
+
 def main():
-    if len(sys.argv) != 2:
-        sys.exit("usage: make_golden.py /path/to/reference-checkout")
+    if len(sys.argv) not in (2, 3):
+        sys.exit("usage: make_golden.py /path/to/reference-checkout [gemm|norm|all]")
     root = sys.argv[1]
+    which = sys.argv[2] if len(sys.argv) == 3 else "all"
     gemm, w4, norm = import_reference(root)
+    if which in ("norm", "all"):
+        producers(norm)
+    if which == "norm":
+        return
     G = 64
     rec = {}
 
