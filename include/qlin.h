@@ -190,6 +190,62 @@ int qlin_silu_mul_quant(const void* g, const void* u, int64_t M, int64_t N, int8
 int qlin_gate_proj(const int8_t* a_q, const float* a_s, int64_t M, int64_t K, const void* wb, const void* wa,
                    int64_t NB, const void* dt_bias, const void* a_log, float* beta, float* gate, void* stream);
 
+/* ---- Decode-step neighbours (kernels/attention.py, kernels/linear_attn.py):
+ * the kernels between the projections of one decode step.  A position may be
+ * passed in device memory (pos_dev, int32; NULL: use the scalar) so that a
+ * decode step can be captured in a CUDA graph once and replayed at every
+ * position.  bf16 data is 16-byte aligned with row strides in elements. ---- */
+
+/* kernels/attention.py:70-133 (qk_norm_rope) and :20-67 (_norm_rope_store).
+ * proj bf16 [T, ldp]: per q head hd query dims then hd gate dims, then nkv k
+ * heads, then nkv v heads.  q and k: RMSNorm over hd with (1 + qn / kn), then
+ * rotate-half RoPE on the first rd dims at angle pos * invf[i] (invf fp32
+ * [rd/2]); q scaled by 1/sqrt(hd) into qout [T, nq*hd].  k and v go to cache
+ * row `pos` of kvc [rows, 2*nkv*hd] (k heads then v heads): bf16, or
+ * (kv_int8) int8 codes with one fp32 scale max(amax/127, 1e-8) per
+ * (position, head, side) in kvs [rows, 2*nkv].  Row t of proj is position
+ * pos0 + t, or with `batch` candidate t at position pos0 in its own cache
+ * slice starting at t * kv_stride (t * kvs_stride for the scales).
+ * hd in {128, 256}. */
+int qlin_qk_norm_rope(const void* proj, int64_t ldp, const void* qn, const void* kn, const float* invf,
+                      int64_t rd, void* qout, void* kvc, float* kvs, int64_t T, int64_t nq, int64_t nkv,
+                      int64_t hd, int64_t pos0, const int32_t* pos_dev, float eps, int kv_int8, int batch,
+                      int64_t kv_stride, int64_t kvs_stride, void* stream);
+
+/* kernels/attention.py:209-267 (attn_decode): for each candidate b and q head
+ * h, softmax(q_h . k_n) over cache positions n = 0..pos (q already scaled)
+ * weighted sum of v_n, bf16 out [batch, nq*hd].  KV head of h: h / (nq/nkv).
+ * Cache as written by qlin_qk_norm_rope; candidate b's rows start at
+ * b * kv_stride.  max_pos (with pos_dev): the largest position a replay will
+ * see, which sets how the positions are split over the CTAs. */
+int qlin_attn_decode(const void* q, const void* kvc, const float* kvs, void* out, int64_t pos,
+                     const int32_t* pos_dev, int64_t max_pos, int64_t batch, int64_t nq, int64_t nkv,
+                     int64_t hd, int kv_int8, int64_t kv_stride, int64_t kvs_stride, void* stream);
+
+/* kernels/linear_attn.py:172-207 (delta_decode): one new token per candidate.
+ * qkv bf16 [batch, ldq] holds q [nh*dk], k [nh*dk], v [nh*dv]; g, beta fp32
+ * [batch, nh]; state fp32 [batch*nh, dk, dv] updated in place:
+ *   qn = q rsqrt(|q|^2 + 1e-6) / sqrt(dk), kn = k rsqrt(|k|^2 + 1e-6),
+ *   S *= exp(g); delta = (v - kn^T S) beta; S += kn delta^T; out = qn^T S
+ * -> bf16 out [batch, nh*dv].  dk = dv = 128. */
+int qlin_delta_decode(const void* qkv, int64_t ldq, const float* g, const float* beta, float* state, void* out,
+                      int64_t batch, int64_t nh, int64_t dk, int64_t dv, void* stream);
+
+/* kernels/linear_attn.py:10-47 (conv_silu): depthwise causal conv of width
+ * ks = 4 with bf16 weights w [C, 4], then SiLU: bf16 x [T, C] (row stride
+ * ldx) -> y [T, C].  Sequence mode: the taps before row 0 read the 3 state
+ * rows state [3, C].  Batch mode: row t is candidate t, taps 0..2 read its
+ * state rows state[3t .. 3t+2], tap 3 its input row.  C % 8 == 0. */
+int qlin_conv_silu(const void* x, int64_t ldx, const void* w, int64_t ks, const void* state, void* y, int64_t T,
+                   int64_t C, int batch, void* stream);
+
+/* kernels/linear_attn.py:50-83 (conv_state_update): the conv window keeps the
+ * last 3 raw input rows.  batch == 1: state [3, C] <- the last 3 of the T new
+ * rows (older state rows when T < 3).  batch > 1 (= T): each candidate's rows
+ * state[3b .. 3b+2] shift down by one and take x row b as the newest. */
+int qlin_conv_state_update(const void* x, int64_t ldx, void* state, int64_t T, int64_t C, int64_t ks,
+                           int64_t batch, void* stream);
+
 /* ---- Multi-GPU (column-split layer): NVLink peer memory through CUDA IPC ----
  * Not part of the reference's interface (it has no multi-GPU path); used by
  * the package's tp.py for its all-gathers. */

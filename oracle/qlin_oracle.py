@@ -442,6 +442,207 @@ def gate_proj(a_q, a_s, wb_bits, wa_bits, dt_bits, alog_bits):
 
 
 # ----------------------------------------------------------------------------
+# f2: decode-step neighbours  (kernels/attention.py, kernels/linear_attn.py)
+# ----------------------------------------------------------------------------
+
+def _norm_rope(x, w, pos, invf, rd, eps, scale):
+    """attention.py:20-67 (_norm_rope_store) before the store, fp32: RMSNorm
+    with (1 + w) over HD, then rotate-half RoPE on the first rd dims, times
+    `scale`.  Returns (plo, phi, yr*scale) as one HD vector."""
+    HD = x.shape[0]
+    d2 = rd // 2
+    blk = HD  # the reference loads the tail with arange(HD) masked to HD - rd
+    xlo, xhi = x[:d2], x[d2:rd]
+    xr = np.zeros(blk, dtype=np.float32)
+    xr[:HD - rd] = x[rd:]
+    wlo = (w[:d2] + np.float32(1.0)).astype(np.float32)
+    whi = (w[d2:rd] + np.float32(1.0)).astype(np.float32)
+    wr = np.zeros(blk, dtype=np.float32)
+    wr[:HD - rd] = w[rd:]
+    wr = (wr + np.float32(1.0)).astype(np.float32)
+    ss = (np.float32(np.sum((xlo * xlo).astype(np.float32), dtype=np.float32))
+          + np.float32(np.sum((xhi * xhi).astype(np.float32), dtype=np.float32)))
+    ss = (np.float32(ss) + np.float32(np.sum((xr * xr).astype(np.float32), dtype=np.float32))).astype(np.float32)
+    var = (np.float32(ss) / np.float32(HD)).astype(np.float32)
+    rstd = _rsqrt((var + np.float32(eps)).astype(np.float32))
+    ylo = ((xlo * rstd).astype(np.float32) * wlo).astype(np.float32)
+    yhi = ((xhi * rstd).astype(np.float32) * whi).astype(np.float32)
+    yr = ((xr * rstd).astype(np.float32) * wr).astype(np.float32)[:HD - rd]
+    theta = (np.float32(pos) * invf).astype(np.float32)
+    c, s = np.cos(theta).astype(np.float32), np.sin(theta).astype(np.float32)
+    sc = np.float32(scale)
+    plo = (((ylo * c).astype(np.float32) - (yhi * s).astype(np.float32)).astype(np.float32) * sc).astype(np.float32)
+    phi = (((yhi * c).astype(np.float32) + (ylo * s).astype(np.float32)).astype(np.float32) * sc).astype(np.float32)
+    return np.concatenate([plo, phi, (yr * sc).astype(np.float32)])
+
+
+def _quant_vec(y):
+    """attention.py:55-60: one amax/127 scale per vector, round_i8 codes."""
+    amax = np.float32(np.max(np.abs(y)))
+    sc = np.maximum((amax / np.float32(127.0)).astype(np.float32), np.float32(1e-8)).astype(np.float32)
+    return round_i8((y / sc).astype(np.float32)), np.float32(sc)
+
+
+def qk_norm_rope(proj_bits, qn_bits, kn_bits, invf, nq, nkv, hd, pos0, kvc, kvs=None, eps=1e-6,
+                 batch=False, mode="rne"):
+    """attention.py:70-133.  proj [T, >= (2 nq + 2 nkv) hd] bf16 bits (per q
+    head: hd query dims then hd gate dims; then k heads, then v heads).
+    Returns q bf16 bits [T, nq*hd] and writes K/V rows into ``kvc`` (a numpy
+    array [rows, 2*nkv*hd]: bf16 bits, or int8 with ``kvs`` [rows, 2*nkv]
+    fp32).  Row of token t: position pos0 + t; in batch mode row t is
+    candidate t at position pos0, in its own slice of kvc.shape[0] // T rows."""
+    p = bf16_bits_to_f32(proj_bits)
+    T = p.shape[0]
+    qn = bf16_bits_to_f32(qn_bits)
+    kn = bf16_bits_to_f32(kn_bits)
+    invf = np.asarray(invf, dtype=np.float32)
+    rd = 2 * invf.shape[0]
+    qscale = np.float32(1.0) / np.sqrt(np.float32(hd))
+    q = np.empty((T, nq * hd), dtype=np.uint16)
+    seq = kvc.shape[0] // T if batch else 0
+    int8 = kvs is not None
+    for t in range(T):
+        pos = pos0 if batch else pos0 + t
+        base = t * seq if batch else 0
+        for h in range(nq):
+            y = _norm_rope(p[t, h * 2 * hd:h * 2 * hd + hd], qn, pos, invf, rd, eps, qscale)
+            q[t, h * hd:(h + 1) * hd] = f32_to_bf16_bits(y, mode)
+        for j in range(nkv):
+            off = 2 * nq * hd
+            y = _norm_rope(p[t, off + j * hd:off + (j + 1) * hd], kn, pos, invf, rd, eps, 1.0)
+            v = p[t, off + nkv * hd + j * hd:off + nkv * hd + (j + 1) * hd]
+            if int8:
+                kvc[base + pos, j * hd:(j + 1) * hd], kvs[base + pos, j] = _quant_vec(y)
+                kvc[base + pos, (nkv + j) * hd:(nkv + j + 1) * hd], kvs[base + pos, nkv + j] = _quant_vec(v)
+            else:
+                kvc[base + pos, j * hd:(j + 1) * hd] = f32_to_bf16_bits(y, mode)
+                kvc[base + pos, (nkv + j) * hd:(nkv + j + 1) * hd] = f32_to_bf16_bits(v, mode)
+    return q
+
+
+def _kv_rows(kvc, kvs, rows, side, kvh, nkv, hd):
+    """fp32 K (side 0) or V (side 1) vectors of one kv head for `rows`."""
+    col = (side * nkv + kvh) * hd
+    if kvs is None:
+        return bf16_bits_to_f32(kvc[rows, col:col + hd])
+    return (kvc[rows, col:col + hd].astype(np.float32) * kvs[rows, side * nkv + kvh][:, None]).astype(np.float32)
+
+
+def attn_decode_f32(q_bits, kvc, pos, kvs=None, batch=1, nq=8, nkv=2, hd=256, block_n=32):
+    """attention.py:209-267 before the bf16 store: per candidate b and q head,
+    online softmax over positions 0..pos in blocks of block_n (m, l, acc
+    rescaled per block, exp in fp32).  q [batch, nq*hd] bf16 bits; kvc rows
+    of candidate b are kvc[b*S : (b+1)*S] with S = rows // batch."""
+    q = bf16_bits_to_f32(q_bits).reshape(batch, nq, hd)
+    S = kvc.shape[0] // batch
+    out = np.empty((batch, nq, hd), dtype=np.float32)
+    n = pos + 1
+    for b in range(batch):
+        for h in range(nq):
+            kvh = h // (nq // nkv)
+            m_i, l_i = np.float32(-np.inf), np.float32(0.0)
+            acc = np.zeros(hd, dtype=np.float32)
+            for s0 in range(0, n, block_n):
+                rows = np.arange(s0, min(n, s0 + block_n))
+                k = _kv_rows(kvc, kvs, b * S + rows, 0, kvh, nkv, hd)
+                v = _kv_rows(kvc, kvs, b * S + rows, 1, kvh, nkv, hd)
+                sc = np.sum((q[b, h][None, :] * k).astype(np.float32), axis=1, dtype=np.float32)
+                m_new = np.float32(max(m_i, np.float32(sc.max())))
+                p = np.exp((sc - m_new).astype(np.float32)).astype(np.float32)
+                alpha = np.float32(np.exp(np.float32(m_i - m_new)))
+                l_i = np.float32(np.float32(l_i * alpha) + np.float32(np.sum(p, dtype=np.float32)))
+                acc = (acc * alpha).astype(np.float32)
+                acc = (acc + np.sum((p[:, None] * v).astype(np.float32), axis=0, dtype=np.float32)).astype(np.float32)
+                m_i = m_new
+            out[b, h] = (acc / l_i).astype(np.float32)
+    return out.reshape(batch, nq * hd)
+
+
+def attn_decode(q_bits, kvc, pos, kvs=None, batch=1, nq=8, nkv=2, hd=256, mode="rne"):
+    """attention.py:209-267 -> bf16 bits [batch, nq*hd]."""
+    return f32_to_bf16_bits(attn_decode_f32(q_bits, kvc, pos, kvs, batch, nq, nkv, hd), mode)
+
+
+def _l2norm(x, scale=None):
+    ss = np.float32(np.sum((x * x).astype(np.float32), dtype=np.float32))
+    y = (x * _rsqrt(np.float32(ss + np.float32(1e-6)))).astype(np.float32)
+    if scale is not None:
+        y = (y * np.float32(scale)).astype(np.float32)
+    return y
+
+
+def delta_decode(qkv_bits, g, beta, state, nh=16, dk=128, dv=128, mode="rne"):
+    """linear_attn.py:172-207, one token per batch row b:
+    qn = l2norm(q) / sqrt(dk), kn = l2norm(k); S *= exp(g);
+    kv = kn^T S; delta = (v - kv) * beta; S += kn delta^T; out = qn^T S.
+    qkv [B, 2 nh dk + nh dv] bf16 bits, g / beta [B, nh] fp32, state
+    [B*nh, dk, dv] fp32 (updated in place).  Returns out bf16 bits [B, nh*dv]."""
+    x = bf16_bits_to_f32(qkv_bits)
+    B = x.shape[0]
+    g = np.asarray(g, dtype=np.float32).reshape(B, nh)
+    beta = np.asarray(beta, dtype=np.float32).reshape(B, nh)
+    out = np.empty((B, nh * dv), dtype=np.float32)
+    inv = np.float32(1.0) / np.sqrt(np.float32(dk))
+    for b in range(B):
+        for h in range(nh):
+            q = x[b, h * dk:(h + 1) * dk]
+            k = x[b, nh * dk + h * dk:nh * dk + (h + 1) * dk]
+            v = x[b, 2 * nh * dk + h * dv:2 * nh * dk + (h + 1) * dv]
+            qn = _l2norm(q, inv)
+            kn = _l2norm(k)
+            S = (state[b * nh + h] * np.float32(np.exp(g[b, h]))).astype(np.float32)
+            kv = np.sum((kn[:, None] * S).astype(np.float32), axis=0, dtype=np.float32)
+            delta = ((v - kv).astype(np.float32) * beta[b, h]).astype(np.float32)
+            S = (S + (kn[:, None] * delta[None, :]).astype(np.float32)).astype(np.float32)
+            out[b, h * dv:(h + 1) * dv] = np.sum((qn[:, None] * S).astype(np.float32), axis=0, dtype=np.float32)
+            state[b * nh + h] = S
+    return f32_to_bf16_bits(out, mode)
+
+
+def conv_silu(x_bits, w_bits, state_bits, T, batch=False, mode="rne"):
+    """linear_attn.py:10-47: depthwise causal conv of width KS = w.shape[1]
+    then SiLU.  Non-batch: output row t sums x[t - KS + 1 + j] * w[:, j] over
+    j (rows before 0 come from the KS - 1 state rows).  Batch: row t is one
+    candidate; taps 0..KS-2 read that candidate's state rows t*(KS-1) + j, the
+    last tap its own input row.  Returns bf16 bits [T, C]."""
+    x = bf16_bits_to_f32(x_bits)
+    w = bf16_bits_to_f32(w_bits)
+    st = bf16_bits_to_f32(state_bits)
+    C, KS = w.shape
+    acc = np.zeros((T, C), dtype=np.float32)
+    for j in range(KS):
+        if batch:
+            src = j - (KS - 1)
+            xa = x[:T] if src >= 0 else st[np.arange(T) * (KS - 1) + j]
+        else:
+            rows = np.arange(T) - (KS - 1) + j
+            xa = np.where((rows >= 0)[:, None], x[np.clip(rows, 0, None)],
+                          st[np.clip(KS - 1 + rows, 0, KS - 2)])
+        acc = (acc + (xa * w[None, :, j]).astype(np.float32)).astype(np.float32)
+    return f32_to_bf16_bits(silu(acc), mode)
+
+
+def conv_state_update(x_bits, state_bits, T, batch=1):
+    """linear_attn.py:50-83 -> the new state (bf16 bits).  Non-batch: the last
+    KS - 1 raw input rows of the T new ones (older ones from the state when T
+    is short).  Batch: each candidate's rows shift down by one and take its
+    own input row as the newest."""
+    x = np.asarray(x_bits, dtype=np.uint16)
+    st = np.array(state_bits, dtype=np.uint16, copy=True)
+    kk = 3
+    if batch > 1:
+        for b in range(batch):
+            st[b * kk:b * kk + kk - 1] = st[b * kk + 1:b * kk + kk].copy()
+            st[b * kk + kk - 1] = x[b]
+        return st
+    new = st.copy()
+    for j in range(kk):
+        src = T - kk + j
+        new[j] = x[src] if src >= 0 else st[src + kk]
+    return new
+
+
+# ----------------------------------------------------------------------------
 # CPU baseline: the reference's own dequant-then-matmul (.dev/test_kernels.py:40-41)
 # ----------------------------------------------------------------------------
 

@@ -38,6 +38,12 @@ SIGNATURES = {
     "qlin_gate_mul_quant": [_P, _P, _I, _I, _I, _I, _P, _P, _P],
     "qlin_silu_mul_quant": [_P, _P, _I, _I, _P, _P, _P],
     "qlin_gate_proj": [_P, _P, _I, _I, _P, _P, _I, _P, _P, _P, _P, _P],
+    "qlin_qk_norm_rope": [_P, _I, _P, _P, _P, _I, _P, _P, _P, _I, _I, _I, _I, _I, _P, ctypes.c_float, ctypes.c_int,
+                          ctypes.c_int, _I, _I, _P],
+    "qlin_attn_decode": [_P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, ctypes.c_int, _I, _I, _P],
+    "qlin_delta_decode": [_P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _P],
+    "qlin_conv_silu": [_P, _I, _P, _I, _P, _P, _I, _I, ctypes.c_int, _P],
+    "qlin_conv_state_update": [_P, _I, _P, _I, _I, _I, _I, _P],
     "qlin_plan_small_m": [ctypes.c_int, ctypes.c_int, _I, _I, _I, _I, ctypes.c_int, _P],
     "qlin_max_active_clusters": [ctypes.c_int, ctypes.c_int, _I, ctypes.c_int, _I, ctypes.POINTER(ctypes.c_int64)],
     "qlin_ipc_get_handle": [_P, _P, ctypes.POINTER(ctypes.c_int64)],

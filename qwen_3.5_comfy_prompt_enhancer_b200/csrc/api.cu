@@ -17,6 +17,7 @@
 #include "quant.cuh"
 #include "peer.cuh"
 #include "producers.cuh"
+#include "decode.cuh"
 #include "tcgemm.cuh"
 #include "tcgemm_w4.cuh"
 #include "tcgemv.cuh"
@@ -1139,6 +1140,87 @@ int peer_launch(const PeerGatherArgs& a, int ctas, cudaStream_t st) {
   if (e != cudaSuccess) return cuda_fail(e, "peer_allgather_kernel launch");
   return QLIN_OK;
 }
+
+// ---------------------------------------------------------------- activation producers (kernels/norm.py)
+int prod_launch(const void* kern, dim3 grid, void** args, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kProdThreads, 1, 1);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelExC(&cfg, kern, args);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(producer)");
+  return QLIN_OK;
+}
+
+int check_rows(int64_t M, int64_t K, const char* what) {
+  if (M < 0 || K < 0) return fail(QLIN_ERR_INVALID_ARGUMENT, "%s: negative size", what);
+  if (M > 65535 * 64) return fail(QLIN_ERR_SHAPE, "%s: M=%lld too large", what, (long long)M);
+  return QLIN_OK;
+}
+
+// ---------------------------------------------------------------- decode-step neighbours
+int dec_launch(const void* kern, dim3 grid, dim3 block, size_t smem, int cluster, void** args, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  int na = 1;
+  if (cluster > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = cluster;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    na = 2;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  cudaError_t e = cudaLaunchKernelExC(&cfg, kern, args);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(decode neighbour)");
+  return QLIN_OK;
+}
+
+// Opt a kernel in to `bytes` of dynamic shared memory once per device.
+int smem_optin(const void* kern, size_t bytes, std::atomic<unsigned long long>& done) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(done.load() & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(smem)");
+    done.fetch_or(bit);
+  }
+  return QLIN_OK;
+}
+
+template <int G, int E, bool INT8>
+int launch_attn_decode(AttnDecodeArgs& a, int S, int nkv, int B, cudaStream_t st) {
+  static std::atomic<unsigned long long> done{0};
+  const void* kern = reinterpret_cast<const void*>(attn_decode_kernel<G, E, INT8>);
+  const size_t smem = attn_decode_smem(G, E);
+  if (int r = smem_optin(kern, smem, done)) return r;
+  void* args[] = {&a};
+  return dec_launch(kern, dim3(S, nkv, B), dim3(kDecThreads), smem, S, args, st);
+}
+
+template <int E, bool INT8>
+int attn_decode_g(int G, AttnDecodeArgs& a, int S, int nkv, int B, cudaStream_t st) {
+  switch (G) {
+    case 1: return launch_attn_decode<1, E, INT8>(a, S, nkv, B, st);
+    case 2: return launch_attn_decode<2, E, INT8>(a, S, nkv, B, st);
+    case 4: return launch_attn_decode<4, E, INT8>(a, S, nkv, B, st);
+    case 8: return launch_attn_decode<8, E, INT8>(a, S, nkv, B, st);
+    default: return fail(QLIN_ERR_SHAPE, "attn_decode: %d query heads per KV head (1, 2, 4 or 8)", G);
+  }
+}
 }  // namespace
 }  // namespace qlin
 
@@ -1606,30 +1688,6 @@ int qlin_quant_row(const void* x, int64_t ldx, int64_t M, int64_t K, int8_t* q, 
 }
 
 
-// ---------------------------------------------------------------- activation producers (kernels/norm.py)
-namespace {
-int prod_launch(const void* kern, dim3 grid, void** args, cudaStream_t st) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(kProdThreads, 1, 1);
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelExC(&cfg, kern, args);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(producer)");
-  return QLIN_OK;
-}
-
-int check_rows(int64_t M, int64_t K, const char* what) {
-  if (M < 0 || K < 0) return fail(QLIN_ERR_INVALID_ARGUMENT, "%s: negative size", what);
-  if (M > 65535 * 64) return fail(QLIN_ERR_SHAPE, "%s: M=%lld too large", what, (long long)M);
-  return QLIN_OK;
-}
-}  // namespace
-
 int qlin_rmsnorm_quant(const void* x, int64_t ldx, const void* w, int64_t M, int64_t K, float eps, int one_plus,
                        int8_t* q, float* s, void* stream) {
   if (int r = check_rows(M, K, "rmsnorm_quant")) return r;
@@ -1759,6 +1817,159 @@ int qlin_gate_proj(const int8_t* a_q, const float* a_s, int64_t M, int64_t K, co
   const void* kern = NB <= 16 ? reinterpret_cast<const void*>(gate_proj_kernel<16>)
                               : reinterpret_cast<const void*>(gate_proj_kernel<32>);
   return prod_launch(kern, dim3(static_cast<unsigned>(M)), args, static_cast<cudaStream_t>(stream));
+}
+
+
+int qlin_qk_norm_rope(const void* proj, int64_t ldp, const void* qn, const void* kn, const float* invf, int64_t rd,
+                      void* qout, void* kvc, float* kvs, int64_t T, int64_t nq, int64_t nkv, int64_t hd, int64_t pos0,
+                      const int32_t* pos_dev, float eps, int kv_int8, int batch, int64_t kv_stride,
+                      int64_t kvs_stride, void* stream) {
+  if (T < 0 || nq <= 0 || nkv <= 0 || pos0 < 0) return fail(QLIN_ERR_INVALID_ARGUMENT, "qk_norm_rope: bad size");
+  if (!(hd == 128 || hd == 256)) return fail(QLIN_ERR_SHAPE, "qk_norm_rope: head dim %lld (128 or 256)", (long long)hd);
+  const int E = static_cast<int>(hd / 32);
+  if (rd <= 0 || rd > hd || rd % (2 * E) != 0 || ((rd / 2) / E) > 16)
+    return fail(QLIN_ERR_SHAPE, "qk_norm_rope: rotary dims %lld must be a multiple of %d up to head dim", (long long)rd,
+                2 * E);
+  if (T == 0) return QLIN_OK;
+  if (!proj || !qn || !kn || !invf || !qout || !kvc || (kv_int8 && !kvs))
+    return fail(QLIN_ERR_INVALID_ARGUMENT, "qk_norm_rope: null pointer");
+  if (ldp < (2 * nq + 2 * nkv) * hd) return fail(QLIN_ERR_SHAPE, "qk_norm_rope: projection row too short");
+  if (!aligned(proj, 16) || ldp % 8 != 0 || !aligned(qn, 16) || !aligned(kn, 16) || !aligned(qout, 16) ||
+      !aligned(kvc, 16) || !aligned(invf, 4) || (kvs && !aligned(kvs, 4)) || (pos_dev && !aligned(pos_dev, 4)))
+    return fail(QLIN_ERR_ALIGNMENT, "qk_norm_rope: 16-byte aligned rows required");
+  if (batch && (kv_stride < 0 || kvs_stride < 0)) return fail(QLIN_ERR_INVALID_ARGUMENT, "qk_norm_rope: strides");
+  DevInfo di;
+  if (int r = launch_info(&di)) return r;
+  QkRopeArgs a;
+  a.proj = static_cast<const __nv_bfloat16*>(proj);
+  a.ldp = ldp;
+  a.qn = static_cast<const __nv_bfloat16*>(qn);
+  a.kn = static_cast<const __nv_bfloat16*>(kn);
+  a.invf = invf;
+  a.qout = static_cast<__nv_bfloat16*>(qout);
+  a.kvc = kvc;
+  a.kvs = kvs;
+  a.pos_dev = pos_dev;
+  a.kv_stride = batch ? kv_stride : 0;
+  a.kvs_stride = batch ? kvs_stride : 0;
+  a.T = static_cast<int>(T);
+  a.nq = static_cast<int>(nq);
+  a.nkv = static_cast<int>(nkv);
+  a.rd = static_cast<int>(rd);
+  a.pos0 = static_cast<int>(pos0);
+  a.batch = batch ? 1 : 0;
+  a.eps = eps;
+  const long long warps = T * (nq + 2 * nkv);
+  const unsigned blocks = static_cast<unsigned>((warps + kDecThreads / 32 - 1) / (kDecThreads / 32));
+  const void* kern = hd == 256 ? (kv_int8 ? reinterpret_cast<const void*>(qk_norm_rope_kernel<256, true>)
+                                          : reinterpret_cast<const void*>(qk_norm_rope_kernel<256, false>))
+                               : (kv_int8 ? reinterpret_cast<const void*>(qk_norm_rope_kernel<128, true>)
+                                          : reinterpret_cast<const void*>(qk_norm_rope_kernel<128, false>));
+  void* args[] = {&a};
+  return dec_launch(kern, dim3(blocks), dim3(kDecThreads), 0, 1, args, static_cast<cudaStream_t>(stream));
+}
+
+int qlin_attn_decode(const void* q, const void* kvc, const float* kvs, void* out, int64_t pos, const int32_t* pos_dev,
+                     int64_t max_pos, int64_t batch, int64_t nq, int64_t nkv, int64_t hd, int kv_int8,
+                     int64_t kv_stride, int64_t kvs_stride, void* stream) {
+  if (batch <= 0 || nq <= 0 || nkv <= 0 || nq % nkv != 0 || pos < 0)
+    return fail(QLIN_ERR_INVALID_ARGUMENT, "attn_decode: bad size");
+  if (!(hd == 128 || hd == 256)) return fail(QLIN_ERR_SHAPE, "attn_decode: head dim %lld (128 or 256)", (long long)hd);
+  if (batch > 65535 || nkv > 65535) return fail(QLIN_ERR_SHAPE, "attn_decode: too many candidates / heads");
+  if (!q || !kvc || !out || (kv_int8 && !kvs)) return fail(QLIN_ERR_INVALID_ARGUMENT, "attn_decode: null pointer");
+  if (!aligned(q, 16) || !aligned(kvc, 16) || (kvs && !aligned(kvs, 4)) || (pos_dev && !aligned(pos_dev, 4)))
+    return fail(QLIN_ERR_ALIGNMENT, "attn_decode: q and the cache need 16-byte alignment");
+  if (batch > 1 && (kv_stride <= 0 || (kv_int8 && kvs_stride <= 0)))
+    return fail(QLIN_ERR_INVALID_ARGUMENT, "attn_decode: per-candidate cache strides required for batch > 1");
+  DevInfo di;
+  if (int r = launch_info(&di)) return r;
+  AttnDecodeArgs a;
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.kvc = kvc;
+  a.kvs = kvs;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.pos_dev = pos_dev;
+  a.kv_stride = batch > 1 ? kv_stride : 0;
+  a.kvs_stride = batch > 1 ? kvs_stride : 0;
+  a.pos = static_cast<int>(pos);
+  a.nq = static_cast<int>(nq);
+  a.nkv = static_cast<int>(nkv);
+  // positions per CTA: about 64 (8 warps x 8), clusters of up to 8 CTAs; with
+  // a device-side position the split follows the largest position expected
+  const long long n = (pos_dev ? (max_pos > pos ? max_pos : pos) : pos) + 1;
+  int S = static_cast<int>((n + 63) / 64);
+  if (S > 8) S = 8;
+  if (S < 1) S = 1;
+  const int G = static_cast<int>(nq / nkv);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int B = static_cast<int>(batch), NKV = static_cast<int>(nkv);
+  if (hd == 256) return kv_int8 ? attn_decode_g<8, true>(G, a, S, NKV, B, st) : attn_decode_g<8, false>(G, a, S, NKV, B, st);
+  return kv_int8 ? attn_decode_g<4, true>(G, a, S, NKV, B, st) : attn_decode_g<4, false>(G, a, S, NKV, B, st);
+}
+
+int qlin_delta_decode(const void* qkv, int64_t ldq, const float* g, const float* beta, float* state, void* out,
+                      int64_t batch, int64_t nh, int64_t dk, int64_t dv, void* stream) {
+  if (batch <= 0 || nh <= 0) return fail(QLIN_ERR_INVALID_ARGUMENT, "delta_decode: bad size");
+  if (dk != kDeltaDK || dv != kDeltaDV) return fail(QLIN_ERR_SHAPE, "delta_decode: head dims must be 128 x 128");
+  if (batch > 65535 || nh > 65535) return fail(QLIN_ERR_SHAPE, "delta_decode: too many candidates / heads");
+  if (!qkv || !g || !beta || !state || !out) return fail(QLIN_ERR_INVALID_ARGUMENT, "delta_decode: null pointer");
+  if (batch > 1 && ldq < (2 * dk + dv) * nh) return fail(QLIN_ERR_SHAPE, "delta_decode: qkv row stride too small");
+  if (!aligned(qkv, 2) || !aligned(state, 16) || !aligned(out, 2) || !aligned(g, 4) || !aligned(beta, 4))
+    return fail(QLIN_ERR_ALIGNMENT, "delta_decode: state needs 16-byte alignment");
+  DevInfo di;
+  if (int r = launch_info(&di)) return r;
+  long long ldq_ = batch > 1 ? ldq : 0;
+  int nh_ = static_cast<int>(nh);
+  const __nv_bfloat16* qp = static_cast<const __nv_bfloat16*>(qkv);
+  __nv_bfloat16* op = static_cast<__nv_bfloat16*>(out);
+  void* args[] = {&qp, &ldq_, const_cast<float**>(&g), const_cast<float**>(&beta), &state, &op, &nh_};
+  return dec_launch(reinterpret_cast<const void*>(delta_decode_kernel),
+                    dim3(static_cast<unsigned>(nh), static_cast<unsigned>(batch), kDeltaDV / 32),
+                    dim3(kDeltaWarps * 32), 0, 1, args, static_cast<cudaStream_t>(stream));
+}
+
+int qlin_conv_silu(const void* x, int64_t ldx, const void* w, int64_t ks, const void* state, void* y, int64_t T,
+                   int64_t C, int batch, void* stream) {
+  if (T < 0 || C < 0) return fail(QLIN_ERR_INVALID_ARGUMENT, "conv_silu: bad size");
+  if (ks != kConvKS) return fail(QLIN_ERR_SHAPE, "conv_silu: kernel width %lld (4 supported)", (long long)ks);
+  if (C % 8 != 0) return fail(QLIN_ERR_SHAPE, "conv_silu: channels must be a multiple of 8");
+  if (T == 0 || C == 0) return QLIN_OK;
+  if (T > 65535) return fail(QLIN_ERR_SHAPE, "conv_silu: T too large");
+  if (!x || !w || !state || !y) return fail(QLIN_ERR_INVALID_ARGUMENT, "conv_silu: null pointer");
+  if (ldx < C) return fail(QLIN_ERR_SHAPE, "conv_silu: row stride smaller than C");
+  if (!aligned(x, 16) || ldx % 8 != 0 || !aligned(w, 16) || !aligned(state, 16) || !aligned(y, 16))
+    return fail(QLIN_ERR_ALIGNMENT, "conv_silu: 16-byte aligned rows required");
+  DevInfo di;
+  if (int r = launch_info(&di)) return r;
+  long long ldx_ = ldx;
+  int T_ = static_cast<int>(T), C_ = static_cast<int>(C), b_ = batch ? 1 : 0;
+  void* args[] = {const_cast<void**>(&x), &ldx_, const_cast<void**>(&w), const_cast<void**>(&state), &y, &T_, &C_, &b_};
+  const unsigned cb = static_cast<unsigned>((C / 8 + kDecThreads - 1) / kDecThreads);
+  return dec_launch(reinterpret_cast<const void*>(conv_silu_kernel), dim3(cb, static_cast<unsigned>(T)),
+                    dim3(kDecThreads), 0, 1, args, static_cast<cudaStream_t>(stream));
+}
+
+int qlin_conv_state_update(const void* x, int64_t ldx, void* state, int64_t T, int64_t C, int64_t ks, int64_t batch,
+                           void* stream) {
+  if (T < 0 || C < 0 || batch <= 0) return fail(QLIN_ERR_INVALID_ARGUMENT, "conv_state_update: bad size");
+  if (ks != kConvKS) return fail(QLIN_ERR_SHAPE, "conv_state_update: kernel width %lld (4 supported)", (long long)ks);
+  if (C % 8 != 0) return fail(QLIN_ERR_SHAPE, "conv_state_update: channels must be a multiple of 8");
+  if (T == 0 || C == 0) return QLIN_OK;
+  if (batch > 1 && batch != T) return fail(QLIN_ERR_SHAPE, "conv_state_update: batch mode takes one row per candidate");
+  if (batch > 65535) return fail(QLIN_ERR_SHAPE, "conv_state_update: batch too large");
+  if (!x || !state) return fail(QLIN_ERR_INVALID_ARGUMENT, "conv_state_update: null pointer");
+  if (ldx < C) return fail(QLIN_ERR_SHAPE, "conv_state_update: row stride smaller than C");
+  if (!aligned(x, 16) || ldx % 8 != 0 || !aligned(state, 16))
+    return fail(QLIN_ERR_ALIGNMENT, "conv_state_update: 16-byte aligned rows required");
+  DevInfo di;
+  if (int r = launch_info(&di)) return r;
+  long long ldx_ = ldx;
+  int T_ = static_cast<int>(T), C_ = static_cast<int>(C), b_ = batch > 1 ? 1 : 0;
+  void* args[] = {const_cast<void**>(&x), &ldx_, &state, &T_, &C_, &b_};
+  const unsigned cb = static_cast<unsigned>((C / 8 + kDecThreads - 1) / kDecThreads);
+  return dec_launch(reinterpret_cast<const void*>(conv_state_update_kernel),
+                    dim3(cb, static_cast<unsigned>(batch > 1 ? batch : 1)), dim3(kDecThreads), 0, 1, args,
+                    static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

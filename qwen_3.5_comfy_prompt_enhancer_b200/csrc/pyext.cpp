@@ -402,6 +402,123 @@ int gate_proj(const Tensor& a_q, const Tensor& a_s, const Tensor& wb, const Tens
   });
 }
 
+// ---------------------------------------------------------------- kernels/attention.py, kernels/linear_attn.py
+// Tensors of the decode neighbours may be 1-D rows (the reference's batch-1
+// calls pass ws.q[0], ws.mixed[0], ...): these checks look at dtype,
+// device, contiguity of the last dimension and element counts.
+void need_any(Call& c, const Tensor& t, const char* name, c10::ScalarType dt) {
+  c.need(t, name, dt, t.dim(), false);
+  if (t.dim() == 0 || t.stride(t.dim() - 1) != 1)
+    throw py::value_error(std::string(name) + " must have unit stride along its last dimension");
+}
+
+const int32_t* pos_ptr(Call& c, const OptT& pos_dev) {
+  if (!pos_dev) return nullptr;
+  c.need(*pos_dev, "pos (device)", at::kInt, pos_dev->dim());
+  if (pos_dev->numel() != 1) throw py::value_error("a device-side position is a one-element int32 tensor");
+  return static_cast<const int32_t*>(pos_dev->data_ptr());
+}
+
+int qk_norm_rope(const Tensor& proj, const Tensor& qn, const Tensor& kn, const Tensor& invf, const Tensor& qout,
+                 const Tensor& kvc, const OptT& kvs, int64_t pos0, const OptT& pos_dev, double eps, bool kv_int8,
+                 bool batch, int64_t kv_stride, int64_t kvs_stride) {
+  Call c;
+  c.need_rows(proj, "proj", at::kBFloat16);
+  c.need(qn, "qn", at::kBFloat16, 1);
+  c.need(kn, "kn", at::kBFloat16, 1);
+  c.need(invf, "invf", at::kFloat, 1);
+  c.need(qout, "qout", at::kBFloat16, 2);
+  c.need(kvc, "kvc", kv_int8 ? at::kChar : at::kBFloat16, 2);
+  if (kv_int8) {
+    if (!kvs) throw py::value_error("kv_int8=True requires the kvs scales tensor");
+    c.need(*kvs, "kvs", at::kFloat, 2);
+  }
+  const int64_t T = proj.size(0), HD = qn.size(0);
+  if (kn.size(0) != HD || HD == 0) throw py::value_error("qn and kn must both have head_dim entries");
+  const int64_t NQ = qout.size(1) / HD, NKV = kvc.size(1) / (2 * HD), RD = 2 * invf.size(0);
+  if (qout.size(0) != T || qout.size(1) != NQ * HD) throw py::value_error("qout must be [T, nq * head_dim]");
+  const int32_t* pd = pos_ptr(c, pos_dev);
+  return c.launch([&](void* st) {
+    return qlin_qk_norm_rope(proj.data_ptr(), proj.stride(0), qn.data_ptr(), kn.data_ptr(),
+                             static_cast<const float*>(invf.data_ptr()), RD, qout.data_ptr(), kvc.data_ptr(),
+                             kv_int8 ? static_cast<float*>(kvs->data_ptr()) : nullptr, T, NQ, NKV, HD, pos0, pd,
+                             static_cast<float>(eps), kv_int8 ? 1 : 0, batch ? 1 : 0, kv_stride, kvs_stride, st);
+  });
+}
+
+int attn_decode(const Tensor& q, const Tensor& kvc, const Tensor& out, int64_t pos, const OptT& pos_dev,
+                int64_t max_pos, const OptT& kvs, bool kv_int8, int64_t batch, int64_t nq, int64_t nkv, int64_t hd) {
+  Call c;
+  need_any(c, q, "q", at::kBFloat16);
+  need_any(c, out, "out", at::kBFloat16);
+  c.need(kvc, "kvc", kv_int8 ? at::kChar : at::kBFloat16, kvc.dim());
+  if (kv_int8) {
+    if (!kvs) throw py::value_error("kv_int8=True requires the kvs scales tensor");
+    c.need(*kvs, "kvs", at::kFloat, kvs->dim());
+  }
+  if (q.numel() != batch * nq * hd || out.numel() != batch * nq * hd || !q.is_contiguous() || !out.is_contiguous())
+    throw py::value_error("q and out must be contiguous with batch * nq * hd elements");
+  const int64_t kv_stride = batch > 1 ? kvc.numel() / batch : 0;
+  const int64_t kvs_stride = (batch > 1 && kvs) ? kvs->numel() / batch : 0;
+  const int32_t* pd = pos_ptr(c, pos_dev);
+  return c.launch([&](void* st) {
+    return qlin_attn_decode(q.data_ptr(), kvc.data_ptr(), kvs ? static_cast<const float*>(kvs->data_ptr()) : nullptr,
+                            out.data_ptr(), pos, pd, max_pos, batch, nq, nkv, hd, kv_int8 ? 1 : 0, kv_stride,
+                            kvs_stride, st);
+  });
+}
+
+int delta_decode(const Tensor& qkv, const Tensor& g, const Tensor& beta, const Tensor& state, const Tensor& out,
+                 int64_t batch) {
+  Call c;
+  need_any(c, qkv, "qkv", at::kBFloat16);
+  c.need(g, "g", at::kFloat, g.dim());
+  c.need(beta, "beta", at::kFloat, beta.dim());
+  c.need(state, "state", at::kFloat, state.dim());
+  need_any(c, out, "out", at::kBFloat16);
+  if (state.dim() < 2) throw py::value_error("state must be [batch*nh, dk, dv]");
+  const int64_t dv = state.size(state.dim() - 1), dk = state.size(state.dim() - 2);
+  const int64_t nh = g.numel() / batch;
+  if (g.numel() != batch * nh || beta.numel() != batch * nh || state.numel() != batch * nh * dk * dv)
+    throw py::value_error("g / beta must hold batch * nh values and state batch * nh * dk * dv");
+  if (out.numel() != batch * nh * dv || !out.is_contiguous()) throw py::value_error("out must hold batch * nh * dv");
+  const int64_t ldq = qkv.dim() >= 2 ? qkv.stride(0) : 0;
+  if (qkv.dim() == 1 && batch != 1) throw py::value_error("a 1-D qkv row serves batch 1 only");
+  return c.launch([&](void* st) {
+    return qlin_delta_decode(qkv.data_ptr(), ldq, static_cast<const float*>(g.data_ptr()),
+                             static_cast<const float*>(beta.data_ptr()), static_cast<float*>(state.data_ptr()),
+                             out.data_ptr(), batch, nh, dk, dv, st);
+  });
+}
+
+int conv_silu(const Tensor& x, const Tensor& w, const Tensor& state, const Tensor& y, int64_t T, bool batch) {
+  Call c;
+  c.need_rows(x, "x", at::kBFloat16);
+  c.need(w, "w", at::kBFloat16, 2);
+  c.need(state, "state", at::kBFloat16, 2);
+  c.need(y, "y", at::kBFloat16, 2);
+  const int64_t C = x.size(1);
+  if (w.size(0) != C || state.size(1) != C || y.size(1) != C || y.size(0) < T || x.size(0) < T)
+    throw py::value_error("conv_silu: x [T, C], w [C, ks], state [rows, C], y [T, C] required");
+  if (state.size(0) < (batch ? 3 * T : 3)) throw py::value_error("conv_silu: state has too few rows");
+  return c.launch([&](void* st) {
+    return qlin_conv_silu(x.data_ptr(), x.stride(0), w.data_ptr(), w.size(1), state.data_ptr(), y.data_ptr(), T, C,
+                          batch ? 1 : 0, st);
+  });
+}
+
+int conv_state_update(const Tensor& x, const Tensor& state, int64_t T, int64_t batch) {
+  Call c;
+  c.need_rows(x, "x", at::kBFloat16);
+  c.need(state, "state", at::kBFloat16, 2);
+  const int64_t C = x.size(1);
+  if (state.size(1) != C || x.size(0) < T || state.size(0) < 3 * batch)
+    throw py::value_error("conv_state_update: x [T, C], state [3 * batch, C] required");
+  return c.launch([&](void* st) {
+    return qlin_conv_state_update(x.data_ptr(), x.stride(0), state.data_ptr(), T, C, 4, batch, st);
+  });
+}
+
 }  // namespace
 
 PYBIND11_MODULE(_qlin_ext, m) {
@@ -419,4 +536,9 @@ PYBIND11_MODULE(_qlin_ext, m) {
   m.def("gate_mul_quant", &gate_mul_quant);
   m.def("silu_mul_quant", &silu_mul_quant);
   m.def("gate_proj", &gate_proj);
+  m.def("qk_norm_rope", &qk_norm_rope);
+  m.def("attn_decode", &attn_decode);
+  m.def("delta_decode", &delta_decode);
+  m.def("conv_silu", &conv_silu);
+  m.def("conv_state_update", &conv_state_update);
 }

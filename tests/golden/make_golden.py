@@ -5,7 +5,9 @@ The reference's Triton kernels (``kernels/gemm.py``, ``kernels/w4.py``,
 (``TRITON_INTERPRET=1``).  This script imports them from a read-only checkout of
 the reference project, runs every hot-path entry point on small seeded inputs
 and stores inputs and outputs in ``ref_golden.npz`` (GEMMs, quant_row) and
-``ref_golden_norm.npz`` (the other activation producers) next to this file.
+``ref_golden_norm.npz`` (the other activation producers) and
+``ref_golden_decode.npz`` (the decode-step neighbours of kernels/attention.py
+and kernels/linear_attn.py) next to this file.
 
 The interpreter converts fp32 -> bf16 by truncation (a GPU build rounds to
 nearest-even), so the fixtures pin the oracle in its ``mode="trunc"``; every
@@ -13,7 +15,7 @@ other step of the arithmetic is shared by both modes.
 
 Usage (in a container that has the reference checkout)::
 
-    python tests/golden/make_golden.py /path/to/reference [gemm|norm|all]
+    python tests/golden/make_golden.py /path/to/reference [gemm|norm|decode|all]
 
 bf16 tensors are stored as uint16 bit patterns.  Nothing at test time reads
 the reference: the tests only load the committed ``.npz``.
@@ -139,15 +141,114 @@ def producers(norm):
     print(f"wrote {out}: {len(rec)} arrays, {os.path.getsize(out)} bytes")
 
 
+def neighbours():
+    """Decode-step neighbours of kernels/attention.py and kernels/linear_attn.py
+    -> ref_golden_decode.npz."""
+    from qwen35_prompt_enhancer.kernels import attention, linear_attn
+    rec = {}
+
+    def bf(t):
+        return t.to(torch.bfloat16)
+
+    NQ, NKV, HD, RD = 8, 2, 256, 64
+    invf = 1.0 / (1e7 ** (torch.arange(0, RD, 2, dtype=torch.float32) / RD))
+    P = NQ * HD * 2 + 2 * NKV * HD
+    # qk_norm_rope (attention.py:70-133): sequence mode (positions pos0 + t)
+    # with bf16 and int8 caches, and batch mode (candidates at one position)
+    for i, (T, pos0, int8, batch) in enumerate([(3, 5, False, False), (3, 5, True, False), (2, 1030, True, True)]):
+        g = torch.Generator().manual_seed(1700 + i)
+        proj = bf(torch.randn(T, P + 64, generator=g) * 0.5)
+        qn = bf(torch.randn(HD, generator=g) * 0.2)
+        kn = bf(torch.randn(HD, generator=g) * 0.2)
+        seq = pos0 + T + 4
+        rows = T * seq if batch else seq
+        kvc = torch.zeros(rows, 2 * NKV * HD, dtype=torch.int8 if int8 else torch.bfloat16)
+        kvs = torch.zeros(rows, 2 * NKV) if int8 else None
+        qout = torch.empty(T, NQ * HD, dtype=torch.bfloat16)
+        attention.qk_norm_rope(proj, qn, kn, invf, qout, kvc, kvs, pos0, 1e-6, kv_int8=int8, batch=batch,
+                               kv_stride=seq * 2 * NKV * HD if batch else None,
+                               kvs_stride=seq * 2 * NKV if batch else None)
+        p = f"qk_rope_{i}_"
+        rec[p + "proj"] = bits(proj); rec[p + "qn"] = bits(qn); rec[p + "kn"] = bits(kn)
+        rec[p + "invf"] = invf.numpy(); rec[p + "cfg"] = np.array([T, pos0, int(int8), int(batch), seq])
+        rec[p + "q"] = bits(qout)
+        rec[p + "kvc"] = kvc.numpy() if int8 else bits(kvc)
+        if int8:
+            rec[p + "kvs"] = kvs.numpy()
+
+    # attn_decode (attention.py:209-267): bf16 / int8 caches, batch 1 and 3,
+    # positions that end inside and on a 32-position block
+    for i, (B, pos, int8) in enumerate([(1, 40, False), (1, 63, True), (3, 70, True)]):
+        g = torch.Generator().manual_seed(1750 + i)
+        S = pos + 9
+        q = bf(torch.randn(B, NQ * HD, generator=g) * 0.1)
+        if int8:
+            kvc = torch.randint(-127, 128, (B * S, 2 * NKV * HD), dtype=torch.int8, generator=g)
+            kvs = torch.rand(B * S, 2 * NKV, generator=g) * 0.02 + 0.001
+        else:
+            kvc = bf(torch.randn(B * S, 2 * NKV * HD, generator=g))
+            kvs = None
+        out = torch.empty(B, NQ * HD, dtype=torch.bfloat16)
+        attention.attn_decode(q if B > 1 else q[0], kvc, out if B > 1 else out[0], pos, kvs=kvs, kv_int8=int8,
+                              batch=B, nq=NQ, nkv=NKV, hd=HD)
+        p = f"attn_decode_{i}_"
+        rec[p + "q"] = bits(q); rec[p + "cfg"] = np.array([B, pos, int(int8)])
+        rec[p + "kvc"] = kvc.numpy() if int8 else bits(kvc)
+        if int8:
+            rec[p + "kvs"] = kvs.numpy()
+        rec[p + "out"] = bits(out)
+
+    # delta_decode (linear_attn.py:172-207), .dev/test_kernels.py:151-163 distributions
+    NH, DK, DV = 16, 128, 128
+    C = 2 * NH * DK + NH * DV
+    for i, B in enumerate([1, 2]):
+        g = torch.Generator().manual_seed(1800 + i)
+        qkv = bf(torch.randn(B, C, generator=g) * 0.3)
+        gg = -torch.rand(B, NH, generator=g) * 0.4
+        beta = torch.rand(B, NH, generator=g)
+        # state values on a 2^-8 grid (|s| <= 0.0625): exact in fp32 and
+        # compressible; the output state is stored for two heads only
+        state = torch.randint(-16, 17, (B * NH, DK, DV), generator=g).float() / 256.0
+        st = state.clone()
+        out = torch.empty(B, NH * DV, dtype=torch.bfloat16)
+        if B == 1:
+            linear_attn.delta_decode(qkv[0], gg[0], beta[0], st, out[0])
+        else:
+            linear_attn.delta_decode(qkv, gg, beta, st, out, batch=B)
+        p = f"delta_decode_{i}_"
+        rec[p + "qkv"] = bits(qkv); rec[p + "g"] = gg.numpy(); rec[p + "beta"] = beta.numpy()
+        rec[p + "state"] = state.numpy(); rec[p + "state_out2"] = st[:2].numpy(); rec[p + "out"] = bits(out)
+
+    # conv_silu / conv_state_update (linear_attn.py:10-83), test_kernels.py:166-184 shapes
+    for i, (T, batch, Cc) in enumerate([(23, False, 2048), (1, False, 512), (3, True, C)]):
+        g = torch.Generator().manual_seed(1850 + i)
+        x = bf(torch.randn(T, Cc, generator=g))
+        w = bf(torch.randn(Cc, 4, generator=g) * 0.1)
+        state = bf(torch.randn(3 * T if batch else 3, Cc, generator=g))
+        y = torch.empty(T, Cc, dtype=torch.bfloat16)
+        linear_attn.conv_silu(x, w, state, y, T, batch=batch)
+        st2 = state.clone()
+        linear_attn.conv_state_update(x, st2, T, batch=T if batch else 1)
+        p = f"conv_{i}_"
+        rec[p + "x"] = bits(x); rec[p + "w"] = bits(w); rec[p + "state"] = bits(state)
+        rec[p + "cfg"] = np.array([T, int(batch)]); rec[p + "y"] = bits(y); rec[p + "state_out"] = bits(st2)
+
+    out = os.path.join(HERE, "ref_golden_decode.npz")
+    np.savez_compressed(out, **rec)
+    print(f"wrote {out}: {len(rec)} arrays, {os.path.getsize(out)} bytes")
+
+
 def main():
     if len(sys.argv) not in (2, 3):
-        sys.exit("usage: make_golden.py /path/to/reference-checkout [gemm|norm|all]")
+        sys.exit("usage: make_golden.py /path/to/reference-checkout [gemm|norm|decode|all]")
     root = sys.argv[1]
     which = sys.argv[2] if len(sys.argv) == 3 else "all"
     gemm, w4, norm = import_reference(root)
     if which in ("norm", "all"):
         producers(norm)
-    if which == "norm":
+    if which in ("decode", "all"):
+        neighbours()
+    if which in ("norm", "decode"):
         return
     G = 64
     rec = {}
