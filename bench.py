@@ -569,6 +569,31 @@ def run_kernel(pkg, dev, name, launches):
                       "fault_word": pkg._lib.load().qlin_device_fault(0)}), flush=True)
 
 
+def decode_step_detail(pkg, dev, peak_gbs, B=4, pos=1024, reps=20, repeats=5):
+    """Config 4: one batched decode step of a random-init Qwen3.5-2B-shaped
+    hybrid stack (24 layers, 3:1 linear/full attention, W8 per-channel linears,
+    int8 KV with fp32 scales), B candidates at position `pos` with seeded
+    random KV / delta / conv state, on this package's kernels only, captured
+    as one CUDA graph with a device-side position.  tokens/s = B / step time;
+    % of HBM over the step's algorithmic bytes (weights + delta state r/w + KV
+    read)."""
+    st = pkg.decode_step.HybridStack(pkg.decode_step.QWEN35_2B, dev, B, pos + 16, kv_int8=True, seed=11)
+    ids = torch.randint(0, st.V, (B,), device=dev)
+    pos_t = torch.tensor([pos], dtype=torch.int32, device=dev)
+    graph = st.capture(ids, pos_t, warmup=2)
+    for _ in range(3):
+        graph.replay()
+    us = _graph_us(graph, reps, repeats, None, dev)
+    nbytes = st.step_bytes(pos)
+    del graph
+    return {"workload": f"config 4: Qwen3.5-2B-shaped hybrid stack decode step, B={B} candidates at position {pos}, "
+                        "int8 KV, all linears W8 per-channel, random init; CUDA graph of the whole step",
+            "step_us": us, "tokens_per_s": B / us * 1e6, "bytes_per_step": nbytes,
+            "tbs": nbytes / us / 1e6, "frac_of_hbm": nbytes / us / 1e3 / peak_gbs,
+            "launches_per_step": st.launches, "weight_bytes": st.weight_bytes(),
+            "timing": f"median of {repeats} samples of {reps} graph replays"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -735,6 +760,7 @@ def main():
     # ---- config 5 (all ranks, collectives) and config 3 (rank-local)
     tp = tp_detail(pkg, dev, world, rank, pg)
     prefill = prefill_detail(pkg, dev, gen)
+    decode = decode_step_detail(pkg, dev, peak)
 
     cpu = None
     if rank == 0 and world == 1:
@@ -776,6 +802,7 @@ def main():
                 "gate_up_w4_m4_us": gu_launch_s * 1e6,
                 "tp_layer": tp,
                 "prefill": prefill,
+                "decode_step": decode,
                 "fault_word": pkg._lib.load().qlin_device_fault(0),
             },
         }

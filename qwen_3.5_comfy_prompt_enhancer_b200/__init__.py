@@ -8,7 +8,7 @@ The directory name contains a dot, so import it through
 ``__graft_entry__.load_package()`` (registers it as ``qwen35_b200``) or any
 other importlib alias; all imports inside the package are relative.
 """
-from . import _lib, tp  # noqa: F401
+from . import _lib, decode_step, tp  # noqa: F401
 from .kernels.attention import attn_decode, qk_norm_rope  # noqa: F401
 from .kernels.common import GROUP  # noqa: F401
 from .kernels.linear_attn import conv_silu, conv_state_update, delta_decode  # noqa: F401
