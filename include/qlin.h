@@ -246,6 +246,25 @@ int qlin_conv_silu(const void* x, int64_t ldx, const void* w, int64_t ks, const 
 int qlin_conv_state_update(const void* x, int64_t ldx, void* state, int64_t T, int64_t C, int64_t ks,
                            int64_t batch, void* stream);
 
+/* ---- Prefill neighbours ---- */
+
+/* kernels/attention.py:136-206 (attn_prefill): causal attention of T query
+ * rows q [T, nq*hd] (bf16, already scaled) at positions pos0 .. pos0 + T - 1
+ * over cache rows 0 .. pos0 + t of kvc [rows, 2*nkv*hd] (bf16, or int8 with
+ * kvs [rows, 2*nkv], dequantised to bf16(code * scale) as the reference
+ * does); bf16 products, fp32 accumulation and softmax, P rounded to bf16 for
+ * the P V product -> bf16 out [T, nq*hd].  hd in {128, 256}. */
+int qlin_attn_prefill(const void* q, const void* kvc, const float* kvs, void* out, int64_t T, int64_t pos0,
+                      int64_t nq, int64_t nkv, int64_t hd, int kv_int8, void* stream);
+
+/* kernels/linear_attn.py:86-169 (delta_prefill): chunked (32 tokens) gated
+ * delta rule over T tokens of qkv bf16 [T, ldq] (q [nh*dk], k [nh*dk],
+ * v [nh*dv]), g / beta fp32 [T, nh], state fp32 [nh, dk, dv] updated in
+ * place; per chunk the WY form with the Neumann-product inverse of the
+ * reference, in fp32 -> bf16 out [T, nh*dv].  dk = 128, dv % 32 == 0. */
+int qlin_delta_prefill(const void* qkv, int64_t ldq, const float* g, const float* beta, float* state, void* out,
+                       int64_t T, int64_t nh, int64_t dk, int64_t dv, void* stream);
+
 /* ---- Multi-GPU (column-split layer): NVLink peer memory through CUDA IPC ----
  * Not part of the reference's interface (it has no multi-GPU path); used by
  * the package's tp.py for its all-gathers. */

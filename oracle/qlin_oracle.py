@@ -643,6 +643,139 @@ def conv_state_update(x_bits, state_bits, T, batch=1):
 
 
 # ----------------------------------------------------------------------------
+# f4: prefill neighbours  (kernels/attention.py:136-206, kernels/linear_attn.py:86-169)
+# ----------------------------------------------------------------------------
+# ``tl.dot`` is float32 ``np.matmul`` under the CPU interpreter; the
+# restatement multiplies blocks of the reference's own shapes the same way.
+
+def _mm(a, b):
+    return np.matmul(np.asarray(a, np.float32), np.asarray(b, np.float32), dtype=np.float32)
+
+
+def attn_prefill(q_bits, kvc, T, pos0=0, kvs=None, nq=8, nkv=2, hd=256, block_m=32, block_n=32, mode="rne"):
+    """attention.py:136-206: causal attention of T query rows (positions
+    pos0 + t) over cache rows 0 .. pos0 + t.  Per (head, block of block_m
+    queries), key blocks of block_n: s = q k^T (bf16 operands; an int8 cache
+    is dequantised to bf16(code * scale)), online softmax, acc += bf16(p) v.
+    q [T, nq*hd] bf16 bits; kvc [rows, 2*nkv*hd] (bf16 bits or int8, kvs
+    fp32).  Returns bf16 bits [T, nq*hd]."""
+    q = bf16_bits_to_f32(q_bits)
+    out = np.zeros((T, nq * hd), dtype=np.float32)
+    sns = 2 * nkv
+    for head in range(nq):
+        kvh = head // (nq // nkv)
+        for mb in range(0, T, block_m):
+            rows = np.arange(mb, mb + block_m)
+            qb = np.zeros((block_m, hd), dtype=np.float32)
+            live = rows < T
+            qb[live] = q[rows[live], head * hd:(head + 1) * hd]
+            m_i = np.full(block_m, -np.inf, dtype=np.float32)
+            l_i = np.zeros(block_m, dtype=np.float32)
+            acc = np.zeros((block_m, hd), dtype=np.float32)
+            total = pos0 + min(mb + block_m, T)
+            for n0 in range(0, total, block_n):
+                n = np.arange(n0, n0 + block_n)
+                nmask = n < total
+                k = np.zeros((block_n, hd), dtype=np.float32)
+                v = np.zeros((block_n, hd), dtype=np.float32)
+                nv = n[nmask]
+                if kvs is None:
+                    k[nmask] = bf16_bits_to_f32(kvc[nv, kvh * hd:(kvh + 1) * hd])
+                    v[nmask] = bf16_bits_to_f32(kvc[nv, (nkv + kvh) * hd:(nkv + kvh + 1) * hd])
+                else:
+                    k[nmask] = (kvc[nv, kvh * hd:(kvh + 1) * hd].astype(np.float32) * kvs[nv, kvh][:, None])
+                    v[nmask] = (kvc[nv, (nkv + kvh) * hd:(nkv + kvh + 1) * hd].astype(np.float32)
+                                * kvs[nv, nkv + kvh][:, None])
+                    k, v = bf16_round(k, mode), bf16_round(v, mode)
+                sc = _mm(qb, k.T)
+                causal = ((pos0 + rows)[:, None] >= n[None, :]) & nmask[None, :]
+                sc = np.where(causal, sc, np.float32(-np.inf)).astype(np.float32)
+                m_new = np.maximum(m_i, sc.max(axis=1)).astype(np.float32)
+                with np.errstate(invalid="ignore"):
+                    p = np.exp((sc - m_new[:, None]).astype(np.float32)).astype(np.float32)
+                    alpha = np.exp((m_i - m_new).astype(np.float32)).astype(np.float32)
+                l_i = ((l_i * alpha).astype(np.float32) + np.sum(p, axis=1, dtype=np.float32)).astype(np.float32)
+                acc = (acc * alpha[:, None]).astype(np.float32)
+                acc = (acc + _mm(bf16_round(p, mode), v)).astype(np.float32)
+                m_i = m_new
+            l_safe = np.where(l_i > 0, l_i, np.float32(1.0)).astype(np.float32)
+            res = (acc / l_safe[:, None]).astype(np.float32)
+            out[rows[live], head * hd:(head + 1) * hd] = res[live]
+    return f32_to_bf16_bits(out, mode)
+
+
+def _ut_inverse(A):
+    """linear_attn.py:86-95: (I - A)^-1 for strictly lower A by the Neumann
+    product: Tm = I + A, P = A; five times P = P P, Tm = Tm + Tm P."""
+    C = A.shape[0]
+    eye = np.eye(C, dtype=np.float32)
+    Tm = (eye + A).astype(np.float32)
+    P = A
+    for _ in range(5):
+        P = _mm(P, P)
+        Tm = (Tm + _mm(Tm, P)).astype(np.float32)
+    return Tm
+
+
+def delta_prefill(qkv_bits, g, beta, state, T, nh=16, dk=128, dv=128, vs=32, chunk=32, mode="rne"):
+    """linear_attn.py:98-169: chunked gated delta rule over T tokens, per head
+    and per vs-column slab of the state (grid (NH, DV/VS)), chunks of 32 in
+    order.  qkv [T, 2 nh dk + nh dv] bf16 bits, g / beta [T, nh] fp32, state
+    [nh, dk, dv] fp32 (updated in place).  Returns out bf16 bits [T, nh*dv]."""
+    x = bf16_bits_to_f32(qkv_bits)
+    g = np.asarray(g, np.float32)
+    beta = np.asarray(beta, np.float32)
+    out = np.zeros((T, nh * dv), dtype=np.float32)
+    inv = np.float32(1.0) / np.sqrt(np.float32(dk))
+    c = np.arange(chunk)
+    for h in range(nh):
+        for slab in range(dv // vs):
+            cols = slice(slab * vs, (slab + 1) * vs)
+            S = state[h][:, cols].astype(np.float32).copy()
+            for c0 in range(0, T, chunk):
+                t = c0 + c
+                live = t < T
+                tl_ = t[live]
+                q = np.zeros((chunk, dk), np.float32)
+                k = np.zeros((chunk, dk), np.float32)
+                v = np.zeros((chunk, vs), np.float32)
+                q[live] = x[tl_, h * dk:(h + 1) * dk]
+                k[live] = x[tl_, nh * dk + h * dk:nh * dk + (h + 1) * dk]
+                v[live] = x[tl_, 2 * nh * dk + h * dv:2 * nh * dk + (h + 1) * dv][:, cols]
+                bt = np.zeros(chunk, np.float32)
+                gg = np.zeros(chunk, np.float32)
+                bt[live] = beta[tl_, h]
+                gg[live] = g[tl_, h]
+                sq = np.sum((q * q).astype(np.float32), axis=1, keepdims=True, dtype=np.float32)
+                sk = np.sum((k * k).astype(np.float32), axis=1, keepdims=True, dtype=np.float32)
+                qn = ((q * _rsqrt((sq + np.float32(1e-6)).astype(np.float32))).astype(np.float32) * inv).astype(
+                    np.float32)
+                kn = (k * _rsqrt((sk + np.float32(1e-6)).astype(np.float32))).astype(np.float32)
+                gc = np.cumsum(gg, dtype=np.float32)
+                with np.errstate(over="ignore"):
+                    decay = np.where(c[:, None] >= c[None, :],
+                                     np.exp((gc[:, None] - gc[None, :]).astype(np.float32)), np.float32(0.0))
+                decay = decay.astype(np.float32)
+                kb = (kn * bt[:, None]).astype(np.float32)
+                A = (-_mm(kb, kn.T) * decay).astype(np.float32)
+                A = np.where(c[:, None] > c[None, :], A, np.float32(0.0)).astype(np.float32)
+                Tm = _ut_inverse(A)
+                vb = (v * bt[:, None]).astype(np.float32)
+                value = _mm(Tm, vb)
+                eg = np.exp(gc).astype(np.float32)
+                kcum = _mm(Tm, (kb * eg[:, None]).astype(np.float32))
+                v_new = (value - _mm(kcum, S)).astype(np.float32)
+                o = _mm((qn * eg[:, None]).astype(np.float32), S)
+                o = (o + _mm((_mm(qn, kn.T) * decay).astype(np.float32), v_new)).astype(np.float32)
+                g_last = np.float32(np.min(gc))
+                w = (kn * np.exp((g_last - gc).astype(np.float32))[:, None]).astype(np.float32)
+                S = ((S * np.float32(np.exp(g_last))).astype(np.float32) + _mm(w.T, v_new)).astype(np.float32)
+                out[tl_, h * dv + slab * vs:h * dv + (slab + 1) * vs] = o[live]
+            state[h][:, cols] = S
+    return f32_to_bf16_bits(out, mode)
+
+
+# ----------------------------------------------------------------------------
 # CPU baseline: the reference's own dequant-then-matmul (.dev/test_kernels.py:40-41)
 # ----------------------------------------------------------------------------
 

@@ -9,9 +9,9 @@ The directory name contains a dot, so import it through
 other importlib alias; all imports inside the package are relative.
 """
 from . import _lib, decode_step, tp  # noqa: F401
-from .kernels.attention import attn_decode, qk_norm_rope  # noqa: F401
+from .kernels.attention import attn_decode, attn_prefill, qk_norm_rope  # noqa: F401
 from .kernels.common import GROUP  # noqa: F401
-from .kernels.linear_attn import conv_silu, conv_state_update, delta_decode  # noqa: F401
+from .kernels.linear_attn import conv_silu, conv_state_update, delta_decode, delta_prefill  # noqa: F401
 from .kernels.gemm import gemm_i8, mlp_gate_up, mlp_gate_up_quant, proj3  # noqa: F401
 from .kernels.norm import (gate_mul_quant, gate_proj, norm_gated, norm_gated_quant, quant_row,  # noqa: F401
                            rmsnorm_quant, silu_mul_quant)
@@ -20,4 +20,4 @@ from .kernels.w4 import gemm_w4, mlp_gate_up_quant_w4, proj3_w4  # noqa: F401
 __all__ = ["GROUP", "gemm_i8", "mlp_gate_up", "mlp_gate_up_quant", "proj3", "gemm_w4",
            "proj3_w4", "mlp_gate_up_quant_w4", "quant_row", "rmsnorm_quant", "norm_gated_quant", "norm_gated",
            "gate_mul_quant", "silu_mul_quant", "gate_proj", "qk_norm_rope", "attn_decode", "conv_silu",
-           "conv_state_update", "delta_decode"]
+           "conv_state_update", "delta_decode", "attn_prefill", "delta_prefill"]

@@ -18,6 +18,8 @@
 #include "peer.cuh"
 #include "producers.cuh"
 #include "decode.cuh"
+#include "prefill_attn.cuh"
+#include "prefill_delta.cuh"
 #include "tcgemm.cuh"
 #include "tcgemm_w4.cuh"
 #include "tcgemv.cuh"
@@ -1970,6 +1972,74 @@ int qlin_conv_state_update(const void* x, int64_t ldx, void* state, int64_t T, i
   return dec_launch(reinterpret_cast<const void*>(conv_state_update_kernel),
                     dim3(cb, static_cast<unsigned>(batch > 1 ? batch : 1)), dim3(kDecThreads), 0, 1, args,
                     static_cast<cudaStream_t>(stream));
+}
+
+
+int qlin_attn_prefill(const void* q, const void* kvc, const float* kvs, void* out, int64_t T, int64_t pos0,
+                      int64_t nq, int64_t nkv, int64_t hd, int kv_int8, void* stream) {
+  if (T < 0 || pos0 < 0 || nq <= 0 || nkv <= 0 || nq % nkv != 0)
+    return fail(QLIN_ERR_INVALID_ARGUMENT, "attn_prefill: bad size");
+  if (!(hd == 128 || hd == 256)) return fail(QLIN_ERR_SHAPE, "attn_prefill: head dim %lld (128 or 256)", (long long)hd);
+  if (T == 0) return QLIN_OK;
+  if (nq > 65535 || (T + kPaRows - 1) / kPaRows > 2147483647ll || pos0 + T > 2147483647ll)
+    return fail(QLIN_ERR_SHAPE, "attn_prefill: too large");
+  if (!q || !kvc || !out || (kv_int8 && !kvs)) return fail(QLIN_ERR_INVALID_ARGUMENT, "attn_prefill: null pointer");
+  if (!aligned(q, 16) || !aligned(kvc, 16) || !aligned(out, 4) || (kvs && !aligned(kvs, 4)))
+    return fail(QLIN_ERR_ALIGNMENT, "attn_prefill: q and the cache need 16-byte alignment");
+  DevInfo di;
+  if (int r = launch_info(&di)) return r;
+  AttnPrefillArgs a;
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.kvc = kvc;
+  a.kvs = kvs;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.T = static_cast<int>(T);
+  a.pos0 = static_cast<int>(pos0);
+  a.nq = static_cast<int>(nq);
+  a.nkv = static_cast<int>(nkv);
+  const void* kern = hd == 256 ? (kv_int8 ? reinterpret_cast<const void*>(attn_prefill_kernel<256, true>)
+                                          : reinterpret_cast<const void*>(attn_prefill_kernel<256, false>))
+                               : (kv_int8 ? reinterpret_cast<const void*>(attn_prefill_kernel<128, true>)
+                                          : reinterpret_cast<const void*>(attn_prefill_kernel<128, false>));
+  const size_t smem = attn_prefill_smem(static_cast<int>(hd));
+  static std::atomic<unsigned long long> done[4];  // one opt-in per kernel instance and device
+  const int inst = (hd == 256 ? 2 : 0) + (kv_int8 ? 1 : 0);
+  if (int r = smem_optin(kern, smem, done[inst])) return r;
+  void* args[] = {&a};
+  return dec_launch(kern, dim3(static_cast<unsigned>((T + kPaRows - 1) / kPaRows), static_cast<unsigned>(nq)),
+                    dim3(kPaThreads), smem, 1, args, static_cast<cudaStream_t>(stream));
+}
+
+int qlin_delta_prefill(const void* qkv, int64_t ldq, const float* g, const float* beta, float* state, void* out,
+                       int64_t T, int64_t nh, int64_t dk, int64_t dv, void* stream) {
+  if (T < 0 || nh <= 0) return fail(QLIN_ERR_INVALID_ARGUMENT, "delta_prefill: bad size");
+  if (dk != kDpDK || dv % kDpVS != 0 || dv <= 0)
+    return fail(QLIN_ERR_SHAPE, "delta_prefill: key dim must be 128 and the value dim a multiple of 32");
+  if (T == 0) return QLIN_OK;
+  if (T > 2147483647ll || nh > 65535) return fail(QLIN_ERR_SHAPE, "delta_prefill: too large");
+  if (!qkv || !g || !beta || !state || !out) return fail(QLIN_ERR_INVALID_ARGUMENT, "delta_prefill: null pointer");
+  if (ldq < (2 * dk + dv) * nh) return fail(QLIN_ERR_SHAPE, "delta_prefill: qkv row stride too small");
+  if (!aligned(qkv, 16) || ldq % 8 != 0 || !aligned(state, 4) || !aligned(out, 2) || !aligned(g, 4) ||
+      !aligned(beta, 4))
+    return fail(QLIN_ERR_ALIGNMENT, "delta_prefill: qkv needs 16-byte aligned rows");
+  DevInfo di;
+  if (int r = launch_info(&di)) return r;
+  DeltaPrefillArgs a;
+  a.qkv = static_cast<const __nv_bfloat16*>(qkv);
+  a.ldq = ldq;
+  a.g = g;
+  a.beta = beta;
+  a.state = state;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.T = static_cast<int>(T);
+  a.nh = static_cast<int>(nh);
+  a.dv = static_cast<int>(dv);
+  static std::atomic<unsigned long long> done{0};
+  const void* kern = reinterpret_cast<const void*>(delta_prefill_kernel);
+  if (int r = smem_optin(kern, sizeof(DpSmem), done)) return r;
+  void* args[] = {&a};
+  return dec_launch(kern, dim3(static_cast<unsigned>(nh), static_cast<unsigned>(dv / kDpVS)), dim3(kDpThreads),
+                    sizeof(DpSmem), 1, args, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

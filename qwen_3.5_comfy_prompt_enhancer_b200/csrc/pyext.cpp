@@ -519,6 +519,46 @@ int conv_state_update(const Tensor& x, const Tensor& state, int64_t T, int64_t b
   });
 }
 
+int attn_prefill(const Tensor& q, const Tensor& kvc, const Tensor& out, int64_t T, int64_t pos0, const OptT& kvs,
+                 bool kv_int8, int64_t nq, int64_t nkv, int64_t hd) {
+  Call c;
+  c.need(q, "q", at::kBFloat16, 2);
+  c.need(out, "out", at::kBFloat16, 2);
+  c.need(kvc, "kvc", kv_int8 ? at::kChar : at::kBFloat16, 2);
+  if (kv_int8) {
+    if (!kvs) throw py::value_error("kv_int8=True requires the kvs scales tensor");
+    c.need(*kvs, "kvs", at::kFloat, 2);
+  }
+  if (q.size(0) < T || q.size(1) != nq * hd || out.size(0) < T || out.size(1) != nq * hd)
+    throw py::value_error("q and out must be [>= T, nq * hd]");
+  if (kvc.size(1) != 2 * nkv * hd || kvc.size(0) < pos0 + T)
+    throw py::value_error("kvc must be [>= pos0 + T, 2 * nkv * hd]");
+  return c.launch([&](void* st) {
+    return qlin_attn_prefill(q.data_ptr(), kvc.data_ptr(), kv_int8 ? static_cast<const float*>(kvs->data_ptr()) : nullptr,
+                             out.data_ptr(), T, pos0, nq, nkv, hd, kv_int8 ? 1 : 0, st);
+  });
+}
+
+int delta_prefill(const Tensor& qkv, const Tensor& g, const Tensor& beta, const Tensor& state, const Tensor& out,
+                  int64_t T) {
+  Call c;
+  c.need_rows(qkv, "qkv", at::kBFloat16);
+  c.need(g, "g", at::kFloat, 2);
+  c.need(beta, "beta", at::kFloat, 2);
+  c.need(state, "state", at::kFloat, 3);
+  c.need(out, "out", at::kBFloat16, 2);
+  const int64_t nh = state.size(0), dk = state.size(1), dv = state.size(2);
+  if (g.size(0) < T || g.size(1) != nh || beta.size(0) < T || beta.size(1) != nh)
+    throw py::value_error("g / beta must be [>= T, nh]");
+  if (out.size(0) < T || out.size(1) != nh * dv || qkv.size(0) < T || qkv.size(1) < (2 * dk + dv) * nh)
+    throw py::value_error("qkv must be [>= T, (2 dk + dv) nh] and out [>= T, nh dv]");
+  return c.launch([&](void* st) {
+    return qlin_delta_prefill(qkv.data_ptr(), qkv.stride(0), static_cast<const float*>(g.data_ptr()),
+                              static_cast<const float*>(beta.data_ptr()), static_cast<float*>(state.data_ptr()),
+                              out.data_ptr(), T, nh, dk, dv, st);
+  });
+}
+
 }  // namespace
 
 PYBIND11_MODULE(_qlin_ext, m) {
@@ -541,4 +581,6 @@ PYBIND11_MODULE(_qlin_ext, m) {
   m.def("delta_decode", &delta_decode);
   m.def("conv_silu", &conv_silu);
   m.def("conv_state_update", &conv_state_update);
+  m.def("attn_prefill", &attn_prefill);
+  m.def("delta_prefill", &delta_prefill);
 }

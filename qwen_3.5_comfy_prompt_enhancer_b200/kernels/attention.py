@@ -50,3 +50,17 @@ def attn_decode(q, kvc, out, pos, kvs=None, kv_int8=False, batch=1, block_n=32,
     if rc:
         raise _lib.QlinError("qlin_attn_decode", rc)
     return out
+
+
+def attn_prefill(q, kvc, out, T, pos0=0, kvs=None, kv_int8=False, block_m=32,
+                 block_n=32, nq=8, nkv=2, hd=256):
+    """Causal prefill over the KV cache; reads the int8 cache when kv_int8
+    (kernels/attention.py:136-206).  Tile keywords are accepted and ignored.
+    Returns ``out``."""
+    if kv_int8 and kvs is None:
+        raise ValueError("kv_int8=True requires the kvs scales tensor")
+    rc = _lib.ext().attn_prefill(q, kvc, out, int(T), int(pos0), kvs if kv_int8 else None, bool(kv_int8), int(nq),
+                                 int(nkv), int(hd))
+    if rc:
+        raise _lib.QlinError("qlin_attn_prefill", rc)
+    return out

@@ -31,3 +31,14 @@ def delta_decode(qkv, g, beta, state, out, vs=32, batch=1):
     if rc:
         raise _lib.QlinError("qlin_delta_decode", rc)
     return out
+
+
+def delta_prefill(qkv, g, beta, state, out, T, vs=32, chunk=32):
+    """Chunked (32-token) gated delta rule over T tokens (kernels/linear_attn.py:98-169);
+    ``state`` [NH, DK, DV] fp32 is updated in place.  ``vs`` / ``chunk`` are
+    accepted and ignored (the kernel's own tiling; the chunk is 32).
+    Returns ``out``."""
+    rc = _lib.ext().delta_prefill(qkv, g, beta, state, out, int(T))
+    if rc:
+        raise _lib.QlinError("qlin_delta_prefill", rc)
+    return out

@@ -141,10 +141,35 @@ def producers(norm):
     print(f"wrote {out}: {len(rec)} arrays, {os.path.getsize(out)} bytes")
 
 
+def _widen_bf16_dot_operands():
+    """Triton 3.6's CPU interpreter stores bf16 tensors as their uint16 bit
+    patterns and its ``tl.dot`` multiplies that storage as integers, so any
+    dot with bf16 operands (attn_prefill's q k^T and p v) comes out as
+    garbage.  Widen such operands to fp32 first -- exact for bf16 -- which is
+    what a bf16 MMA with fp32 accumulation computes.  The reference's code is
+    untouched; only the interpreter's dot is corrected."""
+    import triton.language as tl
+    from triton.runtime import interpreter as interp
+    orig = interp.InterpreterBuilder.create_dot
+    if getattr(orig, "_widened", False):
+        return
+
+    def widen(h):
+        if h.dtype.scalar == tl.bfloat16:
+            return interp.TensorHandle((h.data.astype(np.uint32) << 16).view(np.float32), tl.float32)
+        return h
+
+    def create_dot(self, a, b, d, input_precision, max_num_imprecise_acc):
+        return orig(self, widen(a), widen(b), d, input_precision, max_num_imprecise_acc)
+    create_dot._widened = True
+    interp.InterpreterBuilder.create_dot = create_dot
+
+
 def neighbours():
     """Decode-step neighbours of kernels/attention.py and kernels/linear_attn.py
     -> ref_golden_decode.npz."""
     from qwen35_prompt_enhancer.kernels import attention, linear_attn
+    _widen_bf16_dot_operands()
     rec = {}
 
     def bf(t):
@@ -232,6 +257,42 @@ def neighbours():
         p = f"conv_{i}_"
         rec[p + "x"] = bits(x); rec[p + "w"] = bits(w); rec[p + "state"] = bits(state)
         rec[p + "cfg"] = np.array([T, int(batch)]); rec[p + "y"] = bits(y); rec[p + "state_out"] = bits(st2)
+
+    # attn_prefill (attention.py:136-206): one chunk from position 0 and a
+    # later chunk over an earlier one, bf16 and int8 caches
+    for i, (T, pos0, int8) in enumerate([(40, 0, False), (19, 37, True)]):
+        g = torch.Generator().manual_seed(1900 + i)
+        q = bf(torch.randn(T, NQ * HD, generator=g) * 0.1)
+        S = pos0 + T + 5
+        if int8:
+            kvc = torch.randint(-127, 128, (S, 2 * NKV * HD), dtype=torch.int8, generator=g)
+            kvs = torch.rand(S, 2 * NKV, generator=g) * 0.02 + 0.001
+        else:
+            kvc = bf(torch.randn(S, 2 * NKV * HD, generator=g))
+            kvs = None
+        out = torch.empty(T, NQ * HD, dtype=torch.bfloat16)
+        attention.attn_prefill(q, kvc, out, T, pos0, kvs=kvs, kv_int8=int8, nq=NQ, nkv=NKV, hd=HD)
+        p = f"attn_prefill_{i}_"
+        rec[p + "q"] = bits(q); rec[p + "cfg"] = np.array([T, pos0, int(int8)])
+        rec[p + "kvc"] = kvc.numpy() if int8 else bits(kvc)
+        if int8:
+            rec[p + "kvs"] = kvs.numpy()
+        rec[p + "out"] = bits(out)
+
+    # delta_prefill (linear_attn.py:98-169), test_kernels.py:151-163 distributions:
+    # a partial chunk and a run over two chunks plus a partial one
+    for i, T in enumerate([5, 70]):
+        g = torch.Generator().manual_seed(1950 + i)
+        qkv = bf(torch.randn(T, C, generator=g) * 0.3)
+        gg = -torch.rand(T, NH, generator=g) * 0.4
+        beta = torch.rand(T, NH, generator=g)
+        state = torch.randint(-16, 17, (NH, DK, DV), generator=g).float() / 256.0
+        st = state.clone()
+        out = torch.empty(T, NH * DV, dtype=torch.bfloat16)
+        linear_attn.delta_prefill(qkv, gg, beta, st, out, T)
+        p = f"delta_prefill_{i}_"
+        rec[p + "qkv"] = bits(qkv); rec[p + "g"] = gg.numpy(); rec[p + "beta"] = beta.numpy()
+        rec[p + "state"] = state.numpy(); rec[p + "state_out2"] = st[:2].numpy(); rec[p + "out"] = bits(out)
 
     out = os.path.join(HERE, "ref_golden_decode.npz")
     np.savez_compressed(out, **rec)

@@ -15,7 +15,7 @@ import pytest
 import torch
 
 from oracle import qlin_oracle as O
-from qlin_testutil import bits
+from qlin_testutil import assert_bf16_close, bits
 
 pytestmark = pytest.mark.gpu
 
@@ -96,7 +96,9 @@ def test_decode_step_matches_oracle_composition(pkg, dev):
     got_kv = st.kv.cpu().numpy()[:, :, pos].astype(np.float32) * np.repeat(st.kvs.cpu().numpy()[:, :, pos], 256, -1)
     ref_kv = kv[:, :, pos].astype(np.float32) * np.repeat(kvs[:, :, pos], 256, -1)
     assert rel_l2(got_kv, ref_kv) < 1e-2
-    np.testing.assert_array_equal(bits(st.cstate), cstate)  # the conv window update is a copy
+    # the conv window copies this step's projection rows, which are within the
+    # bf16 bar of the oracle's (the copy itself is bit-exact: test_gpu_decode.py)
+    assert_bf16_close(bits(st.cstate).reshape(-1, st.conv_dim), cstate.reshape(-1, st.conv_dim), "conv window")
 
 
 def test_decode_step_graph_replay_equals_eager(pkg, dev):

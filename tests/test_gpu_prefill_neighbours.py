@@ -1,0 +1,117 @@
+"""Prefill neighbours (kernels/attention.py:136-206 attn_prefill,
+kernels/linear_attn.py:86-169 delta_prefill) on the CUDA path against the
+CPU oracle and the reference's own outputs.
+
+Parity: bf16 outputs |d| <= 1e-3 + 1e-2 |ref| elementwise (products summed in
+another order; attention with 64-key instead of 32-key softmax blocks);
+the fp32 delta-rule state |d| <= 1e-5 + 1e-4 |ref| (a chunk's chain of fp32
+products in another summation order).
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import qlin_oracle as O
+from qlin_testutil import assert_bf16_close, bits, from_bits
+
+pytestmark = pytest.mark.gpu
+
+GOLD = np.load(os.path.join(os.path.dirname(__file__), "golden", "ref_golden_decode.npz"))
+NQ, NKV, HD = 8, 2, 256
+NH, DK, DV = 16, 128, 128
+CONV = 2 * NH * DK + NH * DV
+
+
+def rand_bf16(g, shape, scale=1.0):
+    return (torch.randn(*shape, generator=g) * scale).to(torch.bfloat16)
+
+
+def _state_close(got, ref, what):
+    err = np.abs(got - ref)
+    bad = err > 1e-5 + 1e-4 * np.abs(ref)
+    assert not bad.any(), f"{what}: {int(bad.sum())} state values outside the bar, max err {err.max()}"
+
+
+@pytest.mark.parametrize("T,pos0,int8", [(1, 0, False), (40, 0, False), (64, 0, True), (130, 0, True),
+                                         (19, 37, True), (100, 300, False)])
+def test_attn_prefill_vs_oracle(pkg, dev, T, pos0, int8):
+    g = torch.Generator().manual_seed(2400 + T + pos0)
+    q = rand_bf16(g, (T, NQ * HD), 0.1)
+    S = pos0 + T + 3
+    if int8:
+        kvc = torch.randint(-127, 128, (S, 2 * NKV * HD), dtype=torch.int8, generator=g)
+        kvs = torch.rand(S, 2 * NKV, generator=g) * 0.02 + 0.001
+    else:
+        kvc, kvs = rand_bf16(g, (S, 2 * NKV * HD)), None
+    out = torch.empty(T, NQ * HD, dtype=torch.bfloat16, device=dev)
+    r = pkg.attn_prefill(q.to(dev), kvc.to(dev), out, T, pos0, kvs=None if kvs is None else kvs.to(dev),
+                         kv_int8=int8, nq=NQ, nkv=NKV, hd=HD)
+    assert r is out
+    ref = O.attn_prefill(bits(q), kvc.numpy() if int8 else bits(kvc), T, pos0,
+                         None if kvs is None else kvs.numpy())
+    assert_bf16_close(bits(out), ref, f"attn_prefill T={T} pos0={pos0}")
+
+
+@pytest.mark.parametrize("i", ["0", "1"])
+def test_attn_prefill_vs_reference_golden(pkg, dev, i):
+    p = f"attn_prefill_{i}_"
+    T, pos0, int8 = (int(v) for v in GOLD[p + "cfg"])
+    kvc = torch.from_numpy(GOLD[p + "kvc"]) if int8 else from_bits(GOLD[p + "kvc"])
+    out = torch.empty(T, NQ * HD, dtype=torch.bfloat16, device=dev)
+    pkg.attn_prefill(from_bits(GOLD[p + "q"]).to(dev), kvc.to(dev), out, T, pos0,
+                     kvs=torch.from_numpy(GOLD[p + "kvs"]).to(dev) if int8 else None, kv_int8=bool(int8))
+    assert_bf16_close(bits(out), GOLD[p + "out"], f"golden attn_prefill {i}")
+
+
+@pytest.mark.parametrize("T", [1, 5, 32, 64, 70, 130])
+def test_delta_prefill_vs_oracle(pkg, dev, T):
+    g = torch.Generator().manual_seed(2500 + T)
+    qkv = rand_bf16(g, (T, CONV + 256), 0.3)     # rows of a wider buffer
+    gg = -torch.rand(T, NH, generator=g) * 0.4
+    beta = torch.rand(T, NH, generator=g)
+    state = torch.randn(NH, DK, DV, generator=g) * 0.05
+    st = state.to(dev)
+    out = torch.empty(T, NH * DV, dtype=torch.bfloat16, device=dev)
+    pkg.delta_prefill(qkv.to(dev)[:, :CONV], gg.to(dev), beta.to(dev), st, out, T)
+    ref_state = state.numpy().copy()
+    ref = O.delta_prefill(bits(qkv[:, :CONV]), gg.numpy(), beta.numpy(), ref_state, T)
+    assert_bf16_close(bits(out), ref, f"delta_prefill T={T}")
+    _state_close(st.cpu().numpy(), ref_state, f"delta_prefill state T={T}")
+
+
+@pytest.mark.parametrize("i", ["0", "1"])
+def test_delta_prefill_vs_reference_golden(pkg, dev, i):
+    p = f"delta_prefill_{i}_"
+    qkv = from_bits(GOLD[p + "qkv"]).to(dev)
+    T = qkv.shape[0]
+    st = torch.from_numpy(GOLD[p + "state"].copy()).to(dev)
+    out = torch.empty(T, NH * DV, dtype=torch.bfloat16, device=dev)
+    pkg.delta_prefill(qkv, torch.from_numpy(GOLD[p + "g"]).to(dev), torch.from_numpy(GOLD[p + "beta"]).to(dev), st,
+                      out, T)
+    assert_bf16_close(bits(out), GOLD[p + "out"], f"golden delta_prefill {i}")
+    _state_close(st.cpu().numpy()[:2], GOLD[p + "state_out2"], f"golden delta_prefill state {i}")
+
+
+def test_prefill_then_decode_continues_the_state(pkg, dev):
+    """delta_prefill over T tokens then delta_decode of token T+1 equals
+    delta_prefill over T + 1 tokens (the engine's prefill -> decode hand-off)."""
+    g = torch.Generator().manual_seed(2600)
+    T = 45
+    qkv = rand_bf16(g, (T + 1, CONV), 0.3).to(dev)
+    gg = (-torch.rand(T + 1, NH, generator=g) * 0.4).to(dev)
+    beta = torch.rand(T + 1, NH, generator=g).to(dev)
+    state = (torch.randn(NH, DK, DV, generator=g) * 0.05).to(dev)
+    s1, s2 = state.clone(), state.clone()
+    o1 = torch.empty(T + 1, NH * DV, dtype=torch.bfloat16, device=dev)
+    o2 = torch.empty(T + 1, NH * DV, dtype=torch.bfloat16, device=dev)
+    pkg.delta_prefill(qkv, gg, beta, s1, o1, T + 1)
+    pkg.delta_prefill(qkv[:T], gg[:T], beta[:T], s2, o2[:T], T)
+    pkg.delta_decode(qkv[T], gg[T], beta[T], s2, o2[T])
+    torch.cuda.synchronize()
+    assert_bf16_close(bits(o2[T:]), bits(o1[T:]), "decode after prefill")
+    # the chunked (WY) and the recurrent form of the last token agree to fp32
+    # rounding of two different algorithms
+    err = np.abs(s2.cpu().numpy() - s1.cpu().numpy())
+    assert (err <= 1e-4 + 1e-3 * np.abs(s1.cpu().numpy())).all(), err.max()

@@ -69,3 +69,21 @@ def test_conv(i):
     np.testing.assert_array_equal(y, GOLD[p + "y"])
     st = O.conv_state_update(GOLD[p + "x"], GOLD[p + "state"], T, batch=T if batch else 1)
     np.testing.assert_array_equal(st, GOLD[p + "state_out"])
+
+
+@pytest.mark.parametrize("i", _cases("attn_prefill_"))
+def test_attn_prefill(i):
+    p = f"attn_prefill_{i}_"
+    T, pos0, int8 = (int(v) for v in GOLD[p + "cfg"])
+    out = O.attn_prefill(GOLD[p + "q"], GOLD[p + "kvc"], T, pos0, GOLD[p + "kvs"] if int8 else None, mode="trunc")
+    np.testing.assert_array_equal(out, GOLD[p + "out"])
+
+
+@pytest.mark.parametrize("i", _cases("delta_prefill_"))
+def test_delta_prefill(i):
+    p = f"delta_prefill_{i}_"
+    state = GOLD[p + "state"].copy()
+    T = GOLD[p + "qkv"].shape[0]
+    out = O.delta_prefill(GOLD[p + "qkv"], GOLD[p + "g"], GOLD[p + "beta"], state, T, mode="trunc")
+    np.testing.assert_array_equal(out, GOLD[p + "out"])
+    np.testing.assert_array_equal(state[:2].view(np.uint32), GOLD[p + "state_out2"].view(np.uint32))
