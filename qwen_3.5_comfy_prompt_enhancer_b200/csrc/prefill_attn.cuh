@@ -7,7 +7,9 @@
 // online softmax in fp32, P rounded to bf16 for the P V product, fp32
 // accumulation, out = acc / l as bf16.
 //
-// CTA = 64 query rows of one head (4 warps x 16 rows), key blocks of 64.
+// CTA = 64 query rows of one head (4 warps x 16 rows), key blocks of 32 (the
+// reference's block, so the running max that P is rounded against evolves
+// the same way).
 // Warp-level bf16 MMAs (m16n8k16, fp32 accumulate) on fragments loaded with
 // ldmatrix from XOR-swizzled shared memory: Q once per CTA, K and V once per
 // key block (V through ldmatrix.trans, so the [key, dim] rows feed the B
@@ -21,7 +23,7 @@
 namespace qlin {
 
 constexpr int kPaRows = 64;      // query rows per CTA
-constexpr int kPaKeys = 64;      // keys per block
+constexpr int kPaKeys = 32;      // keys per block (the reference's BLOCK_N: P rounds to bf16 against the same running max)
 constexpr int kPaThreads = 128;  // 4 warps x 16 query rows
 
 struct AttnPrefillArgs {
@@ -68,8 +70,8 @@ __global__ void __launch_bounds__(kPaThreads) attn_prefill_kernel(const __grid_c
   constexpr int CH = HD / 8;  // 16-byte chunks per row
   extern __shared__ __align__(128) uint8_t pa_smem[];
   uint8_t* sq = pa_smem;                            // [64][HD] bf16
-  uint8_t* sk = sq + kPaRows * HD * 2;              // [64][HD] bf16
-  uint8_t* sv = sk + kPaKeys * HD * 2;              // [64][HD] bf16
+  uint8_t* sk = sq + kPaRows * HD * 2;              // [kPaKeys][HD] bf16
+  uint8_t* sv = sk + kPaKeys * HD * 2;              // [kPaKeys][HD] bf16
   pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int mb = blockIdx.x, head = blockIdx.y;
@@ -129,10 +131,11 @@ __global__ void __launch_bounds__(kPaThreads) attn_prefill_kernel(const __grid_c
       *reinterpret_cast<uint4*>(sv + pa_off<HD>(r, ch)) = vv4;
     }
     __syncthreads();
-    // S = Q K^T for this warp's 16 rows x 64 keys (8 tiles of 8 keys)
-    float s[8][4];
+    // S = Q K^T for this warp's 16 rows x 32 keys (4 tiles of 8 keys)
+    constexpr int NT = kPaKeys / 8;
+    float s[NT][4];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
+    for (int j = 0; j < NT; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
 #pragma unroll 4
     for (int kk = 0; kk < HD / 16; ++kk) {
       uint32_t a0, a1, a2, a3;
@@ -142,7 +145,7 @@ __global__ void __launch_bounds__(kPaThreads) attn_prefill_kernel(const __grid_c
         ldsm_x4(sq_u + pa_off<HD>(r, ch), a0, a1, a2, a3);
       }
 #pragma unroll
-      for (int jp = 0; jp < 4; ++jp) {  // two 8-key tiles per ldmatrix.x4
+      for (int jp = 0; jp < NT / 2; ++jp) {  // two 8-key tiles per ldmatrix.x4
         uint32_t b0, b1, b2, b3;
         const int r = jp * 16 + (lane & 7) + 8 * (lane >> 4);
         const int ch = 2 * kk + ((lane >> 3) & 1);
@@ -151,11 +154,11 @@ __global__ void __launch_bounds__(kPaThreads) attn_prefill_kernel(const __grid_c
         mma_bf16(s[2 * jp + 1], a0, a1, a2, a3, b2, b3);
       }
     }
-    // causal mask, online softmax (rows row0 / row1; a row's 64 keys are
-    // spread over the 4 lanes of a quad)
+    // causal mask, online softmax (rows row0 / row1; a row's keys are spread
+    // over the 4 lanes of a quad)
     float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < NT; ++j) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int n = n0 + j * 8 + 2 * tig + (e & 1);
@@ -175,7 +178,7 @@ __global__ void __launch_bounds__(kPaThreads) attn_prefill_kernel(const __grid_c
     }
     float psum[2] = {0.0f, 0.0f};
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < NT; ++j) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int h = e >> 1;
@@ -231,6 +234,6 @@ __global__ void __launch_bounds__(kPaThreads) attn_prefill_kernel(const __grid_c
   }
 }
 
-__host__ __device__ constexpr int attn_prefill_smem(int HD) { return 3 * 64 * HD * 2; }
+__host__ __device__ constexpr int attn_prefill_smem(int HD) { return (kPaRows + 2 * kPaKeys) * HD * 2; }
 
 }  // namespace qlin
