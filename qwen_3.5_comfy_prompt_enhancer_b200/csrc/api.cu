@@ -23,6 +23,7 @@
 #include "tcgemm.cuh"
 #include "tcgemm_w4.cuh"
 #include "tcgemv.cuh"
+#include "dpgemv.cuh"
 
 namespace qlin {
 
@@ -314,7 +315,21 @@ QLIN_KNOB(tune_max_cluster, "QLIN_TUNE_MAX_CLUSTER", 8)
 QLIN_KNOB(tune_rb_max, "QLIN_TUNE_RB_MAX", 0)
 QLIN_KNOB(tune_half, "QLIN_TUNE_HALF", 0)
 QLIN_KNOB(prefill_min_m, "QLIN_PREFILL_MIN_M", 128)
+QLIN_KNOB(tune_timeline, "QLIN_TIMELINE", 0)
+QLIN_KNOB(tune_dp, "QLIN_TUNE_DP", 1)  // 0: decode rows take the tensor-core kernel
 #undef QLIN_KNOB
+
+bool use_dp() { return tune_dp() != 0; }
+
+// Timeline slot of the next small-M launch: tuning builds with
+// QLIN_TIMELINE=1 stamp each launch's phases into slot (launch count % 16).
+int tl_next_slot() {
+#ifdef QLIN_TUNING
+  static std::atomic<int> next{0};
+  if (tune_timeline()) return next.fetch_add(1) % kTlSlots;
+#endif
+  return -1;
+}
 
 // ---------------------------------------------------------------- tcgen05 path planning / launch
 // Activation rows per row block: 1..16, and 32 for W8 (the W4 drain of 32
@@ -829,6 +844,7 @@ int run_tc(int wb, int epi, GemvArgs& a, int tiles, cudaStream_t st) {
   a.nbb = pl.nbb;
   a.part_alias = pl.alias;
   a.fault = di.fault;
+  a.tl_slot = tl_next_slot();
   const dim3 grid(pl.split, tiles, rowblocks);
   if (wb == 8) {
     switch (epi) {
@@ -1019,10 +1035,149 @@ bool mid_m_takes_gemm(int epi, int64_t M, int tiles) {
   return gemm_tiles >= kMidGemmMinTiles;
 }
 
+int smem_optin(const void* kern, size_t bytes, std::atomic<unsigned long long>& done);
+
+// ---------------------------------------------------------------- resident-weight dp4a GEMV (M <= 2)
+// Per-CTA shared memory that keeps two CTAs on an SM (this launch and the
+// next one's, which streams its weights under programmatic dependent launch).
+constexpr uint32_t kDpBudget = 110 * 1024;
+// Rows it serves.  Its dp4a work grows with M while the tensor-core kernel's
+// MMA count does not; measured on B200 (graph replay, rotating weights, us,
+// dp4a vs tcgen05): M = 1 W4 gate/up 2048->2x6144 6.5 vs 8.6, down 6144->2048
+// 4.7 vs 5.7, o 2.9 vs 3.8, qkv 3.7 vs 4.6, W8 2048->6144 3.5 vs 3.9, W8 down
+// 3.9 vs 5.6; M = 4 W4 gate/up 10.4 vs 10.0, W8 gate/up 14.0 vs 7.7, W8
+// 2048->6144 4.6 vs 4.0.
+constexpr int kDpMaxM = 2;
+
+int dp_mr(int64_t M) { return M <= 1 ? 1 : 2; }
+
+// K split for the dp kernel: the smallest split whose CTAs cover the SMs and
+// whose resident weights fit the budget, at most the portable cluster size
+// of 8.  A plan is taken only if all its CTAs are resident at once (at most
+// two per SM: a second wave would request its weights only after the
+// dependency) and its clusters are not of 7 CTAs (which pack poorly into
+// B200's GPCs); otherwise 0, and the tensor-core kernel streams instead.
+// Measured: W8 gate/up 2048->2x6144 at M = 1 needs split 7 (336 CTAs) to fit
+// and took 7.9 us against 6.6 on the tensor-core kernel; the 1187-tile W8
+// lm_head (split 3, 3561 CTAs) 61 against 56 us.
+int plan_dp(int wb, int mr, int ns, int K, int wgrp, int tiles, int sms, int* gmax_out, size_t* smem_out) {
+  const int G = K / kGroup;
+  int best = 0, best_gmax = 0;
+  size_t best_smem = 0;
+  for (int s = 1; s <= 8 && s <= G; ++s) {
+    const int gmax = (G + s - 1) / s;
+    const DpLayout L = dp_layout(wb, mr, ns, wgrp, gmax, s);
+    if (L.total > kDpBudget) continue;
+    best = s, best_gmax = gmax, best_smem = L.total;
+    if (static_cast<long long>(tiles) * s >= sms) break;
+  }
+  if (best == 7 || static_cast<long long>(tiles) * best > 2ll * sms) best = 0;
+  *gmax_out = best_gmax;
+  *smem_out = best_smem;
+  return best;
+}
+
+template <int WB, int MR, int EPI>
+int launch_dp_t(const DpArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
+  auto kern = dp_gemv_kernel<WB, MR, EPI>;
+  static std::atomic<unsigned long long> done{0};
+  if (int r = smem_optin(reinterpret_cast<const void*>(kern), kDpBudget + 1024, done)) return r;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kRgThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = grid.x;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = tune_pdl() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(dp_gemv)");
+  return QLIN_OK;
+}
+
+template <int WB, int EPI>
+int launch_dp_mr(int mr, const DpArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
+  if (mr == 1) return launch_dp_t<WB, 1, EPI>(a, grid, smem, st);
+  return launch_dp_t<WB, 2, EPI>(a, grid, smem, st);  // rows <= kDpMaxM = 2
+}
+
+// Launches the dp kernel if the shape fits it; *taken = false otherwise.
+int run_dp(int wb, int epi, const GemvArgs& a, int tiles, cudaStream_t st, bool* taken) {
+  *taken = false;
+  if (a.M > kDpMaxM || a.M < 1 || tiles > 65535) return QLIN_OK;
+  DevInfo di;
+  if (int r = launch_info(&di)) return r;
+  const int mr = dp_mr(a.M);
+  const int ns = epi == kEpiOut ? 1 : 2;
+  int gmax = 0;
+  size_t smem = 0;
+  const int split = plan_dp(wb, mr, ns, a.K, a.wgrp, tiles, di.sms, &gmax, &smem);
+  if (split == 0) return QLIN_OK;
+  DpArgs d;
+  memset(&d, 0, sizeof(d));
+  const uint32_t nsr = (wb == 4 && a.wgrp == 32) ? 2 : 1;
+  for (int i = 0; i < a.nseg; ++i) {
+    const GemvSeg& s0 = a.seg[i];
+    d.seg[i] = s0;
+    if (wb == 8) {
+      if (int r = make_map(&d.tw[i], s0.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, s0.n, a.K, s0.n, kTileN, 64)) return r;
+    } else {
+      if (int r = make_map(&d.tw[i], s0.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, s0.n, a.K / 2, s0.n, kTileN, 32)) return r;
+      if (int r = make_map(&d.ts[i], s0.sp, CU_TENSOR_MAP_DATA_TYPE_UINT16, s0.n, a.K / a.wgrp, 2ull * s0.n, kTileN,
+                           nsr))
+        return r;
+      if (s0.zp) {
+        if (int r = make_map(&d.tz[i], s0.zp, CU_TENSOR_MAP_DATA_TYPE_UINT8, s0.n, a.K / a.wgrp, s0.n, kTileN, nsr))
+          return r;
+      }
+    }
+  }
+  d.nseg = a.nseg;
+  d.a_q = a.a_q;
+  d.a_s = a.a_s;
+  d.M = a.M;
+  d.K = a.K;
+  d.wgrp = a.wgrp;
+  d.split = split;
+  d.gmax = gmax;
+  d.out = a.out;
+  d.ldo = a.ldo;
+  d.res = a.res;
+  d.ldr = a.ldr;
+  d.out_q = a.out_q;
+  d.out_s = a.out_s;
+  d.n_q = a.n_q;
+  d.fault = di.fault;
+  *taken = true;
+  const dim3 grid(split, tiles, 1);
+  if (wb == 8) {
+    switch (epi) {
+      case kEpiOut: return launch_dp_mr<8, kEpiOut>(mr, d, grid, smem, st);
+      case kEpiSiluBf16: return launch_dp_mr<8, kEpiSiluBf16>(mr, d, grid, smem, st);
+      default: return launch_dp_mr<8, kEpiSiluQuant>(mr, d, grid, smem, st);
+    }
+  }
+  switch (epi) {
+    case kEpiOut: return launch_dp_mr<4, kEpiOut>(mr, d, grid, smem, st);
+    default: return launch_dp_mr<4, kEpiSiluQuant>(mr, d, grid, smem, st);
+  }
+}
+
 int run_gemv(int wb, int epi, GemvArgs& a, int tiles, cudaStream_t st) {
   const bool gemm = a.M >= prefill_min_m() || mid_m_takes_gemm(epi, a.M, tiles);
   if (wb == 8 && gemm) return run_prefill_w8(epi, a, tiles, st);
   if (wb == 4 && gemm && a.wgrp % 64 == 0) return run_prefill_w4(epi, a, tiles, st);
+  if (use_dp()) {
+    bool taken = false;
+    if (int r = run_dp(wb, epi, a, tiles, st, &taken)) return r;
+    if (taken) return QLIN_OK;
+  }
   return run_tc(wb, epi, a, tiles, st);
 }
 
@@ -1452,6 +1607,17 @@ int qlin_device_fault(int clear) {
   }
   return static_cast<int>(v);
 }
+
+#ifdef QLIN_TUNING
+// Tuning builds: copies the phase timeline ([16 slots][2048 CTAs][8] ns stamps)
+// to host memory.
+int qlin_debug_timeline(void* host, int64_t bytes) {
+  if (!host || bytes < static_cast<int64_t>(sizeof(g_qlin_tl))) return fail(QLIN_ERR_INVALID_ARGUMENT, "buffer");
+  cudaError_t e = cudaMemcpyFromSymbol(host, g_qlin_tl, sizeof(g_qlin_tl));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyFromSymbol(timeline)");
+  return QLIN_OK;
+}
+#endif
 
 int qlin_set_wait_limit_ns(int64_t ns) {
   if (ns <= 0) return fail(QLIN_ERR_INVALID_ARGUMENT, "wait limit must be positive");

@@ -56,7 +56,26 @@ struct GemvArgs {
   float* out_s;       // kEpiSiluQuant: fp32 [M, n_q/64]
   int n_q;
   unsigned* fault;    // device fault word (bounded waits)
+  int tl_slot;        // tuning builds: phase-timeline slot of this launch (-1: none)
 };
+
+#ifdef QLIN_TUNING
+// Phase timeline of the small-M kernel (tuning builds only): %globaltimer
+// stamps per CTA and launch slot, read back with qlin_debug_timeline.
+constexpr int kTlSlots = 16, kTlCtas = 2048, kTlStamps = 8;
+__device__ unsigned long long g_qlin_tl[kTlSlots][kTlCtas][kTlStamps];
+#define QLIN_TL(args, k)                                                                          \
+  do {                                                                                            \
+    if ((args).tl_slot >= 0) {                                                                    \
+      const unsigned cta_ = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);       \
+      if (cta_ < kTlCtas) g_qlin_tl[(args).tl_slot][cta_][k] = global_ns();                      \
+    }                                                                                             \
+  } while (0)
+#else
+#define QLIN_TL(args, k) \
+  do {                   \
+  } while (0)
+#endif
 
 __host__ __device__ inline uint32_t align_up(uint32_t x, uint32_t a) { return (x + a - 1) / a * a; }
 

@@ -1,0 +1,427 @@
+// Resident-weight GEMV on CUDA cores for decode rows (M <= 4): the small-M
+// entry points (gemm_i8 / gemm_w4 + residual, proj3(_w4), the fused gate/up
+// epilogues) when every weight of a CTA's K range fits in its shared memory.
+//
+// Why not the tensor cores here.  At M <= 4 the work per weight byte is tiny
+// and a launch is a short step between two grid dependencies: what counts is
+// the time from the dependency to the last store.  This kernel requests ALL
+// its weights (int8 rows, or W4 nibbles kept packed -- 4 KB per 64-K group
+// and 128 columns, half of what an unpacked MMA operand needs) before the
+// dependency, so under programmatic dependent launch the whole weight stream
+// overlaps the preceding kernel.  After the dependency there is no hand-off
+// chain: every warp loads the activations, decodes its groups in registers
+// and accumulates with dp4a, then the CTA and the cluster reduce.
+//
+// Work split.  CTA = one 128-column tile x one K range (cluster of `split`
+// CTAs per tile, as the tensor-core kernel).  Lane l of every warp owns
+// columns 4l .. 4l+3; warp w owns the (group, stream) items w, w + 8, ... of
+// the CTA's K range.  Per item the int32 dot of each (row, column) over the
+// group's 64 K (W4 groups of 32: per 32-K half) is complete inside one
+// thread before the fp32 epilogue of the reference:
+//   W8: acc += float(I) * a_s[m, kb]                   (kernels/gemm.py:43-45)
+//   W4: acc += float(I - z * sum(a)) * (a_s[m, kb] * ws)  (kernels/w4.py:103-104)
+// Four weight rows (4 columns each) are transposed with byte permutes so
+// that dp4a reduces along K; a W4 word of 4 packed rows holds 8 K values of
+// one column: the low nibbles (even K) and high nibbles (odd K) meet
+// activation words pre-split by K parity (dp4a.u32.s32, unsigned nibbles).
+// The zero point is removed exactly: sum(a (nib - z)) = sum(a nib) - z sum(a).
+//
+// Reduction order (fixed): per warp its items in order, then the 8 warps in
+// order, then the cluster's ranks in order; only this fp32 order differs
+// from the reference's ascending-K sum.
+#pragma once
+
+#include "args.cuh"
+#include "qlin_common.cuh"
+
+namespace qlin {
+
+constexpr int kRgThreads = 256;
+constexpr int kRgWarps = kRgThreads / 32;
+
+struct DpArgs {
+  CUtensorMap tw[3];   // weights, plain (unswizzled) boxes: W8 128 columns x 64 rows; W4 128 x 32 packed rows
+  CUtensorMap ts[3];   // W4 group scales (bf16), box 128 x nsub
+  CUtensorMap tz[3];   // W4 zeros (uint8), box 128 x nsub
+  GemvSeg seg[3];      // n, out_col, tile_begin, has_z, bs (W8)
+  int nseg;
+  const int8_t* a_q;   // [M, K]
+  const float* a_s;    // [M, K/64]
+  int M, K, wgrp, split, gmax;
+  void* out;
+  long long ldo;
+  const void* res;
+  long long ldr;
+  int8_t* out_q;
+  float* out_s;
+  int n_q;
+  unsigned* fault;
+};
+
+// Shared-memory carve-up (host and device): weights of every (group,
+// stream) item, the K-range activations, their per-group sums (W4) and
+// scales, the cross-warp reduction (over the weights once they are used),
+// the partial sums received from the other ranks, barriers.
+struct DpLayout {
+  uint32_t item, wbytes, sbytes, act_off, asum_off, as_off, part_off, xchg_off, bar_off, total;
+};
+__host__ __device__ inline DpLayout dp_layout(int wb, int mr, int ns, int wgrp, int gmax, int split) {
+  DpLayout L;
+  const int nsub = (wb == 4 && wgrp == 32) ? 2 : 1;
+  L.wbytes = wb == 8 ? 64 * kTileN : 32 * kTileN;
+  L.sbytes = wb == 8 ? 0 : nsub * kTileN * 3;
+  L.item = align_up(L.wbytes + L.sbytes, 128);
+  uint32_t off = gmax * ns * L.item;
+  const uint32_t red = kRgWarps * ns * mr * kTileN * 4;  // aliases the weights
+  if (off < red) off = red;
+  off = align_up(off, 128);
+  L.act_off = off;
+  off = align_up(off + gmax * mr * 64, 16);
+  L.asum_off = off;
+  off = align_up(off + (wb == 4 ? gmax * mr * 2 * 4 : 0), 16);
+  L.as_off = off;
+  off = align_up(off + gmax * mr * 4, 16);
+  L.part_off = off;
+  off = align_up(off + (split > 1 ? split - 1 : 0) * ns * mr * kTileN * 4, 16);
+  L.xchg_off = off;
+  off = align_up(off + 4 * mr * 4, 16);
+  L.bar_off = off;
+  off += 8 * (kRgWarps + 1);
+  L.total = off + 128;  // alignment slack
+  return L;
+}
+
+// d = c + sum_i a.u8[i] * b.s8[i]
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// 4x4 byte transpose: r_i holds bytes (c0..c3) of row i; c_j returns column
+// j's bytes in row order.
+__device__ __forceinline__ void tr4x4(uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3, uint32_t (&c)[4]) {
+  const uint32_t t0 = __byte_perm(r0, r1, 0x5140);  // a0 b0 a1 b1
+  const uint32_t t1 = __byte_perm(r0, r1, 0x7362);  // a2 b2 a3 b3
+  const uint32_t t2 = __byte_perm(r2, r3, 0x5140);
+  const uint32_t t3 = __byte_perm(r2, r3, 0x7362);
+  c[0] = __byte_perm(t0, t2, 0x5410);
+  c[1] = __byte_perm(t0, t2, 0x7632);
+  c[2] = __byte_perm(t1, t3, 0x5410);
+  c[3] = __byte_perm(t1, t3, 0x7632);
+}
+
+template <int WB, int MR, int EPI>
+__global__ void __launch_bounds__(kRgThreads, 1) dp_gemv_kernel(const __grid_constant__ DpArgs p) {
+  constexpr int NS = (EPI == kEpiOut) ? 1 : 2;
+  extern __shared__ __align__(128) uint8_t dp_smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dp_smem_raw) + 127) & ~uintptr_t(127));
+  const DpLayout L = dp_layout(WB, MR, NS, p.wgrp, p.gmax, p.split);
+  const int nsub = (WB == 4 && p.wgrp == 32) ? 2 : 1;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);  // one per warp
+  uint64_t* recv = full + kRgWarps;
+  int8_t* act = reinterpret_cast<int8_t*>(smem + L.act_off);      // [g][m][64]
+  int* asum = reinterpret_cast<int*>(smem + L.asum_off);           // [g][m][2]
+  float* ass = reinterpret_cast<float*>(smem + L.as_off);          // [g][m]
+  float* part = reinterpret_cast<float*>(smem + L.part_off);       // [rank-1][s][m][128]
+  float* red = reinterpret_cast<float*>(smem);                     // [warp][s][m][128], over the weights
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rank = blockIdx.x, tile = blockIdx.y;
+  int si = 0;
+  if (EPI == kEpiOut) {
+    if (p.nseg > 1 && tile >= p.seg[1].tile_begin) si = 1;
+    if (p.nseg > 2 && tile >= p.seg[2].tile_begin) si = 2;
+  }
+  const GemvSeg& S0 = p.seg[si];
+  const int n0 = (tile - S0.tile_begin) * kTileN;
+  const int G = p.K / kGroup;
+  const int g0 = static_cast<int>(static_cast<long long>(rank) * G / p.split);
+  const int g1 = static_cast<int>(static_cast<long long>(rank + 1) * G / p.split);
+  const int nst = g1 - g0;
+  const int items = nst * NS;
+  auto item_w = [&](int it) { return smem + it * L.item; };
+
+  // ---------------------------------------------------------------- set-up: every weight requested now
+  if (threadIdx.x == 0) {
+    for (int w = 0; w < kRgWarps; ++w) mbar_init(full + w, 1);
+    mbar_init(recv, 1);
+    fence_mbar_init();
+    if (p.split > 1 && rank == 0)
+      mbar_arrive_expect_tx(recv, static_cast<uint32_t>((p.split - 1) * kTileN * NS * MR * 4));
+  }
+  __syncthreads();
+  if (lane == 0) {
+    // warp w requests its own items, completing on its own barrier
+    const uint64_t pol = l2_policy_evict_first();
+    uint32_t bytes = 0;
+    for (int it = warp; it < items; it += kRgWarps) {
+      const int s = NS == 1 ? si : it % NS;
+      bytes += L.wbytes + (WB == 4 ? nsub * kTileN * 2 + (p.seg[s].has_z ? nsub * kTileN : 0) : 0);
+    }
+    if (bytes) mbar_arrive_expect_tx(full + warp, bytes);
+    for (int it = warp; it < items; it += kRgWarps) {
+      const int gl = it / NS, s = NS == 1 ? si : it % NS;
+      const int g = g0 + gl;
+      uint8_t* dst = item_w(it);
+      if (WB == 8) {
+        tma_load_2d(dst, &p.tw[s], n0, g * 64, full + warp, pol);
+      } else {
+        tma_load_2d(dst, &p.tw[s], n0, g * 32, full + warp, pol);
+        const int srow = (g * 64) / p.wgrp;
+        tma_load_2d(dst + L.wbytes, &p.ts[s], n0, srow, full + warp, pol);
+        if (p.seg[s].has_z) tma_load_2d(dst + L.wbytes + nsub * kTileN * 2, &p.tz[s], n0, srow, full + warp, pol);
+      }
+    }
+  }
+  pdl_launch_dependents();
+  if (p.split > 1) {
+    cluster_arrive_relaxed();
+    cluster_wait();
+  }
+
+  // epilogue operands that do not depend on the previous kernel
+  const int c = threadIdx.x;  // epilogue: threads 0..127 own one column each
+  const bool epi_thread = threadIdx.x < kTileN && rank == 0;
+  const int en = n0 + c;
+  const bool evalid = epi_thread && en < S0.n;
+  float pre_s0 = 1.0f, pre_s1 = 1.0f;
+  if (WB == 8 && evalid) {
+    pre_s0 = __ldg((NS == 1 ? S0.bs : p.seg[0].bs) + en);
+    if (NS == 2) pre_s1 = __ldg(p.seg[1].bs + en);
+  }
+
+  // ---------------------------------------------------------------- activations (after the dependency)
+  pdl_wait();
+  float pre_res[MR];
+#pragma unroll
+  for (int m = 0; m < MR; ++m) pre_res[m] = 0.0f;
+  if (EPI == kEpiOut && evalid && p.res) {
+    const __nv_bfloat16* res = reinterpret_cast<const __nv_bfloat16*>(p.res);
+#pragma unroll
+    for (int m = 0; m < MR; ++m)
+      if (m < p.M) pre_res[m] = __bfloat162float(res[static_cast<long long>(m) * p.ldr + S0.out_col + en]);
+  }
+  // a_q rows of the K range -> act[g][m][64]; W4 reorders each 8-K block to
+  // (the 4 even K, the 4 odd K) so one 8-byte load gives both parity words
+  for (int i = threadIdx.x; i < nst * MR * 8; i += kRgThreads) {
+    const int b8 = i % 8, m = (i / 8) % MR, gl = i / (8 * MR);
+    uint2 v = make_uint2(0u, 0u);
+    if (m < p.M) v = *reinterpret_cast<const uint2*>(p.a_q + static_cast<long long>(m) * p.K + (g0 + gl) * 64 + b8 * 8);
+    if (WB == 4) v = make_uint2(__byte_perm(v.x, v.y, 0x6420), __byte_perm(v.x, v.y, 0x7531));
+    *reinterpret_cast<uint2*>(act + (gl * MR + m) * 64 + b8 * 8) = v;
+  }
+  for (int i = threadIdx.x; i < nst * MR; i += kRgThreads) {
+    const int m = i % MR, gl = i / MR;
+    ass[gl * MR + m] = m < p.M ? __ldg(p.a_s + static_cast<long long>(m) * G + g0 + gl) : 0.0f;
+  }
+  __syncthreads();
+  if (WB == 4) {
+    // sum of the activations over each 32-K half of a group (zero points)
+    for (int i = threadIdx.x; i < nst * MR * 2; i += kRgThreads) {
+      const int h = i % 2, m = (i / 2) % MR, gl = i / (2 * MR);
+      const int* a = reinterpret_cast<const int*>(act + (gl * MR + m) * 64 + h * 32);
+      int sa = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sa = __dp4a(a[e], 0x01010101, sa);
+      asum[(gl * MR + m) * 2 + h] = sa;
+    }
+    __syncthreads();
+  }
+
+  // ---------------------------------------------------------------- the dots
+  float acc[NS][4][MR];
+#pragma unroll
+  for (int s = 0; s < NS; ++s)
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int m = 0; m < MR; ++m) acc[s][j][m] = 0.0f;
+  bool ok = true;
+  if (warp < items) ok = mbar_wait(full + warp, 0);
+  if (!ok) {
+    if (lane == 0) record_fault(p.fault, kFaultFullWait);
+    mbar_wait(full + warp, 0);  // copies still in flight land before the region is reused or the CTA exits
+  }
+  for (int it = warp; ok && it < items; it += kRgWarps) {
+    const int gl = it / NS, s = NS == 1 ? 0 : it % NS;
+    const uint8_t* wt = item_w(it);
+    const float* as_g = ass + gl * MR;
+    if (WB == 8) {
+      int isum[4][MR];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int m = 0; m < MR; ++m) isum[j][m] = 0;
+#pragma unroll 4
+      for (int b = 0; b < 16; ++b) {  // 4 K rows per block
+        const uint32_t* rows = reinterpret_cast<const uint32_t*>(wt + b * 4 * kTileN) + lane;
+        uint32_t col[4];
+        tr4x4(rows[0], rows[kTileN / 4], rows[2 * kTileN / 4], rows[3 * kTileN / 4], col);
+#pragma unroll
+        for (int m = 0; m < MR; ++m) {
+          const int aw = *reinterpret_cast<const int*>(act + (gl * MR + m) * 64 + b * 4);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) isum[j][m] = __dp4a(static_cast<int>(col[j]), aw, isum[j][m]);
+        }
+      }
+      // out += float(int32 group sum) * a_s[m, kb]   (kernels/gemm.py:43-45)
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int m = 0; m < MR; ++m)
+          acc[s][j][m] = __fadd_rn(acc[s][j][m], __fmul_rn(__int2float_rn(isum[j][m]), as_g[m]));
+    } else {
+      const GemvSeg& sg = p.seg[NS == 1 ? si : s];
+      const uint16_t* sc = reinterpret_cast<const uint16_t*>(wt + L.wbytes);
+      const uint8_t* zz = wt + L.wbytes + nsub * kTileN * 2;
+      int isum[2][4][MR];  // per 32-K half
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+          for (int m = 0; m < MR; ++m) isum[h][j][m] = 0;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+#pragma unroll 2
+        for (int bb = 0; bb < 4; ++bb) {  // 4 packed rows = 8 K per block
+          const int b = h * 4 + bb;
+          const uint32_t* rows = reinterpret_cast<const uint32_t*>(wt + b * 4 * kTileN) + lane;
+          uint32_t col[4];
+          tr4x4(rows[0], rows[kTileN / 4], rows[2 * kTileN / 4], rows[3 * kTileN / 4], col);
+#pragma unroll
+          for (int m = 0; m < MR; ++m) {
+            const uint2 aw = *reinterpret_cast<const uint2*>(act + (gl * MR + m) * 64 + b * 8);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              isum[h][j][m] = dp4a_us(col[j] & 0x0F0F0F0Fu, static_cast<int>(aw.x), isum[h][j][m]);
+              isum[h][j][m] = dp4a_us((col[j] >> 4) & 0x0F0F0F0Fu, static_cast<int>(aw.y), isum[h][j][m]);
+            }
+          }
+        }
+      }
+      // out += float(int32 sub-block sum) * (a_s * ws)   (kernels/w4.py:103-104)
+      const int* asg = asum + gl * MR * 2;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int col_n = lane * 4 + j;
+        if (nsub == 2) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const float ws = bf16_bits_to_f32(sc[h * kTileN + col_n]);
+            const int z = sg.has_z ? static_cast<int>(zz[h * kTileN + col_n]) : 8;
+#pragma unroll
+            for (int m = 0; m < MR; ++m) {
+              const int v = isum[h][j][m] - z * asg[m * 2 + h];
+              acc[s][j][m] = __fadd_rn(acc[s][j][m], __fmul_rn(__int2float_rn(v), __fmul_rn(as_g[m], ws)));
+            }
+          }
+        } else {
+          const float ws = bf16_bits_to_f32(sc[col_n]);
+          const int z = sg.has_z ? static_cast<int>(zz[col_n]) : 8;
+#pragma unroll
+          for (int m = 0; m < MR; ++m) {
+            const int v = isum[0][j][m] + isum[1][j][m] - z * (asg[m * 2] + asg[m * 2 + 1]);
+            acc[s][j][m] = __fadd_rn(acc[s][j][m], __fmul_rn(__int2float_rn(v), __fmul_rn(as_g[m], ws)));
+          }
+        }
+      }
+    }
+  }
+
+  // ---------------------------------------------------------------- reduce: warps, then the cluster
+  __syncthreads();  // every weight read -> the reduction may overwrite them
+#pragma unroll
+  for (int s = 0; s < NS; ++s)
+#pragma unroll
+    for (int m = 0; m < MR; ++m)
+      *reinterpret_cast<float4*>(red + ((warp * NS + s) * MR + m) * kTileN + lane * 4) =
+          make_float4(acc[s][0][m], acc[s][1][m], acc[s][2][m], acc[s][3][m]);
+  __syncthreads();
+  if (threadIdx.x >= kTileN) return;  // threads 0..127 hold one column each from here
+  float vs[NS][MR];
+#pragma unroll
+  for (int s = 0; s < NS; ++s)
+#pragma unroll
+    for (int m = 0; m < MR; ++m) {
+      float v = 0.0f;
+#pragma unroll
+      for (int w = 0; w < kRgWarps; ++w) v = __fadd_rn(v, red[((w * NS + s) * MR + m) * kTileN + c]);
+      vs[s][m] = v;
+    }
+  if (rank > 0) {
+    // push to rank 0, completing its receive barrier; rank 0 outlives the
+    // stores (it exits only after its receive barrier completed, or after
+    // two bounded waits for it on the fault path)
+    const uint32_t slot0 = smem_u32(part + static_cast<size_t>(rank - 1) * NS * MR * kTileN);
+    const uint32_t dst = map_to_rank(slot0, 0);
+    const uint32_t rbar = map_to_rank(smem_u32(recv), 0);
+#pragma unroll
+    for (int s = 0; s < NS; ++s)
+#pragma unroll
+      for (int m = 0; m < MR; ++m) st_async_f32(dst + ((s * MR + m) * kTileN + c) * 4, vs[s][m], rbar);
+    return;
+  }
+  if (p.split > 1) {
+    if (!mbar_wait_cluster(recv, 0)) {
+      if ((threadIdx.x & 31) == 0) record_fault(p.fault, kFaultFullWait);
+      mbar_wait_cluster(recv, 0);
+    } else {
+      for (int r = 1; r < p.split; ++r) {
+        const float* rp = part + static_cast<size_t>(r - 1) * NS * MR * kTileN;
+#pragma unroll
+        for (int s = 0; s < NS; ++s)
+#pragma unroll
+          for (int m = 0; m < MR; ++m) vs[s][m] = __fadd_rn(vs[s][m], rp[(s * MR + m) * kTileN + c]);
+      }
+    }
+  }
+
+  // ---------------------------------------------------------------- epilogue (threads 0..127 of rank 0)
+  const int q4 = threadIdx.x >> 5;
+  const bool valid = en < S0.n;
+  if (EPI == kEpiOut) {
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
+#pragma unroll
+    for (int m = 0; m < MR; ++m) {
+      if (!valid || m >= p.M) continue;
+      float v = vs[0][m];
+      if (WB == 8) v = __fmul_rn(v, pre_s0);  // out * bs (kernels/gemm.py:51-52)
+      if (p.res) v = __fadd_rn(v, pre_res[m]);
+      out[static_cast<long long>(m) * p.ldo + S0.out_col + en] = __float2bfloat16_rn(v);
+    }
+  } else {
+    float* xchg = reinterpret_cast<float*>(smem + L.xchg_off);
+#pragma unroll
+    for (int m = 0; m < MR; ++m) {
+      float g = vs[0][m], uu = vs[1][m];
+      if (WB == 8) {
+        g = __fmul_rn(g, pre_s0);
+        uu = __fmul_rn(uu, pre_s1);
+      }
+      const float h = __fmul_rn(silu_ref(g), uu);  // silu(g) * u (kernels/gemm.py:197)
+      const bool store = valid && m < p.M;
+      if (EPI == kEpiSiluBf16) {
+        if (store) reinterpret_cast<__nv_bfloat16*>(p.out)[static_cast<long long>(m) * p.ldo + en] = __float2bfloat16_rn(h);
+      } else {
+        // kernels/gemm.py:198-211: round through bf16, per-64 amax, int8 codes
+        const float hb = bf16_round_f32(h);
+        float amax = fabsf(hb);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        if ((threadIdx.x & 31) == 0) xchg[q4 * MR + m] = amax;
+        named_bar_sync(2, kTileN);
+        amax = fmaxf(amax, xchg[(q4 ^ 1) * MR + m]);  // the other warp of this 64-column group
+        const float scq = fmaxf(__fdiv_rn(amax, 127.0f), 1e-8f);
+        const int8_t qv = round_i8(__fdiv_rn(hb, scq));
+        if (store) {
+          p.out_q[static_cast<long long>(m) * p.n_q + en] = qv;
+          if ((c & 63) == 0) p.out_s[static_cast<long long>(m) * (p.n_q / 64) + en / 64] = scq;
+        }
+      }
+    }
+  }
+}
+
+}  // namespace qlin

@@ -143,6 +143,7 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
+  if (threadIdx.x == 0) QLIN_TL(p, 0);
   const int BS = p.bs, RB = p.rb, NBB = p.nbb;
   const int AB = WB == 4 ? p.ab : 0;
   const int ab_div = AB > 0 ? AB : 1;  // W8 has no unpacked ring
@@ -288,6 +289,7 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
     cluster_wait();
   }
   const uint32_t tbase = *tmem_slot;
+  if (threadIdx.x == 0) QLIN_TL(p, 1);
 
   float acc[NS][MR];  // drain threads: this CTA's partial sums for output column c
 #pragma unroll
@@ -315,6 +317,7 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
   } else if (warp == kTcWarpMma) {
     // ------------------------------------------------------------------ MMA issuer
     pdl_wait();
+    if (lane == 0) QLIN_TL(p, 2);
     if (elect_one()) {
       mbar_arrive_expect_tx(bfull, L.nbox * NM * 128);
       const uint64_t pol = l2_policy_evict_last();
@@ -324,6 +327,7 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
     __syncwarp();
     constexpr uint32_t idesc = idesc_i8(128, NM, WB == 8, true, true, false);
     bool ok = mbar_wait(bfull, 0);
+    if (lane == 0) QLIN_TL(p, 3);
     for (int b = 0; ok && b < nbatch; ++b) {
       const int rs = b % RB;
       const int as = WB == 4 ? b % ab_div : 0;
@@ -358,6 +362,7 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
       }
       __syncwarp();
     }
+    if (lane == 0) QLIN_TL(p, 4);
     if (!ok && lane == 0) record_fault(p.fault, kFaultMmaWait);
   } else if (is_drain) {
     // ------------------------------------------------------------------ drain
@@ -452,6 +457,7 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
         if (lane == 0) mbar_arrive(empty + rs);
       }
     }
+    if (td == 0) QLIN_TL(p, 5);
     if (!ok && lane == 0) record_fault(p.fault, kFaultFullWait);
     if (p.part_alias && rank == 0) {
       // The last accumulator batch was observed: every MMA of this CTA has
@@ -550,6 +556,7 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
 #pragma unroll
         for (int m = 0; m < MR; ++m) st_async_f32(dst + ((s * MR + m) * kTileN + c) * 4, acc[s][m], rbar);
     }
+    if (c == 0) QLIN_TL(p, 6);
   }
   if (epi_thread) {
     const int n = en;
@@ -577,6 +584,7 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
           for (int m = 0; m < MR; ++m) vs[s][m] = __fadd_rn(vs[s][m], rp[(s * MR + m) * kTileN + c]);
       }
     }
+    if (c == 0) QLIN_TL(p, 6);
     if (EPI == kEpiOut) {
       __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
 #pragma unroll
@@ -620,6 +628,7 @@ __global__ void __launch_bounds__(tc_threads(WB), 1) tc_gemv_kernel(const __grid
         }
       }
     }
+    if (c == 0) QLIN_TL(p, 7);
   }
 }
 
