@@ -548,6 +548,11 @@ def kernel_case(pkg, dev, name):
         out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
         work = (2.0 * M * N * K, "op") if M >= 128 else (K * N + N * 4 + M * K * (1 + 4 / 64) + M * N * 2, "B")
         return (lambda: pkg.gemm_i8(a_q, a_s, b, bs, out)), work[0], work[1]
+    if name == "decode_step_b4":
+        st = pkg.decode_step.HybridStack(pkg.decode_step.QWEN35_2B, dev, 4, 1040, kv_int8=True, seed=11)
+        ids = torch.randint(0, st.V, (4,), device=dev)
+        pos = torch.tensor([1024], dtype=torch.int32, device=dev)
+        return (lambda: st.step(ids, pos)), st.step_bytes(1024), "B"
     raise SystemExit(f"unknown --kernel {name}")
 
 

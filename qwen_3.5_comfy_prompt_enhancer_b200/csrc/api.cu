@@ -1053,13 +1053,16 @@ int dp_mr(int64_t M) { return M <= 1 ? 1 : 2; }
 
 // K split for the dp kernel: the smallest split whose CTAs cover the SMs and
 // whose resident weights fit the budget, at most the portable cluster size
-// of 8.  A plan is taken only if all its CTAs are resident at once (at most
-// two per SM: a second wave would request its weights only after the
-// dependency) and its clusters are not of 7 CTAs (which pack poorly into
+// of 8.  For W8 a plan is taken only if all its CTAs are resident at once
+// (at most two per SM: a second wave would request its weights only after
+// the dependency) and its clusters are not of 7 CTAs (which pack poorly into
 // B200's GPCs); otherwise 0, and the tensor-core kernel streams instead.
 // Measured: W8 gate/up 2048->2x6144 at M = 1 needs split 7 (336 CTAs) to fit
 // and took 7.9 us against 6.6 on the tensor-core kernel; the 1187-tile W8
-// lm_head (split 3, 3561 CTAs) 61 against 56 us.
+// lm_head (split 3, 3561 CTAs) 61 against 56 us.  W4, whose tensor-core path
+// has to unpack the nibbles first, gains even over several waves: the
+// config-5 W4 gate/up 5120->2x17408 at M = 1 (1088 CTAs) made the one-GPU
+// column-split layer 61.7 instead of 73.9 us.
 int plan_dp(int wb, int mr, int ns, int K, int wgrp, int tiles, int sms, int* gmax_out, size_t* smem_out) {
   const int G = K / kGroup;
   int best = 0, best_gmax = 0;
@@ -1071,7 +1074,7 @@ int plan_dp(int wb, int mr, int ns, int K, int wgrp, int tiles, int sms, int* gm
     best = s, best_gmax = gmax, best_smem = L.total;
     if (static_cast<long long>(tiles) * s >= sms) break;
   }
-  if (best == 7 || static_cast<long long>(tiles) * best > 2ll * sms) best = 0;
+  if (wb == 8 && (best == 7 || static_cast<long long>(tiles) * best > 2ll * sms)) best = 0;
   *gmax_out = best_gmax;
   *smem_out = best_smem;
   return best;
