@@ -184,7 +184,7 @@ int qlin_silu_mul_quant(const void* g, const void* u, int64_t M, int64_t N, int8
 
 /* kernels/norm.py:211-240 (gate_proj): from int8 activations a_q [M, K] with
  * per-64 scales a_s [M, K/64], x = a_q * a_s; b = wb @ x, av = wa @ x for
- * bf16 wb, wa [NB, K] (NB <= 32); beta = sigmoid(b),
+ * bf16 wb, wa [NB, K]; beta = sigmoid(b),
  * gate = -exp(a_log) * softplus(av + dt_bias) with bf16 dt_bias, a_log [NB];
  * beta, gate fp32 [M, NB].  a_q needs 8-byte alignment, wb / wa 16-byte. */
 int qlin_gate_proj(const int8_t* a_q, const float* a_s, int64_t M, int64_t K, const void* wb, const void* wa,
@@ -245,6 +245,13 @@ int qlin_conv_silu(const void* x, int64_t ldx, const void* w, int64_t ks, const 
  * state[3b .. 3b+2] shift down by one and take x row b as the newest. */
 int qlin_conv_state_update(const void* x, int64_t ldx, void* state, int64_t T, int64_t C, int64_t ks,
                            int64_t batch, void* stream);
+
+/* qlin_conv_silu (batch mode) followed by qlin_conv_state_update (batch mode)
+ * of one decode step in one launch: y [batch, C] and the shifted windows
+ * state [3*batch, C], identical to the two calls.  No reference counterpart
+ * (the engine calls the two kernels back to back, engine.py:302-303). */
+int qlin_conv_silu_update(const void* x, int64_t ldx, const void* w, int64_t ks, void* state, void* y,
+                          int64_t batch, int64_t C, void* stream);
 
 /* ---- Prefill neighbours ---- */
 

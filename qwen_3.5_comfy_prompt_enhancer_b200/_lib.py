@@ -44,6 +44,7 @@ SIGNATURES = {
     "qlin_delta_decode": [_P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _P],
     "qlin_conv_silu": [_P, _I, _P, _I, _P, _P, _I, _I, ctypes.c_int, _P],
     "qlin_conv_state_update": [_P, _I, _P, _I, _I, _I, _I, _P],
+    "qlin_conv_silu_update": [_P, _I, _P, _I, _P, _P, _I, _I, _P],
     "qlin_attn_prefill": [_P, _P, _P, _P, _I, _I, _I, _I, _I, ctypes.c_int, _P],
     "qlin_delta_prefill": [_P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _P],
     "qlin_plan_small_m": [ctypes.c_int, ctypes.c_int, _I, _I, _I, _I, ctypes.c_int, _P],

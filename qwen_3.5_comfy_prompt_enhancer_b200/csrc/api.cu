@@ -1971,7 +1971,7 @@ int qlin_gate_proj(const int8_t* a_q, const float* a_s, int64_t M, int64_t K, co
                    int64_t NB, const void* dt_bias, const void* a_log, float* beta, float* gate, void* stream) {
   if (int r = check_rows(M, K, "gate_proj")) return r;
   if (K == 0 || K % kGroup != 0) return fail(QLIN_ERR_SHAPE, "gate_proj: K=%lld must be a positive multiple of 64", (long long)K);
-  if (NB < 1 || NB > 32) return fail(QLIN_ERR_SHAPE, "gate_proj: NB=%lld must be 1..32", (long long)NB);
+  if (NB < 1 || NB > 65535) return fail(QLIN_ERR_SHAPE, "gate_proj: NB=%lld out of range", (long long)NB);
   if (M == 0) return QLIN_OK;
   if (M > 2147483647) return fail(QLIN_ERR_SHAPE, "gate_proj: M too large");
   if (!a_q || !a_s || !wb || !wa || !dt_bias || !a_log || !beta || !gate)
@@ -1985,9 +1985,9 @@ int qlin_gate_proj(const int8_t* a_q, const float* a_s, int64_t M, int64_t K, co
   void* args[] = {const_cast<int8_t**>(&a_q), const_cast<float**>(&a_s), &K_, const_cast<void**>(&wb),
                   const_cast<void**>(&wa), &NB_, const_cast<void**>(&dt_bias), const_cast<void**>(&a_log), &beta,
                   &gate};
-  const void* kern = NB <= 16 ? reinterpret_cast<const void*>(gate_proj_kernel<16>)
-                              : reinterpret_cast<const void*>(gate_proj_kernel<32>);
-  return prod_launch(kern, dim3(static_cast<unsigned>(M)), args, static_cast<cudaStream_t>(stream));
+  if (M > 65535) return fail(QLIN_ERR_SHAPE, "gate_proj: M=%lld too large", (long long)M);
+  return prod_launch(reinterpret_cast<const void*>(gate_proj_kernel),
+                     dim3(static_cast<unsigned>(NB), static_cast<unsigned>(M)), args, static_cast<cudaStream_t>(stream));
 }
 
 
@@ -2141,6 +2141,27 @@ int qlin_conv_state_update(const void* x, int64_t ldx, void* state, int64_t T, i
   return dec_launch(reinterpret_cast<const void*>(conv_state_update_kernel),
                     dim3(cb, static_cast<unsigned>(batch > 1 ? batch : 1)), dim3(kDecThreads), 0, 1, args,
                     static_cast<cudaStream_t>(stream));
+}
+
+int qlin_conv_silu_update(const void* x, int64_t ldx, const void* w, int64_t ks, void* state, void* y, int64_t batch,
+                          int64_t C, void* stream) {
+  if (batch < 0 || C < 0) return fail(QLIN_ERR_INVALID_ARGUMENT, "conv_silu_update: bad size");
+  if (ks != kConvKS) return fail(QLIN_ERR_SHAPE, "conv_silu_update: kernel width %lld (4 supported)", (long long)ks);
+  if (C % 8 != 0) return fail(QLIN_ERR_SHAPE, "conv_silu_update: channels must be a multiple of 8");
+  if (batch == 0 || C == 0) return QLIN_OK;
+  if (batch > 65535) return fail(QLIN_ERR_SHAPE, "conv_silu_update: batch too large");
+  if (!x || !w || !state || !y) return fail(QLIN_ERR_INVALID_ARGUMENT, "conv_silu_update: null pointer");
+  if (ldx < C) return fail(QLIN_ERR_SHAPE, "conv_silu_update: row stride smaller than C");
+  if (!aligned(x, 16) || ldx % 8 != 0 || !aligned(w, 16) || !aligned(state, 16) || !aligned(y, 16))
+    return fail(QLIN_ERR_ALIGNMENT, "conv_silu_update: 16-byte aligned rows required");
+  DevInfo di;
+  if (int r = launch_info(&di)) return r;
+  long long ldx_ = ldx;
+  int C_ = static_cast<int>(C);
+  void* args[] = {const_cast<void**>(&x), &ldx_, const_cast<void**>(&w), &state, &y, &C_};
+  const unsigned cb = static_cast<unsigned>((C / 8 + kDecThreads - 1) / kDecThreads);
+  return dec_launch(reinterpret_cast<const void*>(conv_silu_update_kernel), dim3(cb, static_cast<unsigned>(batch)),
+                    dim3(kDecThreads), 0, 1, args, static_cast<cudaStream_t>(stream));
 }
 
 

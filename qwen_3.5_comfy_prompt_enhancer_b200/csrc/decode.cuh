@@ -496,4 +496,53 @@ __global__ void __launch_bounds__(kDecThreads) conv_state_update_kernel(
   for (int j = 0; j < W; ++j) *reinterpret_cast<uint4*>(st + static_cast<long long>(j) * C) = v[j];
 }
 
+// conv_silu_kernel and conv_state_update_kernel of one decode step (batch
+// mode, one new row per candidate) in one launch: thread = 8 channels of
+// candidate b; it reads the candidate's 3 window rows and its input row,
+// writes y as conv_silu does, then the shifted window as conv_state_update
+// does.  No other thread touches these channels of this window.
+__global__ void __launch_bounds__(kDecThreads) conv_silu_update_kernel(
+    const __nv_bfloat16* __restrict__ x, long long ldx, const __nv_bfloat16* __restrict__ w,
+    __nv_bfloat16* __restrict__ state, __nv_bfloat16* __restrict__ y, int C) {
+  pdl_launch_dependents();
+  const int b = blockIdx.y;
+  const int c8 = blockIdx.x * kDecThreads + threadIdx.x;
+  if (8 * c8 >= C) return;
+  const int c0 = 8 * c8;
+  float wv[8][kConvKS];
+  {
+    const uint4* wp = reinterpret_cast<const uint4*>(w + static_cast<long long>(c0) * kConvKS);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float f[8];
+      bf16x8_to_f32(wp[i], f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) wv[2 * i + j / 4][j % 4] = f[j];
+    }
+  }
+  pdl_wait();
+  constexpr int W = kConvKS - 1;
+  __nv_bfloat16* st = state + static_cast<long long>(b) * W * C + c0;
+  uint4 raw[kConvKS];
+#pragma unroll
+  for (int j = 0; j < W; ++j) raw[j] = *reinterpret_cast<const uint4*>(st + static_cast<long long>(j) * C);
+  raw[W] = *reinterpret_cast<const uint4*>(x + static_cast<long long>(b) * ldx + c0);
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kConvKS; ++j) {
+    float xv[8];
+    bf16x8_to_f32(raw[j], xv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], __fmul_rn(xv[i], wv[i][j]));
+  }
+  float o[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i] = __fmul_rn(acc[i], sigmoid_ref(acc[i]));
+  store_bf16<8>(y + static_cast<long long>(b) * C + c0, o);
+#pragma unroll
+  for (int j = 0; j < W; ++j) *reinterpret_cast<uint4*>(st + static_cast<long long>(j) * C) = raw[j + 1];
+}
+
 }  // namespace qlin

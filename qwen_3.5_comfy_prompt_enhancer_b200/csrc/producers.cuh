@@ -247,69 +247,52 @@ __global__ void __launch_bounds__(kProdThreads) mul_quant_kernel(
 // kernels/norm.py:211-240: from the int8 activations of one row,
 //   x = a_q * a_s;  b = wb @ x;  av = wa @ x  (NB outputs each)
 //   beta = sigmoid(b);  g = -exp(A_log) * softplus(av + dt_bias)
-// One CTA per row; thread t owns 8-element chunks of K; NBT >= NB outputs
-// (16 or 32) accumulate in registers, then reduce over the CTA.
-template <int NBT>
+// One CTA per (output n, row): thread t owns 8-element chunks of K of both
+// weight rows, then the two dot products reduce over the CTA.  (One CTA per
+// row streamed both whole [NB, K] matrices through 4 SMs at decode batch 4.)
 __global__ void __launch_bounds__(kProdThreads) gate_proj_kernel(
     const int8_t* __restrict__ a_q, const float* __restrict__ a_s, int K, const __nv_bfloat16* __restrict__ wb,
     const __nv_bfloat16* __restrict__ wa, int NB, const __nv_bfloat16* __restrict__ dt_bias,
     const __nv_bfloat16* __restrict__ a_log, float* __restrict__ beta, float* __restrict__ gate) {
-  __shared__ float red[kProdThreads / 32][2 * NBT];
+  __shared__ float red[2][kProdThreads / 32];
   pdl_launch_dependents();
-  pdl_wait();
-  const int row = blockIdx.x;
+  const int n = blockIdx.x, row = blockIdx.y;
   const int G = K / kGroup;
-  float accb[NBT], acca[NBT];
-#pragma unroll
-  for (int n = 0; n < NBT; ++n) accb[n] = acca[n] = 0.0f;
+  const __nv_bfloat16* wbn = wb + static_cast<long long>(n) * K;
+  const __nv_bfloat16* wan = wa + static_cast<long long>(n) * K;
+  pdl_wait();
+  float accb = 0.0f, acca = 0.0f;
   for (int c = threadIdx.x; 8 * c < K; c += kProdThreads) {
     const uint2 raw = *reinterpret_cast<const uint2*>(a_q + static_cast<long long>(row) * K + 8 * c);
     const float sc = a_s[static_cast<long long>(row) * G + c / 8];
-    float x[8];
+    float fb[8], fa[8];
+    bf16x8_to_f32(*reinterpret_cast<const uint4*>(wbn + 8 * c), fb);
+    bf16x8_to_f32(*reinterpret_cast<const uint4*>(wan + 8 * c), fa);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const uint32_t word = j < 4 ? raw.x : raw.y;
-      const int8_t b = static_cast<int8_t>((word >> (8 * (j & 3))) & 0xFF);
-      x[j] = __fmul_rn(static_cast<float>(b), sc);
+      const float x = __fmul_rn(static_cast<float>(static_cast<int8_t>((word >> (8 * (j & 3))) & 0xFF)), sc);
+      accb = __fadd_rn(accb, __fmul_rn(fb[j], x));
+      acca = __fadd_rn(acca, __fmul_rn(fa[j], x));
     }
+  }
 #pragma unroll
-    for (int n = 0; n < NBT; ++n) {
-      if (n < NB) {
-        float fb[8], fa[8];
-        bf16x8_to_f32(*reinterpret_cast<const uint4*>(wb + static_cast<long long>(n) * K + 8 * c), fb);
-        bf16x8_to_f32(*reinterpret_cast<const uint4*>(wa + static_cast<long long>(n) * K + 8 * c), fa);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          accb[n] = __fadd_rn(accb[n], __fmul_rn(fb[j], x[j]));
-          acca[n] = __fadd_rn(acca[n], __fmul_rn(fa[j], x[j]));
-        }
-      }
-    }
+  for (int o = 16; o > 0; o >>= 1) {
+    accb = __fadd_rn(accb, __shfl_xor_sync(0xffffffffu, accb, o));
+    acca = __fadd_rn(acca, __shfl_xor_sync(0xffffffffu, acca, o));
   }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-#pragma unroll
-  for (int n = 0; n < NBT; ++n) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      accb[n] = __fadd_rn(accb[n], __shfl_xor_sync(0xffffffffu, accb[n], o));
-      acca[n] = __fadd_rn(acca[n], __shfl_xor_sync(0xffffffffu, acca[n], o));
-    }
-  }
   if (lane == 0) {
-#pragma unroll
-    for (int n = 0; n < NBT; ++n) {
-      red[warp][n] = accb[n];
-      red[warp][NBT + n] = acca[n];
-    }
+    red[0][warp] = accb;
+    red[1][warp] = acca;
   }
   __syncthreads();
-  const int n = threadIdx.x;
-  if (n < NB) {
+  if (threadIdx.x == 0) {
     float b = 0.0f, av = 0.0f;
 #pragma unroll
     for (int i = 0; i < kProdThreads / 32; ++i) {
-      b = __fadd_rn(b, red[i][n]);
-      av = __fadd_rn(av, red[i][NBT + n]);
+      b = __fadd_rn(b, red[0][i]);
+      av = __fadd_rn(av, red[1][i]);
     }
     const float dtb = __bfloat162float(dt_bias[n]);
     const float al = __bfloat162float(a_log[n]);

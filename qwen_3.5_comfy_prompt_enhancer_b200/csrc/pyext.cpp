@@ -519,6 +519,22 @@ int conv_state_update(const Tensor& x, const Tensor& state, int64_t T, int64_t b
   });
 }
 
+int conv_silu_update(const Tensor& x, const Tensor& w, const Tensor& state, const Tensor& y, int64_t batch) {
+  Call c;
+  c.need_rows(x, "x", at::kBFloat16);
+  c.need(w, "w", at::kBFloat16, 2);
+  c.need(state, "state", at::kBFloat16, 2);
+  c.need(y, "y", at::kBFloat16, 2);
+  const int64_t C = x.size(1);
+  if (w.size(0) != C || state.size(1) != C || y.size(1) != C || y.size(0) < batch || x.size(0) < batch ||
+      state.size(0) < 3 * batch)
+    throw py::value_error("conv_silu_update: x [B, C], w [C, ks], state [3B, C], y [B, C] required");
+  return c.launch([&](void* st) {
+    return qlin_conv_silu_update(x.data_ptr(), x.stride(0), w.data_ptr(), w.size(1), state.data_ptr(), y.data_ptr(),
+                                 batch, C, st);
+  });
+}
+
 int attn_prefill(const Tensor& q, const Tensor& kvc, const Tensor& out, int64_t T, int64_t pos0, const OptT& kvs,
                  bool kv_int8, int64_t nq, int64_t nkv, int64_t hd) {
   Call c;
@@ -581,6 +597,7 @@ PYBIND11_MODULE(_qlin_ext, m) {
   m.def("delta_decode", &delta_decode);
   m.def("conv_silu", &conv_silu);
   m.def("conv_state_update", &conv_state_update);
+  m.def("conv_silu_update", &conv_silu_update);
   m.def("attn_prefill", &attn_prefill);
   m.def("delta_prefill", &delta_prefill);
 }

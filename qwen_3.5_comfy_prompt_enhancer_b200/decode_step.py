@@ -6,8 +6,8 @@ quant_formats.py:270-275 does, int8 embedding with per-row scales, int8 or
 bf16 KV cache, fp32 delta-rule state, bf16 conv windows) and runs the
 engine's batched decode step, ``Engine.forward_batch`` (engine.py:342-375):
 B candidates at one shared position, every layer through the same kernel
-calls as engine.py:291-340 -- rmsnorm_quant, proj3, gate_proj, conv_silu,
-conv_state_update, delta_decode, norm_gated_quant, qk_norm_rope, attn_decode,
+calls as engine.py:291-340 -- rmsnorm_quant, proj3, gate_proj, conv_silu and
+conv_state_update (in one launch), delta_decode, norm_gated_quant, qk_norm_rope, attn_decode,
 gate_mul_quant, mlp_gate_up_quant, gemm_i8 with the residual in place -- and
 the int8 lm_head.  Every kernel is this package's own (the embedding gather is
 two torch ops, as in the engine).
@@ -123,7 +123,7 @@ class HybridStack:
         self.gate = torch.empty(B, NH, dtype=torch.float32, **e)
         self.logits = torch.empty(B, V, dtype=torch.bfloat16, **e)
         # kernel launches of one step (the embedding's two torch ops aside)
-        self.launches = sum(8 if t == "linear" else 6 for t in self.types) + 3 * len(self.types) + 2
+        self.launches = sum(7 if t == "linear" else 6 for t in self.types) + 3 * len(self.types) + 2
 
     # ------------------------------------------------------------------ layers
     def _linear(self, L, li, pos):
@@ -133,8 +133,8 @@ class HybridStack:
         norm.gate_proj(self.xq, self.xs, L["b"], L["a"], self.beta, self.gate, L["dt"], L["alog"])
         mixed_in = self.proj[:, :self.conv_dim]
         cst = self.cstate[li].view(B * (self.cfg["conv"] - 1), self.conv_dim)
-        linear_attn.conv_silu(mixed_in, L["conv"], cst, self.mixed, B, batch=True)
-        linear_attn.conv_state_update(mixed_in, cst, B, batch=B)
+        # conv_silu + conv_state_update (engine.py:302-303) in one launch
+        linear_attn.conv_silu_update(mixed_in, L["conv"], cst, self.mixed, B)
         dst = self.dstate[li].view(B * self.NH, self.DK, self.DV)
         linear_attn.delta_decode(self.mixed, self.gate, self.beta, dst, self.dout, batch=B)
         norm.norm_gated_quant(self.dout, self.proj[:, self.conv_dim:], L["norm_w"], self.lq, self.ls, self.eps)

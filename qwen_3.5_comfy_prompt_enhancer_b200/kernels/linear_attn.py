@@ -42,3 +42,15 @@ def delta_prefill(qkv, g, beta, state, out, T, vs=32, chunk=32):
     if rc:
         raise _lib.QlinError("qlin_delta_prefill", rc)
     return out
+
+
+def conv_silu_update(x, w, state, y, batch):
+    """``conv_silu(x, w, state, y, batch, batch=True)`` followed by
+    ``conv_state_update(x, state, batch, batch=batch)`` in one launch (one
+    decode row per candidate); identical results.  Not in the reference,
+    whose engine makes the two calls back to back (engine.py:302-303).
+    Returns ``y``."""
+    rc = _lib.ext().conv_silu_update(x, w, state, y, int(batch))
+    if rc:
+        raise _lib.QlinError("qlin_conv_silu_update", rc)
+    return y

@@ -260,3 +260,20 @@ def test_conv_vs_reference_golden(pkg, dev, i):
     torch.cuda.synchronize()
     assert_bf16_close(bits(y), GOLD[p + "y"], f"golden conv {i}")
     np.testing.assert_array_equal(bits(st), GOLD[p + "state_out"])
+
+
+@pytest.mark.parametrize("B", [1, 4])
+def test_conv_silu_update_equals_the_two_calls(pkg, dev, B):
+    g = torch.Generator().manual_seed(2350 + B)
+    xw = rand_bf16(g, (B, CONV + 2048)).to(dev)
+    x = xw[:, :CONV]
+    w = rand_bf16(g, (CONV, 4), 0.1).to(dev)
+    state = rand_bf16(g, (3 * B, CONV)).to(dev)
+    s1, s2 = state.clone(), state.clone()
+    y1 = torch.empty(B, CONV, dtype=torch.bfloat16, device=dev)
+    y2 = torch.empty_like(y1)
+    pkg.conv_silu(x, w, s1, y1, B, batch=True)
+    pkg.conv_state_update(x, s1, B, batch=B)
+    pkg.kernels.linear_attn.conv_silu_update(x, w, s2, y2, B)
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2) and torch.equal(s1, s2)
