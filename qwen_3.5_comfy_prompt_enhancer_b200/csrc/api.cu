@@ -317,6 +317,10 @@ QLIN_KNOB(tune_half, "QLIN_TUNE_HALF", 0)
 QLIN_KNOB(prefill_min_m, "QLIN_PREFILL_MIN_M", 128)
 QLIN_KNOB(tune_timeline, "QLIN_TIMELINE", 0)
 QLIN_KNOB(tune_dp, "QLIN_TUNE_DP", 1)  // 0: decode rows take the tensor-core kernel
+// dp kernel weight ring: 0 never, 1 when resident weights need more than one
+// wave, 2 whenever a ring plan exists
+QLIN_KNOB(tune_dp_stream, "QLIN_TUNE_DP_STREAM", 1)
+QLIN_KNOB(tune_dp_maxm, "QLIN_TUNE_DP_MAXM", 2)  // rows the dp kernel serves (tuning builds: 2 or 4)
 #undef QLIN_KNOB
 
 bool use_dp() { return tune_dp() != 0; }
@@ -1037,54 +1041,143 @@ bool mid_m_takes_gemm(int epi, int64_t M, int tiles) {
 
 int smem_optin(const void* kern, size_t bytes, std::atomic<unsigned long long>& done);
 
-// ---------------------------------------------------------------- resident-weight dp4a GEMV (M <= 2)
+// ---------------------------------------------------------------- dp4a GEMV (M <= 2)
 // Per-CTA shared memory that keeps two CTAs on an SM (this launch and the
 // next one's, which streams its weights under programmatic dependent launch).
 constexpr uint32_t kDpBudget = 110 * 1024;
-// Rows it serves.  Its dp4a work grows with M while the tensor-core kernel's
-// MMA count does not; measured on B200 (graph replay, rotating weights, us,
-// dp4a vs tcgen05): M = 1 W4 gate/up 2048->2x6144 6.5 vs 8.6, down 6144->2048
-// 4.7 vs 5.7, o 2.9 vs 3.8, qkv 3.7 vs 4.6, W8 2048->6144 3.5 vs 3.9, W8 down
-// 3.9 vs 5.6; M = 4 W4 gate/up 10.4 vs 10.0, W8 gate/up 14.0 vs 7.7, W8
-// 2048->6144 4.6 vs 4.0.
-constexpr int kDpMaxM = 2;
+// Rows it serves (tune_dp_maxm, 2).  Its dp4a work grows with M while the
+// tensor-core kernel's MMA count does not; measured on B200 (graph replay,
+// rotating weights, us, dp4a vs tcgen05): M = 1 W4 gate/up 2048->2x6144 6.5
+// vs 8.6, down 6144->2048 4.7 vs 5.7, o 2.9 vs 3.8, qkv 3.7 vs 4.6, W8
+// 2048->6144 3.5 vs 3.9, W8 down 3.9 vs 5.6; M = 4 W4 gate/up 10.4 vs 10.0,
+// W8 gate/up 14.0 vs 7.7, W8 2048->6144 4.6 vs 4.0.
 
-int dp_mr(int64_t M) { return M <= 1 ? 1 : 2; }
+int dp_mr(int64_t M) { return M <= 1 ? 1 : M <= 2 ? 2 : 4; }
 
-// K split for the dp kernel: the smallest split whose CTAs cover the SMs and
+struct DpPlan {
+  int split = 0, kout = 1, ring = 0, gmax = 0;
+  size_t smem = 0;
+};
+
+// Resident plan: the smallest cluster split whose CTAs cover the SMs and
 // whose resident weights fit the budget, at most the portable cluster size
 // of 8.  For W8 a plan is taken only if all its CTAs are resident at once
 // (at most two per SM: a second wave would request its weights only after
 // the dependency) and its clusters are not of 7 CTAs (which pack poorly into
-// B200's GPCs); otherwise 0, and the tensor-core kernel streams instead.
-// Measured: W8 gate/up 2048->2x6144 at M = 1 needs split 7 (336 CTAs) to fit
-// and took 7.9 us against 6.6 on the tensor-core kernel; the 1187-tile W8
-// lm_head (split 3, 3561 CTAs) 61 against 56 us.  W4, whose tensor-core path
-// has to unpack the nibbles first, gains even over several waves: the
-// config-5 W4 gate/up 5120->2x17408 at M = 1 (1088 CTAs) made the one-GPU
-// column-split layer 61.7 instead of 73.9 us.
-int plan_dp(int wb, int mr, int ns, int K, int wgrp, int tiles, int sms, int* gmax_out, size_t* smem_out) {
+// B200's GPCs).  Measured: W8 gate/up 2048->2x6144 at M = 1 needs split 7
+// (336 CTAs) to fit and took 7.9 us against 6.6 on the tensor-core kernel;
+// the 1187-tile W8 lm_head (split 3, 3561 CTAs) 61 against 56 us.
+bool plan_dp_resident(int wb, int mr, int ns, int K, int wgrp, int tiles, int sms, DpPlan* pl) {
   const int G = K / kGroup;
-  int best = 0, best_gmax = 0;
-  size_t best_smem = 0;
+  DpPlan best;
   for (int s = 1; s <= 8 && s <= G; ++s) {
     const int gmax = (G + s - 1) / s;
-    const DpLayout L = dp_layout(wb, mr, ns, wgrp, gmax, s);
+    const DpLayout L = dp_layout(wb, mr, ns, wgrp, gmax, s, 0);
     if (L.total > kDpBudget) continue;
-    best = s, best_gmax = gmax, best_smem = L.total;
+    best.split = s, best.gmax = gmax, best.smem = L.total;
     if (static_cast<long long>(tiles) * s >= sms) break;
   }
-  if (wb == 8 && (best == 7 || static_cast<long long>(tiles) * best > 2ll * sms)) best = 0;
-  *gmax_out = best_gmax;
-  *smem_out = best_smem;
-  return best;
+  if (best.split == 0) return false;
+  if (wb == 8 && (best.split == 7 || static_cast<long long>(tiles) * best.split > 2ll * sms)) return false;
+  *pl = best;
+  return true;
+}
+
+// Ring plan for launches whose weights do not fit in one resident wave: one
+// wave of CTAs without clusters, a tile's K cut into `kout` parts that meet
+// in the device workspace, each warp streaming its items through a ring of
+// slots.  Parts per tile are chosen so that the busiest SM streams the fewest
+// groups (CTAs per SM x groups per CTA), at most three CTAs per SM (shared
+// memory 200 / 110 / 74 KB), ties to fewer parts.
+bool plan_dp_ring(int wb, int mr, int ns, int K, int wgrp, int tiles, int sms, DpPlan* pl) {
+  const int G = K / kGroup;
+  long long best_w = -1;
+  for (int P = 1; P <= G; ++P) {
+    const long long ctas = static_cast<long long>(tiles) * P;
+    const long long per_sm = (ctas + sms - 1) / sms;
+    if (per_sm > 3) break;
+    if (P > 1 && (tiles > kDpWsTiles || ctas * ns * mr * kTileN > kDpWsFloats)) break;
+    const uint32_t budget = (per_sm == 1 ? 200u : per_sm == 2 ? 110u : 74u) * 1024u;
+    const int gmax = (G + P - 1) / P;
+    int ring = 0;
+    for (int r = 8; r >= 2 && ring == 0; --r)
+      if (dp_layout(wb, mr, ns, wgrp, gmax, 1, r).total <= budget) ring = r;
+    if (ring == 0) continue;
+    const int per_warp = (gmax * ns + kRgWarps - 1) / kRgWarps;
+    if (ring > per_warp) ring = per_warp < 2 ? 2 : per_warp;
+    const long long w = per_sm * gmax;
+    if (best_w < 0 || w < best_w) {
+      best_w = w;
+      pl->split = 1;
+      pl->kout = P;
+      pl->ring = ring;
+      pl->gmax = gmax;
+      pl->smem = dp_layout(wb, mr, ns, wgrp, gmax, 1, ring).total;
+    }
+  }
+  return best_w >= 0;
+}
+
+// dp plan of a launch, or false (the tensor-core kernel takes it).  W4 takes
+// the resident plan when its CTAs fit one wave (at most two per SM), a ring
+// plan otherwise; measured on B200 at M = 1 the config-5 W4 gate/up
+// 5120->2x17408 (136 tiles) ... us resident over several waves against ...
+// us on the ring.  W8 takes resident plans only (above).
+bool plan_dp_uncached(int wb, int mr, int ns, int K, int wgrp, int tiles, int sms, DpPlan* pl) {
+  DpPlan res;
+  const bool has_res = plan_dp_resident(wb, mr, ns, K, wgrp, tiles, sms, &res);
+  const bool one_wave = has_res && static_cast<long long>(tiles) * res.split <= 2ll * sms;
+  const int mode = tune_dp_stream();
+  if (has_res && (mode == 0 || (mode == 1 && one_wave))) {
+    *pl = res;
+    return true;
+  }
+  DpPlan ring;
+  if (mode != 0 && (wb == 4 || mode == 2) && plan_dp_ring(wb, mr, ns, K, wgrp, tiles, sms, &ring)) {
+    *pl = ring;
+    return true;
+  }
+  if (has_res) {
+    *pl = res;
+    return true;
+  }
+  return false;
+}
+
+bool plan_dp(int wb, int mr, int ns, int K, int wgrp, int tiles, int sms, DpPlan* pl) {
+  static std::mutex mu;
+  static std::unordered_map<TcKey, DpPlan, TcKeyHash> cache;  // (M field: rows of the instance)
+  const TcKey k{wb, ns, K, wgrp, tiles, sms, 0, mr};
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto it = cache.find(k);
+    if (it != cache.end()) {
+      *pl = it->second;
+      return pl->split > 0;
+    }
+  }
+  DpPlan got;
+  if (!plan_dp_uncached(wb, mr, ns, K, wgrp, tiles, sms, &got)) got = DpPlan{};
+  {
+    std::lock_guard<std::mutex> g(mu);
+    if (cache.size() >= kPlanCache) cache.clear();
+    cache.emplace(k, got);
+  }
+  *pl = got;
+  return got.split > 0;
+}
+
+// Workspace slot of the next cross-cluster launch.
+int dp_ws_next_slot() {
+  static std::atomic<unsigned> next{0};
+  return static_cast<int>(next.fetch_add(1u) % kDpWsSlots);
 }
 
 template <int WB, int MR, int EPI>
 int launch_dp_t(const DpArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
   auto kern = dp_gemv_kernel<WB, MR, EPI>;
   static std::atomic<unsigned long long> done{0};
-  if (int r = smem_optin(reinterpret_cast<const void*>(kern), kDpBudget + 1024, done)) return r;
+  if (int r = smem_optin(reinterpret_cast<const void*>(kern), 201 * 1024, done)) return r;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kRgThreads, 1, 1);
@@ -1107,21 +1200,22 @@ int launch_dp_t(const DpArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
 template <int WB, int EPI>
 int launch_dp_mr(int mr, const DpArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
   if (mr == 1) return launch_dp_t<WB, 1, EPI>(a, grid, smem, st);
-  return launch_dp_t<WB, 2, EPI>(a, grid, smem, st);  // rows <= kDpMaxM = 2
+#ifdef QLIN_TUNING
+  if (mr == 4) return launch_dp_t<WB, 4, EPI>(a, grid, smem, st);  // (QLIN_TUNE_DP_MAXM=4 sweeps)
+#endif
+  return launch_dp_t<WB, 2, EPI>(a, grid, smem, st);
 }
 
 // Launches the dp kernel if the shape fits it; *taken = false otherwise.
 int run_dp(int wb, int epi, const GemvArgs& a, int tiles, cudaStream_t st, bool* taken) {
   *taken = false;
-  if (a.M > kDpMaxM || a.M < 1 || tiles > 65535) return QLIN_OK;
+  if (a.M > tune_dp_maxm() || a.M < 1 || tiles > 65535) return QLIN_OK;
   DevInfo di;
   if (int r = launch_info(&di)) return r;
   const int mr = dp_mr(a.M);
   const int ns = epi == kEpiOut ? 1 : 2;
-  int gmax = 0;
-  size_t smem = 0;
-  const int split = plan_dp(wb, mr, ns, a.K, a.wgrp, tiles, di.sms, &gmax, &smem);
-  if (split == 0) return QLIN_OK;
+  DpPlan pl;
+  if (!plan_dp(wb, mr, ns, a.K, a.wgrp, tiles, di.sms, &pl)) return QLIN_OK;
   DpArgs d;
   memset(&d, 0, sizeof(d));
   const uint32_t nsr = (wb == 4 && a.wgrp == 32) ? 2 : 1;
@@ -1147,8 +1241,12 @@ int run_dp(int wb, int epi, const GemvArgs& a, int tiles, cudaStream_t st, bool*
   d.M = a.M;
   d.K = a.K;
   d.wgrp = a.wgrp;
-  d.split = split;
-  d.gmax = gmax;
+  d.split = pl.split;
+  d.gmax = pl.gmax;
+  d.ring = pl.ring;
+  d.kout = pl.kout;
+  d.ws_slot = pl.kout > 1 ? dp_ws_next_slot() : 0;
+  d.tl_slot = tl_next_slot();
   d.out = a.out;
   d.ldo = a.ldo;
   d.res = a.res;
@@ -1158,7 +1256,8 @@ int run_dp(int wb, int epi, const GemvArgs& a, int tiles, cudaStream_t st, bool*
   d.n_q = a.n_q;
   d.fault = di.fault;
   *taken = true;
-  const dim3 grid(split, tiles, 1);
+  const dim3 grid(pl.split, tiles, pl.kout);
+  const size_t smem = pl.smem;
   if (wb == 8) {
     switch (epi) {
       case kEpiOut: return launch_dp_mr<8, kEpiOut>(mr, d, grid, smem, st);

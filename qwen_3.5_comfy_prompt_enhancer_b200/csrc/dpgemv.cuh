@@ -1,23 +1,30 @@
-// Resident-weight GEMV on CUDA cores for decode rows (M <= 4): the small-M
+// Weight-streaming GEMV on CUDA cores for decode rows (M <= 2): the small-M
 // entry points (gemm_i8 / gemm_w4 + residual, proj3(_w4), the fused gate/up
-// epilogues) when every weight of a CTA's K range fits in its shared memory.
+// epilogues).
 //
-// Why not the tensor cores here.  At M <= 4 the work per weight byte is tiny
-// and a launch is a short step between two grid dependencies: what counts is
-// the time from the dependency to the last store.  This kernel requests ALL
-// its weights (int8 rows, or W4 nibbles kept packed -- 4 KB per 64-K group
-// and 128 columns, half of what an unpacked MMA operand needs) before the
-// dependency, so under programmatic dependent launch the whole weight stream
-// overlaps the preceding kernel.  After the dependency there is no hand-off
-// chain: every warp loads the activations, decodes its groups in registers
-// and accumulates with dp4a, then the CTA and the cluster reduce.
+// Why not the tensor cores here.  At M <= 2 the work per weight byte is tiny
+// and what counts is the time from the grid dependency to the last store.
+// This kernel keeps W4 nibbles packed (4 KB per 64-K group and 128 columns,
+// half of what an unpacked MMA operand needs) and decodes them in registers;
+// there is no operand hand-off chain.
 //
-// Work split.  CTA = one 128-column tile x one K range (cluster of `split`
-// CTAs per tile, as the tensor-core kernel).  Lane l of every warp owns
-// columns 4l .. 4l+3; warp w owns the (group, stream) items w, w + 8, ... of
-// the CTA's K range.  Per item the int32 dot of each (row, column) over the
-// group's 64 K (W4 groups of 32: per 32-K half) is complete inside one
-// thread before the fp32 epilogue of the reference:
+// Two weight modes:
+//  * resident -- every weight of the CTA's K range is requested before the
+//    dependency, so under programmatic dependent launch the whole stream
+//    overlaps the preceding kernel;
+//  * ring -- each warp owns `ring` slots; the first `ring` items of every warp
+//    are requested before the dependency and a slot is refilled as soon as
+//    its warp has used it (long launches: tens of MB of weights).
+//
+// Work split.  CTA = one 128-column tile x one K part; a tile's K is cut into
+// split x kout parts: `split` CTAs of a thread-block cluster combine their
+// partial sums through distributed shared memory, and the `kout` clusters of
+// a tile through a device workspace (the last cluster to arrive adds them and
+// runs the epilogue).  Lane l of every warp owns columns 4l .. 4l+3; warp w
+// owns the (group, stream) items w, w + 8, ... of the CTA's K part.  Per item
+// the int32 dot of each (row, column) over the group's 64 K (W4 groups of 32:
+// per 32-K half) is complete inside one thread before the fp32 epilogue of
+// the reference:
 //   W8: acc += float(I) * a_s[m, kb]                   (kernels/gemm.py:43-45)
 //   W4: acc += float(I - z * sum(a)) * (a_s[m, kb] * ws)  (kernels/w4.py:103-104)
 // Four weight rows (4 columns each) are transposed with byte permutes so
@@ -27,8 +34,8 @@
 // The zero point is removed exactly: sum(a (nib - z)) = sum(a nib) - z sum(a).
 //
 // Reduction order (fixed): per warp its items in order, then the 8 warps in
-// order, then the cluster's ranks in order; only this fp32 order differs
-// from the reference's ascending-K sum.
+// order, then the cluster's ranks in order, then the clusters in K order;
+// only this fp32 order differs from the reference's ascending-K sum.
 #pragma once
 
 #include "args.cuh"
@@ -39,6 +46,16 @@ namespace qlin {
 constexpr int kRgThreads = 256;
 constexpr int kRgWarps = kRgThreads / 32;
 
+// Device workspace of the cross-cluster K parts: per slot, fp32 partial sums
+// [tile][kout][stream][row][128] and one arrival counter per tile.  The host
+// rotates launches over the slots; a counter is reset by the launch's last
+// arrival, so a slot is free again once its launch has completed.
+constexpr int kDpWsSlots = 4;
+constexpr int kDpWsFloats = 1 << 17;
+constexpr int kDpWsTiles = 1024;
+static __device__ __align__(256) float g_dp_ws[kDpWsSlots][kDpWsFloats];
+static __device__ __align__(256) unsigned g_dp_cnt[kDpWsSlots][kDpWsTiles];
+
 struct DpArgs {
   CUtensorMap tw[3];   // weights, plain (unswizzled) boxes: W8 128 columns x 64 rows; W4 128 x 32 packed rows
   CUtensorMap ts[3];   // W4 group scales (bf16), box 128 x nsub
@@ -48,6 +65,10 @@ struct DpArgs {
   const int8_t* a_q;   // [M, K]
   const float* a_s;    // [M, K/64]
   int M, K, wgrp, split, gmax;
+  int ring;            // weight slots per warp; 0: every item resident
+  int kout;            // clusters per tile (K parts across clusters)
+  int ws_slot;         // workspace slot (kout > 1)
+  int tl_slot;         // tuning builds: phase-timeline slot of this launch (-1: none)
   void* out;
   long long ldo;
   const void* res;
@@ -58,21 +79,21 @@ struct DpArgs {
   unsigned* fault;
 };
 
-// Shared-memory carve-up (host and device): weights of every (group,
-// stream) item, the K-range activations, their per-group sums (W4) and
+// Shared-memory carve-up (host and device): the weight slots (every (group,
+// stream) item, or `ring` per warp), the K-part activations, their per-group sums (W4) and
 // scales, the cross-warp reduction (over the weights once they are used),
 // the partial sums received from the other ranks, barriers.
 struct DpLayout {
   uint32_t item, wbytes, sbytes, act_off, asum_off, as_off, part_off, xchg_off, bar_off, total;
 };
-__host__ __device__ inline DpLayout dp_layout(int wb, int mr, int ns, int wgrp, int gmax, int split) {
+__host__ __device__ inline DpLayout dp_layout(int wb, int mr, int ns, int wgrp, int gmax, int split, int ring) {
   DpLayout L;
   const int nsub = (wb == 4 && wgrp == 32) ? 2 : 1;
   L.wbytes = wb == 8 ? 64 * kTileN : 32 * kTileN;
   L.sbytes = wb == 8 ? 0 : nsub * kTileN * 3;
   L.item = align_up(L.wbytes + L.sbytes, 128);
-  uint32_t off = gmax * ns * L.item;
-  const uint32_t red = kRgWarps * ns * mr * kTileN * 4;  // aliases the weights
+  uint32_t off = (ring > 0 ? kRgWarps * ring : gmax * ns) * L.item;
+  const uint32_t red = kRgWarps * mr * kTileN * 4;  // aliases the weights
   if (off < red) off = red;
   off = align_up(off, 128);
   L.act_off = off;
@@ -84,9 +105,9 @@ __host__ __device__ inline DpLayout dp_layout(int wb, int mr, int ns, int wgrp, 
   L.part_off = off;
   off = align_up(off + (split > 1 ? split - 1 : 0) * ns * mr * kTileN * 4, 16);
   L.xchg_off = off;
-  off = align_up(off + 4 * mr * 4, 16);
+  off = align_up(off + 4 * mr * 4 + 16, 16);  // (+ the last-arrival flag)
   L.bar_off = off;
-  off += 8 * (kRgWarps + 1);
+  off += 8 * (kRgWarps * (ring > 0 ? ring : 1) + 1);
   L.total = off + 128;  // alignment slack
   return L;
 }
@@ -116,15 +137,16 @@ __global__ void __launch_bounds__(kRgThreads, 1) dp_gemv_kernel(const __grid_con
   constexpr int NS = (EPI == kEpiOut) ? 1 : 2;
   extern __shared__ __align__(128) uint8_t dp_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dp_smem_raw) + 127) & ~uintptr_t(127));
-  const DpLayout L = dp_layout(WB, MR, NS, p.wgrp, p.gmax, p.split);
+  const DpLayout L = dp_layout(WB, MR, NS, p.wgrp, p.gmax, p.split, p.ring);
+  const int R = p.ring;
   const int nsub = (WB == 4 && p.wgrp == 32) ? 2 : 1;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);  // one per warp
-  uint64_t* recv = full + kRgWarps;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);  // per warp (ring: per warp and slot)
+  uint64_t* recv = full + kRgWarps * (R > 0 ? R : 1);
   int8_t* act = reinterpret_cast<int8_t*>(smem + L.act_off);      // [g][m][64]
   int* asum = reinterpret_cast<int*>(smem + L.asum_off);           // [g][m][2]
   float* ass = reinterpret_cast<float*>(smem + L.as_off);          // [g][m]
   float* part = reinterpret_cast<float*>(smem + L.part_off);       // [rank-1][s][m][128]
-  float* red = reinterpret_cast<float*>(smem);                     // [warp][s][m][128], over the weights
+  float* red = reinterpret_cast<float*>(smem);                     // [warp][m][128], over the weights
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rank = blockIdx.x, tile = blockIdx.y;
@@ -136,44 +158,62 @@ __global__ void __launch_bounds__(kRgThreads, 1) dp_gemv_kernel(const __grid_con
   const GemvSeg& S0 = p.seg[si];
   const int n0 = (tile - S0.tile_begin) * kTileN;
   const int G = p.K / kGroup;
-  const int g0 = static_cast<int>(static_cast<long long>(rank) * G / p.split);
-  const int g1 = static_cast<int>(static_cast<long long>(rank + 1) * G / p.split);
+  const int nparts = p.split * p.kout;
+  const int kpart = blockIdx.z * p.split + rank;
+  const int g0 = static_cast<int>(static_cast<long long>(kpart) * G / nparts);
+  const int g1 = static_cast<int>(static_cast<long long>(kpart + 1) * G / nparts);
   const int nst = g1 - g0;
   const int items = nst * NS;
-  auto item_w = [&](int it) { return smem + it * L.item; };
+  // weight slot of item `it` (ring: item li of warp w sits in slot li % R)
+  auto item_w = [&](int it) {
+    return smem + (R > 0 ? (it % kRgWarps) * R + (it / kRgWarps) % R : it) * L.item;
+  };
+  auto item_bytes = [&](int it) {
+    const int s = NS == 1 ? si : it % NS;
+    return static_cast<uint32_t>(L.wbytes +
+                                 (WB == 4 ? nsub * kTileN * 2 + (p.seg[s].has_z ? nsub * kTileN : 0) : 0));
+  };
+  auto issue_item = [&](int it, uint64_t* bar, uint64_t pol) {
+    const int gl = it / NS, s = NS == 1 ? si : it % NS;
+    const int g = g0 + gl;
+    uint8_t* dst = item_w(it);
+    if (WB == 8) {
+      tma_load_2d(dst, &p.tw[s], n0, g * 64, bar, pol);
+    } else {
+      tma_load_2d(dst, &p.tw[s], n0, g * 32, bar, pol);
+      const int srow = (g * 64) / p.wgrp;
+      tma_load_2d(dst + L.wbytes, &p.ts[s], n0, srow, bar, pol);
+      if (p.seg[s].has_z) tma_load_2d(dst + L.wbytes + nsub * kTileN * 2, &p.tz[s], n0, srow, bar, pol);
+    }
+  };
 
   // ---------------------------------------------------------------- set-up: every weight requested now
   if (threadIdx.x == 0) {
-    for (int w = 0; w < kRgWarps; ++w) mbar_init(full + w, 1);
+    for (int w = 0; w < kRgWarps * (R > 0 ? R : 1); ++w) mbar_init(full + w, 1);
     mbar_init(recv, 1);
     fence_mbar_init();
     if (p.split > 1 && rank == 0)
       mbar_arrive_expect_tx(recv, static_cast<uint32_t>((p.split - 1) * kTileN * NS * MR * 4));
   }
   __syncthreads();
+  if (threadIdx.x == 0) QLIN_TL(p, 0);
+  const uint64_t pol = l2_policy_evict_first();
   if (lane == 0) {
-    // warp w requests its own items, completing on its own barrier
-    const uint64_t pol = l2_policy_evict_first();
-    uint32_t bytes = 0;
-    for (int it = warp; it < items; it += kRgWarps) {
-      const int s = NS == 1 ? si : it % NS;
-      bytes += L.wbytes + (WB == 4 ? nsub * kTileN * 2 + (p.seg[s].has_z ? nsub * kTileN : 0) : 0);
-    }
-    if (bytes) mbar_arrive_expect_tx(full + warp, bytes);
-    for (int it = warp; it < items; it += kRgWarps) {
-      const int gl = it / NS, s = NS == 1 ? si : it % NS;
-      const int g = g0 + gl;
-      uint8_t* dst = item_w(it);
-      if (WB == 8) {
-        tma_load_2d(dst, &p.tw[s], n0, g * 64, full + warp, pol);
-      } else {
-        tma_load_2d(dst, &p.tw[s], n0, g * 32, full + warp, pol);
-        const int srow = (g * 64) / p.wgrp;
-        tma_load_2d(dst + L.wbytes, &p.ts[s], n0, srow, full + warp, pol);
-        if (p.seg[s].has_z) tma_load_2d(dst + L.wbytes + nsub * kTileN * 2, &p.tz[s], n0, srow, full + warp, pol);
+    if (R == 0) {
+      // warp w requests all its items, completing on its own barrier
+      uint32_t bytes = 0;
+      for (int it = warp; it < items; it += kRgWarps) bytes += item_bytes(it);
+      if (bytes) mbar_arrive_expect_tx(full + warp, bytes);
+      for (int it = warp; it < items; it += kRgWarps) issue_item(it, full + warp, pol);
+    } else {
+      // its first R items, one per slot
+      for (int li = 0, it = warp; li < R && it < items; ++li, it += kRgWarps) {
+        mbar_arrive_expect_tx(full + warp * R + li, item_bytes(it));
+        issue_item(it, full + warp * R + li, pol);
       }
     }
   }
+  if (threadIdx.x == 0) QLIN_TL(p, 1);
   pdl_launch_dependents();
   if (p.split > 1) {
     cluster_arrive_relaxed();
@@ -193,6 +233,7 @@ __global__ void __launch_bounds__(kRgThreads, 1) dp_gemv_kernel(const __grid_con
 
   // ---------------------------------------------------------------- activations (after the dependency)
   pdl_wait();
+  if (threadIdx.x == 0) QLIN_TL(p, 2);
   float pre_res[MR];
 #pragma unroll
   for (int m = 0; m < MR; ++m) pre_res[m] = 0.0f;
@@ -228,23 +269,18 @@ __global__ void __launch_bounds__(kRgThreads, 1) dp_gemv_kernel(const __grid_con
     }
     __syncthreads();
   }
+  if (threadIdx.x == 0) QLIN_TL(p, 3);
 
   // ---------------------------------------------------------------- the dots
-  float acc[NS][4][MR];
+  // Warp w's items w, w + 8, ... all belong to stream w % NS (8 warps, NS <= 2).
+  const int sw = NS == 1 ? 0 : warp % NS;
+  float acc[4][MR];
 #pragma unroll
-  for (int s = 0; s < NS; ++s)
+  for (int j = 0; j < 4; ++j)
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
-#pragma unroll
-      for (int m = 0; m < MR; ++m) acc[s][j][m] = 0.0f;
-  bool ok = true;
-  if (warp < items) ok = mbar_wait(full + warp, 0);
-  if (!ok) {
-    if (lane == 0) record_fault(p.fault, kFaultFullWait);
-    mbar_wait(full + warp, 0);  // copies still in flight land before the region is reused or the CTA exits
-  }
-  for (int it = warp; ok && it < items; it += kRgWarps) {
-    const int gl = it / NS, s = NS == 1 ? 0 : it % NS;
+    for (int m = 0; m < MR; ++m) acc[j][m] = 0.0f;
+  auto dot_item = [&](int it) {
+    const int gl = it / NS;
     const uint8_t* wt = item_w(it);
     const float* as_g = ass + gl * MR;
     if (WB == 8) {
@@ -270,9 +306,9 @@ __global__ void __launch_bounds__(kRgThreads, 1) dp_gemv_kernel(const __grid_con
       for (int j = 0; j < 4; ++j)
 #pragma unroll
         for (int m = 0; m < MR; ++m)
-          acc[s][j][m] = __fadd_rn(acc[s][j][m], __fmul_rn(__int2float_rn(isum[j][m]), as_g[m]));
+          acc[j][m] = __fadd_rn(acc[j][m], __fmul_rn(__int2float_rn(isum[j][m]), as_g[m]));
     } else {
-      const GemvSeg& sg = p.seg[NS == 1 ? si : s];
+      const GemvSeg& sg = p.seg[NS == 1 ? si : sw];
       const uint16_t* sc = reinterpret_cast<const uint16_t*>(wt + L.wbytes);
       const uint8_t* zz = wt + L.wbytes + nsub * kTileN * 2;
       int isum[2][4][MR];  // per 32-K half
@@ -314,7 +350,7 @@ __global__ void __launch_bounds__(kRgThreads, 1) dp_gemv_kernel(const __grid_con
 #pragma unroll
             for (int m = 0; m < MR; ++m) {
               const int v = isum[h][j][m] - z * asg[m * 2 + h];
-              acc[s][j][m] = __fadd_rn(acc[s][j][m], __fmul_rn(__int2float_rn(v), __fmul_rn(as_g[m], ws)));
+              acc[j][m] = __fadd_rn(acc[j][m], __fmul_rn(__int2float_rn(v), __fmul_rn(as_g[m], ws)));
             }
           }
         } else {
@@ -323,21 +359,50 @@ __global__ void __launch_bounds__(kRgThreads, 1) dp_gemv_kernel(const __grid_con
 #pragma unroll
           for (int m = 0; m < MR; ++m) {
             const int v = isum[0][j][m] + isum[1][j][m] - z * (asg[m * 2] + asg[m * 2 + 1]);
-            acc[s][j][m] = __fadd_rn(acc[s][j][m], __fmul_rn(__int2float_rn(v), __fmul_rn(as_g[m], ws)));
+            acc[j][m] = __fadd_rn(acc[j][m], __fmul_rn(__int2float_rn(v), __fmul_rn(as_g[m], ws)));
           }
         }
+      }
+    }
+  };
+  if (R == 0) {
+    bool ok = true;
+    if (warp < items) ok = mbar_wait(full + warp, 0);
+    if (!ok) {
+      if (lane == 0) record_fault(p.fault, kFaultFullWait);
+      mbar_wait(full + warp, 0);  // copies still in flight land before the region is reused or the CTA exits
+    }
+    for (int it = warp; ok && it < items; it += kRgWarps) dot_item(it);
+  } else {
+    const int nw = items > warp ? (items - warp + kRgWarps - 1) / kRgWarps : 0;  // this warp's items
+    for (int li = 0; li < nw; ++li) {
+      const int it = warp + li * kRgWarps;
+      uint64_t* bar = full + warp * R + li % R;
+      if (!mbar_wait(bar, (li / R) & 1)) {
+        if (lane == 0) record_fault(p.fault, kFaultFullWait);
+        // copies still in flight (items li .. li + R - 1) land before the
+        // region is reused or the CTA exits
+        for (int k = li; k < nw && k < li + R; ++k) mbar_wait(full + warp * R + k % R, (k / R) & 1);
+        break;
+      }
+      dot_item(it);
+      __syncwarp();  // every lane's reads of the slot are done
+      const int nx = li + R;
+      if (lane == 0 && nx < nw) {
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(bar, item_bytes(warp + nx * kRgWarps));
+        issue_item(warp + nx * kRgWarps, bar, pol);
       }
     }
   }
 
   // ---------------------------------------------------------------- reduce: warps, then the cluster
+  if (threadIdx.x == 0) QLIN_TL(p, 4);
   __syncthreads();  // every weight read -> the reduction may overwrite them
 #pragma unroll
-  for (int s = 0; s < NS; ++s)
-#pragma unroll
-    for (int m = 0; m < MR; ++m)
-      *reinterpret_cast<float4*>(red + ((warp * NS + s) * MR + m) * kTileN + lane * 4) =
-          make_float4(acc[s][0][m], acc[s][1][m], acc[s][2][m], acc[s][3][m]);
+  for (int m = 0; m < MR; ++m)
+    *reinterpret_cast<float4*>(red + (warp * MR + m) * kTileN + lane * 4) =
+        make_float4(acc[0][m], acc[1][m], acc[2][m], acc[3][m]);
   __syncthreads();
   if (threadIdx.x >= kTileN) return;  // threads 0..127 hold one column each from here
   float vs[NS][MR];
@@ -347,9 +412,10 @@ __global__ void __launch_bounds__(kRgThreads, 1) dp_gemv_kernel(const __grid_con
     for (int m = 0; m < MR; ++m) {
       float v = 0.0f;
 #pragma unroll
-      for (int w = 0; w < kRgWarps; ++w) v = __fadd_rn(v, red[((w * NS + s) * MR + m) * kTileN + c]);
+      for (int w = s; w < kRgWarps; w += NS) v = __fadd_rn(v, red[(w * MR + m) * kTileN + c]);
       vs[s][m] = v;
     }
+  if (threadIdx.x == 0) QLIN_TL(p, 5);
   if (rank > 0) {
     // push to rank 0, completing its receive barrier; rank 0 outlives the
     // stores (it exits only after its receive barrier completed, or after
@@ -378,7 +444,37 @@ __global__ void __launch_bounds__(kRgThreads, 1) dp_gemv_kernel(const __grid_con
     }
   }
 
-  // ---------------------------------------------------------------- epilogue (threads 0..127 of rank 0)
+  if (p.kout > 1) {
+    // Clusters of this tile meet in the workspace: every cluster stores its
+    // partial sums, the last to arrive adds them in K order.
+    float* ws = g_dp_ws[p.ws_slot] + static_cast<size_t>(tile) * p.kout * NS * MR * kTileN;
+#pragma unroll
+    for (int s = 0; s < NS; ++s)
+#pragma unroll
+      for (int m = 0; m < MR; ++m) __stcg(ws + ((blockIdx.z * NS + s) * MR + m) * kTileN + c, vs[s][m]);
+    __threadfence();
+    named_bar_sync(1, kTileN);
+    int* last = reinterpret_cast<int*>(smem + L.xchg_off) + 4 * MR;
+    if (c == 0) {
+      const unsigned before = atomicAdd(&g_dp_cnt[p.ws_slot][tile], 1u);
+      *last = before == static_cast<unsigned>(p.kout - 1);
+      if (*last) g_dp_cnt[p.ws_slot][tile] = 0u;  // every arrival of this launch is in
+    }
+    named_bar_sync(1, kTileN);
+    if (!*last) return;
+    __threadfence();
+#pragma unroll
+    for (int s = 0; s < NS; ++s)
+#pragma unroll
+      for (int m = 0; m < MR; ++m) {
+        float v = __ldcg(ws + (s * MR + m) * kTileN + c);
+        for (int k = 1; k < p.kout; ++k) v = __fadd_rn(v, __ldcg(ws + ((k * NS + s) * MR + m) * kTileN + c));
+        vs[s][m] = v;
+      }
+  }
+
+  // ---------------------------------------------------------------- epilogue (threads 0..127 of one rank 0)
+  if (threadIdx.x == 0) QLIN_TL(p, 6);
   const int q4 = threadIdx.x >> 5;
   const bool valid = en < S0.n;
   if (EPI == kEpiOut) {
@@ -422,6 +518,7 @@ __global__ void __launch_bounds__(kRgThreads, 1) dp_gemv_kernel(const __grid_con
       }
     }
   }
+  if (threadIdx.x == 0) QLIN_TL(p, 7);
 }
 
 }  // namespace qlin

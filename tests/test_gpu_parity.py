@@ -361,7 +361,7 @@ def test_config2_w4_layer_full_size(pkg, dev, M):
     assert_bf16_close(bits(hd)[:, c], ref2, "cfg2 o_proj")
 
 
-@pytest.mark.parametrize("M", [1, 4])
+@pytest.mark.parametrize("M", [1, 2, 4])
 def test_config5_tp_layer_shapes(pkg, dev, M):
     """Config 5 shapes on one GPU: gate_up K=5120 N=17408 (x2), down K=17408 N=5120."""
     g = gen(7200 + M)
@@ -386,6 +386,40 @@ def test_config5_tp_layer_shapes(pkg, dev, M):
     ref = O.gemm_w4(hq.cpu().numpy(), hs.cpu().numpy(), D_[0].numpy()[:, c], bits(D_[1])[:, c],
                     D_[2].numpy()[:, c])
     assert_bf16_close(bits(out)[:, c], ref, "cfg5 down")
+
+
+@pytest.mark.parametrize("M", [1, 2])
+@pytest.mark.parametrize("wg,zeros", [(32, True), (64, False), (128, True)])
+def test_long_k_few_tiles_k_parts(pkg, dev, M, wg, zeros):
+    """Long K over few column tiles (the 8-GPU config-5 down projection,
+    K=17408 -> 640 columns = 5 tiles): decode rows cut each tile's K into
+    parts on separate CTAs that meet in a device workspace.  Unit scales give
+    the exact integer sum, bit for bit; then real scales with an in-place
+    residual against the oracle, and repeated launches (rotating workspace
+    slots, self-resetting counters) bit-identical."""
+    K, N = 17408, 640
+    g = gen(3300 + M + wg)
+    a = torch.randint(-127, 128, (M, K), dtype=torch.int8, generator=g)
+    b, sc, z = w4(g, K, N, wg, zeros)
+    out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    pkg.gemm_w4(cu(a), cu(torch.ones(M, K // 64)), cu(b), cu(torch.ones(K // wg, N, dtype=torch.bfloat16)), out,
+                b_z=cu(z))
+    w = O.unpack_w4(b.numpy(), None if z is None else z.numpy(), wg).astype(np.int64)
+    exact = a.numpy().astype(np.int64) @ w
+    np.testing.assert_array_equal(bits(out), O.f32_to_bf16_bits(exact.astype(np.float32)))
+
+    a2, s2 = acts_x(g, M, K)
+    res = torch.randn(M, N, generator=g).to(torch.bfloat16)
+    o2 = cu(res.clone())
+    pkg.gemm_w4(cu(a2), cu(s2), cu(b), cu(sc), o2, residual=o2, b_z=cu(z))
+    ref = O.gemm_w4(a2.numpy(), s2.numpy(), b.numpy(), bits(sc), None if z is None else z.numpy(), bits(res))
+    assert_bf16_close(bits(o2), ref, f"long-K M={M} wg={wg} zeros={zeros}")
+    first = None
+    for _ in range(6):
+        o3 = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+        pkg.gemm_w4(cu(a2), cu(s2), cu(b), cu(sc), o3, b_z=cu(z))
+        first = bits(o3) if first is None else first
+        np.testing.assert_array_equal(bits(o3), first)
 
 
 @pytest.mark.parametrize("M", [1, 4])
