@@ -57,6 +57,31 @@ int cuda_fail(cudaError_t e, const char* what) {
   return fail(QLIN_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
 }
 
+// Every kernel of the library runs with the largest shared-memory carveout
+// (once per kernel and device).  A CTA can only be placed on an SM whose
+// L1 / shared-memory split suits it; left to the driver's per-kernel choice,
+// a launch placed early under programmatic dependent launch can find the
+// SMs held by its predecessor's CTAs at a smaller split and wait for them to
+// drain.  One split for all keeps consecutive launches co-resident.
+int prefer_shared(const void* kern) {
+  static std::mutex mu;
+  static std::unordered_map<const void*, unsigned long long> done;  // kernel -> devices configured
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return QLIN_OK;  // the launch itself reports the error
+  }
+  const unsigned long long bit = 1ull << (dev & 63);
+  std::lock_guard<std::mutex> g(mu);
+  unsigned long long& mask = done[kern];
+  if (mask & bit) return QLIN_OK;
+  cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(carveout)");
+  mask |= bit;
+  return QLIN_OK;
+}
+
 // ---------------------------------------------------------------- device info
 struct DevInfo {
   int dev = -1;
@@ -559,6 +584,7 @@ int configure_tc() {
   if (!(configured.load() & bit)) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(smem)");
+    if (int r = prefer_shared(reinterpret_cast<const void*>(kern))) return r;
     configured.fetch_or(bit);
   }
   return QLIN_OK;
@@ -874,6 +900,7 @@ int launch_prefill_w8(const GemmArgs& g, int grid, cudaStream_t st) {
   if (!(configured.load() & bit)) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kGmSmem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc_gemm smem)");
+    if (int r = prefer_shared(reinterpret_cast<const void*>(kern))) return r;
     configured.fetch_or(bit);
   }
   cudaLaunchConfig_t cfg = {};
@@ -955,6 +982,7 @@ int launch_prefill_w4(const GemmW4Args& g, int grid, cudaStream_t st) {
   if (!(configured.load() & bit)) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kG4Smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc_gemm_w4 smem)");
+    if (int r = prefer_shared(reinterpret_cast<const void*>(kern))) return r;
     configured.fetch_or(bit);
   }
   cudaLaunchConfig_t cfg = {};
@@ -1120,9 +1148,12 @@ bool plan_dp_ring(int wb, int mr, int ns, int K, int wgrp, int tiles, int sms, D
 
 // dp plan of a launch, or false (the tensor-core kernel takes it).  W4 takes
 // the resident plan when its CTAs fit one wave (at most two per SM), a ring
-// plan otherwise; measured on B200 at M = 1 the config-5 W4 gate/up
-// 5120->2x17408 (136 tiles) ... us resident over several waves against ...
-// us on the ring.  W8 takes resident plans only (above).
+// plan otherwise.  Measured on B200 (graph replay, rotating weights, us, M = 1,
+// ring / resident over several waves / tensor cores): config-5 W4 gate/up
+// 5120->2x17408 30.1 / 29.5 / 42.7, its column shards of 2, 4, 8 GPUs 17.8 /
+// 17.2 / 22.1, 10.1 / 10.1 / 12.3, 5.9 / 5.9 / 9.1; config-5 down 17408->5120
+// (no resident plan) 14.4 / - / 25.5, shards 11.9 / - / 16.0, 9.3 / - / 15.1,
+// 8.8 / - / 13.4.  W8 takes resident plans only (above).
 bool plan_dp_uncached(int wb, int mr, int ns, int K, int wgrp, int tiles, int sms, DpPlan* pl) {
   DpPlan res;
   const bool has_res = plan_dp_resident(wb, mr, ns, K, wgrp, tiles, sms, &res);
@@ -1394,6 +1425,7 @@ int peer_buffers(PeerGatherArgs& a, void* const* bufs, void* const* arrive, int 
 }
 
 int peer_launch(const PeerGatherArgs& a, int ctas, cudaStream_t st) {
+  if (int r = prefer_shared(reinterpret_cast<const void*>(peer_allgather_kernel))) return r;
   peer_allgather_kernel<<<ctas, kPeerThreads, 0, st>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "peer_allgather_kernel launch");
@@ -1402,6 +1434,7 @@ int peer_launch(const PeerGatherArgs& a, int ctas, cudaStream_t st) {
 
 // ---------------------------------------------------------------- activation producers (kernels/norm.py)
 int prod_launch(const void* kern, dim3 grid, void** args, cudaStream_t st) {
+  if (int r = prefer_shared(kern)) return r;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kProdThreads, 1, 1);
@@ -1424,6 +1457,7 @@ int check_rows(int64_t M, int64_t K, const char* what) {
 
 // ---------------------------------------------------------------- decode-step neighbours
 int dec_launch(const void* kern, dim3 grid, dim3 block, size_t smem, int cluster, void** args, cudaStream_t st) {
+  if (int r = prefer_shared(kern)) return r;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -1455,6 +1489,7 @@ int smem_optin(const void* kern, size_t bytes, std::atomic<unsigned long long>& 
   if (!(done.load() & bit)) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(smem)");
+    if (int r = prefer_shared(kern)) return r;
     done.fetch_or(bit);
   }
   return QLIN_OK;
@@ -1949,6 +1984,9 @@ int qlin_quant_row(const void* x, int64_t ldx, int64_t M, int64_t K, int8_t* q, 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (int r = prefer_shared(vec ? reinterpret_cast<const void*>(quant_row_vec_kernel)
+                                : reinterpret_cast<const void*>(quant_row_kernel)))
+    return r;
   cudaError_t e = cudaLaunchKernelEx(&cfg, vec ? quant_row_vec_kernel : quant_row_kernel,
                                      static_cast<const __nv_bfloat16*>(x),
                                      static_cast<long long>(ldx), static_cast<int>(M),

@@ -195,11 +195,34 @@ struct SoftmaxState {
   float m[G], l[G], acc[G][E];
 };
 
+// Raw cache words of one lane: NWD 32-bit words, loaded in one access.
+template <int NWD>
+__device__ __forceinline__ void load_words(const void* p, uint32_t (&w)[NWD]) {
+  if constexpr (NWD == 4) {
+    const uint4 r = *reinterpret_cast<const uint4*>(p);
+    w[0] = r.x, w[1] = r.y, w[2] = r.z, w[3] = r.w;
+  } else if constexpr (NWD == 2) {
+    const uint2 r = *reinterpret_cast<const uint2*>(p);
+    w[0] = r.x, w[1] = r.y;
+  } else {
+    w[0] = *reinterpret_cast<const uint32_t*>(p);
+  }
+}
+// element j of raw words: int8 (4 per word) or bf16 (2 per word) -> fp32
+template <bool INT8, int NWD>
+__device__ __forceinline__ float raw_elem(const uint32_t (&w)[NWD], int j) {
+  if constexpr (INT8) return static_cast<float>(static_cast<int8_t>((w[j >> 2] >> (8 * (j & 3))) & 0xFF));
+  return __uint_as_float((j & 1) ? (w[j >> 1] & 0xFFFF0000u) : (w[j >> 1] << 16));
+}
+
 // kernels/attention.py:209-267.  Cluster of S CTAs per (KV head, candidate):
 // rank r covers positions [r n / S, (r+1) n / S) of the n = pos + 1; warp w of
-// a CTA the positions w, w + 8, ... of that range, one at a time:
-//   s_h = q_h . k;  m' = max(m, s);  l = l e^{m - m'} + e^{s - m'};
-//   acc = acc e^{m - m'} + e^{s - m'} v.
+// a CTA the positions w, w + 8, ... of that range, CH at a time: the chunk's
+// K/V rows are all requested before any is used (one memory latency per
+// chunk, not per position), then per query head the CH scores (lane partial
+// dots, warp sums interleaved), and one online-softmax update per chunk:
+//   m' = max(m, max_c s_c);  l = l e^{m - m'} + sum_c e^{s_c - m'};
+//   acc = acc e^{m - m'} + sum_c e^{s_c - m'} v_c.
 // The warps' states merge in shared memory, the ranks' states in rank 0's
 // shared memory (remote stores after a cluster barrier), then out = acc / l.
 template <int G, int E, bool INT8>
@@ -238,37 +261,82 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(const __grid_c
     for (int j = 0; j < E; ++j) st.acc[g][j] = 0.0f;
   }
   const long long kb = b * a.kv_stride, sb = b * a.kvs_stride;
-  for (int p = p0 + warp; p < p1; p += NW) {
-    float k[E], v[E];
-    const long long rowk = kb + static_cast<long long>(p) * sns * HD;
-    if constexpr (INT8) {
-      const int8_t* kv = static_cast<const int8_t*>(a.kvc);
-      load_i8<E>(kv + rowk + kvh * HD + lane * E, k);
-      load_i8<E>(kv + rowk + (a.nkv + kvh) * HD + lane * E, v);
-      const float ks = a.kvs[sb + static_cast<long long>(p) * sns + kvh];
-      const float vs = a.kvs[sb + static_cast<long long>(p) * sns + a.nkv + kvh];
+  constexpr int CH = (INT8 && G <= 4) ? 8 : 4;   // positions per chunk of a warp (register budget)
+  constexpr int NWD = INT8 ? E / 4 : E / 2;       // raw 32-bit words per lane and row
+  constexpr int EB = INT8 ? 1 : 2;                // bytes per cache element
+  const uint8_t* kvb = static_cast<const uint8_t*>(a.kvc);
+  for (int base = p0 + warp; base < p1; base += NW * CH) {
+    uint32_t kr[CH][NWD], vr[CH][NWD];
+    float ksc[CH], vsc[CH];
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const int p = base + c * NW;
+      if (p < p1) {
+        const long long rowk = (kb + static_cast<long long>(p) * sns * HD) * EB;
+        load_words<NWD>(kvb + rowk + (kvh * HD + lane * E) * EB, kr[c]);
+        load_words<NWD>(kvb + rowk + ((a.nkv + kvh) * HD + lane * E) * EB, vr[c]);
+        if constexpr (INT8) {
+          ksc[c] = a.kvs[sb + static_cast<long long>(p) * sns + kvh];
+          vsc[c] = a.kvs[sb + static_cast<long long>(p) * sns + a.nkv + kvh];
+        } else {
+          ksc[c] = vsc[c] = 1.0f;
+        }
+      } else {
+#pragma unroll
+        for (int w = 0; w < NWD; ++w) kr[c][w] = vr[c][w] = 0u;
+        ksc[c] = vsc[c] = 0.0f;
+      }
+    }
+    float sc[G][CH];
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      float k[E];
 #pragma unroll
       for (int j = 0; j < E; ++j) {
-        k[j] = __fmul_rn(k[j], ks);
-        v[j] = __fmul_rn(v[j], vs);
+        k[j] = raw_elem<INT8, NWD>(kr[c], j);
+        if constexpr (INT8) k[j] = __fmul_rn(k[j], ksc[c]);
       }
-    } else {
-      const __nv_bfloat16* kv = static_cast<const __nv_bfloat16*>(a.kvc);
-      load_bf16<E>(kv + rowk + kvh * HD + lane * E, k);
-      load_bf16<E>(kv + rowk + (a.nkv + kvh) * HD + lane * E, v);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float d = 0.0f;
+#pragma unroll
+        for (int j = 0; j < E; ++j) d = __fadd_rn(d, __fmul_rn(q[g][j], k[j]));
+        sc[g][c] = d;
+      }
     }
 #pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int c = 0; c < CH; ++c) sc[g][c] = __fadd_rn(sc[g][c], __shfl_xor_sync(0xffffffffu, sc[g][c], o));
+#pragma unroll
     for (int g = 0; g < G; ++g) {
-      float d = 0.0f;
+      float mc = sc[g][0];  // position base < p1 always
 #pragma unroll
-      for (int j = 0; j < E; ++j) d = __fadd_rn(d, __fmul_rn(q[g][j], k[j]));
-      const float s = warp_sum(d);
-      const float mn = fmaxf(st.m[g], s);
-      const float alpha = expf(st.m[g] - mn);  // 0 for the first position (m = -inf)
-      const float pe = expf(s - mn);
-      st.l[g] = __fadd_rn(__fmul_rn(st.l[g], alpha), pe);
+      for (int c = 1; c < CH; ++c)
+        if (base + c * NW < p1) mc = fmaxf(mc, sc[g][c]);
+      const float mn = fmaxf(st.m[g], mc);
+      const float alpha = expf(st.m[g] - mn);  // 0 for the first chunk (m = -inf)
+      float pe[CH];
+      float ps = 0.0f;
 #pragma unroll
-      for (int j = 0; j < E; ++j) st.acc[g][j] = __fadd_rn(__fmul_rn(st.acc[g][j], alpha), __fmul_rn(pe, v[j]));
+      for (int c = 0; c < CH; ++c) {
+        pe[c] = base + c * NW < p1 ? expf(sc[g][c] - mn) : 0.0f;
+        ps = __fadd_rn(ps, pe[c]);
+      }
+      st.l[g] = __fadd_rn(__fmul_rn(st.l[g], alpha), ps);
+#pragma unroll
+      for (int j = 0; j < E; ++j) {
+        float t = __fmul_rn(st.acc[g][j], alpha);
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+          float v = raw_elem<INT8, NWD>(vr[c], j);
+          if constexpr (INT8) v = __fmul_rn(v, vsc[c]);
+          t = __fadd_rn(t, __fmul_rn(pe[c], v));
+        }
+        st.acc[g][j] = t;
+      }
       st.m[g] = mn;
     }
   }
