@@ -345,7 +345,7 @@ QLIN_KNOB(tune_dp, "QLIN_TUNE_DP", 1)  // 0: decode rows take the tensor-core ke
 // dp kernel weight ring: 0 never, 1 when resident weights need more than one
 // wave, 2 whenever a ring plan exists
 QLIN_KNOB(tune_dp_stream, "QLIN_TUNE_DP_STREAM", 1)
-QLIN_KNOB(tune_dp_maxm, "QLIN_TUNE_DP_MAXM", 2)  // rows the dp kernel serves (tuning builds: 2 or 4)
+QLIN_KNOB(tune_dp_maxm, "QLIN_TUNE_DP_MAXM", 4)  // rows the dp kernel may serve
 #undef QLIN_KNOB
 
 bool use_dp() { return tune_dp() != 0; }
@@ -1069,16 +1069,15 @@ bool mid_m_takes_gemm(int epi, int64_t M, int tiles) {
 
 int smem_optin(const void* kern, size_t bytes, std::atomic<unsigned long long>& done);
 
-// ---------------------------------------------------------------- dp4a GEMV (M <= 2)
+// ---------------------------------------------------------------- dp4a GEMV (decode rows)
 // Per-CTA shared memory that keeps two CTAs on an SM (this launch and the
 // next one's, which streams its weights under programmatic dependent launch).
 constexpr uint32_t kDpBudget = 110 * 1024;
-// Rows it serves (tune_dp_maxm, 2).  Its dp4a work grows with M while the
-// tensor-core kernel's MMA count does not; measured on B200 (graph replay,
-// rotating weights, us, dp4a vs tcgen05): M = 1 W4 gate/up 2048->2x6144 6.5
-// vs 8.6, down 6144->2048 4.7 vs 5.7, o 2.9 vs 3.8, qkv 3.7 vs 4.6, W8
-// 2048->6144 3.5 vs 3.9, W8 down 3.9 vs 5.6; M = 4 W4 gate/up 10.4 vs 10.0,
-// W8 gate/up 14.0 vs 7.7, W8 2048->6144 4.6 vs 4.0.
+// Rows it serves: 1-2 (any weights), 3-4 (W4, short launches: plan_dp).  Its
+// dp4a work grows with M while the tensor-core kernel's MMA count does not;
+// measured on B200 (graph replay, rotating weights, us, dp4a vs tcgen05, M =
+// 1): W4 gate/up 2048->2x6144 4.6 vs 8.6, down 6144->2048 3.8 vs 5.7, o 2.6
+// vs 3.8, qkv 3.0 vs 4.6, W8 2048->6144 3.3 vs 3.9, W8 down 4.0 vs 5.6.
 
 int dp_mr(int64_t M) { return M <= 1 ? 1 : M <= 2 ? 2 : 4; }
 
@@ -1115,17 +1114,17 @@ bool plan_dp_resident(int wb, int mr, int ns, int K, int wgrp, int tiles, int sm
 // wave of CTAs without clusters, a tile's K cut into `kout` parts that meet
 // in the device workspace, each warp streaming its items through a ring of
 // slots.  Parts per tile are chosen so that the busiest SM streams the fewest
-// groups (CTAs per SM x groups per CTA), at most three CTAs per SM (shared
-// memory 200 / 110 / 74 KB), ties to fewer parts.
+// groups (CTAs per SM x groups per CTA), at most two CTAs per SM (the
+// kernel's register bound; shared memory 200 / 110 KB), ties to fewer parts.
 bool plan_dp_ring(int wb, int mr, int ns, int K, int wgrp, int tiles, int sms, DpPlan* pl) {
   const int G = K / kGroup;
   long long best_w = -1;
   for (int P = 1; P <= G; ++P) {
     const long long ctas = static_cast<long long>(tiles) * P;
     const long long per_sm = (ctas + sms - 1) / sms;
-    if (per_sm > 3) break;
+    if (per_sm > 2) break;
     if (P > 1 && (tiles > kDpWsTiles || ctas * ns * mr * kTileN > kDpWsFloats)) break;
-    const uint32_t budget = (per_sm == 1 ? 200u : per_sm == 2 ? 110u : 74u) * 1024u;
+    const uint32_t budget = (per_sm == 1 ? 200u : 110u) * 1024u;
     const int gmax = (G + P - 1) / P;
     int ring = 0;
     for (int r = 8; r >= 2 && ring == 0; --r)
@@ -1158,6 +1157,17 @@ bool plan_dp_uncached(int wb, int mr, int ns, int K, int wgrp, int tiles, int sm
   DpPlan res;
   const bool has_res = plan_dp_resident(wb, mr, ns, K, wgrp, tiles, sms, &res);
   const bool one_wave = has_res && static_cast<long long>(tiles) * res.split <= 2ll * sms;
+  if (mr > 2) {
+    // 3-4 rows: W4 only, resident single-wave plans with at most two items
+    // per warp (the dot work grows with the rows, the MMA count does not).
+    // Measured on B200 (graph replay, us, dp4a vs tcgen05, M = 4): config-2
+    // W4 gate/up 8.2 vs 10.0 (two items per warp), down 6.2 vs 6.8, o 3.9 vs
+    // 4.0, qkv 4.9 vs 4.7; config-5 gate/up shards (2.5 items per warp) 19.8
+    // vs 16.9 and 18.3 vs 12.2; W8 config 1 4.7 vs 4.0.
+    if (wb != 4 || !has_res || !one_wave || res.gmax * ns > 2 * kRgWarps) return false;
+    *pl = res;
+    return true;
+  }
   const int mode = tune_dp_stream();
   if (has_res && (mode == 0 || (mode == 1 && one_wave))) {
     *pl = res;
@@ -1231,9 +1241,9 @@ int launch_dp_t(const DpArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
 template <int WB, int EPI>
 int launch_dp_mr(int mr, const DpArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
   if (mr == 1) return launch_dp_t<WB, 1, EPI>(a, grid, smem, st);
-#ifdef QLIN_TUNING
-  if (mr == 4) return launch_dp_t<WB, 4, EPI>(a, grid, smem, st);  // (QLIN_TUNE_DP_MAXM=4 sweeps)
-#endif
+  if constexpr (WB == 4) {
+    if (mr == 4) return launch_dp_t<WB, 4, EPI>(a, grid, smem, st);
+  }
   return launch_dp_t<WB, 2, EPI>(a, grid, smem, st);
 }
 
@@ -2208,11 +2218,25 @@ int qlin_attn_decode(const void* q, const void* kvc, const float* kvs, void* out
   int S = static_cast<int>((n + 63) / 64);
   if (S > 8) S = 8;
   if (S < 1) S = 1;
-  const int G = static_cast<int>(nq / nkv);
+  const int Gfull = static_cast<int>(nq / nkv);
+  if (!(Gfull == 1 || Gfull == 2 || Gfull == 4 || Gfull == 8))
+    return fail(QLIN_ERR_SHAPE, "attn_decode: %d query heads per KV head (1, 2, 4 or 8)", Gfull);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int B = static_cast<int>(batch), NKV = static_cast<int>(nkv);
-  if (hd == 256) return kv_int8 ? attn_decode_g<8, true>(G, a, S, NKV, B, st) : attn_decode_g<8, false>(G, a, S, NKV, B, st);
-  return kv_int8 ? attn_decode_g<4, true>(G, a, S, NKV, B, st) : attn_decode_g<4, false>(G, a, S, NKV, B, st);
+  // Split a KV head's query heads over more CTAs until the launch covers the
+  // SMs (the extra reads of the same cache rows mostly hit L2).  Measured on
+  // B200, config 4 (B = 4, 8 query / 2 KV heads, 1025 int8 positions): one
+  // CTA group per KV head took 19.3 us per launch.
+  int hsplit = 1;
+  while (hsplit < Gfull && static_cast<long long>(S) * NKV * hsplit * B < di.sms) hsplit *= 2;
+  if (static_cast<long long>(NKV) * hsplit > 65535) hsplit = 1;
+  a.hsplit = hsplit;
+  const int G = Gfull / hsplit;
+  if (hd == 256)
+    return kv_int8 ? attn_decode_g<8, true>(G, a, S, NKV * hsplit, B, st)
+                   : attn_decode_g<8, false>(G, a, S, NKV * hsplit, B, st);
+  return kv_int8 ? attn_decode_g<4, true>(G, a, S, NKV * hsplit, B, st)
+                 : attn_decode_g<4, false>(G, a, S, NKV * hsplit, B, st);
 }
 
 int qlin_delta_decode(const void* qkv, int64_t ldq, const float* g, const float* beta, float* state, void* out,

@@ -187,6 +187,7 @@ struct AttnDecodeArgs {
   const int* pos_dev;      // last position (inclusive) from device memory, or null
   long long kv_stride, kvs_stride;
   int pos, nq, nkv;
+  int hsplit;              // CTAs per KV head, each serving G of its query heads
 };
 
 // Per-warp online-softmax state of the G query heads of one KV head.
@@ -215,7 +216,9 @@ __device__ __forceinline__ float raw_elem(const uint32_t (&w)[NWD], int j) {
   return __uint_as_float((j & 1) ? (w[j >> 1] & 0xFFFF0000u) : (w[j >> 1] << 16));
 }
 
-// kernels/attention.py:209-267.  Cluster of S CTAs per (KV head, candidate):
+// kernels/attention.py:209-267.  Cluster of S CTAs per (KV head, group of G of
+// its query heads, candidate) -- a KV head's query heads may be split over
+// `hsplit` CTA groups that read the same cache rows, for more CTAs:
 // rank r covers positions [r n / S, (r+1) n / S) of the n = pos + 1; warp w of
 // a CTA the positions w, w + 8, ... of that range, CH at a time: the chunk's
 // K/V rows are all requested before any is used (one memory latency per
@@ -223,8 +226,11 @@ __device__ __forceinline__ float raw_elem(const uint32_t (&w)[NWD], int j) {
 // dots, warp sums interleaved), and one online-softmax update per chunk:
 //   m' = max(m, max_c s_c);  l = l e^{m - m'} + sum_c e^{s_c - m'};
 //   acc = acc e^{m - m'} + sum_c e^{s_c - m'} v_c.
-// The warps' states merge in shared memory, the ranks' states in rank 0's
-// shared memory (remote stores after a cluster barrier), then out = acc / l.
+// The warps' states merge in shared memory; every rank > 0 then stores its
+// merged state into its slot of rank 0's shared memory (remote stores, one
+// cluster barrier with release / acquire), and rank 0 merges the ranks in
+// rank order from its own shared memory, then out = acc / l.
+constexpr int kAdMaxRanks = 8;
 template <int G, int E, bool INT8>
 __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(const __grid_constant__ AttnDecodeArgs a) {
   constexpr int HD = 32 * E;
@@ -238,11 +244,14 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(const __grid_c
   float* sm_acc = sm + 2 * NW * G;
   float* fm = sm_acc + NW * G * HD;
   float* fl = fm + G;
+  float* xs = fl + G;  // rank 0: slot r - 1 holds rank r's merged acc [G * HD], m [G], l [G]
+  constexpr int kSlot = G * HD + 2 * G;
   pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = static_cast<int>(gridDim.x);
   const int rank = static_cast<int>(blockIdx.x);
-  const int kvh = blockIdx.y, b = blockIdx.z;
+  const int kvh = blockIdx.y / a.hsplit, b = blockIdx.z;
+  const int h0 = kvh * G * a.hsplit + (blockIdx.y % a.hsplit) * G;  // first query head of this CTA
   pdl_wait();
   const int n = (a.pos_dev ? *a.pos_dev : a.pos) + 1;
   const int p0 = static_cast<int>(static_cast<long long>(rank) * n / S);
@@ -251,7 +260,7 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(const __grid_c
   float q[G][E];
 #pragma unroll
   for (int g = 0; g < G; ++g)
-    load_bf16<E>(a.q + static_cast<long long>(b) * a.nq * HD + (kvh * G + g) * HD + lane * E, q[g]);
+    load_bf16<E>(a.q + static_cast<long long>(b) * a.nq * HD + (h0 + g) * HD + lane * E, q[g]);
   SoftmaxState<G, E> st;
 #pragma unroll
   for (int g = 0; g < G; ++g) {
@@ -375,38 +384,45 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(const __grid_c
     fl[g] = L;
   }
   __syncthreads();
-  // rank 0 merges the ranks' states in rank order, then divides
+  // ranks > 0: merged state -> their slot of rank 0's shared memory
+  if (S > 1 && rank > 0) {
+    const uint32_t slot = map_to_rank(smem_u32(xs + (rank - 1) * kSlot), 0);
+    for (int idx = threadIdx.x; idx < G * HD; idx += kDecThreads) st_cluster_f32(slot + idx * 4, sm_acc[idx]);
+    if (threadIdx.x < G) {
+      st_cluster_f32(slot + (G * HD + threadIdx.x) * 4, fm[threadIdx.x]);
+      st_cluster_f32(slot + (G * HD + G + threadIdx.x) * 4, fl[threadIdx.x]);
+    }
+  }
   if (S > 1) {
-    cluster_arrive_relaxed();
+    cluster_arrive_release();
     cluster_wait();
   }
+  // rank 0 merges the ranks' states in rank order, then divides
   if (rank == 0) {
     for (int idx = threadIdx.x; idx < G * HD; idx += kDecThreads) {
       const int g = idx / HD, d = idx % HD;
       float M = fm[g];
-      for (int r = 1; r < S; ++r) M = fmaxf(M, ld_cluster_f32(map_to_rank(smem_u32(fm + g), r)));
+      for (int r = 1; r < S; ++r) M = fmaxf(M, xs[(r - 1) * kSlot + G * HD + g]);
       float acc = 0.0f, L = 0.0f;
       for (int r = 0; r < S; ++r) {
-        const float mr = r == 0 ? fm[g] : ld_cluster_f32(map_to_rank(smem_u32(fm + g), r));
+        const float* xr = xs + (r - 1) * kSlot;
+        const float mr = r == 0 ? fm[g] : xr[G * HD + g];
         if (mr == -INFINITY) continue;  // a rank without positions
         const float f = expf(mr - M);
-        const float lr = r == 0 ? fl[g] : ld_cluster_f32(map_to_rank(smem_u32(fl + g), r));
-        const float ar = r == 0 ? sm_acc[g * HD + d] : ld_cluster_f32(map_to_rank(smem_u32(sm_acc + g * HD + d), r));
+        const float lr = r == 0 ? fl[g] : xr[G * HD + G + g];
+        const float ar = r == 0 ? sm_acc[idx] : xr[idx];
         L = __fadd_rn(L, __fmul_rn(lr, f));
         acc = __fadd_rn(acc, __fmul_rn(ar, f));
       }
-      a.out[static_cast<long long>(b) * a.nq * HD + (kvh * G + g) * HD + d] = __float2bfloat16_rn(__fdiv_rn(acc, L));
+      a.out[static_cast<long long>(b) * a.nq * HD + (h0 + g) * HD + d] = __float2bfloat16_rn(__fdiv_rn(acc, L));
     }
-  }
-  // the other ranks' shared memory must outlive rank 0's reads
-  if (S > 1) {
-    cluster_arrive_relaxed();
-    cluster_wait();
   }
 }
 
 __host__ __device__ constexpr int attn_decode_smem(int G, int E) {
-  return (2 * (kDecThreads / 32) * G + (kDecThreads / 32) * G * 32 * E + 2 * G) * 4;
+  return (2 * (kDecThreads / 32) * G + (kDecThreads / 32) * G * 32 * E + 2 * G +
+          (kAdMaxRanks - 1) * (G * 32 * E + 2 * G)) *
+         4;
 }
 
 // ---------------------------------------------------------------- delta_decode

@@ -45,6 +45,19 @@ namespace qlin {
 
 constexpr int kRgThreads = 256;
 constexpr int kRgWarps = kRgThreads / 32;
+// Blocks of a weight item unrolled together in the dot loop (W8: 16 blocks of
+// 4 K rows, W4: 4 blocks of 8 K per 32-K half).  Measured on B200 (graph
+// replay, us, full unroll vs 4 / 2): config-2 W4 gate/up 4.6 vs 5.6, down 3.8
+// vs 4.6, qkv 3.0 vs 3.7, config-1 W8 3.3 vs 3.5 at M = 1; W4 gate/up 8.2 vs
+// 9.0 at M = 4.
+#ifndef QLIN_DP_UNROLL_W8
+#define QLIN_DP_UNROLL_W8 16
+#endif
+#ifndef QLIN_DP_UNROLL_W4
+#define QLIN_DP_UNROLL_W4 4
+#endif
+constexpr int kDpUnrollW8 = QLIN_DP_UNROLL_W8;
+constexpr int kDpUnrollW4 = QLIN_DP_UNROLL_W4;
 
 // Device workspace of the cross-cluster K parts: per slot, fp32 partial sums
 // [tile][kout][stream][row][128] and one arrival counter per tile.  The host
@@ -80,11 +93,11 @@ struct DpArgs {
 };
 
 // Shared-memory carve-up (host and device): the weight slots (every (group,
-// stream) item, or `ring` per warp), the K-part activations, their per-group sums (W4) and
-// scales, the cross-warp reduction (over the weights once they are used),
-// the partial sums received from the other ranks, barriers.
+// stream) item, or `ring` per warp), the K-part activation rows, the
+// cross-warp reduction (over the weights once they are used), the partial
+// sums received from the other ranks, barriers.
 struct DpLayout {
-  uint32_t item, wbytes, sbytes, act_off, asum_off, as_off, part_off, xchg_off, bar_off, total;
+  uint32_t item, wbytes, sbytes, act_off, part_off, xchg_off, bar_off, total;
 };
 __host__ __device__ inline DpLayout dp_layout(int wb, int mr, int ns, int wgrp, int gmax, int split, int ring) {
   DpLayout L;
@@ -98,16 +111,12 @@ __host__ __device__ inline DpLayout dp_layout(int wb, int mr, int ns, int wgrp, 
   off = align_up(off, 128);
   L.act_off = off;
   off = align_up(off + gmax * mr * 64, 16);
-  L.asum_off = off;
-  off = align_up(off + (wb == 4 ? gmax * mr * 2 * 4 : 0), 16);
-  L.as_off = off;
-  off = align_up(off + gmax * mr * 4, 16);
   L.part_off = off;
   off = align_up(off + (split > 1 ? split - 1 : 0) * ns * mr * kTileN * 4, 16);
   L.xchg_off = off;
   off = align_up(off + 4 * mr * 4 + 16, 16);  // (+ the last-arrival flag)
   L.bar_off = off;
-  off += 8 * (kRgWarps * (ring > 0 ? ring : 1) + 1);
+  off += 8 * (kRgWarps * (ring > 0 ? ring : 1) + 2);
   L.total = off + 128;  // alignment slack
   return L;
 }
@@ -133,7 +142,7 @@ __device__ __forceinline__ void tr4x4(uint32_t r0, uint32_t r1, uint32_t r2, uin
 }
 
 template <int WB, int MR, int EPI>
-__global__ void __launch_bounds__(kRgThreads, 1) dp_gemv_kernel(const __grid_constant__ DpArgs p) {
+__global__ void __launch_bounds__(kRgThreads, 2) dp_gemv_kernel(const __grid_constant__ DpArgs p) {
   constexpr int NS = (EPI == kEpiOut) ? 1 : 2;
   extern __shared__ __align__(128) uint8_t dp_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dp_smem_raw) + 127) & ~uintptr_t(127));
@@ -142,9 +151,8 @@ __global__ void __launch_bounds__(kRgThreads, 1) dp_gemv_kernel(const __grid_con
   const int nsub = (WB == 4 && p.wgrp == 32) ? 2 : 1;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);  // per warp (ring: per warp and slot)
   uint64_t* recv = full + kRgWarps * (R > 0 ? R : 1);
-  int8_t* act = reinterpret_cast<int8_t*>(smem + L.act_off);      // [g][m][64]
-  int* asum = reinterpret_cast<int*>(smem + L.asum_off);           // [g][m][2]
-  float* ass = reinterpret_cast<float*>(smem + L.as_off);          // [g][m]
+  uint64_t* abar = recv + 1;                                       // activation rows landed
+  int8_t* act = reinterpret_cast<int8_t*>(smem + L.act_off);      // [m][gmax][64]: the K part of row m
   float* part = reinterpret_cast<float*>(smem + L.part_off);       // [rank-1][s][m][128]
   float* red = reinterpret_cast<float*>(smem);                     // [warp][m][128], over the weights
 
@@ -191,6 +199,7 @@ __global__ void __launch_bounds__(kRgThreads, 1) dp_gemv_kernel(const __grid_con
   if (threadIdx.x == 0) {
     for (int w = 0; w < kRgWarps * (R > 0 ? R : 1); ++w) mbar_init(full + w, 1);
     mbar_init(recv, 1);
+    mbar_init(abar, 1);
     fence_mbar_init();
     if (p.split > 1 && rank == 0)
       mbar_arrive_expect_tx(recv, static_cast<uint32_t>((p.split - 1) * kTileN * NS * MR * 4));
@@ -243,31 +252,19 @@ __global__ void __launch_bounds__(kRgThreads, 1) dp_gemv_kernel(const __grid_con
     for (int m = 0; m < MR; ++m)
       if (m < p.M) pre_res[m] = __bfloat162float(res[static_cast<long long>(m) * p.ldr + S0.out_col + en]);
   }
-  // a_q rows of the K range -> act[g][m][64]; W4 reorders each 8-K block to
-  // (the 4 even K, the 4 odd K) so one 8-byte load gives both parity words
-  for (int i = threadIdx.x; i < nst * MR * 8; i += kRgThreads) {
-    const int b8 = i % 8, m = (i / 8) % MR, gl = i / (8 * MR);
-    uint2 v = make_uint2(0u, 0u);
-    if (m < p.M) v = *reinterpret_cast<const uint2*>(p.a_q + static_cast<long long>(m) * p.K + (g0 + gl) * 64 + b8 * 8);
-    if (WB == 4) v = make_uint2(__byte_perm(v.x, v.y, 0x6420), __byte_perm(v.x, v.y, 0x7531));
-    *reinterpret_cast<uint2*>(act + (gl * MR + m) * 64 + b8 * 8) = v;
+  // the K part of every activation row, one bulk copy per row (K % 64 == 0
+  // and a 16-byte aligned a_q make every row slice 16-byte aligned); rows
+  // past M are never stored, so their slots are left as they are
+  const int mv = p.M < MR ? p.M : MR;
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(abar, static_cast<uint32_t>(mv * nst * 64));
+    for (int m = 0; m < mv; ++m)
+      bulk_load(act + m * p.gmax * 64, p.a_q + static_cast<long long>(m) * p.K + g0 * 64,
+                static_cast<uint32_t>(nst * 64), abar);
   }
-  for (int i = threadIdx.x; i < nst * MR; i += kRgThreads) {
-    const int m = i % MR, gl = i / MR;
-    ass[gl * MR + m] = m < p.M ? __ldg(p.a_s + static_cast<long long>(m) * G + g0 + gl) : 0.0f;
-  }
-  __syncthreads();
-  if (WB == 4) {
-    // sum of the activations over each 32-K half of a group (zero points)
-    for (int i = threadIdx.x; i < nst * MR * 2; i += kRgThreads) {
-      const int h = i % 2, m = (i / 2) % MR, gl = i / (2 * MR);
-      const int* a = reinterpret_cast<const int*>(act + (gl * MR + m) * 64 + h * 32);
-      int sa = 0;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) sa = __dp4a(a[e], 0x01010101, sa);
-      asum[(gl * MR + m) * 2 + h] = sa;
-    }
-    __syncthreads();
+  if (!mbar_wait(abar, 0)) {
+    if ((threadIdx.x & 31) == 0) record_fault(p.fault, kFaultFullWait);
+    mbar_wait(abar, 0);  // the copy lands before the CTA may exit
   }
   if (threadIdx.x == 0) QLIN_TL(p, 3);
 
@@ -282,21 +279,23 @@ __global__ void __launch_bounds__(kRgThreads, 1) dp_gemv_kernel(const __grid_con
   auto dot_item = [&](int it) {
     const int gl = it / NS;
     const uint8_t* wt = item_w(it);
-    const float* as_g = ass + gl * MR;
+    float as_g[MR];  // a_s[m, group]: loaded first, used after the integer work
+#pragma unroll
+    for (int m = 0; m < MR; ++m) as_g[m] = m < p.M ? __ldg(p.a_s + static_cast<long long>(m) * G + g0 + gl) : 0.0f;
     if (WB == 8) {
       int isum[4][MR];
 #pragma unroll
       for (int j = 0; j < 4; ++j)
 #pragma unroll
         for (int m = 0; m < MR; ++m) isum[j][m] = 0;
-#pragma unroll 4
+#pragma unroll kDpUnrollW8
       for (int b = 0; b < 16; ++b) {  // 4 K rows per block
         const uint32_t* rows = reinterpret_cast<const uint32_t*>(wt + b * 4 * kTileN) + lane;
         uint32_t col[4];
         tr4x4(rows[0], rows[kTileN / 4], rows[2 * kTileN / 4], rows[3 * kTileN / 4], col);
 #pragma unroll
         for (int m = 0; m < MR; ++m) {
-          const int aw = *reinterpret_cast<const int*>(act + (gl * MR + m) * 64 + b * 4);
+          const int aw = *reinterpret_cast<const int*>(act + (m * p.gmax + gl) * 64 + b * 4);
 #pragma unroll
           for (int j = 0; j < 4; ++j) isum[j][m] = __dp4a(static_cast<int>(col[j]), aw, isum[j][m]);
         }
@@ -312,15 +311,18 @@ __global__ void __launch_bounds__(kRgThreads, 1) dp_gemv_kernel(const __grid_con
       const uint16_t* sc = reinterpret_cast<const uint16_t*>(wt + L.wbytes);
       const uint8_t* zz = wt + L.wbytes + nsub * kTileN * 2;
       int isum[2][4][MR];  // per 32-K half
+      int asum[2][MR];     // sum of the activations per 32-K half (zero points)
 #pragma unroll
       for (int h = 0; h < 2; ++h)
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
+        for (int m = 0; m < MR; ++m) {
+          asum[h][m] = 0;
 #pragma unroll
-          for (int m = 0; m < MR; ++m) isum[h][j][m] = 0;
+          for (int j = 0; j < 4; ++j) isum[h][j][m] = 0;
+        }
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-#pragma unroll 2
+#pragma unroll kDpUnrollW4
         for (int bb = 0; bb < 4; ++bb) {  // 4 packed rows = 8 K per block
           const int b = h * 4 + bb;
           const uint32_t* rows = reinterpret_cast<const uint32_t*>(wt + b * 4 * kTileN) + lane;
@@ -328,7 +330,10 @@ __global__ void __launch_bounds__(kRgThreads, 1) dp_gemv_kernel(const __grid_con
           tr4x4(rows[0], rows[kTileN / 4], rows[2 * kTileN / 4], rows[3 * kTileN / 4], col);
 #pragma unroll
           for (int m = 0; m < MR; ++m) {
-            const uint2 aw = *reinterpret_cast<const uint2*>(act + (gl * MR + m) * 64 + b * 8);
+            // 8 K of row m split by parity: (the 4 even K, the 4 odd K)
+            const uint2 raw = *reinterpret_cast<const uint2*>(act + (m * p.gmax + gl) * 64 + b * 8);
+            const uint2 aw = make_uint2(__byte_perm(raw.x, raw.y, 0x6420), __byte_perm(raw.x, raw.y, 0x7531));
+            asum[h][m] = __dp4a(static_cast<int>(raw.x), 0x01010101, __dp4a(static_cast<int>(raw.y), 0x01010101, asum[h][m]));
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               isum[h][j][m] = dp4a_us(col[j] & 0x0F0F0F0Fu, static_cast<int>(aw.x), isum[h][j][m]);
@@ -338,7 +343,6 @@ __global__ void __launch_bounds__(kRgThreads, 1) dp_gemv_kernel(const __grid_con
         }
       }
       // out += float(int32 sub-block sum) * (a_s * ws)   (kernels/w4.py:103-104)
-      const int* asg = asum + gl * MR * 2;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int col_n = lane * 4 + j;
@@ -349,7 +353,7 @@ __global__ void __launch_bounds__(kRgThreads, 1) dp_gemv_kernel(const __grid_con
             const int z = sg.has_z ? static_cast<int>(zz[h * kTileN + col_n]) : 8;
 #pragma unroll
             for (int m = 0; m < MR; ++m) {
-              const int v = isum[h][j][m] - z * asg[m * 2 + h];
+              const int v = isum[h][j][m] - z * asum[h][m];
               acc[j][m] = __fadd_rn(acc[j][m], __fmul_rn(__int2float_rn(v), __fmul_rn(as_g[m], ws)));
             }
           }
@@ -358,7 +362,7 @@ __global__ void __launch_bounds__(kRgThreads, 1) dp_gemv_kernel(const __grid_con
           const int z = sg.has_z ? static_cast<int>(zz[col_n]) : 8;
 #pragma unroll
           for (int m = 0; m < MR; ++m) {
-            const int v = isum[0][j][m] + isum[1][j][m] - z * (asg[m * 2] + asg[m * 2 + 1]);
+            const int v = isum[0][j][m] + isum[1][j][m] - z * (asum[0][m] + asum[1][m]);
             acc[j][m] = __fadd_rn(acc[j][m], __fmul_rn(__int2float_rn(v), __fmul_rn(as_g[m], ws)));
           }
         }

@@ -64,7 +64,8 @@ struct GemmArgs {
   unsigned* fault;
 };
 
-__device__ __forceinline__ int gm_seg_of(const GemmArgs& p, int ht) {
+template <class Args>
+__device__ __forceinline__ int gm_seg_of(const Args& p, int ht) {
   int si = 0;
   if (p.nseg > 1 && ht >= p.seg[1].tile_begin) si = 1;
   if (p.nseg > 2 && ht >= p.seg[2].tile_begin) si = 2;

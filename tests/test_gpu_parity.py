@@ -257,7 +257,7 @@ def test_gate_up_quant_w8_sweep(pkg, dev, M):
     assert_quant_close(q.cpu().numpy(), qs.cpu().numpy(), rq, rs, f"gate_up_quant M={M}")
 
 
-@pytest.mark.parametrize("M", [1, 4, 9])
+@pytest.mark.parametrize("M", [1, 3, 4, 9])
 @pytest.mark.parametrize("wg,zeros", [(128, True), (64, False), (32, True)])
 def test_gate_up_quant_w4_sweep(pkg, dev, M, wg, zeros):
     K, N = 2048, 1536
