@@ -548,6 +548,17 @@ def kernel_case(pkg, dev, name):
         out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
         work = (2.0 * M * N * K, "op") if M >= 128 else (K * N + N * 4 + M * K * (1 + 4 / 64) + M * N * 2, "B")
         return (lambda: pkg.gemm_i8(a_q, a_s, b, bs, out)), work[0], work[1]
+    if name == "attn_decode_cfg4":
+        # config-4 attention read: B=4, 8 query / 2 KV heads of 256 dims, 1025 int8 positions
+        B, NQ, NKV, HD, SEQ = 4, 8, 2, 256, 1040
+        q = (torch.randn(B, NQ * HD, device=dev, generator=g) * 0.06).to(torch.bfloat16)
+        kv = torch.randint(-127, 128, (B * SEQ, 2 * NKV * HD), dtype=torch.int8, device=dev, generator=g)
+        kvs = torch.rand(B * SEQ, 2 * NKV, device=dev, generator=g) * 0.02 + 1e-3
+        out = torch.empty(B, NQ * HD, dtype=torch.bfloat16, device=dev)
+        pos = torch.tensor([1024], dtype=torch.int32, device=dev)
+        nbytes = B * 1025 * (2 * NKV * HD + 2 * NKV * 4) + 2 * B * NQ * HD * 2
+        return (lambda: pkg.attn_decode(q, kv, out, pos, kvs=kvs, kv_int8=True, batch=B, nq=NQ, nkv=NKV, hd=HD,
+                                        max_pos=SEQ - 1)), nbytes, "B"
     if name == "decode_step_b4":
         st = pkg.decode_step.HybridStack(pkg.decode_step.QWEN35_2B, dev, 4, 1040, kv_int8=True, seed=11)
         ids = torch.randint(0, st.V, (4,), device=dev)
@@ -790,7 +801,7 @@ def main():
                 "repeats": len(samples),
                 "ms_per_step_spread": [secs_min / args.steps * 1e3, secs_max / args.steps * 1e3],
                 "parallelism": f"replicas x{world}"},
-            "roofline": {"bound": "hbm", "kernel": "mlp_gate_up_quant_w4 M=4 (tcgen05 weight streaming)",
+            "roofline": {"bound": "hbm", "kernel": "mlp_gate_up_quant_w4 M=4 (dp4a GEMV, W4 weights resident and packed)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": peak_kind, "bytes_per_launch": gu_bytes,
                          "launch_us": gu_launch_s * 1e6,

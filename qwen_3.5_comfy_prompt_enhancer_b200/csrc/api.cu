@@ -346,6 +346,10 @@ QLIN_KNOB(tune_dp, "QLIN_TUNE_DP", 1)  // 0: decode rows take the tensor-core ke
 // wave, 2 whenever a ring plan exists
 QLIN_KNOB(tune_dp_stream, "QLIN_TUNE_DP_STREAM", 1)
 QLIN_KNOB(tune_dp_maxm, "QLIN_TUNE_DP_MAXM", 4)  // rows the dp kernel may serve
+QLIN_KNOB(tune_ad_smax, "QLIN_TUNE_AD_SMAX", 8)  // attn_decode: largest cluster
+QLIN_KNOB(tune_dp_m4, "QLIN_TUNE_DP_M4", 0)  // 1: 3-4 rows take any dp plan (W8 too)
+QLIN_KNOB(tune_dp_m4ring, "QLIN_TUNE_DP_M4RING", 1)  // 0: 3-4 rows never take a ring plan
+QLIN_KNOB(tune_ad_hsplit, "QLIN_TUNE_AD_HSPLIT", 0)  // attn_decode: forced query-head split (0: planner)
 #undef QLIN_KNOB
 
 bool use_dp() { return tune_dp() != 0; }
@@ -1164,9 +1168,20 @@ bool plan_dp_uncached(int wb, int mr, int ns, int K, int wgrp, int tiles, int sm
     // W4 gate/up 8.2 vs 10.0 (two items per warp), down 6.2 vs 6.8, o 3.9 vs
     // 4.0, qkv 4.9 vs 4.7; config-5 gate/up shards (2.5 items per warp) 19.8
     // vs 16.9 and 18.3 vs 12.2; W8 config 1 4.7 vs 4.0.
-    if (wb != 4 || !has_res || !one_wave || res.gmax * ns > 2 * kRgWarps) return false;
-    *pl = res;
-    return true;
+    if (tune_dp_m4() == 0) {
+      if (wb != 4) return false;
+      if (has_res && one_wave && res.gmax * ns <= 2 * kRgWarps) {
+        *pl = res;
+        return true;
+      }
+      // long-K launches of one stream with no resident plan: the ring, with
+      // K parts over the SMs (the tensor-core kernel caps the K split at the
+      // cluster size).  Config-5 down 17408 -> 5120 and its 2-, 4-, 8-GPU
+      // shards at M = 4: 25.1 / 16.4 / 16.1 / 17.7 us against 30.2 / 16.5 /
+      // 19.7 / 18.0 on the tensor cores.
+      if (ns == 1 && !has_res && tune_dp_m4ring()) return plan_dp_ring(wb, mr, ns, K, wgrp, tiles, sms, pl);
+      return false;
+    }
   }
   const int mode = tune_dp_stream();
   if (has_res && (mode == 0 || (mode == 1 && one_wave))) {
@@ -1241,9 +1256,13 @@ int launch_dp_t(const DpArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
 template <int WB, int EPI>
 int launch_dp_mr(int mr, const DpArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
   if (mr == 1) return launch_dp_t<WB, 1, EPI>(a, grid, smem, st);
+#ifdef QLIN_TUNING
+  if (mr == 4) return launch_dp_t<WB, 4, EPI>(a, grid, smem, st);
+#else
   if constexpr (WB == 4) {
     if (mr == 4) return launch_dp_t<WB, 4, EPI>(a, grid, smem, st);
   }
+#endif
   return launch_dp_t<WB, 2, EPI>(a, grid, smem, st);
 }
 
@@ -2216,7 +2235,7 @@ int qlin_attn_decode(const void* q, const void* kvc, const float* kvs, void* out
   // a device-side position the split follows the largest position expected
   const long long n = (pos_dev ? (max_pos > pos ? max_pos : pos) : pos) + 1;
   int S = static_cast<int>((n + 63) / 64);
-  if (S > 8) S = 8;
+  if (S > tune_ad_smax()) S = tune_ad_smax();
   if (S < 1) S = 1;
   const int Gfull = static_cast<int>(nq / nkv);
   if (!(Gfull == 1 || Gfull == 2 || Gfull == 4 || Gfull == 8))
@@ -2225,10 +2244,13 @@ int qlin_attn_decode(const void* q, const void* kvc, const float* kvs, void* out
   const int B = static_cast<int>(batch), NKV = static_cast<int>(nkv);
   // Split a KV head's query heads over more CTAs until the launch covers the
   // SMs (the extra reads of the same cache rows mostly hit L2).  Measured on
-  // B200, config 4 (B = 4, 8 query / 2 KV heads, 1025 int8 positions): one
-  // CTA group per KV head took 19.3 us per launch.
+  // B200, config 4 (B = 4, 8 query / 2 KV heads, 1025 int8 positions, graph
+  // replay): 12.9 us with the heads split over 4 CTA groups (256 CTAs in
+  // clusters of 8), 22.6 us over 2, 19.1 us unsplit; clusters of 4 at the
+  // 4-way split 18.7 us.
   int hsplit = 1;
   while (hsplit < Gfull && static_cast<long long>(S) * NKV * hsplit * B < di.sms) hsplit *= 2;
+  if (tune_ad_hsplit() > 0 && tune_ad_hsplit() <= Gfull && Gfull % tune_ad_hsplit() == 0) hsplit = tune_ad_hsplit();
   if (static_cast<long long>(NKV) * hsplit > 65535) hsplit = 1;
   a.hsplit = hsplit;
   const int G = Gfull / hsplit;

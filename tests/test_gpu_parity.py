@@ -388,7 +388,7 @@ def test_config5_tp_layer_shapes(pkg, dev, M):
     assert_bf16_close(bits(out)[:, c], ref, "cfg5 down")
 
 
-@pytest.mark.parametrize("M", [1, 2])
+@pytest.mark.parametrize("M", [1, 2, 3, 4])
 @pytest.mark.parametrize("wg,zeros", [(32, True), (64, False), (128, True)])
 def test_long_k_few_tiles_k_parts(pkg, dev, M, wg, zeros):
     """Long K over few column tiles (the 8-GPU config-5 down projection,
