@@ -1455,9 +1455,17 @@ int peer_buffers(PeerGatherArgs& a, void* const* bufs, void* const* arrive, int 
 
 int peer_launch(const PeerGatherArgs& a, int ctas, cudaStream_t st) {
   if (int r = prefer_shared(reinterpret_cast<const void*>(peer_allgather_kernel))) return r;
-  peer_allgather_kernel<<<ctas, kPeerThreads, 0, st>>>(a);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "peer_allgather_kernel launch");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ctas, 1, 1);
+  cfg.blockDim = dim3(kPeerThreads, 1, 1);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, peer_allgather_kernel, a);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(peer_allgather)");
   return QLIN_OK;
 }
 

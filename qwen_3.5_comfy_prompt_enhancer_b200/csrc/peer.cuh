@@ -61,9 +61,9 @@ struct PeerGatherArgs {
 __device__ __forceinline__ void st_release_sys_add(unsigned* p, unsigned v) {
   asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+__device__ __forceinline__ unsigned ld_relaxed_sys(const unsigned* p) {
   unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 
@@ -82,15 +82,23 @@ __device__ __forceinline__ void peer_copy_part(const PeerGatherArgs& a, const Pe
 }
 
 __global__ void __launch_bounds__(kPeerThreads) peer_allgather_kernel(const __grid_constant__ PeerGatherArgs a) {
+  // The next launch may be placed now; the parts are read only once the
+  // preceding kernel (their producer) has completed.
+  pdl_launch_dependents();
+  pdl_wait();
   // 1. my parts -> my slot of every rank's buffer
   for (int pi = 0; pi < a.nparts; ++pi) {
     if (a.part[pi].unit == 16) peer_copy_part<uint4>(a, a.part[pi]);
     else peer_copy_part<uint32_t>(a, a.part[pi]);
   }
-  // 2. announce this CTA's part on every rank
-  __threadfence_system();
+  // 2. announce this CTA's part on every rank: the CTA barrier orders every
+  // thread's stores before the signalling thread's system-scope release
+  // (cumulativity), so one fence per signal, not one per thread
   __syncthreads();
-  if (threadIdx.x < a.world) st_release_sys_add(a.arrive[threadIdx.x] + a.rank, 1u);
+  if (threadIdx.x < a.world) {
+    __threadfence_system();
+    st_release_sys_add(a.arrive[threadIdx.x] + a.rank, 1u);
+  }
   if (!a.all_wait && blockIdx.x != 0) return;
   // 3. wait for every rank's parts of this call
   __shared__ int failed;
@@ -100,13 +108,16 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allgather_kernel(const __gr
     const unsigned want = a.expected[threadIdx.x] + gridDim.x;
     const unsigned* mine = a.arrive[a.rank] + threadIdx.x;
     const unsigned long long t0 = global_ns();
-    // counters wrap after 2^32 parts; the signed difference stays valid
-    while (static_cast<int>(ld_acquire_sys(mine) - want) < 0) {
+    // counters wrap after 2^32 parts; the signed difference stays valid.
+    // Relaxed polling, then one system-scope fence: the acquire side of the
+    // peers' release.
+    while (static_cast<int>(ld_relaxed_sys(mine) - want) < 0) {
       if (global_ns() - t0 > wait_limit_ns()) {
         failed = 1;
         break;
       }
     }
+    __threadfence_system();
   }
   __syncthreads();
   if (threadIdx.x == 0 && failed) record_fault(a.fault, kFaultFullWait);
