@@ -303,13 +303,14 @@ int qlin_dev_free(void* ptr);
 int qlin_peer_allgather(void* const* bufs, void* const* arrive, void* expected, const void* src,
                         int64_t shard_bytes, int world, int rank, void* dst, void* stream);
 
-/* One 2-D block of this rank's data for qlin_peer_allgather_parts: `rows`
- * rows of `row_bytes` bytes, `src_ld` bytes apart.  Rank q's block lands in
- * every rank's gather buffer at byte dst_off + q * row_bytes, rows dst_ld
- * bytes apart -- so a shard of output COLUMNS goes straight into its column
- * range of a row-major [rows, world * row_bytes / element size] matrix.
- * Sizes, strides, offsets and the source address must be multiples of 4
- * (16 for the fast path). */
+/* One 2-D block of this rank's data for qlin_peer_allgather_ll: `rows` rows
+ * of `row_bytes` bytes, `src_ld` bytes apart.  Rank q's block lands in every
+ * rank's destination at byte dst_off + q * row_bytes, rows dst_ld bytes apart
+ * -- so a shard of output COLUMNS goes straight into its column range of a
+ * row-major [rows, world * row_bytes / element size] matrix.  row_bytes,
+ * dst_off and dst_ld must be multiples of 4 (multiples of 8 move twice the
+ * data per store); the source, its stride and the destination must be
+ * aligned to the same 8 or 4 bytes. */
 typedef struct {
   const void* src;
   int64_t src_ld;
@@ -319,24 +320,34 @@ typedef struct {
   int64_t dst_ld;
 } qlin_gather_part;
 
-/* Words of the per-rank state array of qlin_peer_allgather_parts. */
+/* Words of the per-rank state array of qlin_peer_allgather_ll. */
 #define QLIN_PEER_STATE_WORDS 16
 
-/* All-gather of one or two 2-D parts (qlin_gather_part) into every rank's
- * buffer bufs[q] (each must hold dst_off + (rows - 1) * dst_ld +
- * world * row_bytes bytes for every part), then a wait until every rank's
- * parts have landed in bufs[rank].  If `dst` is not null, every CTA then
- * copies the first dst_bytes (multiple of 16) of bufs[rank] to dst within
- * the same launch.  arrive[q] is rank q's array of `world` uint32 arrival
- * counters (zero once, never reset); `state` is this rank's device array of
- * QLIN_PEER_STATE_WORDS uint32 (zero once) holding the expected counts.
- * Every rank must call it with the same sizes.  A wait that does not finish
- * within the wait limit records a device fault.  Not part of the
- * reference's interface (it has no multi-GPU path); the column-split layer
- * (tp.py) gathers its h codes + scales and its output with it. */
-int qlin_peer_allgather_parts(void* const* bufs, void* const* arrive, void* state,
-                              const qlin_gather_part* parts, int nparts, int world, int rank,
-                              void* dst, int64_t dst_bytes, void* stream);
+/* Bytes of the exchange buffer every rank needs for qlin_peer_allgather_ll
+ * with these parts at `world` ranks (twice the data of all ranks, twice over
+ * for the two alternating halves).  No GPU needed. */
+int qlin_peer_ll_bytes(const qlin_gather_part* parts, int nparts, int world, int64_t* bytes);
+
+/* All-gather of one to four 2-D parts (qlin_gather_part) into `dst`, this
+ * rank's destination, on every rank.  ll[q] is rank q's exchange buffer
+ * (this rank's own at [rank], the others opened through CUDA IPC), at least
+ * ll_bytes >= qlin_peer_ll_bytes(...) bytes, 16-byte aligned and zeroed once;
+ * `state` is this rank's device array of QLIN_PEER_STATE_WORDS uint32, zeroed
+ * once.  Every 8-byte word a rank stores into a peer's exchange buffer
+ * carries the call's sequence number beside 4 data bytes, so the receiving
+ * kernel knows a word has landed by reading it: no fence, counter or second
+ * round trip stands between the stores and the data's use, which is what
+ * makes this the low-latency form for the few-KB gathers of a decode step.
+ * The kernel copies this rank's blocks into its own slots of dst, stores them
+ * into every peer's exchange buffer, then waits for every peer's words and
+ * writes them into the peers' slots of dst.  Every rank must call it with the
+ * same sizes, the same number of times, in the same order for the same
+ * buffers.  A wait that does not finish within the wait limit records a
+ * device fault.  Not part of the reference's interface (it has no multi-GPU
+ * path); the column-split layer (tp.py) gathers its h codes + scales and its
+ * output with it. */
+int qlin_peer_allgather_ll(void* const* ll, int64_t ll_bytes, void* state, const qlin_gather_part* parts,
+                           int nparts, int world, int rank, void* dst, void* stream);
 
 /* All-gather that allocates nothing, for one rank.  It has no counterpart in
  * the reference.  Meant for a process that runs the column-split layer on a

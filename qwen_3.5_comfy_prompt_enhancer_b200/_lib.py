@@ -55,7 +55,8 @@ SIGNATURES = {
     "qlin_dev_alloc": [_I, ctypes.POINTER(ctypes.c_void_p)],
     "qlin_dev_free": [_P],
     "qlin_peer_allgather": [_P, _P, _P, _P, _I, ctypes.c_int, ctypes.c_int, _P, _P],
-    "qlin_peer_allgather_parts": [_P, _P, _P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _I, _P],
+    "qlin_peer_ll_bytes": [_P, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int64)],
+    "qlin_peer_allgather_ll": [_P, _I, _P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P],
     "qlin_peer_allgather_static": [_P, _I, _P, _P],
 }
 _RESTYPES = {

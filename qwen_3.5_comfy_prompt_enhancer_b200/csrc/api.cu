@@ -1654,48 +1654,102 @@ int qlin_peer_allgather(void* const* bufs, void* const* arrive, void* expected, 
   return QLIN_OK;
 }
 
-int qlin_peer_allgather_parts(void* const* bufs, void* const* arrive, void* state, const qlin_gather_part* parts,
-                              int nparts, int world, int rank, void* dst, int64_t dst_bytes, void* stream) {
-  if (world < 1 || world > kPeerMax || rank < 0 || rank >= world)
-    return fail(QLIN_ERR_INVALID_ARGUMENT, "world %d / rank %d", world, rank);
-  if (!bufs || !arrive || !state || !parts) return fail(QLIN_ERR_INVALID_ARGUMENT, "null argument");
-  if (nparts < 1 || nparts > kPeerMaxParts)
-    return fail(QLIN_ERR_INVALID_ARGUMENT, "%d parts (1 to %d)", nparts, kPeerMaxParts);
-  if (!aligned(state, 4)) return fail(QLIN_ERR_ALIGNMENT, "state must be 4-byte aligned");
-  if (dst && (dst_bytes <= 0 || dst_bytes % 16 != 0 || !aligned(dst, 16)))
-    return fail(QLIN_ERR_ALIGNMENT, "dst must be 16-byte aligned with a positive multiple of 16 bytes");
-  DevInfo di;
-  if (int r = launch_info(&di)) return r;
-  PeerGatherArgs a;
-  memset(&a, 0, sizeof(a));
-  if (int r = peer_buffers(a, bufs, arrive, world)) return r;
-  long long units16 = 0;
+// Flagged-word exchange layout of `parts`: per part its unit (8 data bytes
+// per 16-byte store, or 4 per 8-byte store) and its offset in a sender slot.
+// Depends on the sizes only, so every rank (same sizes) gets the same layout.
+int ll_layout(const qlin_gather_part* parts, int nparts, int world, LlGatherArgs* a) {
+  if (world < 1 || world > kPeerMax) return fail(QLIN_ERR_INVALID_ARGUMENT, "world %d (1 to %d)", world, kPeerMax);
+  if (!parts) return fail(QLIN_ERR_INVALID_ARGUMENT, "null parts");
+  if (nparts < 1 || nparts > kLlMaxParts)
+    return fail(QLIN_ERR_INVALID_ARGUMENT, "%d parts (1 to %d)", nparts, kLlMaxParts);
+  long long off = 0, units = 0;
   for (int i = 0; i < nparts; ++i) {
     const qlin_gather_part& q = parts[i];
-    if (!q.src || q.rows < 1 || q.row_bytes < 4 || q.src_ld < 0 || q.dst_off < 0 || q.dst_ld < 0)
-      return fail(QLIN_ERR_INVALID_ARGUMENT, "part %d: null source or bad size", i);
+    if (q.rows < 1 || q.row_bytes < 4 || q.src_ld < 0 || q.dst_off < 0 || q.dst_ld < 0)
+      return fail(QLIN_ERR_INVALID_ARGUMENT, "part %d: bad size", i);
     if (q.rows > 1 && (q.src_ld < q.row_bytes || q.dst_ld < static_cast<int64_t>(world) * q.row_bytes))
       return fail(QLIN_ERR_SHAPE, "part %d: row strides overlap the rows / the ranks' slots", i);
-    auto all_mult = [&](int u) {
-      return q.row_bytes % u == 0 && q.src_ld % u == 0 && q.dst_off % u == 0 && q.dst_ld % u == 0 &&
-             aligned(q.src, u);
-    };
-    const int unit = all_mult(16) ? 16 : all_mult(4) ? 4 : 0;
-    if (!unit) return fail(QLIN_ERR_ALIGNMENT, "part %d: sizes, strides and addresses must be multiples of 4", i);
-    a.part[i] = PeerPart{static_cast<const uint8_t*>(q.src), q.src_ld, q.rows, q.row_bytes, q.dst_off, q.dst_ld,
-                         unit};
-    units16 += (q.rows * q.row_bytes + 15) / 16;
+    auto mult = [&](int u) { return q.row_bytes % u == 0 && q.dst_off % u == 0 && q.dst_ld % u == 0; };
+    const int unit = mult(8) ? 8 : mult(4) ? 4 : 0;
+    if (!unit) return fail(QLIN_ERR_ALIGNMENT, "part %d: row bytes and destination offsets must be multiples of 4", i);
+    LlPart& p = a->part[i];
+    p.src = static_cast<const uint8_t*>(q.src);
+    p.src_ld = q.src_ld;
+    p.rows = q.rows;
+    p.row_bytes = q.row_bytes;
+    p.dst_off = q.dst_off;
+    p.dst_ld = q.dst_ld;
+    p.ll_off = off;
+    p.first = units;
+    p.unit = unit;
+    const long long n = q.rows * (q.row_bytes / unit);
+    units += n;
+    off += (n * 2 * unit + 15) / 16 * 16;
   }
-  a.nparts = nparts;
-  a.expected = static_cast<unsigned*>(state);
+  a->nparts = nparts;
+  a->units = units;
+  a->slot_bytes = off;
+  return QLIN_OK;
+}
+
+int qlin_peer_ll_bytes(const qlin_gather_part* parts, int nparts, int world, int64_t* bytes) {
+  if (!bytes) return fail(QLIN_ERR_INVALID_ARGUMENT, "null result");
+  LlGatherArgs a;
+  memset(&a, 0, sizeof(a));
+  if (int r = ll_layout(parts, nparts, world, &a)) return r;
+  *bytes = 2LL * world * a.slot_bytes;
+  return QLIN_OK;
+}
+
+int qlin_peer_allgather_ll(void* const* ll, int64_t ll_bytes, void* state, const qlin_gather_part* parts,
+                           int nparts, int world, int rank, void* dst, void* stream) {
+  if (world < 1 || world > kPeerMax || rank < 0 || rank >= world)
+    return fail(QLIN_ERR_INVALID_ARGUMENT, "world %d / rank %d", world, rank);
+  if (!ll || !state || !parts || !dst) return fail(QLIN_ERR_INVALID_ARGUMENT, "null argument");
+  if (!aligned(state, 4)) return fail(QLIN_ERR_ALIGNMENT, "state must be 4-byte aligned");
+  LlGatherArgs a;
+  memset(&a, 0, sizeof(a));
+  if (int r = ll_layout(parts, nparts, world, &a)) return r;
+  if (ll_bytes < 2LL * world * a.slot_bytes)
+    return fail(QLIN_ERR_SHAPE, "exchange buffers of %lld bytes, %lld needed", (long long)ll_bytes,
+                2LL * world * a.slot_bytes);
+  for (int q = 0; q < world; ++q) {
+    if (!ll[q] || !aligned(ll[q], 16)) return fail(QLIN_ERR_ALIGNMENT, "exchange buffer %d is null or misaligned", q);
+    a.ll[q] = static_cast<uint8_t*>(ll[q]);
+  }
+  for (int i = 0; i < nparts; ++i) {
+    const LlPart& p = a.part[i];
+    if (!p.src || !aligned(p.src, p.unit) || p.src_ld % p.unit != 0 || !aligned(dst, p.unit))
+      return fail(QLIN_ERR_ALIGNMENT, "part %d: source, source stride and destination must be %d-byte aligned", i,
+                  p.unit);
+  }
+  DevInfo di;
+  if (int r = launch_info(&di)) return r;
+  a.state = static_cast<unsigned*>(state);
   a.dst = static_cast<uint8_t*>(dst);
-  a.dst_bytes = dst ? dst_bytes : 0;
-  a.all_wait = dst ? 1 : 0;
   a.world = world;
   a.rank = rank;
   a.fault = di.fault;
-  if (dst && dst_bytes / 16 > units16) units16 = dst_bytes / 16;
-  return peer_launch(a, peer_ctas(units16), static_cast<cudaStream_t>(stream));
+  // units per thread: about two sends or receives
+  const long long work = a.units * (world > 1 ? world - 1 : 1);
+  long long ctas = (work + kPeerThreads * 2 - 1) / (kPeerThreads * 2);
+  if (ctas > kLlMaxCtas) ctas = kLlMaxCtas;
+  if (ctas > di.sms) ctas = di.sms;
+  if (ctas < 1) ctas = 1;
+  const void* kern = reinterpret_cast<const void*>(peer_ll_gather_kernel);
+  if (int r = prefer_shared(kern)) return r;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(ctas), 1, 1);
+  cfg.blockDim = dim3(kPeerThreads, 1, 1);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, peer_ll_gather_kernel, a);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(peer_ll_gather)");
+  return QLIN_OK;
 }
 
 int qlin_peer_allgather_static(const void* src, int64_t shard_bytes, void* dst, void* stream) {

@@ -1,30 +1,21 @@
-// All-gather over NVLink peer memory for the column-split layer.
+// All-gathers over NVLink peer memory for the column-split layer.
 //
-// Every rank owns a gather buffer and an arrival array of `world` 32-bit
-// counters, both opened by every other rank through CUDA IPC (no multicast
-// objects).  One launch of peer_allgather_kernel on rank r:
-//   1. every CTA copies its slice of r's parts into r's slot of every rank's
-//      gather buffer -- its own included -- over NVLink.  A part is a 2-D
-//      block (rows x row_bytes, source row stride src_ld); rank r's slot
-//      starts at dst_off + r * row_bytes with row stride dst_ld, so a shard of
-//      output COLUMNS lands directly in its column range of every rank's
-//      [rows, world * row_bytes] matrix (a 1-D shard is one row);
-//   2. each CTA then fences at system scope and adds 1 to arrival[r] on every
-//      rank (release, system scope);
-//   3. the waiting CTAs (CTA 0, or every CTA when the gathered bytes are also
-//      copied out) wait until their own arrival[q] has reached expected[q] +
-//      gridDim.x for every rank q (acquire).  expected lives in device memory
-//      and advances by gridDim.x per call, so the kernel also works inside
-//      CUDA-graph replays; when every CTA waits, the last one to finish (a
-//      completion counter) advances it, after all CTAs have read it.  The wait
-//      is time-bounded: past the limit it records a fault and returns (the
+// peer_allgather_kernel (arrival counters).  Every rank owns a gather buffer
+// and an arrival array of `world` 32-bit counters, both opened by every
+// other rank through CUDA IPC (no multicast objects).  One launch on rank r:
+//   1. every CTA copies its slice of r's shard into r's slot of every rank's
+//      gather buffer -- its own included -- over NVLink;
+//   2. each CTA then adds 1 to arrival[r] on every rank (release, system
+//      scope, after one system-scope fence);
+//   3. CTA 0 waits until its own arrival[q] has reached expected[q] +
+//      gridDim.x for every rank q, then advances expected (device memory, so
+//      the kernel also works inside CUDA-graph replays).  The wait is
+//      time-bounded: past the limit it records a fault and returns (the
 //      context stays usable).
-//   4. optionally every CTA then copies its slice of the local gather buffer
-//      to `dst`.
-// Counters only grow, so no reset is ever needed.  A buffer is not rewritten
-// while a peer may still read it: the layer calls the gather twice per
-// forward (h, then the output), and a rank's second gather cannot complete
-// before every rank has finished the work between the two.
+// Counters only grow, so no reset is ever needed.
+//
+// peer_ll_gather_kernel (flagged words, below) is the lower-latency form the
+// column-split layer uses.
 #pragma once
 
 #include "qlin_common.cuh"
@@ -48,12 +39,9 @@ struct PeerPart {
 struct PeerGatherArgs {
   uint8_t* bufs[kPeerMax];        // every rank's gather buffer (peer pointers; own at [rank])
   unsigned* arrive[kPeerMax];     // every rank's arrival counters (peer pointers)
-  unsigned* expected;             // this rank's expected counts [world] (+ a completion counter at [kPeerMax])
+  unsigned* expected;             // this rank's expected counts [world]
   PeerPart part[kPeerMaxParts];
   int nparts;
-  uint8_t* dst;                   // optional: local gathered bytes [0, dst_bytes) copied here
-  long long dst_bytes;            // multiple of 16
-  int all_wait;                   // every CTA waits (needed for the copy to dst)
   int world, rank;
   unsigned* fault;
 };
@@ -99,7 +87,7 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allgather_kernel(const __gr
     __threadfence_system();
     st_release_sys_add(a.arrive[threadIdx.x] + a.rank, 1u);
   }
-  if (!a.all_wait && blockIdx.x != 0) return;
+  if (blockIdx.x != 0) return;
   // 3. wait for every rank's parts of this call
   __shared__ int failed;
   if (threadIdx.x == 0) failed = 0;
@@ -121,27 +109,163 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allgather_kernel(const __gr
   }
   __syncthreads();
   if (threadIdx.x == 0 && failed) record_fault(a.fault, kFaultFullWait);
-  // 4. copy the gathered bytes out
-  if (a.dst) {
-    const long long n16 = a.dst_bytes / 16;
-    const uint4* s = reinterpret_cast<const uint4*>(a.bufs[a.rank]);
-    uint4* d = reinterpret_cast<uint4*>(a.dst);
-    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n16;
-         i += static_cast<long long>(gridDim.x) * blockDim.x)
-      d[i] = s[i];
+  // advance the expected counts (only this CTA reads them)
+  if (threadIdx.x < a.world) a.expected[threadIdx.x] += gridDim.x;
+}
+
+// ---------------------------------------------------------------- flagged-word all-gather
+// The column-split layer's gathers are a few KB to a few MB per rank and sit
+// between two dependent kernels, so their latency, not their bandwidth, is
+// what the layer pays.  The arrival-counter protocol above needs a
+// system-scope fence after the NVLink stores (a round trip to every peer)
+// before the release, and an acquire on the waiting side.  This protocol
+// needs neither: every 8-byte word a rank sends carries the call's sequence
+// number in its high half, so a receiver that reads a word with the current
+// sequence number holds valid data (a naturally aligned 64-bit access is
+// single-copy atomic, and each word is checked on its own).
+//
+// Exchange buffer of every rank (zero once): [2 parities][world senders]
+// [slot_bytes]; call number s uses parity s & 1.  A sender's slot holds its
+// parts one after the other, each padded to 16 bytes, as words
+// (seq << 32 | 4 data bytes): two words per 8 data bytes (unit 8, one 16-byte
+// store) or one word per 4 data bytes (unit 4).  One launch on rank r:
+//   1. for every unit of r's parts: copy it into r's slot of `dst` and store
+//      its words into r's slot of every other rank's exchange buffer;
+//   2. for every unit of every other rank q: poll own exchange buffer until
+//      the words carry this call's sequence number (bounded), then write the
+//      data into q's slot of `dst`;
+//   3. the last CTA to finish advances the sequence number in `state`.
+// Two parities suffice: rank r's call s + 2 starts after its call s + 1 has
+// received every rank's call-(s + 1) words, which every rank sends only once
+// its own call s (and so its reads of parity s & 1) has completed.
+constexpr int kLlMaxParts = 4;
+constexpr int kLlMaxCtas = 148;
+
+struct LlPart {
+  const uint8_t* src;    // this rank's block: rows x row_bytes, row stride src_ld
+  long long src_ld;
+  long long rows, row_bytes;
+  long long dst_off, dst_ld;   // rank q's block at dst + dst_off + q * row_bytes, rows dst_ld apart
+  long long ll_off;      // byte offset of the part's words in a sender slot (multiple of 16)
+  long long first;       // index of the part's first unit among all parts' units
+  int unit;              // data bytes per unit: 8 or 4
+};
+
+struct LlGatherArgs {
+  uint8_t* ll[kPeerMax];   // every rank's exchange buffer (peer pointers; own at [rank])
+  long long slot_bytes;    // bytes of one sender slot
+  unsigned* state;         // [0] sequence number of the last call, [1] completion counter
+  LlPart part[kLlMaxParts];
+  int nparts;
+  long long units;         // all parts' units
+  uint8_t* dst;            // this rank's destination
+  int world, rank;
+  unsigned* fault;
+};
+
+__device__ __forceinline__ void st_sys_v2(void* p, unsigned long long a, unsigned long long b) {
+  asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+__device__ __forceinline__ void st_sys_u64(void* p, unsigned long long a) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(a) : "memory");
+}
+__device__ __forceinline__ void ld_sys_v2(const void* p, unsigned long long& a, unsigned long long& b) {
+  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_sys_u64(const void* p) {
+  unsigned long long a;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(a) : "l"(p) : "memory");
+  return a;
+}
+// word carries call `seq` (or a later one, which the protocol never produces)
+__device__ __forceinline__ bool ll_fresh(unsigned long long w, unsigned seq) {
+  return static_cast<int>(static_cast<unsigned>(w >> 32) - seq) >= 0;
+}
+
+__device__ __forceinline__ int ll_part_of(const LlGatherArgs& a, long long u) {
+  int p = 0;
+  while (p + 1 < a.nparts && u >= a.part[p + 1].first) ++p;
+  return p;
+}
+
+__global__ void __launch_bounds__(kPeerThreads) peer_ll_gather_kernel(const __grid_constant__ LlGatherArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const unsigned seq = a.state[0] + 1u;
+  const long long par = static_cast<long long>(seq & 1u) * a.world * a.slot_bytes;
+  const long long tid = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  const unsigned long long tag = static_cast<unsigned long long>(seq) << 32;
+  // 1. send
+  for (long long u = tid; u < a.units; u += stride) {
+    const LlPart& p = a.part[ll_part_of(a, u)];
+    const long long v = u - p.first, per_row = p.row_bytes / p.unit;
+    const long long row = v / per_row, c = (v - row * per_row) * p.unit;
+    const uint8_t* s = p.src + row * p.src_ld + c;
+    uint8_t* d = a.dst + p.dst_off + a.rank * p.row_bytes + row * p.dst_ld + c;
+    const long long e = par + a.rank * a.slot_bytes + p.ll_off + v * 2 * p.unit;
+    if (p.unit == 8) {
+      const uint2 x = *reinterpret_cast<const uint2*>(s);
+      *reinterpret_cast<uint2*>(d) = x;
+      for (int q = 0; q < a.world; ++q)
+        if (q != a.rank) st_sys_v2(a.ll[q] + e, tag | x.x, tag | x.y);
+    } else {
+      const uint32_t x = *reinterpret_cast<const uint32_t*>(s);
+      *reinterpret_cast<uint32_t*>(d) = x;
+      for (int q = 0; q < a.world; ++q)
+        if (q != a.rank) st_sys_u64(a.ll[q] + e, tag | x);
+    }
   }
-  // advance the expected counts once every waiting CTA has read them
-  if (!a.all_wait) {
-    if (threadIdx.x < a.world) a.expected[threadIdx.x] += gridDim.x;
-    return;
-  }
+  // 2. receive
+  __shared__ int failed;
+  if (threadIdx.x == 0) failed = 0;
   __syncthreads();
+  bool dead = false;
+  const unsigned long long t0 = global_ns();
+  const long long total = static_cast<long long>(a.world - 1) * a.units;
+  for (long long i = tid; i < total && !dead; i += stride) {
+    const long long qi = i / a.units, u = i - qi * a.units;
+    const int q = static_cast<int>(qi) < a.rank ? static_cast<int>(qi) : static_cast<int>(qi) + 1;
+    const LlPart& p = a.part[ll_part_of(a, u)];
+    const long long v = u - p.first, per_row = p.row_bytes / p.unit;
+    const long long row = v / per_row, c = (v - row * per_row) * p.unit;
+    const uint8_t* w = a.ll[a.rank] + par + q * a.slot_bytes + p.ll_off + v * 2 * p.unit;
+    uint8_t* d = a.dst + p.dst_off + q * p.row_bytes + row * p.dst_ld + c;
+    unsigned spin = 0;
+    if (p.unit == 8) {
+      unsigned long long w0, w1;
+      for (;;) {
+        ld_sys_v2(w, w0, w1);
+        if (ll_fresh(w0, seq) && ll_fresh(w1, seq)) break;
+        if ((++spin & 63u) == 0 && global_ns() - t0 > wait_limit_ns()) {
+          dead = true;
+          break;
+        }
+      }
+      if (!dead) *reinterpret_cast<uint2*>(d) = make_uint2(static_cast<unsigned>(w0), static_cast<unsigned>(w1));
+    } else {
+      unsigned long long w0;
+      for (;;) {
+        w0 = ld_sys_u64(w);
+        if (ll_fresh(w0, seq)) break;
+        if ((++spin & 63u) == 0 && global_ns() - t0 > wait_limit_ns()) {
+          dead = true;
+          break;
+        }
+      }
+      if (!dead) *reinterpret_cast<uint32_t*>(d) = static_cast<unsigned>(w0);
+    }
+  }
+  if (dead) failed = 1;
+  __syncthreads();
+  if (threadIdx.x == 0 && failed) record_fault(a.fault, kFaultFullWait);
+  // 3. the last CTA advances the sequence number (every CTA has read it)
   __shared__ unsigned last;
-  if (threadIdx.x == 0) last = atomicAdd(a.expected + kPeerMax, 1u) == gridDim.x - 1 ? 1u : 0u;
+  if (threadIdx.x == 0) last = atomicAdd(a.state + 1, 1u) == gridDim.x - 1 ? 1u : 0u;
   __syncthreads();
-  if (last) {
-    if (threadIdx.x < a.world) a.expected[threadIdx.x] += gridDim.x;
-    if (threadIdx.x == 0) a.expected[kPeerMax] = 0;
+  if (last && threadIdx.x == 0) {
+    a.state[0] = seq;
+    a.state[1] = 0u;
   }
 }
 

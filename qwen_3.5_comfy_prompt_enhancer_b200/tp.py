@@ -16,11 +16,12 @@ launch shape, can differ):
   4. all-gather of the bf16 outputs -> [M, H] on every rank.
 
 With CUDA and world > 1 the gathers are this package's own kernel
-(``qlin_peer_allgather_parts``): each rank stores its column shard straight
-into its column range of every rank's h / output matrix over NVLink (CUDA IPC
-buffers, no NCCL on the data path), so the down projection reads h where it
-landed and the output gather also copies the result into ``out`` in the same
-launch -- four launches per forward.  ``gather="dist"`` uses
+(``qlin_peer_allgather_ll``): each rank stores its column shard as flagged
+8-byte words into every peer's exchange buffer over NVLink (CUDA IPC buffers,
+no NCCL on the data path), and every rank's kernel writes each peer's words,
+once they carry the call's number, into their column range of its own h /
+output matrix -- the down projection reads h where it landed and the output
+gather writes ``out`` itself: four launches per forward.  ``gather="dist"`` uses
 ``torch.distributed.all_gather_into_tensor`` (NCCL or gloo) and a column
 reassembly instead; that is the path the CPU tests take.
 
@@ -63,13 +64,14 @@ class _DeviceBytes:
 
 
 class PeerBuffer:
-    """A gather buffer of ``nbytes`` on every rank of ``group``, written by
-    every rank over NVLink peer memory (``qlin_peer_allgather_parts``).
+    """A gather destination of ``nbytes`` on every rank of ``group``, filled
+    by ``qlin_peer_allgather_ll`` over NVLink peer memory.
 
-    Each rank allocates its own buffer (one cudaMalloc of its own, shared
-    through one CUDA IPC handle exchanged once over the process group) with
-    its arrival counters behind it, plus a small state array.  ``local`` is a
-    torch uint8 view of this rank's buffer."""
+    ``local`` (torch uint8) is this rank's destination.  Behind it sits an
+    exchange buffer that every other rank stores its flagged words into: one
+    allocation of its own per rank, shared through one CUDA IPC handle
+    exchanged once over the process group, sized for gathers of at most
+    ``nbytes`` in all, plus a small state array (the call count)."""
 
     def __init__(self, nbytes, device, group=None):
         from . import _lib
@@ -80,15 +82,16 @@ class PeerBuffer:
         self.rank = dist.get_rank(group) if init else 0
         self.nbytes = _pad16(nbytes)
         self.device = torch.device(device)
-        total = self.nbytes + 256
+        # per sender: two 8-byte words per 8 data bytes, each part padded to 16
+        self.ll_bytes = 2 * self.world * (2 * _pad16(-(-self.nbytes // self.world)) + 16 * 4)
+        self.local = torch.zeros(self.nbytes, dtype=torch.uint8, device=self.device)
         with torch.cuda.device(self.device):
             own = ctypes.c_void_p()
-            _lib.check("qlin_dev_alloc", self._lib.qlin_dev_alloc(total, ctypes.byref(own)))
+            _lib.check("qlin_dev_alloc", self._lib.qlin_dev_alloc(self.ll_bytes, ctypes.byref(own)))
             self._own = own.value
             handle = (ctypes.c_ubyte * 64)()
             off = ctypes.c_int64()
             _lib.check("qlin_ipc_get_handle", self._lib.qlin_ipc_get_handle(self._own, handle, ctypes.byref(off)))
-        self.local = torch.as_tensor(_DeviceBytes(self._own, self.nbytes), device=self.device)
         self.state = torch.zeros(_lib.PEER_STATE_WORDS, dtype=torch.int32, device=self.device)
         mine = torch.tensor(list(bytes(handle)) + list(off.value.to_bytes(8, "little")), dtype=torch.uint8)
         if self.world > 1:
@@ -100,7 +103,7 @@ class PeerBuffer:
         else:
             allh = mine.view(1, 72)
         self._opened = []
-        bufs, arrive = [], []
+        ll = []
         with torch.cuda.device(self.device):
             for q in range(self.world):
                 if q == self.rank:
@@ -112,28 +115,26 @@ class PeerBuffer:
                     _lib.check("qlin_ipc_open", self._lib.qlin_ipc_open(h, qoff, ctypes.byref(ptr)))
                     base = ptr.value
                     self._opened.append((base, qoff))
-                bufs.append(base)
-                arrive.append(base + self.nbytes)
-        self._bufs = (ctypes.c_void_p * self.world)(*bufs)
-        self._arrive = (ctypes.c_void_p * self.world)(*arrive)
+                ll.append(base)
+        self._ll = (ctypes.c_void_p * self.world)(*ll)
         torch.cuda.synchronize(self.device)
         if self.world > 1:
-            dist.barrier(group=group)   # every rank's counters are zero before anyone writes
+            dist.barrier(group=group)   # every rank's exchange buffer is zero before anyone writes
 
-    def gather(self, parts, out=None, out_bytes=0):
-        """All-gather ``parts`` (a list of ``_lib.GatherPart``) into every rank's
-        buffer; with ``out``, this rank's gathered first ``out_bytes`` are then
-        copied to the tensor ``out`` in the same launch."""
+    def gather(self, parts, dst=None):
+        """All-gather ``parts`` (a list of ``_lib.GatherPart`` whose offsets
+        refer to the destination) into ``dst`` (a CUDA tensor; default
+        ``local``) on every rank, on the current stream."""
         from .kernels._host import stream_of
+        dst = self.local if dst is None else dst
         arr = (type(parts[0]) * len(parts))(*parts)
-        rc = self._lib.qlin_peer_allgather_parts(
-            self._bufs, self._arrive, self.state.data_ptr(), arr, len(parts), self.world, self.rank,
-            None if out is None else out.data_ptr(), out_bytes, stream_of(self.local))
-        self._check("qlin_peer_allgather_parts", rc)
+        rc = self._lib.qlin_peer_allgather_ll(self._ll, self.ll_bytes, self.state.data_ptr(), arr, len(parts),
+                                              self.world, self.rank, dst.data_ptr(), stream_of(self.local))
+        self._check("qlin_peer_allgather_ll", rc)
 
     def close(self):
-        """Unmap the peers' buffers and free this rank's.  The caller must
-        make sure every rank has stopped using them first (GPU work
+        """Unmap the peers' exchange buffers and free this rank's.  The caller
+        must make sure every rank has stopped using them first (GPU work
         synchronised, then a barrier), as ColumnParallelW4MLP.close does."""
         with torch.cuda.device(self.device):
             for base, off in self._opened:
@@ -281,8 +282,9 @@ class ColumnParallelW4MLP:
             rec(2)
             self.ops.gemm_w4(ws["hq"], ws["hs"], d[0], d[1], ws["o_slot"], b_z=d[2])
             rec(3)
-            direct = out.is_contiguous() and out.data_ptr() % 16 == 0
-            ws["obuf"].gather(ws["o_parts"], out if direct else None, M * self.hidden * 2 if direct else 0)
+            # the output gather lands in ``out`` itself when it can
+            direct = out.is_contiguous() and out.data_ptr() % 8 == 0
+            ws["obuf"].gather(ws["o_parts"], out if direct else None)
             if not direct:
                 out.copy_(ws["out_full"])
             rec(4)

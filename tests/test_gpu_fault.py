@@ -91,3 +91,53 @@ def test_timed_out_wait_is_reported_and_cleared(pkg, dev, lib):
     rq, rs = O.quant_row(bits(x))
     np.testing.assert_array_equal(q.cpu().numpy(), rq)
     np.testing.assert_array_equal(s.cpu().numpy().view(np.uint32), rs.view(np.uint32))
+
+
+def test_flagged_word_gather_times_out_without_its_peer(pkg, dev, lib):
+    """The column-split layer's gather (qlin_peer_allgather_ll) as rank 0 of
+    two, both exchange buffers local: rank 1's words never come, so the
+    receiving threads give up after the 50 ms bound and the fault is
+    recorded; rank 0's own block still reached its slot of the destination
+    and, as flagged words of call 1, rank 1's exchange buffer."""
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    x = torch.randn(4, 256, device=dev).to(torch.bfloat16)
+    q = torch.empty(4, 256, dtype=torch.int8, device=dev)
+    s = torch.empty(4, 4, dtype=torch.float32, device=dev)
+    pkg.quant_row(x, q, s)            # sets up the host-visible fault mirror
+    torch.cuda.synchronize()
+    assert lib.qlin_device_fault(1) == 0
+
+    rows, rb = 4, 1024
+    g = torch.Generator(device=dev).manual_seed(12)
+    src = torch.randint(0, 256, (rows, rb), dtype=torch.uint8, device=dev, generator=g)
+    parts = (pkg._lib.GatherPart * 1)(pkg._lib.GatherPart(src.data_ptr(), rb, rows, rb, 0, 2 * rb))
+    need = ctypes.c_int64()
+    assert lib.qlin_peer_ll_bytes(parts, 1, 2, ctypes.byref(need)) == 0
+    assert need.value == 2 * 2 * (rows * rb * 2)
+    ll = [torch.zeros(need.value, dtype=torch.uint8, device=dev) for _ in range(2)]
+    state = torch.zeros(16, dtype=torch.int32, device=dev)
+    dst = torch.zeros(rows, 2 * rb, dtype=torch.uint8, device=dev)
+    assert lib.qlin_set_wait_limit_ns(50_000_000) == 0
+    try:
+        t0 = time.perf_counter()
+        rc = lib.qlin_peer_allgather_ll(_ptrs(*ll), need.value, state.data_ptr(), parts, 1, 2, 0,
+                                        dst.data_ptr(), stream)
+        assert rc == 0, lib.qlin_last_error()
+        torch.cuda.synchronize()
+        elapsed = time.perf_counter() - t0
+    finally:
+        assert lib.qlin_set_wait_limit_ns(2_000_000_000) == 0
+    assert elapsed < 1.5, f"kernel returned after {elapsed:.2f} s, not after the 50 ms bound"
+    assert torch.equal(dst[:, :rb], src)
+    assert not dst[:, rb:].any()      # rank 1's slot: nothing came
+    # call 1 uses the odd half; rank 0's slot of rank 1's buffer holds words (1 << 32 | data)
+    words = ll[1].cpu().numpy().view(np.uint64)[need.value // 16: need.value // 16 + rows * rb // 4]
+    np.testing.assert_array_equal(words >> np.uint64(32), np.ones(rows * rb // 4, dtype=np.uint64))
+    np.testing.assert_array_equal((words & np.uint64(0xFFFFFFFF)).astype(np.uint32).view(np.uint8).reshape(rows, rb),
+                                  src.cpu().numpy())
+    assert state[0].item() == 1       # the call still completed and counted itself
+    assert lib.qlin_device_fault(0) & 1
+    rc = lib.qlin_quant_row(x.data_ptr(), 256, 4, 256, q.data_ptr(), s.data_ptr(), stream)
+    assert rc == QLIN_ERR_DEVICE_FAULT
+    assert lib.qlin_device_fault(1) & 1
+    assert lib.qlin_device_fault(0) == 0

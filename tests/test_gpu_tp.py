@@ -122,9 +122,11 @@ def test_tp_layer_nccl_ranks_equal_one_gpu(pkg, dev, M):
 
 
 # (rows, row_bytes, source row stride, destination gap after the world's slots):
-# 16-byte parts, a 4-byte part (the h scales of config 5 at 8 ranks are 136
-# bytes per row) and one long row
-PART_SHAPES = [(3, 1280, 1296, 32), (5, 136, 136, 8), (1, 1 << 20, 1 << 20, 0)]
+# 8-byte-unit parts, a 4-byte-unit part (row bytes not a multiple of 8) and one
+# long row; the last entry gathers two parts in one call (the h layout: codes,
+# then scales at an offset)
+PART_SHAPES = [[(3, 1280, 1296, 32)], [(5, 136, 136, 8)], [(4, 68, 72, 4)], [(1, 1 << 20, 1 << 20, 0)],
+               [(4, 2176, 2176, 0), (4, 36, 36, 0)]]
 
 
 def _pattern(rank, rows, row_bytes, it):
@@ -133,42 +135,52 @@ def _pattern(rank, rows, row_bytes, it):
 
 
 def _check_gather(pkg, rank, world, dev):
-    """Every part shape: eager calls (the counters advance across calls), then
-    replays of a captured gather; each checks every rank's slot of the local
-    buffer and the copy into ``out`` made by the same launch."""
+    """Every part set: eager calls (the call count advances across calls),
+    then replays of a captured gather; destinations alternate between the
+    buffer's own ``local`` and another tensor, and every rank's slot of the
+    destination is checked."""
     ok = True
-    for rows, rb, ld, gap in PART_SHAPES:
-        dst_ld = world * rb + gap
-        nbytes = rows * dst_ld
-        pb = pkg.tp.PeerBuffer(nbytes, dev)
-        src = torch.zeros(rows, ld, dtype=torch.uint8, device=dev)
-        out = torch.zeros(pb.nbytes, dtype=torch.uint8, device=dev)
-        part = pkg.tp._part(src, rows, rb, ld, 0, dst_ld)
+    for shapes in PART_SHAPES:
+        layout, off = [], 0
+        for rows, rb, ld, gap in shapes:
+            dst_ld = world * rb + gap
+            layout.append((rows, rb, ld, dst_ld, off))
+            off += -(-rows * dst_ld // 16) * 16
+        pb = pkg.tp.PeerBuffer(off, dev)
+        srcs = [torch.zeros(rows, ld, dtype=torch.uint8, device=dev) for rows, rb, ld, _, _ in layout]
+        other = torch.zeros(pb.nbytes, dtype=torch.uint8, device=dev)
+        parts = [pkg.tp._part(src, rows, rb, ld, o, dst_ld) for src, (rows, rb, ld, dst_ld, o) in zip(srcs, layout)]
 
-        def check(it):
-            got = pb.local[:nbytes].view(rows, dst_ld).cpu()
-            cp = out[:nbytes].view(rows, dst_ld).cpu()
-            good = torch.equal(got, cp)
-            for r in range(world):
-                good = good and torch.equal(got[:, r * rb:(r + 1) * rb], _pattern(r, rows, rb, it))
+        def fill(it):
+            for src, (rows, rb, _, _, _) in zip(srcs, layout):
+                src[:, :rb].copy_(_pattern(rank, rows, rb, it))
+
+        def check(dst, it):
+            good = True
+            for rows, rb, _, dst_ld, o in layout:
+                got = dst[o:o + rows * dst_ld].view(rows, dst_ld).cpu()
+                for r in range(world):
+                    good = good and torch.equal(got[:, r * rb:(r + 1) * rb], _pattern(r, rows, rb, it))
             return good
 
-        for it in range(3):
-            src[:, :rb].copy_(_pattern(rank, rows, rb, it))
-            pb.gather([part], out, pb.nbytes)
-            ok = ok and check(it)
+        for it in range(4):
+            fill(it)
+            dst = pb.local if it % 2 == 0 else other
+            pb.gather(parts, None if it % 2 == 0 else other)
+            ok = ok and check(dst, it)
         s = torch.cuda.Stream(device=dev)
         s.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(s):
-            pb.gather([part], out, pb.nbytes)
+            pb.gather(parts, other)
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=s):
-            pb.gather([part], out, pb.nbytes)
-        for it in range(3, 6):
-            src[:, :rb].copy_(_pattern(rank, rows, rb, it))
+            pb.gather(parts, other)
+        for it in range(4, 7):
+            fill(it)
             graph.replay()
-            ok = ok and check(it)
+            torch.cuda.synchronize()
+            ok = ok and check(other, it)
         torch.cuda.synchronize()
         del graph
         if world > 1:
@@ -196,9 +208,9 @@ def _peer_rank(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_peer_allgather_parts_world1(pkg, dev):
-    """The parts gather at world 1 on one GPU (its own slot, the fused copy,
-    strided and 4-byte parts, eager and graph replays)."""
+def test_peer_allgather_ll_world1(pkg, dev):
+    """The flagged-word gather at world 1 on one GPU (its own slots, 8- and
+    4-byte units, two parts in one call, eager calls and graph replays)."""
     assert _check_gather(pkg, 0, 1, dev)
     assert pkg._lib.load().qlin_device_fault(1) == 0
 
