@@ -97,7 +97,7 @@ struct DpArgs {
 // cross-warp reduction (over the weights once they are used), the partial
 // sums received from the other ranks, barriers.
 struct DpLayout {
-  uint32_t item, wbytes, sbytes, act_off, part_off, xchg_off, bar_off, total;
+  uint32_t item, wbytes, sbytes, act_off, as_off, part_off, xchg_off, bar_off, total;
 };
 __host__ __device__ inline DpLayout dp_layout(int wb, int mr, int ns, int wgrp, int gmax, int split, int ring) {
   DpLayout L;
@@ -111,6 +111,8 @@ __host__ __device__ inline DpLayout dp_layout(int wb, int mr, int ns, int wgrp, 
   off = align_up(off, 128);
   L.act_off = off;
   off = align_up(off + gmax * mr * 64, 16);
+  L.as_off = off;  // the K part's activation scales [m][gmax]
+  off = align_up(off + gmax * mr * 4, 16);
   L.part_off = off;
   off = align_up(off + (split > 1 ? split - 1 : 0) * ns * mr * kTileN * 4, 16);
   L.xchg_off = off;
@@ -153,6 +155,7 @@ __global__ void __launch_bounds__(kRgThreads, 2) dp_gemv_kernel(const __grid_con
   uint64_t* recv = full + kRgWarps * (R > 0 ? R : 1);
   uint64_t* abar = recv + 1;                                       // activation rows landed
   int8_t* act = reinterpret_cast<int8_t*>(smem + L.act_off);      // [m][gmax][64]: the K part of row m
+  float* as_sm = reinterpret_cast<float*>(smem + L.as_off);        // [m][gmax]: its scales a_s[m, g0 + gl]
   float* part = reinterpret_cast<float*>(smem + L.part_off);       // [rank-1][s][m][128]
   float* red = reinterpret_cast<float*>(smem);                     // [warp][m][128], over the weights
 
@@ -262,10 +265,17 @@ __global__ void __launch_bounds__(kRgThreads, 2) dp_gemv_kernel(const __grid_con
       bulk_load(act + m * p.gmax * 64, p.a_q + static_cast<long long>(m) * p.K + g0 * 64,
                 static_cast<uint32_t>(nst * 64), abar);
   }
+  // the scales of the K part, while the rows are in flight (one round trip
+  // for all of them instead of one per item); rows past M scale by zero
+  for (int i = threadIdx.x; i < MR * nst; i += kRgThreads) {
+    const int m = i / nst, gl = i - m * nst;
+    as_sm[m * p.gmax + gl] = m < p.M ? __ldg(p.a_s + static_cast<long long>(m) * G + g0 + gl) : 0.0f;
+  }
   if (!mbar_wait(abar, 0)) {
     if ((threadIdx.x & 31) == 0) record_fault(p.fault, kFaultFullWait);
     mbar_wait(abar, 0);  // the copy lands before the CTA may exit
   }
+  __syncthreads();  // as_sm
   if (threadIdx.x == 0) QLIN_TL(p, 3);
 
   // ---------------------------------------------------------------- the dots
@@ -279,9 +289,9 @@ __global__ void __launch_bounds__(kRgThreads, 2) dp_gemv_kernel(const __grid_con
   auto dot_item = [&](int it) {
     const int gl = it / NS;
     const uint8_t* wt = item_w(it);
-    float as_g[MR];  // a_s[m, group]: loaded first, used after the integer work
+    float as_g[MR];  // a_s[m, group]
 #pragma unroll
-    for (int m = 0; m < MR; ++m) as_g[m] = m < p.M ? __ldg(p.a_s + static_cast<long long>(m) * G + g0 + gl) : 0.0f;
+    for (int m = 0; m < MR; ++m) as_g[m] = as_sm[m * p.gmax + gl];
     if (WB == 8) {
       int isum[4][MR];
 #pragma unroll
@@ -467,12 +477,35 @@ __global__ void __launch_bounds__(kRgThreads, 2) dp_gemv_kernel(const __grid_con
     named_bar_sync(1, kTileN);
     if (!*last) return;
     __threadfence();
+    // The tile's kout x NS x MR x 128 partial sums come in with one bulk copy
+    // over the used weight slots (one L2 round trip instead of one per part),
+    // then each thread adds its column's parts in K order from shared memory.
+    const uint32_t wbytes = static_cast<uint32_t>(p.kout * NS * MR * kTileN * 4);
+    const bool bulk = wbytes <= L.act_off;
+    const float* src = ws;
+    if (bulk) {
+      float* wsm = reinterpret_cast<float*>(smem);
+      if (c == 0) {
+        fence_proxy_async_global();
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(abar, wbytes);
+        bulk_load(wsm, ws, wbytes, abar);
+      }
+      if (!mbar_wait(abar, 1)) {
+        if ((threadIdx.x & 31) == 0) record_fault(p.fault, kFaultFullWait);
+        mbar_wait(abar, 1);  // the copy lands before the CTA may exit
+      }
+      src = wsm;
+    }
 #pragma unroll
     for (int s = 0; s < NS; ++s)
 #pragma unroll
       for (int m = 0; m < MR; ++m) {
-        float v = __ldcg(ws + (s * MR + m) * kTileN + c);
-        for (int k = 1; k < p.kout; ++k) v = __fadd_rn(v, __ldcg(ws + ((k * NS + s) * MR + m) * kTileN + c));
+        float v = bulk ? src[(s * MR + m) * kTileN + c] : __ldcg(src + (s * MR + m) * kTileN + c);
+        for (int k = 1; k < p.kout; ++k) {
+          const float* q = src + ((k * NS + s) * MR + m) * kTileN + c;
+          v = __fadd_rn(v, bulk ? *q : __ldcg(q));
+        }
         vs[s][m] = v;
       }
   }
