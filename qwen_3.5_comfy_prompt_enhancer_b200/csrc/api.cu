@@ -350,6 +350,7 @@ QLIN_KNOB(tune_ad_smax, "QLIN_TUNE_AD_SMAX", 8)  // attn_decode: largest cluster
 QLIN_KNOB(tune_dp_m4, "QLIN_TUNE_DP_M4", 0)  // 1: 3-4 rows take any dp plan (W8 too)
 QLIN_KNOB(tune_dp_m4ring, "QLIN_TUNE_DP_M4RING", 1)  // 0: 3-4 rows never take a ring plan
 QLIN_KNOB(tune_ad_hsplit, "QLIN_TUNE_AD_HSPLIT", 0)  // attn_decode: forced query-head split (0: planner)
+QLIN_KNOB(tune_kparts, "QLIN_TUNE_KPARTS", 0)  // W4 GEMM: forced K parts per tile (0: planner)
 #undef QLIN_KNOB
 
 bool use_dp() { return tune_dp() != 0; }
@@ -1047,12 +1048,53 @@ int run_prefill_w4(int epi, const GemvArgs& a, int half_tiles, cudaStream_t st) 
   if (epi == kEpiOut && tune_half() == 2) hs = 2;
 #endif
   const long long tiles = mtiles * ((g.half_tiles + hs - 1) / hs);
-  const int grid = static_cast<int>(tiles < di.sms ? tiles : di.sms);
-  if (epi != kEpiOut) return launch_prefill_w4<kEpiSiluQuant>(g, grid, st);
+  int grid = static_cast<int>(tiles < di.sms ? tiles : di.sms);
+  // K parts: a launch with fewer tiles than SMs (a column shard of a
+  // tensor-parallel layer, a mid-size M) gives each tile up to sms / tiles
+  // CTAs over disjoint stage ranges, at least two 128-K stages each.
+  const int nstage = (a.K / kGroup + 1) / 2;
+  long long kp = tiles < di.sms ? di.sms / tiles : 1;
+  if (kp > nstage / 2) kp = nstage / 2;
+  if (kp > kG4MaxParts) kp = kG4MaxParts;
 #ifdef QLIN_TUNING
-  if (hs == 2) return launch_prefill_w4<kEpiOut>(g, grid, st);
+  if (tune_kparts() > 0) kp = tune_kparts() < nstage ? tune_kparts() : nstage;
+  if (kp > kG4MaxParts) kp = kG4MaxParts;
 #endif
-  return launch_prefill_w4<kEpiOut, 1>(g, grid, st);
+  // every part's rows of one CTA are summed in the stage ring
+  while (kp > 1 && kp * ((128 + kp - 1) / kp) * hs * 128 * 4 > static_cast<long long>(kG4Stages) * kG4StageAligned)
+    --kp;
+  if (kp < 1) kp = 1;
+  void* ws = nullptr;
+  if (kp > 1) {
+    const size_t ws_bytes = static_cast<size_t>(tiles) * kp * 128 * hs * 128 * 4;
+    const size_t cnt_bytes = static_cast<size_t>(tiles) * 4;
+    cudaError_t e = cudaMallocAsync(&ws, ws_bytes + cnt_bytes, st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMallocAsync(K-part workspace)");
+    g.ws = static_cast<float*>(ws);
+    g.cnt = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + ws_bytes);
+    e = cudaMemsetAsync(g.cnt, 0, cnt_bytes, st);
+    if (e != cudaSuccess) {
+      cudaFreeAsync(ws, st);
+      return cuda_fail(e, "cudaMemsetAsync(K-part counters)");
+    }
+    grid = static_cast<int>(tiles * kp);  // one CTA per (tile, part), all resident
+  }
+  g.kparts = static_cast<int>(kp);
+  int r;
+  if (epi != kEpiOut) {
+    r = launch_prefill_w4<kEpiSiluQuant>(g, grid, st);
+  } else {
+#ifdef QLIN_TUNING
+    if (hs == 2) r = launch_prefill_w4<kEpiOut>(g, grid, st);
+    else
+#endif
+    r = launch_prefill_w4<kEpiOut, 1>(g, grid, st);
+  }
+  if (ws) {
+    cudaError_t e = cudaFreeAsync(ws, st);
+    if (r == QLIN_OK && e != cudaSuccess) return cuda_fail(e, "cudaFreeAsync(K-part workspace)");
+  }
+  return r;
 }
 
 // Fills the split / ring fields of `a`, then launches.
@@ -1063,11 +1105,19 @@ int run_prefill_w4(int epi, const GemvArgs& a, int half_tiles, cudaStream_t st) 
 // (K = 5120, 136 GEMM tiles) 418 us small-M vs 219 us GEMM; W8 K = 5120, N =
 // 17408 (68 tiles) 82 vs 67 us; with 48 or fewer tiles the small-M kernel
 // wins (config-2 gate/up 67 vs 102 us, config-5 down 420 vs 671 us).
+// Long-K W4 plain outputs with at least kMidGemmLongKTiles column tiles take the
+// GEMM too: its K parts spread a few tiles over the SMs while the small-M
+// kernel re-streams the long weight rows per 16-row block.  Measured at M = 64
+// (config-5 down 17408 -> 5120 and its column shards of 2, 4, 8 GPUs, us,
+// small-M vs GEMM): 143 vs 103, 81 vs 55, 40 vs 37, 22 vs 33.
 constexpr int kMidGemmMinM = 33;
 constexpr long long kMidGemmMinTiles = 64;
-bool mid_m_takes_gemm(int epi, int64_t M, int tiles) {
+constexpr int64_t kMidGemmLongK = 8192;
+constexpr int kMidGemmLongKTiles = 8;
+bool mid_m_takes_gemm(int wb, int epi, int64_t M, int64_t K, int tiles) {
   if (M < kMidGemmMinM) return false;
   const long long gemm_tiles = ((M + kGmRows - 1) / kGmRows) * (epi == kEpiOut ? (tiles + 1) / 2 : tiles);
+  if (wb == 4 && epi == kEpiOut && K >= kMidGemmLongK && tiles >= kMidGemmLongKTiles) return true;  // (W4 GEMM: K parts)
   return gemm_tiles >= kMidGemmMinTiles;
 }
 
@@ -1332,7 +1382,7 @@ int run_dp(int wb, int epi, const GemvArgs& a, int tiles, cudaStream_t st, bool*
 }
 
 int run_gemv(int wb, int epi, GemvArgs& a, int tiles, cudaStream_t st) {
-  const bool gemm = a.M >= prefill_min_m() || mid_m_takes_gemm(epi, a.M, tiles);
+  const bool gemm = a.M >= prefill_min_m() || mid_m_takes_gemm(wb, epi, a.M, a.K, tiles);
   if (wb == 8 && gemm) return run_prefill_w8(epi, a, tiles, st);
   if (wb == 4 && gemm && a.wgrp % 64 == 0) return run_prefill_w4(epi, a, tiles, st);
   if (use_dp()) {

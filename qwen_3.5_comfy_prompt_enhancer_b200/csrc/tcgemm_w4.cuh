@@ -18,7 +18,14 @@
 //     MN-major 128-byte-swizzled operand tiles, and copy the group scales,
 //     converted to fp32, into an 8-slot ring that outlives the raw stage;
 //   * the epilogue multiplies the row's activation scale by each column's
-//     weight scale before the multiply-add, in the reference's order.
+//     weight scale before the multiply-add, in the reference's order;
+//   * launches with fewer tiles than SMs (column shards of a tensor-parallel
+//     layer, mid-size M) cut each tile's K into `kparts` stage ranges, one CTA
+//     each.  The parts' fp32 sums meet in a workspace; once every part of the
+//     tile has arrived (a counter, a bounded wait -- all CTAs are resident:
+//     grid = tiles x kparts <= SMs at one CTA per SM), CTA kp adds the parts
+//     of rows [kp x 128 / kparts, ...) in part order and runs the epilogue on
+//     them, so the reduction is spread over the tile's CTAs.
 #pragma once
 
 #include "tcgemm.cuh"
@@ -46,6 +53,10 @@ constexpr uint32_t kG4UOff = kG4Stages * kG4StageAligned;
 constexpr uint32_t kG4ScaleOff = kG4UOff + kG4UBufs * kG4UStage;
 constexpr uint32_t kG4BarOff = kG4ScaleOff + kG4ScaleRing;
 constexpr uint32_t kG4Smem = kG4BarOff + 256 + 1024;
+// K parts per tile: at most 16 (128 / kparts >= 8 rows per CTA); the host
+// also keeps every part's rows of one CTA (kparts x ceil(128 / kparts) rows
+// of HS x 128 fp32) within the stage ring.
+constexpr int kG4MaxParts = 16;
 static_assert(kG4Smem <= 227 * 1024, "W4 prefill ring exceeds shared memory");
 
 struct GemmW4Args {
@@ -63,6 +74,9 @@ struct GemmW4Args {
   int8_t* out_q;      // kEpiSiluQuant: int8 [M, n_q]
   float* out_s;       // kEpiSiluQuant: fp32 [M, n_q / 64]
   int n_q;
+  int kparts;         // K parts per tile (1: none); > 1 needs grid == tiles * kparts <= SMs
+  float* ws;          // kparts > 1: fp32 partial sums [tile][kpart][128 rows][HS * 128]
+  unsigned* cnt;      // kparts > 1: per-tile arrival counters, zero at launch
   unsigned* fault;
 };
 
@@ -79,6 +93,12 @@ __device__ __forceinline__ float2 f2_mul(float2 a, float2 b) {
   return d;
 }
 
+// First stage of K part kp + 1 (the end of part kp) out of `parts` equal
+// ranges of `nstage` 128-K stages; kp = -1 gives 0.
+__host__ __device__ inline int g4_stage_end(int kp, int parts, int nstage) {
+  return static_cast<int>(static_cast<long long>(kp + 1) * nstage / parts);
+}
+
 template <int EPI, int HS>
 __global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_constant__ GemmW4Args p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -89,7 +109,8 @@ __global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_
   uint64_t* uempty = ufull + kG4UBufs;
   uint64_t* tfull = uempty + kG4UBufs;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);  // (+ the K-part wait flag at [1])
+  uint64_t* kbar = tempty + 3;                                       // K-part rows landed
   float* sring = reinterpret_cast<float*>(smem + kG4ScaleOff);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -98,6 +119,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_
   const int mtiles = (p.M + kGmRows - 1) / kGmRows;
   const int ptiles = (p.half_tiles + HS - 1) / HS;
   const int tiles = mtiles * ptiles;
+  const int units = tiles * p.kparts;  // (tile, K part), tile fastest
   const int nsr = g4_scale_rows(p.wgrp);
 
   if (warp == 0) {
@@ -114,6 +136,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_
         mbar_init(tfull + i, 1);
         mbar_init(tempty + i, 256);
       }
+      mbar_init(kbar, 1);
       fence_mbar_init();
     }
     __syncwarp();
@@ -132,10 +155,12 @@ __global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_
     uint32_t sc = 0;
     bool ok = true;
     const uint64_t pol = l2_policy_evict_last();
-    for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
+    for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+      const int t = u % tiles;
       const int m0 = (t % mtiles) * kGmRows;
       const int pt = t / mtiles;
-      for (int st = 0; st < nstage; ++st, ++sc) {
+      const int st1 = g4_stage_end(u / tiles, p.kparts, nstage);
+      for (int st = g4_stage_end(u / tiles - 1, p.kparts, nstage); st < st1; ++st, ++sc) {
         const int slot = sc % kG4Stages;
         if (!mbar_wait(empty + slot, ((sc / kG4Stages) & 1) ^ 1)) {
           ok = false;
@@ -174,9 +199,10 @@ __global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_
     const int u = threadIdx.x - kG4WarpUnpack * 32;
     uint32_t sc = 0, gbase = 0;
     bool ok = true;
-    for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
-      const int pt = t / mtiles;
-      for (int st = 0; st < nstage; ++st, ++sc) {
+    for (int wu = blockIdx.x; ok && wu < units; wu += gridDim.x) {
+      const int pt = (wu % tiles) / mtiles;
+      const int st1 = g4_stage_end(wu / tiles, p.kparts, nstage);
+      for (int st = g4_stage_end(wu / tiles - 1, p.kparts, nstage); st < st1; ++st, ++sc) {
         const int slot = sc % kG4Stages;
         const int ub = sc % kG4UBufs;
         if (!mbar_wait(full + slot, (sc / kG4Stages) & 1) ||
@@ -244,10 +270,11 @@ __global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_
     constexpr uint32_t idesc = idesc_i8(128, 128, true, true, false, true);
     uint32_t sc = 0, gc = 0;
     bool ok = true;
-    for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
-      const int pt = t / mtiles;
+    for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+      const int pt = (u % tiles) / mtiles;
       const int nh = HS == 2 && 2 * pt + 1 < p.half_tiles ? 2 : 1;
-      for (int st = 0; ok && st < nstage; ++st, ++sc) {
+      const int st1 = g4_stage_end(u / tiles, p.kparts, nstage);
+      for (int st = g4_stage_end(u / tiles - 1, p.kparts, nstage); ok && st < st1; ++st, ++sc) {
         const int slot = sc % kG4Stages;
         const int ub = sc % kG4UBufs;
         ok = mbar_wait(full + slot, (sc / kG4Stages) & 1) && mbar_wait(ufull + ub, (sc / kG4UBufs) & 1);
@@ -298,23 +325,78 @@ __global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_
     mbar_arrive(tempty + 0);
     mbar_arrive(tempty + 1);
 
+    // tile epilogue of row m, columns [64 c2e, 64 c2e + 64) of each half, from a
+    auto emit = [&](int m, int pt, int c2e, const float2 (&a)[64]) {
+      if constexpr (EPI == kEpiOut) {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          int si, n0;
+          if (!gm_half<EPI, HS>(p, pt, hh, si, n0)) continue;
+          const GemvSeg& sg = p.seg[si];
+          __nv_bfloat16* orow =
+              reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<long long>(m) * p.ldo + sg.out_col;
+          const __nv_bfloat16* rrow =
+              p.res ? reinterpret_cast<const __nv_bfloat16*>(p.res) + static_cast<long long>(m) * p.ldr + sg.out_col
+                    : nullptr;
+#pragma unroll
+          for (int c8 = 0; c8 < 8; ++c8) {
+            const int n = n0 + c2e * 64 + 8 * c8;
+            if (n >= sg.n) continue;  // N % 16 == 0: a chunk of 8 is all in or all out
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              v[2 * e] = a[32 * hh + 4 * c8 + e].x;
+              v[2 * e + 1] = a[32 * hh + 4 * c8 + e].y;
+            }
+            if (rrow) {
+              if (p.vec_out) {
+                const uint4 rv = *reinterpret_cast<const uint4*>(rrow + n);
+                const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rv);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(v[e], __bfloat162float(rb[e]));
+              } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(v[e], __bfloat162float(rrow[n + e]));
+              }
+            }
+            if (p.vec_out) {
+              uint4 ov;
+              __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&ov);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) ob[e] = __float2bfloat16_rn(v[e]);
+              *reinterpret_cast<uint4*>(orow + n) = ov;
+            } else {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) orow[n + e] = __float2bfloat16_rn(v[e]);
+            }
+          }
+        }
+      } else {
+        gm_gate_up_epilogue<EPI>(p, m, pt * kTileN + c2e * 64, a, nullptr, nullptr);
+      }
+    };
+
     uint32_t gc = 0;
     bool ok = true;
     const float2 neg_magic = make_float2(-12582912.0f, -12582912.0f);
-    for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
+    for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+      const int t = u % tiles, kp = u / tiles;
+      const int gb = 2 * g4_stage_end(kp - 1, p.kparts, nstage);
+      const int ge = min(2 * g4_stage_end(kp, p.kparts, nstage), G);
       const int m0 = (t % mtiles) * kGmRows;
       const int pt = t / mtiles;
       const int m = m0 + 32 * q + lane;
       const bool mvalid = m < p.M;
+      int m_e = m, c2_e = c2;  // the row and columns this thread's epilogue writes
       const float* asrow = p.a_s + static_cast<long long>(mvalid ? m : 0) * G;
       float2 acc[64];  // [0, 32): half 0 columns, [32, 64): half 1 columns, two per entry
 #pragma unroll
       for (int j = 0; j < 64; ++j) acc[j] = make_float2(0.0f, 0.0f);
-      float s_next = mvalid ? __ldg(asrow) : 0.0f;
-      for (int g = 0; g < G; ++g, ++gc) {
+      float s_next = mvalid ? __ldg(asrow + gb) : 0.0f;
+      for (int g = gb; g < ge; ++g, ++gc) {
         const int b = gc & 1;
         const float as = s_next;
-        if (g + 1 < G) s_next = mvalid ? __ldg(asrow + g + 1) : 0.0f;
+        if (g + 1 < ge) s_next = mvalid ? __ldg(asrow + g + 1) : 0.0f;
         ok = mbar_wait(tfull + b, (gc >> 1) & 1);
         if (!ok) break;
         tc_fence_after();
@@ -342,55 +424,90 @@ __global__ void __launch_bounds__(kG4Threads, 1) tc_gemm_w4_kernel(const __grid_
         mbar_arrive(tempty + b);
       }
       if (!ok) break;
-      if (!mvalid) continue;
-      // ---------------------------------------------------------------- tile epilogue
-      if constexpr (EPI == kEpiOut) {
+      if (p.kparts > 1) {
+        // ---------------------------------------------------------------- K parts of the tile meet
+        // (this CTA's only unit: the host launches one CTA per (tile, part))
+        const int KP = p.kparts;
+        constexpr int RW = HS * 128;  // floats per row of a part
+        const int et = threadIdx.x - 64;  // epilogue thread 0..255
+        float* wt = p.ws + static_cast<size_t>(t) * KP * 128 * RW;
+        float* mine = wt + (static_cast<size_t>(kp) * 128 + 32 * q + lane) * RW + c2 * 64;
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          int si, n0;
-          if (!gm_half<EPI, HS>(p, pt, hh, si, n0)) continue;
-          const GemvSeg& sg = p.seg[si];
-          __nv_bfloat16* orow =
-              reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<long long>(m) * p.ldo + sg.out_col;
-          const __nv_bfloat16* rrow =
-              p.res ? reinterpret_cast<const __nv_bfloat16*>(p.res) + static_cast<long long>(m) * p.ldr + sg.out_col
-                    : nullptr;
+        for (int c = 0; c < 4 * HS; ++c) {
+          float4* d = reinterpret_cast<float4*>(mine + (c >> 2) * 128 + 16 * (c & 3));
 #pragma unroll
-          for (int c8 = 0; c8 < 8; ++c8) {
-            const int n = n0 + c2 * 64 + 8 * c8;
-            if (n >= sg.n) continue;  // N % 16 == 0: a chunk of 8 is all in or all out
-            float v[8];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              v[2 * e] = acc[32 * hh + 4 * c8 + e].x;
-              v[2 * e + 1] = acc[32 * hh + 4 * c8 + e].y;
-            }
-            if (rrow) {
-              if (p.vec_out) {
-                const uint4 rv = *reinterpret_cast<const uint4*>(rrow + n);
-                const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rv);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(v[e], __bfloat162float(rb[e]));
-              } else {
-#pragma unroll
-                for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(v[e], __bfloat162float(rrow[n + e]));
-              }
-            }
-            if (p.vec_out) {
-              uint4 ov;
-              __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&ov);
-#pragma unroll
-              for (int e = 0; e < 8; ++e) ob[e] = __float2bfloat16_rn(v[e]);
-              *reinterpret_cast<uint4*>(orow + n) = ov;
-            } else {
-#pragma unroll
-              for (int e = 0; e < 8; ++e) orow[n + e] = __float2bfloat16_rn(v[e]);
+          for (int e = 0; e < 4; ++e)
+            __stcg(d + e, make_float4(acc[8 * c + 2 * e].x, acc[8 * c + 2 * e].y, acc[8 * c + 2 * e + 1].x,
+                                      acc[8 * c + 2 * e + 1].y));
+        }
+        __threadfence();
+        named_bar_sync(1, 256);
+        volatile int* ks_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+        if (et == 0) {
+          atomicAdd(p.cnt + t, 1u);
+          const unsigned long long t0 = global_ns();
+          int f = 0;
+          while (*reinterpret_cast<volatile unsigned*>(p.cnt + t) < static_cast<unsigned>(KP)) {
+            if (global_ns() - t0 > wait_limit_ns()) {
+              f = 1;
+              break;
             }
           }
+          *ks_flag = f;
         }
-      } else {
-        gm_gate_up_epilogue<EPI>(p, m, pt * kTileN + c2 * 64, acc, nullptr, nullptr);
+        named_bar_sync(1, 256);
+        if (*ks_flag) {
+          ok = false;
+          break;
+        }
+        __threadfence();
+        // rows [r0, r1) of every part, one bulk copy each, over the stage ring
+        // (free: every stage of this unit has been consumed)
+        const int r0 = kp * 128 / KP, r1 = (kp + 1) * 128 / KP, nr = r1 - r0;
+        const uint32_t slab = static_cast<uint32_t>(nr * RW * 4);
+        float* sl = reinterpret_cast<float*>(smem + kG4RawOff);
+        if (et == 0) {
+          fence_proxy_async_global();
+          fence_proxy_async_smem();
+          mbar_arrive_expect_tx(kbar, KP * slab);
+          for (int k = 0; k < KP; ++k)
+            bulk_load(sl + static_cast<size_t>(k) * nr * RW, wt + (static_cast<size_t>(k) * 128 + r0) * RW, slab, kbar);
+        }
+        if (!mbar_wait(kbar, 0)) {
+          if (lane == 0) record_fault(p.fault, kFaultFullWait);
+          mbar_wait(kbar, 0);  // the copies land before the region is reused or the CTA exits
+          ok = false;
+          break;
+        }
+        // parts added in K order, in place over part 0's rows
+        float4* sl4 = reinterpret_cast<float4*>(sl);
+        const int n4 = nr * RW / 4;
+        for (int x = et; x < n4; x += 256) {
+          float4 v = sl4[x];
+          for (int k = 1; k < KP; ++k) {
+            const float4 w = sl4[k * n4 + x];
+            v.x = __fadd_rn(v.x, w.x);
+            v.y = __fadd_rn(v.y, w.y);
+            v.z = __fadd_rn(v.z, w.z);
+            v.w = __fadd_rn(v.w, w.w);
+          }
+          sl4[x] = v;
+        }
+        named_bar_sync(1, 256);
+        // thread (row r0 + rl, columns c2e) runs the epilogue on the sum
+        if (et >= 2 * nr) continue;
+        const int rl = et >> 1;
+        c2_e = et & 1;
+        m_e = m0 + r0 + rl;
+        const float* row = sl + rl * RW + c2_e * 64;
+#pragma unroll
+        for (int c = 0; c < 4 * HS; ++c)
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            acc[8 * c + j] = *reinterpret_cast<const float2*>(row + (c >> 2) * 128 + 16 * (c & 3) + 2 * j);
       }
+      if (m_e >= p.M) continue;
+      emit(m_e, pt, c2_e, acc);
     }
     if (!ok && lane == 0) record_fault(p.fault, kFaultFullWait);
   }

@@ -156,6 +156,24 @@ def test_prefill_w4_integer_exact(pkg, dev, M, K, wg):
     np.testing.assert_array_equal(bits(out), O.f32_to_bf16_bits(exact.astype(np.float32)))
 
 
+@pytest.mark.parametrize("M,K,N", [(256, 4096, 640), (128, 8192, 640), (64, 8192, 1280)])
+def test_prefill_w4_k_parts_integer_exact(pkg, dev, M, K, N):
+    """Few output tiles (a column shard of a tensor-parallel down projection):
+    each tile's K is cut into parts on several CTAs (14, 16 and 14 parts here,
+    rows shared unevenly among them) whose sums meet in a workspace; M = 64
+    takes this GEMM through the long-K mid-M rule.  Unit scales: every part's
+    fp32 sum and their total are exact integers."""
+    g = gen(6750 + M)
+    a = torch.randint(-127, 128, (M, K), dtype=torch.int8, generator=g)
+    b, _, z = w4(g, K, N, 128, True)
+    sc = torch.ones(K // 128, N, dtype=torch.bfloat16)
+    out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    pkg.gemm_w4(cu(a), cu(torch.ones(M, K // 64)), cu(b), cu(sc), out, b_z=cu(z))
+    w = O.unpack_w4(b.numpy(), z.numpy(), 128).astype(np.float64)
+    exact = a.numpy().astype(np.float64) @ w
+    np.testing.assert_array_equal(bits(out), O.f32_to_bf16_bits(exact.astype(np.float32)))
+
+
 def test_prefill_proj3_w4(pkg, dev):
     M, K, wg = 160, 2048, 128
     g = gen(6800)
@@ -230,6 +248,23 @@ def test_prefill_gate_up_quant_w4(pkg, dev, M, wg, zeros):
     rq, rs = O.mlp_gate_up_quant_w4(a.numpy(), s.numpy(), gw.numpy(), bits(gs), uw.numpy(), bits(us),
                                     None if gz is None else gz.numpy(), None if uz is None else uz.numpy())
     assert_quant_close(q.cpu().numpy(), qs.cpu().numpy(), rq, rs, f"prefill gate_up_quant W4 M={M} wg={wg}")
+
+
+def test_prefill_gate_up_quant_w4_k_parts(pkg, dev):
+    """A column shard of the config-5 gate/up (5 tiles of 128 gate + 128 up
+    columns at M = 256): K parts on several CTAs per tile, then the fused
+    SiLU + requantisation on the summed parts."""
+    M, K, N = 256, 2048, 640
+    g = gen(7350)
+    a, s = acts_x(g, M, K)
+    gw, gs, gz = w4(g, K, N, 128, True)
+    uw, us, uz = w4(g, K, N, 128, True)
+    q = torch.empty(M, N, dtype=torch.int8, device=dev)
+    qs = torch.empty(M, N // 64, dtype=torch.float32, device=dev)
+    pkg.mlp_gate_up_quant_w4(cu(a), cu(s), cu(gw), cu(gs), cu(uw), cu(us), q, qs, zg=cu(gz), zu=cu(uz))
+    rq, rs = O.mlp_gate_up_quant_w4(a.numpy(), s.numpy(), gw.numpy(), bits(gs), uw.numpy(), bits(us),
+                                    gz.numpy(), uz.numpy())
+    assert_quant_close(q.cpu().numpy(), qs.cpu().numpy(), rq, rs, "prefill gate_up_quant W4 K parts")
 
 
 # ----------------------------------------------------------------------------- mid M (33..127), many tiles
