@@ -111,8 +111,8 @@ __host__ __device__ inline DpLayout dp_layout(int wb, int mr, int ns, int wgrp, 
   off = align_up(off, 128);
   L.act_off = off;
   off = align_up(off + gmax * mr * 64, 16);
-  L.as_off = off;  // the K part's activation scales [m][gmax]
-  off = align_up(off + gmax * mr * 4, 16);
+  L.as_off = off;  // the K part's activation scales [m][gmax], then (W4, 16-byte aligned) sums [m][gmax][2]
+  off = align_up(off + gmax * mr * 4, 16) + (wb == 4 ? align_up(gmax * mr * 8, 16) : 0);
   L.part_off = off;
   off = align_up(off + (split > 1 ? split - 1 : 0) * ns * mr * kTileN * 4, 16);
   L.xchg_off = off;
@@ -156,6 +156,7 @@ __global__ void __launch_bounds__(kRgThreads, 2) dp_gemv_kernel(const __grid_con
   uint64_t* abar = recv + 1;                                       // activation rows landed
   int8_t* act = reinterpret_cast<int8_t*>(smem + L.act_off);      // [m][gmax][64]: the K part of row m
   float* as_sm = reinterpret_cast<float*>(smem + L.as_off);        // [m][gmax]: its scales a_s[m, g0 + gl]
+  int* asum_sm = reinterpret_cast<int*>(smem + L.as_off + align_up(MR * p.gmax * 4, 16));  // W4: [m][gmax][2]
   float* part = reinterpret_cast<float*>(smem + L.part_off);       // [rank-1][s][m][128]
   float* red = reinterpret_cast<float*>(smem);                     // [warp][m][128], over the weights
 
@@ -275,7 +276,26 @@ __global__ void __launch_bounds__(kRgThreads, 2) dp_gemv_kernel(const __grid_con
     if ((threadIdx.x & 31) == 0) record_fault(p.fault, kFaultFullWait);
     mbar_wait(abar, 0);  // the copy lands before the CTA may exit
   }
-  __syncthreads();  // as_sm
+  if (WB == 4) {
+    // Once per CTA instead of once per item and stream: every 8-byte block of
+    // every row is split into its even-K and odd-K bytes (the order of the
+    // low and high nibbles of a packed weight word), and each 32-K half is
+    // summed for the zero points.  Rows past M hold stale bytes; they are
+    // scaled by zero.
+    for (int i = threadIdx.x; i < MR * nst * 2; i += kRgThreads) {
+      const int m = i / (nst * 2), r = i - m * nst * 2, gl = r >> 1, h = r & 1;
+      uint2* blk = reinterpret_cast<uint2*>(act + (m * p.gmax + gl) * 64 + h * 32);
+      int sum = 0;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const uint2 raw = blk[b];
+        sum = __dp4a(static_cast<int>(raw.x), 0x01010101, __dp4a(static_cast<int>(raw.y), 0x01010101, sum));
+        blk[b] = make_uint2(__byte_perm(raw.x, raw.y, 0x6420), __byte_perm(raw.x, raw.y, 0x7531));
+      }
+      asum_sm[(m * p.gmax + gl) * 2 + h] = sum;
+    }
+  }
+  __syncthreads();  // as_sm (and the split rows)
   if (threadIdx.x == 0) QLIN_TL(p, 3);
 
   // ---------------------------------------------------------------- the dots
@@ -321,12 +341,10 @@ __global__ void __launch_bounds__(kRgThreads, 2) dp_gemv_kernel(const __grid_con
       const uint16_t* sc = reinterpret_cast<const uint16_t*>(wt + L.wbytes);
       const uint8_t* zz = wt + L.wbytes + nsub * kTileN * 2;
       int isum[2][4][MR];  // per 32-K half
-      int asum[2][MR];     // sum of the activations per 32-K half (zero points)
 #pragma unroll
       for (int h = 0; h < 2; ++h)
 #pragma unroll
         for (int m = 0; m < MR; ++m) {
-          asum[h][m] = 0;
 #pragma unroll
           for (int j = 0; j < 4; ++j) isum[h][j][m] = 0;
         }
@@ -340,10 +358,8 @@ __global__ void __launch_bounds__(kRgThreads, 2) dp_gemv_kernel(const __grid_con
           tr4x4(rows[0], rows[kTileN / 4], rows[2 * kTileN / 4], rows[3 * kTileN / 4], col);
 #pragma unroll
           for (int m = 0; m < MR; ++m) {
-            // 8 K of row m split by parity: (the 4 even K, the 4 odd K)
-            const uint2 raw = *reinterpret_cast<const uint2*>(act + (m * p.gmax + gl) * 64 + b * 8);
-            const uint2 aw = make_uint2(__byte_perm(raw.x, raw.y, 0x6420), __byte_perm(raw.x, raw.y, 0x7531));
-            asum[h][m] = __dp4a(static_cast<int>(raw.x), 0x01010101, __dp4a(static_cast<int>(raw.y), 0x01010101, asum[h][m]));
+            // 8 K of row m, already split by parity: (the 4 even K, the 4 odd K)
+            const uint2 aw = *reinterpret_cast<const uint2*>(act + (m * p.gmax + gl) * 64 + b * 8);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               isum[h][j][m] = dp4a_us(col[j] & 0x0F0F0F0Fu, static_cast<int>(aw.x), isum[h][j][m]);
@@ -351,6 +367,13 @@ __global__ void __launch_bounds__(kRgThreads, 2) dp_gemv_kernel(const __grid_con
             }
           }
         }
+      }
+      int asum[2][MR];  // sum of the activations per 32-K half (zero points)
+#pragma unroll
+      for (int m = 0; m < MR; ++m) {
+        const int2 a2 = *reinterpret_cast<const int2*>(asum_sm + (m * p.gmax + gl) * 2);
+        asum[0][m] = a2.x;
+        asum[1][m] = a2.y;
       }
       // out += float(int32 sub-block sum) * (a_s * ws)   (kernels/w4.py:103-104)
 #pragma unroll
