@@ -349,6 +349,48 @@ int qlin_peer_ll_bytes(const qlin_gather_part* parts, int nparts, int world, int
 int qlin_peer_allgather_ll(void* const* ll, int64_t ll_bytes, void* state, const qlin_gather_part* parts,
                            int nparts, int world, int rank, void* dst, void* stream);
 
+/* The two halves of qlin_peer_allgather_ll, for a gather whose sending or
+ * receiving side sits inside another kernel (the column-split layer's down
+ * projection, qlin_tp_gemm_w4_ll).  qlin_peer_ll_send stores this rank's
+ * parts as flagged words of call state[0] + 1 into every rank's exchange
+ * buffer, this rank's own included, and advances nothing.  qlin_peer_ll_recv
+ * waits for every rank's words of call state[0] + 1 (own included) and writes
+ * them into their slots of dst; its last CTA then stores that call number in
+ * state[0] and, if state2 is not null, adds one to state2[0] (the call count
+ * of a buffer whose readers finished before this launch).  Same layouts,
+ * sizes and rules as qlin_peer_allgather_ll.  No reference counterpart. */
+int qlin_peer_ll_send(void* const* ll, int64_t ll_bytes, void* state, const qlin_gather_part* parts, int nparts,
+                      int world, int rank, void* stream);
+int qlin_peer_ll_recv(void* const* ll, int64_t ll_bytes, void* state, const qlin_gather_part* parts, int nparts,
+                      int world, int rank, void* dst, void* state2, void* stream);
+
+/* The column-split layer's W4 down projection (kernels/w4.py:139-166
+ * gemm_w4, without residual) for 1-4 rows with both all-gathers around it
+ * inside the kernel: the activation rows h [M, K] and their scales come from
+ * the ranks' flagged words in this rank's exchange buffer of h (h_ll[rank],
+ * sent by qlin_peer_ll_send with h_parts = [codes rows M x K/world bytes,
+ * scales rows M x K/world/64 floats], call h_state[0] + 1), and every row of
+ * this rank's output [M, N] goes to out (row stride ldo) and, as flagged words
+ * of call o_state[0] + 1, to every rank's exchange buffer of the output
+ * (o_ll, o_parts = [rows M x 2N bytes]) for qlin_peer_ll_recv.  hq / hs, if
+ * not null, receive a copy of the gathered h and scales.  K / world must be a
+ * multiple of 128.  Returns QLIN_ERR_UNSUPPORTED if the decode-row kernel has
+ * no plan for the shape (qlin_plan_dp); the caller then uses the separate
+ * gathers.  No reference counterpart (the reference has no multi-GPU path). */
+int qlin_tp_gemm_w4_ll(int64_t M, int64_t K, const uint8_t* b, const void* b_s, const uint8_t* b_z, int64_t N,
+                       int64_t wgrp, void* out, int64_t ldo, void* const* h_ll, int64_t h_ll_bytes, const void* h_state,
+                       const qlin_gather_part* h_parts, int h_nparts, void* const* o_ll, int64_t o_ll_bytes,
+                       const void* o_state, const qlin_gather_part* o_parts, int o_nparts, int world, int rank,
+                       void* hq, void* hs, void* stream);
+
+/* Diagnostic: the decode-row (dp4a) kernel's plan for wbits 8 or 4, one
+ * output stream (gate_up 0) or the fused gate/up (1), M rows, K, `tiles`
+ * 128-column tiles, W4 group size and `sms` SMs (0: the current device).
+ * out[0..3] = cluster split, K parts across clusters, weight-ring slots per
+ * warp (0: resident), 64-K groups per CTA; all zero if the shape goes to the
+ * tensor-core kernels.  No GPU needed when sms > 0. */
+int qlin_plan_dp(int wbits, int gate_up, int64_t M, int64_t K, int64_t tiles, int64_t wgrp, int sms, int64_t* out);
+
 /* All-gather that allocates nothing, for one rank.  It has no counterpart in
  * the reference.  Meant for a process that runs the column-split layer on a
  * single GPU (world = 1) and may not call cudaMalloc itself -- for instance a

@@ -1364,6 +1364,7 @@ int run_dp(int wb, int epi, const GemvArgs& a, int tiles, cudaStream_t st, bool*
   d.out_q = a.out_q;
   d.out_s = a.out_s;
   d.n_q = a.n_q;
+  if (a.peer) d.peer = *static_cast<const DpPeer*>(a.peer);
   d.fault = di.fault;
   *taken = true;
   const dim3 grid(pl.split, tiles, pl.kout);
@@ -1382,6 +1383,13 @@ int run_dp(int wb, int epi, const GemvArgs& a, int tiles, cudaStream_t st, bool*
 }
 
 int run_gemv(int wb, int epi, GemvArgs& a, int tiles, cudaStream_t st) {
+  if (a.peer) {
+    // the column-split layer's down projection with its gathers inside: the dp kernel only
+    bool taken = false;
+    if (int r = run_dp(wb, epi, a, tiles, st, &taken)) return r;
+    if (!taken) return fail(QLIN_ERR_UNSUPPORTED, "no decode-row plan for this shape");
+    return QLIN_OK;
+  }
   const bool gemm = a.M >= prefill_min_m() || mid_m_takes_gemm(wb, epi, a.M, a.K, tiles);
   if (wb == 8 && gemm) return run_prefill_w8(epi, a, tiles, st);
   if (wb == 4 && gemm && a.wgrp % 64 == 0) return run_prefill_w4(epi, a, tiles, st);
@@ -1751,12 +1759,30 @@ int qlin_peer_ll_bytes(const qlin_gather_part* parts, int nparts, int world, int
   return QLIN_OK;
 }
 
+static int ll_gather(void* const* ll, int64_t ll_bytes, void* state, const qlin_gather_part* parts, int nparts, int world,
+              int rank, void* dst, int mode, void* state2, void* stream);
+
 int qlin_peer_allgather_ll(void* const* ll, int64_t ll_bytes, void* state, const qlin_gather_part* parts,
                            int nparts, int world, int rank, void* dst, void* stream) {
+  return ll_gather(ll, ll_bytes, state, parts, nparts, world, rank, dst, 0, nullptr, stream);
+}
+
+int qlin_peer_ll_send(void* const* ll, int64_t ll_bytes, void* state, const qlin_gather_part* parts, int nparts,
+                      int world, int rank, void* stream) {
+  return ll_gather(ll, ll_bytes, state, parts, nparts, world, rank, nullptr, 1, nullptr, stream);
+}
+
+int qlin_peer_ll_recv(void* const* ll, int64_t ll_bytes, void* state, const qlin_gather_part* parts, int nparts,
+                      int world, int rank, void* dst, void* state2, void* stream) {
+  return ll_gather(ll, ll_bytes, state, parts, nparts, world, rank, dst, 2, state2, stream);
+}
+
+static int ll_gather(void* const* ll, int64_t ll_bytes, void* state, const qlin_gather_part* parts, int nparts, int world,
+              int rank, void* dst, int mode, void* state2, void* stream) {
   if (world < 1 || world > kPeerMax || rank < 0 || rank >= world)
     return fail(QLIN_ERR_INVALID_ARGUMENT, "world %d / rank %d", world, rank);
-  if (!ll || !state || !parts || !dst) return fail(QLIN_ERR_INVALID_ARGUMENT, "null argument");
-  if (!aligned(state, 4)) return fail(QLIN_ERR_ALIGNMENT, "state must be 4-byte aligned");
+  if (!ll || !state || !parts || (!dst && mode != 1)) return fail(QLIN_ERR_INVALID_ARGUMENT, "null argument");
+  if (!aligned(state, 4) || !aligned(state2, 4)) return fail(QLIN_ERR_ALIGNMENT, "state must be 4-byte aligned");
   LlGatherArgs a;
   memset(&a, 0, sizeof(a));
   if (int r = ll_layout(parts, nparts, world, &a)) return r;
@@ -1769,7 +1795,7 @@ int qlin_peer_allgather_ll(void* const* ll, int64_t ll_bytes, void* state, const
   }
   for (int i = 0; i < nparts; ++i) {
     const LlPart& p = a.part[i];
-    if (!p.src || !aligned(p.src, p.unit) || p.src_ld % p.unit != 0 || !aligned(dst, p.unit))
+    if ((mode != 2 && (!p.src || !aligned(p.src, p.unit) || p.src_ld % p.unit != 0)) || !aligned(dst, p.unit))
       return fail(QLIN_ERR_ALIGNMENT, "part %d: source, source stride and destination must be %d-byte aligned", i,
                   p.unit);
   }
@@ -1779,9 +1805,11 @@ int qlin_peer_allgather_ll(void* const* ll, int64_t ll_bytes, void* state, const
   a.dst = static_cast<uint8_t*>(dst);
   a.world = world;
   a.rank = rank;
+  a.mode = mode;
+  a.state2 = static_cast<unsigned*>(state2);
   a.fault = di.fault;
   // units per thread: about two sends or receives
-  const long long work = a.units * (world > 1 ? world - 1 : 1);
+  const long long work = a.units * (mode != 0 ? world : world > 1 ? world - 1 : 1);
   long long ctas = (work + kPeerThreads * 2 - 1) / (kPeerThreads * 2);
   if (ctas > kLlMaxCtas) ctas = kLlMaxCtas;
   if (ctas > di.sms) ctas = di.sms;
@@ -1954,6 +1982,88 @@ int qlin_gemm_w4(const int8_t* a_q, const float* a_s, int64_t M, int64_t K, cons
   a.res = residual;
   a.ldr = residual ? ldr : 0;
   return run_gemv(4, kEpiOut, a, tiles_of(N), static_cast<cudaStream_t>(stream));
+}
+
+int qlin_tp_gemm_w4_ll(int64_t M, int64_t K, const uint8_t* b, const void* b_s, const uint8_t* b_z, int64_t N,
+                       int64_t wgrp, void* out, int64_t ldo, void* const* h_ll, int64_t h_ll_bytes, const void* h_state,
+                       const qlin_gather_part* h_parts, int h_nparts, void* const* o_ll, int64_t o_ll_bytes,
+                       const void* o_state, const qlin_gather_part* o_parts, int o_nparts, int world, int rank,
+                       void* hq, void* hs, void* stream) {
+  if (world < 1 || world > kDpPeerMax || rank < 0 || rank >= world)
+    return fail(QLIN_ERR_INVALID_ARGUMENT, "world %d / rank %d", world, rank);
+  if (!h_ll || !o_ll || !h_state || !o_state || !out) return fail(QLIN_ERR_INVALID_ARGUMENT, "null argument");
+  if (M < 1 || M > 4) return fail(QLIN_ERR_SHAPE, "M=%lld: the fused column-split down projection serves 1-4 rows",
+                                  (long long)M);
+  if (K % (128LL * world) != 0 || N % 16 != 0 || ldo < N)
+    return fail(QLIN_ERR_SHAPE, "K=%lld must split into %d multiples of 128, N=%lld a multiple of 16", (long long)K,
+                world, (long long)N);
+  if (int r = check_wgrp(K, wgrp)) return r;
+  if (!aligned(h_state, 4) || !aligned(o_state, 4) || !aligned(out, 8) || ldo % 4 != 0 || (hq && !aligned(hq, 8)) ||
+      (hs && !aligned(hs, 4)))
+    return fail(QLIN_ERR_ALIGNMENT, "state, out, hq or hs misaligned");
+  const int64_t kloc = K / world;
+  // the exchange layouts must be those of qlin_peer_allgather_ll for [codes, scales] of h and [rows] of the output
+  LlGatherArgs hl, ol;
+  memset(&hl, 0, sizeof(hl));
+  memset(&ol, 0, sizeof(ol));
+  if (int r = ll_layout(h_parts, h_nparts, world, &hl)) return r;
+  if (int r = ll_layout(o_parts, o_nparts, world, &ol)) return r;
+  if (h_nparts != 2 || h_parts[0].rows != M || h_parts[0].row_bytes != kloc || h_parts[1].rows != M ||
+      h_parts[1].row_bytes != kloc / 64 * 4 || hl.part[0].unit != 8 || hl.part[1].unit != 8 || o_nparts != 1 ||
+      o_parts[0].rows != M || o_parts[0].row_bytes != N * 2 || ol.part[0].unit != 8)
+    return fail(QLIN_ERR_SHAPE, "gather parts are not h [codes, scales] and the output rows of this launch");
+  if (h_ll_bytes < 2LL * world * hl.slot_bytes || o_ll_bytes < 2LL * world * ol.slot_bytes)
+    return fail(QLIN_ERR_SHAPE, "exchange buffers too small");
+  DpPeer pr;
+  memset(&pr, 0, sizeof(pr));
+  pr.rx = static_cast<const uint8_t*>(h_ll[rank]);
+  pr.rx_slot = hl.slot_bytes;
+  pr.rx_off_s = hl.part[1].ll_off;
+  pr.rx_state = static_cast<const unsigned*>(h_state);
+  pr.rx_kloc = static_cast<int>(kloc);
+  pr.rx_hq = static_cast<int8_t*>(hq);
+  pr.rx_hs = static_cast<float*>(hs);
+  for (int q = 0; q < world; ++q) {
+    if (!h_ll[q] || !o_ll[q] || !aligned(h_ll[q], 16) || !aligned(o_ll[q], 16))
+      return fail(QLIN_ERR_ALIGNMENT, "exchange buffer %d is null or misaligned", q);
+    pr.tx[q] = static_cast<uint8_t*>(o_ll[q]);
+  }
+  pr.tx_slot = ol.slot_bytes;
+  pr.tx_state = static_cast<const unsigned*>(o_state);
+  pr.world = world;
+  pr.rank = rank;
+  GemvArgs a;
+  memset(&a, 0, sizeof(a));
+  if (int r = seg_w4(a.seg[0], b, b_s, b_z, K, N, wgrp)) return r;
+  a.nseg = 1;
+  a.M = static_cast<int>(M);
+  a.K = static_cast<int>(K);
+  a.wgrp = static_cast<int>(wgrp);
+  a.out = out;
+  a.ldo = ldo;
+  a.peer = &pr;
+  return run_gemv(4, kEpiOut, a, tiles_of(N), static_cast<cudaStream_t>(stream));
+}
+
+int qlin_plan_dp(int wbits, int gate_up, int64_t M, int64_t K, int64_t tiles, int64_t wgrp, int sms, int64_t* out) {
+  if ((wbits != 8 && wbits != 4) || !out || M <= 0 || tiles <= 0 || sms < 0 || K <= 0)
+    return fail(QLIN_ERR_INVALID_ARGUMENT, "bad plan query");
+  if (sms == 0) {
+    DevInfo di;
+    if (int r = launch_info(&di)) return r;
+    sms = di.sms;
+  }
+  for (int i = 0; i < 4; ++i) out[i] = 0;
+  if (M > tune_dp_maxm() || !use_dp()) return QLIN_OK;
+  DpPlan pl;
+  if (!plan_dp(wbits, dp_mr(M), gate_up ? 2 : 1, static_cast<int>(K), static_cast<int>(wgrp), static_cast<int>(tiles),
+               sms, &pl))
+    return QLIN_OK;
+  out[0] = pl.split;
+  out[1] = pl.kout;
+  out[2] = pl.ring;
+  out[3] = pl.gmax;
+  return QLIN_OK;
 }
 
 int qlin_proj3(const int8_t* a_q, const float* a_s, int64_t M, int64_t K, const int8_t* w1,

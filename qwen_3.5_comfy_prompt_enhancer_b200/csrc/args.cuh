@@ -57,6 +57,7 @@ struct GemvArgs {
   int n_q;
   unsigned* fault;    // device fault word (bounded waits)
   int tl_slot;        // tuning builds: phase-timeline slot of this launch (-1: none)
+  const void* peer;   // column-split layer: the dp kernel's DpPeer (host copy), or null
 };
 
 #ifdef QLIN_TUNING

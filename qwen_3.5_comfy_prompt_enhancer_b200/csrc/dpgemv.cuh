@@ -69,6 +69,26 @@ constexpr int kDpWsTiles = 1024;
 static __device__ __align__(256) float g_dp_ws[kDpWsSlots][kDpWsFloats];
 static __device__ __align__(256) unsigned g_dp_cnt[kDpWsSlots][kDpWsTiles];
 
+// Column-split layer only (kEpiOut, one segment): the activation rows come
+// from the ranks' flagged words of h in this rank's exchange buffer instead of
+// a_q / a_s, and every output row also goes to every rank's exchange buffer of
+// the output as flagged words (the layouts of qlin_peer_allgather_ll: codes
+// [M][kloc] then scales [M][kloc / 64] per sender; outputs [M][N] bf16).
+constexpr int kDpPeerMax = 8;
+struct DpPeer {
+  const uint8_t* rx;          // this rank's exchange buffer of h, or null
+  long long rx_slot;          // bytes of one sender slot
+  long long rx_off_s;         // byte offset of the scale words in a slot (codes at 0)
+  const unsigned* rx_state;   // call number = rx_state[0] + 1
+  int rx_kloc;                // h columns each rank sends (multiple of 128)
+  int8_t* rx_hq;              // optional copy of the received rows [M][K] (tile 0 writes it), or null
+  float* rx_hs;               // and of their scales [M][K / 64]
+  uint8_t* tx[kDpPeerMax];    // every rank's exchange buffer of the output, or null
+  long long tx_slot;
+  const unsigned* tx_state;   // call number = tx_state[0] + 1
+  int world, rank;
+};
+
 struct DpArgs {
   CUtensorMap tw[3];   // weights, plain (unswizzled) boxes: W8 128 columns x 64 rows; W4 128 x 32 packed rows
   CUtensorMap ts[3];   // W4 group scales (bf16), box 128 x nsub
@@ -89,6 +109,7 @@ struct DpArgs {
   int8_t* out_q;
   float* out_s;
   int n_q;
+  DpPeer peer;
   unsigned* fault;
 };
 
@@ -260,21 +281,76 @@ __global__ void __launch_bounds__(kRgThreads, 2) dp_gemv_kernel(const __grid_con
   // and a 16-byte aligned a_q make every row slice 16-byte aligned); rows
   // past M are never stored, so their slots are left as they are
   const int mv = p.M < MR ? p.M : MR;
-  if (threadIdx.x == 0) {
-    mbar_arrive_expect_tx(abar, static_cast<uint32_t>(mv * nst * 64));
-    for (int m = 0; m < mv; ++m)
-      bulk_load(act + m * p.gmax * 64, p.a_q + static_cast<long long>(m) * p.K + g0 * 64,
-                static_cast<uint32_t>(nst * 64), abar);
-  }
-  // the scales of the K part, while the rows are in flight (one round trip
-  // for all of them instead of one per item); rows past M scale by zero
-  for (int i = threadIdx.x; i < MR * nst; i += kRgThreads) {
-    const int m = i / nst, gl = i - m * nst;
-    as_sm[m * p.gmax + gl] = m < p.M ? __ldg(p.a_s + static_cast<long long>(m) * G + g0 + gl) : 0.0f;
-  }
-  if (!mbar_wait(abar, 0)) {
-    if ((threadIdx.x & 31) == 0) record_fault(p.fault, kFaultFullWait);
-    mbar_wait(abar, 0);  // the copy lands before the CTA may exit
+  if (p.peer.rx) {
+    // Column-split layer: poll the flagged words of the K part's h codes (8
+    // bytes per word pair) and scales (two groups per word pair) from their
+    // sender's slot until they carry this call's number (bounded).
+    const DpPeer& pr = p.peer;
+    const unsigned seq = pr.rx_state[0] + 1u;
+    const uint8_t* base = pr.rx + static_cast<long long>(seq & 1u) * pr.world * pr.rx_slot;
+    const int ncodes = mv * nst * 8, nall = ncodes + mv * nst;
+    const bool keep = pr.rx_hq != nullptr && tile == 0;
+    bool dead = false;
+    const unsigned long long t0 = global_ns();
+    for (int i = threadIdx.x; i < nall && !dead; i += kRgThreads) {
+      const bool code = i < ncodes;
+      int m, gl, c8 = 0;
+      if (code) {
+        m = i / (nst * 8);
+        const int r = i - m * nst * 8;
+        gl = r >> 3;
+        c8 = r & 7;
+      } else {
+        m = (i - ncodes) / nst;
+        gl = i - ncodes - m * nst;
+      }
+      const int k = (g0 + gl) * 64 + c8 * 8;
+      const int q = k / pr.rx_kloc, kl = k - q * pr.rx_kloc;
+      const uint8_t* w = base + q * pr.rx_slot +
+                         (code ? (static_cast<long long>(m) * (pr.rx_kloc / 8) + kl / 8) * 16
+                               : pr.rx_off_s + (static_cast<long long>(m) * (pr.rx_kloc / 128) + kl / 128) * 16);
+      unsigned long long w0, w1;
+      unsigned spin = 0;
+      for (;;) {
+        ld_sys_v2(w, w0, w1);
+        if (ll_fresh(w0, seq) && ll_fresh(w1, seq)) break;
+        if ((++spin & 63u) == 0 && global_ns() - t0 > wait_limit_ns()) {
+          dead = true;
+          break;
+        }
+      }
+      if (dead) break;
+      if (code) {
+        const uint2 v = make_uint2(static_cast<unsigned>(w0), static_cast<unsigned>(w1));
+        *reinterpret_cast<uint2*>(act + (m * p.gmax + gl) * 64 + c8 * 8) = v;
+        if (keep) *reinterpret_cast<uint2*>(pr.rx_hq + static_cast<long long>(m) * p.K + k) = v;
+      } else {
+        const float sv = __uint_as_float(static_cast<unsigned>(((kl / 64) & 1) ? w1 : w0));
+        as_sm[m * p.gmax + gl] = sv;
+        if (keep) pr.rx_hs[static_cast<long long>(m) * G + k / 64] = sv;
+      }
+    }
+    if (dead) record_fault(p.fault, kFaultFullWait);
+    for (int i = threadIdx.x; i < (MR - mv) * nst; i += kRgThreads) as_sm[(mv + i / nst) * p.gmax + i % nst] = 0.0f;
+    if (threadIdx.x == 0) mbar_arrive(abar);  // phase 0 done: the K-part combine uses phase 1
+    __syncthreads();  // the received rows
+  } else {
+    if (threadIdx.x == 0) {
+      mbar_arrive_expect_tx(abar, static_cast<uint32_t>(mv * nst * 64));
+      for (int m = 0; m < mv; ++m)
+        bulk_load(act + m * p.gmax * 64, p.a_q + static_cast<long long>(m) * p.K + g0 * 64,
+                  static_cast<uint32_t>(nst * 64), abar);
+    }
+    // the scales of the K part, while the rows are in flight (one round trip
+    // for all of them instead of one per item); rows past M scale by zero
+    for (int i = threadIdx.x; i < MR * nst; i += kRgThreads) {
+      const int m = i / nst, gl = i - m * nst;
+      as_sm[m * p.gmax + gl] = m < p.M ? __ldg(p.a_s + static_cast<long long>(m) * G + g0 + gl) : 0.0f;
+    }
+    if (!mbar_wait(abar, 0)) {
+      if ((threadIdx.x & 31) == 0) record_fault(p.fault, kFaultFullWait);
+      mbar_wait(abar, 0);  // the copy lands before the CTA may exit
+    }
   }
   if (WB == 4) {
     // Once per CTA instead of once per item and stream: every 8-byte block of
@@ -539,13 +615,38 @@ __global__ void __launch_bounds__(kRgThreads, 2) dp_gemv_kernel(const __grid_con
   const bool valid = en < S0.n;
   if (EPI == kEpiOut) {
     __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
+    if (p.peer.tx[0]) {
+      // Column-split layer: every row also goes to every rank's exchange
+      // buffer, four columns (two flagged words) per store from lanes 4j.
+      const DpPeer& pr = p.peer;
+      const unsigned seq = pr.tx_state[0] + 1u;
+      const unsigned long long tag = static_cast<unsigned long long>(seq) << 32;
+      const long long obase = static_cast<long long>(seq & 1u) * pr.world * pr.tx_slot + pr.rank * pr.tx_slot;
 #pragma unroll
-    for (int m = 0; m < MR; ++m) {
-      if (!valid || m >= p.M) continue;
-      float v = vs[0][m];
-      if (WB == 8) v = __fmul_rn(v, pre_s0);  // out * bs (kernels/gemm.py:51-52)
-      if (p.res) v = __fadd_rn(v, pre_res[m]);
-      out[static_cast<long long>(m) * p.ldo + S0.out_col + en] = __float2bfloat16_rn(v);
+      for (int m = 0; m < MR; ++m) {
+        const bool sto = valid && m < p.M;
+        float v = vs[0][m];
+        if (WB == 8) v = __fmul_rn(v, pre_s0);
+        const __nv_bfloat16 bv = __float2bfloat16_rn(v);
+        if (sto) out[static_cast<long long>(m) * p.ldo + S0.out_col + en] = bv;
+        const unsigned b0 = sto ? static_cast<unsigned>(__bfloat16_as_ushort(bv)) : 0u;
+        const unsigned b1 = __shfl_down_sync(0xffffffffu, b0, 1);
+        const unsigned b2 = __shfl_down_sync(0xffffffffu, b0, 2);
+        const unsigned b3 = __shfl_down_sync(0xffffffffu, b0, 3);
+        if (sto && (c & 3) == 0) {
+          const long long e = obase + (static_cast<long long>(m) * (S0.n / 4) + en / 4) * 16;
+          for (int q = 0; q < pr.world; ++q) st_sys_v2(pr.tx[q] + e, tag | (b0 | (b1 << 16)), tag | (b2 | (b3 << 16)));
+        }
+      }
+    } else {
+#pragma unroll
+      for (int m = 0; m < MR; ++m) {
+        if (!valid || m >= p.M) continue;
+        float v = vs[0][m];
+        if (WB == 8) v = __fmul_rn(v, pre_s0);  // out * bs (kernels/gemm.py:51-52)
+        if (p.res) v = __fadd_rn(v, pre_res[m]);
+        out[static_cast<long long>(m) * p.ldo + S0.out_col + en] = __float2bfloat16_rn(v);
+      }
     }
   } else {
     float* xchg = reinterpret_cast<float*>(smem + L.xchg_off);

@@ -160,27 +160,13 @@ struct LlGatherArgs {
   long long units;         // all parts' units
   uint8_t* dst;            // this rank's destination
   int world, rank;
+  // 0: the full gather; 1: send only (every rank's exchange, this rank's own
+  // included; nothing advanced); 2: receive only (from every rank, own
+  // included; advances `state` and, if set, adds one to state2[0])
+  int mode;
+  unsigned* state2;
   unsigned* fault;
 };
-
-__device__ __forceinline__ void st_sys_v2(void* p, unsigned long long a, unsigned long long b) {
-  asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
-}
-__device__ __forceinline__ void st_sys_u64(void* p, unsigned long long a) {
-  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(a) : "memory");
-}
-__device__ __forceinline__ void ld_sys_v2(const void* p, unsigned long long& a, unsigned long long& b) {
-  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
-}
-__device__ __forceinline__ unsigned long long ld_sys_u64(const void* p) {
-  unsigned long long a;
-  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(a) : "l"(p) : "memory");
-  return a;
-}
-// word carries call `seq` (or a later one, which the protocol never produces)
-__device__ __forceinline__ bool ll_fresh(unsigned long long w, unsigned seq) {
-  return static_cast<int>(static_cast<unsigned>(w >> 32) - seq) >= 0;
-}
 
 __device__ __forceinline__ int ll_part_of(const LlGatherArgs& a, long long u) {
   int p = 0;
@@ -197,7 +183,7 @@ __global__ void __launch_bounds__(kPeerThreads) peer_ll_gather_kernel(const __gr
   const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
   const unsigned long long tag = static_cast<unsigned long long>(seq) << 32;
   // 1. send
-  for (long long u = tid; u < a.units; u += stride) {
+  for (long long u = tid; a.mode != 2 && u < a.units; u += stride) {
     const LlPart& p = a.part[ll_part_of(a, u)];
     const long long v = u - p.first, per_row = p.row_bytes / p.unit;
     const long long row = v / per_row, c = (v - row * per_row) * p.unit;
@@ -206,14 +192,14 @@ __global__ void __launch_bounds__(kPeerThreads) peer_ll_gather_kernel(const __gr
     const long long e = par + a.rank * a.slot_bytes + p.ll_off + v * 2 * p.unit;
     if (p.unit == 8) {
       const uint2 x = *reinterpret_cast<const uint2*>(s);
-      *reinterpret_cast<uint2*>(d) = x;
+      if (a.mode == 0) *reinterpret_cast<uint2*>(d) = x;
       for (int q = 0; q < a.world; ++q)
-        if (q != a.rank) st_sys_v2(a.ll[q] + e, tag | x.x, tag | x.y);
+        if (a.mode == 1 || q != a.rank) st_sys_v2(a.ll[q] + e, tag | x.x, tag | x.y);
     } else {
       const uint32_t x = *reinterpret_cast<const uint32_t*>(s);
-      *reinterpret_cast<uint32_t*>(d) = x;
+      if (a.mode == 0) *reinterpret_cast<uint32_t*>(d) = x;
       for (int q = 0; q < a.world; ++q)
-        if (q != a.rank) st_sys_u64(a.ll[q] + e, tag | x);
+        if (a.mode == 1 || q != a.rank) st_sys_u64(a.ll[q] + e, tag | x);
     }
   }
   // 2. receive
@@ -222,10 +208,10 @@ __global__ void __launch_bounds__(kPeerThreads) peer_ll_gather_kernel(const __gr
   __syncthreads();
   bool dead = false;
   const unsigned long long t0 = global_ns();
-  const long long total = static_cast<long long>(a.world - 1) * a.units;
+  const long long total = a.mode == 1 ? 0 : static_cast<long long>(a.mode == 2 ? a.world : a.world - 1) * a.units;
   for (long long i = tid; i < total && !dead; i += stride) {
     const long long qi = i / a.units, u = i - qi * a.units;
-    const int q = static_cast<int>(qi) < a.rank ? static_cast<int>(qi) : static_cast<int>(qi) + 1;
+    const int q = (a.mode == 2 || static_cast<int>(qi) < a.rank) ? static_cast<int>(qi) : static_cast<int>(qi) + 1;
     const LlPart& p = a.part[ll_part_of(a, u)];
     const long long v = u - p.first, per_row = p.row_bytes / p.unit;
     const long long row = v / per_row, c = (v - row * per_row) * p.unit;
@@ -264,7 +250,8 @@ __global__ void __launch_bounds__(kPeerThreads) peer_ll_gather_kernel(const __gr
   if (threadIdx.x == 0) last = atomicAdd(a.state + 1, 1u) == gridDim.x - 1 ? 1u : 0u;
   __syncthreads();
   if (last && threadIdx.x == 0) {
-    a.state[0] = seq;
+    if (a.mode != 1) a.state[0] = seq;
+    if (a.mode == 2 && a.state2) a.state2[0] += 1u;
     a.state[1] = 0u;
   }
 }

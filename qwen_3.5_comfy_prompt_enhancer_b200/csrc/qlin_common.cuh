@@ -55,6 +55,28 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// ---------------------------------------------------------------- flagged 8-byte words (peer exchanges)
+// A word carries a call's sequence number in its high half and 4 data bytes
+// in its low half; a naturally aligned 64-bit access is single-copy atomic.
+__device__ __forceinline__ void st_sys_v2(void* p, unsigned long long a, unsigned long long b) {
+  asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+__device__ __forceinline__ void st_sys_u64(void* p, unsigned long long a) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(a) : "memory");
+}
+__device__ __forceinline__ void ld_sys_v2(const void* p, unsigned long long& a, unsigned long long& b) {
+  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_sys_u64(const void* p) {
+  unsigned long long a;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(a) : "l"(p) : "memory");
+  return a;
+}
+// word carries call `seq` (or a later one, which the protocol never produces)
+__device__ __forceinline__ bool ll_fresh(unsigned long long w, unsigned seq) {
+  return static_cast<int>(static_cast<unsigned>(w >> 32) - seq) >= 0;
+}
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)

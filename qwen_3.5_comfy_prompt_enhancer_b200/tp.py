@@ -132,6 +132,28 @@ class PeerBuffer:
                                               self.world, self.rank, dst.data_ptr(), stream_of(self.local))
         self._check("qlin_peer_allgather_ll", rc)
 
+    def send(self, parts):
+        """The sending half of ``gather``: this rank's parts go to every rank's
+        exchange buffer (its own included) as words of the next call number;
+        nothing waits and nothing advances (``qlin_peer_ll_send``)."""
+        from .kernels._host import stream_of
+        arr = (type(parts[0]) * len(parts))(*parts)
+        rc = self._lib.qlin_peer_ll_send(self._ll, self.ll_bytes, self.state.data_ptr(), arr, len(parts),
+                                         self.world, self.rank, stream_of(self.local))
+        self._check("qlin_peer_ll_send", rc)
+
+    def recv(self, parts, dst=None, state2=None):
+        """The receiving half: every rank's words of the next call number
+        (own included) into ``dst`` (default ``local``); then the call count
+        advances, and ``state2``'s by one if given (``qlin_peer_ll_recv``)."""
+        from .kernels._host import stream_of
+        dst = self.local if dst is None else dst
+        arr = (type(parts[0]) * len(parts))(*parts)
+        rc = self._lib.qlin_peer_ll_recv(self._ll, self.ll_bytes, self.state.data_ptr(), arr, len(parts),
+                                         self.world, self.rank, dst.data_ptr(),
+                                         None if state2 is None else state2.data_ptr(), stream_of(self.local))
+        self._check("qlin_peer_ll_recv", rc)
+
     def close(self):
         """Unmap the peers' exchange buffers and free this rank's.  The caller
         must make sure every rank has stopped using them first (GPU work
@@ -169,7 +191,7 @@ class ColumnParallelW4MLP:
     the full layer; ``device`` is this rank's GPU.
     """
 
-    def __init__(self, gate, up, down, device, group=None, ops=None, gather=None):
+    def __init__(self, gate, up, down, device, group=None, ops=None, gather=None, fused=True):
         self.group = group
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -196,6 +218,13 @@ class ColumnParallelW4MLP:
         if gather not in ("peer", "dist"):
             raise ValueError(f"gather must be 'peer' or 'dist', got {gather!r}")
         self.gather = gather
+        # "peer" gathers around a 1-2-row down projection that the decode-row
+        # kernel serves run inside it (qlin_tp_gemm_w4_ll): it polls h's words
+        # in its prologue and sends its output rows from its epilogue.
+        # Measured on 2 GPUs (graph replay, us per forward, separate / fused):
+        # M = 1 35.3 / 33.1, M = 2 40.5 / 39.2, M = 4 47.5 / 48.1 (not taken).
+        self.fused = fused
+        self.down_wg = self.inter // down[1].shape[0]
 
     def _workspace(self, M):
         ws = self._ws.get(M)
@@ -227,6 +256,11 @@ class ColumnParallelW4MLP:
                 h_parts=[_part(ws["hq_loc"], M, self.i_loc, self.i_loc, 0, self.inter),
                          _part(ws["hs_loc"], M, ng_loc * 4, ng_loc * 4, hs_off, ng * 4)])
             ws["o_parts"] = [_part(ws["o_slot"], M, self.h_loc * 2, self.hidden * 2, 0, self.hidden * 2)]
+            ws["fused"] = self.fused and self._fused_ok(M)
+            if ws["fused"]:
+                from ._lib import GatherPart
+                ws["h_arr"] = (GatherPart * 2)(*ws["h_parts"])
+                ws["o_arr"] = (GatherPart * 1)(*ws["o_parts"])
         else:
             nq, ns = M * self.i_loc, M * ng_loc * 4
             # the local codes and scales share one byte buffer, so a single
@@ -243,6 +277,29 @@ class ColumnParallelW4MLP:
                 o_all=torch.empty(g * M, self.h_loc, dtype=torch.bfloat16, device=d))
         self._ws[M] = ws
         return ws
+
+    def _fused_ok(self, M):
+        """Whether the down projection of M rows runs on the decode-row kernel
+        (the only one with the gathers inside) and the shard sizes fit it."""
+        if M > 2 or self.i_loc % 128 or self.h_loc % 16:
+            return False
+        from . import _lib
+        plan = (ctypes.c_int64 * 4)()
+        with torch.cuda.device(self.device):
+            _lib.check("qlin_plan_dp", _lib.load().qlin_plan_dp(4, 0, M, self.inter, -(-self.h_loc // 128),
+                                                                self.down_wg, 0, plan))
+        return plan[0] > 0
+
+    def _down_fused(self, ws, M):
+        from . import _lib
+        from .kernels._host import stream_of
+        d, hb, ob = self.down, ws["hbuf"], ws["obuf"]
+        rc = _lib.load().qlin_tp_gemm_w4_ll(
+            M, self.inter, d[0].data_ptr(), d[1].data_ptr(), None if d[2] is None else d[2].data_ptr(), self.h_loc,
+            self.down_wg, ws["o_slot"].data_ptr(), self.hidden, hb._ll, hb.ll_bytes, hb.state.data_ptr(),
+            ws["h_arr"], 2, ob._ll, ob.ll_bytes, ob.state.data_ptr(), ws["o_arr"], 1, self.world, self.rank,
+            ws["hq"].data_ptr(), ws["hs"].data_ptr(), stream_of(d[0]))
+        _lib.check("qlin_tp_gemm_w4_ll", rc)
 
     def _gather_h_dist(self, ws, M):
         """torch.distributed all-gather of the packed (codes, scales) shards,
@@ -275,6 +332,19 @@ class ColumnParallelW4MLP:
             rec(2)
             self.ops.gemm_w4(ws["hq"], ws["hs"], d[0], d[1], out, b_z=d[2])
             rec(3)
+            rec(4)
+            return out
+        if self.gather == "peer" and ws["fused"]:
+            # h's words leave now; the down projection polls them, sends its
+            # output rows, and the receive lands every rank's rows in out
+            ws["hbuf"].send(ws["h_parts"])
+            rec(2)
+            self._down_fused(ws, M)
+            rec(3)
+            direct = out.is_contiguous() and out.data_ptr() % 8 == 0
+            ws["obuf"].recv(ws["o_parts"], out if direct else None, state2=ws["hbuf"].state)
+            if not direct:
+                out.copy_(ws["out_full"])
             rec(4)
             return out
         if self.gather == "peer":

@@ -234,3 +234,61 @@ def test_peer_allgather_eager_and_graph(pkg, dev):
     for rank, ok, fault in got:
         assert ok, f"rank {rank}: gathered bytes differ"
         assert fault == 0, f"rank {rank}: device fault word {fault}"
+
+
+@pytest.mark.parametrize("M", [1, 2, 4])
+@pytest.mark.parametrize("K,N", [(4096, 640), (17408, 640)])
+def test_fused_down_projection_world1(pkg, dev, M, K, N):
+    """The down projection with the gathers inside (qlin_tp_gemm_w4_ll) at
+    world 1: h goes out as flagged words (send half), the kernel polls them
+    in its prologue and sends its rows from its epilogue, the receive half
+    writes them into out.  Two calls in a row (the call numbers advance);
+    the output must equal gemm_w4 on the same h bit for bit (same kernel and
+    plan), and the kernel's copy of the received h must equal h."""
+    from ctypes import c_int64
+    torch.cuda.set_device(dev)
+    lib = pkg._lib.load()
+    g = torch.Generator(device=dev).manual_seed(8800 + M + K)
+    b = torch.randint(0, 256, (K // 2, N), dtype=torch.uint8, device=dev, generator=g)
+    s = torch.exp(torch.randn(K // WG, N, device=dev, generator=g) * 0.5 - 5.0).to(torch.bfloat16)
+    z = torch.randint(0, 16, (K // WG, N), dtype=torch.uint8, device=dev, generator=g)
+    plan = (c_int64 * 4)()
+    assert lib.qlin_plan_dp(4, 0, M, K, N // 128, WG, 0, plan) == 0
+    if plan[0] == 0:
+        pytest.skip("shape not on the decode-row kernel")
+    hs_off = -(-M * K // 16) * 16
+    hbuf = pkg.tp.PeerBuffer(hs_off + M * (K // 64) * 4, dev)
+    obuf = pkg.tp.PeerBuffer(M * N * 2, dev)
+    hq_loc = torch.empty(M, K, dtype=torch.int8, device=dev)
+    hs_loc = torch.empty(M, K // 64, dtype=torch.float32, device=dev)
+    slot = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    hq = hbuf.local[:M * K].view(torch.int8).view(M, K)
+    hs = hbuf.local[hs_off:hs_off + M * (K // 64) * 4].view(torch.float32).view(M, K // 64)
+    h_parts = [pkg.tp._part(hq_loc, M, K, K, 0, K), pkg.tp._part(hs_loc, M, K // 16, K // 16, hs_off, K // 16)]
+    o_parts = [pkg.tp._part(slot, M, 2 * N, 2 * N, 0, 2 * N)]
+    GP = pkg._lib.GatherPart
+    h_arr, o_arr = (GP * 2)(*h_parts), (GP * 1)(*o_parts)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    for it in range(2):
+        hq_loc.copy_(torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev, generator=g))
+        hs_loc.copy_(torch.rand(M, K // 64, device=dev, generator=g) * 0.02)
+        out = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device=dev)
+        hq.zero_()
+        hs.zero_()
+        hbuf.send(h_parts)
+        rc = lib.qlin_tp_gemm_w4_ll(M, K, b.data_ptr(), s.data_ptr(), z.data_ptr(), N, WG, slot.data_ptr(), N,
+                                    hbuf._ll, hbuf.ll_bytes, hbuf.state.data_ptr(), h_arr, 2, obuf._ll,
+                                    obuf.ll_bytes, obuf.state.data_ptr(), o_arr, 1, 1, 0, hq.data_ptr(),
+                                    hs.data_ptr(), stream)
+        assert rc == 0, lib.qlin_last_error()
+        obuf.recv(o_parts, out, state2=hbuf.state)
+        ref = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+        pkg.gemm_w4(hq_loc, hs_loc, b, s, ref, b_z=z)
+        torch.cuda.synchronize()
+        assert torch.equal(hq, hq_loc) and torch.equal(hs, hs_loc), f"call {it}: received h differs"
+        assert torch.equal(slot.view(torch.int16), ref.view(torch.int16)), f"call {it}: rows differ from gemm_w4"
+        assert torch.equal(out.view(torch.int16), ref.view(torch.int16)), f"call {it}: received rows differ"
+        assert hbuf.state[0].item() == it + 1 and obuf.state[0].item() == it + 1
+    assert lib.qlin_device_fault(1) == 0
+    hbuf.close()
+    obuf.close()
