@@ -650,6 +650,7 @@ __global__ void __launch_bounds__(kRgThreads, 2) dp_gemv_kernel(const __grid_con
     }
   } else {
     float* xchg = reinterpret_cast<float*>(smem + L.xchg_off);
+    float hb[MR], amax[MR];
 #pragma unroll
     for (int m = 0; m < MR; ++m) {
       float g = vs[0][m], uu = vs[1][m];
@@ -658,21 +659,32 @@ __global__ void __launch_bounds__(kRgThreads, 2) dp_gemv_kernel(const __grid_con
         uu = __fmul_rn(uu, pre_s1);
       }
       const float h = __fmul_rn(silu_ref(g), uu);  // silu(g) * u (kernels/gemm.py:197)
-      const bool store = valid && m < p.M;
       if (EPI == kEpiSiluBf16) {
-        if (store) reinterpret_cast<__nv_bfloat16*>(p.out)[static_cast<long long>(m) * p.ldo + en] = __float2bfloat16_rn(h);
+        if (valid && m < p.M)
+          reinterpret_cast<__nv_bfloat16*>(p.out)[static_cast<long long>(m) * p.ldo + en] = __float2bfloat16_rn(h);
       } else {
         // kernels/gemm.py:198-211: round through bf16, per-64 amax, int8 codes
-        const float hb = bf16_round_f32(h);
-        float amax = fabsf(hb);
+        hb[m] = bf16_round_f32(h);
+        amax[m] = fabsf(hb[m]);
+      }
+    }
+    if (EPI == kEpiSiluQuant) {
+      // every row's warp amax first, one exchange with the other warp of each
+      // 64-column group for all rows, then the codes
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        if ((threadIdx.x & 31) == 0) xchg[q4 * MR + m] = amax;
-        named_bar_sync(2, kTileN);
-        amax = fmaxf(amax, xchg[(q4 ^ 1) * MR + m]);  // the other warp of this 64-column group
-        const float scq = fmaxf(__fdiv_rn(amax, 127.0f), 1e-8f);
-        const int8_t qv = round_i8(__fdiv_rn(hb, scq));
-        if (store) {
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int m = 0; m < MR; ++m) amax[m] = fmaxf(amax[m], __shfl_xor_sync(0xffffffffu, amax[m], o));
+      if ((threadIdx.x & 31) == 0)
+#pragma unroll
+        for (int m = 0; m < MR; ++m) xchg[q4 * MR + m] = amax[m];
+      named_bar_sync(2, kTileN);
+#pragma unroll
+      for (int m = 0; m < MR; ++m) {
+        const float am = fmaxf(amax[m], xchg[(q4 ^ 1) * MR + m]);  // the other warp of this 64-column group
+        const float scq = fmaxf(__fdiv_rn(am, 127.0f), 1e-8f);
+        const int8_t qv = round_i8(__fdiv_rn(hb[m], scq));
+        if (valid && m < p.M) {
           p.out_q[static_cast<long long>(m) * p.n_q + en] = qv;
           if ((c & 63) == 0) p.out_s[static_cast<long long>(m) * (p.n_q / 64) + en / 64] = scq;
         }
