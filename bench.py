@@ -255,6 +255,9 @@ def cpu_measure(seconds, max_steps=None, warmup=1):
 # ----------------------------------------------------------------------------- main
 # ----------------------------------------------------------------------------- config 5 / config 3 details
 TP_K, TP_I, TP_H, TP_WG = 5120, 17408, 5120, 128
+TP_ROTATE_BYTES = 300 * 2 ** 20   # weight bytes each rank rotates over (> 126 MB of L2)
+TP_MAX_COPIES = 16
+TP_ONE_COPIES = 3                 # full-layer copies of the unsplit reference (3 x 140 MB)
 
 
 def tp_layer_bytes():
@@ -274,7 +277,9 @@ def _median_max(pg, dev, values):
 
 def _graph_us(graph, reps, repeats, pg, dev):
     """Device time per replay (us): `repeats` samples of `reps` back-to-back
-    replays, each bracketed by CUDA events; median per rank, max over ranks."""
+    replays (a list of graphs is replayed in turn), each bracketed by CUDA
+    events; median per rank, max over ranks."""
+    graphs = graph if isinstance(graph, (list, tuple)) else [graph]
     samples = []
     for _ in range(repeats):
         torch.cuda.synchronize()
@@ -284,8 +289,8 @@ def _graph_us(graph, reps, repeats, pg, dev):
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
-        for _ in range(reps):
-            graph.replay()
+        for i in range(reps):
+            graphs[i % len(graphs)].replay()
         e1.record()
         e1.synchronize()
         samples.append(e0.elapsed_time(e1) / reps * 1e3)
@@ -346,7 +351,8 @@ def _tp_parity(pkg, M, world, rank, pg, dev, layer, out, full):
 
 def tp_detail(pkg, dev, world, rank, pg, reps=20, repeats=5):
     """Config 5: the column-split W4 MLP at M in {1, 4, 64, 256} on `world` GPUs
-    (strong scaling: the whole layer's work is fixed).
+    (strong scaling: the whole layer's work is fixed).  Weights rotate over
+    copies whose bytes per rank exceed L2, for the split and unsplit layers.
 
     Per M: device time per forward (`us`: CUDA-graph replay of the whole
     forward; `eager_us`: one Python call per forward), the same-run time of
@@ -364,6 +370,20 @@ def tp_detail(pkg, dev, world, rank, pg, reps=20, repeats=5):
                 torch.randint(0, 16, (k // TP_WG, n), dtype=torch.uint8, device=dev, generator=g))
     full = (w(TP_K, TP_I), w(TP_K, TP_I), w(TP_I, TP_H))
     layer = pkg.tp.ColumnParallelW4MLP(*full, dev)
+    # Graph replays rotate over copies of the layer's weights (sharing its
+    # gather buffers) whose shards add up to more than L2 per rank, so every
+    # forward streams its weights from HBM; the unsplit layer on rank 0
+    # rotates over TP_ONE_COPIES full copies the same way.
+    ncopy = max(1, min(TP_MAX_COPIES, -(-TP_ROTATE_BYTES * world // tp_layer_bytes())))
+    layers = [layer]
+    fulls = [full] if rank == 0 else []
+    for _ in range(ncopy - 1):
+        fc = (w(TP_K, TP_I), w(TP_K, TP_I), w(TP_I, TP_H))
+        layers.append(layer.sharing(*fc))
+        if rank == 0 and len(fulls) < TP_ONE_COPIES:
+            fulls.append(fc)
+    while rank == 0 and len(fulls) < TP_ONE_COPIES:
+        fulls.append((w(TP_K, TP_I), w(TP_K, TP_I), w(TP_I, TP_H)))
     if rank != 0:
         full = None
     res = {}
@@ -376,7 +396,7 @@ def tp_detail(pkg, dev, world, rank, pg, reps=20, repeats=5):
         for _ in range(3):
             layer(a_q, a_s, out)
         torch.cuda.synchronize()
-        graph = layer.capture(a_q, a_s, out)
+        graph = [lc.capture(a_q, a_s, out) for lc in layers]
         us = _graph_us(graph, reps, repeats, pg, dev)
         # eager forwards, with per-stage events on the last of each sample
         eager, stages = [], []
@@ -400,23 +420,26 @@ def tp_detail(pkg, dev, world, rank, pg, reps=20, repeats=5):
         # the unsplit layer on rank 0's GPU, same run
         one_us = torch.zeros(1, device=dev)
         if rank == 0:
-            (gw, gs, gz), (uw, us_, uz), (dw, ds, dz) = full
             hq1 = torch.empty(M, TP_I, dtype=torch.int8, device=dev)
             hs1 = torch.empty(M, TP_I // 64, dtype=torch.float32, device=dev)
             o1 = torch.empty(M, TP_H, dtype=torch.bfloat16, device=dev)
 
-            def unsplit():
+            def unsplit(fw):
+                (gw, gs, gz), (uw, us_, uz), (dw, ds, dz) = fw
                 pkg.mlp_gate_up_quant_w4(a_q, a_s, gw, gs, uw, us_, hq1, hs1, zg=gz, zu=uz)
                 pkg.gemm_w4(hq1, hs1, dw, ds, o1, b_z=dz)
             s1 = torch.cuda.Stream(device=dev)
             s1.wait_stream(torch.cuda.current_stream(dev))
             with torch.cuda.stream(s1):
                 for _ in range(3):
-                    unsplit()
+                    for fw in fulls:
+                        unsplit(fw)
             torch.cuda.current_stream(dev).wait_stream(s1)
-            g1 = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g1, stream=s1):
-                unsplit()
+            g1 = []
+            for fw in fulls:
+                g1.append(torch.cuda.CUDAGraph())
+                with torch.cuda.graph(g1[-1], stream=s1):
+                    unsplit(fw)
             one_us[0] = _graph_us(g1, reps, repeats, None, dev)
             del g1
         if pg:
@@ -425,19 +448,23 @@ def tp_detail(pkg, dev, world, rank, pg, reps=20, repeats=5):
         parity.append(_tp_parity(pkg, M, world, rank, pg, dev, layer, out, full))
         del graph
         res[f"M{M}"] = {"us": us, "eager_us": eager_us, "one_gpu_us": one, "speedup_vs_1gpu": one / us,
-                        "stages_us": stage_us, "weight_tbs": tp_layer_bytes() / us / 1e6}
+                        "stages_us": stage_us, "weight_tbs": tp_layer_bytes() / us / 1e6,
+                        "gathers_in_down": bool(layer._ws.get(M, {}).get("fused", False))}
     gather = layer.gather
     layer.close()
     bad = [p for p in parity if p != "ok"]
     return {"workload": "config 5: W4 g128 gate_up 5120->2x17408 (fused SiLU+requant) + down 17408->5120, "
                         "columns split over ranks, all-gather of h and of the output",
-            "gather": ("NVLink peer-memory stores into the column slots (own kernel)" if gather == "peer"
+            "gather": ("flagged 8-byte words over NVLink peer memory into the column slots (own kernels; "
+                       "inside the down projection where gathers_in_down)" if gather == "peer"
                        else "none (one rank)" if world == 1 else "torch.distributed"),
             "n_gpus": world, "scaling": "strong", "layer_weight_bytes": tp_layer_bytes(),
             "parity": bad[0] if bad else "ok",
             "parity_rule": "ranks bit-equal; gathered h vs unsplit h: >=99.9% codes equal, all within +-1; "
                            "output vs unsplit down projection of that h: |d| <= 1e-3 + 1e-2|ref|",
-            "timing": f"median of {repeats} samples of {reps} forwards per rank, max over ranks",
+            "timing": f"median of {repeats} samples of {reps} forwards per rank, max over ranks; graph replays "
+                      f"rotate over {ncopy} weight copies (unsplit: {TP_ONE_COPIES})",
+            "weight_copies": ncopy,
             "per_M": res}
 
 

@@ -30,6 +30,7 @@ it is not used.  Weights are given in the engine layouts (packed uint8 [K/2, N],
 bf16 scales [K/WG, N], optional uint8 zeros [K/WG, N]); each rank keeps a
 contiguous copy of its columns only.
 """
+import copy
 import ctypes
 
 import torch
@@ -225,6 +226,23 @@ class ColumnParallelW4MLP:
         # M = 1 35.3 / 33.1, M = 2 40.5 / 39.2, M = 4 47.5 / 48.1 (not taken).
         self.fused = fused
         self.down_wg = self.inter // down[1].shape[0]
+
+    def sharing(self, gate, up, down):
+        """The same layer shape with other weights (full-layer triples, sharded
+        like the constructor's), sharing this layer's workspaces: gather
+        buffers and their call counts.  Forwards of the layers that share them
+        must run one after another on one stream, in the same order on every
+        rank; only the first layer's ``close`` releases the buffers."""
+        other = copy.copy(self)
+        lo, hi = shard_range(self.inter, self.rank, self.world)
+        dlo, dhi = shard_range(self.hidden, self.rank, self.world)
+        put = (lambda t: None if t is None else t.to(self.device))
+        other.gate = tuple(put(_cols(t, lo, hi)) for t in gate)
+        other.up = tuple(put(_cols(t, lo, hi)) for t in up)
+        other.down = tuple(put(_cols(t, dlo, dhi)) for t in down)
+        if other.gate[0].shape != self.gate[0].shape or other.down[0].shape != self.down[0].shape:
+            raise ValueError("weights of another shape")
+        return other
 
     def _workspace(self, M):
         ws = self._ws.get(M)
