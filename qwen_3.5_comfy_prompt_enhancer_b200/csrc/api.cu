@@ -1808,11 +1808,12 @@ static int ll_gather(void* const* ll, int64_t ll_bytes, void* state, const qlin_
   a.mode = mode;
   a.state2 = static_cast<unsigned*>(state2);
   a.fault = di.fault;
-  // units per thread: about two sends or receives
+  // about two received words (or sends) per thread, at most two CTAs per SM
+  // (all resident: a CTA's polls wait only on other GPUs); large gathers keep
+  // kLlBatch words per thread in flight
   const long long work = a.units * (mode != 0 ? world : world > 1 ? world - 1 : 1);
   long long ctas = (work + kPeerThreads * 2 - 1) / (kPeerThreads * 2);
-  if (ctas > kLlMaxCtas) ctas = kLlMaxCtas;
-  if (ctas > di.sms) ctas = di.sms;
+  if (ctas > 2LL * di.sms) ctas = 2LL * di.sms;
   if (ctas < 1) ctas = 1;
   const void* kern = reinterpret_cast<const void*>(peer_ll_gather_kernel);
   if (int r = prefer_shared(kern)) return r;

@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allgather_kernel(const __gr
 // received every rank's call-(s + 1) words, which every rank sends only once
 // its own call s (and so its reads of parity s & 1) has completed.
 constexpr int kLlMaxParts = 4;
-constexpr int kLlMaxCtas = 148;
+constexpr int kLlBatch = 4;  // words a receiving thread keeps in flight
 
 struct LlPart {
   const uint8_t* src;    // this rank's block: rows x row_bytes, row stride src_ld
@@ -209,37 +209,60 @@ __global__ void __launch_bounds__(kPeerThreads) peer_ll_gather_kernel(const __gr
   bool dead = false;
   const unsigned long long t0 = global_ns();
   const long long total = a.mode == 1 ? 0 : static_cast<long long>(a.mode == 2 ? a.world : a.world - 1) * a.units;
-  for (long long i = tid; i < total && !dead; i += stride) {
-    const long long qi = i / a.units, u = i - qi * a.units;
-    const int q = (a.mode == 2 || static_cast<int>(qi) < a.rank) ? static_cast<int>(qi) : static_cast<int>(qi) + 1;
-    const LlPart& p = a.part[ll_part_of(a, u)];
-    const long long v = u - p.first, per_row = p.row_bytes / p.unit;
-    const long long row = v / per_row, c = (v - row * per_row) * p.unit;
-    const uint8_t* w = a.ll[a.rank] + par + q * a.slot_bytes + p.ll_off + v * 2 * p.unit;
-    uint8_t* d = a.dst + p.dst_off + q * p.row_bytes + row * p.dst_ld + c;
+  // kLlBatch words per thread in flight: their loads go out together, and a
+  // word is polled again only while it is stale
+  for (long long i0 = tid; i0 < total && !dead; i0 += stride * kLlBatch) {
+    const uint8_t* w[kLlBatch];
+    uint8_t* d[kLlBatch];
+    bool need[kLlBatch];
+    bool wide[kLlBatch];
+#pragma unroll
+    for (int b = 0; b < kLlBatch; ++b) {
+      const long long i = i0 + b * stride;
+      need[b] = i < total;
+      w[b] = nullptr;
+      d[b] = nullptr;
+      wide[b] = false;
+      if (!need[b]) continue;
+      const long long qi = i / a.units, u = i - qi * a.units;
+      const int q = (a.mode == 2 || static_cast<int>(qi) < a.rank) ? static_cast<int>(qi) : static_cast<int>(qi) + 1;
+      const LlPart& p = a.part[ll_part_of(a, u)];
+      const long long v = u - p.first, per_row = p.row_bytes / p.unit;
+      const long long row = v / per_row, c = (v - row * per_row) * p.unit;
+      w[b] = a.ll[a.rank] + par + q * a.slot_bytes + p.ll_off + v * 2 * p.unit;
+      d[b] = a.dst + p.dst_off + q * p.row_bytes + row * p.dst_ld + c;
+      wide[b] = p.unit == 8;
+    }
     unsigned spin = 0;
-    if (p.unit == 8) {
-      unsigned long long w0, w1;
-      for (;;) {
-        ld_sys_v2(w, w0, w1);
-        if (ll_fresh(w0, seq) && ll_fresh(w1, seq)) break;
-        if ((++spin & 63u) == 0 && global_ns() - t0 > wait_limit_ns()) {
-          dead = true;
-          break;
+    for (;;) {
+      bool pending = false;
+#pragma unroll
+      for (int b = 0; b < kLlBatch; ++b) {
+        if (!need[b]) continue;
+        if (wide[b]) {
+          unsigned long long w0, w1;
+          ld_sys_v2(w[b], w0, w1);
+          if (ll_fresh(w0, seq) && ll_fresh(w1, seq)) {
+            *reinterpret_cast<uint2*>(d[b]) = make_uint2(static_cast<unsigned>(w0), static_cast<unsigned>(w1));
+            need[b] = false;
+          } else {
+            pending = true;
+          }
+        } else {
+          const unsigned long long w0 = ld_sys_u64(w[b]);
+          if (ll_fresh(w0, seq)) {
+            *reinterpret_cast<uint32_t*>(d[b]) = static_cast<unsigned>(w0);
+            need[b] = false;
+          } else {
+            pending = true;
+          }
         }
       }
-      if (!dead) *reinterpret_cast<uint2*>(d) = make_uint2(static_cast<unsigned>(w0), static_cast<unsigned>(w1));
-    } else {
-      unsigned long long w0;
-      for (;;) {
-        w0 = ld_sys_u64(w);
-        if (ll_fresh(w0, seq)) break;
-        if ((++spin & 63u) == 0 && global_ns() - t0 > wait_limit_ns()) {
-          dead = true;
-          break;
-        }
+      if (!pending) break;
+      if ((++spin & 63u) == 0 && global_ns() - t0 > wait_limit_ns()) {
+        dead = true;
+        break;
       }
-      if (!dead) *reinterpret_cast<uint32_t*>(d) = static_cast<unsigned>(w0);
     }
   }
   if (dead) failed = 1;
