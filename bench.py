@@ -549,16 +549,20 @@ def kernel_case(pkg, dev, name):
     g = torch.Generator(device=dev).manual_seed(77)
     if name.startswith("gate_up_w4_"):
         K, N, M = {"cfg2_m1": (H, I, 1), "cfg2_m4": (H, I, 4), "cfg5_m1": (TP_K, TP_I, 1),
-                   "cfg5_m4": (TP_K, TP_I, 4)}[name[len("gate_up_w4_"):]]
+                   "cfg5_m4": (TP_K, TP_I, 4), "cfg5s8_m256": (TP_K, TP_I // 8, 256)}[name[len("gate_up_w4_"):]]
         (gw, gs, gz), (uw, us, uz) = _w4(dev, g, K, N), _w4(dev, g, K, N)
         a_q, a_s = _acts(dev, g, M, K)
         q = torch.empty(M, N, dtype=torch.int8, device=dev)
         qs = torch.empty(M, N // 64, dtype=torch.float32, device=dev)
         nbytes = 2 * (K * N // 2 + (K // WG) * N * 3) + M * K * (1 + 4 / 64) + M * N * (1 + 4 / 64)
+        if M >= 128:
+            return (lambda: pkg.mlp_gate_up_quant_w4(a_q, a_s, gw, gs, uw, us, q, qs, zg=gz, zu=uz)), \
+                4.0 * M * N * K, "op"
         return (lambda: pkg.mlp_gate_up_quant_w4(a_q, a_s, gw, gs, uw, us, q, qs, zg=gz, zu=uz)), nbytes, "B"
     if name.startswith("gemm_w4_"):
         K, N, M = {"cfg2_down_m1": (I, H, 1), "cfg2_down_m4": (I, H, 4), "cfg5_down_m1": (TP_I, TP_H, 1),
-                   "cfg5_down_m4": (TP_I, TP_H, 4), "cfg3_m2048": (2048, 12288, 2048)}[name[len("gemm_w4_"):]]
+                   "cfg5_down_m4": (TP_I, TP_H, 4), "cfg3_m2048": (2048, 12288, 2048),
+                   "cfg5_down8_m256": (TP_I, TP_H // 8, 256)}[name[len("gemm_w4_"):]]
         b, bs, bz = _w4(dev, g, K, N)
         a_q, a_s = _acts(dev, g, M, K)
         out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
