@@ -1005,6 +1005,33 @@ int launch_prefill_w4(const GemmW4Args& g, int grid, cudaStream_t st) {
   return QLIN_OK;
 }
 
+// Stream-ordered pool of the W4 GEMM's K-part workspaces, one per device,
+// owned by the library.  Freed blocks stay in the pool (no release
+// threshold), so an eager launch reuses the previous launch's memory instead
+// of mapping new pages (a default pool trims at every synchronisation).
+cudaMemPool_t g_ws_pool[kMaxDevices] = {};
+std::mutex g_ws_pool_mu;
+
+int ws_pool(int dev, cudaMemPool_t* pool) {
+  if (dev < 0 || dev >= kMaxDevices) return fail(QLIN_ERR_CUDA, "device %d out of range", dev);
+  std::lock_guard<std::mutex> g(g_ws_pool_mu);
+  if (!g_ws_pool[dev]) {
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    cudaMemPool_t p = nullptr;
+    cudaError_t e = cudaMemPoolCreate(&p, &props);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemPoolCreate(K-part workspace)");
+    unsigned long long keep = ~0ull;
+    e = cudaMemPoolSetAttribute(p, cudaMemPoolAttrReleaseThreshold, &keep);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemPoolSetAttribute(release threshold)");
+    g_ws_pool[dev] = p;
+  }
+  *pool = g_ws_pool[dev];
+  return QLIN_OK;
+}
+
 int run_prefill_w4(int epi, const GemvArgs& a, int half_tiles, cudaStream_t st) {
   DevInfo di;
   if (int r = launch_info(&di)) return r;
@@ -1065,11 +1092,13 @@ int run_prefill_w4(int epi, const GemvArgs& a, int half_tiles, cudaStream_t st) 
     --kp;
   if (kp < 1) kp = 1;
   void* ws = nullptr;
+  cudaMemPool_t pool = nullptr;
   if (kp > 1) {
+    if (int r = ws_pool(di.dev, &pool)) return r;
     const size_t ws_bytes = static_cast<size_t>(tiles) * kp * 128 * hs * 128 * 4;
     const size_t cnt_bytes = static_cast<size_t>(tiles) * 4;
-    cudaError_t e = cudaMallocAsync(&ws, ws_bytes + cnt_bytes, st);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMallocAsync(K-part workspace)");
+    cudaError_t e = cudaMallocFromPoolAsync(&ws, ws_bytes + cnt_bytes, pool, st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMallocFromPoolAsync(K-part workspace)");
     g.ws = static_cast<float*>(ws);
     g.cnt = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + ws_bytes);
     e = cudaMemsetAsync(g.cnt, 0, cnt_bytes, st);
