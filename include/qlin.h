@@ -349,6 +349,22 @@ int qlin_peer_ll_bytes(const qlin_gather_part* parts, int nparts, int world, int
 int qlin_peer_allgather_ll(void* const* ll, int64_t ll_bytes, void* state, const qlin_gather_part* parts,
                            int nparts, int world, int rank, void* dst, void* stream);
 
+/* All-gather of one or two 2-D parts (qlin_gather_part) straight into every
+ * rank's gather buffer bufs[q] (each holding dst_off + (rows - 1) * dst_ld +
+ * world * row_bytes bytes for every part), then a wait until every rank's
+ * parts have landed in bufs[rank]: the arrival-counter protocol of
+ * qlin_peer_allgather (plain stores, one system-scope fence and release per
+ * CTA, counters in every rank's memory).  It moves each byte once where the
+ * flagged words of qlin_peer_allgather_ll move it twice, so large gathers
+ * (hundreds of KB per rank and up) take it.  arrive[q]: rank q's `world`
+ * uint32 arrival counters (zero once); `expected`: this rank's `world` uint32
+ * (zero once).  Sizes, strides and addresses multiples of 4 (16 for full-width
+ * stores).  Every rank must call it with the same sizes.  A wait that does not
+ * finish within the wait limit records a device fault.  No reference
+ * counterpart. */
+int qlin_peer_allgather_fenced(void* const* bufs, void* const* arrive, void* expected, const qlin_gather_part* parts,
+                               int nparts, int world, int rank, void* stream);
+
 /* The two halves of qlin_peer_allgather_ll, for a gather whose sending or
  * receiving side sits inside another kernel (the column-split layer's down
  * projection, qlin_tp_gemm_w4_ll).  qlin_peer_ll_send stores this rank's

@@ -57,6 +57,7 @@ SIGNATURES = {
     "qlin_peer_allgather": [_P, _P, _P, _P, _I, ctypes.c_int, ctypes.c_int, _P, _P],
     "qlin_peer_ll_bytes": [_P, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int64)],
     "qlin_peer_allgather_ll": [_P, _I, _P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P],
+    "qlin_peer_allgather_fenced": [_P, _P, _P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P],
     "qlin_peer_ll_send": [_P, _I, _P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P],
     "qlin_peer_ll_recv": [_P, _I, _P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P, _P],
     "qlin_tp_gemm_w4_ll": [_I, _I, _P, _P, _P, _I, _I, _P, _I, _P, _I, _P, _P, ctypes.c_int, _P, _I, _P, _P,

@@ -1741,6 +1741,48 @@ int qlin_peer_allgather(void* const* bufs, void* const* arrive, void* expected, 
   return QLIN_OK;
 }
 
+int qlin_peer_allgather_fenced(void* const* bufs, void* const* arrive, void* expected, const qlin_gather_part* parts,
+                               int nparts, int world, int rank, void* stream) {
+  if (world < 1 || world > kPeerMax || rank < 0 || rank >= world)
+    return fail(QLIN_ERR_INVALID_ARGUMENT, "world %d / rank %d", world, rank);
+  if (!bufs || !arrive || !expected || !parts) return fail(QLIN_ERR_INVALID_ARGUMENT, "null argument");
+  if (nparts < 1 || nparts > kPeerMaxParts)
+    return fail(QLIN_ERR_INVALID_ARGUMENT, "%d parts (1 to %d)", nparts, kPeerMaxParts);
+  if (!aligned(expected, 4)) return fail(QLIN_ERR_ALIGNMENT, "expected counts must be 4-byte aligned");
+  DevInfo di;
+  if (int r = launch_info(&di)) return r;
+  PeerGatherArgs a;
+  memset(&a, 0, sizeof(a));
+  if (int r = peer_buffers(a, bufs, arrive, world)) return r;
+  long long units16 = 0;
+  for (int i = 0; i < nparts; ++i) {
+    const qlin_gather_part& q = parts[i];
+    if (!q.src || q.rows < 1 || q.row_bytes < 4 || q.src_ld < 0 || q.dst_off < 0 || q.dst_ld < 0)
+      return fail(QLIN_ERR_INVALID_ARGUMENT, "part %d: null source or bad size", i);
+    if (q.rows > 1 && (q.src_ld < q.row_bytes || q.dst_ld < static_cast<int64_t>(world) * q.row_bytes))
+      return fail(QLIN_ERR_SHAPE, "part %d: row strides overlap the rows / the ranks' slots", i);
+    auto all_mult = [&](int u) {
+      return q.row_bytes % u == 0 && q.src_ld % u == 0 && q.dst_off % u == 0 && q.dst_ld % u == 0 &&
+             aligned(q.src, u);
+    };
+    const int unit = all_mult(16) ? 16 : all_mult(4) ? 4 : 0;
+    if (!unit) return fail(QLIN_ERR_ALIGNMENT, "part %d: sizes, strides and addresses must be multiples of 4", i);
+    a.part[i] = PeerPart{static_cast<const uint8_t*>(q.src), q.src_ld, q.rows, q.row_bytes, q.dst_off, q.dst_ld,
+                         unit};
+    units16 += (q.rows * q.row_bytes + 15) / 16;
+  }
+  a.nparts = nparts;
+  a.expected = static_cast<unsigned*>(expected);
+  a.world = world;
+  a.rank = rank;
+  a.fault = di.fault;
+  // large shards: up to one CTA per SM, about 8 16-byte units per thread
+  long long ctas = (units16 + kPeerThreads * 8 - 1) / (kPeerThreads * 8);
+  if (ctas > di.sms) ctas = di.sms;
+  if (ctas < 1) ctas = 1;
+  return peer_launch(a, static_cast<int>(ctas), static_cast<cudaStream_t>(stream));
+}
+
 // Flagged-word exchange layout of `parts`: per part its unit (8 data bytes
 // per 16-byte store, or 4 per 8-byte store) and its offset in a sender slot.
 // Depends on the sizes only, so every rank (same sizes) gets the same layout.

@@ -163,11 +163,35 @@ def _check_gather(pkg, rank, world, dev):
                     good = good and torch.equal(got[:, r * rb:(r + 1) * rb], _pattern(r, rows, rb, it))
             return good
 
+        big = sum(rows * rb for rows, rb, _, _, _ in layout) >= (256 << 10)
         for it in range(4):
             fill(it)
             dst = pb.local if it % 2 == 0 else other
             pb.gather(parts, None if it % 2 == 0 else other)
             ok = ok and check(dst, it)
+        if big:
+            # the arrival-counter protocol into local (its size threshold
+            # lowered for the test, on every rank), eager then captured
+            saved, pkg.tp.FENCED_MIN_BYTES = pkg.tp.FENCED_MIN_BYTES, 0
+            for it in range(20, 23):
+                fill(it)
+                pb.gather(parts, fenced=True)
+                ok = ok and check(pb.local, it)
+            s = torch.cuda.Stream(device=dev)
+            s.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(s):
+                pb.gather(parts, fenced=True)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=s):
+                pb.gather(parts, fenced=True)
+            for it in range(23, 26):
+                fill(it)
+                graph.replay()
+                torch.cuda.synchronize()
+                ok = ok and check(pb.local, it)
+            del graph
+            pkg.tp.FENCED_MIN_BYTES = saved
         s = torch.cuda.Stream(device=dev)
         s.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(s):
