@@ -549,7 +549,8 @@ def kernel_case(pkg, dev, name):
     g = torch.Generator(device=dev).manual_seed(77)
     if name.startswith("gate_up_w4_"):
         K, N, M = {"cfg2_m1": (H, I, 1), "cfg2_m4": (H, I, 4), "cfg5_m1": (TP_K, TP_I, 1),
-                   "cfg5_m4": (TP_K, TP_I, 4), "cfg5s8_m256": (TP_K, TP_I // 8, 256)}[name[len("gate_up_w4_"):]]
+                   "cfg5_m4": (TP_K, TP_I, 4), "cfg5s8_m256": (TP_K, TP_I // 8, 256), "cfg5s2_m256": (TP_K, TP_I // 2, 256),
+                   "cfg5_m256": (TP_K, TP_I, 256)}[name[len("gate_up_w4_"):]]
         (gw, gs, gz), (uw, us, uz) = _w4(dev, g, K, N), _w4(dev, g, K, N)
         a_q, a_s = _acts(dev, g, M, K)
         q = torch.empty(M, N, dtype=torch.int8, device=dev)
