@@ -88,7 +88,7 @@ def _rank(rank, world, port, M, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("M", [1, 4])
+@pytest.mark.parametrize("M", [1, 2, 4])
 def test_tp_layer_nccl_ranks_equal_one_gpu(pkg, dev, M):
     world = min(torch.cuda.device_count(), 8)
     world = 8 if world >= 8 else (4 if world >= 4 else 2)
