@@ -161,16 +161,23 @@ def make_layer(pkg, dev, gen):
 
 
 class Workspace:
-    def __init__(self, pkg, dev, M, gen):
+    """Buffers of one row count; xq / xs / hidden may be row ranges of tensors
+    shared by every row count (so that the e2e leg moves all rows with one
+    copy each way and quantises them in one call)."""
+
+    def __init__(self, pkg, dev, M, gen, xq=None, xs=None, hidden=None):
         self.M = M
         x = torch.randn(M, H, device=dev, generator=gen).to(torch.bfloat16)
-        self.xq = torch.empty(M, H, dtype=torch.int8, device=dev)
-        self.xs = torch.empty(M, H // 64, dtype=torch.float32, device=dev)
+        self.xq = torch.empty(M, H, dtype=torch.int8, device=dev) if xq is None else xq
+        self.xs = torch.empty(M, H // 64, dtype=torch.float32, device=dev) if xs is None else xs
         pkg.quant_row(x, self.xq, self.xs)
         self.proj = torch.empty(M, QKV, dtype=torch.bfloat16, device=dev)
         self.hq = torch.empty(M, I, dtype=torch.int8, device=dev)
         self.hs = torch.empty(M, I // 64, dtype=torch.float32, device=dev)
         self.hidden = (torch.randn(M, H, device=dev, generator=gen) * 0.1).to(torch.bfloat16)
+        if hidden is not None:
+            hidden.copy_(self.hidden)
+            self.hidden = hidden
 
 
 def run_layer(pkg, L, ws):
@@ -702,7 +709,15 @@ def main():
 
     gen = torch.Generator(device=dev).manual_seed(1000 + rank)
     layers = [make_layer(pkg, dev, gen) for _ in range(COPIES)]
-    wss = {M: Workspace(pkg, dev, M, gen) for M in MS}
+    # every row count's activation codes, scales and hidden rows are row
+    # ranges of one tensor each (rows of M = 1 first, then M = 4)
+    rows = sum(MS)
+    xq_all = torch.empty(rows, H, dtype=torch.int8, device=dev)
+    xs_all = torch.empty(rows, H // 64, dtype=torch.float32, device=dev)
+    hid_all = torch.empty(rows, H, dtype=torch.bfloat16, device=dev)
+    r0 = {M: sum(MS[:i]) for i, M in enumerate(MS)}
+    wss = {M: Workspace(pkg, dev, M, gen, xq_all[r0[M]:r0[M] + M], xs_all[r0[M]:r0[M] + M],
+                        hid_all[r0[M]:r0[M] + M]) for M in MS}
     torch.cuda.synchronize()
 
     def copy_for(li, j):
@@ -774,17 +789,19 @@ def main():
 
     # ---- e2e through the public API with host buffers (rank-local)
     e2e_steps = min(args.steps, 2000)
-    host_x = {M: torch.randn(M, H).to(torch.bfloat16).pin_memory() for M in MS}
-    host_out = {M: torch.empty(M, H, dtype=torch.bfloat16).pin_memory() for M in MS}
-    dev_x = {M: torch.empty(M, H, dtype=torch.bfloat16, device=dev) for M in MS}
+    # per step: every row count's input rows in one host-to-device copy, one
+    # quant_row over all of them, the layers, every output row in one
+    # device-to-host copy
+    host_x = torch.randn(rows, H).to(torch.bfloat16).pin_memory()
+    host_out = torch.empty(rows, H, dtype=torch.bfloat16).pin_memory()
+    dev_x = torch.empty(rows, H, dtype=torch.bfloat16, device=dev)
 
     def e2e_step(li):
+        dev_x.copy_(host_x, non_blocking=True)
+        pkg.quant_row(dev_x, xq_all, xs_all)
         for M in MS:
-            ws = wss[M]
-            dev_x[M].copy_(host_x[M], non_blocking=True)
-            pkg.quant_row(dev_x[M], ws.xq, ws.xs)
-            run_layer(pkg, copy_for(li, MS.index(M)), ws)
-            host_out[M].copy_(ws.hidden, non_blocking=True)
+            run_layer(pkg, copy_for(li, MS.index(M)), wss[M])
+        host_out.copy_(hid_all, non_blocking=True)
     with torch.cuda.stream(stream):
         for li in range(3):
             e2e_step(li)
