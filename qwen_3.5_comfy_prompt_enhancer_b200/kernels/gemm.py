@@ -14,7 +14,7 @@ import torch
 from .. import _lib
 from ._host import need_block_k
 from .common import GROUP  # noqa: F401  (re-exported like the reference)
-from .w4 import gemm_w4, mlp_gate_up_quant_w4, proj3_w4
+from .w4 import gemm_w4, mlp_gate_up_quant_w4, proj3_w4  # noqa: F401  (the W4 names, as the reference exposes them)
 
 _U8 = torch.uint8
 
@@ -33,11 +33,14 @@ def gemm_i8(a_q, a_s, b, b_s, out, residual=None, block_m=None, block_n=None, bl
     ``a_s`` holds one scale per GROUP of K ([M, K//GROUP]).  ``residual`` may
     alias ``out``.  Returns ``out``.
     """
-    if b.dtype == _U8:
-        return gemm_w4(a_q, a_s, b, b_s, out, residual=residual, b_z=b_z, block_m=block_m,
-                       block_n=block_n, block_k=block_k, group_m=group_m)
     if block_k != 64:
         need_block_k(block_k)
+    if b.dtype == _U8:
+        # the W4 entry point, called here directly (one Python frame less per call)
+        rc = _lib.ext().gemm_w4(a_q, a_s, b, b_s, out, residual, b_z)
+        if rc:
+            raise _lib.QlinError("qlin_gemm_w4", rc)
+        return out
     rc = _lib.ext().gemm_i8(a_q, a_s, b, b_s, out, residual)
     if rc:
         raise _lib.QlinError("qlin_gemm_i8", rc)
@@ -57,11 +60,13 @@ def mlp_gate_up(a_q, a_s, wg, wsg, wu, wsu, out, block_k=64):
 def mlp_gate_up_quant(a_q, a_s, wg, wsg, wu, wsu, out_q, out_s, block_k=64, zg=None, zu=None):
     """Fused gate/up MLP + int8 quantisation of h, the down_proj input
     (kernels/gemm.py:154-231).  Returns ``(out_q, out_s)``."""
-    if wg.dtype == _U8:
-        return mlp_gate_up_quant_w4(a_q, a_s, wg, wsg, wu, wsu, out_q, out_s, zg=zg, zu=zu,
-                                    block_k=block_k)
     if block_k != 64:
         need_block_k(block_k)
+    if wg.dtype == _U8:
+        rc = _lib.ext().mlp_gate_up_quant_w4(a_q, a_s, wg, wsg, wu, wsu, out_q, out_s, zg, zu)
+        if rc:
+            raise _lib.QlinError("qlin_mlp_gate_up_quant_w4", rc)
+        return out_q, out_s
     rc = _lib.ext().mlp_gate_up_quant(a_q, a_s, wg, wsg, wu, wsu, out_q, out_s)
     if rc:
         raise _lib.QlinError("qlin_mlp_gate_up_quant", rc)
@@ -71,11 +76,13 @@ def mlp_gate_up_quant(a_q, a_s, wg, wsg, wu, wsu, out_q, out_s, block_k=64, zg=N
 def proj3(a_q, a_s, w1, s1, w2, s2, w3, s3, out, block_k=64, z1=None, z2=None, z3=None):
     """Three projections sharing A, written into out[:, 0:N1 | N1:N1+N2 | ...]
     (kernels/gemm.py:234-312).  ``None`` weights contribute no columns."""
-    if w1.dtype == _U8:
-        return proj3_w4(a_q, a_s, w1, s1, w2, s2, w3, s3, out, block_k=block_k, z1=z1, z2=z2,
-                        z3=z3)
     if block_k != 64:
         need_block_k(block_k)
+    if w1.dtype == _U8:
+        rc = _lib.ext().proj3_w4(a_q, a_s, w1, s1, w2, s2, w3, s3, out, z1, z2, z3)
+        if rc:
+            raise _lib.QlinError("qlin_proj3_w4", rc)
+        return out
     rc = _lib.ext().proj3(a_q, a_s, w1, s1, w2, s2, w3, s3, out)
     if rc:
         raise _lib.QlinError("qlin_proj3", rc)

@@ -22,26 +22,28 @@ def test_cpu_tensors_rejected(pkg):
 
 
 def test_w4_dispatch_on_uint8(pkg, monkeypatch):
-    """uint8 weights route gemm_i8 -> gemm_w4 (kernels/gemm.py:69-72)."""
+    """uint8 weights route gemm_i8 / mlp_gate_up_quant / proj3 to the W4 entry
+    points, int8 weights to the W8 ones (kernels/gemm.py:15-17, 69-72)."""
     from qwen35_b200.kernels import gemm as G
-    seen = {}
+    calls = []
 
-    def fake(*args, **kw):
-        seen["w4"] = True
-        return "w4"
+    class FakeExt:
+        def __getattr__(self, name):
+            def call(*args):
+                calls.append(name)
+                return 0
+            return call
 
-    monkeypatch.setattr(G, "gemm_w4", fake)
-    b = torch.zeros(32, 128, dtype=torch.uint8)
-    assert G.gemm_i8(None, None, b, None, None) == "w4" and seen["w4"]
-
-
-def test_gate_up_and_proj3_dispatch(pkg, monkeypatch):
-    from qwen35_b200.kernels import gemm as G
-    monkeypatch.setattr(G, "mlp_gate_up_quant_w4", lambda *a, **k: "gu4")
-    monkeypatch.setattr(G, "proj3_w4", lambda *a, **k: "p34")
-    w = torch.zeros(32, 128, dtype=torch.uint8)
-    assert G.mlp_gate_up_quant(None, None, w, None, w, None, None, None) == "gu4"
-    assert G.proj3(None, None, w, None, None, None, None, None, None) == "p34"
+    monkeypatch.setattr(G._lib, "ext", lambda: FakeExt())
+    b4 = torch.zeros(32, 128, dtype=torch.uint8)
+    b8 = torch.zeros(64, 128, dtype=torch.int8)
+    G.gemm_i8(None, None, b4, None, None)
+    G.mlp_gate_up_quant(None, None, b4, None, b4, None, None, None)
+    G.proj3(None, None, b4, None, None, None, None, None, None)
+    G.gemm_i8(None, None, b8, None, None)
+    G.mlp_gate_up_quant(None, None, b8, None, b8, None, None, None)
+    G.proj3(None, None, b8, None, None, None, None, None, None)
+    assert calls == ["gemm_w4", "mlp_gate_up_quant_w4", "proj3_w4", "gemm_i8", "mlp_gate_up_quant", "proj3"]
 
 
 def test_block_k_must_be_group(pkg):
