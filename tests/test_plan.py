@@ -137,3 +137,44 @@ def test_launch_plans_fit_one_wave_of_clusters(pkg, gate_up, M, K, N):
         c = lambda x: (lib.qlin_max_active_clusters(4, gate_up, M, x, pl["smem"], ctypes.byref(out)), out.value)[1]
         cap = 2 * c(1) if s == 1 else c(s // 2) if s % 2 == 0 else (c((s - 1) // 2) + c((s + 1) // 2)) // 2
     assert tiles_of(N) <= cap, (pl, cap)
+
+
+def _plan_dp(pkg, wbits, gate_up, M, K, N, wgrp=128):
+    import ctypes
+    out = (ctypes.c_int64 * 4)()
+    assert pkg._lib.load().qlin_plan_dp(wbits, gate_up, M, K, tiles_of(N), wgrp, SMS, out) == 0
+    return list(out)
+
+
+def test_decode_row_plans(pkg):
+    """qlin_plan_dp (no GPU needed with an SM count): the decode-row launches
+    of configs 1, 2 and 5 get the plans their profiles show, every plan covers
+    K, and more than four rows go to the tensor-core kernels."""
+    assert _plan_dp(pkg, 4, 1, 1, 2048, 6144)[:3] == [4, 1, 0]   # config-2 gate/up M = 1: resident, clusters of 4
+    assert _plan_dp(pkg, 4, 1, 4, 2048, 6144)[:3] == [4, 1, 0]   # and M = 4
+    assert _plan_dp(pkg, 8, 0, 1, 2048, 6144)[:3] == [4, 1, 0]   # config-1 W8
+    split, kout, ring, _ = _plan_dp(pkg, 4, 0, 1, 17408, 640)    # config-5 8-GPU down shard: ring + K parts
+    assert split == 1 and kout > 1 and ring > 0
+    split, kout, ring, _ = _plan_dp(pkg, 4, 0, 1, 17408, 5120)   # config-5 down on one GPU: (1, 40, 7) grid
+    assert (split, kout) == (1, 7) and ring > 0
+    assert _plan_dp(pkg, 4, 0, 8, 2048, 2048) == [0, 0, 0, 0]
+    for wbits, gate_up, M, K, N in itertools.product((4, 8), (0, 1), (1, 2, 3, 4), (2048, 5120, 6144, 17408),
+                                                     (640, 2048, 6144, 17408)):
+        split, kout, ring, gmax = _plan_dp(pkg, wbits, gate_up, M, K, N)
+        if split:
+            assert split * kout * gmax >= K // 64 and split <= 8
+
+
+def test_flagged_word_exchange_size(pkg):
+    """qlin_peer_ll_bytes: two halves x world senders x (two 8-byte words per 8
+    data bytes, or per 4 data bytes where rows are not a multiple of 8), each
+    part padded to 16 bytes."""
+    import ctypes
+    P = pkg._lib.GatherPart
+    lib = pkg._lib.load()
+    parts = (P * 2)(P(0, 2176, 4, 2176, 0, 8 * 2176), P(0, 36, 4, 36, 99999 * 8, 8 * 36))
+    need = ctypes.c_int64()
+    assert lib.qlin_peer_ll_bytes(parts, 2, 8, ctypes.byref(need)) == 0
+    slot = 4 * 2176 * 2 + -(-(4 * 36 // 4) * 8 // 16) * 16
+    assert need.value == 2 * 8 * slot
+    assert lib.qlin_peer_ll_bytes(parts, 2, 9, ctypes.byref(need)) != 0   # more ranks than the kernels serve
