@@ -141,3 +141,60 @@ def test_flagged_word_gather_times_out_without_its_peer(pkg, dev, lib):
     assert rc == QLIN_ERR_DEVICE_FAULT
     assert lib.qlin_device_fault(1) & 1
     assert lib.qlin_device_fault(0) == 0
+
+
+def test_fused_down_projection_times_out_without_its_peer(pkg, dev, lib):
+    """The column-split down projection with the gathers inside
+    (qlin_tp_gemm_w4_ll) as rank 0 of two, every buffer local: rank 0's h
+    words are sent, rank 1's never, so the CTAs whose K part lies in rank 1's
+    columns give up polling after the 50 ms bound and record the fault; the
+    launch returns and a clear restores service."""
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    x = torch.randn(4, 256, device=dev).to(torch.bfloat16)
+    q = torch.empty(4, 256, dtype=torch.int8, device=dev)
+    s = torch.empty(4, 4, dtype=torch.float32, device=dev)
+    pkg.quant_row(x, q, s)            # sets up the host-visible fault mirror
+    torch.cuda.synchronize()
+    assert lib.qlin_device_fault(1) == 0
+
+    M, K, N, WG, world = 1, 4096, 640, 128, 2
+    kloc = K // world
+    g = torch.Generator(device=dev).manual_seed(13)
+    b = torch.randint(0, 256, (K // 2, N), dtype=torch.uint8, device=dev, generator=g)
+    sc = torch.full((K // WG, N), 0.01, dtype=torch.bfloat16, device=dev)
+    hq_loc = torch.randint(-127, 128, (M, kloc), dtype=torch.int8, device=dev, generator=g)
+    hs_loc = torch.full((M, kloc // 64), 0.01, dtype=torch.float32, device=dev)
+    slot = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    P = pkg._lib.GatherPart
+    hs_off = K  # codes [M, K] then scales
+    h_arr = (P * 2)(P(hq_loc.data_ptr(), kloc, M, kloc, 0, K), P(hs_loc.data_ptr(), kloc // 16, M, kloc // 16, hs_off, K // 16))
+    o_arr = (P * 1)(P(slot.data_ptr(), 2 * N, M, 2 * N, 0, 2 * N))
+    hb, ob = ctypes.c_int64(), ctypes.c_int64()
+    assert lib.qlin_peer_ll_bytes(h_arr, 2, world, ctypes.byref(hb)) == 0
+    assert lib.qlin_peer_ll_bytes(o_arr, 1, world, ctypes.byref(ob)) == 0
+    h_ll = [torch.zeros(hb.value, dtype=torch.uint8, device=dev) for _ in range(world)]
+    o_ll = [torch.zeros(ob.value, dtype=torch.uint8, device=dev) for _ in range(world)]
+    h_state = torch.zeros(16, dtype=torch.int32, device=dev)
+    o_state = torch.zeros(16, dtype=torch.int32, device=dev)
+    plan = (ctypes.c_int64 * 4)()
+    assert lib.qlin_plan_dp(4, 0, M, K, N // 128, WG, 0, plan) == 0 and plan[0] > 0
+    assert lib.qlin_set_wait_limit_ns(50_000_000) == 0
+    try:
+        t0 = time.perf_counter()
+        assert lib.qlin_peer_ll_send(_ptrs(*h_ll), hb.value, h_state.data_ptr(), h_arr, 2, world, 0, stream) == 0
+        rc = lib.qlin_tp_gemm_w4_ll(M, K, b.data_ptr(), sc.data_ptr(), None, N, WG, slot.data_ptr(), N,
+                                    _ptrs(*h_ll), hb.value, h_state.data_ptr(), h_arr, 2, _ptrs(*o_ll), ob.value,
+                                    o_state.data_ptr(), o_arr, 1, world, 0, None, None, stream)
+        assert rc == 0, lib.qlin_last_error()
+        torch.cuda.synchronize()
+        elapsed = time.perf_counter() - t0
+    finally:
+        assert lib.qlin_set_wait_limit_ns(2_000_000_000) == 0
+    assert elapsed < 1.5, f"kernel returned after {elapsed:.2f} s, not after the 50 ms bound"
+    assert lib.qlin_device_fault(0) & 1
+    rc = lib.qlin_quant_row(x.data_ptr(), 256, 4, 256, q.data_ptr(), s.data_ptr(), stream)
+    assert rc == QLIN_ERR_DEVICE_FAULT
+    assert lib.qlin_device_fault(1) & 1
+    assert lib.qlin_device_fault(0) == 0
+    pkg.quant_row(x, q, s)
+    torch.cuda.synchronize()
